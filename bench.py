@@ -1,0 +1,440 @@
+"""Benchmark of the fused W8A8 tanh-GELU DiT MLP (config 1) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the fused gated MLP over one chunk of M = 32,760 tokens
+(d = 3072, ffn = 12288; fc1 -> tanh-GELU -> per-token requant -> fc2 -> gated
+residual), inputs resident in HBM. With N > 1 (torchrun, one rank per GPU) every
+rank processes its own 32,760-token shard (token sharding, no data-path
+collective: weak scaling); the time is the max over ranks.
+
+Rank 0 prints one JSON line. ``value`` is whole-job tokens/s; ``e2e`` is the same
+metric through the public operator with pinned host buffers copied in and out
+inside the timed region; ``roofline`` describes the dominant kernel (the fc1
+GEMM) against the INT8 tensor peak; ``components`` times each kernel of the
+step and the fused norm-RoPE (config 3) against HBM bandwidth.
+
+``--impl reference`` times the reference's eager CPU path (its torch-CPU
+restatement under ``oracle/``) on the host cores on a bounded token sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "x-minimaxh3_b200"))
+sys.path.insert(0, ROOT)
+
+M_TOKENS, D_MODEL, D_FFN = 32760, 3072, 12288
+OPS_PER_TOKEN = 4 * D_MODEL * D_FFN          # two int8 GEMMs, 2 ops per MAC
+METRIC = "fused INT8/W4A8 DiT-MLP tokens/s and int8 TOPS vs B200 peak at 1/2/4/8 GPUs"
+NR_BYTES_PER_TOKEN = 24576                   # Q and K rows of 3072 bf16, one read and one write each
+NR_TABLE_BYTES_PER_TOKEN = 64 * 4 * 4        # fp32 [64, 2, 2] rotation table, read once per token
+MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    try:
+        with open(MEASURED_PEAKS) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes from the committed ncu summary (profiles/traffic.json), if present."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int, period_ms: int = 100):
+        self.index = index
+        self.period_ms = period_ms
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 f"-lms={self.period_ms}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline
+# ---------------------------------------------------------------------------
+
+
+def _cpu_mlp_inputs(rows, seed=2):
+    import torch
+
+    from oracle import torch_port as P
+
+    g = torch.Generator().manual_seed(seed)
+    w1 = (torch.randn(D_FFN, D_MODEL, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(D_MODEL, D_FFN, generator=g) * 0.02).to(torch.bfloat16)
+    w1q, s1 = P.quantize_int8_rowwise(w1)
+    w2q, s2 = P.quantize_int8_rowwise(w2)
+    x = torch.randn(rows, D_MODEL, generator=g).to(torch.bfloat16)
+    gate = torch.randn(D_MODEL, generator=g).to(torch.bfloat16)
+    res = torch.randn(rows, D_MODEL, generator=g).to(torch.bfloat16)
+    return x, w1q, s1.reshape(-1), w2q, s2.reshape(-1), gate, res
+
+
+def cpu_mlp_tokens_per_s(rows: int, repeats: int = 3):
+    """Median tokens/s of the torch-CPU port of the reference eager MLP on `rows` tokens."""
+    import torch
+
+    from oracle import torch_port as P
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    args = _cpu_mlp_inputs(rows)
+    P.w8a8_gelu_mlp(*args)  # warm-up
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        P.w8a8_gelu_mlp(*args)
+        times.append(time.perf_counter() - t0)
+    return rows / statistics.median(times), torch.get_num_threads()
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    import torch
+
+    from oracle import torch_port as P
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    # size the per-step token sample so the whole run stays within ~2 minutes
+    probe_rows = 64
+    x, w1q, s1, w2q, s2, gate, res = _cpu_mlp_inputs(probe_rows)
+    P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
+    t0 = time.perf_counter()
+    P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
+    per_row = (time.perf_counter() - t0) / probe_rows
+    budget = 100.0 / max(1, args.steps + args.warmup)
+    rows = int(max(16, min(2048, budget / max(per_row, 1e-9))))
+    x, w1q, s1, w2q, s2, gate, res = _cpu_mlp_inputs(rows)
+    for _ in range(args.warmup):
+        P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
+    dt = time.perf_counter() - t0
+    value = rows * args.steps / dt
+    cores = torch.get_num_threads()
+    sample = f"{rows} of {M_TOKENS} config-1 tokens per step (per-token math; torch-CPU port of the eager path)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": "cfg1 fused W8A8 tanh-GELU DiT MLP, d=3072 ffn=12288", "tokens_per_step": rows,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "int8_tops": value * OPS_PER_TOKEN / 1e12,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def timed(fn, reps, stream):
+    import torch
+
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import h3b200
+    from h3b200 import ops
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    h3b200.library()
+    stream = torch.cuda.current_stream(dev)
+
+    # weights: identical on every rank (seeded), quantized per channel on the GPU
+    g = torch.Generator(device=dev).manual_seed(2)
+    w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(D_MODEL, D_FFN, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wt = h3b200.W8A8MLPWeights.from_float(w1, w2)
+    del w1, w2
+    # this rank's token shard
+    gs = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(M_TOKENS, D_MODEL, generator=gs, device=dev).to(torch.bfloat16)
+    res = torch.randn(M_TOKENS, D_MODEL, generator=gs, device=dev).to(torch.bfloat16)
+    gate = torch.randn(D_MODEL, generator=gs, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(res)
+    ws_bytes = int(h3b200.library().h3b200_fused_gated_mlp_workspace_bytes(M_TOKENS, D_MODEL, D_FFN))
+    work = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+
+    def step():
+        h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=out, workspace=work)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    status = h3b200.device_status(local_rank)
+    ms_per_step = ms / args.steps
+    value = world * M_TOKENS * args.steps / (ms / 1e3)
+
+    # ---- per-kernel timing of the same step (events around each launch) ----
+    xq = torch.empty(M_TOKENS, D_MODEL, dtype=torch.int8, device=dev)
+    xs = torch.empty(M_TOKENS, 1, dtype=torch.float32, device=dev)
+    amax = torch.zeros(M_TOKENS, dtype=torch.float32, device=dev)
+    act = torch.empty(M_TOKENS, D_FFN, dtype=torch.bfloat16, device=dev)
+    q2 = torch.empty(M_TOKENS, D_FFN, dtype=torch.int8, device=dev)
+    xs2 = torch.empty(M_TOKENS, 1, dtype=torch.float32, device=dev)
+    lib = h3b200.library()
+    sp = stream.cuda_stream
+
+    def k_quant():
+        lib.h3b200_quantize_int8_rowwise(x.data_ptr(), M_TOKENS, D_MODEL, D_MODEL, 0, xq.data_ptr(), xs.data_ptr(), sp)
+
+    def k_fc1():
+        ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_GELU_ABSMAX, xs, wt.s1, out=act, row_absmax=amax)
+
+    def k_requant():
+        lib.h3b200_quantize_int8_rowwise_absmax(act.data_ptr(), amax.data_ptr(), M_TOKENS, D_FFN, D_FFN,
+                                                q2.data_ptr(), xs2.data_ptr(), sp)
+
+    def k_fc2():
+        ops.int8_gemm_fused(q2, wt.w2q, ops.EPI_GATED_RESIDUAL, xs2, wt.s2, gate=gate, residual=res, out=out)
+
+    for f in (k_quant, k_fc1, k_requant, k_fc2):
+        f()
+    reps = 20
+    comp_ms = {name: timed(f, reps, stream) for name, f in
+               (("quantize_x", k_quant), ("fc1_gemm_gelu_absmax", k_fc1), ("requant_fc2_input", k_requant),
+                ("fc2_gemm_gated_residual", k_fc2))}
+    fc1_ops = 2.0 * M_TOKENS * D_MODEL * D_FFN
+    fc2_ops = fc1_ops
+
+    # ---- fused norm-RoPE (config 3), HBM-bound ----
+    from h3b200.rope import rope_grid_table
+
+    gn = torch.Generator(device=dev).manual_seed(4)
+    qn = torch.randn(M_TOKENS, 24, 128, generator=gn, device=dev).to(torch.bfloat16)
+    kn = torch.randn(M_TOKENS, 24, 128, generator=gn, device=dev).to(torch.bfloat16)
+    sh = (torch.randn(3072, generator=gn, device=dev) * 0.1).to(torch.bfloat16)
+    sc = (torch.randn(3072, generator=gn, device=dev) * 0.1).to(torch.bfloat16)
+    wq = (1 + 0.02 * torch.randn(3072, generator=gn, device=dev)).to(torch.bfloat16)
+    wk = (1 + 0.02 * torch.randn(3072, generator=gn, device=dev)).to(torch.bfloat16)
+    table = rope_grid_table((21, 39, 40), device=dev)
+    qo = torch.empty_like(qn)
+    ko = torch.empty_like(kn)
+
+    def k_nr():
+        ops.adaln_rms_rope_(qn, kn, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko)
+
+    for _ in range(3):
+        k_nr()
+    nr_ms = timed(k_nr, 50, stream)
+    nr_bytes = M_TOKENS * NR_BYTES_PER_TOKEN
+
+    peaks, peak_src = load_peaks()
+    int8_peak_tops = 2.0 * peaks["bf16_tflops"]
+    traffic = load_traffic()
+    fc1_tops = fc1_ops / (comp_ms["fc1_gemm_gelu_absmax"] * 1e-3) / 1e12
+    nr_gbs = nr_bytes / (nr_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public operator with host buffers ----
+    x_h = x.cpu().pin_memory()
+    r_h = res.cpu().pin_memory()
+    o_h = torch.empty(M_TOKENS, D_MODEL, dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x)
+    r_d = torch.empty_like(res)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        r_d.copy_(r_h, non_blocking=True)
+        h3b200.fused_gated_mlp(r_d, x_d, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=r_d, workspace=work)
+        o_h.copy_(r_d, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_steps = max(3, min(args.steps, 20))
+    if world > 1:
+        dist.barrier()
+    e2e_ms = timed(e2e_step, e2e_steps, stream)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * M_TOKENS / (e2e_ms * 1e-3)
+    h2d = x.numel() * 2 + res.numel() * 2
+    d2h = out.numel() * 2
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = 512
+        v, cores = cpu_mlp_tokens_per_s(rows)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{rows} config-1 tokens, median of 3 after 1 warm-up (torch-CPU port of the eager path)"}
+
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded N(0,1) activations/gate/residual, N(0,0.02) weights, per-channel int8)",
+            "config": {"workload": "cfg1 fused W8A8 tanh-GELU DiT MLP (fc1 -> GELU -> requant -> fc2 -> gated residual)",
+                       "tokens_per_gpu": M_TOKENS, "d": D_MODEL, "ffn": D_FFN, "parallelism": f"token-shard x{world}",
+                       "l2": "inputs larger than L2 (x, residual 201 MB each); int8 weights (75 MB) stay L2-resident"},
+            "int8_tops": value * OPS_PER_TOKEN / 1e12,
+            "roofline": {"kernel": "gemm_i8_kernel<fc1: GELU+absmax epilogue>", "bound": "tensor",
+                         "achieved": fc1_tops, "peak": int8_peak_tops, "unit": "TOP/s",
+                         "frac": fc1_tops / int8_peak_tops,
+                         "peak_source": f"2 x {peak_src} bf16 dense burst ({peaks['bf16_tflops']} TF/s); "
+                                        "tcgen05 kind::i8 issues at twice the kind::f16 rate",
+                         "traffic": traffic.get("fc1_gemm_gelu_absmax")},
+            "components": {
+                **{k: {"ms": v} for k, v in comp_ms.items()},
+                "fc2_gemm_gated_residual_tops": fc2_ops / (comp_ms["fc2_gemm_gated_residual"] * 1e-3) / 1e12,
+                "norm_rope_cfg3": {"ms": nr_ms, "achieved": nr_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                   "frac": nr_gbs / peaks["hbm_gbs"], "bytes_per_token": NR_BYTES_PER_TOKEN,
+                                   "table_bytes_per_token": NR_TABLE_BYTES_PER_TOKEN,
+                                   "traffic": traffic.get("norm_rope_cfg3")},
+            },
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,217 @@
+/*
+ * h3b200 -- B200-native (sm_100a) kernels for X-MinimaxH3's quantized DiT-block
+ * hot path, exported through a plain C ABI.
+ *
+ * Conventions (mirroring comfy_kitchen's CUDA backend launchers):
+ *  - Pointers are device pointers unless stated; the caller allocates every
+ *    output and workspace. Nothing here frees or keeps caller memory.
+ *  - Launches are asynchronous on `stream` (a cudaStream_t, e.g. torch's
+ *    current stream). No entry point synchronises the device except
+ *    h3b200_device_status().
+ *  - bf16 tensors are 16-bit storage; int8 tensors are signed bytes.
+ *  - Every entry point returns an int status (H3B200_OK on success). A
+ *    non-zero status leaves a message in h3b200_last_error(). No C++
+ *    exception crosses this boundary and nothing falls back to another path.
+ *  - Activation codes follow comfy_kitchen backends/cuda/input_act_codes.h:13
+ *    (0 none, 1 gelu_tanh); dtype codes follow eager/quantization.py:34-40
+ *    (0 fp32, 1 fp16, 2 bf16).
+ */
+#ifndef H3B200_H_
+#define H3B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define H3B200_API __attribute__((visibility("default")))
+#else
+#define H3B200_API
+#endif
+
+typedef void* h3b200_stream_t; /* cudaStream_t */
+
+enum {
+  H3B200_OK = 0,
+  H3B200_ERR_INVALID = 1,     /* shape / stride / alignment / code outside the contract */
+  H3B200_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  H3B200_ERR_LAUNCH = 3,      /* CUDA runtime error at launch */
+  H3B200_ERR_DEVICE = 4       /* a kernel recorded a device-side failure (bounded wait expired) */
+};
+
+enum { H3B200_ACT_NONE = 0, H3B200_ACT_GELU_TANH = 1 };
+enum { H3B200_DTYPE_F32 = 0, H3B200_DTYPE_F16 = 1, H3B200_DTYPE_BF16 = 2, H3B200_DTYPE_I32 = 3 };
+
+/* Library identification and diagnostics. */
+H3B200_API const char* h3b200_version(void);
+/* Message for the last non-zero status returned on the calling thread. */
+H3B200_API const char* h3b200_last_error(void);
+/* Reads (and optionally clears) the device status word of `device`, where
+ * kernels record bounded-wait timeouts. Synchronises that device. */
+H3B200_API int h3b200_device_status(int device, unsigned int* status, int clear);
+
+/*
+ * Elementwise pre-quantization activation on bf16 (y may alias x).
+ * Replaces apply_input_act (backends/_activations.py:40-53; gelu_tanh =
+ * torch.nn.functional.gelu(approximate="tanh")); bit-identical to the
+ * reference's CPU result for every bf16 input.
+ */
+H3B200_API int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act, h3b200_stream_t stream);
+
+/*
+ * Per-token absmax INT8 quantizer.
+ * Replaces comfy_kitchen quantize_int8_rowwise: eager/quantization.py:857-875,
+ * CUDA _C.quantize_int8_rowwise (backends/cuda/dlpack_bindings.cpp:2623,
+ * kernel backends/cuda/ops/int8_linear.cu:157-200).
+ * x: bf16 [m, k] with row stride ldx elements; act applied to x first
+ * (backends/_activations.py:40-53). q: int8 [m, k] contiguous; scale: fp32 [m].
+ */
+H3B200_API int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ldx, int act, int8_t* q,
+                                 float* scale, h3b200_stream_t stream);
+
+/*
+ * Quantizer body with a precomputed per-row absmax (fp32 [m]); same arithmetic
+ * as h3b200_quantize_int8_rowwise. Used for fc2's input after the fc1 epilogue
+ * has reduced the row absmax (the reference quantizes the activated fc1 output
+ * with quantize_int8_rowwise inside int8_linear, eager/quantization.py:1024).
+ */
+H3B200_API int h3b200_quantize_int8_rowwise_absmax(const void* x, const float* absmax, int64_t m, int64_t k, int64_t ldx,
+                                        int8_t* q, float* scale, h3b200_stream_t stream);
+
+/*
+ * INT8 GEMM with int32 accumulators: out[m, n] = a[m, k] . w[n, k]^T.
+ * Replaces comfy_kitchen mm_int8 / _int8_matmul_accumulate
+ * (eager/quantization.py:749-800; CUDA cublas_gemm_int8.cu:204).
+ * a, w: int8, rows contiguous along k (k % 16 == 0); out: int32 [m, n], n % 8 == 0.
+ */
+H3B200_API int h3b200_int8_mm(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k, int32_t* out,
+                   h3b200_stream_t stream);
+
+/*
+ * Dequantizing INT8 linear from an already quantized activation:
+ * out = bf16(float(acc) * (x_scale[row] * w_scale[col])) (+ bf16 bias).
+ * Replaces int8_linear_prequantized (backends/cuda/__init__.py:1934-1957) /
+ * _C.cutlass_int8_dequant (dlpack_bindings.cpp:2713, cutlass_gemm_int8.cu:613),
+ * with the eager epilogue association (eager/quantization.py:1044-1048).
+ * w_scale_numel is 1 (tensor-wise) or n (per channel). bias may be NULL.
+ * out_dtype must be H3B200_DTYPE_BF16.
+ */
+H3B200_API int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_scale, const int8_t* w, const float* w_scale,
+                                    int64_t w_scale_numel, const void* bias, int out_dtype, void* out, int64_t m,
+                                    int64_t n, int64_t k, h3b200_stream_t stream);
+
+/*
+ * One INT8 GEMM with a fused epilogue -- the building block of the fused MLP,
+ * exposed so each stage can be launched and timed on its own.
+ * epilogue: 0 int32 out; 1 bf16 dequant (+bias); 2 dequant -> tanh-GELU -> bf16
+ * out with the per-row absmax of |out| atomically max-reduced into row_absmax
+ * (fp32 [m], caller zero-fills); 3 out = bf16(residual + dequant * gate).
+ * Arithmetic as h3b200_int8_linear_prequantized / h3b200_fused_gated_mlp.
+ * Replaces the reference's CUTLASS EVT GEMM (backends/cuda/ops/cutlass_gemm_int8.cu:242-324)
+ * and the experimental fc2 + dequant + gate + residual Triton epilogue
+ * (h3serve/native_engine/model/fused_mlp.py:58-143).
+ */
+H3B200_API int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int64_t m,
+                                      int64_t n, int64_t k, int epilogue, const float* a_scale,
+                                      const float* w_scale, int64_t w_scale_numel, const void* bias,
+                                      const void* gate, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                                      float* row_absmax, h3b200_stream_t stream);
+
+/*
+ * Full dynamically quantized INT8 linear: act -> per-row quantize -> GEMM ->
+ * dequant (+ bias). Replaces comfy_kitchen int8_linear(x, weight, weight_scale,
+ * bias, out_dtype, convrot=False, input_act) (__init__.py:722-764; CUDA
+ * backends/cuda/__init__.py:1960-2081; eager eager/quantization.py:971-1056).
+ * workspace: at least h3b200_int8_linear_workspace_bytes(m, k) bytes, 256-byte aligned.
+ */
+H3B200_API int64_t h3b200_int8_linear_workspace_bytes(int64_t m, int64_t k);
+H3B200_API int h3b200_int8_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale, int64_t w_scale_numel,
+                       const void* bias, int act, void* out, int64_t m, int64_t n, int64_t k, void* workspace,
+                       int64_t workspace_bytes, h3b200_stream_t stream);
+
+/*
+ * Fused gated W8A8 MLP on a token chunk:
+ *   h = int8_linear(x, w1, s1); a = act(h); y = int8_linear(a, w2, s2);
+ *   out = residual + y * gate   (bf16 addcmul)
+ * Replaces try_fused_gated_mlp (h3serve/native_engine/model/fused_mlp.py:269-426,
+ * fc1 -> fused-act fc2 -> addcmul_ :393-425) and the original backend's
+ * resident_weight_chunked_gated_mlp (backends/original/native_acceleration.py:79-126)
+ * for the tanh-GELU activation (act must be H3B200_ACT_GELU_TANH).
+ * x, residual, out: bf16 [m, d] (row strides ldx / ldr / ldo elements; out may
+ * alias residual); w1: int8 [ffn, d]; s1: fp32 [ffn]; w2: int8 [d, ffn];
+ * s2: fp32 [d]; gate: bf16 [d]. d % 16 == 0 and ffn % 16 == 0.
+ */
+H3B200_API int64_t h3b200_fused_gated_mlp_workspace_bytes(int64_t m, int64_t d, int64_t ffn);
+H3B200_API int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const int8_t* w2,
+                           const float* s2, const void* gate, const void* residual, int64_t ldr, void* out,
+                           int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
+                           int64_t workspace_bytes, h3b200_stream_t stream);
+
+/*
+ * Fused (AdaLN-modulate +) RMSNorm + split-half RoPE on Q and K.
+ * Q/K: bf16 [m, heads, head_dim] with token strides ldq/ldk (elements; rows of
+ * heads*head_dim contiguous); outputs may alias inputs.
+ * norm_span 0 = row: RMSNorm over heads*head_dim with q_weight/k_weight [heads*head_dim],
+ *   then h*(1+scale) and +shift ([heads*head_dim] bf16, bf16 after each step)
+ *   -- rms_adaln (h3serve/native_engine/model/kernels.py:7586-7634, eager order
+ *   :7623-7631; comfy rms_adaln eager/adaln.py:132) fused with the rope below.
+ * norm_span 1 = head: per-head RMSNorm with [head_dim] weights
+ *   -- rms_rope_split_half(_) (__init__.py:549-580; eager/rope.py:67-143;
+ *   CUDA backends/cuda/ops/rms_rope.cu:36-229, launcher :353-384). scale/shift,
+ *   when non-NULL, are applied per row after the norm.
+ * RoPE: freqs fp32 [m, rot_dim/2, 2, 2] packed [[cos,-sin],[sin,cos]]
+ *   (h3serve/native_engine/model/layers.py:61-69); pair i couples element i and
+ *   i + rot_dim/2 of each head (eager/rope.py:39-42); rot_dim 0 means head_dim;
+ *   dims >= rot_dim pass through.
+ * Supported: head_dim == 128, rot_dim % 16 == 0, heads <= 32, 16-byte aligned rows.
+ */
+H3B200_API int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk, void* q_out, int64_t ldqo,
+                          void* k_out, int64_t ldko, const float* freqs, const void* q_weight, const void* k_weight,
+                          const void* scale, const void* shift, int64_t m, int64_t heads, int64_t head_dim,
+                          int64_t rot_dim, int norm_span, float eps, h3b200_stream_t stream);
+
+/*
+ * W4A8: decode packed uint4 weights to the int8 grid,
+ * clamp(rne((u - 8) * s_rel[row, group]), -127, 127), even column = low nibble.
+ * Replaces _C.dequant_int4_grouped_to_int8 (dlpack_bindings.cpp:2781-2790;
+ * kernel backends/cuda/ops/w4a8_gemm.cu:36-90; eager eager/w4a8_int8.py:344-363).
+ * qdata: int8 [n, k/2]; s_rel: fp32 [n, k/group]; out: int8 [n, k].
+ */
+H3B200_API int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k,
+                                        int64_t group_size, int8_t* out, h3b200_stream_t stream);
+
+/*
+ * ConvRot (regular Hadamard, group 256) + per-row INT8 quantization, with an
+ * optional activation applied first.
+ * Replaces _C.quantize_int8_rowwise_convrot / quantize_int8_rowwise_convrot64
+ * (dlpack_bindings.cpp:2835; kernels backends/cuda/ops/int8_linear.cu:256-340,
+ * 942-1027; eager quantize_and_rotate_rowwise eager/quantization.py:878-895).
+ * The rotated row is rounded to bf16 before quantization, as the reference's
+ * bf16 rotation matmul does. k % 256 == 0.
+ */
+H3B200_API int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, int64_t k, int64_t ldx, int64_t group_size,
+                                         int act, int8_t* q, float* scale, h3b200_stream_t stream);
+
+/*
+ * W4A8 INT8 linear with asymmetric group correction:
+ *   xr, xq, xs = convrot-quantize(act(x)); acc = xq . grid^T;
+ *   out = bf16(bf16(acc * (xs * s_channel)) + (bf16(bf16(sum_g xq) * bf16(xs)) . correction))
+ * Replaces comfy_kitchen w4a8_int8_linear (tensor/w4a8_int8.py:89-115; CUDA
+ * backends/cuda/__init__.py:2139-2298, asymmetric correction :2294-2297).
+ * grid: int8 [n, k] decoded weight (h3b200_dequant_int4_grouped_to_int8);
+ * s_channel: fp32 [n]; correction: bf16 [k/group, n] or NULL (symmetric).
+ * workspace: h3b200_w4a8_linear_workspace_bytes(m, k, group) bytes.
+ */
+H3B200_API int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t k, int64_t group_size);
+H3B200_API int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
+                            const void* correction, int64_t group_size, int64_t convrot_group, int act, void* out,
+                            int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                            h3b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B200_H_ */

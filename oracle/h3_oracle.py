@@ -1,0 +1,469 @@
+"""NumPy restatement of X-MinimaxH3's quantized DiT-block hot path.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``). Every function restates
+the reference eager algorithm (comfy_kitchen 0.2.28 vendored at
+``backends/turbo/vendor/comfy_kitchen``; paths below are relative to that
+directory unless they start with ``h3serve/``) with explicit IEEE fp32 and bf16
+round-to-nearest-even steps, so the result is a deterministic function of the
+inputs and does not depend on the host CPU's vector width.
+
+bf16 tensors are carried as ``uint16`` bit patterns; ``bf16_to_f32`` and
+``f32_to_bf16`` convert. Integer work (int8 quantization, int32 accumulators)
+is exact. Floating work reproduces the reference operation order; the only
+places where the reference itself is not a pure function of IEEE arithmetic are
+documented where they occur:
+
+* ``torch.nn.functional.gelu(approximate="tanh")`` on CPU evaluates tanh with
+  SLEEF ``tanhf_u10`` (torch 2.11 ATen ``GeluKernel`` vector path), which is
+  faithfully rounded and saturates to +-1 above |x| > 8.664339742. The oracle
+  uses a double-precision tanh rounded to fp32 plus the same saturation; the
+  golden table ``tests/golden/gelu_tanh_bf16_all.npz`` pins it on all 65,536
+  bf16 inputs.
+* ``torch.nn.functional.rms_norm`` sums x^2 in fp32 in an ISA-dependent order.
+  The oracle sums in float64 and rounds the mean to fp32 once (error below the
+  reference's own), so rare last-bit differences against the reference remain
+  and are checked under the float tolerance.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+__all__ = [
+    "bf16_to_f32",
+    "f32_to_bf16",
+    "quantize_int8_rowwise",
+    "quantize_int8_rowwise_given_absmax",
+    "gelu_tanh_bf16",
+    "int8_matmul_accumulate",
+    "dequant_epilogue",
+    "int8_linear",
+    "gated_residual",
+    "w8a8_gelu_mlp",
+    "rms_norm_row",
+    "rms_adaln",
+    "rope_split_half",
+    "adaln_rms_rope",
+    "rms_rope_split_half",
+    "rope_axis_inv_freq",
+    "rope_grid_table",
+    "build_hadamard",
+    "rotate_activation",
+    "decode_int4_grouped_to_int8",
+    "w4a8_int8_linear_quantized",
+    "w4a8_quantize_weight",
+    "GELU_TANH_SATURATION",
+]
+
+F32 = np.float32
+
+# ---------------------------------------------------------------------------
+# bf16 <-> fp32
+# ---------------------------------------------------------------------------
+
+
+def bf16_to_f32(u16: np.ndarray) -> np.ndarray:
+    """Widen bf16 bit patterns (uint16) to fp32 exactly."""
+    u16 = np.ascontiguousarray(u16, dtype=np.uint16)
+    return (u16.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f: np.ndarray) -> np.ndarray:
+    """Round fp32 to bf16 (round-to-nearest-even), returning uint16 bit patterns.
+
+    Same rounding as torch's ``c10::BFloat16`` conversion (NaN -> 0x7FC0)."""
+    f = np.ascontiguousarray(f, dtype=np.float32)
+    u = f.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(f)
+    if nan.any():
+        r[nan] = 0x7FC0
+    return r
+
+
+def _bf16_round(f: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 -> fp32 (the value a bf16 store leaves behind)."""
+    return bf16_to_f32(f32_to_bf16(f))
+
+
+# ---------------------------------------------------------------------------
+# (a) per-token absmax INT8 quantizer
+# ---------------------------------------------------------------------------
+
+
+def _quantize_rows(xf: np.ndarray, absmax: np.ndarray):
+    # scale = (absmax.float() / 127).clamp(min=1e-30)      eager/quantization.py:872
+    scale = np.maximum((absmax.astype(np.float32) / F32(127.0)).astype(np.float32), F32(1e-30))
+    scale = scale.astype(np.float32)
+    # _int8_scale_for_math: scale.to(x.dtype), 0 -> tiny      eager/quantization.py:815-818
+    sb = _bf16_round(scale)
+    sb = np.where(sb == 0, np.float32(np.finfo(np.float32).tiny), sb).astype(np.float32)
+    # x / scale in bf16 (fp32 divide, bf16 store), then round_() + clamp_()   :821-826, :874
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        quo = _bf16_round((xf / sb).astype(np.float32))
+    q = np.clip(np.rint(quo), -128.0, 127.0).astype(np.int8)
+    return q, scale
+
+
+def quantize_int8_rowwise(x_bf16: np.ndarray):
+    """Per-row absmax INT8 quantization.
+
+    Follows ``quantize_int8_rowwise`` eager/quantization.py:857-875 (CUDA twin
+    backends/cuda/ops/int8_linear.cu:157-200): row absmax in bf16 (exact),
+    ``scale = max(absmax/127, 1e-30)`` in fp32, quotient ``x / bf16(scale)``
+    stored as bf16, round-half-even, clamp to [-128, 127].
+
+    Returns (int8 [..., K], fp32 scale [..., 1]).
+    """
+    xf = bf16_to_f32(x_bf16)
+    absmax = np.abs(xf).max(axis=-1, keepdims=True) if xf.shape[-1] else np.zeros(xf.shape[:-1] + (1,), np.float32)
+    return _quantize_rows(xf, absmax)
+
+
+def quantize_int8_rowwise_given_absmax(x_bf16: np.ndarray, absmax: np.ndarray):
+    """Quantizer body with a precomputed row absmax (fp32 [..., 1]).
+
+    Same arithmetic as ``quantize_int8_rowwise``; the fused MLP computes the
+    absmax inside the fc1 epilogue and quantizes fc2's input with it."""
+    return _quantize_rows(bf16_to_f32(x_bf16), np.asarray(absmax, np.float32))
+
+
+# ---------------------------------------------------------------------------
+# tanh-GELU on bf16 (input_act="gelu_tanh")
+# ---------------------------------------------------------------------------
+
+GELU_TANH_SATURATION = F32(8.664339742)
+_GELU_BETA = F32(np.sqrt(2.0) * (2.0 / np.sqrt(np.pi)) * 0.5)
+_GELU_KAPPA = F32(0.044715)
+
+
+def gelu_tanh_bf16(x_bf16: np.ndarray) -> np.ndarray:
+    """tanh-GELU of bf16 values, returned as bf16 bits.
+
+    ``apply_input_act(x, "gelu_tanh")`` backends/_activations.py:40-53 calls
+    ``torch.nn.functional.gelu(x, approximate="tanh")``. On a bf16 CPU tensor
+    torch 2.11 (ATen ``GeluKernel``, tanh branch, reduced-float path) computes in
+    fp32, left to right, without fused multiply-add::
+
+        cube  = (x * x) * x
+        inner = beta * (x + kappa * cube)        beta = f32(sqrt(2)*2/sqrt(pi)*0.5)
+        out   = (0.5 * x) * (1 + tanh(inner))    kappa = f32(0.044715)
+
+    and stores bf16. tanh is SLEEF ``tanhf_u10``: faithfully rounded, exactly
+    +-1 for |inner| > 8.664339742. Restated with a double tanh rounded to fp32.
+    """
+    x = bf16_to_f32(x_bf16)
+    with np.errstate(all="ignore"):
+        cube = ((x * x).astype(np.float32) * x).astype(np.float32)
+        inner = (_GELU_BETA * (x + (_GELU_KAPPA * cube).astype(np.float32)).astype(np.float32)).astype(np.float32)
+        t = np.tanh(inner.astype(np.float64)).astype(np.float32)
+        t = np.where(np.abs(inner) > GELU_TANH_SATURATION, np.copysign(F32(1.0), inner), t).astype(np.float32)
+        out = ((F32(0.5) * x).astype(np.float32) * (F32(1.0) + t).astype(np.float32)).astype(np.float32)
+    return f32_to_bf16(out)
+
+
+# ---------------------------------------------------------------------------
+# INT8 GEMM + dequant epilogue
+# ---------------------------------------------------------------------------
+
+
+def int8_matmul_accumulate(a_i8: np.ndarray, w_i8: np.ndarray, row_chunk: int = 4096) -> np.ndarray:
+    """int32 accumulators ``A[M,K] @ W[N,K]^T``.
+
+    ``_int8_matmul_accumulate`` eager/quantization.py:749-783 (``torch._int_mm``).
+    Evaluated as a float64 GEMM: every partial sum is an integer below 2^53
+    (|acc| <= 2^14 * K), so the result is exact whatever the summation order.
+    """
+    a = np.asarray(a_i8)
+    w = np.asarray(w_i8)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"K mismatch: {k} vs {w.shape[1]}")
+    if k > (1 << 24):
+        raise ValueError("K too large for the exact float64 accumulation")
+    wt = w.astype(np.float64).T.copy()
+    out = np.empty((m, n), dtype=np.int32)
+    for s in range(0, m, row_chunk):
+        out[s:s + row_chunk] = (a[s:s + row_chunk].astype(np.float64) @ wt).astype(np.int32)
+    return out
+
+
+def dequant_epilogue(acc: np.ndarray, x_scale: np.ndarray, w_scale: np.ndarray, bias_bf16=None) -> np.ndarray:
+    """``bf16(float(acc) * (x_scale[m] * w_scale[n]))`` (+ bf16 bias).
+
+    eager/quantization.py:1034-1053: the row and channel scales are multiplied
+    first (fp32), then the int32 accumulator is converted to fp32 and scaled,
+    then stored as bf16; bias is added to the bf16 result in bf16."""
+    xs = np.asarray(x_scale, np.float32).reshape(-1, 1)
+    ws = np.asarray(w_scale, np.float32).reshape(1, -1)
+    s = (xs * ws).astype(np.float32)
+    out = _bf16_round((acc.astype(np.float32) * s).astype(np.float32))
+    if bias_bf16 is not None:
+        out = _bf16_round((out + bf16_to_f32(bias_bf16).reshape(1, -1)).astype(np.float32))
+    return f32_to_bf16(out)
+
+
+def int8_linear(x_bf16, w_i8, w_scale, bias_bf16=None, input_act=None):
+    """``int8_linear(x, weight, weight_scale, bias, bf16, convrot=False, input_act)``.
+
+    eager/quantization.py:971-1056: optional activation on the bf16 input,
+    per-row quantization, int32 GEMM, dequant epilogue. Returns bf16 bits."""
+    x = np.asarray(x_bf16, np.uint16)
+    if input_act == "gelu_tanh":
+        x = gelu_tanh_bf16(x)
+    elif input_act not in (None, "none"):
+        raise ValueError(f"unsupported input_act {input_act!r}")
+    q, s = quantize_int8_rowwise(x)
+    acc = int8_matmul_accumulate(q, w_i8)
+    return dequant_epilogue(acc, s, w_scale, bias_bf16)
+
+
+def gated_residual(residual_bf16, y_bf16, gate_bf16):
+    """``residual.clone().addcmul_(y, gate)`` in bf16.
+
+    h3serve/native_engine/model/fused_mlp.py:414-425 (``addcmul_`` per segment).
+    torch's reduced-float CPU addcmul evaluates ``self + (1*y)*gate`` in fp32
+    with separate multiply and add, then stores bf16."""
+    r = bf16_to_f32(residual_bf16)
+    y = bf16_to_f32(y_bf16)
+    g = bf16_to_f32(gate_bf16).reshape(1, -1)
+    p = (y * g).astype(np.float32)
+    return f32_to_bf16((r + p).astype(np.float32))
+
+
+def w8a8_gelu_mlp(x_bf16, w1_i8, s1, w2_i8, s2, gate_bf16, residual_bf16, return_intermediates=False):
+    """Gated tanh-GELU W8A8 MLP: fc1 -> GELU -> per-token requant -> fc2 -> gated residual.
+
+    Composition of reference operators (``int8_linear`` twice, the second with
+    ``input_act="gelu_tanh"``, then ``addcmul_``), as in
+    h3serve/native_engine/model/fused_mlp.py:393-425 with the activation
+    replaced by tanh-GELU (backends/_activations.py:19-24)."""
+    h = int8_linear(x_bf16, w1_i8, s1)
+    a = gelu_tanh_bf16(h)
+    q2, xs2 = quantize_int8_rowwise(a)
+    acc2 = int8_matmul_accumulate(q2, w2_i8)
+    y = dequant_epilogue(acc2, xs2, s2)
+    out = gated_residual(residual_bf16, y, gate_bf16)
+    if return_intermediates:
+        return out, {"h": h, "a": a, "q2": q2, "xs2": xs2, "acc2": acc2, "y": y}
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (c) AdaLN-modulate + RMSNorm + split-half RoPE
+# ---------------------------------------------------------------------------
+
+
+def _rms_rstd(xf: np.ndarray, eps: float) -> np.ndarray:
+    ms = (np.square(xf.astype(np.float64)).sum(axis=-1, keepdims=True) / xf.shape[-1]).astype(np.float32)
+    v = (ms + F32(eps)).astype(np.float32)
+    return (F32(1.0) / np.sqrt(v).astype(np.float32)).astype(np.float32)
+
+
+def rms_norm_row(x_bf16, weight_bf16, eps=1e-6):
+    """``F.rms_norm(x, (D,), weight, eps)`` on bf16.
+
+    torch 2.11 CPU: mean(x^2) in fp32, ``rstd = 1/sqrt(mean + eps)``, result
+    ``(x * rstd) * weight`` in fp32, one bf16 store (h3serve/native_engine/model/
+    layers.py:43-48; kernels.py:7623). The oracle sums x^2 in float64."""
+    xf = bf16_to_f32(x_bf16)
+    rstd = _rms_rstd(xf, eps)
+    w = bf16_to_f32(weight_bf16)
+    return f32_to_bf16(((xf * rstd).astype(np.float32) * w).astype(np.float32))
+
+
+def rms_adaln(x_bf16, weight_bf16, scale_bf16, shift_bf16, eps=1e-6):
+    """RMSNorm with weight, then ``mul_(1 + scale)``, then ``add_(shift)``, bf16 after each.
+
+    h3serve/native_engine/model/kernels.py:7623-7631 (eager order of ``rms_adaln``):
+    ``hidden = norm(value); hidden.mul_(1.0 + scale.to(bf16)).add_(shift.to(bf16))``."""
+    h = bf16_to_f32(rms_norm_row(x_bf16, weight_bf16, eps))
+    one_plus = _bf16_round((F32(1.0) + bf16_to_f32(scale_bf16)).astype(np.float32))
+    h = _bf16_round((h * one_plus).astype(np.float32))
+    h = _bf16_round((h + bf16_to_f32(shift_bf16)).astype(np.float32))
+    return f32_to_bf16(h)
+
+
+def rope_split_half(x_bf16, table_f32, rot_dim=0):
+    """Split-half RoPE per head.
+
+    ``apply_rope_split_half1`` eager/rope.py:39-42 with the partial-rotary rule
+    of ``_rms_rope1`` eager/rope.py:67-92. x: bf16 [M, H, D]; table: fp32
+    [M, rot_dim/2, 2, 2] packed ``[[cos, -sin], [sin, cos]]``
+    (h3serve/native_engine/model/layers.py:61-69). Pair i couples element i and
+    i + rot_dim/2: ``y0 = t00*x0 + t01*x1``, ``y1 = t10*x0 + t11*x1`` in fp32
+    (two products, one add), then bf16."""
+    x = bf16_to_f32(x_bf16)
+    m, h, d = x.shape
+    rd = d if rot_dim in (0, d) else rot_dim
+    half = rd // 2
+    t = np.asarray(table_f32, np.float32).reshape(m, 1, half, 2, 2)
+    x0 = x[..., :half]
+    x1 = x[..., half:rd]
+    y0 = ((t[..., 0, 0] * x0).astype(np.float32) + (t[..., 0, 1] * x1).astype(np.float32)).astype(np.float32)
+    y1 = ((t[..., 1, 0] * x0).astype(np.float32) + (t[..., 1, 1] * x1).astype(np.float32)).astype(np.float32)
+    out = np.concatenate([y0, y1, x[..., rd:]], axis=-1).astype(np.float32)
+    return f32_to_bf16(out)
+
+
+def adaln_rms_rope(q_bf16, k_bf16, table_f32, q_weight, k_weight, scale, shift, eps=1e-6, norm_span="row", rot_dim=0):
+    """Fused AdaLN-modulate + RMSNorm + split-half RoPE on Q and K ([M, H, D] bf16).
+
+    ``norm_span="row"``: ``rms_adaln`` over the H*D row (kernels.py:7586-7634 eager
+    order), then per-head RoPE. ``norm_span="head"``: per-head RMSNorm with a
+    [D] weight (``rms_rope_split_half``, eager/rope.py:129-143) and the same
+    modulation applied per row afterwards when ``scale``/``shift`` are given.
+    Returns (q_out, k_out) bf16 bits."""
+    outs = []
+    for x, w in ((q_bf16, q_weight), (k_bf16, k_weight)):
+        m, h, d = x.shape
+        if norm_span == "row":
+            y = rms_adaln(x.reshape(m, h * d), w, scale, shift, eps).reshape(m, h, d)
+        elif norm_span == "head":
+            y = rms_norm_row(x, w, eps)
+            if scale is not None:
+                yf = bf16_to_f32(y).reshape(m, h * d)
+                one_plus = _bf16_round((F32(1.0) + bf16_to_f32(scale)).astype(np.float32))
+                yf = _bf16_round((yf * one_plus).astype(np.float32))
+                yf = _bf16_round((yf + bf16_to_f32(shift)).astype(np.float32))
+                y = f32_to_bf16(yf).reshape(m, h, d)
+        else:
+            raise ValueError(f"norm_span must be 'row' or 'head', got {norm_span!r}")
+        outs.append(rope_split_half(y, table_f32, rot_dim))
+    return outs[0], outs[1]
+
+
+def rms_rope_split_half(q_bf16, k_bf16, table_f32, q_weight, k_weight=None, eps=1e-6, rot_dim=0):
+    """``rms_rope_split_half(q, k, freqs, q_scale, k_scale, eps, rot_dim)`` eager/rope.py:129-143."""
+    if k_weight is None:
+        k_weight = q_weight
+    return adaln_rms_rope(q_bf16, k_bf16, table_f32, q_weight, k_weight, None, None, eps, "head", rot_dim)
+
+
+def rope_axis_inv_freq(dim: int, base: float = 10000.0) -> np.ndarray:
+    """``1 / base^(arange(0, dim, 2) / dim)`` for one RoPE axis of width ``dim`` (float64, rounded to fp32)."""
+    return (1.0 / (base ** (np.arange(0, dim, 2, dtype=np.float64) / dim))).astype(np.float32)
+
+
+def rope_grid_table(grid, dims=(44, 42, 42), base=10000.0, token_slice=None) -> np.ndarray:
+    """Packed split-half rotation table for a (t, h, w) token grid, fp32 [M, sum(dims)/2, 2, 2].
+
+    Positions are the row-major (t, h, w) meshgrid; each axis contributes
+    ``pos * inv_freq`` angles (h3serve/native_engine/model/layers.py:51-58, with a
+    per-axis frequency width), and the table packs ``[[cos, -sin], [sin, cos]]``
+    (layers.py:61-69). ``token_slice`` restricts to a contiguous token range.
+    The table is an input to the kernels, not part of their measured work."""
+    t, h, w = grid
+    m = t * h * w
+    lo, hi = (0, m) if token_slice is None else token_slice
+    idx = np.arange(lo, hi, dtype=np.int64)
+    pos = np.stack([idx // (h * w), (idx // w) % h, idx % w], axis=1).astype(np.float32)
+    angs = [pos[:, a:a + 1] * rope_axis_inv_freq(d, base)[None, :] for a, d in enumerate(dims)]
+    ang = np.concatenate(angs, axis=1).astype(np.float32)
+    c = np.cos(ang.astype(np.float64)).astype(np.float32)
+    s = np.sin(ang.astype(np.float64)).astype(np.float32)
+    return np.stack([c, -s, s, c], axis=-1).reshape(hi - lo, ang.shape[1], 2, 2).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# W4A8 (asymmetric grouped int4 weights, ConvRot-256 activations)
+# ---------------------------------------------------------------------------
+
+
+def build_hadamard(size: int = 256) -> np.ndarray:
+    """Normalized regular Hadamard matrix H4^(x)n / sqrt(size) (tensor/int8_utils.py:11-38)."""
+    if size < 4 or size & (size - 1) or (size.bit_length() - 1) % 2:
+        raise ValueError(f"Regular Hadamard size must be a power of 4, got {size}")
+    h4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], dtype=np.float64)
+    h = h4
+    while h.shape[0] < size:
+        h = np.kron(h, h4)
+    return h / np.sqrt(size)
+
+
+def rotate_activation(x_bf16, group_size: int = 256) -> np.ndarray:
+    """ConvRot online rotation ``x_grouped @ H`` per group, bf16 out (tensor/int8_utils.py:58-74).
+
+    The reference runs a bf16 matmul with fp32 accumulation; the oracle forms the
+    exact sum in float64 and rounds to fp32 then bf16, so last-bit differences
+    against the reference are possible and checked under tolerance."""
+    x = bf16_to_f32(x_bf16).astype(np.float64)
+    k = x.shape[-1]
+    if k % group_size:
+        raise ValueError(f"features {k} not divisible by group_size {group_size}")
+    hm = build_hadamard(group_size)
+    y = (x.reshape(-1, k // group_size, group_size) @ hm).reshape(x.shape)
+    return f32_to_bf16(y.astype(np.float32))
+
+
+def decode_int4_grouped_to_int8(qdata_i8, s_rel_f32, group_size: int) -> np.ndarray:
+    """Decode packed uint4 to the int8 grid: ``clamp(rne((u - 8) * s_rel), -127, 127)``.
+
+    ``_dequant_int4_grouped_to_int8`` eager/w4a8_int8.py:344-363 (even column =
+    low nibble; fp32 ``s_rel`` per (row, group)); CUDA twin
+    backends/cuda/ops/w4a8_gemm.cu:36-90."""
+    p = np.asarray(qdata_i8).view(np.uint8).astype(np.int32)
+    n, kh = p.shape
+    k = kh * 2
+    u = np.empty((n, k), dtype=np.int32)
+    u[:, 0::2] = p & 0xF
+    u[:, 1::2] = (p >> 4) & 0xF
+    vals = (u.astype(np.float32) - F32(8.0)).reshape(n, k // group_size, group_size)
+    vals = (vals * np.asarray(s_rel_f32, np.float32)[..., None]).astype(np.float32)
+    return np.clip(np.rint(vals), -127, 127).astype(np.int8).reshape(n, k)
+
+
+def w4a8_int8_linear_quantized(x_bf16, qdata_i8, s_rel, s_channel, correction_bf16, group_size=128,
+                               convrot_groupsize=256, return_intermediates=False):
+    """W4A8 linear with quantized activations (the reference's CUDA route).
+
+    backends/cuda/__init__.py:2139-2298 for asymmetric weights: ConvRot-rotate and
+    row-quantize x, decode the int4 weight to the int8 grid, int32 GEMM, dequant
+    ``bf16(acc * (xs * s_channel))``, then the asymmetric correction
+    ``out + bf16(bf16(sum_g xq) * bf16(xs)) @ correction`` (:2294-2297) accumulated
+    in fp32 and rounded once. The eager reference (eager/w4a8_int8.py:481-492)
+    instead dequantizes the weight to bf16 and runs a bf16 ``F.linear`` on the
+    unquantized input; the two agree within the float tolerance."""
+    xr = rotate_activation(x_bf16, convrot_groupsize)
+    xq, xs = quantize_int8_rowwise(xr)
+    wgrid = decode_int4_grouped_to_int8(qdata_i8, s_rel, group_size)
+    acc = int8_matmul_accumulate(xq, wgrid)
+    out = bf16_to_f32(dequant_epilogue(acc, xs, s_channel))
+    if correction_bf16 is not None:
+        m, k = xq.shape
+        gs = xq.astype(np.int32).reshape(m, k // group_size, group_size).sum(-1)
+        sx = _bf16_round(_bf16_round(gs.astype(np.float32)) * _bf16_round(xs.astype(np.float32)))
+        corr = bf16_to_f32(correction_bf16).astype(np.float64)
+        out = (out.astype(np.float64) + sx.astype(np.float64) @ corr).astype(np.float32)
+    res = f32_to_bf16(out)
+    if return_intermediates:
+        return res, {"xr": xr, "xq": xq, "xs": xs, "wgrid": wgrid, "acc": acc}
+    return res
+
+
+def w4a8_quantize_weight(w_bf16, group_size=128, convrot_groupsize=256):
+    """Asymmetric W4A8 weight preparation (offline), float32 ``s_rel``, no codebook.
+
+    ``quantize_w4a8_int8_weight(symmetric=False, codebook=False,
+    scale_dtype=float32)`` eager/w4a8_int8.py:315-341 -> :122-209 (asymmetric
+    branch :175-186, ``s_channel``/``s_rel`` :188-191, packing :200-202), after the
+    offline ConvRot rotation ``W @ H^T`` per 256-group (tensor/int8_utils.py:41-55,
+    a bf16 matmul in the reference; float64 here). Returns
+    (qdata int8 [N, K/2], s_rel fp32 [N, K/g], s_channel fp32 [N], correction bf16 [K/g, N])."""
+    w = bf16_to_f32(w_bf16).astype(np.float64)
+    n, k = w.shape
+    hm = build_hadamard(convrot_groupsize)
+    wr = bf16_to_f32(f32_to_bf16((w.reshape(n, k // convrot_groupsize, convrot_groupsize) @ hm.T)
+                                 .reshape(n, k).astype(np.float32)))
+    g = wr.astype(np.float32).reshape(n, k // group_size, group_size)
+    mn = g.min(-1, keepdims=True)
+    gsc = np.maximum(((g.max(-1, keepdims=True) - mn) / F32(15.0)).astype(np.float32), F32(1e-8))
+    u = np.clip(np.rint(((g - mn) / gsc).astype(np.float32)), 0, 15).astype(np.int32)
+    shifted = ((u - 8).astype(np.float32) * gsc).astype(np.float32)
+    corr = f32_to_bf16((F32(8.0) * gsc + mn).astype(np.float32).squeeze(-1).T.copy())
+    s_ch = np.maximum((np.abs(shifted).max(axis=(1, 2)) / F32(127.0)).astype(np.float32), F32(1e-8))
+    s_rel = (gsc.squeeze(-1) / s_ch[:, None]).astype(np.float32)
+    u = u.reshape(n, k)
+    packed = ((u[:, 0::2] & 0xF) | ((u[:, 1::2] & 0xF) << 4)).astype(np.uint8).view(np.int8)
+    return packed, s_rel, s_ch.astype(np.float32), corr

@@ -1,0 +1,184 @@
+"""Generate golden vectors by running X-MinimaxH3's own eager implementation.
+
+Run once in a container where the reference checkout is importable:
+
+    python tests/golden/make_golden.py --reference <path-to-X-MinimaxH3>
+
+It imports the reference's vendored ``comfy_kitchen`` eager backend and the
+``h3serve`` model helpers (nothing is copied), draws seeded synthetic inputs,
+runs the reference functions on CPU and writes compressed ``.npz`` fixtures next
+to this file. bf16 tensors are stored as uint16 bit patterns. The tests and the
+GPU parity checks read only the fixtures; the reference is never needed at run
+time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def b16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    args = ap.parse_args()
+    ref = os.path.abspath(args.reference)
+    sys.path.insert(0, os.path.join(ref, "backends", "turbo", "vendor"))
+    sys.path.insert(0, ref)
+
+    from comfy_kitchen.backends._activations import apply_input_act
+    from comfy_kitchen.backends.eager import quantization as eq
+    from comfy_kitchen.backends.eager import rope as erope
+    from comfy_kitchen.backends.eager import w4a8_int8 as ew4
+    from comfy_kitchen.tensor.int8_utils import _build_hadamard
+    from h3serve.native_engine.model import layers as h3layers
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    out = {}
+
+    # 1. tanh-GELU on every bf16 bit pattern.
+    allb = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    out["gelu_tanh_bf16_all"] = {"y": b16(apply_input_act(allb.clone(), "gelu_tanh"))}
+
+    # 2. Row quantizer: config-0 activations plus edge rows.
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(256, 3072, generator=g).to(torch.bfloat16)
+    x[3] = 0                      # all-zero row -> scale clamps to 1e-30
+    x[5, 7] = 1e4                 # one dominant value
+    x[6] *= 1e-20                 # tiny row
+    x[7, :] = -2.5                # constant row, ties at the clamp
+    x[8, ::2] = 0.5
+    x[9, 100] = -3.0e38           # near bf16 max
+    q, s = eq.quantize_int8_rowwise(x)
+    g2 = torch.Generator().manual_seed(11)
+    ragged = (torch.randn(37, 40, generator=g2) * 3).to(torch.bfloat16)   # odd rows, K % 16 != 0
+    rq, rs = eq.quantize_int8_rowwise(ragged)
+    one = (torch.randn(1, 12288, generator=g2)).to(torch.bfloat16)
+    oq, os_ = eq.quantize_int8_rowwise(one)
+    out["quantize_rowwise"] = {
+        "x": b16(x), "q": q.numpy(), "s": s.numpy(),
+        "x_ragged": b16(ragged), "q_ragged": rq.numpy(), "s_ragged": rs.numpy(),
+        "x_one": b16(one), "q_one": oq.numpy(), "s_one": os_.numpy(),
+    }
+
+    # 3. W8A8 linear, config-0 slice: x [256,3072] seed 1, W rows 0..383 of the seed-0 weight.
+    gw = torch.Generator().manual_seed(0)
+    w = (torch.randn(12288, 3072, generator=gw) * 0.02).to(torch.bfloat16)[:384].contiguous()
+    wq, ws = eq.quantize_int8_rowwise(w)
+    ws = ws.reshape(-1)
+    gx = torch.Generator().manual_seed(1)
+    x0 = torch.randn(256, 3072, generator=gx).to(torch.bfloat16)
+    xq, xs = eq.quantize_int8_rowwise(x0)
+    acc = eq._int8_matmul_accumulate(xq, wq.T.contiguous())
+    y = eq.int8_linear(x0, wq, ws, None, torch.bfloat16)
+    gb = torch.Generator().manual_seed(5)
+    bias = torch.randn(384, generator=gb).to(torch.bfloat16)
+    yb = eq.int8_linear(x0, wq, ws, bias, torch.bfloat16)
+    ya = eq.int8_linear(x0, wq, ws, None, torch.bfloat16, input_act="gelu_tanh")
+    out["linear_cfg0_slice"] = {
+        "w_bf16": b16(w), "wq": wq.numpy(), "ws": ws.numpy(), "x": b16(x0), "xq": xq.numpy(),
+        "xs": xs.numpy(), "acc": acc.numpy(), "y": b16(y), "bias": b16(bias), "y_bias": b16(yb),
+        "y_gelu_in": b16(ya),
+    }
+
+    # 4. Gated tanh-GELU W8A8 MLP at reduced width (d=256, ffn=1024, M=100).
+    gm = torch.Generator().manual_seed(2)
+    d, ffn, m = 256, 1024, 100
+    w1 = (torch.randn(ffn, d, generator=gm) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(d, ffn, generator=gm) * 0.02).to(torch.bfloat16)
+    xm = torch.randn(m, d, generator=gm).to(torch.bfloat16)
+    gate = torch.randn(d, generator=gm).to(torch.bfloat16)
+    resid = torch.randn(m, d, generator=gm).to(torch.bfloat16)
+    w1q, s1 = eq.quantize_int8_rowwise(w1)
+    w2q, s2 = eq.quantize_int8_rowwise(w2)
+    s1, s2 = s1.reshape(-1), s2.reshape(-1)
+    h = eq.int8_linear(xm, w1q, s1, None, torch.bfloat16)
+    a = apply_input_act(h, "gelu_tanh")
+    q2, xs2 = eq.quantize_int8_rowwise(a)
+    acc2 = eq._int8_matmul_accumulate(q2, w2q.T.contiguous())
+    ym = eq.int8_linear(h, w2q, s2, None, torch.bfloat16, input_act="gelu_tanh")
+    om = resid.clone().addcmul_(ym, gate)
+    out["mlp_small"] = {
+        "x": b16(xm), "w1q": w1q.numpy(), "s1": s1.numpy(), "w2q": w2q.numpy(), "s2": s2.numpy(),
+        "gate": b16(gate), "residual": b16(resid), "h": b16(h), "a": b16(a), "q2": q2.numpy(),
+        "xs2": xs2.numpy(), "acc2": acc2.numpy(), "y": b16(ym), "out": b16(om),
+    }
+
+    # 5. AdaLN-modulate + RMSNorm + 3-D split-half RoPE, 24x128 heads, grid (2,5,8).
+    gr = torch.Generator().manual_seed(4)
+    grid = (2, 5, 8)
+    mt = grid[0] * grid[1] * grid[2]
+    qn = torch.randn(mt, 24, 128, generator=gr).to(torch.bfloat16)
+    kn = torch.randn(mt, 24, 128, generator=gr).to(torch.bfloat16)
+    shift = (torch.randn(3072, generator=gr) * 0.1).to(torch.bfloat16)
+    scale = (torch.randn(3072, generator=gr) * 0.1).to(torch.bfloat16)
+    wq_ = (1 + 0.02 * torch.randn(3072, generator=gr)).to(torch.bfloat16)
+    wk_ = (1 + 0.02 * torch.randn(3072, generator=gr)).to(torch.bfloat16)
+    wqh = (1 + 0.02 * torch.randn(128, generator=gr)).to(torch.bfloat16)
+    wkh = (1 + 0.02 * torch.randn(128, generator=gr)).to(torch.bfloat16)
+    tt, hh, ww = torch.meshgrid(torch.arange(grid[0]), torch.arange(grid[1]), torch.arange(grid[2]), indexing="ij")
+    pos = torch.stack([tt.reshape(-1), hh.reshape(-1), ww.reshape(-1)], dim=1)
+    invs = [1.0 / (10000.0 ** (torch.arange(0, dd, 2, dtype=torch.float32) / dd)) for dd in (44, 42, 42)]
+    half = torch.cat([pos[:, i:i + 1].float() * invs[i].reshape(1, -1) for i in range(3)], dim=-1)
+    angles = torch.cat((half, half), dim=-1)
+    table = h3layers.rope_rotation_table(angles, torch.float32)   # [1, M, 1, 64, 2, 2]
+
+    class _Norm:  # the RMSNorm call used by kernels.rms_adaln's eager branch
+        def __init__(self, weight):
+            self.weight = weight
+
+        def __call__(self, value):
+            return torch.nn.functional.rms_norm(value, (self.weight.shape[0],), weight=self.weight, eps=1e-6)
+
+    def adaln_rope(xx, wgt):
+        hid = _Norm(wgt)(xx.reshape(mt, 3072))
+        hid.mul_(1.0 + scale.to(hid.dtype)).add_(shift.to(hid.dtype))
+        return erope.apply_rope_split_half1(hid.reshape(1, mt, 24, 128), table)[0]
+
+    qo, ko = adaln_rope(qn, wq_), adaln_rope(kn, wk_)
+    qh, kh = erope.rms_rope_split_half(qn.unsqueeze(0), kn.unsqueeze(0), table, wqh, wkh, 1e-6, 0)
+    qp, kp = erope.rms_rope_split_half(qn.unsqueeze(0), kn.unsqueeze(0), table[..., :48, :, :], wqh, wkh, 1e-6, 96)
+    out["norm_rope"] = {
+        "q": b16(qn), "k": b16(kn), "shift": b16(shift), "scale": b16(scale), "wq": b16(wq_),
+        "wk": b16(wk_), "wq_head": b16(wqh), "wk_head": b16(wkh), "grid": np.array(grid),
+        "table": table.reshape(mt, 64, 2, 2).numpy(), "q_out": b16(qo), "k_out": b16(ko),
+        "q_head": b16(qh[0]), "k_head": b16(kh[0]), "q_partial96": b16(qp[0]), "k_partial96": b16(kp[0]),
+    }
+
+    # 6. W4A8 asymmetric group-128, fp32 s_rel, ConvRot-256 (N=256, K=512, M=64).
+    g4 = torch.Generator().manual_seed(3)
+    w4 = (torch.randn(256, 512, generator=g4) * 0.02).to(torch.bfloat16)
+    x4 = torch.randn(64, 512, generator=g4).to(torch.bfloat16)
+    qd, srel, sch, corr, cb = ew4.quantize_w4a8_int8_weight(
+        w4, group_size=128, convrot_groupsize=256, symmetric=False, scale_dtype=torch.float32, codebook=False)
+    assert cb is None
+    grid8 = ew4._dequant_int4_grouped_to_int8(qd, srel, None, 128)
+    hmat = _build_hadamard(256, dtype=torch.bfloat16)
+    xr = torch.matmul(x4.reshape(-1, 2, 256), hmat).reshape(64, 512)
+    xq4, xs4 = eq.quantize_and_rotate_rowwise(x4, hmat, 256)
+    acc4 = eq._int8_matmul_accumulate(xq4, grid8.T.contiguous())
+    y4 = ew4.w4a8_int8_linear(x4, qd, srel, sch, None, corr, None, 128, 256, torch.bfloat16)
+    out["w4a8_small"] = {
+        "w_bf16": b16(w4), "x": b16(x4), "qdata": qd.numpy(), "s_rel": srel.numpy(), "s_channel": sch.numpy(),
+        "correction": b16(corr), "grid": grid8.numpy(), "x_rot": b16(xr), "xq": xq4.numpy(), "xs": xs4.numpy(),
+        "acc": acc4.numpy(), "y_eager": b16(y4),
+    }
+
+    for name, arrays in out.items():
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **arrays)
+        print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+
+
+if __name__ == "__main__":
+    main()

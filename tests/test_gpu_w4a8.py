@@ -1,0 +1,60 @@
+"""GPU parity: W4A8 decode (bit-exact), ConvRot quantizer and W4A8 linear (tolerance)."""
+
+import numpy as np
+import pytest
+import torch
+
+import h3b200
+import oracle as O
+from gpu_util import np_, randn_bf16, t2u, u2t
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a = O.bf16_to_f32(a).astype(np.float64)
+    b = O.bf16_to_f32(b).astype(np.float64)
+    return np.linalg.norm(a - b) / np.linalg.norm(b), float(np.abs(a - b).max())
+
+
+def test_decode_golden_bit_exact(golden):
+    g = golden("w4a8_small")
+    grid = h3b200.dequant_int4_grouped_to_int8(torch.from_numpy(g["qdata"]).cuda(),
+                                               torch.from_numpy(g["s_rel"]).cuda(), 128)
+    np.testing.assert_array_equal(np_(grid), g["grid"])
+
+
+def test_convrot_quantize_vs_golden(golden):
+    g = golden("w4a8_small")
+    xq, xs = h3b200.quantize_int8_rowwise_convrot(u2t(g["x"]), 256)
+    same = (np_(xq) == g["xq"]).all(-1)
+    assert same.mean() >= 0.95
+    np.testing.assert_array_equal(np_(xs)[same], g["xs"][same])
+
+
+def test_convrot_quantize_vs_oracle_large():
+    gen = torch.Generator().manual_seed(31)
+    x = randn_bf16((2000, 12288), gen)
+    xq, xs = h3b200.quantize_int8_rowwise_convrot(x.cuda(), 256)
+    oq, os_ = O.quantize_int8_rowwise(O.rotate_activation(t2u(x), 256))
+    rows = (np_(xq) == oq).all(-1)
+    assert rows.mean() >= 0.9                    # fp32 butterfly vs exact rotation: rare bf16 flips
+    assert np.abs(np_(xq).astype(np.int32) - oq).max() <= 1
+
+
+def test_w4a8_linear_vs_reference(golden):
+    g = golden("w4a8_small")
+    y = h3b200.w4a8_int8_linear(u2t(g["x"]), torch.from_numpy(g["qdata"]).cuda(), torch.from_numpy(g["s_rel"]).cuda(),
+                                torch.from_numpy(g["s_channel"]).cuda(), correction=u2t(g["correction"]),
+                                group_size=128, convrot_groupsize=256)
+    rel, mx = rel_l2(t2u(y), g["y_eager"])
+    assert rel <= 1e-2 and mx <= 2e-2
+    o = O.w4a8_int8_linear_quantized(g["x"], g["qdata"], g["s_rel"], g["s_channel"], g["correction"], 128, 256)
+    rel, mx = rel_l2(t2u(y), o)
+    assert rel <= 2e-3
+
+
+def test_w4a8_int32_accumulators_exact(golden):
+    g = golden("w4a8_small")
+    acc = h3b200.mm_int8(torch.from_numpy(g["xq"]).cuda(), torch.from_numpy(g["grid"]).cuda().t())
+    np.testing.assert_array_equal(np_(acc), g["acc"])

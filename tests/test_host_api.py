@@ -1,0 +1,43 @@
+"""Host-side contract of the Python operator surface (CPU, no kernel launches)."""
+
+import pytest
+import torch
+
+import h3b200
+
+
+def test_cpu_tensors_are_rejected_no_fallback():
+    x = torch.zeros(4, 16, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        h3b200.quantize_int8_rowwise(x)
+    w = torch.zeros(8, 16, dtype=torch.int8)
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        h3b200.int8_linear(x, w, torch.ones(8))
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        h3b200.mm_int8(w, w.t())
+
+
+def test_input_act_codes_match_reference():
+    # backends/cuda/input_act_codes.h:13 -- 0 none, 1 gelu_tanh
+    assert h3b200.input_act_code(None) == 0
+    assert h3b200.input_act_code("none") == 0
+    assert h3b200.input_act_code("gelu_tanh") == 1
+    with pytest.raises(ValueError, match="unsupported input_act"):
+        h3b200.input_act_code("relu")
+
+
+def test_stochastic_rounding_not_built():
+    with pytest.raises(NotImplementedError):
+        h3b200.quantize_int8_rowwise(torch.zeros(2, 8, dtype=torch.bfloat16), stochastic_rounding=3)
+
+
+def test_rope_table_builder_matches_oracle():
+    import numpy as np
+
+    import oracle as O
+    from h3b200.rope import rope_grid_table
+
+    for grid, sl in (((21, 39, 40), None), ((45, 52, 84), (1000, 1700)), ((2, 5, 8), None)):
+        t = rope_grid_table(grid, token_slice=sl, device="cpu").numpy()
+        o = O.rope_grid_table(grid, token_slice=sl)
+        np.testing.assert_array_equal(t, o)

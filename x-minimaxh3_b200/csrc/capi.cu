@@ -1,0 +1,291 @@
+// extern "C" entry points: argument validation, workspace carving, launches.
+// Errors are returned as status codes with a thread-local message; nothing
+// falls back to another implementation.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int from_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return H3B200_OK;
+  if (e == cudaErrorNotSupported) return fail(H3B200_ERR_UNSUPPORTED, "%s: shape, stride or alignment outside the kernel contract", what);
+  return fail(H3B200_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+}
+
+inline cudaStream_t S(h3b200_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+
+inline int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Carves consecutive 256-byte aligned regions out of a caller workspace.
+struct Carver {
+  uint8_t* base;
+  int64_t size;
+  int64_t off = 0;
+  bool ok = true;
+  void* take(int64_t bytes) {
+    off = round_up(off, 256);
+    void* p = base + off;
+    off += bytes;
+    if (off > size) ok = false;
+    return p;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* h3b200_version(void) { return "h3b200 0.1.0 (sm_100a)"; }
+
+const char* h3b200_last_error(void) { return t_last_error.c_str(); }
+
+int h3b200_device_status(int device, unsigned int* status, int clear) {
+  if (status == nullptr) return fail(H3B200_ERR_INVALID, "device_status: status is NULL");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status, h3::g_status, sizeof(unsigned int));
+  if (e == cudaSuccess && clear) {
+    unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(h3::g_status, &zero, sizeof(unsigned int));
+  }
+  cudaSetDevice(prev);
+  return from_cuda(e, "device_status");
+}
+
+int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act, h3b200_stream_t stream) {
+  if (n < 0) return fail(H3B200_ERR_INVALID, "apply_input_act: negative size");
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "apply_input_act: unsupported act code %d", act);
+  if (n > 0 && (x == nullptr || y == nullptr)) return fail(H3B200_ERR_INVALID, "apply_input_act: NULL pointer");
+  if (n > (1ll << 40)) return fail(H3B200_ERR_UNSUPPORTED, "apply_input_act: n too large");
+  return from_cuda(h3::launch_apply_act(x, y, n, act, S(stream)), "apply_input_act");
+}
+
+int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ldx, int act, int8_t* q, float* scale,
+                                 h3b200_stream_t stream) {
+  if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: bad shape m=%lld k=%lld ldx=%lld", (long long)m, (long long)k, (long long)ldx);
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: unsupported act code %d", act);
+  if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: NULL pointer");
+  if (m > 0x7fffffffll) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise: m too large");
+  return from_cuda(h3::launch_quantize_rows(x, ldx, m, k, act, nullptr, q, scale, S(stream)), "quantize_int8_rowwise");
+}
+
+int h3b200_quantize_int8_rowwise_absmax(const void* x, const float* absmax, int64_t m, int64_t k, int64_t ldx,
+                                        int8_t* q, float* scale, h3b200_stream_t stream) {
+  if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_absmax: bad shape");
+  if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr || absmax == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_absmax: NULL pointer");
+  if (m > 0x7fffffffll) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_absmax: m too large");
+  return from_cuda(h3::launch_quantize_rows(x, ldx, m, k, H3B200_ACT_NONE, absmax, q, scale, S(stream)), "quantize_int8_rowwise_absmax");
+}
+
+int h3b200_int8_mm(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k, int32_t* out,
+                   h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "int8_mm: negative shape");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (a == nullptr || w == nullptr || out == nullptr) return fail(H3B200_ERR_INVALID, "int8_mm: NULL pointer");
+  if (k % 16 || n % 8) return fail(H3B200_ERR_UNSUPPORTED, "int8_mm: needs k %% 16 == 0 and n %% 8 == 0 (k=%lld n=%lld)", (long long)k, (long long)n);
+  h3::GemmArgs g;
+  g.a = a; g.w = w; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = h3::kEpiI32; g.out = out; g.ldo = n;
+  return from_cuda(h3::launch_gemm_i8(g, S(stream)), "int8_mm");
+}
+
+int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_scale, const int8_t* w, const float* w_scale,
+                                    int64_t w_scale_numel, const void* bias, int out_dtype, void* out, int64_t m,
+                                    int64_t n, int64_t k, h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: negative shape");
+  if (out_dtype != H3B200_DTYPE_BF16) return fail(H3B200_ERR_UNSUPPORTED, "int8_linear_prequantized: only bf16 output is built (got code %d)", out_dtype);
+  if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: weight scale must be scalar or per-output-channel, got %lld for n=%lld", (long long)w_scale_numel, (long long)n);
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!xq || !x_scale || !w || !w_scale || !out) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: NULL pointer");
+  if (k % 16 || n % 8) return fail(H3B200_ERR_UNSUPPORTED, "int8_linear_prequantized: needs k %% 16 == 0 and n %% 8 == 0");
+  h3::GemmArgs g;
+  g.a = xq; g.w = w; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = h3::kEpiBF16; g.a_scale = x_scale; g.w_scale = w_scale; g.w_scale_per_channel = w_scale_numel == n && n != 1 ? 1 : 0;
+  if (w_scale_numel == n && n == 1) g.w_scale_per_channel = 0;
+  g.bias = bias; g.out = out; g.ldo = n;
+  return from_cuda(h3::launch_gemm_i8(g, S(stream)), "int8_linear_prequantized");
+}
+
+int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int64_t m, int64_t n,
+                           int64_t k, int epilogue, const float* a_scale, const float* w_scale,
+                           int64_t w_scale_numel, const void* bias, const void* gate, const void* residual,
+                           int64_t ldr, void* out, int64_t ldo, float* row_absmax, h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0 || lda < k || ldw < k || ldo < n) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: bad shape");
+  if (epilogue < h3::kEpiI32 || epilogue > h3::kEpiGatedResidual) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: unknown epilogue %d", epilogue);
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!a || !w || !out) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: NULL pointer");
+  if (epilogue != h3::kEpiI32) {
+    if (!a_scale || !w_scale) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: scales required");
+    if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: weight scale must be scalar or per-output-channel");
+  }
+  if (epilogue == h3::kEpiGeluAbsmax && !row_absmax) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: row_absmax required");
+  if (epilogue == h3::kEpiGatedResidual && (!gate || !residual || ldr < n)) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: gate and residual required");
+  h3::GemmArgs g;
+  g.a = a; g.w = w; g.m = m; g.n = n; g.k = k; g.lda = lda; g.ldw = ldw;
+  g.epilogue = epilogue; g.a_scale = a_scale; g.w_scale = w_scale; g.w_scale_per_channel = (w_scale_numel == n && n > 1) ? 1 : 0;
+  g.bias = bias; g.gate = gate; g.residual = residual; g.ldr = ldr; g.out = out; g.ldo = ldo; g.row_absmax = row_absmax;
+  return from_cuda(h3::launch_gemm_i8(g, S(stream)), "int8_gemm_fused");
+}
+
+int64_t h3b200_int8_linear_workspace_bytes(int64_t m, int64_t k) {
+  return round_up(m * k, 256) + round_up(m * 4, 256) + 512;
+}
+
+int h3b200_int8_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale, int64_t w_scale_numel,
+                       const void* bias, int act, void* out, int64_t m, int64_t n, int64_t k, void* workspace,
+                       int64_t workspace_bytes, h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "int8_linear: bad shape");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (workspace == nullptr || workspace_bytes < h3b200_int8_linear_workspace_bytes(m, k)) return fail(H3B200_ERR_INVALID, "int8_linear: workspace too small (need %lld bytes)", (long long)h3b200_int8_linear_workspace_bytes(m, k));
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* xq = static_cast<int8_t*>(c.take(m * k));
+  float* xs = static_cast<float*>(c.take(m * 4));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "int8_linear: workspace too small");
+  int st = h3b200_quantize_int8_rowwise(x, m, k, ldx, act, xq, xs, stream);
+  if (st != H3B200_OK) return st;
+  return h3b200_int8_linear_prequantized(xq, xs, w, w_scale, w_scale_numel, bias, H3B200_DTYPE_BF16, out, m, n, k, stream);
+}
+
+int64_t h3b200_fused_gated_mlp_workspace_bytes(int64_t m, int64_t d, int64_t ffn) {
+  return round_up(m * d, 256) + round_up(m * 4, 256) * 3 + round_up(m * ffn * 2, 256) + round_up(m * ffn, 256) + 1024;
+}
+
+int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const int8_t* w2,
+                           const float* s2, const void* gate, const void* residual, int64_t ldr, void* out,
+                           int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
+                           int64_t workspace_bytes, h3b200_stream_t stream) {
+  if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: bad shape m=%lld d=%lld ffn=%lld", (long long)m, (long long)d, (long long)ffn);
+  if (act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp: only act=gelu_tanh (1) is built, got %d", act);
+  if (m == 0) return H3B200_OK;
+  if (!x || !w1 || !s1 || !w2 || !s2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: NULL pointer");
+  if (d % 16 || ffn % 16) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp: needs d %% 16 == 0 and ffn %% 16 == 0");
+  if (workspace == nullptr || workspace_bytes < h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn)) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: workspace too small (need %lld bytes)", (long long)h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn));
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* xq = static_cast<int8_t*>(c.take(m * d));
+  float* xs = static_cast<float*>(c.take(m * 4));
+  float* amax = static_cast<float*>(c.take(m * 4));
+  float* xs2 = static_cast<float*>(c.take(m * 4));
+  void* a = c.take(m * ffn * 2);
+  int8_t* q2 = static_cast<int8_t*>(c.take(m * ffn));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: workspace too small");
+  cudaStream_t st = S(stream);
+  int rc = h3b200_quantize_int8_rowwise(x, m, d, ldx, H3B200_ACT_NONE, xq, xs, stream);
+  if (rc != H3B200_OK) return rc;
+  cudaError_t e = cudaMemsetAsync(amax, 0, m * 4, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: memset");
+  h3::GemmArgs g1;
+  g1.a = xq; g1.w = w1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
+  g1.epilogue = h3::kEpiGeluAbsmax; g1.a_scale = xs; g1.w_scale = s1; g1.w_scale_per_channel = 1;
+  g1.out = a; g1.ldo = ffn; g1.row_absmax = amax;
+  e = h3::launch_gemm_i8(g1, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: fc1");
+  e = h3::launch_quantize_rows(a, ffn, m, ffn, H3B200_ACT_NONE, amax, q2, xs2, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: requant");
+  h3::GemmArgs g2;
+  g2.a = q2; g2.w = w2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
+  g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = s2; g2.w_scale_per_channel = 1;
+  g2.gate = gate; g2.residual = residual; g2.ldr = ldr; g2.out = out; g2.ldo = ldo;
+  e = h3::launch_gemm_i8(g2, st);
+  return from_cuda(e, "fused_gated_mlp: fc2");
+}
+
+int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk, void* q_out, int64_t ldqo,
+                          void* k_out, int64_t ldko, const float* freqs, const void* q_weight, const void* k_weight,
+                          const void* scale, const void* shift, int64_t m, int64_t heads, int64_t head_dim,
+                          int64_t rot_dim, int norm_span, float eps, h3b200_stream_t stream) {
+  if (m < 0 || heads <= 0 || head_dim <= 0) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: bad shape");
+  if (norm_span != 0 && norm_span != 1) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: norm_span must be 0 (row) or 1 (head)");
+  const int64_t rot = rot_dim == 0 ? head_dim : rot_dim;
+  if (rot < 0 || rot > head_dim || rot % 2) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: rot_dim %lld invalid for head_dim %lld", (long long)rot_dim, (long long)head_dim);
+  if ((scale == nullptr) != (shift == nullptr)) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: scale and shift must both be given or both be NULL");
+  if (ldq < heads * head_dim || ldk < heads * head_dim || ldqo < heads * head_dim || ldko < heads * head_dim) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: token stride smaller than a row");
+  if (m == 0) return H3B200_OK;
+  h3::NormRopeArgs a;
+  a.q = q; a.k = k; a.q_out = q_out; a.k_out = k_out; a.ldq = ldq; a.ldk = ldk; a.ldqo = ldqo; a.ldko = ldko;
+  a.freqs = freqs; a.q_weight = q_weight; a.k_weight = k_weight; a.scale = scale; a.shift = shift;
+  a.m = m; a.heads = heads; a.head_dim = head_dim; a.rot_dim = rot; a.norm_span = norm_span; a.eps = eps;
+  return from_cuda(h3::launch_adaln_rms_rope(a, S(stream)), "adaln_rms_rope");
+}
+
+int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k,
+                                        int64_t group_size, int8_t* out, h3b200_stream_t stream) {
+  if (n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: negative shape");
+  if (group_size < 4 || k % 16 || k % group_size || (16 % group_size && group_size % 16))
+    return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: K=%lld must be divisible by 16 and group_size=%lld; group_size must be >=4 and divide 16 or be a multiple of 16", (long long)k, (long long)group_size);
+  if (n == 0 || k == 0) return H3B200_OK;
+  if (!qdata || !s_rel || !out) return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: NULL pointer");
+  return from_cuda(h3::launch_dequant_int4(qdata, s_rel, n, k, group_size, out, S(stream)), "dequant_int4_grouped_to_int8");
+}
+
+int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, int64_t k, int64_t ldx, int64_t group_size,
+                                         int act, int8_t* q, float* scale, h3b200_stream_t stream) {
+  if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: bad shape");
+  if (group_size != 256) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_convrot: only group_size 256 is built (got %lld)", (long long)group_size);
+  if (k % 256) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: ConvRot group size 256 does not divide input features %lld", (long long)k);
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: unsupported act %d", act);
+  if (m == 0) return H3B200_OK;
+  if (!x || !q || !scale) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: NULL pointer");
+  return from_cuda(h3::launch_quantize_convrot(x, ldx, m, k, act, q, scale, nullptr, 0, S(stream)), "quantize_int8_rowwise_convrot");
+}
+
+int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t k, int64_t group_size) {
+  const int64_t g = group_size > 0 ? k / group_size : 0;
+  return round_up(m * k, 256) + round_up(m * 4, 256) + round_up(m * g * 4, 256) + 768;
+}
+
+int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
+                            const void* correction, int64_t group_size, int64_t convrot_group, int act, void* out,
+                            int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                            h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: bad shape");
+  if (group_size < 4 || k % 16 || k % group_size || k % convrot_group || (16 % group_size && group_size % 16))
+    return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: K=%lld must be divisible by 16, group_size=%lld, and convrot_groupsize=%lld", (long long)k, (long long)group_size, (long long)convrot_group);
+  if (convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: only convrot_groupsize 256 is built");
+  if (correction != nullptr && (group_size % 8 || 256 % group_size)) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: asymmetric correction needs group_size dividing 256");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!x || !grid || !s_channel || !out) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: NULL pointer");
+  if (n % 8) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: needs n %% 8 == 0");
+  if (workspace == nullptr || workspace_bytes < h3b200_w4a8_linear_workspace_bytes(m, k, group_size)) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: workspace too small (need %lld bytes)", (long long)h3b200_w4a8_linear_workspace_bytes(m, k, group_size));
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* xq = static_cast<int8_t*>(c.take(m * k));
+  float* xs = static_cast<float*>(c.take(m * 4));
+  int32_t* gs = static_cast<int32_t*>(c.take(m * (k / group_size) * 4));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: workspace too small");
+  cudaStream_t st = S(stream);
+  cudaError_t e = h3::launch_quantize_convrot(x, ldx, m, k, act, xq, xs, correction ? gs : nullptr, group_size, st);
+  if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: convrot quantize");
+  h3::GemmArgs g;
+  g.a = xq; g.w = grid; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = h3::kEpiBF16; g.a_scale = xs; g.w_scale = s_channel; g.w_scale_per_channel = 1;
+  g.out = out; g.ldo = n;
+  e = h3::launch_gemm_i8(g, st);
+  if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: gemm");
+  if (correction != nullptr) {
+    e = h3::launch_w4a8_correction(gs, xs, correction, m, n, k / group_size, out, n, st);
+    if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction");
+  }
+  return H3B200_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,392 @@
+// Persistent, warp-specialised INT8 GEMM for sm_100a with fused epilogues.
+//
+//   D[m, n] = sum_k A[m, k] * W[n, k]      (int8 x int8 -> int32, exact)
+//
+// Replaces the reference's SM80 CUTLASS FusedInt8Gemm
+// (backends/cuda/ops/cutlass_gemm_int8.cu:242-324) and cuBLASLt INT8 GEMM
+// (backends/cuda/ops/cublas_gemm_int8.cu:204); epilogue arithmetic follows the
+// eager path (backends/eager/quantization.py:1034-1053).
+//
+// Structure (one CTA per SM, 384 threads):
+//   warp 0      TMA producer: A tile 128x128 B and W tile 256x128 B per stage,
+//               128-byte swizzle, 4-stage ring guarded by full/empty mbarriers.
+//   warp 1      MMA issuer: 4 x tcgen05.mma.cta_group::1.kind::i8 (128x256x32)
+//               per stage into a TMEM accumulator; tcgen05.commit frees the
+//               stage and, after the last k-block, publishes the accumulator.
+//   warp 2      TMEM allocator (512 columns = two 128x256 s32 accumulators).
+//   warps 4-11  epilogue: tcgen05.ld 32 columns at a time, fused dequant /
+//               activation / gated residual, 128-bit global stores. The two
+//               accumulators let the epilogue of tile i overlap the mainloop of
+//               tile i+1.
+// Tiles are visited n-fastest so that the concurrently running CTAs share the
+// same A rows and the whole weight stays resident in the 126 MB L2.
+// No cluster multicast is used anywhere (the same binary runs in multi-GPU jobs).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace h3 {
+
+__device__ unsigned int g_status = 0u;
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = umma_idesc_i8(BM, BN);
+constexpr int BAR_BYTES = 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+
+// status codes recorded when a bounded wait expires
+constexpr unsigned kErrProducer = 0x101, kErrMmaAcc = 0x102, kErrMmaFull = 0x103, kErrEpi = 0x104,
+                   kErrDrain = 0x105;
+
+struct KParams {
+  int m, n, k;
+  int num_n_blk, num_k_blk, num_tiles;
+  const float* a_scale;
+  const float* w_scale;
+  int w_pc;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* gate;
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  void* out;
+  int64_t ldo;
+  float* row_absmax;
+};
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const KParams& p, int row, int col0, const uint32_t (&r)[32],
+                                               float xs, float& amax, int lane) {
+  const bool row_ok = row < p.m;
+  if constexpr (EPI == kEpiI32) {
+    if (row_ok) {
+      int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (col0 + 4 * g < p.n) stg_v4(o + 4 * g, make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]));
+    }
+    return;
+  } else {
+    const int cl = col0 + lane;
+    const bool col_ok = cl < p.n;
+    const float wsl = p.w_pc ? (col_ok ? __ldg(p.w_scale + cl) : 0.0f) : __ldg(p.w_scale);
+    float aux = 0.0f;
+    if constexpr (EPI == kEpiBF16) {
+      if (p.bias != nullptr && col_ok) aux = __bfloat162float(p.bias[cl]);
+    }
+    if constexpr (EPI == kEpiGatedResidual) {
+      if (col_ok) aux = __bfloat162float(p.gate[cl]);
+    }
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float sc = __fmul_rn(xs, __shfl_sync(0xffffffffu, wsl, j));
+      v[j] = bf16_round(__fmul_rn(__int2float_rn((int)r[j]), sc));
+    }
+    if constexpr (EPI == kEpiBF16) {
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = bf16_round(__fadd_rn(v[j], __shfl_sync(0xffffffffu, aux, j)));
+      }
+    }
+    if constexpr (EPI == kEpiGeluAbsmax) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = bf16_round(gelu_tanh_exact(v[j]));
+        amax = fmaxf(amax, fabsf(v[j]));
+      }
+    }
+    if constexpr (EPI == kEpiGatedResidual) {
+      float g[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) g[j] = __shfl_sync(0xffffffffu, aux, j);
+      if (row_ok) {
+        const __nv_bfloat16* rp = p.residual + (int64_t)row * p.ldr + col0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (col0 + 8 * q < p.n) {
+            const uint4 rv = ldg_v4(rp + 8 * q);
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = 8 * q + 2 * e;
+              v[j] = bf16_round(__fadd_rn(bf16_lo(rw[e]), __fmul_rn(v[j], g[j])));
+              v[j + 1] = bf16_round(__fadd_rn(bf16_hi(rw[e]), __fmul_rn(v[j + 1], g[j + 1])));
+            }
+          }
+        }
+      }
+    }
+    if (row_ok) {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (col0 + 8 * q < p.n) {
+          const int j = 8 * q;
+          stg_v4(o + j, make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
+                                   pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7])));
+        }
+      }
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], NUM_EPI_WARPS);
+    }
+    mbar_init(drain_bar, 1);
+    fence_barrier_init();
+    fence_proxy_async_shared();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile / p.num_n_blk;
+        const int n_blk = tile - m_blk * p.num_n_blk;
+        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, kErrProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m_blk * BM);
+          tma_load_2d(sa + A_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
+        }
+      }
+      // Let every copy this thread issued land before the CTA can exit.
+      for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        mbar_wait(&full_bar[j % STAGES], (uint32_t)(j / STAGES) & 1u, kErrDrain, 200000000ull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int it = 0;
+      int tcount = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
+        if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, kErrMmaAcc)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&full_bar[s], ph, kErrMmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            umma_i8(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC,
+                    (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&empty_bar[s]);
+        }
+        if (ok) umma_commit(&tfull_bar[acc]);
+      }
+      if (issued) {
+        // All MMAs this thread issued complete before TMEM can be released.
+        umma_commit(drain_bar);
+        mbar_wait(drain_bar, 0u, kErrDrain, 200000000ull);
+      }
+    }
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- epilogue ----------------
+    const int ew = warp - EPI_WARP0;
+    const int quarter = warp & 3;          // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int half = ew >> 2;              // columns [128*half, 128*half + 128)
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+      const int m_blk = tile / p.num_n_blk;
+      const int n_blk = tile - m_blk * p.num_n_blk;
+      const int acc = tcount & 1;
+      const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
+      if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
+      tc_fence_after();
+      const int row = m_blk * BM + quarter * 32 + lane;
+      const int col_base = n_blk * BN + half * 128;
+      float xs = 0.0f;
+      if constexpr (EPI != kEpiI32) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
+      float amax = 0.0f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
+        if (col_base + c < p.n) epilogue_chunk<EPI>(p, row, col_base + c, r, xs, amax, lane);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if constexpr (EPI == kEpiGeluAbsmax) {
+        if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, __float_as_uint(amax));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld_bytes, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI>
+cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
+                       cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  gemm_i8_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, kp);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int num_sms(int device) {
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
+  if (a.m <= 0 || a.n <= 0) return cudaSuccess;
+  if (a.k <= 0 || a.k % 16 != 0 || a.n % 8 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.m > (1ll << 30) ||
+      a.n > (1ll << 30) || a.k > (1ll << 30))
+    return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.out) & 15) || a.ldo % 8 != 0)
+    return cudaErrorNotSupported;
+  if (a.epilogue == kEpiGatedResidual && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0))
+    return cudaErrorNotSupported;
+  CUtensorMap ta, tb;
+  if (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN))
+    return cudaErrorInvalidValue;
+  KParams kp;
+  kp.m = (int)a.m;
+  kp.n = (int)a.n;
+  kp.k = (int)a.k;
+  kp.num_n_blk = (int)((a.n + BN - 1) / BN);
+  kp.num_k_blk = (int)((a.k + BK - 1) / BK);
+  const int64_t num_m_blk = (a.m + BM - 1) / BM;
+  const int64_t tiles = num_m_blk * kp.num_n_blk;
+  if (tiles > (1ll << 30)) return cudaErrorNotSupported;
+  kp.num_tiles = (int)tiles;
+  kp.a_scale = a.a_scale;
+  kp.w_scale = a.w_scale;
+  kp.w_pc = a.w_scale_per_channel;
+  kp.bias = static_cast<const __nv_bfloat16*>(a.bias);
+  kp.gate = static_cast<const __nv_bfloat16*>(a.gate);
+  kp.residual = static_cast<const __nv_bfloat16*>(a.residual);
+  kp.ldr = a.ldr;
+  kp.out = a.out;
+  kp.ldo = a.ldo;
+  kp.row_absmax = a.row_absmax;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = (int)std::min<int64_t>(tiles, (int64_t)num_sms(dev));
+  switch (a.epilogue) {
+    case kEpiI32: return launch_epi<kEpiI32>(ta, tb, kp, grid, stream);
+    case kEpiBF16: return launch_epi<kEpiBF16>(ta, tb, kp, grid, stream);
+    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, kp, grid, stream);
+    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, kp, grid, stream);
+    default: return cudaErrorNotSupported;
+  }
+}
+
+}  // namespace h3

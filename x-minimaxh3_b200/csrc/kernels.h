@@ -1,0 +1,74 @@
+// Internal launchers shared between the kernel files and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace h3 {
+
+// Epilogue variants of the tcgen05 INT8 GEMM.
+enum GemmEpilogue : int {
+  kEpiI32 = 0,             // raw int32 accumulators
+  kEpiBF16 = 1,            // bf16(acc * (xs * ws)) (+ bf16 bias)
+  kEpiGeluAbsmax = 2,      // a = gelu(bf16(acc * (xs * ws))) stored bf16, row absmax of |a| via atomicMax
+  kEpiGatedResidual = 3,   // out = bf16(residual + bf16(acc * (xs * ws)) * gate)
+  kEpiW4A8Correction = 4,  // bf16(bf16(acc * (xs * ws)) + sum_g bf16(gsum*xs) * corr[g, n])
+};
+
+struct GemmArgs {
+  const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes
+  const int8_t* w = nullptr;  // [n, k] int8, row stride ldw bytes
+  int64_t m = 0, n = 0, k = 0;
+  int64_t lda = 0, ldw = 0;
+  int epilogue = kEpiBF16;
+  const float* a_scale = nullptr;  // [m]
+  const float* w_scale = nullptr;  // [n] or [1]
+  int w_scale_per_channel = 1;
+  const void* bias = nullptr;      // bf16 [n]
+  const void* gate = nullptr;      // bf16 [n]
+  const void* residual = nullptr;  // bf16 [m, ldr]
+  int64_t ldr = 0;
+  void* out = nullptr;  // bf16 or int32 [m, ldo]
+  int64_t ldo = 0;
+  float* row_absmax = nullptr;              // fp32 [m], must start at 0 (values are non-negative)
+  const int32_t* group_sums = nullptr;      // int32 [m, k/group]
+  const void* correction = nullptr;         // bf16 [k/group, n]
+  int64_t groups = 0;
+};
+
+cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream);
+cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
+                                 int8_t* q, float* scale, cudaStream_t stream);
+
+// Returns cudaErrorNotSupported when the shape is outside the kernel's contract.
+cudaError_t launch_gemm_i8(const GemmArgs& args, cudaStream_t stream);
+
+struct NormRopeArgs {
+  const void* q = nullptr;
+  const void* k = nullptr;
+  void* q_out = nullptr;
+  void* k_out = nullptr;
+  int64_t ldq = 0, ldk = 0, ldqo = 0, ldko = 0;
+  const float* freqs = nullptr;
+  const void* q_weight = nullptr;
+  const void* k_weight = nullptr;
+  const void* scale = nullptr;
+  const void* shift = nullptr;
+  int64_t m = 0, heads = 0, head_dim = 0, rot_dim = 0;
+  int norm_span = 0;
+  float eps = 1e-6f;
+};
+cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream);
+
+cudaError_t launch_dequant_int4(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k, int64_t group,
+                                int8_t* out, cudaStream_t stream);
+cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64_t k, int act, int8_t* q,
+                                    float* scale, int32_t* group_sums, int64_t sum_group, cudaStream_t stream);
+
+cudaError_t launch_w4a8_correction(const int32_t* gsum, const float* xs, const void* corr, int64_t m, int64_t n,
+                                   int64_t groups, void* out, int64_t ldo, cudaStream_t stream);
+
+int num_sms(int device);
+
+}  // namespace h3

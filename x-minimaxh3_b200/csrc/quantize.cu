@@ -1,0 +1,181 @@
+// Per-token absmax INT8 quantizer (HBM-bound).
+//
+// Reference algorithm: comfy_kitchen quantize_int8_rowwise
+// (backends/eager/quantization.py:857-875, rounding helpers :815-826; CUDA
+// kernel backends/cuda/ops/int8_linear.cu:157-200):
+//   absmax = max |x| over the row (exact on bf16)
+//   scale  = max(absmax / 127, 1e-30)            fp32, stored
+//   sb     = bf16(scale)                          scale as the bf16 operand
+//   q      = clamp(rne(bf16(x / sb)), -128, 127)
+//
+// B200 layout: one CTA of 256 threads per row; the row stays in registers
+// between the absmax reduction and the quantize pass, so HBM sees exactly one
+// read of x (2 B/elem) and one write of q (1 B/elem) plus 4 B of scale per row.
+// Loads are 128-bit (8 bf16), stores 64-bit (8 int8).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace h3 {
+
+namespace {
+
+constexpr int kQThreads = 256;
+
+__device__ __forceinline__ float quant_divisor(float scale) {
+  float sb = bf16_round(scale);
+  return sb == 0.0f ? 1.17549435e-38f : sb;  // torch.finfo(bf16).tiny substitution
+}
+
+__device__ __forceinline__ int8_t quant_one(float x, float sb) {
+  float v = rintf(bf16_round(__fdiv_rn(x, sb)));
+  v = fminf(fmaxf(v, -128.0f), 127.0f);
+  return (int8_t)(int)v;
+}
+
+__device__ __forceinline__ float act_apply(float x, int act) {
+  return act == H3B200_ACT_GELU_TANH ? bf16_round(gelu_tanh_exact(x)) : x;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < kQThreads / 32; ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+// Vector path: k % 8 == 0, 16-byte aligned rows, k <= kQThreads * 8 * VPT.
+template <int VPT, bool GIVEN_ABSMAX>
+__global__ void __launch_bounds__(kQThreads) quantize_rows_vec_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                      int64_t m, int64_t k, int act,
+                                                                      const float* __restrict__ absmax_in,
+                                                                      int8_t* __restrict__ q,
+                                                                      float* __restrict__ scale) {
+  __shared__ float red[kQThreads / 32];
+  const int64_t row = blockIdx.x;
+  if (row >= m) return;
+  const int64_t nvec = k >> 3;
+  const __nv_bfloat16* xr = x + row * ldx;
+  uint4 v[VPT];
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + (int64_t)j * kQThreads;
+    if (vi < nvec) {
+      v[j] = ldg_nc_v4(xr + vi * 8);
+      if (act != H3B200_ACT_NONE) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v[j]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = pack_bf16(act_apply(bf16_lo(w[e]), act), act_apply(bf16_hi(w[e]), act));
+      }
+      if (!GIVEN_ABSMAX) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[j]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fmaxf(fabsf(bf16_lo(w[e])), fabsf(bf16_hi(w[e]))));
+      }
+    }
+  }
+  float rowmax;
+  if (GIVEN_ABSMAX) {
+    rowmax = absmax_in[row];
+  } else {
+    rowmax = block_max(amax, red);
+  }
+  const float s = fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f);
+  const float sb = quant_divisor(s);
+  int8_t* qr = q + row * k;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + (int64_t)j * kQThreads;
+    if (vi < nvec) {
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[j]);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        lo |= (uint32_t)(uint8_t)quant_one(bf16_lo(w[e]), sb) << (16 * e);
+        lo |= (uint32_t)(uint8_t)quant_one(bf16_hi(w[e]), sb) << (16 * e + 8);
+        hi |= (uint32_t)(uint8_t)quant_one(bf16_lo(w[e + 2]), sb) << (16 * e);
+        hi |= (uint32_t)(uint8_t)quant_one(bf16_hi(w[e + 2]), sb) << (16 * e + 8);
+      }
+      *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(lo, hi);
+    }
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+// Generic path (any k / alignment): two passes over the row in global memory.
+__global__ void __launch_bounds__(kQThreads) quantize_rows_scalar_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                         int64_t ldx, int64_t m, int64_t k, int act,
+                                                                         const float* __restrict__ absmax_in,
+                                                                         int8_t* __restrict__ q,
+                                                                         float* __restrict__ scale) {
+  __shared__ float red[kQThreads / 32];
+  const int64_t row = blockIdx.x;
+  if (row >= m) return;
+  const __nv_bfloat16* xr = x + row * ldx;
+  float rowmax;
+  if (absmax_in != nullptr) {
+    rowmax = absmax_in[row];
+  } else {
+    float amax = 0.0f;
+    for (int64_t i = threadIdx.x; i < k; i += kQThreads) amax = fmaxf(amax, fabsf(act_apply(__bfloat162float(xr[i]), act)));
+    rowmax = block_max(amax, red);
+  }
+  const float s = fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f);
+  const float sb = quant_divisor(s);
+  for (int64_t i = threadIdx.x; i < k; i += kQThreads) q[row * k + i] = quant_one(act_apply(__bfloat162float(xr[i]), act), sb);
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
+template <bool GIVEN>
+cudaError_t launch_vec(int vpt, const __nv_bfloat16* x, int64_t ldx, int64_t m, int64_t k, int act, const float* am,
+                       int8_t* q, float* s, cudaStream_t st) {
+  dim3 grid((unsigned)m), block(kQThreads);
+  switch (vpt) {
+    case 1: quantize_rows_vec_kernel<1, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    case 2: quantize_rows_vec_kernel<2, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    case 4: quantize_rows_vec_kernel<4, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    case 6: quantize_rows_vec_kernel<6, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    default: quantize_rows_vec_kernel<8, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+  }
+  return cudaGetLastError();
+}
+
+__global__ void apply_act_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n,
+                                 int act) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(act_apply(__bfloat162float(x[i]), act));
+}
+
+}  // namespace
+
+cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  apply_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                   static_cast<__nv_bfloat16*>(y), n, act);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
+                                 int8_t* q, float* scale, cudaStream_t stream) {
+  if (m == 0) return cudaSuccess;
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  const bool aligned = (k % 8 == 0) && (ldx % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
+  const int64_t nvec = k / 8;
+  const int64_t per_thread = (nvec + kQThreads - 1) / kQThreads;
+  if (aligned && k > 0 && per_thread <= 8) {
+    const int vpt = per_thread <= 1 ? 1 : per_thread <= 2 ? 2 : per_thread <= 4 ? 4 : per_thread <= 6 ? 6 : 8;
+    if (absmax_in != nullptr) return launch_vec<true>(vpt, xb, ldx, m, k, act, absmax_in, q, scale, stream);
+    return launch_vec<false>(vpt, xb, ldx, m, k, act, nullptr, q, scale, stream);
+  }
+  quantize_rows_scalar_kernel<<<dim3((unsigned)m), dim3(kQThreads), 0, stream>>>(xb, ldx, m, k, act, absmax_in, q,
+                                                                                  scale);
+  return cudaGetLastError();
+}
+
+}  // namespace h3

@@ -1,0 +1,43 @@
+"""h3b200: B200-native (sm_100a) quantized DiT-block hot path for X-MinimaxH3.
+
+Public operators mirror the comfy_kitchen backend surface that
+``h3serve/native_engine`` and ``backends/turbo`` call (``int8_linear``,
+``quantize_int8_rowwise``, ``int8_linear_prequantized``, ``mm_int8``,
+``w4a8_int8_linear``, ``rms_rope_split_half(_)``) plus the fused entry points
+``fused_gated_mlp`` and ``adaln_rms_rope(_)``. All of them run hand-written CUDA
+from ``libh3b200.so`` through its C ABI; there is no other backend.
+"""
+
+from . import _lib
+from .ops import (  # noqa: F401
+    adaln_rms_rope,
+    apply_input_act,
+    adaln_rms_rope_,
+    dequant_int4_grouped_to_int8,
+    fused_gated_mlp,
+    input_act_code,
+    int8_gemm_fused,
+    int8_linear,
+    int8_linear_prequantized,
+    mm_int8,
+    quantize_int8_rowwise,
+    quantize_int8_rowwise_absmax,
+    quantize_int8_rowwise_convrot,
+    rms_rope_split_half,
+    rms_rope_split_half_,
+    w4a8_int8_linear,
+)
+from .rope import rope_grid_table  # noqa: F401
+from .weights import quantize_int8_weight, W8A8MLPWeights  # noqa: F401
+
+__version__ = "0.1.0"
+
+
+def library():
+    """Load and return the ctypes handle of libh3b200.so (raises if it is missing)."""
+    return _lib.load()
+
+
+def device_status(device: int = 0, clear: bool = False) -> int:
+    """Device status word (0 = healthy; non-zero = a bounded wait expired). Synchronises."""
+    return _lib.device_status(device, clear)

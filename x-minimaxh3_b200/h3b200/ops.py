@@ -1,0 +1,465 @@
+"""Operator surface of the quantized DiT-block hot path (comfy_kitchen-compatible).
+
+Every function takes CUDA tensors, allocates its outputs with torch on the
+tensor's device, and launches the sm_100a kernels of ``libh3b200.so`` through
+the C ABI on ``torch.cuda.current_stream()``. Argument names, meanings and
+errors follow the reference operators (comfy_kitchen 0.2.28, vendored in
+X-MinimaxH3 under ``backends/turbo/vendor/comfy_kitchen``); each function cites
+the one it replaces. There is no CPU or library fallback: unsupported inputs
+raise.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "apply_input_act",
+    "quantize_int8_rowwise",
+    "quantize_int8_rowwise_absmax",
+    "mm_int8",
+    "int8_linear_prequantized",
+    "int8_linear",
+    "int8_gemm_fused",
+    "fused_gated_mlp",
+    "adaln_rms_rope",
+    "adaln_rms_rope_",
+    "rms_rope_split_half",
+    "rms_rope_split_half_",
+    "dequant_int4_grouped_to_int8",
+    "quantize_int8_rowwise_convrot",
+    "w4a8_int8_linear",
+    "input_act_code",
+]
+
+_ACT = {None: _lib.ACT_NONE, "none": _lib.ACT_NONE, "gelu_tanh": _lib.ACT_GELU_TANH}
+
+
+def input_act_code(input_act) -> int:
+    """Kernel code for ``input_act`` (backends/_activations.py:19-33); swiglu is not built."""
+    try:
+        return _ACT[input_act]
+    except KeyError:
+        known = sorted(k for k in _ACT if k is not None)
+        raise ValueError(f"unsupported input_act: {input_act!r} (expected one of {known})") from None
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("h3b200 operators take CUDA tensors only (no CPU fallback)")
+
+
+def _rows(x: torch.Tensor):
+    """View x as [rows, K] with unit stride along K; returns (x2d, row_stride)."""
+    k = x.shape[-1]
+    if x.dim() == 2 and x.stride(1) == 1 and x.stride(0) >= k:
+        return x, x.stride(0)
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1 or (x2.shape[0] > 1 and x2.stride(0) < k):
+        x2 = x2.contiguous()
+    return x2, (x2.stride(0) if x2.shape[0] > 1 else k)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def apply_input_act(x: torch.Tensor, input_act) -> torch.Tensor:
+    """Pre-quantization activation (backends/_activations.py:40-53), bit-identical to
+    the reference's CPU ``gelu(approximate="tanh")`` for every bf16 input."""
+    _need_cuda(x)
+    code = input_act_code(input_act)
+    if code == _lib.ACT_NONE:
+        return x
+    if x.dtype != torch.bfloat16:
+        raise ValueError("apply_input_act expects bf16")
+    xc = x.contiguous()
+    y = torch.empty_like(xc)
+    _lib.call("h3b200_apply_input_act", xc.data_ptr(), y.data_ptr(), xc.numel(), code, _stream(x))
+    return y
+
+
+# ---------------------------------------------------------------------------
+# (a) quantizer
+# ---------------------------------------------------------------------------
+
+
+def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int | None = 0, input_act=None):
+    """Per-row absmax INT8 quantization -> (int8 [..., K], fp32 scales [..., 1]).
+
+    Replaces ``comfy_kitchen.quantize_int8_rowwise`` (__init__.py:702-709;
+    eager eager/quantization.py:857-875; CUDA backends/cuda/ops/int8_linear.cu:157-200).
+    Stochastic rounding is not built (the DiT path never uses it)."""
+    if stochastic_rounding:
+        raise NotImplementedError("stochastic rounding is not built in h3b200")
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"quantize_int8_rowwise expects bf16, got {x.dtype}")
+    x2, ldx = _rows(x)
+    m, k = x2.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    _lib.call("h3b200_quantize_int8_rowwise", x2.data_ptr(), m, k, ldx, input_act_code(input_act), q.data_ptr(),
+              s.data_ptr(), _stream(x))
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+
+
+def quantize_int8_rowwise_absmax(x: torch.Tensor, absmax: torch.Tensor):
+    """Quantizer body with a precomputed fp32 row absmax [..., 1] (same arithmetic)."""
+    _need_cuda(x, absmax)
+    x2, ldx = _rows(x)
+    m, k = x2.shape
+    am = absmax.reshape(-1).to(torch.float32).contiguous()
+    if am.numel() != m:
+        raise ValueError("absmax must have one value per row")
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    _lib.call("h3b200_quantize_int8_rowwise_absmax", x2.data_ptr(), am.data_ptr(), m, k, ldx, q.data_ptr(),
+              s.data_ptr(), _stream(x))
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+
+
+# ---------------------------------------------------------------------------
+# (b) INT8 GEMM / linear / fused MLP
+# ---------------------------------------------------------------------------
+
+
+def mm_int8(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """INT8 matmul ``C[M, N] = A[M, K] @ B[K, N]`` with int32 accumulators.
+
+    Replaces ``comfy_kitchen.mm_int8`` / ``_int8_matmul_accumulate``
+    (eager/quantization.py:749-800). ``b`` may be a transposed view of a
+    row-major [N, K] weight (no copy in that case)."""
+    _need_cuda(a, b)
+    if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2:
+        raise ValueError("mm_int8 takes 2-D int8 tensors")
+    if a.size(1) != b.size(0):
+        raise ValueError(f"K mismatch: {a.size(1)} vs {b.size(0)}")
+    a = a.contiguous()
+    w = b.t()
+    if not w.is_contiguous():
+        w = w.contiguous()
+    m, k = a.shape
+    n = w.shape[0]
+    out = torch.empty((m, n), dtype=torch.int32, device=a.device)
+    _lib.call("h3b200_int8_mm", a.data_ptr(), w.data_ptr(), m, n, k, out.data_ptr(), _stream(a))
+    return out
+
+
+def _weight_scale(weight_scale: torch.Tensor, n: int, device) -> torch.Tensor:
+    ws = weight_scale.to(device=device, dtype=torch.float32).reshape(-1).contiguous()
+    if ws.numel() not in (1, n):
+        raise ValueError(f"INT8 weight scale must be scalar or per-output-channel, got {tuple(weight_scale.shape)} "
+                         f"for {n} output channels")
+    return ws
+
+
+def int8_linear_prequantized(x_qdata: torch.Tensor, x_scale: torch.Tensor, weight: torch.Tensor,
+                             weight_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                             out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """INT8 linear from a row-quantized activation (backends/cuda/__init__.py:1934-1957).
+
+    ``out = bf16(float(acc) * (x_scale[row] * weight_scale[col])) (+ bias)`` with
+    the eager association (eager/quantization.py:1044-1048)."""
+    _need_cuda(x_qdata, x_scale, weight)
+    if out_dtype != torch.bfloat16:
+        raise NotImplementedError("h3b200 builds bf16 outputs only")
+    xq = x_qdata.reshape(-1, x_qdata.shape[-1]).contiguous()
+    m, k = xq.shape
+    n, kw = weight.shape
+    if k != kw:
+        raise ValueError(f"Input and weight inner dimensions must match, got {k} and {kw}")
+    w = weight.contiguous()
+    xs = x_scale.reshape(-1).to(torch.float32).contiguous()
+    ws = _weight_scale(weight_scale, n, xq.device)
+    b = None if bias is None else bias.to(device=xq.device, dtype=torch.bfloat16).contiguous()
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=xq.device)
+    _lib.call("h3b200_int8_linear_prequantized", xq.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(),
+              ws.numel(), _ptr(b), _lib.DTYPE_BF16, out.data_ptr(), m, n, k, _stream(xq))
+    return out.reshape(*x_qdata.shape[:-1], n)
+
+
+EPI_I32, EPI_BF16, EPI_GELU_ABSMAX, EPI_GATED_RESIDUAL = 0, 1, 2, 3
+
+
+def int8_gemm_fused(a: torch.Tensor, w: torch.Tensor, epilogue: int, a_scale=None, w_scale=None, bias=None,
+                    gate=None, residual=None, out=None, row_absmax=None) -> torch.Tensor:
+    """One tcgen05 INT8 GEMM with a fused epilogue (the stages of :func:`fused_gated_mlp`).
+
+    ``epilogue``: EPI_I32 (int32 accumulators), EPI_BF16 (dequant + bias),
+    EPI_GELU_ABSMAX (dequant -> tanh-GELU -> bf16, row absmax into ``row_absmax``),
+    EPI_GATED_RESIDUAL (``residual + dequant * gate``). ``a`` [M, K] and ``w`` [N, K]
+    are int8 with unit stride along K."""
+    _need_cuda(a, w)
+    m, k = a.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.int32 if epilogue == EPI_I32 else torch.bfloat16, device=a.device)
+    ws = None if w_scale is None else _weight_scale(w_scale, n, a.device)
+    xs = None if a_scale is None else a_scale.reshape(-1).to(torch.float32).contiguous()
+    _lib.call("h3b200_int8_gemm_fused", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), m, n, k, int(epilogue),
+              _ptr(xs), _ptr(ws), 0 if ws is None else ws.numel(), _ptr(bias), _ptr(gate), _ptr(residual),
+              0 if residual is None else residual.stride(0), out.data_ptr(), out.stride(0), _ptr(row_absmax),
+              _stream(a))
+    return out
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor, bias: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None, convrot: bool = False, convrot_groupsize: int = 256,
+                input_act: str | None = None) -> torch.Tensor:
+    """Dynamically quantized INT8 linear.
+
+    Replaces ``comfy_kitchen.int8_linear`` (__init__.py:722-764; CUDA
+    backends/cuda/__init__.py:1960-2081; eager eager/quantization.py:971-1056):
+    ``input_act`` on x, per-row quantization, INT8 GEMM, dequant (+ bias).
+    ``convrot=True`` rotates the activation with the regular Hadamard-256 first."""
+    _need_cuda(x, weight)
+    if out_dtype is None:
+        out_dtype = torch.bfloat16
+    if out_dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
+    if x.shape[-1] != weight.shape[-1]:
+        raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {weight.shape[-1]}")
+    act = input_act_code(input_act)
+    n = weight.shape[0]
+    if convrot:
+        xq, xs = quantize_int8_rowwise_convrot(x, convrot_groupsize, input_act)
+        return int8_linear_prequantized(xq, xs, weight, weight_scale, bias, out_dtype)
+    x2, ldx = _rows(x)
+    m, k = x2.shape
+    w = weight.contiguous()
+    ws = _weight_scale(weight_scale, n, x.device)
+    b = None if bias is None else bias.to(device=x.device, dtype=torch.bfloat16).contiguous()
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    nbytes = int(_lib.load().h3b200_int8_linear_workspace_bytes(m, k))
+    work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _lib.call("h3b200_int8_linear", x2.data_ptr(), ldx, w.data_ptr(), ws.data_ptr(), ws.numel(), _ptr(b), act,
+              out.data_ptr(), m, n, k, work.data_ptr(), nbytes, _stream(x))
+    return out.reshape(*x.shape[:-1], n)
+
+
+def fused_gated_mlp(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Tensor, s1: torch.Tensor,
+                    w2q: torch.Tensor, s2: torch.Tensor, gate: torch.Tensor, act: str = "gelu_tanh",
+                    out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + int8_linear(act(int8_linear(hidden, w1q, s1)), w2q, s2) * gate`` in one launch chain.
+
+    Drop-in for ``try_fused_gated_mlp`` (h3serve/native_engine/model/fused_mlp.py:269-426;
+    composition :393-425) with one modulation row (``gate`` [d]) and the tanh-GELU
+    activation. ``out`` may be ``residual`` (in-place ``addcmul_``)."""
+    _need_cuda(residual, hidden, w1q, w2q, gate)
+    if act != "gelu_tanh":
+        raise NotImplementedError(f"fused_gated_mlp builds act='gelu_tanh' only, got {act!r}")
+    for name, t in (("residual", residual), ("hidden", hidden), ("gate", gate)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16, got {t.dtype}")
+    x2, ldx = _rows(hidden)
+    r2, ldr = _rows(residual)
+    m, d = x2.shape
+    ffn = w1q.shape[0]
+    if tuple(w1q.shape) != (ffn, d) or tuple(w2q.shape) != (d, ffn):
+        raise ValueError(f"weights must be w1 [ffn, d] and w2 [d, ffn], got {tuple(w1q.shape)} and {tuple(w2q.shape)}")
+    if r2.shape != x2.shape:
+        raise ValueError("residual and hidden must have the same shape")
+    g = gate.reshape(-1).contiguous()
+    if g.numel() != d:
+        raise ValueError(f"gate must have {d} elements (one modulation row)")
+    ws1 = _weight_scale(s1, ffn, hidden.device)
+    ws2 = _weight_scale(s2, d, hidden.device)
+    if ws1.numel() != ffn or ws2.numel() != d:
+        raise ValueError("fused_gated_mlp needs per-channel weight scales")
+    if out is None:
+        out = torch.empty_like(r2)
+    o2, ldo = _rows(out)
+    nbytes = int(_lib.load().h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn))
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
+    _lib.call("h3b200_fused_gated_mlp", x2.data_ptr(), ldx, w1q.contiguous().data_ptr(), ws1.data_ptr(),
+              w2q.contiguous().data_ptr(), ws2.data_ptr(), g.data_ptr(), r2.data_ptr(), ldr, o2.data_ptr(), ldo,
+              m, d, ffn, _lib.ACT_GELU_TANH, workspace.data_ptr(), workspace.numel(), _stream(hidden))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# (c) AdaLN + RMSNorm + RoPE
+# ---------------------------------------------------------------------------
+
+
+def _qk3(t: torch.Tensor):
+    """[1, M, H, D] / [M, H, D] -> ([M, H, D] view, token stride)."""
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise ValueError("batch dimension must be 1 (packed token layout)")
+        t = t[0]
+    if t.dim() != 3:
+        raise ValueError(f"expected [M, H, D] or [1, M, H, D], got {tuple(t.shape)}")
+    if t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+        raise ValueError("heads x head_dim must be contiguous within a token")
+    return t, t.stride(0)
+
+
+def _freqs(freqs_cis: torch.Tensor, m: int, half: int) -> torch.Tensor:
+    f = freqs_cis
+    if f.dtype != torch.float32:
+        raise ValueError("freqs_cis must be fp32")
+    f = f.reshape(-1, f.shape[-3], 2, 2)
+    if f.shape[0] != m or f.shape[1] < half:
+        raise ValueError(f"freqs_cis must hold [M={m}, >= {half}, 2, 2] rotations, got {tuple(freqs_cis.shape)}")
+    if f.shape[1] != half:
+        f = f[:, :half]
+    return f.contiguous()
+
+
+def adaln_rms_rope_(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=None, eps: float = 1e-6,
+                    norm_span: str = "row", rot_dim: int = 0, q_out=None, k_out=None):
+    """Fused AdaLN-modulate + RMSNorm + split-half RoPE on Q and K, in place by default.
+
+    ``norm_span="row"``: RMSNorm over heads*head_dim with [H*D] weights, then
+    ``*(1 + scale)`` and ``+ shift`` (bf16 after each) -- the eager order of H3's
+    ``rms_adaln`` (h3serve/native_engine/model/kernels.py:7586-7634) -- then
+    per-head split-half RoPE (eager/rope.py:39-42). ``norm_span="head"``:
+    per-head RMSNorm with [D] weights (``rms_rope_split_half``, eager/rope.py:67-143),
+    optional modulation after it. Returns (q_out, k_out)."""
+    _need_cuda(q, k, freqs_cis, q_weight)
+    if k_weight is None:
+        k_weight = q_weight
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise ValueError("q and k must be bf16")
+    q3, ldq = _qk3(q)
+    k3, ldk = _qk3(k)
+    if q3.shape != k3.shape:
+        raise ValueError("q and k must have the same [M, H, D] shape")
+    m, h, d = q3.shape
+    rd = d if rot_dim in (0, None) else int(rot_dim)
+    if q_out is None:
+        q_out = q
+    if k_out is None:
+        k_out = k
+    qo3, ldqo = _qk3(q_out)
+    ko3, ldko = _qk3(k_out)
+    span = {"row": 0, "head": 1}.get(norm_span)
+    if span is None:
+        raise ValueError(f"norm_span must be 'row' or 'head', got {norm_span!r}")
+    width = h * d if span == 0 else d
+    wq = q_weight.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+    wk = k_weight.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+    if wq.numel() != width or wk.numel() != width:
+        raise ValueError(f"norm weights must have {width} elements for norm_span={norm_span!r}")
+    sc = sh = None
+    if scale is not None or shift is not None:
+        if scale is None or shift is None:
+            raise ValueError("scale and shift must be given together")
+        sc = scale.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+        sh = shift.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+        if sc.numel() != h * d or sh.numel() != h * d:
+            raise ValueError(f"scale/shift must have {h * d} elements (one modulation row)")
+    f = _freqs(freqs_cis, m, rd // 2)
+    _lib.call("h3b200_adaln_rms_rope", q3.data_ptr(), ldq, k3.data_ptr(), ldk, qo3.data_ptr(), ldqo, ko3.data_ptr(),
+              ldko, f.data_ptr(), wq.data_ptr(), wk.data_ptr(), _ptr(sc), _ptr(sh), m, h, d, rd, span, float(eps),
+              _stream(q))
+    return q_out, k_out
+
+
+def adaln_rms_rope(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=None, eps: float = 1e-6,
+                   norm_span: str = "row", rot_dim: int = 0):
+    """Out-of-place variant of :func:`adaln_rms_rope_`."""
+    return adaln_rms_rope_(q, k, freqs_cis, q_weight, k_weight, scale, shift, eps, norm_span, rot_dim,
+                           q_out=torch.empty_like(q), k_out=torch.empty_like(k))
+
+
+def rms_rope_split_half_(q, k, freqs_cis, q_scale, k_scale=None, epsilon: float = 1e-6, rot_dim: int = 0):
+    """In-place per-head RMSNorm + split-half RoPE (``comfy_kitchen.rms_rope_split_half_``,
+    __init__.py:566-580; CUDA backends/cuda/ops/rms_rope.cu:36-229)."""
+    return adaln_rms_rope_(q, k, freqs_cis, q_scale, k_scale, None, None, epsilon, "head", rot_dim)
+
+
+def rms_rope_split_half(q, k, freqs_cis, q_scale, k_scale=None, epsilon: float = 1e-6, rot_dim: int = 0):
+    """Out-of-place ``comfy_kitchen.rms_rope_split_half`` (__init__.py:549-563)."""
+    return adaln_rms_rope(q, k, freqs_cis, q_scale, k_scale, None, None, epsilon, "head", rot_dim)
+
+
+# ---------------------------------------------------------------------------
+# W4A8
+# ---------------------------------------------------------------------------
+
+
+def dequant_int4_grouped_to_int8(qdata: torch.Tensor, s_rel: torch.Tensor, group_size: int) -> torch.Tensor:
+    """Decode packed uint4 to the int8 grid (eager/w4a8_int8.py:344-363; CUDA w4a8_gemm.cu:36-90)."""
+    _need_cuda(qdata, s_rel)
+    if s_rel.dtype != torch.float32:
+        raise NotImplementedError("h3b200 builds fp32 s_rel only (no fp8-e4m3 scales, no codebook)")
+    qd = qdata.contiguous()
+    n, kh = qd.shape
+    k = kh * 2
+    sr = s_rel.contiguous()
+    if tuple(sr.shape) != (n, k // group_size):
+        raise ValueError(f"s_rel must have shape {(n, k // group_size)}, got {tuple(sr.shape)}")
+    out = torch.empty((n, k), dtype=torch.int8, device=qd.device)
+    _lib.call("h3b200_dequant_int4_grouped_to_int8", qd.data_ptr(), sr.data_ptr(), n, k, group_size, out.data_ptr(),
+              _stream(qd))
+    return out
+
+
+def quantize_int8_rowwise_convrot(x: torch.Tensor, convrot_groupsize: int = 256, input_act=None):
+    """ConvRot-256 rotation + row quantization (``quantize_and_rotate_rowwise``,
+    eager/quantization.py:878-895; CUDA int8_linear.cu:256-340)."""
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("x must be bf16")
+    x2, ldx = _rows(x)
+    m, k = x2.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    _lib.call("h3b200_quantize_int8_rowwise_convrot", x2.data_ptr(), m, k, ldx, convrot_groupsize,
+              input_act_code(input_act), q.data_ptr(), s.data_ptr(), _stream(x))
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+
+
+def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, s_channel: torch.Tensor,
+                     codebook: torch.Tensor | None = None, correction: torch.Tensor | None = None,
+                     bias: torch.Tensor | None = None, group_size: int = 16, convrot_groupsize: int = 256,
+                     out_dtype: torch.dtype = torch.bfloat16, grid: torch.Tensor | None = None,
+                     input_act=None) -> torch.Tensor:
+    """W4A8 linear (``comfy_kitchen`` w4a8_int8_linear, tensor/w4a8_int8.py:89-115; CUDA
+    backends/cuda/__init__.py:2139-2298): ConvRot-quantize x, INT8 GEMM against
+    the decoded int8 grid, dequant by ``s_channel``, asymmetric group correction.
+
+    ``grid`` is the decoded weight from :func:`dequant_int4_grouped_to_int8`;
+    pass it to keep the decode out of the per-call path (weights are static)."""
+    _need_cuda(x, qdata, s_rel, s_channel)
+    if codebook is not None:
+        raise NotImplementedError("codebook W4A8 is not built in h3b200")
+    if bias is not None:
+        raise NotImplementedError("bias is not built for W4A8")
+    if out_dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
+    n, kh = qdata.shape
+    k = kh * 2
+    if x.shape[-1] != k:
+        raise ValueError(f"Input K={x.shape[-1]} does not match qdata K={k}")
+    if grid is None:
+        grid = dequant_int4_grouped_to_int8(qdata, s_rel, group_size)
+    groups = k // group_size
+    corr = None
+    if correction is not None:
+        if tuple(correction.shape) != (groups, n):
+            raise ValueError(f"correction must have shape {(groups, n)}, got {tuple(correction.shape)}")
+        corr = correction.to(torch.bfloat16).contiguous()
+    sch = s_channel.to(torch.float32).contiguous()
+    if tuple(sch.shape) != (n,):
+        raise ValueError(f"s_channel must have shape {(n,)}, got {tuple(sch.shape)}")
+    x2, ldx = _rows(x)
+    m = x2.shape[0]
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    nbytes = int(_lib.load().h3b200_w4a8_linear_workspace_bytes(m, k, group_size))
+    work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _lib.call("h3b200_w4a8_int8_linear", x2.data_ptr(), ldx, grid.contiguous().data_ptr(), sch.data_ptr(), _ptr(corr),
+              group_size, convrot_groupsize, input_act_code(input_act), out.data_ptr(), m, n, k, work.data_ptr(),
+              nbytes, _stream(x))
+    return out.reshape(*x.shape[:-1], n)
