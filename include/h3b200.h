@@ -120,6 +120,18 @@ H3B200_API int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t
                                       float* row_absmax, h3b200_stream_t stream);
 
 /*
+ * Dequant + gated residual on reduced int32 accumulators (tensor-parallel fc2):
+ * out = bf16(residual + bf16(float(acc) * (x_scale[row] * w_scale[col])) * gate[col]).
+ * The same arithmetic as epilogue 3 of h3b200_int8_gemm_fused, for when the
+ * accumulators of a row-split fc2 were summed across ranks first (the
+ * reference's addcmul_ gated residual, h3serve/native_engine/model/fused_mlp.py:414-425).
+ * acc: int32 [m, n] contiguous; n % 8 == 0; out may alias residual.
+ */
+H3B200_API int h3b200_dequant_gated_residual(const int32_t* acc, const float* x_scale, const float* w_scale,
+                                             const void* gate, const void* residual, int64_t ldr, void* out,
+                                             int64_t ldo, int64_t m, int64_t n, h3b200_stream_t stream);
+
+/*
  * Full dynamically quantized INT8 linear: act -> per-row quantize -> GEMM ->
  * dequant (+ bias). Replaces comfy_kitchen int8_linear(x, weight, weight_scale,
  * bias, out_dtype, convrot=False, input_act) (__init__.py:722-764; CUDA

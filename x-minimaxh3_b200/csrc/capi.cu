@@ -148,6 +148,15 @@ int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t* w, int64_
   return from_cuda(h3::launch_gemm_i8(g, S(stream)), "int8_gemm_fused");
 }
 
+int h3b200_dequant_gated_residual(const int32_t* acc, const float* x_scale, const float* w_scale, const void* gate,
+                                  const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
+                                  h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || ldr < n || ldo < n) return fail(H3B200_ERR_INVALID, "dequant_gated_residual: bad shape");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!acc || !x_scale || !w_scale || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "dequant_gated_residual: NULL pointer");
+  return from_cuda(h3::launch_dequant_gated_residual(acc, x_scale, w_scale, gate, residual, ldr, out, ldo, m, n, S(stream)), "dequant_gated_residual");
+}
+
 int64_t h3b200_int8_linear_workspace_bytes(int64_t m, int64_t k) {
   return round_up(m * k, 256) + round_up(m * 4, 256) + 512;
 }

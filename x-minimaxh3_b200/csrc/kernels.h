@@ -37,6 +37,9 @@ struct GemmArgs {
   int64_t groups = 0;
 };
 
+cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,
+                                          const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,
+                                          int64_t n, cudaStream_t stream);
 cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
                                  int8_t* q, float* scale, cudaStream_t stream);

@@ -151,7 +151,51 @@ __global__ void apply_act_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloa
   if (i < n) y[i] = __float2bfloat16_rn(act_apply(__bfloat162float(x[i]), act));
 }
 
+// out = bf16(residual + bf16(float(acc) * (xs[row] * ws[col])) * gate[col]); 8 columns per thread.
+__global__ void dequant_gated_residual_kernel(const int32_t* __restrict__ acc, const float* __restrict__ xs,
+                                              const float* __restrict__ ws, const __nv_bfloat16* __restrict__ gate,
+                                              const __nv_bfloat16* residual, int64_t ldr, __nv_bfloat16* out,
+                                              int64_t ldo, int64_t m, int64_t n) {
+  const int64_t per_row = n / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= m * per_row) return;
+  const int64_t row = idx / per_row;
+  const int64_t c = (idx - row * per_row) * 8;
+  const float x = xs[row];
+  const uint4 a0 = *reinterpret_cast<const uint4*>(acc + row * n + c);
+  const uint4 a1 = *reinterpret_cast<const uint4*>(acc + row * n + c + 4);
+  const uint32_t av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  const uint4 rv = ldg_v4(residual + row * ldr + c);
+  const uint4 gv = ldg_nc_v4(gate + c);
+  const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float y0 = bf16_round(__fmul_rn(__int2float_rn((int)av[2 * e]), __fmul_rn(x, ws[c + 2 * e])));
+    float y1 = bf16_round(__fmul_rn(__int2float_rn((int)av[2 * e + 1]), __fmul_rn(x, ws[c + 2 * e + 1])));
+    o[e] = pack_bf16(__fadd_rn(bf16_lo(rw[e]), __fmul_rn(y0, bf16_lo(gw[e]))),
+                     __fadd_rn(bf16_hi(rw[e]), __fmul_rn(y1, bf16_hi(gw[e]))));
+  }
+  stg_v4(out + row * ldo + c, make_uint4(o[0], o[1], o[2], o[3]));
+}
+
 }  // namespace
+
+cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,
+                                          const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,
+                                          int64_t n, cudaStream_t stream) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  if (n % 8 || ldr % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(acc) & 15) ||
+      (reinterpret_cast<uintptr_t>(residual) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(gate) & 15))
+    return cudaErrorNotSupported;
+  const int64_t total = m * (n / 8);
+  dequant_gated_residual_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      acc, xs, ws, static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(residual), ldr,
+      static_cast<__nv_bfloat16*>(out), ldo, m, n);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;

@@ -23,6 +23,7 @@ __all__ = [
     "int8_linear_prequantized",
     "int8_linear",
     "int8_gemm_fused",
+    "dequant_gated_residual",
     "fused_gated_mlp",
     "adaln_rms_rope",
     "adaln_rms_rope_",
@@ -208,6 +209,24 @@ def int8_gemm_fused(a: torch.Tensor, w: torch.Tensor, epilogue: int, a_scale=Non
               _ptr(xs), _ptr(ws), 0 if ws is None else ws.numel(), _ptr(bias), _ptr(gate), _ptr(residual),
               0 if residual is None else residual.stride(0), out.data_ptr(), out.stride(0), _ptr(row_absmax),
               _stream(a))
+    return out
+
+
+def dequant_gated_residual(acc: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor, gate: torch.Tensor,
+                           residual: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + bf16(acc * (x_scale * w_scale)) * gate`` on (cross-rank reduced) int32 accumulators."""
+    _need_cuda(acc, x_scale, w_scale, gate, residual)
+    m, n = acc.shape
+    acc = acc.contiguous()
+    xs = x_scale.reshape(-1).to(torch.float32).contiguous()
+    ws = w_scale.reshape(-1).to(torch.float32).contiguous()
+    g = gate.reshape(-1).contiguous()
+    r2, ldr = _rows(residual)
+    if out is None:
+        out = torch.empty_like(r2)
+    o2, ldo = _rows(out)
+    _lib.call("h3b200_dequant_gated_residual", acc.data_ptr(), xs.data_ptr(), ws.data_ptr(), g.data_ptr(),
+              r2.data_ptr(), ldr, o2.data_ptr(), ldo, m, n, _stream(acc))
     return out
 
 

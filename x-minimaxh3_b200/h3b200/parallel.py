@@ -1,0 +1,160 @@
+"""Multi-GPU execution of the hot path (one process per GPU, torch.distributed / NCCL).
+
+The reference is single-GPU (no collective anywhere); scaling it out is new.
+Two modes:
+
+* Token sharding (data parallel over tokens). The quantizer, the MLP and the
+  norm-RoPE are per-token functions, so each rank takes a contiguous token
+  range (and the matching rows of the RoPE table) and runs the single-GPU
+  kernels on it. There is no collective on the data path; results equal the
+  single-GPU results bit for bit.
+* Tensor-parallel MLP (long-video config). fc1 is column-split (rank r owns
+  ffn rows [r*ffn/g, (r+1)*ffn/g) of W1), GELU is local, and the per-token
+  requant scale needs the row absmax over all ffn columns: one all-reduce(MAX)
+  of an fp32 [M] vector, after which every rank quantizes with the global scale
+  (so the int8 activations are the single-GPU ones). fc2 is row-split along
+  its K = ffn: each rank produces partial int32 accumulators, summed exactly by
+  an all-reduce(SUM) over int32, followed by the dequant + gated-residual
+  epilogue. The output is bit-identical to the single-GPU fused MLP.
+  Tokens are processed in chunks; the collectives of chunk i run
+  asynchronously while chunk i+1 computes.
+
+The kernel calls go through an ``ops`` object (default: the CUDA kernels of
+this package) so the orchestration can be exercised on CPU ranks in tests.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(m: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous near-equal token range of ``rank`` (the first ``m % world`` ranks get one more)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world {world}")
+    base, extra = divmod(m, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def column_shard(ffn: int, world: int, rank: int) -> tuple[int, int]:
+    """fc1 output-column (= fc2 input-column) range owned by ``rank`` in the tensor-parallel MLP."""
+    if ffn % world:
+        raise ValueError(f"ffn={ffn} is not divisible by the tensor-parallel size {world}")
+    step = ffn // world
+    return rank * step, (rank + 1) * step
+
+
+class CudaOps:
+    """Stage kernels of the fused MLP (libh3b200.so)."""
+
+    def quantize(self, x):
+        from .ops import quantize_int8_rowwise
+
+        return quantize_int8_rowwise(x)
+
+    def fc1_gelu_absmax(self, xq, xs, w1q, s1, absmax):
+        from .ops import EPI_GELU_ABSMAX, int8_gemm_fused
+
+        return int8_gemm_fused(xq, w1q, EPI_GELU_ABSMAX, xs, s1, row_absmax=absmax)
+
+    def quantize_absmax(self, a, absmax):
+        from .ops import quantize_int8_rowwise_absmax
+
+        return quantize_int8_rowwise_absmax(a, absmax)
+
+    def gemm_i32(self, q, w):
+        from .ops import EPI_I32, int8_gemm_fused
+
+        return int8_gemm_fused(q, w, EPI_I32)
+
+    def dequant_gated_residual(self, acc, xs, ws, gate, residual, out):
+        from .ops import dequant_gated_residual
+
+        return dequant_gated_residual(acc, xs, ws, gate, residual, out)
+
+    def fused_mlp(self, residual, x, w1q, s1, w2q, s2, gate, out):
+        from .ops import fused_gated_mlp
+
+        return fused_gated_mlp(residual, x, w1q, s1, w2q, s2, gate, out=out)
+
+    def norm_rope(self, q, k, table, wq, wk, scale, shift, eps, span):
+        from .ops import adaln_rms_rope
+
+        return adaln_rms_rope(q, k, table, wq, wk, scale, shift, eps, span)
+
+
+@dataclass
+class TPShard:
+    """This rank's slice of one gated MLP's weights for tensor parallelism."""
+
+    w1q: torch.Tensor  # [ffn/g, d]
+    s1: torch.Tensor   # [ffn/g]
+    w2q: torch.Tensor  # [d, ffn/g] (contiguous)
+    s2: torch.Tensor   # [d] (replicated)
+
+    @classmethod
+    def from_full(cls, w1q, s1, w2q, s2, world: int, rank: int) -> "TPShard":
+        lo, hi = column_shard(w1q.shape[0], world, rank)
+        return cls(w1q[lo:hi].contiguous(), s1[lo:hi].contiguous(), w2q[:, lo:hi].contiguous(), s2.contiguous())
+
+
+def tp_gated_mlp(x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor, shard: TPShard,
+                 group=None, chunk_tokens: int = 8192, ops=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tensor-parallel fused gated W8A8 MLP; ``x``/``residual`` [M, d] are replicated on every rank.
+
+    Every rank takes the same collective steps in the same order (two
+    all-reduces per chunk), so the ranks stay matched in every path."""
+    ops = ops or CudaOps()
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty_like(residual)
+    pending = []
+    for lo in range(0, m, chunk_tokens):
+        hi = min(m, lo + chunk_tokens)
+        xq, xs = ops.quantize(x[lo:hi])
+        absmax = torch.zeros(hi - lo, dtype=torch.float32, device=x.device)
+        a = ops.fc1_gelu_absmax(xq, xs, shard.w1q, shard.s1, absmax)
+        dist.all_reduce(absmax, op=dist.ReduceOp.MAX, group=group)
+        q2, xs2 = ops.quantize_absmax(a, absmax)
+        acc = ops.gemm_i32(q2, shard.w2q)
+        work = dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=group, async_op=True)
+        pending.append((lo, hi, acc, xs2, work))
+    for lo, hi, acc, xs2, work in pending:
+        work.wait()
+        ops.dequant_gated_residual(acc, xs2, shard.s2, gate, residual[lo:hi], out[lo:hi])
+    return out
+
+
+def token_sharded_mlp(x_shard, residual_shard, gate, w1q, s1, w2q, s2, ops=None, out=None):
+    """Data-parallel MLP on this rank's token shard (no collective)."""
+    ops = ops or CudaOps()
+    if out is None:
+        out = torch.empty_like(residual_shard)
+    return ops.fused_mlp(residual_shard, x_shard, w1q, s1, w2q, s2, gate, out)
+
+
+def token_sharded_block(q, k, table, wq, wk, scale, shift, x, residual, gate, w1q, s1, w2q, s2,
+                        eps: float = 1e-6, ops=None):
+    """Long-video DiT-block slice on this rank's tokens: norm-RoPE on Q/K, then the W8A8 MLP.
+
+    ``q``/``k``/``table``/``x``/``residual`` are this rank's rows (see :func:`shard_range`)."""
+    ops = ops or CudaOps()
+    qo, ko = ops.norm_rope(q, k, table, wq, wk, scale, shift, eps, "row")
+    y = token_sharded_mlp(x, residual, gate, w1q, s1, w2q, s2, ops=ops)
+    return qo, ko, y
+
+
+def gather_tokens(local: torch.Tensor, m: int, group=None) -> torch.Tensor:
+    """All-gather contiguous token shards (verification only; not on the data path)."""
+    world = dist.get_world_size(group)
+    sizes = [shard_range(m, world, r) for r in range(world)]
+    width = max(hi - lo for lo, hi in sizes)
+    pad = torch.zeros((width,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[: local.shape[0]] = local
+    bufs = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(bufs, pad, group=group)
+    return torch.cat([b[: hi - lo] for b, (lo, hi) in zip(bufs, sizes)], dim=0)
