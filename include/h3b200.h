@@ -144,6 +144,26 @@ H3B200_API int h3b200_int8_linear(const void* x, int64_t ldx, const int8_t* w, c
                        int64_t workspace_bytes, h3b200_stream_t stream);
 
 /*
+ * Allocation-free variant of h3b200_int8_linear. It has no counterpart in the
+ * reference. It is for callers that cannot allocate device memory per call
+ * (a runtime that owns all device memory and passes only inputs and outputs,
+ * or a serving loop that must not allocate after start-up): the quantized
+ * activation and its row scales live in a static device array of
+ * h3b200_int8_linear_noalloc_max_scratch_bytes() bytes (8 MiB) that every GPU
+ * loading the library holds until exit, and no memory is allocated.
+ * Limit: round_up(m * k, 256) + 4 * m must fit in that array (e.g. m <= 2600 at
+ * k = 3072); larger calls are rejected with H3B200_ERR_INVALID. The first call
+ * on a device looks up the array's device address with that device current;
+ * make that first call before any stream capture. All calls share the array:
+ * calls that overlap on the GPU race on it. Same arithmetic and result as
+ * h3b200_int8_linear; the caller still passes x, w, scales, bias and out.
+ */
+H3B200_API int64_t h3b200_int8_linear_noalloc_max_scratch_bytes(void);
+H3B200_API int h3b200_int8_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
+                                          int64_t w_scale_numel, const void* bias, int act, void* out, int64_t m,
+                                          int64_t n, int64_t k, h3b200_stream_t stream);
+
+/*
  * Fused gated W8A8 MLP on a token chunk:
  *   h = int8_linear(x, w1, s1); a = act(h); y = int8_linear(a, w2, s2);
  *   out = residual + y * gate   (bf16 addcmul)

@@ -5,6 +5,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -295,6 +296,92 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
     if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction");
   }
   return H3B200_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free INT8 linear.
+//
+// Some callers cannot allocate device memory for a call: a host runtime that
+// hands this library only the input and output buffers it owns, or a serving
+// loop that forbids allocation after start-up so that its memory use stays
+// fixed. For them, h3b200_int8_linear_noalloc keeps the quantized activation
+// (int8 [m, k]) and its row scales (fp32 [m]) in the static device array below
+// instead of a caller workspace. Every GPU that loads this library holds the
+// array until the process exits. All calls share it and it keeps the last
+// call's contents; both parts are fully rewritten by every call, so nothing
+// has to start at zero. Calls whose executions overlap on the GPU (different
+// streams, or different host threads on one device) race on it.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // 8 MiB per device
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch array on `device`. The first call on a device
+// looks it up with that device current (cudaGetSymbolAddress); later calls use
+// the cached address. Host code must never pass g_noalloc_scratch itself to a
+// kernel: on the host that name is only a stand-in, not a device address.
+cudaError_t noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return e;
+    if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t h3b200_int8_linear_noalloc_max_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int h3b200_int8_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
+                               int64_t w_scale_numel, const void* bias, int act, void* out, int64_t m, int64_t n,
+                               int64_t k, h3b200_stream_t stream) {
+  if (m < 0 || n < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: bad shape");
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: unsupported act code %d", act);
+  if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: weight scale must be scalar or per-output-channel");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!x || !w || !w_scale || !out) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: NULL pointer");
+  if (k % 16 || n % 8) return fail(H3B200_ERR_UNSUPPORTED, "int8_linear_noalloc: needs k %% 16 == 0 and n %% 8 == 0");
+  if (m > (1ll << 30) || k > (1ll << 30)) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: m or k too large");
+  const int64_t q_bytes = round_up(m * k, 256);
+  const int64_t need = q_bytes + m * 4;
+  if (need > kNoAllocScratchBytes)
+    return fail(H3B200_ERR_INVALID,
+                "int8_linear_noalloc: m=%lld, k=%lld needs %lld bytes of scratch (int8 activations + fp32 row "
+                "scales) but the static scratch holds %lld; split the rows or use h3b200_int8_linear",
+                (long long)m, (long long)k, (long long)need, (long long)kNoAllocScratchBytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  void* base = nullptr;
+  if (e == cudaSuccess) e = noalloc_scratch(dev, &base);
+  if (e != cudaSuccess) return from_cuda(e, "int8_linear_noalloc: scratch set-up");
+  int8_t* xq = static_cast<int8_t*>(base);
+  float* xs = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + q_bytes);
+  cudaStream_t st = S(stream);
+  e = h3::launch_quantize_rows(x, ldx, m, k, act, nullptr, xq, xs, st);
+  if (e != cudaSuccess) return from_cuda(e, "int8_linear_noalloc: quantize");
+  h3::GemmArgs g;
+  g.a = xq; g.w = w; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = h3::kEpiBF16; g.a_scale = xs; g.w_scale = w_scale; g.w_scale_per_channel = (w_scale_numel == n && n > 1) ? 1 : 0;
+  g.bias = bias; g.out = out; g.ldo = n;
+  return from_cuda(h3::launch_gemm_i8(g, st), "int8_linear_noalloc: gemm");
 }
 
 }  // extern "C"

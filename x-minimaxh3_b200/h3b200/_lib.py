@@ -38,6 +38,8 @@ SIGNATURES = {
     "h3b200_dequant_gated_residual": (_i32, [_p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _p]),
     "h3b200_int8_linear_workspace_bytes": (_i64, [_i64, _i64]),
     "h3b200_int8_linear": (_i32, [_p, _i64, _p, _p, _i64, _p, _i32, _p, _i64, _i64, _i64, _p, _i64, _p]),
+    "h3b200_int8_linear_noalloc_max_scratch_bytes": (_i64, []),
+    "h3b200_int8_linear_noalloc": (_i32, [_p, _i64, _p, _p, _i64, _p, _i32, _p, _i64, _i64, _i64, _p]),
     "h3b200_fused_gated_mlp_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "h3b200_fused_gated_mlp": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32,
                                       _p, _i64, _p]),
