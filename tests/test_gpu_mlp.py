@@ -82,3 +82,19 @@ def test_mlp_rejects_bad_shapes():
         h3b200.fused_gated_mlp(x, x, wt.w1q, wt.s1, wt.w2q, wt.s2, torch.zeros(3, dtype=torch.bfloat16, device="cuda"))
     with pytest.raises(NotImplementedError):
         h3b200.fused_gated_mlp(x, x, wt.w1q, wt.s1, wt.w2q, wt.s2, x[0], act="swiglu")
+
+
+def test_mlp_host_pipeline_matches_device_call():
+    """Host-buffer entry point: chunked, copy-overlapped, bit-identical to one device call."""
+    gen, wt = _weights(512, 2048, 9)
+    m = 1000                                               # 3 full chunks of 300 + a ragged one
+    x = randn_bf16((m, 512), gen).pin_memory()
+    res = randn_bf16((m, 512), gen).pin_memory()
+    gate = randn_bf16((512,), gen).cuda()
+    expect = h3b200.fused_gated_mlp(res.cuda(), x.cuda(), wt.w1q, wt.s1, wt.w2q, wt.s2, gate)
+    out = h3b200.fused_gated_mlp_host(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, chunk_tokens=300)
+    np.testing.assert_array_equal(t2u(out), t2u(expect))
+    # a second call reuses the staging slots; in place on the residual buffer
+    res2 = res.clone().pin_memory()
+    h3b200.fused_gated_mlp_host(res2, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=res2, chunk_tokens=300)
+    np.testing.assert_array_equal(t2u(res2), t2u(expect))

@@ -40,7 +40,9 @@ constexpr int NUM_EPI_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint32_t IDESC = umma_idesc_i8(BM, BN);
 constexpr int BAR_BYTES = 256;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+constexpr int STAGE_OPS_BYTES = NUM_EPI_WARPS * 2 * 128 * 4;   // per-warp column scales + bias/gate
+constexpr int GELU_TAB_BYTES = 2 * 19 * 128 * 2;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + STAGE_OPS_BYTES + GELU_TAB_BYTES + 1024;
 
 // status codes recorded when a bounded wait expires
 constexpr unsigned kErrProducer = 0x101, kErrMmaAcc = 0x102, kErrMmaFull = 0x103, kErrEpi = 0x104,
@@ -61,9 +63,81 @@ struct KParams {
   float* row_absmax;
 };
 
+// Exact bf16 tanh-GELU by table. The activation input is a bf16 value, so the
+// GELU is a function on at most 65,536 inputs. Every CTA of the GELU variant
+// fills a shared-memory table with gelu_tanh_exact (bit-identical to the
+// reference, verified on all bf16 inputs) for |x| in [2^-16, 8) and both signs
+// (2 x 19 binades x 128 mantissas). The lookup itself is branch-free (the
+// index is clamped into the table); a lane whose chunk holds an input outside
+// that range (rare: zero, tiny, huge, non-finite) recomputes the chunk with
+// gelu_tanh_exact.
+constexpr uint32_t kGeluE0 = 111;   // exponent field of 2^-16
+constexpr uint32_t kGeluNE = 19;    // binades 2^-16 .. 2^2
+constexpr int kGeluEntries = 2 * kGeluNE * 128;
+
+__device__ __forceinline__ uint32_t gelu_table_bits(uint32_t i) {
+  const uint32_t sgn = i / (kGeluNE * 128);
+  const uint32_t rem = i - sgn * (kGeluNE * 128);
+  return (sgn << 15) | ((kGeluE0 + rem / 128) << 7) | (rem & 127u);
+}
+
+// Table lookup; sets `miss` when hb is outside the table's range.
+__device__ __forceinline__ uint32_t gelu_lookup_fast(uint32_t hb, const uint16_t* tab, bool& miss) {
+  const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
+  miss |= rel >= kGeluNE;
+  return tab[(hb >> 15) * (kGeluNE * 128) + min(rel, kGeluNE - 1) * 128 + (hb & 0x7Fu)];
+}
+
+__device__ __forceinline__ uint32_t gelu_lookup(uint32_t hb, const uint16_t* tab) {
+  const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
+  if (rel < kGeluNE) return tab[(hb >> 15) * (kGeluNE * 128) + rel * 128 + (hb & 0x7Fu)];
+  return bf16_bits(gelu_tanh_exact(__uint_as_float(hb << 16)));
+}
+
+// Dequantized bf16 bits of the 32 accumulators of one chunk (GELU variant input).
+__device__ __forceinline__ uint32_t dequant_bits(uint32_t acc, float xs, float ws) {
+  return bf16_bits(__fmul_rn(__int2float_rn((int)acc), __fmul_rn(xs, ws)));
+}
+
+// fc1 chunk: out bits (packed pairs) = gelu(bf16(acc * (xs * ws))); chunk absmax bits.
+__device__ __forceinline__ void gelu_chunk(const uint32_t (&r)[32], float xs, const float* ws_s, const uint16_t* gtab,
+                                           uint32_t (&ob)[16], uint32_t& amax_bits) {
+  bool miss = false;
+  uint32_t cmax = 0u;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
+    const uint32_t g0 = gelu_lookup_fast(dequant_bits(r[4 * q + 0], xs, w4.x), gtab, miss);
+    const uint32_t g1 = gelu_lookup_fast(dequant_bits(r[4 * q + 1], xs, w4.y), gtab, miss);
+    const uint32_t g2 = gelu_lookup_fast(dequant_bits(r[4 * q + 2], xs, w4.z), gtab, miss);
+    const uint32_t g3 = gelu_lookup_fast(dequant_bits(r[4 * q + 3], xs, w4.w), gtab, miss);
+    ob[2 * q] = g0 | (g1 << 16);
+    ob[2 * q + 1] = g2 | (g3 << 16);
+    cmax = max(cmax, max(max(g0 & 0x7FFFu, g1 & 0x7FFFu), max(g2 & 0x7FFFu, g3 & 0x7FFFu)));
+  }
+  if (miss) {
+    cmax = 0u;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
+      const uint32_t g0 = gelu_lookup(dequant_bits(r[4 * q + 0], xs, w4.x), gtab);
+      const uint32_t g1 = gelu_lookup(dequant_bits(r[4 * q + 1], xs, w4.y), gtab);
+      const uint32_t g2 = gelu_lookup(dequant_bits(r[4 * q + 2], xs, w4.z), gtab);
+      const uint32_t g3 = gelu_lookup(dequant_bits(r[4 * q + 3], xs, w4.w), gtab);
+      ob[2 * q] = g0 | (g1 << 16);
+      ob[2 * q + 1] = g2 | (g3 << 16);
+      cmax = max(cmax, max(max(g0 & 0x7FFFu, g1 & 0x7FFFu), max(g2 & 0x7FFFu, g3 & 0x7FFFu)));
+    }
+  }
+  amax_bits = max(amax_bits, cmax);
+}
+
+// One 32-column chunk of one accumulator row. ws_s / aux_s: this warp's staged
+// per-column weight scales and bias-or-gate (fp32) for the chunk.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const KParams& p, int row, int col0, const uint32_t (&r)[32],
-                                               float xs, float& amax, int lane) {
+                                               float xs, const float* ws_s, const float* aux_s,
+                                               const uint16_t* gtab, uint32_t& amax_bits) {
   const bool row_ok = row < p.m;
   if constexpr (EPI == kEpiI32) {
     if (row_ok) {
@@ -74,66 +148,52 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, int row, int co
     }
     return;
   } else {
-    const int cl = col0 + lane;
-    const bool col_ok = cl < p.n;
-    const float wsl = p.w_pc ? (col_ok ? __ldg(p.w_scale + cl) : 0.0f) : __ldg(p.w_scale);
-    float aux = 0.0f;
-    if constexpr (EPI == kEpiBF16) {
-      if (p.bias != nullptr && col_ok) aux = __bfloat162float(p.bias[cl]);
-    }
-    if constexpr (EPI == kEpiGatedResidual) {
-      if (col_ok) aux = __bfloat162float(p.gate[cl]);
-    }
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float sc = __fmul_rn(xs, __shfl_sync(0xffffffffu, wsl, j));
-      v[j] = bf16_round(__fmul_rn(__int2float_rn((int)r[j]), sc));
-    }
-    if constexpr (EPI == kEpiBF16) {
-      if (p.bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = bf16_round(__fadd_rn(v[j], __shfl_sync(0xffffffffu, aux, j)));
-      }
-    }
+    uint32_t ob[16];
     if constexpr (EPI == kEpiGeluAbsmax) {
+      gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
+    } else {
+      uint32_t res_w[16];
+      if constexpr (EPI == kEpiGatedResidual) {
+        if (row_ok) {
+          const __nv_bfloat16* rp = p.residual + (int64_t)row * p.ldr + col0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        v[j] = bf16_round(gelu_tanh_exact(v[j]));
-        amax = fmaxf(amax, fabsf(v[j]));
-      }
-    }
-    if constexpr (EPI == kEpiGatedResidual) {
-      float g[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) g[j] = __shfl_sync(0xffffffffu, aux, j);
-      if (row_ok) {
-        const __nv_bfloat16* rp = p.residual + (int64_t)row * p.ldr + col0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (col0 + 8 * q < p.n) {
-            const uint4 rv = ldg_v4(rp + 8 * q);
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = 8 * q + 2 * e;
-              v[j] = bf16_round(__fadd_rn(bf16_lo(rw[e]), __fmul_rn(v[j], g[j])));
-              v[j + 1] = bf16_round(__fadd_rn(bf16_hi(rw[e]), __fmul_rn(v[j + 1], g[j + 1])));
-            }
+          for (int q = 0; q < 4; ++q) {
+            uint4 rv = make_uint4(0, 0, 0, 0);
+            if (col0 + 8 * q < p.n) rv = ldg_v4(rp + 8 * q);
+            res_w[4 * q] = rv.x; res_w[4 * q + 1] = rv.y; res_w[4 * q + 2] = rv.z; res_w[4 * q + 3] = rv.w;
           }
         }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+        const float4 a4 = *reinterpret_cast<const float4*>(aux_s + 4 * q);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+        uint32_t hb[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 4 * q + e;
+          uint32_t b = dequant_bits(r[j], xs, wv[e]);
+          if constexpr (EPI == kEpiBF16) {
+            if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
+          }
+          if constexpr (EPI == kEpiGatedResidual) {
+            const uint32_t rw = res_w[j >> 1];
+            const float rv = (j & 1) ? bf16_hi(rw) : bf16_lo(rw);
+            b = bf16_bits(__fadd_rn(rv, __fmul_rn(__uint_as_float(b << 16), av[e])));
+          }
+          hb[e] = b;
+        }
+        ob[2 * q] = hb[0] | (hb[1] << 16);
+        ob[2 * q + 1] = hb[2] | (hb[3] << 16);
       }
     }
     if (row_ok) {
       __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (col0 + 8 * q < p.n) {
-          const int j = 8 * q;
-          stg_v4(o + j, make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
-                                   pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7])));
-        }
-      }
+      for (int q = 0; q < 4; ++q)
+        if (col0 + 8 * q < p.n) stg_v4(o + 8 * q, make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]));
     }
   }
 }
@@ -150,6 +210,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  float* ops_smem = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + STAGES * STAGE_BYTES + BAR_BYTES + STAGE_OPS_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -172,6 +234,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 2) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
+  }
+  if constexpr (EPI == kEpiGeluAbsmax) {
+    for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
+      gelu_tab[i] = (uint16_t)bf16_bits(gelu_tanh_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
   }
   tc_fence_before();
   __syncthreads();
@@ -247,32 +313,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int ew = warp - EPI_WARP0;
     const int quarter = warp & 3;          // TMEM lanes [32*quarter, 32*quarter + 32)
     const int half = ew >> 2;              // columns [128*half, 128*half + 128)
+    float* ws_s = ops_smem + ew * 256;     // this warp's 128 column scales ...
+    float* aux_s = ws_s + 128;             // ... and 128 bias / gate values
     int tcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
       const int m_blk = tile / p.num_n_blk;
       const int n_blk = tile - m_blk * p.num_n_blk;
       const int acc = tcount & 1;
       const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
-      if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
-      tc_fence_after();
       const int row = m_blk * BM + quarter * 32 + lane;
       const int col_base = n_blk * BN + half * 128;
+      if constexpr (EPI != kEpiI32) {
+        // stage this tile's per-column operands while the MMAs run
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = lane + 32 * i;
+          const int col = col_base + c;
+          const bool ok = col < p.n;
+          ws_s[c] = ok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
+          float a = 0.0f;
+          if (EPI == kEpiBF16 && p.bias != nullptr && ok) a = __bfloat162float(p.bias[col]);
+          if (EPI == kEpiGatedResidual && ok) a = __bfloat162float(p.gate[col]);
+          aux_s[c] = a;
+        }
+        __syncwarp();
+      }
+      if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
+      tc_fence_after();
       float xs = 0.0f;
       if constexpr (EPI != kEpiI32) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
-      float amax = 0.0f;
+      uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         tmem_wait_ld();
-        if (col_base + c < p.n) epilogue_chunk<EPI>(p, row, col_base + c, r, xs, amax, lane);
+        if (col_base + c < p.n)
+          epilogue_chunk<EPI>(p, row, col_base + c, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       if constexpr (EPI == kEpiGeluAbsmax) {
-        if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, __float_as_uint(amax));
+        if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, amax_bits << 16);
       }
     }
   }

@@ -11,23 +11,43 @@
 // RMSNorm: rstd = 1 / sqrt(mean(x^2) + eps) in fp32, y = bf16((x * rstd) * w).
 // The sum of squares is accumulated in double so the fp32 mean is the
 // correctly rounded one (the reference sums in fp32, order ISA-dependent).
+// Modulation: bf16(bf16(h * bf16(1 + scale)) + shift); both steps are one
+// correctly rounded bf16x2 operation on bf16 operands, which equals the
+// reference's fp32 operation followed by a bf16 rounding (the fp32 product of
+// two bf16 values is exact, and the fp32 sum of two bf16 values rounds to the
+// same bf16 value as the exact sum).
 // RoPE: y0 = t00*x0 + t01*x1, y1 = t10*x0 + t11*x1 (fp32, two products and one
-// add), bf16 store; table fp32 [m, rot_dim/2, 2, 2].
+// add, no fusion: scalar __fmul_rn / __fadd_rn), bf16 store; table fp32
+// [m, rot_dim/2, 2, 2].
 //
-// B200 layout: one warp per token, persistent over tokens. Lane l owns the
-// 16-byte vectors v = l + 32*j of the heads*128-wide row, so its position
-// inside a head (v mod 16 = l mod 16) is the same for every j: the RoPE
-// coefficients it needs are loaded once per token into registers and the
-// rotation partner (vector v +- rot_dim/16, same head) sits in lane
-// (l & 16) | partner, one shuffle away. Q and K rows of a token are loaded
-// together (2 x 6 KB in flight per warp), each byte is read and written once.
+// B200 design: a persistent CTA per SM streams tokens through a shared-memory
+// ring with bulk asynchronous copies (cp.async.bulk, no multicast): one
+// producer thread loads a token's Q row, K row and rotation-table row into a
+// stage; each of kPairs warp pairs takes every kPairs-th token of the CTA, one
+// warp for Q and one for K. A warp reads its row from the stage twice (sum of
+// squares, reduced with shuffles; then normalise / modulate / rotate; lane l
+// owns the 16-byte vectors l + 32*j), writes the result with coalesced 128-bit
+// stores and frees the stage. Lane l's
+// position inside a head (l mod 16) is the same for every j, so its RoPE
+// coefficients are read once per token and its rotation partner (vector
+// v +- rot_dim/16 of the same head) is one shuffle away. Per-column weights,
+// bf16(1 + scale) and shift are staged in shared memory once per CTA. The
+// normalisation products use the packed f32x2 multiply of sm_100 (two IEEE
+// round-to-nearest products per instruction). The RoPE sums stay scalar: a
+// packed multiply followed by a packed add was measured to round like a fused
+// multiply-add (last-bit differences in about 1 of 10^5 outputs), even with
+// contraction disabled.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace h3 {
 namespace {
 
-constexpr int kNRThreads = 256;
+constexpr int kPairs = 5;                          // consumer warp pairs per CTA
+constexpr int kNRThreads = 32 * (1 + 2 * kPairs);  // producer warp + consumers
+constexpr int kMaxStages = 15;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr unsigned kErrNRFull = 0x201, kErrNRProducer = 0x202, kErrNRDrain = 0x203;
 
 struct NRParams {
   const __nv_bfloat16* x[2];
@@ -39,174 +59,286 @@ struct NRParams {
   const __nv_bfloat16* shift;
   int64_t m;
   int heads;
-  int half_v;   // rot_dim / 16: vectors in each rotation half
+  int half_v;     // rot_dim / 16: vectors in each rotation half
   int row_elems;
+  int row_bytes;  // heads * 256
+  int tab_bytes;  // rot_dim / 2 * 16
+  int stages;
   float eps;
 };
 
-template <int VPL, bool ROW_SPAN, bool MODULATE>
-__global__ void __launch_bounds__(kNRThreads) adaln_rms_rope_kernel(const NRParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = ((int64_t)blockIdx.x * kNRThreads + threadIdx.x) >> 5;
-  const int64_t nw = ((int64_t)gridDim.x * kNRThreads) >> 5;
-  const int hv = lane & 15;
-  const int nvec = p.heads * 16;
-  // rotation role of this lane: 0 = first half, 1 = second half, 2 = passthrough
-  const int role = hv < p.half_v ? 0 : (hv < 2 * p.half_v ? 1 : 2);
-  const int partner = (lane & 16) | (role == 0 ? hv + p.half_v : (role == 1 ? hv - p.half_v : hv));
-  const int pair0 = 8 * (role == 0 ? hv : hv - p.half_v);
-  const int64_t freq_stride = (int64_t)p.half_v * 8 * 4;
+// ---- packed arithmetic -----------------------------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// two fp32 (packed) -> bf16x2 (low half from the low float), round to nearest even
+__device__ __forceinline__ uint32_t f2_to_bf16x2(uint64_t v) {
+  uint32_t r, lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "r"(hi), "r"(lo));
+  return r;
+}
+// bf16x2 -> two fp32 (packed)
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(w << 16), "r"(w & 0xFFFF0000u));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 
-  // head-span weights depend only on the lane's in-head position
-  uint4 whead[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-  if (!ROW_SPAN) {
-    whead[0] = ldg_nc_v4(p.w[0] + 8 * hv);
-    whead[1] = ldg_nc_v4(p.w[1] + 8 * hv);
+// ---- bulk copy global -> shared, completion counted on an mbarrier ---------
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int VPL, bool ROW_SPAN, bool MODULATE, bool FULL_ROT>
+__global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int nvec = p.heads * 16;
+  const int S = p.stages;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty_bar = full_bar + kMaxStages;
+  uint4* cst = reinterpret_cast<uint4*>(smem + 256);
+  // ROW_SPAN: per-vector weights of Q (cst[0, nvec)) and K (cst[nvec, 2 nvec))
+  uint4* m_s = cst + (ROW_SPAN ? 2 : 0) * nvec;                // MODULATE: bf16(1 + scale)
+  uint4* sh_s = m_s + nvec;                                    // MODULATE: shift
+  const int n_cst = ((ROW_SPAN ? 2 : 0) + (MODULATE ? 2 : 0)) * nvec;
+  uint8_t* ring = smem + 256 + ((n_cst * 16 + 127) & ~127);
+  const int stage_bytes = 2 * p.row_bytes + p.tab_bytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t G = gridDim.x;
+  const int64_t cnt = p.m > blockIdx.x ? (p.m - blockIdx.x + G - 1) / G : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 2);
+    }
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < nvec; i += kNRThreads) {
+    if (ROW_SPAN) {
+      cst[i] = ldg_nc_v4(p.w[0] + 8 * i);
+      cst[nvec + i] = ldg_nc_v4(p.w[1] + 8 * i);
+    }
+    if (MODULATE) {
+      const uint4 sc = ldg_nc_v4(p.scale + 8 * i);
+      const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sc);
+      uint4 mv;
+      uint32_t* mw = reinterpret_cast<uint32_t*>(&mv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mw[e] = pack_bf16(__fadd_rn(1.0f, bf16_lo(sw[e])), __fadd_rn(1.0f, bf16_hi(sw[e])));
+      m_s[i] = mv;
+      sh_s[i] = ldg_nc_v4(p.shift + 8 * i);
+    }
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer ----------------
+      int64_t j = 0;
+      for (; j < cnt; ++j) {
+        const int s = (int)(j % S);
+        const uint32_t use = (uint32_t)(j / S);
+        if (!mbar_wait(&empty_bar[s], (use & 1u) ^ 1u, kErrNRProducer)) break;
+        const int64_t tok = blockIdx.x + j * G;
+        uint8_t* st = ring + (size_t)s * stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)stage_bytes);
+        bulk_g2s(st, p.x[0] + tok * p.ldx[0], (uint32_t)p.row_bytes, &full_bar[s]);
+        bulk_g2s(st + p.row_bytes, p.x[1] + tok * p.ldx[1], (uint32_t)p.row_bytes, &full_bar[s]);
+        bulk_g2s(st + 2 * p.row_bytes, reinterpret_cast<const uint8_t*>(p.freqs) + tok * (int64_t)p.tab_bytes,
+                 (uint32_t)p.tab_bytes, &full_bar[s]);
+      }
+      // every copy issued lands before the CTA may exit
+      for (int64_t i = (j > S ? j - S : 0); i < j; ++i)
+        mbar_wait(&full_bar[i % S], (uint32_t)(i / S) & 1u, kErrNRDrain, 200000000ull);
+    }
+    return;
   }
 
-  for (int64_t tok = gw; tok < p.m; tok += nw) {
-    uint4 v[2][VPL];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const __nv_bfloat16* xr = p.x[t] + tok * p.ldx[t];
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int vi = lane + 32 * j;
-        v[t][j] = vi < nvec ? ldg_v4(xr + 8 * vi) : make_uint4(0, 0, 0, 0);
-      }
-    }
-    // RoPE coefficients for this lane's 8 pairs: (t00, t01) or (t10, t11)
-    float ca[8], cb[8];
+  // ---------------- consumers ----------------
+  const int cw = warp - 1;
+  const int pair = cw >> 1;
+  const int t = cw & 1;  // 0 = Q, 1 = K
+  const int hv = lane & 15;
+  const int half_v = p.half_v;
+  const int role = hv < half_v ? 0 : (hv < 2 * half_v ? 1 : 2);  // first half, second half, pass-through
+  const int partner = (lane & 16) | (role == 0 ? hv + half_v : (role == 1 ? hv - half_v : hv));
+  const int pair0 = 8 * (role == 0 ? hv : (role == 1 ? hv - half_v : 0));
+
+  const uint4* w_row = cst + t * nvec;
+  uint4 whead = make_uint4(0, 0, 0, 0);
+  if (!ROW_SPAN) whead = ldg_nc_v4(p.w[t] + 8 * hv);
+  __nv_bfloat16* const ybase = p.y[t];
+  const int64_t ldy = p.ldy[t];
+
+  for (int64_t j = pair; j < cnt; j += kPairs) {
+    const int s = (int)(j % S);
+    if (!mbar_wait(&full_bar[s], (uint32_t)(j / S) & 1u, kErrNRFull)) break;
+    const uint8_t* st = ring + (size_t)s * stage_bytes;
+    const uint4* xs = reinterpret_cast<const uint4*>(st + t * p.row_bytes);
+    // RoPE coefficients of this lane's 8 pairs: out = A * own + B * partner
+    uint64_t A[4], B[4];
     if (role != 2) {
-      const float4* fr = reinterpret_cast<const float4*>(p.freqs + tok * freq_stride) + pair0;
+      const float4* fr = reinterpret_cast<const float4*>(st + 2 * p.row_bytes) + pair0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float4 c = __ldg(fr + e);
-        ca[e] = role == 0 ? c.x : c.z;
-        cb[e] = role == 0 ? c.y : c.w;
+      for (int e = 0; e < 4; ++e) {
+        const float4 c0 = fr[2 * e], c1 = fr[2 * e + 1];
+        // role 0 (x0): t00 * x0 + t01 * x1; role 1 (x1): t11 * x1 + t10 * x0
+        A[e] = role == 0 ? f2_pack(c0.x, c1.x) : f2_pack(c0.w, c1.w);
+        B[e] = role == 0 ? f2_pack(c0.y, c1.y) : f2_pack(c0.z, c1.z);
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ca[e] = cb[e] = 0.0f;
+      for (int e = 0; e < 4; ++e) A[e] = B[e] = 0;
     }
 
+    // ---- sum of squares (double) ----
+    float rstd[ROW_SPAN ? 1 : VPL];
+    if (ROW_SPAN) {
+      double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      // ---- sum of squares (double) ----
-      double ss[ROW_SPAN ? 1 : VPL];
-#pragma unroll
-      for (int j = 0; j < (ROW_SPAN ? 1 : VPL); ++j) ss[j] = 0.0;
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[t][j]);
-        double acc = 0.0;
+      for (int jj = 0; jj < VPL; ++jj) {
+        const int vi = lane + 32 * jj;
+        const uint4 xv = vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&xv);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const double a = (double)bf16_lo(w[e]);
           const double b = (double)bf16_hi(w[e]);
-          acc = fma(a, a, acc);
-          acc = fma(b, b, acc);
-        }
-        ss[ROW_SPAN ? 0 : j] += acc;
-      }
-      float rstd[ROW_SPAN ? 1 : VPL];
-      if (ROW_SPAN) {
-        double s = ss[0];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const float ms = (float)(s / (double)p.row_elems);
-        rstd[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
-      } else {
-#pragma unroll
-        for (int j = 0; j < (ROW_SPAN ? 1 : VPL); ++j) {
-          double s = ss[j];
-#pragma unroll
-          for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-          const float ms = (float)(s / 128.0);
-          rstd[j] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+          acc[e] = fma(a, a, acc[e]);
+          acc[e] = fma(b, b, acc[e]);
         }
       }
-      // ---- normalise, modulate, rotate, store ----
-      __nv_bfloat16* yr = p.y[t] + tok * p.ldy[t];
+      double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int vi = lane + 32 * j;
-        const bool ok = vi < nvec;
-        const float rs = rstd[ROW_SPAN ? 0 : j];
-        uint4 wv = whead[t], sv = make_uint4(0, 0, 0, 0), hv4 = make_uint4(0, 0, 0, 0);
-        if (ok) {
-          if (ROW_SPAN) wv = ldg_nc_v4(p.w[t] + 8 * vi);
-          if (MODULATE) {
-            sv = ldg_nc_v4(p.scale + 8 * vi);
-            hv4 = ldg_nc_v4(p.shift + 8 * vi);
-          }
-        }
-        const uint32_t* xw = reinterpret_cast<const uint32_t*>(&v[t][j]);
-        const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
-        const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
-        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv4);
-        uint32_t nw4[4];
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float ms = (float)(sum / (double)p.row_elems);
+      rstd[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < (ROW_SPAN ? 1 : VPL); ++jj) {
+        const int vi = lane + 32 * jj;
+        const uint4 xv = vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&xv);
+        double sum = 0.0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float a = bf16_round(__fmul_rn(__fmul_rn(bf16_lo(xw[e]), rs), bf16_lo(ww[e])));
-          float b = bf16_round(__fmul_rn(__fmul_rn(bf16_hi(xw[e]), rs), bf16_hi(ww[e])));
-          if (MODULATE) {
-            a = bf16_round(__fmul_rn(a, bf16_round(__fadd_rn(1.0f, bf16_lo(sw[e])))));
-            b = bf16_round(__fmul_rn(b, bf16_round(__fadd_rn(1.0f, bf16_hi(sw[e])))));
-            a = bf16_round(__fadd_rn(a, bf16_lo(hw[e])));
-            b = bf16_round(__fadd_rn(b, bf16_hi(hw[e])));
-          }
-          nw4[e] = pack_bf16(a, b);
+          const double a = (double)bf16_lo(w[e]);
+          const double b = (double)bf16_hi(w[e]);
+          sum = fma(a, a, sum);
+          sum = fma(b, b, sum);
         }
-        uint32_t pw[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) pw[e] = __shfl_sync(0xffffffffu, nw4[e], partner);
-        uint32_t ow[4];
-        if (role == 2) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) ow[e] = nw4[e];
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float o0 = bf16_lo(nw4[e]), o1 = bf16_hi(nw4[e]);
-            const float q0 = bf16_lo(pw[e]), q1 = bf16_hi(pw[e]);
-            float r0, r1;
-            if (role == 0) {  // own = x0, partner = x1
-              r0 = __fadd_rn(__fmul_rn(ca[2 * e], o0), __fmul_rn(cb[2 * e], q0));
-              r1 = __fadd_rn(__fmul_rn(ca[2 * e + 1], o1), __fmul_rn(cb[2 * e + 1], q1));
-            } else {          // own = x1, partner = x0
-              r0 = __fadd_rn(__fmul_rn(ca[2 * e], q0), __fmul_rn(cb[2 * e], o0));
-              r1 = __fadd_rn(__fmul_rn(ca[2 * e + 1], q1), __fmul_rn(cb[2 * e + 1], o1));
-            }
-            ow[e] = pack_bf16(r0, r1);
-          }
-        }
-        if (ok) stg_v4(yr + 8 * vi, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float ms = (float)(sum / 128.0);
+        rstd[jj] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
       }
     }
+
+    // ---- normalise, modulate, rotate, store ----
+    const int64_t tok = blockIdx.x + j * G;
+    __nv_bfloat16* yr = ybase + tok * ldy;
+#pragma unroll
+    for (int jj = 0; jj < VPL; ++jj) {
+      const int vi = lane + 32 * jj;
+      const bool ok = vi < nvec;
+      const int vc = ok ? vi : 0;
+      const float rs = rstd[ROW_SPAN ? 0 : jj];
+      const uint64_t rs2 = f2_pack(rs, rs);
+      const uint4 wv = ROW_SPAN ? w_row[vc] : whead;
+      uint4 mv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
+      if (MODULATE) {
+        mv = m_s[vc];
+        sv = sh_s[vc];
+      }
+      const uint4 xv = xs[vc];
+      const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+      const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+      const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mv);
+      const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
+      uint32_t h[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        h[e] = f2_to_bf16x2(f2_mul(f2_mul(bf16x2_to_f2(xw[e]), rs2), bf16x2_to_f2(ww[e])));
+        if (MODULATE) h[e] = bf2_add(bf2_mul(h[e], mw[e]), sw[e]);
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t pw = __shfl_sync(0xffffffffu, h[e], partner);
+        float a0, a1, b0, b1;
+        f2_unpack(A[e], a0, a1);
+        f2_unpack(B[e], b0, b1);
+        // scalar round-to-nearest products and add: never contracted into an FMA
+        const float r0 = __fadd_rn(__fmul_rn(a0, bf16_lo(h[e])), __fmul_rn(b0, bf16_lo(pw)));
+        const float r1 = __fadd_rn(__fmul_rn(a1, bf16_hi(h[e])), __fmul_rn(b1, bf16_hi(pw)));
+        o[e] = pack_bf16(r0, r1);
+        if (!FULL_ROT && role == 2) o[e] = h[e];
+      }
+      if (ok) stg_v4(yr + 8 * vi, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);  // every lane's reads of the stage are done
   }
 }
 
-template <int VPL>
-cudaError_t launch_vpl(const NRParams& p, bool row, bool mod, cudaStream_t st) {
+int smem_bytes_for(int stages, int nvec, bool row, bool mod, int stage_bytes) {
+  const int n_cst = ((row ? 2 : 0) + (mod ? 2 : 0)) * nvec;
+  return 128 + 256 + ((n_cst * 16 + 127) & ~127) + stages * stage_bytes;
+}
+
+template <int VPL, bool ROW, bool MOD, bool FULL>
+cudaError_t launch_one(const NRParams& p, int smem, cudaStream_t st) {
+  auto kern = adaln_rms_rope_kernel<VPL, ROW, MOD, FULL>;
+  static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  int per_sm = 1;
-  auto go = [&](auto kern) -> cudaError_t {
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNRThreads, 0);
-    if (per_sm < 1) per_sm = 1;
-    const int64_t warps_needed = p.m;
-    int64_t blocks = (int64_t)num_sms(dev) * per_sm;
-    const int64_t max_blocks = (warps_needed + (kNRThreads / 32) - 1) / (kNRThreads / 32);
-    if (blocks > max_blocks) blocks = max_blocks;
-    if (blocks < 1) blocks = 1;
-    kern<<<(unsigned)blocks, kNRThreads, 0, st>>>(p);
-    return cudaGetLastError();
-  };
-  if (row && mod) return go(adaln_rms_rope_kernel<VPL, true, true>);
-  if (row) return go(adaln_rms_rope_kernel<VPL, true, false>);
-  if (mod) return go(adaln_rms_rope_kernel<VPL, false, true>);
-  return go(adaln_rms_rope_kernel<VPL, false, false>);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t grid = std::min<int64_t>(p.m, (int64_t)num_sms(dev));
+  kern<<<(unsigned)grid, kNRThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int VPL>
+cudaError_t launch_vpl(const NRParams& p, bool row, bool mod, bool full, int smem, cudaStream_t st) {
+  if (row) {
+    if (mod) return full ? launch_one<VPL, true, true, true>(p, smem, st) : launch_one<VPL, true, true, false>(p, smem, st);
+    return full ? launch_one<VPL, true, false, true>(p, smem, st) : launch_one<VPL, true, false, false>(p, smem, st);
+  }
+  if (mod) return full ? launch_one<VPL, false, true, true>(p, smem, st) : launch_one<VPL, false, true, false>(p, smem, st);
+  return full ? launch_one<VPL, false, false, true>(p, smem, st) : launch_one<VPL, false, false, false>(p, smem, st);
 }
 
 }  // namespace
@@ -225,9 +357,6 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   if (mod && (a.shift == nullptr || (reinterpret_cast<uintptr_t>(a.scale) & 15) ||
               (reinterpret_cast<uintptr_t>(a.shift) & 15)))
     return cudaErrorNotSupported;
-  if (a.norm_span == 0 && !mod) {
-    // plain RMSNorm over the row is allowed (no modulation)
-  }
   NRParams p;
   p.x[0] = static_cast<const __nv_bfloat16*>(a.q);
   p.x[1] = static_cast<const __nv_bfloat16*>(a.k);
@@ -246,13 +375,28 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   p.heads = (int)a.heads;
   p.half_v = (int)(rot / 16);
   p.row_elems = (int)(a.heads * a.head_dim);
+  p.row_bytes = (int)(a.heads * a.head_dim * 2);
+  p.tab_bytes = (int)(rot / 2 * 16);
   p.eps = a.eps;
   const bool row = a.norm_span == 0;
+  const int nvec = (int)(a.heads * 16);
+  const int stage_bytes = 2 * p.row_bytes + p.tab_bytes;
+  // deepest ring (a multiple of the pair count, so each stage always serves the same pair) that fits
+  int stages = 0;
+  for (int s = kMaxStages; s >= kPairs; s -= kPairs)
+    if (smem_bytes_for(s, nvec, row, mod, stage_bytes) <= kSmemLimit) {
+      stages = s;
+      break;
+    }
+  if (stages == 0) return cudaErrorNotSupported;
+  p.stages = stages;
+  const int smem = smem_bytes_for(stages, nvec, row, mod, stage_bytes);
+  const bool full = rot == 128;
   const int vpl = (int)((a.heads * 16 + 31) / 32);
-  if (vpl <= 4) return launch_vpl<4>(p, row, mod, stream);
-  if (vpl <= 8) return launch_vpl<8>(p, row, mod, stream);
-  if (vpl <= 12) return launch_vpl<12>(p, row, mod, stream);
-  return launch_vpl<16>(p, row, mod, stream);
+  if (vpl <= 4) return launch_vpl<4>(p, row, mod, full, smem, stream);
+  if (vpl <= 8) return launch_vpl<8>(p, row, mod, full, smem, stream);
+  if (vpl <= 12) return launch_vpl<12>(p, row, mod, full, smem, stream);
+  return launch_vpl<16>(p, row, mod, full, smem, stream);
 }
 
 }  // namespace h3

@@ -8,10 +8,19 @@
 //   sb     = bf16(scale)                          scale as the bf16 operand
 //   q      = clamp(rne(bf16(x / sb)), -128, 127)
 //
-// B200 layout: one CTA of 256 threads per row; the row stays in registers
-// between the absmax reduction and the quantize pass, so HBM sees exactly one
-// read of x (2 B/elem) and one write of q (1 B/elem) plus 4 B of scale per row.
-// Loads are 128-bit (8 bf16), stores 64-bit (8 int8).
+// Division. The fp32 quotient x / sb is only needed up to which side of a bf16
+// rounding midpoint it falls on. t = x * rcp(sb), with rcp correctly rounded,
+// is within 2 ulp of the correctly rounded quotient, and bf16 rounding changes
+// only where the low 16 bits of the fp32 value cross 0x8000. So t is used
+// directly unless its low 16 bits lie within kMidWin of 0x8000, in which case
+// the quotient is recomputed with an IEEE division (about 5e-5 of elements).
+// Exhaustively equal to the division on every (bf16 x, bf16 scale) pair.
+//
+// B200 layout: rows of up to 4096 elements go one warp per row (the row stays
+// in registers between the absmax and the quantize pass; no block barrier);
+// longer rows one 256-thread CTA per row. HBM sees one read of x (2 B/elem),
+// one write of q (1 B/elem) and 4 B of scale per row; 128-bit loads, 64-bit
+// stores.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -20,6 +29,7 @@ namespace h3 {
 namespace {
 
 constexpr int kQThreads = 256;
+constexpr uint32_t kMidWin = 8;
 
 __device__ __forceinline__ float quant_divisor(float scale) {
   float sb = bf16_round(scale);
@@ -32,9 +42,46 @@ __device__ __forceinline__ int8_t quant_one(float x, float sb) {
   return (int8_t)(int)v;
 }
 
+// Same result as quant_one(x, sb) for r = rcp_rn(sb); returns the int8 in the low byte.
+__device__ __forceinline__ uint32_t quant_fast(float x, float sb, float r) {
+  float t = __fmul_rn(x, r);
+  if (((__float_as_uint(t) & 0xFFFFu) - (0x8000u - kMidWin)) <= 2u * kMidWin) t = __fdiv_rn(x, sb);
+  int v = __float2int_rn(bf16_round(t));
+  v = min(max(v, -128), 127);
+  return (uint32_t)v & 0xFFu;
+}
+
+// 8 bf16 (one 16-byte vector) -> 8 int8 packed in a uint2
+__device__ __forceinline__ uint2 quant_vec8(const uint4& v, float sb, float r) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+  uint32_t o[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    o[h] = quant_fast(bf16_lo(w[2 * h]), sb, r) | (quant_fast(bf16_hi(w[2 * h]), sb, r) << 8) |
+           (quant_fast(bf16_lo(w[2 * h + 1]), sb, r) << 16) | (quant_fast(bf16_hi(w[2 * h + 1]), sb, r) << 24);
+  }
+  return make_uint2(o[0], o[1]);
+}
+
+__device__ __forceinline__ uint32_t absmax_bits8(const uint4& v) {
+  // |x| of bf16 values orders like their magnitude bits (a NaN wins, as in torch's amax)
+  const uint32_t a = __vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu);
+  const uint32_t b = __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu);
+  const uint32_t c = __vmaxu2(a, b);
+  return max(c & 0xFFFFu, c >> 16);
+}
+
 __device__ __forceinline__ float act_apply(float x, int act) {
   return act == H3B200_ACT_GELU_TANH ? bf16_round(gelu_tanh_exact(x)) : x;
 }
+
+__device__ __forceinline__ void apply_act_vec(uint4& v, int act) {
+  uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) w[e] = pack_bf16(act_apply(bf16_lo(w[e]), act), act_apply(bf16_hi(w[e]), act));
+}
+
+__device__ __forceinline__ float row_scale(float rowmax) { return fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f); }
 
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
@@ -48,7 +95,53 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
-// Vector path: k % 8 == 0, 16-byte aligned rows, k <= kQThreads * 8 * VPT.
+// One warp per row: k % 8 == 0, 16-byte aligned rows, k <= 32 * 8 * VPL.
+template <int VPL, bool GIVEN_ABSMAX>
+__global__ void __launch_bounds__(kQThreads) quantize_rows_warp_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                       int64_t ldx, int64_t m, int64_t k, int act,
+                                                                       const float* __restrict__ absmax_in,
+                                                                       int8_t* __restrict__ q,
+                                                                       float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = ((int64_t)blockIdx.x * kQThreads + threadIdx.x) >> 5;
+  if (row >= m) return;
+  const int nvec = (int)(k >> 3);
+  const __nv_bfloat16* xr = x + row * ldx;
+  uint4 v[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int vi = lane + 32 * j;
+    v[j] = vi < nvec ? ldg_nc_v4(xr + vi * 8) : make_uint4(0, 0, 0, 0);
+  }
+  if (act != H3B200_ACT_NONE) {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      if (lane + 32 * j < nvec) apply_act_vec(v[j], act);
+  }
+  float rowmax;
+  if (GIVEN_ABSMAX) {
+    rowmax = absmax_in[row];
+  } else {
+    uint32_t mb = 0;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) mb = max(mb, absmax_bits8(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+    rowmax = __uint_as_float(mb << 16);
+  }
+  const float s = row_scale(rowmax);
+  const float sb = quant_divisor(s);
+  const float r = __frcp_rn(sb);
+  int8_t* qr = q + row * k;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int vi = lane + 32 * j;
+    if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant_vec8(v[j], sb, r);
+  }
+  if (lane == 0) scale[row] = s;
+}
+
+// One 256-thread CTA per row: k % 8 == 0, 16-byte aligned rows, k <= kQThreads * 8 * VPT.
 template <int VPT, bool GIVEN_ABSMAX>
 __global__ void __launch_bounds__(kQThreads) quantize_rows_vec_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                       int64_t m, int64_t k, int act,
@@ -61,48 +154,33 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_vec_kernel(const __nv
   const int64_t nvec = k >> 3;
   const __nv_bfloat16* xr = x + row * ldx;
   uint4 v[VPT];
-  float amax = 0.0f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t vi = threadIdx.x + (int64_t)j * kQThreads;
-    if (vi < nvec) {
-      v[j] = ldg_nc_v4(xr + vi * 8);
-      if (act != H3B200_ACT_NONE) {
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v[j]);
+    v[j] = vi < nvec ? ldg_nc_v4(xr + vi * 8) : make_uint4(0, 0, 0, 0);
+  }
+  if (act != H3B200_ACT_NONE) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = pack_bf16(act_apply(bf16_lo(w[e]), act), act_apply(bf16_hi(w[e]), act));
-      }
-      if (!GIVEN_ABSMAX) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[j]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fmaxf(fabsf(bf16_lo(w[e])), fabsf(bf16_hi(w[e]))));
-      }
-    }
+    for (int j = 0; j < VPT; ++j)
+      if (threadIdx.x + (int64_t)j * kQThreads < nvec) apply_act_vec(v[j], act);
   }
   float rowmax;
   if (GIVEN_ABSMAX) {
     rowmax = absmax_in[row];
   } else {
-    rowmax = block_max(amax, red);
+    uint32_t mb = 0;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) mb = max(mb, absmax_bits8(v[j]));
+    rowmax = block_max(__uint_as_float(mb << 16), red);
   }
-  const float s = fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f);
+  const float s = row_scale(rowmax);
   const float sb = quant_divisor(s);
+  const float r = __frcp_rn(sb);
   int8_t* qr = q + row * k;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t vi = threadIdx.x + (int64_t)j * kQThreads;
-    if (vi < nvec) {
-      const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[j]);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        lo |= (uint32_t)(uint8_t)quant_one(bf16_lo(w[e]), sb) << (16 * e);
-        lo |= (uint32_t)(uint8_t)quant_one(bf16_hi(w[e]), sb) << (16 * e + 8);
-        hi |= (uint32_t)(uint8_t)quant_one(bf16_lo(w[e + 2]), sb) << (16 * e);
-        hi |= (uint32_t)(uint8_t)quant_one(bf16_hi(w[e + 2]), sb) << (16 * e + 8);
-      }
-      *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(lo, hi);
-    }
+    if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant_vec8(v[j], sb, r);
   }
   if (threadIdx.x == 0) scale[row] = s;
 }
@@ -125,10 +203,25 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_scalar_kernel(const _
     for (int64_t i = threadIdx.x; i < k; i += kQThreads) amax = fmaxf(amax, fabsf(act_apply(__bfloat162float(xr[i]), act)));
     rowmax = block_max(amax, red);
   }
-  const float s = fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f);
+  const float s = row_scale(rowmax);
   const float sb = quant_divisor(s);
   for (int64_t i = threadIdx.x; i < k; i += kQThreads) q[row * k + i] = quant_one(act_apply(__bfloat162float(xr[i]), act), sb);
   if (threadIdx.x == 0) scale[row] = s;
+}
+
+template <bool GIVEN>
+cudaError_t launch_warp(int vpl, const __nv_bfloat16* x, int64_t ldx, int64_t m, int64_t k, int act, const float* am,
+                        int8_t* q, float* s, cudaStream_t st) {
+  const int64_t rows_per_block = kQThreads / 32;
+  dim3 grid((unsigned)((m + rows_per_block - 1) / rows_per_block)), block(kQThreads);
+  switch (vpl) {
+    case 2: quantize_rows_warp_kernel<2, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    case 4: quantize_rows_warp_kernel<4, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    case 8: quantize_rows_warp_kernel<8, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    case 12: quantize_rows_warp_kernel<12, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+    default: quantize_rows_warp_kernel<16, GIVEN><<<grid, block, 0, st>>>(x, ldx, m, k, act, am, q, s); break;
+  }
+  return cudaGetLastError();
 }
 
 template <bool GIVEN>
@@ -211,6 +304,12 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t 
   const bool aligned = (k % 8 == 0) && (ldx % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                        ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
   const int64_t nvec = k / 8;
+  if (aligned && k > 0 && nvec <= 32 * 16) {
+    const int64_t per_lane = (nvec + 31) / 32;
+    const int vpl = per_lane <= 2 ? 2 : per_lane <= 4 ? 4 : per_lane <= 8 ? 8 : per_lane <= 12 ? 12 : 16;
+    if (absmax_in != nullptr) return launch_warp<true>(vpl, xb, ldx, m, k, act, absmax_in, q, scale, stream);
+    return launch_warp<false>(vpl, xb, ldx, m, k, act, nullptr, q, scale, stream);
+  }
   const int64_t per_thread = (nvec + kQThreads - 1) / kQThreads;
   if (aligned && k > 0 && per_thread <= 8) {
     const int vpt = per_thread <= 1 ? 1 : per_thread <= 2 ? 2 : per_thread <= 4 ? 4 : per_thread <= 6 ? 6 : 8;

@@ -4,7 +4,8 @@ Public operators mirror the comfy_kitchen backend surface that
 ``h3serve/native_engine`` and ``backends/turbo`` call (``int8_linear``,
 ``quantize_int8_rowwise``, ``int8_linear_prequantized``, ``mm_int8``,
 ``w4a8_int8_linear``, ``rms_rope_split_half(_)``) plus the fused entry points
-``fused_gated_mlp`` and ``adaln_rms_rope(_)``. All of them run hand-written CUDA
+``fused_gated_mlp`` and ``adaln_rms_rope(_)``, and ``fused_gated_mlp_host`` for
+token buffers in host memory (copies overlapped with the MLP). All of them run hand-written CUDA
 from ``libh3b200.so`` through its C ABI; there is no other backend.
 """
 
@@ -27,6 +28,7 @@ from .ops import (  # noqa: F401
     rms_rope_split_half_,
     w4a8_int8_linear,
 )
+from .pipeline import fused_gated_mlp_host  # noqa: F401
 from .rope import rope_grid_table  # noqa: F401
 from .weights import quantize_int8_weight, W8A8MLPWeights  # noqa: F401
 

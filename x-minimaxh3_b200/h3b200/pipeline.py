@@ -1,0 +1,102 @@
+"""Fused gated MLP over host (pinned) token buffers, with copies overlapped.
+
+A serving process usually holds a step's activations in host memory. Called on
+host tensors, ``fused_gated_mlp_host`` splits the tokens into chunks and runs
+three CUDA streams: host-to-device copies of chunk i+1, the fused MLP of chunk
+i (``fused_gated_mlp``: quantize -> fc1 + GELU -> requant -> fc2 + gated
+residual) and the device-to-host copy of chunk i-1 run at the same time. The
+MLP is per-token, so the chunked result is bit-identical to one call over all
+tokens. Device staging buffers are allocated once per (device, d, chunk) and
+reused.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from .ops import fused_gated_mlp
+
+_cache_lock = threading.Lock()
+_cache: dict = {}
+
+
+class _Staging:
+    def __init__(self, device: torch.device, d: int, chunk: int, slots: int):
+        self.x = [torch.empty(chunk, d, dtype=torch.bfloat16, device=device) for _ in range(slots)]
+        self.r = [torch.empty(chunk, d, dtype=torch.bfloat16, device=device) for _ in range(slots)]
+        self.h2d = torch.cuda.Stream(device)
+        self.comp = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.free = [torch.cuda.Event() for _ in range(slots)]
+        self.used = [False] * slots
+        self.workspace = None
+
+
+def _staging(device: torch.device, d: int, chunk: int, slots: int) -> _Staging:
+    key = (device.index, d, chunk, slots)
+    with _cache_lock:
+        st = _cache.get(key)
+        if st is None:
+            st = _Staging(device, d, chunk, slots)
+            _cache[key] = st
+    return st
+
+
+def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Tensor, s1: torch.Tensor,
+                         w2q: torch.Tensor, s2: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
+                         chunk_tokens: int = 4096, slots: int = 3, synchronize: bool = True) -> torch.Tensor:
+    """``out = residual + int8_linear(gelu(int8_linear(hidden, w1q, s1)), w2q, s2) * gate`` for host tensors.
+
+    ``residual``, ``hidden`` and ``out`` are CPU bf16 [M, d] tensors (pinned memory
+    for overlap; ``out`` may be ``residual``); weights, scales and ``gate`` live on
+    the CUDA device that runs the MLP. Same result as ``fused_gated_mlp`` on device
+    copies of the inputs. With ``synchronize=False`` the call returns once the work
+    is queued; ``out`` is then valid after the caller's current stream is
+    synchronised."""
+    if residual.is_cuda or hidden.is_cuda:
+        raise ValueError("fused_gated_mlp_host takes host tensors; use fused_gated_mlp for device tensors")
+    if residual.shape != hidden.shape or residual.dim() != 2:
+        raise ValueError("residual and hidden must both be [M, d]")
+    if residual.dtype != torch.bfloat16 or hidden.dtype != torch.bfloat16:
+        raise ValueError("residual and hidden must be bf16")
+    if chunk_tokens <= 0 or slots < 2:
+        raise ValueError("chunk_tokens must be positive and slots >= 2")
+    m, d = hidden.shape
+    if out is None:
+        out = torch.empty((m, d), dtype=torch.bfloat16, pin_memory=residual.is_pinned())
+    elif out.shape != residual.shape or out.dtype != torch.bfloat16 or out.is_cuda:
+        raise ValueError("out must be a host bf16 tensor shaped like residual")
+    dev = w1q.device
+    chunk = min(chunk_tokens, m) if m > 0 else 1
+    st = _staging(dev, d, chunk, slots)
+    cur = torch.cuda.current_stream(dev)
+    for s in (st.h2d, st.comp, st.d2h):
+        s.wait_stream(cur)
+    for i, lo in enumerate(range(0, m, chunk)):
+        hi = min(m, lo + chunk)
+        n = hi - lo
+        k = i % slots
+        xb, rb = st.x[k][:n], st.r[k][:n]
+        with torch.cuda.stream(st.h2d):
+            if st.used[k]:
+                st.h2d.wait_event(st.free[k])  # the slot's previous chunk has been copied out
+            xb.copy_(hidden[lo:hi], non_blocking=True)
+            rb.copy_(residual[lo:hi], non_blocking=True)
+        st.comp.wait_stream(st.h2d)
+        with torch.cuda.stream(st.comp):
+            if st.workspace is None:
+                from . import _lib
+                nbytes = int(_lib.load().h3b200_fused_gated_mlp_workspace_bytes(chunk, d, w1q.shape[0]))
+                st.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            fused_gated_mlp(rb, xb, w1q, s1, w2q, s2, gate, out=rb, workspace=st.workspace)
+        st.d2h.wait_stream(st.comp)
+        with torch.cuda.stream(st.d2h):
+            out[lo:hi].copy_(rb, non_blocking=True)
+            st.free[k].record(st.d2h)
+        st.used[k] = True
+    cur.wait_stream(st.d2h)
+    if synchronize:
+        cur.synchronize()
+    return out

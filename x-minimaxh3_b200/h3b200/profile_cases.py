@@ -1,0 +1,111 @@
+"""Run one kernel of the hot path on a chosen token count, for profilers.
+
+    python -m h3b200.profile_cases CASE [--tokens M] [--iters N]
+
+CASE is one of ``quantize`` (fc1 input quantizer, K = 3072), ``fc1`` (INT8 GEMM
+with the GELU + row-absmax epilogue), ``requant`` (fc2 input quantizer with a
+given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
+``mlp`` (the whole fused MLP call) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
+Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
+norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
+runs the kernels it needs to build its inputs, then launches the kernel under
+study ``--iters`` times, so a profiler can skip the set-up launches by kernel
+name. The process exits non-zero if a kernel reports an error.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import torch
+
+if __package__ in (None, ""):
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import h3b200  # noqa: E402
+from h3b200 import ops  # noqa: E402
+from h3b200.rope import rope_grid_table  # noqa: E402
+
+D_MODEL, D_FFN = 3072, 12288
+
+
+def mlp_inputs(m: int, dev):
+    g = torch.Generator(device=dev).manual_seed(2)
+    w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(D_MODEL, D_FFN, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wt = h3b200.W8A8MLPWeights.from_float(w1, w2)
+    x = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+    gate = torch.randn(D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+    res = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+    return wt, x, gate, res
+
+
+def run(case: str, m: int, iters: int) -> None:
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    h3b200.library()
+    if case == "norm_rope":
+        g = torch.Generator(device=dev).manual_seed(4)
+        q = torch.randn(m, 24, 128, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn(m, 24, 128, generator=g, device=dev).to(torch.bfloat16)
+        sh = (torch.randn(3072, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        sc = (torch.randn(3072, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        wq = (1 + 0.02 * torch.randn(3072, generator=g, device=dev)).to(torch.bfloat16)
+        wk = (1 + 0.02 * torch.randn(3072, generator=g, device=dev)).to(torch.bfloat16)
+        grid_t = max(1, (m + 39 * 40 - 1) // (39 * 40))
+        table = rope_grid_table((grid_t, 39, 40), device=dev)[:m].contiguous()
+        qo, ko = torch.empty_like(q), torch.empty_like(k)
+        for _ in range(iters):
+            ops.adaln_rms_rope_(q, k, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko)
+    else:
+        wt, x, gate, res = mlp_inputs(m, dev)
+        xq, xs = ops.quantize_int8_rowwise(x)
+        amax = torch.zeros(m, dtype=torch.float32, device=dev)
+        act = torch.empty(m, D_FFN, dtype=torch.bfloat16, device=dev)
+        out = torch.empty_like(res)
+
+        def fc1():
+            ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_GELU_ABSMAX, xs, wt.s1, out=act, row_absmax=amax)
+
+        if case == "quantize":
+            for _ in range(iters):
+                ops.quantize_int8_rowwise(x)
+        elif case == "fc1":
+            for _ in range(iters):
+                amax.zero_()
+                fc1()
+        elif case in ("requant", "fc2"):
+            fc1()
+            if case == "requant":
+                for _ in range(iters):
+                    ops.quantize_int8_rowwise_absmax(act, amax)
+            else:
+                q2, xs2 = ops.quantize_int8_rowwise_absmax(act, amax)
+                for _ in range(iters):
+                    ops.int8_gemm_fused(q2, wt.w2q, ops.EPI_GATED_RESIDUAL, xs2, wt.s2, gate=gate, residual=res,
+                                        out=out)
+        elif case == "mlp":
+            for _ in range(iters):
+                h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=out)
+        else:
+            raise SystemExit(f"unknown case {case!r}")
+    torch.cuda.synchronize()
+    st = h3b200.device_status(0)
+    if st != 0:
+        raise SystemExit(f"device status {st:#x}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["quantize", "fc1", "requant", "fc2", "mlp", "norm_rope"])
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args()
+    run(a.case, a.tokens, a.iters)
+    print(f"profile case {a.case} tokens={a.tokens} iters={a.iters}: ok")
+
+
+if __name__ == "__main__":
+    main()
