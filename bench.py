@@ -328,6 +328,20 @@ def run_ours(args, rank, world, local_rank):
     nr_ms = timed(k_nr, 50, stream)
     nr_bytes = M_TOKENS * NR_BYTES_PER_TOKEN
 
+    # ---- library INT8 reference: cuBLASLt through torch._int_mm, 8192^3, same box and run ----
+    lib_int8_tops = None
+    try:
+        ga = torch.Generator(device=dev).manual_seed(7)
+        ia = torch.randint(-128, 128, (8192, 8192), generator=ga, device=dev, dtype=torch.int8)
+        ib = torch.randint(-128, 128, (8192, 8192), generator=ga, device=dev, dtype=torch.int8).t()
+        for _ in range(3):
+            torch._int_mm(ia, ib)
+        lib_ms = timed(lambda: torch._int_mm(ia, ib), 10, stream)
+        lib_int8_tops = 2.0 * 8192 ** 3 / (lib_ms * 1e-3) / 1e12
+        del ia, ib
+    except Exception:
+        lib_int8_tops = None
+
     peaks, peak_src = load_peaks()
     int8_peak_tops = 2.0 * peaks["bf16_tflops"]
     traffic = load_traffic()
@@ -387,6 +401,7 @@ def run_ours(args, rank, world, local_rank):
             "components": {
                 **{k: {"ms": v} for k, v in comp_ms.items()},
                 "fc2_gemm_gated_residual_tops": fc2_ops / (comp_ms["fc2_gemm_gated_residual"] * 1e-3) / 1e12,
+                "cublaslt_int8_8192_tops": lib_int8_tops,
                 "norm_rope_cfg3": {"ms": nr_ms, "achieved": nr_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                    "frac": nr_gbs / peaks["hbm_gbs"], "bytes_per_token": NR_BYTES_PER_TOKEN,
                                    "table_bytes_per_token": NR_TABLE_BYTES_PER_TOKEN,

@@ -74,4 +74,9 @@ cudaError_t launch_w4a8_correction(const int32_t* gsum, const float* xs, const v
 
 int num_sms(int device);
 
+// 2-D tiled TMA descriptor (no interleave, 256-byte L2 promotion, no OOB fill);
+// false when the driver's encoder is unavailable or rejects the layout.
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t rows,
+                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle);
+
 }  // namespace h3

@@ -11,6 +11,10 @@
 // RMSNorm: rstd = 1 / sqrt(mean(x^2) + eps) in fp32, y = bf16((x * rstd) * w).
 // The sum of squares is accumulated in double so the fp32 mean is the
 // correctly rounded one (the reference sums in fp32, order ISA-dependent).
+// |x| is turned into a double with two integer operations on its bf16 bits
+// (exact for normal values; zero and subnormals become a value below 2^-126
+// whose square cannot change the fp32 mean); a row whose mean is not finite
+// is re-summed with exact conversions, so inf and NaN behave as in the reference.
 // Modulation: bf16(bf16(h * bf16(1 + scale)) + shift); both steps are one
 // correctly rounded bf16x2 operation on bf16 operands, which equals the
 // reference's fp32 operation followed by a bf16 rounding (the fp32 product of
@@ -21,10 +25,12 @@
 // [m, rot_dim/2, 2, 2].
 //
 // B200 design: a persistent CTA per SM streams tokens through a shared-memory
-// ring with bulk asynchronous copies (cp.async.bulk, no multicast): one
-// producer thread loads a token's Q row, K row and rotation-table row into a
-// stage; each of kPairs warp pairs takes every kPairs-th token of the CTA, one
-// warp for Q and one for K. A warp reads its row from the stage twice (sum of
+// ring with asynchronous copies (no multicast): one producer thread loads a
+// token's Q row and K row with cp.async.bulk and its rotation-table row with a
+// 128-byte-swizzled TMA tensor load (the swizzle lets the 8 lanes that read 8
+// different 128-byte table segments hit 8 different bank groups); each of
+// kPairs warp pairs takes every kPairs-th token of the CTA, one warp for Q and
+// one for K. A warp reads its row from the stage twice (sum of
 // squares, reduced with shuffles; then normalise / modulate / rotate; lane l
 // owns the 16-byte vectors l + 32*j), writes the result with coalesced 128-bit
 // stores and frees the stage. Lane l's
@@ -43,9 +49,9 @@
 namespace h3 {
 namespace {
 
-constexpr int kPairs = 5;                          // consumer warp pairs per CTA
+constexpr int kPairs = 7;                          // consumer warp pairs per CTA
 constexpr int kNRThreads = 32 * (1 + 2 * kPairs);  // producer warp + consumers
-constexpr int kMaxStages = 15;
+constexpr int kMaxStages = 14;
 constexpr int kSmemLimit = 227 * 1024;
 constexpr unsigned kErrNRFull = 0x201, kErrNRProducer = 0x202, kErrNRDrain = 0x203;
 
@@ -61,8 +67,11 @@ struct NRParams {
   int heads;
   int half_v;     // rot_dim / 16: vectors in each rotation half
   int row_elems;
-  int row_bytes;  // heads * 256
-  int tab_bytes;  // rot_dim / 2 * 16
+  int row_bytes;    // heads * 256
+  int nseg;         // rot_dim / 16: 128-byte table segments (8 pairs each) per token
+  int tab_off;      // table offset inside a stage (1024-aligned for the swizzle)
+  int stage_bytes;  // multiple of 1024
+  int ring_off;     // ring offset from the 1024-aligned shared-memory base
   int stages;
   float eps;
 };
@@ -105,6 +114,38 @@ __device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
   return r;
 }
 
+// |bf16| of the low / high half of w as a double: exponent rebiased by
+// 1023 - 127 = 896, mantissa moved to the top of the double's fraction.
+__device__ __forceinline__ double abs_lo_as_double(uint32_t w) {
+  return __hiloint2double((int)(((w & 0x7FFFu) << 13) + 0x38000000u), 0);
+}
+__device__ __forceinline__ double abs_hi_as_double(uint32_t w) {
+  return __hiloint2double((int)(((w >> 3) & 0x0FFFE000u) + 0x38000000u), 0);
+}
+
+// sum of squares of the 8 bf16 values of v (fast: integer-built doubles)
+__device__ __forceinline__ void sumsq8_fast(const uint4& v, double (&acc)[4]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const double a = abs_lo_as_double(w[e]);
+    const double b = abs_hi_as_double(w[e]);
+    acc[e] = fma(a, a, acc[e]);
+    acc[e] = fma(b, b, acc[e]);
+  }
+}
+// the same with exact conversions (inf / NaN aware)
+__device__ __forceinline__ void sumsq8_exact(const uint4& v, double (&acc)[4]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const double a = (double)bf16_lo(w[e]);
+    const double b = (double)bf16_hi(w[e]);
+    acc[e] = fma(a, a, acc[e]);
+    acc[e] = fma(b, b, acc[e]);
+  }
+}
+
 // ---- bulk copy global -> shared, completion counted on an mbarrier ---------
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -115,9 +156,10 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
 }
 
 template <int VPL, bool ROW_SPAN, bool MODULATE, bool FULL_ROT>
-__global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRParams p) {
+__global__ void __launch_bounds__(kNRThreads, 1)
+    adaln_rms_rope_kernel(const __grid_constant__ CUtensorMap tm_table, const NRParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int nvec = p.heads * 16;
   const int S = p.stages;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
@@ -126,9 +168,8 @@ __global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRP
   // ROW_SPAN: per-vector weights of Q (cst[0, nvec)) and K (cst[nvec, 2 nvec))
   uint4* m_s = cst + (ROW_SPAN ? 2 : 0) * nvec;                // MODULATE: bf16(1 + scale)
   uint4* sh_s = m_s + nvec;                                    // MODULATE: shift
-  const int n_cst = ((ROW_SPAN ? 2 : 0) + (MODULATE ? 2 : 0)) * nvec;
-  uint8_t* ring = smem + 256 + ((n_cst * 16 + 127) & ~127);
-  const int stage_bytes = 2 * p.row_bytes + p.tab_bytes;
+  uint8_t* ring = smem + p.ring_off;
+  const int stage_bytes = p.stage_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -141,6 +182,7 @@ __global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRP
       mbar_init(&empty_bar[s], 2);
     }
     fence_barrier_init();
+    tma_prefetch_desc(&tm_table);
   }
   for (int i = threadIdx.x; i < nvec; i += kNRThreads) {
     if (ROW_SPAN) {
@@ -170,11 +212,10 @@ __global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRP
         if (!mbar_wait(&empty_bar[s], (use & 1u) ^ 1u, kErrNRProducer)) break;
         const int64_t tok = blockIdx.x + j * G;
         uint8_t* st = ring + (size_t)s * stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)stage_bytes);
+        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(2 * p.row_bytes + p.nseg * 128));
         bulk_g2s(st, p.x[0] + tok * p.ldx[0], (uint32_t)p.row_bytes, &full_bar[s]);
         bulk_g2s(st + p.row_bytes, p.x[1] + tok * p.ldx[1], (uint32_t)p.row_bytes, &full_bar[s]);
-        bulk_g2s(st + 2 * p.row_bytes, reinterpret_cast<const uint8_t*>(p.freqs) + tok * (int64_t)p.tab_bytes,
-                 (uint32_t)p.tab_bytes, &full_bar[s]);
+        tma_load_2d(st + p.tab_off, &tm_table, &full_bar[s], 0, (int32_t)(tok * p.nseg));
       }
       // every copy issued lands before the CTA may exit
       for (int64_t i = (j > S ? j - S : 0); i < j; ++i)
@@ -204,13 +245,17 @@ __global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRP
     if (!mbar_wait(&full_bar[s], (uint32_t)(j / S) & 1u, kErrNRFull)) break;
     const uint8_t* st = ring + (size_t)s * stage_bytes;
     const uint4* xs = reinterpret_cast<const uint4*>(st + t * p.row_bytes);
-    // RoPE coefficients of this lane's 8 pairs: out = A * own + B * partner
+    // RoPE coefficients of this lane's 8 pairs: out = A * own + B * partner.
+    // Table segment `seg` (pairs 8 seg .. 8 seg + 7) holds 16-byte chunk c at
+    // c ^ seg (128-byte swizzle).
     uint64_t A[4], B[4];
     if (role != 2) {
-      const float4* fr = reinterpret_cast<const float4*>(st + 2 * p.row_bytes) + pair0;
+      const int seg = pair0 >> 3;
+      const uint8_t* tb = st + p.tab_off + seg * 128;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float4 c0 = fr[2 * e], c1 = fr[2 * e + 1];
+        const float4 c0 = *reinterpret_cast<const float4*>(tb + (((2 * e) ^ seg) << 4));
+        const float4 c1 = *reinterpret_cast<const float4*>(tb + (((2 * e + 1) ^ seg) << 4));
         // role 0 (x0): t00 * x0 + t01 * x1; role 1 (x1): t11 * x1 + t10 * x0
         A[e] = role == 0 ? f2_pack(c0.x, c1.x) : f2_pack(c0.w, c1.w);
         B[e] = role == 0 ? f2_pack(c0.y, c1.y) : f2_pack(c0.z, c1.z);
@@ -227,38 +272,45 @@ __global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRP
 #pragma unroll
       for (int jj = 0; jj < VPL; ++jj) {
         const int vi = lane + 32 * jj;
-        const uint4 xv = vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0);
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&xv);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const double a = (double)bf16_lo(w[e]);
-          const double b = (double)bf16_hi(w[e]);
-          acc[e] = fma(a, a, acc[e]);
-          acc[e] = fma(b, b, acc[e]);
-        }
+        sumsq8_fast(vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0), acc);
       }
       double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      const float ms = (float)(sum / (double)p.row_elems);
+      float ms = (float)(sum / (double)p.row_elems);
+      if (!isfinite(ms)) {  // inf / NaN / huge row: exact conversions (warp-uniform branch)
+        double ex[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll 1
+        for (int jj = 0; jj < VPL; ++jj) {
+          const int vi = lane + 32 * jj;
+          sumsq8_exact(vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0), ex);
+        }
+        double se = (ex[0] + ex[1]) + (ex[2] + ex[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+        ms = (float)(se / (double)p.row_elems);
+      }
       rstd[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
     } else {
 #pragma unroll
       for (int jj = 0; jj < (ROW_SPAN ? 1 : VPL); ++jj) {
         const int vi = lane + 32 * jj;
         const uint4 xv = vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0);
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&xv);
-        double sum = 0.0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const double a = (double)bf16_lo(w[e]);
-          const double b = (double)bf16_hi(w[e]);
-          sum = fma(a, a, sum);
-          sum = fma(b, b, sum);
-        }
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
+        sumsq8_fast(xv, acc);
+        double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        const float ms = (float)(sum / 128.0);
+        float ms = (float)(sum / 128.0);
+        const bool bad = !isfinite(ms);
+        if (__any_sync(0xffffffffu, bad)) {
+          double ex[4] = {0.0, 0.0, 0.0, 0.0};
+          sumsq8_exact(xv, ex);
+          double se = (ex[0] + ex[1]) + (ex[2] + ex[3]);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+          if (bad) ms = (float)(se / 128.0);
+        }
         rstd[jj] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
       }
     }
@@ -310,13 +362,13 @@ __global__ void __launch_bounds__(kNRThreads, 1) adaln_rms_rope_kernel(const NRP
   }
 }
 
-int smem_bytes_for(int stages, int nvec, bool row, bool mod, int stage_bytes) {
+int ring_offset(int nvec, bool row, bool mod) {
   const int n_cst = ((row ? 2 : 0) + (mod ? 2 : 0)) * nvec;
-  return 128 + 256 + ((n_cst * 16 + 127) & ~127) + stages * stage_bytes;
+  return (256 + n_cst * 16 + 1023) & ~1023;
 }
 
 template <int VPL, bool ROW, bool MOD, bool FULL>
-cudaError_t launch_one(const NRParams& p, int smem, cudaStream_t st) {
+cudaError_t launch_one(const CUtensorMap& tm, const NRParams& p, int smem, cudaStream_t st) {
   auto kern = adaln_rms_rope_kernel<VPL, ROW, MOD, FULL>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -327,18 +379,19 @@ cudaError_t launch_one(const NRParams& p, int smem, cudaStream_t st) {
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const int64_t grid = std::min<int64_t>(p.m, (int64_t)num_sms(dev));
-  kern<<<(unsigned)grid, kNRThreads, smem, st>>>(p);
+  kern<<<(unsigned)grid, kNRThreads, smem, st>>>(tm, p);
   return cudaGetLastError();
 }
 
 template <int VPL>
-cudaError_t launch_vpl(const NRParams& p, bool row, bool mod, bool full, int smem, cudaStream_t st) {
+cudaError_t launch_vpl(const CUtensorMap& tm, const NRParams& p, bool row, bool mod, bool full, int smem,
+                       cudaStream_t st) {
   if (row) {
-    if (mod) return full ? launch_one<VPL, true, true, true>(p, smem, st) : launch_one<VPL, true, true, false>(p, smem, st);
-    return full ? launch_one<VPL, true, false, true>(p, smem, st) : launch_one<VPL, true, false, false>(p, smem, st);
+    if (mod) return full ? launch_one<VPL, true, true, true>(tm, p, smem, st) : launch_one<VPL, true, true, false>(tm, p, smem, st);
+    return full ? launch_one<VPL, true, false, true>(tm, p, smem, st) : launch_one<VPL, true, false, false>(tm, p, smem, st);
   }
-  if (mod) return full ? launch_one<VPL, false, true, true>(p, smem, st) : launch_one<VPL, false, true, false>(p, smem, st);
-  return full ? launch_one<VPL, false, false, true>(p, smem, st) : launch_one<VPL, false, false, false>(p, smem, st);
+  if (mod) return full ? launch_one<VPL, false, true, true>(tm, p, smem, st) : launch_one<VPL, false, true, false>(tm, p, smem, st);
+  return full ? launch_one<VPL, false, false, true>(tm, p, smem, st) : launch_one<VPL, false, false, false>(tm, p, smem, st);
 }
 
 }  // namespace
@@ -376,27 +429,34 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   p.half_v = (int)(rot / 16);
   p.row_elems = (int)(a.heads * a.head_dim);
   p.row_bytes = (int)(a.heads * a.head_dim * 2);
-  p.tab_bytes = (int)(rot / 2 * 16);
+  p.nseg = (int)(rot / 16);
   p.eps = a.eps;
   const bool row = a.norm_span == 0;
   const int nvec = (int)(a.heads * 16);
-  const int stage_bytes = 2 * p.row_bytes + p.tab_bytes;
+  p.tab_off = (2 * p.row_bytes + 1023) & ~1023;
+  p.stage_bytes = (p.tab_off + p.nseg * 128 + 1023) & ~1023;
+  p.ring_off = ring_offset(nvec, row, mod);
   // deepest ring (a multiple of the pair count, so each stage always serves the same pair) that fits
   int stages = 0;
   for (int s = kMaxStages; s >= kPairs; s -= kPairs)
-    if (smem_bytes_for(s, nvec, row, mod, stage_bytes) <= kSmemLimit) {
+    if (1024 + p.ring_off + s * p.stage_bytes <= kSmemLimit) {
       stages = s;
       break;
     }
   if (stages == 0) return cudaErrorNotSupported;
   p.stages = stages;
-  const int smem = smem_bytes_for(stages, nvec, row, mod, stage_bytes);
+  const int smem = 1024 + p.ring_off + stages * p.stage_bytes;
+  // rotation table as rows of 128 bytes (8 pairs), one box = one token's nseg rows
+  CUtensorMap tm;
+  if (!encode_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.freqs, 32, (uint64_t)a.m * (uint64_t)p.nseg, 128, 32,
+                      (uint32_t)p.nseg, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
   const bool full = rot == 128;
   const int vpl = (int)((a.heads * 16 + 31) / 32);
-  if (vpl <= 4) return launch_vpl<4>(p, row, mod, full, smem, stream);
-  if (vpl <= 8) return launch_vpl<8>(p, row, mod, full, smem, stream);
-  if (vpl <= 12) return launch_vpl<12>(p, row, mod, full, smem, stream);
-  return launch_vpl<16>(p, row, mod, full, smem, stream);
+  if (vpl <= 4) return launch_vpl<4>(tm, p, row, mod, full, smem, stream);
+  if (vpl <= 8) return launch_vpl<8>(tm, p, row, mod, full, smem, stream);
+  if (vpl <= 12) return launch_vpl<12>(tm, p, row, mod, full, smem, stream);
+  return launch_vpl<16>(tm, p, row, mod, full, smem, stream);
 }
 
 }  // namespace h3

@@ -3,14 +3,16 @@
     python -m h3b200.profile_cases CASE [--tokens M] [--iters N]
 
 CASE is one of ``quantize`` (fc1 input quantizer, K = 3072), ``fc1`` (INT8 GEMM
-with the GELU + row-absmax epilogue), ``requant`` (fc2 input quantizer with a
+with the GELU + row-absmax epilogue; ``fc1_bf16`` / ``fc1_i32``: the same GEMM with
+the plain dequant or the int32 epilogue), ``requant`` (fc2 input quantizer with a
 given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
 ``mlp`` (the whole fused MLP call) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
 Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
 norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
 runs the kernels it needs to build its inputs, then launches the kernel under
 study ``--iters`` times, so a profiler can skip the set-up launches by kernel
-name. The process exits non-zero if a kernel reports an error.
+name; ``--time`` also reports the mean CUDA-event time of those launches. The
+process exits non-zero if a kernel reports an error.
 """
 
 from __future__ import annotations
@@ -42,7 +44,23 @@ def mlp_inputs(m: int, dev):
     return wt, x, gate, res
 
 
-def run(case: str, m: int, iters: int) -> None:
+def _timed(fn, iters: int, report: bool):
+    if not report:
+        for _ in range(iters):
+            fn()
+        return None
+    fn()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def run(case: str, m: int, iters: int, report: bool = False):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     h3b200.library()
@@ -57,8 +75,8 @@ def run(case: str, m: int, iters: int) -> None:
         grid_t = max(1, (m + 39 * 40 - 1) // (39 * 40))
         table = rope_grid_table((grid_t, 39, 40), device=dev)[:m].contiguous()
         qo, ko = torch.empty_like(q), torch.empty_like(k)
-        for _ in range(iters):
-            ops.adaln_rms_rope_(q, k, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko)
+        ms = _timed(lambda: ops.adaln_rms_rope_(q, k, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko),
+                    iters, report)
     else:
         wt, x, gate, res = mlp_inputs(m, dev)
         xq, xs = ops.quantize_int8_rowwise(x)
@@ -70,41 +88,46 @@ def run(case: str, m: int, iters: int) -> None:
             ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_GELU_ABSMAX, xs, wt.s1, out=act, row_absmax=amax)
 
         if case == "quantize":
-            for _ in range(iters):
-                ops.quantize_int8_rowwise(x)
+            ms = _timed(lambda: ops.quantize_int8_rowwise(x), iters, report)
         elif case == "fc1":
-            for _ in range(iters):
-                amax.zero_()
-                fc1()
+            ms = _timed(fc1, iters, report)   # row absmax only grows: re-running on the same inputs is idempotent
+        elif case == "fc1_bf16":
+            ms = _timed(lambda: ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_BF16, xs, wt.s1, out=act), iters, report)
+        elif case == "fc1_i32":
+            acc = torch.empty(m, D_FFN, dtype=torch.int32, device=dev)
+            ms = _timed(lambda: ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_I32, out=acc), iters, report)
         elif case in ("requant", "fc2"):
             fc1()
             if case == "requant":
-                for _ in range(iters):
-                    ops.quantize_int8_rowwise_absmax(act, amax)
+                ms = _timed(lambda: ops.quantize_int8_rowwise_absmax(act, amax), iters, report)
             else:
                 q2, xs2 = ops.quantize_int8_rowwise_absmax(act, amax)
-                for _ in range(iters):
-                    ops.int8_gemm_fused(q2, wt.w2q, ops.EPI_GATED_RESIDUAL, xs2, wt.s2, gate=gate, residual=res,
-                                        out=out)
+                ms = _timed(lambda: ops.int8_gemm_fused(q2, wt.w2q, ops.EPI_GATED_RESIDUAL, xs2, wt.s2, gate=gate,
+                                                        residual=res, out=out), iters, report)
         elif case == "mlp":
-            for _ in range(iters):
-                h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=out)
+            ms = _timed(lambda: h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=out), iters,
+                        report)
         else:
             raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
     st = h3b200.device_status(0)
     if st != 0:
         raise SystemExit(f"device status {st:#x}")
+    return ms
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["quantize", "fc1", "requant", "fc2", "mlp", "norm_rope"])
+    ap.add_argument("case", nargs="+", choices=["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp",
+                                                "norm_rope"])
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="report the mean CUDA-event time per launch")
     a = ap.parse_args()
-    run(a.case, a.tokens, a.iters)
-    print(f"profile case {a.case} tokens={a.tokens} iters={a.iters}: ok")
+    for case in a.case:
+        ms = run(case, a.tokens, a.iters, a.time)
+        extra = f" mean {ms:.4f} ms per launch" if ms is not None else ""
+        print(f"profile case {case} tokens={a.tokens} iters={a.iters}: ok{extra}", flush=True)
 
 
 if __name__ == "__main__":
