@@ -15,9 +15,11 @@
 //               stage and, after the last k-block, publishes the accumulator.
 //   warp 2      TMEM allocator (512 columns = two 128x256 s32 accumulators).
 //   warps 4-11  epilogue: tcgen05.ld 32 columns at a time, fused dequant /
-//               activation / gated residual, 128-bit global stores. The two
-//               accumulators let the epilogue of tile i overlap the mainloop of
-//               tile i+1.
+//               activation / gated residual; each warp stages its 32x32 bf16
+//               result in shared memory (64-byte swizzle, conflict-free) and one
+//               lane writes it with a TMA tensor store (int32 results use
+//               128-bit global stores). The two accumulators let the epilogue
+//               of tile i overlap the mainloop of tile i+1.
 // Tiles are visited n-fastest so that the concurrently running CTAs share the
 // same A rows and the whole weight stays resident in the 126 MB L2.
 // No cluster multicast is used anywhere (the same binary runs in multi-GPU jobs).
@@ -42,7 +44,13 @@ constexpr uint32_t IDESC = umma_idesc_i8(BM, BN);
 constexpr int BAR_BYTES = 256;
 constexpr int STAGE_OPS_BYTES = NUM_EPI_WARPS * 2 * 128 * 4;   // per-warp column scales + bias/gate
 constexpr int GELU_TAB_BYTES = 2 * 19 * 128 * 2;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + STAGE_OPS_BYTES + GELU_TAB_BYTES + 1024;
+constexpr int EPI_STAGE_BYTES = 32 * 32 * 2;                    // one 32x32 bf16 box per epilogue warp
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int OFF_OPS = OFF_BAR + BAR_BYTES;
+constexpr int OFF_GELU = OFF_OPS + STAGE_OPS_BYTES;
+constexpr int OFF_EPI = (OFF_GELU + GELU_TAB_BYTES + 1023) / 1024 * 1024;  // swizzled boxes: 1024-aligned
+constexpr int SMEM_BYTES = OFF_EPI + NUM_EPI_WARPS * EPI_STAGE_BYTES + 1024;
+static_assert(SMEM_BYTES <= 232448, "GEMM shared memory exceeds the 227 KB per-block limit");
 
 // status codes recorded when a bounded wait expires
 constexpr unsigned kErrProducer = 0x101, kErrMmaAcc = 0x102, kErrMmaFull = 0x103, kErrEpi = 0x104,
@@ -132,68 +140,60 @@ __device__ __forceinline__ void gelu_chunk(const uint32_t (&r)[32], float xs, co
   amax_bits = max(amax_bits, cmax);
 }
 
-// One 32-column chunk of one accumulator row. ws_s / aux_s: this warp's staged
-// per-column weight scales and bias-or-gate (fp32) for the chunk.
+// int32 accumulators of one 32-column chunk of one row, 128-bit stores.
+__device__ __forceinline__ void store_i32_chunk(const KParams& p, int row, int col0, const uint32_t (&r)[32]) {
+  if (row < p.m) {
+    int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      if (col0 + 4 * g < p.n) stg_v4(o + 4 * g, make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]));
+  }
+}
+
+// bf16 results (packed pairs) of one 32-column chunk of one accumulator row.
+// ws_s / aux_s: this warp's staged per-column weight scales and bias-or-gate
+// (fp32) for the chunk.
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const KParams& p, int row, int col0, const uint32_t (&r)[32],
-                                               float xs, const float* ws_s, const float* aux_s,
-                                               const uint16_t* gtab, uint32_t& amax_bits) {
-  const bool row_ok = row < p.m;
-  if constexpr (EPI == kEpiI32) {
-    if (row_ok) {
-      int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
-#pragma unroll
-      for (int g = 0; g < 8; ++g)
-        if (col0 + 4 * g < p.n) stg_v4(o + 4 * g, make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]));
-    }
-    return;
+__device__ __forceinline__ void epilogue_values(const KParams& p, int row, int col0, const uint32_t (&r)[32],
+                                                float xs, const float* ws_s, const float* aux_s,
+                                                const uint16_t* gtab, uint32_t& amax_bits, uint32_t (&ob)[16]) {
+  if constexpr (EPI == kEpiGeluAbsmax) {
+    gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
   } else {
-    uint32_t ob[16];
-    if constexpr (EPI == kEpiGeluAbsmax) {
-      gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
-    } else {
-      uint32_t res_w[16];
-      if constexpr (EPI == kEpiGatedResidual) {
-        if (row_ok) {
-          const __nv_bfloat16* rp = p.residual + (int64_t)row * p.ldr + col0;
+    uint32_t res_w[16];
+    if constexpr (EPI == kEpiGatedResidual) {
+      const bool row_ok = row < p.m;
+      const __nv_bfloat16* rp = p.residual + (int64_t)row * p.ldr + col0;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 rv = make_uint4(0, 0, 0, 0);
-            if (col0 + 8 * q < p.n) rv = ldg_v4(rp + 8 * q);
-            res_w[4 * q] = rv.x; res_w[4 * q + 1] = rv.y; res_w[4 * q + 2] = rv.z; res_w[4 * q + 3] = rv.w;
-          }
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-        const float4 a4 = *reinterpret_cast<const float4*>(aux_s + 4 * q);
-        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-        uint32_t hb[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = 4 * q + e;
-          uint32_t b = dequant_bits(r[j], xs, wv[e]);
-          if constexpr (EPI == kEpiBF16) {
-            if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
-          }
-          if constexpr (EPI == kEpiGatedResidual) {
-            const uint32_t rw = res_w[j >> 1];
-            const float rv = (j & 1) ? bf16_hi(rw) : bf16_lo(rw);
-            b = bf16_bits(__fadd_rn(rv, __fmul_rn(__uint_as_float(b << 16), av[e])));
-          }
-          hb[e] = b;
-        }
-        ob[2 * q] = hb[0] | (hb[1] << 16);
-        ob[2 * q + 1] = hb[2] | (hb[3] << 16);
+      for (int q = 0; q < 4; ++q) {
+        uint4 rv = make_uint4(0, 0, 0, 0);
+        if (row_ok && col0 + 8 * q < p.n) rv = ldg_v4(rp + 8 * q);
+        res_w[4 * q] = rv.x; res_w[4 * q + 1] = rv.y; res_w[4 * q + 2] = rv.z; res_w[4 * q + 3] = rv.w;
       }
     }
-    if (row_ok) {
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (col0 + 8 * q < p.n) stg_v4(o + 8 * q, make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]));
+    for (int q = 0; q < 8; ++q) {
+      const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      const float4 a4 = *reinterpret_cast<const float4*>(aux_s + 4 * q);
+      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+      uint32_t hb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = 4 * q + e;
+        uint32_t b = dequant_bits(r[j], xs, wv[e]);
+        if constexpr (EPI == kEpiBF16) {
+          if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
+        }
+        if constexpr (EPI == kEpiGatedResidual) {
+          const uint32_t rw = res_w[j >> 1];
+          const float rv = (j & 1) ? bf16_hi(rw) : bf16_lo(rw);
+          b = bf16_bits(__fadd_rn(rv, __fmul_rn(__uint_as_float(b << 16), av[e])));
+        }
+        hb[e] = b;
+      }
+      ob[2 * q] = hb[0] | (hb[1] << 16);
+      ob[2 * q + 1] = hb[2] | (hb[3] << 16);
     }
   }
 }
@@ -201,17 +201,17 @@ __device__ __forceinline__ void epilogue_chunk(const KParams& p, int row, int co
 template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const KParams p) {
+                   const __grid_constant__ CUtensorMap tmO, const KParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  float* ops_smem = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
-  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + STAGES * STAGE_BYTES + BAR_BYTES + STAGE_OPS_BYTES);
+  float* ops_smem = reinterpret_cast<float*>(smem + OFF_OPS);
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + OFF_GELU);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_proxy_async_shared();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (EPI != kEpiI32) tma_prefetch_desc(&tmO);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -315,6 +316,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int half = ew >> 2;              // columns [128*half, 128*half + 128)
     float* ws_s = ops_smem + ew * 256;     // this warp's 128 column scales ...
     float* aux_s = ws_s + 128;             // ... and 128 bias / gate values
+    uint8_t* box = smem + OFF_EPI + ew * EPI_STAGE_BYTES;  // this warp's 32x32 bf16 output box
+    // row `lane` of the box, 16-byte chunk q, at the 64-byte-swizzle position q ^ ((lane >> 1) & 3)
+    uint8_t* box_row = box + lane * 64;
+    const int box_sw = (lane >> 1) & 3;
     int tcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
       const int m_blk = tile / p.num_n_blk;
@@ -349,8 +354,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         tmem_wait_ld();
-        if (col_base + c < p.n)
-          epilogue_chunk<EPI>(p, row, col_base + c, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits);
+        if (col_base + c >= p.n) continue;  // warp-uniform
+        if constexpr (EPI == kEpiI32) {
+          store_i32_chunk(p, row, col_base + c, r);
+        } else {
+          uint32_t ob[16];
+          epilogue_values<EPI>(p, row, col_base + c, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, ob);
+          if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(box_row + ((q ^ box_sw) << 4)) =
+                make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]);
+          fence_proxy_async_shared();
+          __syncwarp();
+          const int box_row0 = m_blk * BM + quarter * 32;
+          if (lane == 0 && box_row0 < p.m) {
+            tma_store_2d(&tmO, box, col_base + c, box_row0);  // rows >= m and columns >= n are clipped
+            bulk_commit_group();
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -358,6 +381,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (EPI == kEpiGeluAbsmax) {
         if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, amax_bits << 16);
       }
+    }
+    if constexpr (EPI != kEpiI32) {
+      if (lane == 0) bulk_wait_all();  // every output box written before the CTA exits
+      __syncwarp();
     }
   }
 
@@ -378,8 +405,8 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
 }
 
 template <int EPI>
-cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, int grid,
-                       cudaStream_t stream) {
+cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const KParams& kp,
+                       int grid, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -388,7 +415,7 @@ cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const KPara
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  gemm_i8_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, kp);
+  gemm_i8_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, kp);
   return cudaGetLastError();
 }
 
@@ -445,9 +472,15 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
     return cudaErrorNotSupported;
   if (a.epilogue == kEpiGatedResidual && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0))
     return cudaErrorNotSupported;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   if (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN))
     return cudaErrorInvalidValue;
+  if (a.epilogue == kEpiI32) {
+    to = tb;  // unused: int32 results are stored directly
+  } else if (!encode_tmap_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
+                             (uint64_t)a.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
+    return cudaErrorInvalidValue;
+  }
   KParams kp;
   kp.m = (int)a.m;
   kp.n = (int)a.n;
@@ -472,10 +505,10 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = (int)std::min<int64_t>(tiles, (int64_t)num_sms(dev));
   switch (a.epilogue) {
-    case kEpiI32: return launch_epi<kEpiI32>(ta, tb, kp, grid, stream);
-    case kEpiBF16: return launch_epi<kEpiBF16>(ta, tb, kp, grid, stream);
-    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, kp, grid, stream);
-    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, kp, grid, stream);
+    case kEpiI32: return launch_epi<kEpiI32>(ta, tb, to, kp, grid, stream);
+    case kEpiBF16: return launch_epi<kEpiBF16>(ta, tb, to, kp, grid, stream);
+    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, to, kp, grid, stream);
+    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, to, kp, grid, stream);
     default: return cudaErrorNotSupported;
   }
 }
