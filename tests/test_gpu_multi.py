@@ -1,0 +1,87 @@
+"""GPU parity on 2 GPUs (NCCL): tensor-parallel MLP and token sharding vs one GPU.
+
+Each rank runs in its own spawned process with one GPU. The tensor-parallel MLP
+(fc1 column-split, all-reduce(MAX) of the row absmax, fc2 row-split, int32
+all-reduce(SUM)) and the token-sharded MLP must both reproduce the single-GPU
+fused MLP bit for bit. Skipped when fewer than 2 GPUs are visible.
+"""
+
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, outdir):
+    sys.path.insert(0, os.path.join(ROOT, "x-minimaxh3_b200"))
+    import torch.distributed as dist
+
+    import h3b200
+    from h3b200 import parallel as P
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        d, ffn, m = 512, 2048, 1000
+        g = torch.Generator().manual_seed(11)           # identical weights and inputs on every rank
+        w1 = (torch.randn(ffn, d, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        w2 = (torch.randn(d, ffn, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        x = torch.randn(m, d, generator=g).to(torch.bfloat16).to(dev)
+        res = torch.randn(m, d, generator=g).to(torch.bfloat16).to(dev)
+        gate = torch.randn(d, generator=g).to(torch.bfloat16).to(dev)
+        wt = h3b200.W8A8MLPWeights.from_float(w1, w2)
+        ref = h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate)
+
+        shard = P.TPShard.from_full(wt.w1q, wt.s1, wt.w2q, wt.s2, world, rank)
+        tp = P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=384)
+
+        lo, hi = P.shard_range(m, world, rank)
+        local = P.token_sharded_mlp(x[lo:hi], res[lo:hi], gate, wt.w1q, wt.s1, wt.w2q, wt.s2)
+        ts = P.gather_tokens(local, m)
+        torch.cuda.synchronize()
+        ok = {
+            "tp": bool(torch.equal(tp, ref)),
+            "token_shard": bool(torch.equal(ts, ref)),
+            "status": h3b200.device_status(rank),
+        }
+        with open(os.path.join(outdir, f"rank{rank}.txt"), "w") as f:
+            f.write(repr(ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_mlp_and_token_sharding_two_gpus(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for r in range(2):
+        res = eval((tmp_path / f"rank{r}.txt").read_text())
+        assert res == {"tp": True, "token_shard": True, "status": 0}, (r, res)
