@@ -328,6 +328,56 @@ def run_ours(args, rank, world, local_rank):
     nr_ms = timed(k_nr, 50, stream)
     nr_bytes = M_TOKENS * NR_BYTES_PER_TOKEN
 
+    # ---- config 2: fused W4A8 MLP (reference's asymmetric group-128 format, int4 at rest) ----
+    g3 = torch.Generator(device=dev).manual_seed(3)
+    w1f = (torch.randn(D_FFN, D_MODEL, generator=g3, device=dev) * 0.02).to(torch.bfloat16)
+    w2f = (torch.randn(D_MODEL, D_FFN, generator=g3, device=dev) * 0.02).to(torch.bfloat16)
+    w4 = h3b200.W4A8MLPWeights.from_float(w1f, w2f, 128)
+    del w1f, w2f
+    x3 = torch.randn(M_TOKENS, D_MODEL, generator=g3, device=dev).to(torch.bfloat16)
+    ws4 = int(h3b200.library().h3b200_fused_gated_mlp_w4a8_workspace_bytes(M_TOKENS, D_MODEL, D_FFN, 128))
+    work4 = torch.empty(ws4, dtype=torch.uint8, device=dev)
+
+    def k_w4a8():
+        h3b200.fused_gated_mlp_w4a8(res, x3, w4, gate, out=out, workspace=work4)
+
+    for _ in range(3):
+        k_w4a8()
+    w4_ms = timed(k_w4a8, 10, stream)
+    del work4, x3
+
+    # ---- config 4: long-video DiT-block slice (norm-RoPE then W8A8 MLP) on this rank's token shard ----
+    from h3b200 import parallel as PAR
+
+    M4, GRID4 = 196560, (45, 52, 84)
+    lo4, hi4 = PAR.shard_range(M4, world, rank)
+    m4 = hi4 - lo4
+    g5 = torch.Generator(device=dev).manual_seed(5 + rank)
+    q4 = torch.randn(m4, 24, 128, generator=g5, device=dev).to(torch.bfloat16)
+    k4 = torch.randn(m4, 24, 128, generator=g5, device=dev).to(torch.bfloat16)
+    x4 = torch.randn(m4, D_MODEL, generator=g5, device=dev).to(torch.bfloat16)
+    r4 = torch.randn(m4, D_MODEL, generator=g5, device=dev).to(torch.bfloat16)
+    o4 = torch.empty_like(r4)
+    table4 = rope_grid_table(GRID4, token_slice=(lo4, hi4), device=dev)
+    work5 = torch.empty(int(h3b200.library().h3b200_fused_gated_mlp_workspace_bytes(m4, D_MODEL, D_FFN)),
+                        dtype=torch.uint8, device=dev)
+
+    def k_block():
+        ops.adaln_rms_rope_(q4, k4, table4, wq, wk, sc, sh, 1e-6, "row", 0)
+        h3b200.fused_gated_mlp(r4, x4, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=o4, workspace=work5)
+
+    for _ in range(2):
+        k_block()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    blk_ms = timed(k_block, 5, stream)
+    if world > 1:
+        t = torch.tensor([blk_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        blk_ms = float(t.item())
+    del q4, k4, x4, r4, o4, table4, work5
+
     # ---- library INT8 reference: cuBLASLt through torch._int_mm, 8192^3, same box and run ----
     lib_int8_tops = None
     try:
@@ -402,6 +452,12 @@ def run_ours(args, rank, world, local_rank):
                 **{k: {"ms": v} for k, v in comp_ms.items()},
                 "fc2_gemm_gated_residual_tops": fc2_ops / (comp_ms["fc2_gemm_gated_residual"] * 1e-3) / 1e12,
                 "cublaslt_int8_8192_tops": lib_int8_tops,
+                "w4a8_mlp_cfg2": {"ms": w4_ms, "tokens_per_s": M_TOKENS / (w4_ms * 1e-3),
+                                  "int8_tops": M_TOKENS * OPS_PER_TOKEN / (w4_ms * 1e-3) / 1e12,
+                                  "weights": "asymmetric int4, group 128, ConvRot-256, decoded per call"},
+                "long_video_block_cfg4": {"tokens_total": M4, "tokens_this_rank": m4, "ms": blk_ms,
+                                          "tokens_per_s": M4 / (blk_ms * 1e-3),
+                                          "mode": f"token-shard x{world} (norm-RoPE + W8A8 MLP per rank)"},
                 "norm_rope_cfg3": {"ms": nr_ms, "achieved": nr_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                    "frac": nr_gbs / peaks["hbm_gbs"], "bytes_per_token": NR_BYTES_PER_TOKEN,
                                    "table_bytes_per_token": NR_TABLE_BYTES_PER_TOKEN,

@@ -242,6 +242,31 @@ H3B200_API int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t*
                             int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                             h3b200_stream_t stream);
 
+/*
+ * Fused gated W4A8 MLP on a token chunk (config 2):
+ *   h = w4a8_linear(x, W1); a = gelu_tanh(h); y = w4a8_linear(a, W2);
+ *   out = residual + y * gate   (bf16 addcmul)
+ * with w4a8_linear as h3b200_w4a8_int8_linear (ConvRot-256 + per-token INT8
+ * activations, asymmetric group correction). The weights stay in the
+ * reference's packed format (int4 at rest: qdata int8 [n, k/2], s_rel fp32
+ * [n, k/group], s_channel fp32 [n], correction bf16 [k/group, n]); each call
+ * decodes them into an int8 grid in the workspace (the GEMM then reads it
+ * from L2). Composition of w4a8_int8_linear (tensor/w4a8_int8.py:89-115),
+ * apply_input_act (backends/_activations.py:40-53) and the addcmul of
+ * try_fused_gated_mlp (h3serve/native_engine/model/fused_mlp.py:414-425).
+ * x, residual, out: bf16 [m, d] (out may alias residual); gate: bf16 [d];
+ * W1 is [ffn, d], W2 is [d, ffn]; d and ffn multiples of 256 and of group_size.
+ */
+H3B200_API int64_t h3b200_fused_gated_mlp_w4a8_workspace_bytes(int64_t m, int64_t d, int64_t ffn,
+                                                              int64_t group_size);
+H3B200_API int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1, const float* s_rel1,
+                                           const float* s_channel1, const void* correction1, const int8_t* qdata2,
+                                           const float* s_rel2, const float* s_channel2, const void* correction2,
+                                           const void* gate, const void* residual, int64_t ldr, void* out,
+                                           int64_t ldo, int64_t m, int64_t d, int64_t ffn, int64_t group_size,
+                                           int act, void* workspace, int64_t workspace_bytes,
+                                           h3b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,3 +58,35 @@ def test_w4a8_int32_accumulators_exact(golden):
     g = golden("w4a8_small")
     acc = h3b200.mm_int8(torch.from_numpy(g["xq"]).cuda(), torch.from_numpy(g["grid"]).cuda().t())
     np.testing.assert_array_equal(np_(acc), g["acc"])
+
+
+def test_fused_w4a8_mlp_matches_op_chain_and_oracle():
+    """Config-2 MLP: the fused entry point equals the chain of single W4A8 ops bit for bit,
+    and the oracle composition within the north-star tolerance."""
+    gen = torch.Generator().manual_seed(3)
+    d, ffn, m = 512, 1024, 200
+    w1 = randn_bf16((ffn, d), gen, std=0.02)
+    w2 = randn_bf16((d, ffn), gen, std=0.02)
+    x = randn_bf16((m, d), gen)
+    gate = randn_bf16((d,), gen)
+    res = randn_bf16((m, d), gen)
+    wt = h3b200.W4A8MLPWeights.from_float(w1, w2).to("cuda")
+    out = h3b200.fused_gated_mlp_w4a8(res.cuda(), x.cuda(), wt, gate.cuda())
+    assert h3b200.device_status(0) == 0
+    h = h3b200.w4a8_int8_linear(x.cuda(), wt.q1, wt.s_rel1, wt.s_ch1, correction=wt.corr1, group_size=128)
+    y = h3b200.w4a8_int8_linear(h, wt.q2, wt.s_rel2, wt.s_ch2, correction=wt.corr2, group_size=128,
+                                input_act="gelu_tanh")
+    f = O.bf16_to_f32
+    expect = O.f32_to_bf16(f(t2u(res)) + f(t2u(y)) * f(t2u(gate))[None, :])
+    np.testing.assert_array_equal(t2u(out), expect)
+    # oracle composition (exact rotation, float64 correction)
+    q1, q2 = np_(wt.q1), np_(wt.q2)
+    oh = O.w4a8_int8_linear_quantized(t2u(x), q1, np_(wt.s_rel1), np_(wt.s_ch1), t2u(wt.corr1), 128, 256)
+    oy = O.w4a8_int8_linear_quantized(O.gelu_tanh_bf16(oh), q2, np_(wt.s_rel2), np_(wt.s_ch2), t2u(wt.corr2), 128, 256)
+    ref = O.gated_residual(t2u(res), oy, t2u(gate))
+    rel, mx = rel_l2(t2u(out), ref)
+    assert rel <= 1e-2 and mx <= 2e-2
+    # in place on the residual
+    r2 = res.cuda()
+    h3b200.fused_gated_mlp_w4a8(r2, x.cuda(), wt, gate.cuda(), out=r2)
+    np.testing.assert_array_equal(t2u(r2), t2u(out))

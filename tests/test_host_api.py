@@ -41,3 +41,31 @@ def test_rope_table_builder_matches_oracle():
         t = rope_grid_table(grid, token_slice=sl, device="cpu").numpy()
         o = O.rope_grid_table(grid, token_slice=sl)
         np.testing.assert_array_equal(t, o)
+
+
+def test_w4a8_weight_quantizer_matches_reference_golden_and_oracle(golden):
+    """Offline W4A8 weight preparation (torch) vs the reference's quantize_w4a8_int8_weight output."""
+    import numpy as np
+    import torch
+
+    import oracle as O
+    from h3b200.weights import quantize_w4a8_weight
+
+    def to_t(u):
+        return torch.from_numpy(np.ascontiguousarray(u).view(np.int16)).view(torch.bfloat16)
+
+    def to_u(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    g = golden("w4a8_small")
+    q, s_rel, s_ch, corr = quantize_w4a8_weight(to_t(g["w_bf16"]), 128, 256)
+    np.testing.assert_array_equal(q.numpy(), g["qdata"])
+    np.testing.assert_array_equal(s_rel.numpy(), g["s_rel"])
+    np.testing.assert_array_equal(s_ch.numpy(), g["s_channel"])
+    np.testing.assert_array_equal(to_u(corr), g["correction"])
+    w = (torch.randn(384, 1024, generator=torch.Generator().manual_seed(3)) * 0.02).to(torch.bfloat16)
+    got = quantize_w4a8_weight(w, 128, 256)
+    want = O.w4a8_quantize_weight(to_u(w), 128, 256)
+    for a, b in zip(got[:3], want[:3]):
+        np.testing.assert_array_equal(a.numpy(), b)
+    np.testing.assert_array_equal(to_u(got[3]), want[3])

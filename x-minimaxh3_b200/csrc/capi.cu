@@ -298,6 +298,74 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
   return H3B200_OK;
 }
 
+
+int64_t h3b200_fused_gated_mlp_w4a8_workspace_bytes(int64_t m, int64_t d, int64_t ffn, int64_t group_size) {
+  if (m < 0 || d <= 0 || ffn <= 0 || group_size <= 0) return 0;
+  return round_up(ffn * d, 256) * 2 + round_up(m * d, 256) * 3 + round_up(m * 4, 256) * 2 +
+         round_up(m * (d / group_size) * 4, 256) + round_up(m * ffn * 2, 256) + round_up(m * ffn, 256) +
+         round_up(m * (ffn / group_size) * 4, 256) + 2048;
+}
+
+int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1, const float* s_rel1,
+                                const float* s_channel1, const void* correction1, const int8_t* qdata2,
+                                const float* s_rel2, const float* s_channel2, const void* correction2,
+                                const void* gate, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                                int64_t m, int64_t d, int64_t ffn, int64_t group_size, int act, void* workspace,
+                                int64_t workspace_bytes, h3b200_stream_t stream) {
+  if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: bad shape m=%lld d=%lld ffn=%lld", (long long)m, (long long)d, (long long)ffn);
+  if (act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_w4a8: only act=gelu_tanh (1) is built, got %d", act);
+  if (group_size < 16 || group_size % 16 || 256 % group_size) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_w4a8: group_size must be 16..256 and divide 256, got %lld", (long long)group_size);
+  if (d % 256 || ffn % 256) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_w4a8: d and ffn must be multiples of 256 (ConvRot-256)");
+  if (m == 0) return H3B200_OK;
+  if (!x || !qdata1 || !s_rel1 || !s_channel1 || !qdata2 || !s_rel2 || !s_channel2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: NULL pointer");
+  const int64_t need = h3b200_fused_gated_mlp_w4a8_workspace_bytes(m, d, ffn, group_size);
+  if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: workspace too small (need %lld bytes)", (long long)need);
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* grid1 = static_cast<int8_t*>(c.take(ffn * d));
+  int8_t* grid2 = static_cast<int8_t*>(c.take(d * ffn));
+  int8_t* xq = static_cast<int8_t*>(c.take(m * d));
+  float* xs = static_cast<float*>(c.take(m * 4));
+  int32_t* gs1 = static_cast<int32_t*>(c.take(m * (d / group_size) * 4));
+  void* h = c.take(m * ffn * 2);
+  int8_t* q2 = static_cast<int8_t*>(c.take(m * ffn));
+  float* xs2 = static_cast<float*>(c.take(m * 4));
+  int32_t* gs2 = static_cast<int32_t*>(c.take(m * (ffn / group_size) * 4));
+  void* y = c.take(m * d * 2);
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: workspace too small");
+  cudaStream_t st = S(stream);
+  cudaError_t e = h3::launch_dequant_int4(qdata1, s_rel1, ffn, d, group_size, grid1, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: decode W1");
+  e = h3::launch_dequant_int4(qdata2, s_rel2, d, ffn, group_size, grid2, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: decode W2");
+  // fc1: ConvRot-quantize x, GEMM, asymmetric correction
+  e = h3::launch_quantize_convrot(x, ldx, m, d, H3B200_ACT_NONE, xq, xs, correction1 ? gs1 : nullptr, group_size, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize x");
+  h3::GemmArgs g1;
+  g1.a = xq; g1.w = grid1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
+  g1.epilogue = h3::kEpiBF16; g1.a_scale = xs; g1.w_scale = s_channel1; g1.w_scale_per_channel = 1;
+  g1.out = h; g1.ldo = ffn;
+  e = h3::launch_gemm_i8(g1, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1");
+  if (correction1) {
+    e = h3::launch_w4a8_correction(gs1, xs, correction1, m, ffn, d / group_size, h, ffn, st);
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1 correction");
+  }
+  // fc2: GELU + ConvRot-quantize h, GEMM, correction, gated residual
+  e = h3::launch_quantize_convrot(h, ffn, m, ffn, H3B200_ACT_GELU_TANH, q2, xs2, correction2 ? gs2 : nullptr, group_size, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize gelu(h)");
+  h3::GemmArgs g2;
+  g2.a = q2; g2.w = grid2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
+  g2.epilogue = h3::kEpiBF16; g2.a_scale = xs2; g2.w_scale = s_channel2; g2.w_scale_per_channel = 1;
+  g2.out = y; g2.ldo = d;
+  e = h3::launch_gemm_i8(g2, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2");
+  if (correction2) {
+    e = h3::launch_w4a8_correction(gs2, xs2, correction2, m, d, ffn / group_size, y, d, st);
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2 correction");
+  }
+  e = h3::launch_gated_residual_bf16(y, d, gate, residual, ldr, out, ldo, m, d, st);
+  return from_cuda(e, "fused_gated_mlp_w4a8: gated residual");
+}
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -85,6 +85,13 @@ __device__ __forceinline__ float gelu_tanh_exact(float x) {
   return gelu_finish(hx, tc);
 }
 
+// Exact tanh-GELU of every bf16 input (index = the input's bits), filled once
+// per device from gelu_tanh_exact by ensure_gelu_table() before the first
+// kernel that reads it.
+extern __device__ uint16_t g_gelu_bf16[65536];
+
+__device__ __forceinline__ uint32_t gelu_bf16_bits(uint32_t xbits16) { return g_gelu_bf16[xbits16 & 0xFFFFu]; }
+
 // ---------------------------------------------------------------------------
 // mbarrier (shared::cta) with bounded waits
 // ---------------------------------------------------------------------------

@@ -74,6 +74,16 @@ cudaError_t launch_w4a8_correction(const int32_t* gsum, const float* xs, const v
 
 int num_sms(int device);
 
+// Fills the device's exact bf16 tanh-GELU table on first use (once per device,
+// synchronously on `stream`); cudaErrorStreamCaptureUnsupported if that first
+// use happens inside a stream capture.
+cudaError_t ensure_gelu_table(cudaStream_t stream);
+
+// out = bf16(residual + y * gate) (fp32 math, one rounding), bf16 [m, n] rows.
+cudaError_t launch_gated_residual_bf16(const void* y, int64_t ldy, const void* gate, const void* residual,
+                                       int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
+                                       cudaStream_t stream);
+
 // 2-D tiled TMA descriptor (no interleave, 256-byte L2 promotion, no OOB fill);
 // false when the driver's encoder is unavailable or rejects the layout.
 bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t rows,

@@ -21,98 +21,22 @@
 // longer rows one 256-thread CTA per row. HBM sees one read of x (2 B/elem),
 // one write of q (1 B/elem) and 4 B of scale per row; 128-bit loads, 64-bit
 // stores.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "quant_math.cuh"
 
 namespace h3 {
 
 namespace {
 
 constexpr int kQThreads = 256;
-constexpr uint32_t kMidWin = 8;
-
-__device__ __forceinline__ float quant_divisor(float scale) {
-  float sb = bf16_round(scale);
-  return sb == 0.0f ? 1.17549435e-38f : sb;  // torch.finfo(bf16).tiny substitution
-}
 
 __device__ __forceinline__ int8_t quant_one(float x, float sb) {
   float v = rintf(bf16_round(__fdiv_rn(x, sb)));
   v = fminf(fmaxf(v, -128.0f), 127.0f);
   return (int8_t)(int)v;
-}
-
-// ---- packed helpers (sm_100: f32x2 and bf16x2 arithmetic) ----
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_dup(float v) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(w << 16), "r"(w & 0xFFFF0000u));
-  return r;
-}
-__device__ __forceinline__ void f2_bits(uint64_t v, uint32_t& lo, uint32_t& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint32_t bf16x2_from_bits(uint32_t lo, uint32_t hi) {  // round to nearest even
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "r"(hi), "r"(lo));
-  return r;
-}
-__device__ __forceinline__ uint32_t bf16x2_clamp_i8(uint32_t b) {  // clamp both halves to [-128, 127]
-  uint32_t r;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(b), "r"(0xC300C300u));
-  asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(0x42FE42FEu));
-  return r;
-}
-
-// True when fp32 bits t have their low 16 bits within kMidWin of 0x8000 (a bf16
-// rounding midpoint): (t << 16) + ((kMidWin - 0x8000) << 16) < (2 kMidWin + 1) << 16.
-__device__ __forceinline__ bool near_midpoint(uint32_t t) {
-  return t * 65536u + ((kMidWin - 0x8000u) << 16) < ((2u * kMidWin + 1u) << 16);
-}
-
-// 8 bf16 (one 16-byte vector) -> 8 int8 packed in a uint2, for r = rcp_rn(sb);
-// the same result as quant_one on each element. Per pair: packed product,
-// midpoint test, bf16x2 rounding and clamp, then round-to-nearest-even to an
-// integer by adding 1.5 * 2^23 (the integer lands in the low byte of the sum).
-__device__ __forceinline__ uint2 quant_vec8(const uint4& v, float sb, float r) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  const uint64_t r2 = f2_dup(r);
-  uint32_t b[4];
-  bool amb = false;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    uint32_t t0, t1;
-    f2_bits(f2_mul(bf16x2_to_f2(w[e]), r2), t0, t1);
-    amb |= near_midpoint(t0) | near_midpoint(t1);
-    b[e] = bf16x2_from_bits(t0, t1);
-  }
-  if (amb) {  // rare: recompute this vector's quotients with the IEEE division
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      b[e] = bf16x2_from_bits(__float_as_uint(__fdiv_rn(bf16_lo(w[e]), sb)),
-                              __float_as_uint(__fdiv_rn(bf16_hi(w[e]), sb)));
-  }
-  const uint64_t magic = f2_dup(12582912.0f);  // 1.5 * 2^23
-  uint32_t q[8];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) f2_bits(f2_add(bf16x2_to_f2(bf16x2_clamp_i8(b[e])), magic), q[2 * e], q[2 * e + 1]);
-  const uint32_t lo = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
-  const uint32_t hi = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
-  return make_uint2(lo, hi);
 }
 
 __device__ __forceinline__ uint32_t absmax_bits8(const uint4& v) {
@@ -123,14 +47,16 @@ __device__ __forceinline__ uint32_t absmax_bits8(const uint4& v) {
   return max(c & 0xFFFFu, c >> 16);
 }
 
+// x is a bf16 value (as fp32); the activation result is bf16 too
 __device__ __forceinline__ float act_apply(float x, int act) {
-  return act == H3B200_ACT_GELU_TANH ? bf16_round(gelu_tanh_exact(x)) : x;
+  return act == H3B200_ACT_GELU_TANH ? __uint_as_float(gelu_bf16_bits(__float_as_uint(x) >> 16) << 16) : x;
 }
 
 __device__ __forceinline__ void apply_act_vec(uint4& v, int act) {
+  if (act != H3B200_ACT_GELU_TANH) return;
   uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-  for (int e = 0; e < 4; ++e) w[e] = pack_bf16(act_apply(bf16_lo(w[e]), act), act_apply(bf16_hi(w[e]), act));
+  for (int e = 0; e < 4; ++e) w[e] = gelu_bf16_bits(w[e]) | (gelu_bf16_bits(w[e] >> 16) << 16);
 }
 
 __device__ __forceinline__ float row_scale(float rowmax) { return fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f); }
@@ -325,7 +251,69 @@ __global__ void dequant_gated_residual_kernel(const int32_t* __restrict__ acc, c
   stg_v4(out + row * ldo + c, make_uint4(o[0], o[1], o[2], o[3]));
 }
 
+__global__ void gelu_table_init_kernel() {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536u) g_gelu_bf16[i] = bf16_bits(gelu_tanh_exact(__uint_as_float(i << 16)));
+}
+
+// out = bf16(residual + y * gate), 8 columns per thread
+__global__ void gated_residual_bf16_kernel(const __nv_bfloat16* y, int64_t ldy, const __nv_bfloat16* __restrict__ gate,
+                                           const __nv_bfloat16* residual, int64_t ldr, __nv_bfloat16* out,
+                                           int64_t ldo, int64_t m, int64_t n) {
+  const int64_t per_row = n / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= m * per_row) return;
+  const int64_t row = idx / per_row;
+  const int64_t c = (idx - row * per_row) * 8;
+  const uint4 yv = ldg_v4(y + row * ldy + c);
+  const uint4 rv = ldg_v4(residual + row * ldr + c);
+  const uint4 gv = ldg_nc_v4(gate + c);
+  const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    o[e] = pack_bf16(__fadd_rn(bf16_lo(rw[e]), __fmul_rn(bf16_lo(yw[e]), bf16_lo(gw[e]))),
+                     __fadd_rn(bf16_hi(rw[e]), __fmul_rn(bf16_hi(yw[e]), bf16_hi(gw[e]))));
+  stg_v4(out + row * ldo + c, make_uint4(o[0], o[1], o[2], o[3]));
+}
+
 }  // namespace
+
+__device__ uint16_t g_gelu_bf16[65536];
+
+cudaError_t ensure_gelu_table(cudaStream_t stream) {
+  static std::mutex mu;
+  static bool ready[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ready[dev]) return cudaSuccess;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if ((e = cudaStreamIsCapturing(stream, &cap)) != cudaSuccess) return e;
+  if (cap != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
+  gelu_table_init_kernel<<<256, 256, 0, stream>>>();
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
+  ready[dev] = true;
+  return cudaSuccess;
+}
+
+cudaError_t launch_gated_residual_bf16(const void* y, int64_t ldy, const void* gate, const void* residual,
+                                       int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
+                                       cudaStream_t stream) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  if (n % 8 || ldy % 8 || ldr % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(y) & 15) ||
+      (reinterpret_cast<uintptr_t>(residual) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(gate) & 15))
+    return cudaErrorNotSupported;
+  const int64_t total = m * (n / 8);
+  gated_residual_bf16_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(y), ldy, static_cast<const __nv_bfloat16*>(gate),
+      static_cast<const __nv_bfloat16*>(residual), ldr, static_cast<__nv_bfloat16*>(out), ldo, m, n);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,
                                           const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,
@@ -344,6 +332,10 @@ cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, c
 
 cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
+  if (act == H3B200_ACT_GELU_TANH) {
+    const cudaError_t e = ensure_gelu_table(stream);
+    if (e != cudaSuccess) return e;
+  }
   apply_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
                                                                    static_cast<__nv_bfloat16*>(y), n, act);
   return cudaGetLastError();
@@ -352,6 +344,10 @@ cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStr
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
                                  int8_t* q, float* scale, cudaStream_t stream) {
   if (m == 0) return cudaSuccess;
+  if (act == H3B200_ACT_GELU_TANH) {
+    const cudaError_t e = ensure_gelu_table(stream);
+    if (e != cudaSuccess) return e;
+  }
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
   const bool aligned = (k % 8 == 0) && (ldx % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                        ((reinterpret_cast<uintptr_t>(q) & 7) == 0);

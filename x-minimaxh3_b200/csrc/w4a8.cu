@@ -9,6 +9,7 @@
 // backends/cuda/__init__.py:2294-2297).
 #include "common.cuh"
 #include "kernels.h"
+#include "quant_math.cuh"
 
 namespace h3 {
 namespace {
@@ -89,16 +90,16 @@ __global__ void __launch_bounds__(256) quantize_convrot_kernel(const __nv_bfloat
     const int64_t g = warp + 8 * gi;
     if (g < ngroups) {  // warp-uniform
       const uint4 raw = ldg_nc_v4(x + row * ldx + g * 256 + lane * 8);
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      if (act == H3B200_ACT_GELU_TANH) {  // exact bf16 GELU from the device table
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = gelu_bf16_bits(w[e]) | (gelu_bf16_bits(w[e] >> 16) << 16);
+      }
       float v[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         v[2 * e] = bf16_lo(w[e]);
         v[2 * e + 1] = bf16_hi(w[e]);
-      }
-      if (act == H3B200_ACT_GELU_TANH) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = bf16_round(gelu_tanh_exact(v[e]));
       }
       // digit 0 (lane-local, elements 4a + b)
 #pragma unroll
@@ -139,25 +140,19 @@ __global__ void __launch_bounds__(256) quantize_convrot_kernel(const __nv_bfloat
 #pragma unroll
   for (int i = 1; i < 8; ++i) rowmax = fmaxf(rowmax, red[i]);
   const float s = fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f);
-  float sb = bf16_round(s);
-  if (sb == 0.0f) sb = 1.17549435e-38f;
+  const float sb = quant_divisor(s);
+  const float rcp = __frcp_rn(sb);
   const int lanes_per_sum = (int)(sum_group / 8);
 #pragma unroll
   for (int gi = 0; gi < GPW; ++gi) {
     const int64_t g = warp + 8 * gi;
     if (g < ngroups) {
-      uint32_t lo = 0, hi = 0;
-      int isum = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float qv = rintf(bf16_round(__fdiv_rn(vals[gi][e], sb)));
-        qv = fminf(fmaxf(qv, -128.0f), 127.0f);
-        const int qi = (int)qv;
-        isum += qi;
-        if (e < 4) lo |= (uint32_t)(uint8_t)(int8_t)qi << (8 * e);
-        else hi |= (uint32_t)(uint8_t)(int8_t)qi << (8 * (e - 4));
-      }
-      *reinterpret_cast<uint2*>(q + row * k + g * 256 + lane * 8) = make_uint2(lo, hi);
+      // the rotated values are bf16-exact: pack them and quantize like quantize_int8_rowwise
+      const uint4 pv = make_uint4(pack_bf16(vals[gi][0], vals[gi][1]), pack_bf16(vals[gi][2], vals[gi][3]),
+                                  pack_bf16(vals[gi][4], vals[gi][5]), pack_bf16(vals[gi][6], vals[gi][7]));
+      const uint2 qq = quant_vec8(pv, sb, rcp);
+      int isum = __dp4a((int)qq.x, 0x01010101, __dp4a((int)qq.y, 0x01010101, 0));  // sum of the 8 int8
+      *reinterpret_cast<uint2*>(q + row * k + g * 256 + lane * 8) = qq;
       if (gsum != nullptr) {
         for (int o = 1; o < lanes_per_sum; o <<= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
         if ((lane % lanes_per_sum) == 0) gsum[row * (k / sum_group) + (g * 256 + lane * 8) / sum_group] = isum;
@@ -256,6 +251,10 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
   if (k % 256 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 7))
     return cudaErrorNotSupported;
   if (group_sums != nullptr && (sum_group < 8 || sum_group > 256 || 256 % sum_group)) return cudaErrorNotSupported;
+  if (act == H3B200_ACT_GELU_TANH) {
+    const cudaError_t e = ensure_gelu_table(stream);
+    if (e != cudaSuccess) return e;
+  }
   const int64_t ng = k / 256;
   const int64_t gpw = (ng + 7) / 8;
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);

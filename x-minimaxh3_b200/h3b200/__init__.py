@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     adaln_rms_rope_,
     dequant_int4_grouped_to_int8,
     fused_gated_mlp,
+    fused_gated_mlp_w4a8,
     input_act_code,
     int8_gemm_fused,
     int8_linear,
@@ -30,7 +31,7 @@ from .ops import (  # noqa: F401
 )
 from .pipeline import fused_gated_mlp_host  # noqa: F401
 from .rope import rope_grid_table  # noqa: F401
-from .weights import quantize_int8_weight, W8A8MLPWeights  # noqa: F401
+from .weights import quantize_int8_weight, quantize_w4a8_weight, W4A8MLPWeights, W8A8MLPWeights  # noqa: F401
 
 __version__ = "0.1.0"
 

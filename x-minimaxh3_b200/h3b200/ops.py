@@ -25,6 +25,7 @@ __all__ = [
     "int8_gemm_fused",
     "dequant_gated_residual",
     "fused_gated_mlp",
+    "fused_gated_mlp_w4a8",
     "adaln_rms_rope",
     "adaln_rms_rope_",
     "rms_rope_split_half",
@@ -302,6 +303,45 @@ def fused_gated_mlp(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Ten
     _lib.call("h3b200_fused_gated_mlp", x2.data_ptr(), ldx, w1q.contiguous().data_ptr(), ws1.data_ptr(),
               w2q.contiguous().data_ptr(), ws2.data_ptr(), g.data_ptr(), r2.data_ptr(), ldr, o2.data_ptr(), ldo,
               m, d, ffn, _lib.ACT_GELU_TANH, workspace.data_ptr(), workspace.numel(), _stream(hidden))
+    return out
+
+
+def fused_gated_mlp_w4a8(residual: torch.Tensor, hidden: torch.Tensor, weights, gate: torch.Tensor,
+                         act: str = "gelu_tanh", out: torch.Tensor | None = None,
+                         workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + w4a8_linear(gelu(w4a8_linear(hidden, W1)), W2) * gate`` (config-2 MLP).
+
+    ``weights`` is a :class:`h3b200.W4A8MLPWeights` (the reference's asymmetric
+    group-128 format, int4 at rest); each call decodes it into the workspace.
+    Composition of ``w4a8_int8_linear`` (tensor/w4a8_int8.py:89-115), the
+    tanh-GELU input activation and the addcmul of ``try_fused_gated_mlp``
+    (h3serve/native_engine/model/fused_mlp.py:414-425)."""
+    _need_cuda(residual, hidden, gate)
+    if act != "gelu_tanh":
+        raise NotImplementedError(f"fused_gated_mlp_w4a8 builds act='gelu_tanh' only, got {act!r}")
+    for name, t in (("residual", residual), ("hidden", hidden), ("gate", gate)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16, got {t.dtype}")
+    x2, ldx = _rows(hidden)
+    r2, ldr = _rows(residual)
+    m, d = x2.shape
+    ffn = weights.ffn
+    if weights.d != d or r2.shape != x2.shape:
+        raise ValueError(f"hidden/residual [M, {d}] do not match the weights (d={weights.d})")
+    g = gate.reshape(-1).contiguous()
+    if g.numel() != d:
+        raise ValueError(f"gate must have {d} elements (one modulation row)")
+    if out is None:
+        out = torch.empty_like(r2)
+    o2, ldo = _rows(out)
+    nbytes = int(_lib.load().h3b200_fused_gated_mlp_w4a8_workspace_bytes(m, d, ffn, weights.group_size))
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
+    w = weights
+    _lib.call("h3b200_fused_gated_mlp_w4a8", x2.data_ptr(), ldx, w.q1.data_ptr(), w.s_rel1.data_ptr(),
+              w.s_ch1.data_ptr(), w.corr1.data_ptr(), w.q2.data_ptr(), w.s_rel2.data_ptr(), w.s_ch2.data_ptr(),
+              w.corr2.data_ptr(), g.data_ptr(), r2.data_ptr(), ldr, o2.data_ptr(), ldo, m, d, ffn, w.group_size,
+              _lib.ACT_GELU_TANH, workspace.data_ptr(), workspace.numel(), _stream(hidden))
     return out
 
 
