@@ -234,9 +234,11 @@ H3B200_API int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, in
  * backends/cuda/__init__.py:2139-2298, asymmetric correction :2294-2297).
  * grid: int8 [n, k] decoded weight (h3b200_dequant_int4_grouped_to_int8);
  * s_channel: fp32 [n]; correction: bf16 [k/group, n] or NULL (symmetric).
- * workspace: h3b200_w4a8_linear_workspace_bytes(m, k, group) bytes.
+ * workspace: h3b200_w4a8_linear_workspace_bytes(m, n, k, group) bytes. The
+ * correction runs as a bf16 tensor-core GEMM (fp32 accumulation), at most 128
+ * groups.
  */
-H3B200_API int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t k, int64_t group_size);
+H3B200_API int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group_size);
 H3B200_API int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
                             const void* correction, int64_t group_size, int64_t convrot_group, int act, void* out,
                             int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,

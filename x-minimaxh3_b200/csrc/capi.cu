@@ -256,12 +256,12 @@ int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, int64_t k, in
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: unsupported act %d", act);
   if (m == 0) return H3B200_OK;
   if (!x || !q || !scale) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: NULL pointer");
-  return from_cuda(h3::launch_quantize_convrot(x, ldx, m, k, act, q, scale, nullptr, 0, S(stream)), "quantize_int8_rowwise_convrot");
+  return from_cuda(h3::launch_quantize_convrot(x, ldx, m, k, act, q, scale, nullptr, 0, 0, S(stream)), "quantize_int8_rowwise_convrot");
 }
 
-int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t k, int64_t group_size) {
-  const int64_t g = group_size > 0 ? k / group_size : 0;
-  return round_up(m * k, 256) + round_up(m * 4, 256) + round_up(m * g * 4, 256) + 768;
+int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group_size) {
+  const int64_t kp = group_size > 0 ? h3::correction_kpad(k / group_size) : 0;
+  return round_up(m * k, 256) + round_up(m * 4, 256) + round_up(m * kp * 2, 256) + round_up(n * kp * 2, 256) + 1024;
 }
 
 int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
@@ -276,14 +276,17 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
   if (m == 0 || n == 0) return H3B200_OK;
   if (!x || !grid || !s_channel || !out) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: NULL pointer");
   if (n % 8) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: needs n %% 8 == 0");
-  if (workspace == nullptr || workspace_bytes < h3b200_w4a8_linear_workspace_bytes(m, k, group_size)) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: workspace too small (need %lld bytes)", (long long)h3b200_w4a8_linear_workspace_bytes(m, k, group_size));
+  if (workspace == nullptr || workspace_bytes < h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size)) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: workspace too small (need %lld bytes)", (long long)h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size));
+  const int64_t groups = k / group_size, kp = h3::correction_kpad(groups);
+  if (correction != nullptr && kp > 128) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: at most 128 correction groups are built (K / group_size = %lld)", (long long)groups);
   Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
   int8_t* xq = static_cast<int8_t*>(c.take(m * k));
   float* xs = static_cast<float*>(c.take(m * 4));
-  int32_t* gs = static_cast<int32_t*>(c.take(m * (k / group_size) * 4));
+  void* sx = c.take(m * kp * 2);
+  void* corr_t = c.take(n * kp * 2);
   if (!c.ok) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: workspace too small");
   cudaStream_t st = S(stream);
-  cudaError_t e = h3::launch_quantize_convrot(x, ldx, m, k, act, xq, xs, correction ? gs : nullptr, group_size, st);
+  cudaError_t e = h3::launch_quantize_convrot(x, ldx, m, k, act, xq, xs, correction ? sx : nullptr, group_size, kp, st);
   if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: convrot quantize");
   h3::GemmArgs g;
   g.a = xq; g.w = grid; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
@@ -292,7 +295,9 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
   e = h3::launch_gemm_i8(g, st);
   if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: gemm");
   if (correction != nullptr) {
-    e = h3::launch_w4a8_correction(gs, xs, correction, m, n, k / group_size, out, n, st);
+    e = h3::launch_correction_transpose(correction, groups, n, kp, corr_t, st);
+    if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction layout");
+    e = h3::launch_w4a8_correction(sx, corr_t, kp, m, n, out, n, st);
     if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction");
   }
   return H3B200_OK;
@@ -301,9 +306,10 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
 
 int64_t h3b200_fused_gated_mlp_w4a8_workspace_bytes(int64_t m, int64_t d, int64_t ffn, int64_t group_size) {
   if (m < 0 || d <= 0 || ffn <= 0 || group_size <= 0) return 0;
+  const int64_t kp1 = h3::correction_kpad(d / group_size), kp2 = h3::correction_kpad(ffn / group_size);
   return round_up(ffn * d, 256) * 2 + round_up(m * d, 256) * 3 + round_up(m * 4, 256) * 2 +
-         round_up(m * (d / group_size) * 4, 256) + round_up(m * ffn * 2, 256) + round_up(m * ffn, 256) +
-         round_up(m * (ffn / group_size) * 4, 256) + 2048;
+         round_up(m * kp1 * 2, 256) + round_up(ffn * kp1 * 2, 256) + round_up(m * ffn * 2, 256) +
+         round_up(m * ffn, 256) + round_up(m * kp2 * 2, 256) + round_up(d * kp2 * 2, 256) + 4096;
 }
 
 int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1, const float* s_rel1,
@@ -320,16 +326,21 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   if (!x || !qdata1 || !s_rel1 || !s_channel1 || !qdata2 || !s_rel2 || !s_channel2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: NULL pointer");
   const int64_t need = h3b200_fused_gated_mlp_w4a8_workspace_bytes(m, d, ffn, group_size);
   if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: workspace too small (need %lld bytes)", (long long)need);
+  const int64_t ng1 = d / group_size, ng2 = ffn / group_size;
+  const int64_t kp1 = h3::correction_kpad(ng1), kp2 = h3::correction_kpad(ng2);
+  if (kp1 > 128 || kp2 > 128) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_w4a8: at most 128 correction groups are built");
   Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
   int8_t* grid1 = static_cast<int8_t*>(c.take(ffn * d));
   int8_t* grid2 = static_cast<int8_t*>(c.take(d * ffn));
   int8_t* xq = static_cast<int8_t*>(c.take(m * d));
   float* xs = static_cast<float*>(c.take(m * 4));
-  int32_t* gs1 = static_cast<int32_t*>(c.take(m * (d / group_size) * 4));
+  void* sx1 = c.take(m * kp1 * 2);
+  void* ct1 = c.take(ffn * kp1 * 2);
   void* h = c.take(m * ffn * 2);
   int8_t* q2 = static_cast<int8_t*>(c.take(m * ffn));
   float* xs2 = static_cast<float*>(c.take(m * 4));
-  int32_t* gs2 = static_cast<int32_t*>(c.take(m * (ffn / group_size) * 4));
+  void* sx2 = c.take(m * kp2 * 2);
+  void* ct2 = c.take(d * kp2 * 2);
   void* y = c.take(m * d * 2);
   if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: workspace too small");
   cudaStream_t st = S(stream);
@@ -338,7 +349,7 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   e = h3::launch_dequant_int4(qdata2, s_rel2, d, ffn, group_size, grid2, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: decode W2");
   // fc1: ConvRot-quantize x, GEMM, asymmetric correction
-  e = h3::launch_quantize_convrot(x, ldx, m, d, H3B200_ACT_NONE, xq, xs, correction1 ? gs1 : nullptr, group_size, st);
+  e = h3::launch_quantize_convrot(x, ldx, m, d, H3B200_ACT_NONE, xq, xs, correction1 ? sx1 : nullptr, group_size, kp1, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize x");
   h3::GemmArgs g1;
   g1.a = xq; g1.w = grid1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
@@ -347,11 +358,12 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   e = h3::launch_gemm_i8(g1, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1");
   if (correction1) {
-    e = h3::launch_w4a8_correction(gs1, xs, correction1, m, ffn, d / group_size, h, ffn, st);
+    e = h3::launch_correction_transpose(correction1, ng1, ffn, kp1, ct1, st);
+    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx1, ct1, kp1, m, ffn, h, ffn, st);
     if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1 correction");
   }
   // fc2: GELU + ConvRot-quantize h, GEMM, correction, gated residual
-  e = h3::launch_quantize_convrot(h, ffn, m, ffn, H3B200_ACT_GELU_TANH, q2, xs2, correction2 ? gs2 : nullptr, group_size, st);
+  e = h3::launch_quantize_convrot(h, ffn, m, ffn, H3B200_ACT_GELU_TANH, q2, xs2, correction2 ? sx2 : nullptr, group_size, kp2, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize gelu(h)");
   h3::GemmArgs g2;
   g2.a = q2; g2.w = grid2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
@@ -360,7 +372,8 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   e = h3::launch_gemm_i8(g2, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2");
   if (correction2) {
-    e = h3::launch_w4a8_correction(gs2, xs2, correction2, m, d, ffn / group_size, y, d, st);
+    e = h3::launch_correction_transpose(correction2, ng2, d, kp2, ct2, st);
+    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx2, ct2, kp2, m, d, y, d, st);
     if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2 correction");
   }
   e = h3::launch_gated_residual_bf16(y, d, gate, residual, ldr, out, ldo, m, d, st);

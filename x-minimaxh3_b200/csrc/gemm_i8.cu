@@ -13,12 +13,17 @@
 //   warp 1      MMA issuer: 4 x tcgen05.mma.cta_group::1.kind::i8 (128x256x32)
 //               per stage into a TMEM accumulator; tcgen05.commit frees the
 //               stage and, after the last k-block, publishes the accumulator.
+//               (The kEpiAddBF16 variant is a bf16 GEMM: kind::f16, 128x256x16,
+//               the same 128-byte k-block rows and fp32 accumulators.)
 //   warp 2      TMEM allocator (512 columns = two 128x256 s32 accumulators).
 //   warps 4-11  epilogue: tcgen05.ld 32 columns at a time, fused dequant /
 //               activation / gated residual; each warp stages its 32x32 bf16
 //               result in shared memory (64-byte swizzle, conflict-free) and one
 //               lane writes it with a TMA tensor store (int32 results use
-//               128-bit global stores). The two accumulators let the epilogue
+//               128-bit global stores). Epilogues that read a bf16 tensor of
+//               the output's shape (residual, or the output itself for
+//               kEpiAddBF16) TMA-load its 32x32 box into the same staging box
+//               first. The two accumulators let the epilogue
 //               of tile i overlap the mainloop of tile i+1.
 // Tiles are visited n-fastest so that the concurrently running CTAs share the
 // same A rows and the whole weight stays resident in the 126 MB L2.
@@ -40,7 +45,8 @@ constexpr int NUM_THREADS = 384;
 constexpr int EPI_WARP0 = 4;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr uint32_t IDESC = umma_idesc_i8(BM, BN);
+constexpr uint32_t IDESC_I8 = umma_idesc_i8(BM, BN);
+constexpr uint32_t IDESC_BF16 = umma_idesc_bf16(BM, BN);
 constexpr int BAR_BYTES = 256;
 constexpr int STAGE_OPS_BYTES = NUM_EPI_WARPS * 2 * 128 * 4;   // per-warp column scales + bias/gate
 constexpr int GELU_TAB_BYTES = 2 * 19 * 128 * 2;
@@ -54,7 +60,7 @@ static_assert(SMEM_BYTES <= 232448, "GEMM shared memory exceeds the 227 KB per-b
 
 // status codes recorded when a bounded wait expires
 constexpr unsigned kErrProducer = 0x101, kErrMmaAcc = 0x102, kErrMmaFull = 0x103, kErrEpi = 0x104,
-                   kErrDrain = 0x105;
+                   kErrDrain = 0x105, kErrEpiIn = 0x106;
 
 struct KParams {
   int m, n, k;
@@ -152,25 +158,21 @@ __device__ __forceinline__ void store_i32_chunk(const KParams& p, int row, int c
 
 // bf16 results (packed pairs) of one 32-column chunk of one accumulator row.
 // ws_s / aux_s: this warp's staged per-column weight scales and bias-or-gate
-// (fp32) for the chunk.
+// (fp32) for the chunk; in_w: the row's 32 bf16 input values (residual, or the
+// output being accumulated into) for the epilogues that read one.
 template <int EPI>
-__device__ __forceinline__ void epilogue_values(const KParams& p, int row, int col0, const uint32_t (&r)[32],
-                                                float xs, const float* ws_s, const float* aux_s,
-                                                const uint16_t* gtab, uint32_t& amax_bits, uint32_t (&ob)[16]) {
+__device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t (&r)[32], float xs,
+                                                const float* ws_s, const float* aux_s, const uint16_t* gtab,
+                                                uint32_t& amax_bits, const uint32_t (&in_w)[16],
+                                                uint32_t (&ob)[16]) {
   if constexpr (EPI == kEpiGeluAbsmax) {
     gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
-  } else {
-    uint32_t res_w[16];
-    if constexpr (EPI == kEpiGatedResidual) {
-      const bool row_ok = row < p.m;
-      const __nv_bfloat16* rp = p.residual + (int64_t)row * p.ldr + col0;
+  } else if constexpr (EPI == kEpiAddBF16) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 rv = make_uint4(0, 0, 0, 0);
-        if (row_ok && col0 + 8 * q < p.n) rv = ldg_v4(rp + 8 * q);
-        res_w[4 * q] = rv.x; res_w[4 * q + 1] = rv.y; res_w[4 * q + 2] = rv.z; res_w[4 * q + 3] = rv.w;
-      }
-    }
+    for (int j = 0; j < 16; ++j)
+      ob[j] = pack_bf16(__fadd_rn(bf16_lo(in_w[j]), __uint_as_float(r[2 * j])),
+                        __fadd_rn(bf16_hi(in_w[j]), __uint_as_float(r[2 * j + 1])));
+  } else {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
@@ -186,7 +188,7 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, int row, int c
           if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
         }
         if constexpr (EPI == kEpiGatedResidual) {
-          const uint32_t rw = res_w[j >> 1];
+          const uint32_t rw = in_w[j >> 1];
           const float rv = (j & 1) ? bf16_hi(rw) : bf16_lo(rw);
           b = bf16_bits(__fadd_rn(rv, __fmul_rn(__uint_as_float(b << 16), av[e])));
         }
@@ -201,7 +203,10 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, int row, int c
 template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, const KParams p) {
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
+                   const KParams p) {
+  constexpr bool kBF16Mma = EPI == kEpiAddBF16;
+  constexpr bool kInBox = EPI == kEpiGatedResidual || EPI == kEpiAddBF16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -209,7 +214,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* in_bar = drain_bar + 1;  // [NUM_EPI_WARPS]: input-box loads of the epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(in_bar + NUM_EPI_WARPS);
   float* ops_smem = reinterpret_cast<float*>(smem + OFF_OPS);
   uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + OFF_GELU);
 
@@ -226,11 +232,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&tempty_bar[b], NUM_EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
+    for (int w = 0; w < NUM_EPI_WARPS; ++w) mbar_init(&in_bar[w], 1);
     fence_barrier_init();
     fence_proxy_async_shared();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (EPI != kEpiI32) tma_prefetch_desc(&tmO);
+    if (kInBox) tma_prefetch_desc(&tmR);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -295,8 +303,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
-            umma_i8(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC,
-                    (kb > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kBF16Mma)
+              umma_bf16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC_BF16,
+                        (kb > 0 || kk > 0) ? 1u : 0u);
+            else
+              umma_i8(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC_I8,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
           }
           issued = true;
           umma_commit(&empty_bar[s]);
@@ -321,24 +333,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* box_row = box + lane * 64;
     const int box_sw = (lane >> 1) & 3;
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+    uint32_t in_phase = 0;
+    bool in_pending = false;  // an input-box load was issued and not yet waited for
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tcount) {
       const int m_blk = tile / p.num_n_blk;
       const int n_blk = tile - m_blk * p.num_n_blk;
       const int acc = tcount & 1;
       const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
       const int row = m_blk * BM + quarter * 32 + lane;
       const int col_base = n_blk * BN + half * 128;
-      if constexpr (EPI != kEpiI32) {
+      if constexpr (EPI != kEpiI32 && EPI != kEpiAddBF16) {
         // stage this tile's per-column operands while the MMAs run
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int c = lane + 32 * i;
           const int col = col_base + c;
-          const bool ok = col < p.n;
-          ws_s[c] = ok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
+          const bool cok = col < p.n;
+          ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
           float a = 0.0f;
-          if (EPI == kEpiBF16 && p.bias != nullptr && ok) a = __bfloat162float(p.bias[col]);
-          if (EPI == kEpiGatedResidual && ok) a = __bfloat162float(p.gate[col]);
+          if (EPI == kEpiBF16 && p.bias != nullptr && cok) a = __bfloat162float(p.bias[col]);
+          if (EPI == kEpiGatedResidual && cok) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
         }
         __syncwarp();
@@ -346,9 +361,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
       tc_fence_after();
       float xs = 0.0f;
-      if constexpr (EPI != kEpiI32) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
+      if constexpr (EPI != kEpiI32 && EPI != kEpiAddBF16) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
+      const int box_row0 = m_blk * BM + quarter * 32;
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         uint32_t r[32];
@@ -358,9 +374,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if constexpr (EPI == kEpiI32) {
           store_i32_chunk(p, row, col_base + c, r);
         } else {
-          uint32_t ob[16];
-          epilogue_values<EPI>(p, row, col_base + c, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, ob);
+          if (box_row0 >= p.m) continue;      // warp-uniform: no row of this box exists
           if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
+          uint32_t in_w[16];
+          if constexpr (kInBox) {
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&in_bar[ew], EPI_STAGE_BYTES);
+              tma_load_2d(box, &tmR, &in_bar[ew], col_base + c, box_row0);
+            }
+            in_pending = true;
+            if (!mbar_wait(&in_bar[ew], in_phase, kErrEpiIn)) {
+              ok = false;
+              break;
+            }
+            in_pending = false;
+            in_phase ^= 1u;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 v = *reinterpret_cast<const uint4*>(box_row + ((q ^ box_sw) << 4));
+              in_w[4 * q] = v.x; in_w[4 * q + 1] = v.y; in_w[4 * q + 2] = v.z; in_w[4 * q + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) in_w[j] = 0u;
+          }
+          uint32_t ob[16];
+          epilogue_values<EPI>(p, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, in_w, ob);
           __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -368,8 +407,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]);
           fence_proxy_async_shared();
           __syncwarp();
-          const int box_row0 = m_blk * BM + quarter * 32;
-          if (lane == 0 && box_row0 < p.m) {
+          if (lane == 0) {
             tma_store_2d(&tmO, box, col_base + c, box_row0);  // rows >= m and columns >= n are clipped
             bulk_commit_group();
           }
@@ -381,6 +419,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (EPI == kEpiGeluAbsmax) {
         if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, amax_bits << 16);
       }
+    }
+    if constexpr (kInBox) {
+      if (in_pending) mbar_wait(&in_bar[ew], in_phase, kErrDrain, 200000000ull);  // let a late box land
     }
     if constexpr (EPI != kEpiI32) {
       if (lane == 0) bulk_wait_all();  // every output box written before the CTA exits
@@ -405,8 +446,8 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
 }
 
 template <int EPI>
-cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const KParams& kp,
-                       int grid, cudaStream_t stream) {
+cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
+                       const KParams& kp, int grid, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -415,7 +456,7 @@ cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  gemm_i8_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, kp);
+  gemm_i8_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, tr, kp);
   return cudaGetLastError();
 }
 
@@ -464,29 +505,47 @@ int num_sms(int device) {
 
 cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   if (a.m <= 0 || a.n <= 0) return cudaSuccess;
-  if (a.k <= 0 || a.k % 16 != 0 || a.n % 8 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.m > (1ll << 30) ||
-      a.n > (1ll << 30) || a.k > (1ll << 30))
+  const bool bf16_in = a.epilogue == kEpiAddBF16;  // bf16 operands, kind::f16
+  const int64_t esz = bf16_in ? 2 : 1;
+  if (a.k <= 0 || (a.k * esz) % 16 != 0 || a.n % 8 != 0 || (a.lda * esz) % 16 != 0 || (a.ldw * esz) % 16 != 0 ||
+      a.m > (1ll << 30) || a.n > (1ll << 30) || a.k > (1ll << 30))
     return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
       (reinterpret_cast<uintptr_t>(a.out) & 15) || a.ldo % 8 != 0)
     return cudaErrorNotSupported;
   if (a.epilogue == kEpiGatedResidual && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0))
     return cudaErrorNotSupported;
-  CUtensorMap ta, tb, to;
-  if (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN))
+  CUtensorMap ta, tb, to, tr;
+  if (bf16_in) {
+    // 64 bf16 (128 bytes) per k-block row, 128-byte swizzle: the same smem tiles as the int8 path
+    if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.a, (uint64_t)a.k, (uint64_t)a.m,
+                        (uint64_t)a.lda * 2, BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.w, (uint64_t)a.k, (uint64_t)a.n,
+                        (uint64_t)a.ldw * 2, BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  } else if (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN)) {
     return cudaErrorInvalidValue;
+  }
   if (a.epilogue == kEpiI32) {
     to = tb;  // unused: int32 results are stored directly
   } else if (!encode_tmap_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
                              (uint64_t)a.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return cudaErrorInvalidValue;
   }
+  if (a.epilogue == kEpiGatedResidual) {
+    if (!encode_tmap_2d(&tr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.residual, (uint64_t)a.n, (uint64_t)a.m,
+                        (uint64_t)a.ldr * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return cudaErrorInvalidValue;
+  } else {
+    tr = to;  // kEpiAddBF16 reads the output it accumulates into; unused otherwise
+  }
   KParams kp;
   kp.m = (int)a.m;
   kp.n = (int)a.n;
   kp.k = (int)a.k;
   kp.num_n_blk = (int)((a.n + BN - 1) / BN);
-  kp.num_k_blk = (int)((a.k + BK - 1) / BK);
+  const int64_t k_per_blk = BK / esz;
+  kp.num_k_blk = (int)((a.k + k_per_blk - 1) / k_per_blk);
   const int64_t num_m_blk = (a.m + BM - 1) / BM;
   const int64_t tiles = num_m_blk * kp.num_n_blk;
   if (tiles > (1ll << 30)) return cudaErrorNotSupported;
@@ -505,10 +564,11 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const int grid = (int)std::min<int64_t>(tiles, (int64_t)num_sms(dev));
   switch (a.epilogue) {
-    case kEpiI32: return launch_epi<kEpiI32>(ta, tb, to, kp, grid, stream);
-    case kEpiBF16: return launch_epi<kEpiBF16>(ta, tb, to, kp, grid, stream);
-    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, to, kp, grid, stream);
-    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, to, kp, grid, stream);
+    case kEpiI32: return launch_epi<kEpiI32>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiBF16: return launch_epi<kEpiBF16>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiAddBF16: return launch_epi<kEpiAddBF16>(ta, tb, to, tr, kp, grid, stream);
     default: return cudaErrorNotSupported;
   }
 }

@@ -13,12 +13,13 @@ enum GemmEpilogue : int {
   kEpiBF16 = 1,            // bf16(acc * (xs * ws)) (+ bf16 bias)
   kEpiGeluAbsmax = 2,      // a = gelu(bf16(acc * (xs * ws))) stored bf16, row absmax of |a| via atomicMax
   kEpiGatedResidual = 3,   // out = bf16(residual + bf16(acc * (xs * ws)) * gate)
-  kEpiW4A8Correction = 4,  // bf16(bf16(acc * (xs * ws)) + sum_g bf16(gsum*xs) * corr[g, n])
+  kEpiAddBF16 = 4,         // bf16 x bf16 -> fp32 GEMM (kind::f16): out = bf16(out + acc), in place
+                           // (the W4A8 asymmetric correction sx[m, g] . corr[g, n] added to a linear's output)
 };
 
 struct GemmArgs {
-  const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes
-  const int8_t* w = nullptr;  // [n, k] int8, row stride ldw bytes
+  const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes (kEpiAddBF16: bf16, lda elements)
+  const int8_t* w = nullptr;  // [n, k] int8, row stride ldw bytes (kEpiAddBF16: bf16, ldw elements)
   int64_t m = 0, n = 0, k = 0;
   int64_t lda = 0, ldw = 0;
   int epilogue = kEpiBF16;
@@ -66,11 +67,19 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream);
 
 cudaError_t launch_dequant_int4(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k, int64_t group,
                                 int8_t* out, cudaStream_t stream);
+// ConvRot-256 + row quantization; with sx != nullptr also writes the correction
+// operand sx (bf16 [m, kp], zero beyond k / sum_group).
 cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64_t k, int act, int8_t* q,
-                                    float* scale, int32_t* group_sums, int64_t sum_group, cudaStream_t stream);
+                                    float* scale, void* sx, int64_t sum_group, int64_t kp, cudaStream_t stream);
+// corr_t[n, kp] (bf16) = correction[g, n] transposed, zero for g >= groups
+cudaError_t launch_correction_transpose(const void* corr, int64_t groups, int64_t n, int64_t kp, void* corr_t,
+                                        cudaStream_t stream);
+// out[m, n] = bf16(out + sx . corr_t^T) (tcgen05 kind::f16 GEMM, K = kp)
+cudaError_t launch_w4a8_correction(const void* sx, const void* corr_t, int64_t kp, int64_t m, int64_t n, void* out,
+                                   int64_t ldo, cudaStream_t stream);
 
-cudaError_t launch_w4a8_correction(const int32_t* gsum, const float* xs, const void* corr, int64_t m, int64_t n,
-                                   int64_t groups, void* out, int64_t ldo, cudaStream_t stream);
+// K padding of the correction GEMM: groups rounded up to 64 (one 128-byte bf16 k-block)
+inline int64_t correction_kpad(int64_t groups) { return (groups + 63) / 64 * 64; }
 
 int num_sms(int device);
 

@@ -1,6 +1,8 @@
 // W4A8 pieces: int4 -> int8 grid decode, ConvRot-256 rotation + row
-// quantization (with int8 group sums for the asymmetric correction), and the
-// asymmetric group-correction epilogue.
+// quantization (emitting the asymmetric-correction operand
+// sx[m, g] = bf16(bf16(sum_{k in g} q) * bf16(xs))), and the correction itself,
+// out += sx . corr, run as a tcgen05 bf16 GEMM (gemm_i8.cu, kEpiAddBF16) against
+// the transposed, zero-padded correction matrix.
 //
 // Reference: comfy_kitchen W4A8 (backends/eager/w4a8_int8.py:344-363 decode;
 // backends/cuda/ops/w4a8_gemm.cu:36-90; ConvRot quantizer
@@ -77,7 +79,8 @@ template <int GPW>
 __global__ void __launch_bounds__(256) quantize_convrot_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                int64_t m, int64_t k, int act, int8_t* __restrict__ q,
                                                                float* __restrict__ scale,
-                                                               int32_t* __restrict__ gsum, int64_t sum_group) {
+                                                               __nv_bfloat16* __restrict__ sx, int64_t sum_group,
+                                                               int64_t kp) {
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   if (row >= m) return;
@@ -153,79 +156,27 @@ __global__ void __launch_bounds__(256) quantize_convrot_kernel(const __nv_bfloat
       const uint2 qq = quant_vec8(pv, sb, rcp);
       int isum = __dp4a((int)qq.x, 0x01010101, __dp4a((int)qq.y, 0x01010101, 0));  // sum of the 8 int8
       *reinterpret_cast<uint2*>(q + row * k + g * 256 + lane * 8) = qq;
-      if (gsum != nullptr) {
+      if (sx != nullptr) {
         for (int o = 1; o < lanes_per_sum; o <<= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-        if ((lane % lanes_per_sum) == 0) gsum[row * (k / sum_group) + (g * 256 + lane * 8) / sum_group] = isum;
+        if ((lane % lanes_per_sum) == 0)
+          sx[row * kp + (g * 256 + lane * 8) / sum_group] =
+              __float2bfloat16_rn(__fmul_rn(bf16_round((float)isum), bf16_round(s)));
       }
     }
+  }
+  if (sx != nullptr) {  // zero the K padding of the correction operand
+    for (int64_t i = k / sum_group + threadIdx.x; i < kp; i += blockDim.x) sx[row * kp + i] = __float2bfloat16_rn(0.0f);
   }
   if (threadIdx.x == 0) scale[row] = s;
 }
 
-// ---------------------------------------------------------------------------
-// Asymmetric correction: out = bf16(out + sum_g sx[m, g] * corr[g, n]) with
-// sx = bf16(bf16(gsum) * bf16(xs)). CTA tile 64 rows x 128 columns, operands
-// staged in shared memory, fp32 accumulation.
-// ---------------------------------------------------------------------------
-constexpr int kCorrRows = 64, kCorrCols = 128, kCorrMaxG = 128;
-
-__global__ void __launch_bounds__(256) w4a8_correction_kernel(const int32_t* __restrict__ gsum,
-                                                              const float* __restrict__ xs,
-                                                              const __nv_bfloat16* __restrict__ corr, int64_t m,
-                                                              int64_t n, int groups, __nv_bfloat16* __restrict__ out,
-                                                              int64_t ldo) {
-  extern __shared__ float sm[];
-  float* sx = sm;                                   // [kCorrRows][groups + 1]
-  float* cr = sm + kCorrRows * (groups + 1);        // [groups][kCorrCols]
-  const int64_t r0 = (int64_t)blockIdx.y * kCorrRows;
-  const int64_t c0 = (int64_t)blockIdx.x * kCorrCols;
-  for (int i = threadIdx.x; i < kCorrRows * groups; i += blockDim.x) {
-    const int r = i / groups, g = i - r * groups;
-    float v = 0.0f;
-    if (r0 + r < m) {
-      const float gs = bf16_round((float)gsum[(r0 + r) * groups + g]);
-      v = bf16_round(__fmul_rn(gs, bf16_round(xs[r0 + r])));
-    }
-    sx[r * (groups + 1) + g] = v;
-  }
-  for (int i = threadIdx.x; i < groups * kCorrCols; i += blockDim.x) {
-    const int g = i / kCorrCols, c = i - g * kCorrCols;
-    cr[i] = (c0 + c < n) ? __bfloat162float(corr[(int64_t)g * n + c0 + c]) : 0.0f;
-  }
-  __syncthreads();
-  // thread -> 4 rows x 8 columns
-  const int tc = threadIdx.x & 15, tr = threadIdx.x >> 4;
-  float acc[4][8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-  for (int g = 0; g < groups; ++g) {
-    float a[4], b[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) a[i] = sx[(tr * 4 + i) * (groups + 1) + g];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) b[j] = cr[g * kCorrCols + tc * 8 + j];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t r = r0 + tr * 4 + i;
-    const int64_t c = c0 + tc * 8;
-    if (r < m && c < n) {
-      __nv_bfloat16* op = out + r * ldo + c;
-      const uint4 ov = *reinterpret_cast<const uint4*>(op);
-      const uint32_t w[4] = {ov.x, ov.y, ov.z, ov.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        o[e] = pack_bf16(__fadd_rn(bf16_lo(w[e]), acc[i][2 * e]), __fadd_rn(bf16_hi(w[e]), acc[i][2 * e + 1]));
-      *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
+// corrT[n, kp] = correction[g, n] for g < groups, 0 for groups <= g < kp
+__global__ void correction_transpose_kernel(const __nv_bfloat16* __restrict__ corr, int64_t groups, int64_t n,
+                                            int64_t kp, __nv_bfloat16* __restrict__ corr_t) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n * kp) return;
+  const int64_t col = i / kp, g = i - col * kp;
+  corr_t[i] = g < groups ? corr[g * n + col] : __float2bfloat16_rn(0.0f);
 }
 
 }  // namespace
@@ -246,11 +197,12 @@ cudaError_t launch_dequant_int4(const int8_t* qdata, const float* s_rel, int64_t
 }
 
 cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64_t k, int act, int8_t* q,
-                                    float* scale, int32_t* group_sums, int64_t sum_group, cudaStream_t stream) {
+                                    float* scale, void* sx, int64_t sum_group, int64_t kp, cudaStream_t stream) {
   if (m == 0) return cudaSuccess;
   if (k % 256 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 7))
     return cudaErrorNotSupported;
-  if (group_sums != nullptr && (sum_group < 8 || sum_group > 256 || 256 % sum_group)) return cudaErrorNotSupported;
+  if (sx != nullptr && (sum_group < 8 || sum_group > 256 || 256 % sum_group || kp < k / sum_group))
+    return cudaErrorNotSupported;
   if (act == H3B200_ACT_GELU_TANH) {
     const cudaError_t e = ensure_gelu_table(stream);
     if (e != cudaSuccess) return e;
@@ -258,31 +210,36 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
   const int64_t ng = k / 256;
   const int64_t gpw = (ng + 7) / 8;
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
   dim3 grid((unsigned)m);
-  if (gpw <= 1) quantize_convrot_kernel<1><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, group_sums, sum_group);
-  else if (gpw <= 2) quantize_convrot_kernel<2><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, group_sums, sum_group);
-  else if (gpw <= 4) quantize_convrot_kernel<4><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, group_sums, sum_group);
-  else if (gpw <= 6) quantize_convrot_kernel<6><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, group_sums, sum_group);
-  else if (gpw <= 8) quantize_convrot_kernel<8><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, group_sums, sum_group);
+  if (gpw <= 1) quantize_convrot_kernel<1><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp);
+  else if (gpw <= 2) quantize_convrot_kernel<2><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp);
+  else if (gpw <= 4) quantize_convrot_kernel<4><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp);
+  else if (gpw <= 6) quantize_convrot_kernel<6><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp);
+  else if (gpw <= 8) quantize_convrot_kernel<8><<<grid, 256, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp);
   else return cudaErrorNotSupported;
   return cudaGetLastError();
 }
 
-cudaError_t launch_w4a8_correction(const int32_t* gsum, const float* xs, const void* corr, int64_t m, int64_t n,
-                                   int64_t groups, void* out, int64_t ldo, cudaStream_t stream) {
-  if (m == 0 || n == 0) return cudaSuccess;
-  if (groups <= 0 || groups > kCorrMaxG || n % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(out) & 15))
-    return cudaErrorNotSupported;
-  const size_t smem = sizeof(float) * ((size_t)kCorrRows * (groups + 1) + (size_t)groups * kCorrCols);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(w4a8_correction_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-    attr = true;
-  }
-  dim3 grid((unsigned)((n + kCorrCols - 1) / kCorrCols), (unsigned)((m + kCorrRows - 1) / kCorrRows));
-  w4a8_correction_kernel<<<grid, 256, smem, stream>>>(gsum, xs, static_cast<const __nv_bfloat16*>(corr), m, n,
-                                                       (int)groups, static_cast<__nv_bfloat16*>(out), ldo);
+cudaError_t launch_correction_transpose(const void* corr, int64_t groups, int64_t n, int64_t kp, void* corr_t,
+                                        cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  if (groups <= 0 || kp < groups) return cudaErrorNotSupported;
+  const int64_t total = n * kp;
+  correction_transpose_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(corr), groups, n, kp, static_cast<__nv_bfloat16*>(corr_t));
   return cudaGetLastError();
+}
+
+cudaError_t launch_w4a8_correction(const void* sx, const void* corr_t, int64_t kp, int64_t m, int64_t n, void* out,
+                                   int64_t ldo, cudaStream_t stream) {
+  GemmArgs g;
+  g.a = static_cast<const int8_t*>(sx);
+  g.w = static_cast<const int8_t*>(corr_t);
+  g.m = m; g.n = n; g.k = kp; g.lda = kp; g.ldw = kp;
+  g.epilogue = kEpiAddBF16;
+  g.out = out; g.ldo = ldo;
+  return launch_gemm_i8(g, stream);
 }
 
 }  // namespace h3

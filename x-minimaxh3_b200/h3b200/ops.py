@@ -516,7 +516,7 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     x2, ldx = _rows(x)
     m = x2.shape[0]
     out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
-    nbytes = int(_lib.load().h3b200_w4a8_linear_workspace_bytes(m, k, group_size))
+    nbytes = int(_lib.load().h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size))
     work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
     _lib.call("h3b200_w4a8_int8_linear", x2.data_ptr(), ldx, grid.contiguous().data_ptr(), sch.data_ptr(), _ptr(corr),
               group_size, convrot_groupsize, input_act_code(input_act), out.data_ptr(), m, n, k, work.data_ptr(),
