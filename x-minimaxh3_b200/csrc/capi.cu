@@ -297,7 +297,7 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
   if (correction != nullptr) {
     e = h3::launch_correction_transpose(correction, groups, n, kp, corr_t, st);
     if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction layout");
-    e = h3::launch_w4a8_correction(sx, corr_t, kp, m, n, out, n, st);
+    e = h3::launch_w4a8_correction(sx, corr_t, kp, m, n, out, n, false, st);
     if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction");
   }
   return H3B200_OK;
@@ -359,11 +359,13 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1");
   if (correction1) {
     e = h3::launch_correction_transpose(correction1, ng1, ffn, kp1, ct1, st);
-    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx1, ct1, kp1, m, ffn, h, ffn, st);
+    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx1, ct1, kp1, m, ffn, h, ffn, true, st);  // + GELU
     if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1 correction");
   }
-  // fc2: GELU + ConvRot-quantize h, GEMM, correction, gated residual
-  e = h3::launch_quantize_convrot(h, ffn, m, ffn, H3B200_ACT_GELU_TANH, q2, xs2, correction2 ? sx2 : nullptr, group_size, kp2, st);
+  // fc2: ConvRot-quantize gelu(h), GEMM, correction, gated residual
+  // gelu(h) was applied by the fc1 correction epilogue; without a correction the quantizer applies it
+  e = h3::launch_quantize_convrot(h, ffn, m, ffn, correction1 ? H3B200_ACT_NONE : H3B200_ACT_GELU_TANH, q2, xs2,
+                                  correction2 ? sx2 : nullptr, group_size, kp2, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize gelu(h)");
   h3::GemmArgs g2;
   g2.a = q2; g2.w = grid2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
@@ -373,7 +375,7 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2");
   if (correction2) {
     e = h3::launch_correction_transpose(correction2, ng2, d, kp2, ct2, st);
-    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx2, ct2, kp2, m, d, y, d, st);
+    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx2, ct2, kp2, m, d, y, d, false, st);
     if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2 correction");
   }
   e = h3::launch_gated_residual_bf16(y, d, gate, residual, ldr, out, ldo, m, d, st);

@@ -167,11 +167,24 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
                                                 uint32_t (&ob)[16]) {
   if constexpr (EPI == kEpiGeluAbsmax) {
     gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
-  } else if constexpr (EPI == kEpiAddBF16) {
+  } else if constexpr (EPI == kEpiAddBF16 || EPI == kEpiAddBF16Gelu) {
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       ob[j] = pack_bf16(__fadd_rn(bf16_lo(in_w[j]), __uint_as_float(r[2 * j])),
                         __fadd_rn(bf16_hi(in_w[j]), __uint_as_float(r[2 * j + 1])));
+    if constexpr (EPI == kEpiAddBF16Gelu) {
+      bool miss = false;
+      uint32_t g[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        g[j] = gelu_lookup_fast(ob[j] & 0xFFFFu, gtab, miss) | (gelu_lookup_fast(ob[j] >> 16, gtab, miss) << 16);
+      if (miss) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) g[j] = gelu_lookup(ob[j] & 0xFFFFu, gtab) | (gelu_lookup(ob[j] >> 16, gtab) << 16);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) ob[j] = g[j];
+    }
   } else {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -205,8 +218,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const KParams p) {
-  constexpr bool kBF16Mma = EPI == kEpiAddBF16;
-  constexpr bool kInBox = EPI == kEpiGatedResidual || EPI == kEpiAddBF16;
+  constexpr bool kBF16Mma = EPI == kEpiAddBF16 || EPI == kEpiAddBF16Gelu;
+  constexpr bool kInBox = EPI == kEpiGatedResidual || kBF16Mma;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -244,7 +257,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
-  if constexpr (EPI == kEpiGeluAbsmax) {
+  if constexpr (EPI == kEpiGeluAbsmax || EPI == kEpiAddBF16Gelu) {
     for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
       gelu_tab[i] = (uint16_t)bf16_bits(gelu_tanh_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
   }
@@ -343,7 +356,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
       const int row = m_blk * BM + quarter * 32 + lane;
       const int col_base = n_blk * BN + half * 128;
-      if constexpr (EPI != kEpiI32 && EPI != kEpiAddBF16) {
+      if constexpr (EPI != kEpiI32 && !kBF16Mma) {
         // stage this tile's per-column operands while the MMAs run
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -361,7 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
       tc_fence_after();
       float xs = 0.0f;
-      if constexpr (EPI != kEpiI32 && EPI != kEpiAddBF16) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
+      if constexpr (EPI != kEpiI32 && !kBF16Mma) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
       const int box_row0 = m_blk * BM + quarter * 32;
@@ -505,7 +518,7 @@ int num_sms(int device) {
 
 cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   if (a.m <= 0 || a.n <= 0) return cudaSuccess;
-  const bool bf16_in = a.epilogue == kEpiAddBF16;  // bf16 operands, kind::f16
+  const bool bf16_in = a.epilogue == kEpiAddBF16 || a.epilogue == kEpiAddBF16Gelu;  // bf16 operands, kind::f16
   const int64_t esz = bf16_in ? 2 : 1;
   if (a.k <= 0 || (a.k * esz) % 16 != 0 || a.n % 8 != 0 || (a.lda * esz) % 16 != 0 || (a.ldw * esz) % 16 != 0 ||
       a.m > (1ll << 30) || a.n > (1ll << 30) || a.k > (1ll << 30))
@@ -569,6 +582,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
     case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, to, tr, kp, grid, stream);
     case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, to, tr, kp, grid, stream);
     case kEpiAddBF16: return launch_epi<kEpiAddBF16>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiAddBF16Gelu: return launch_epi<kEpiAddBF16Gelu>(ta, tb, to, tr, kp, grid, stream);
     default: return cudaErrorNotSupported;
   }
 }

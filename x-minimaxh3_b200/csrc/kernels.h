@@ -15,6 +15,7 @@ enum GemmEpilogue : int {
   kEpiGatedResidual = 3,   // out = bf16(residual + bf16(acc * (xs * ws)) * gate)
   kEpiAddBF16 = 4,         // bf16 x bf16 -> fp32 GEMM (kind::f16): out = bf16(out + acc), in place
                            // (the W4A8 asymmetric correction sx[m, g] . corr[g, n] added to a linear's output)
+  kEpiAddBF16Gelu = 5,     // as kEpiAddBF16, then out = tanh-GELU(out) (exact bf16)
 };
 
 struct GemmArgs {
@@ -74,9 +75,9 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
 // corr_t[n, kp] (bf16) = correction[g, n] transposed, zero for g >= groups
 cudaError_t launch_correction_transpose(const void* corr, int64_t groups, int64_t n, int64_t kp, void* corr_t,
                                         cudaStream_t stream);
-// out[m, n] = bf16(out + sx . corr_t^T) (tcgen05 kind::f16 GEMM, K = kp)
+// out[m, n] = bf16(out + sx . corr_t^T) (tcgen05 kind::f16 GEMM, K = kp), then gelu(out) when `gelu`
 cudaError_t launch_w4a8_correction(const void* sx, const void* corr_t, int64_t kp, int64_t m, int64_t n, void* out,
-                                   int64_t ldo, cudaStream_t stream);
+                                   int64_t ldo, bool gelu, cudaStream_t stream);
 
 // K padding of the correction GEMM: groups rounded up to 64 (one 128-byte bf16 k-block)
 inline int64_t correction_kpad(int64_t groups) { return (groups + 63) / 64 * 64; }
