@@ -15,8 +15,10 @@ def rand_i8(shape, gen):
     return torch.randint(-128, 128, shape, generator=gen, dtype=torch.int16).to(torch.int8)
 
 
+# (300, 12288, 3072) and (1000, 12288, 2064) have enough 256 x 256 tiles to run on
+# CTA pairs (cta_group::2); the others run on single CTAs
 @pytest.mark.parametrize("m,n,k", [(1, 256, 128), (128, 256, 128), (130, 264, 48), (257, 512, 3072),
-                                   (1000, 1024, 12288), (37, 8, 16), (300, 12288, 3072)])
+                                   (1000, 1024, 12288), (37, 8, 16), (300, 12288, 3072), (1000, 12288, 2064)])
 def test_mm_int8_exact(m, n, k):
     gen = torch.Generator().manual_seed(m + 3 * n + 7 * k)
     a = rand_i8((m, k), gen)

@@ -46,6 +46,7 @@ constexpr int EPI_WARP0 = 4;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint32_t IDESC_I8 = umma_idesc_i8(BM, BN);
+constexpr uint32_t IDESC_I8_PAIR = umma_idesc_i8(2 * BM, BN);  // cta_group::2: 256 x 256 per CTA pair
 constexpr uint32_t IDESC_BF16 = umma_idesc_bf16(BM, BN);
 constexpr int BAR_BYTES = 256;
 constexpr int STAGE_OPS_BYTES = NUM_EPI_WARPS * 2 * 128 * 4;   // per-warp column scales + bias/gate
@@ -213,18 +214,35 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
   }
 }
 
-template <int EPI>
+// CG = 1: one CTA per tile of 128 x 256. CG = 2: a cluster of two CTAs on an SM
+// pair computes a 256 x 256 tile with tcgen05.mma.cta_group::2 issued by the
+// rank-0 CTA: rank r loads A rows [128 r, 128 r + 128) and W rows
+// [128 r, 128 r + 128) of the tile into its own shared memory (32 KB per
+// k-block instead of 48, 6 stages), both CTAs' loads complete on rank 0's
+// full barrier, each commit of rank 0 arrives on the barriers of both CTAs, and
+// rank r's TMEM receives output rows [128 r, 128 r + 128) of the tile. Both
+// epilogues release an accumulator on rank 0's barrier.
+template <int EPI, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const KParams p) {
   constexpr bool kBF16Mma = EPI == kEpiAddBF16 || EPI == kEpiAddBF16Gelu;
   constexpr bool kInBox = EPI == kEpiGatedResidual || kBF16Mma;
+  static_assert(CG == 1 || (CG == 2 && !kBF16Mma), "CTA pairs run the int8 MMA only");
+  constexpr int kStages = CG == 2 ? 6 : STAGES;
+  constexpr int kBBytes = B_BYTES / CG;
+  constexpr int kStageBytes = A_BYTES + kBBytes;
+  static_assert(kStages * kStageBytes <= OFF_BAR, "stage ring overflows its region");
+  constexpr int kTileRows = BM * CG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int cid = (int)blockIdx.x / CG;      // tile walker (cluster) index
+  const int ncl = (int)gridDim.x / CG;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint64_t* in_bar = drain_bar + 1;  // [NUM_EPI_WARPS]: input-box loads of the epilogue warps
@@ -236,13 +254,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
 
   if (warp == 0 && lane == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], NUM_EPI_WARPS);
+      mbar_init(&tempty_bar[b], NUM_EPI_WARPS * CG);  // CG = 2: both CTAs' epilogue warps
     }
     mbar_init(drain_bar, 1);
     for (int w = 0; w < NUM_EPI_WARPS; ++w) mbar_init(&in_bar[w], 1);
@@ -254,8 +272,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (kInBox) tma_prefetch_desc(&tmR);
   }
   if (warp == 2) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);  // collective with the peer CTA's warp 2
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if constexpr (EPI == kEpiGeluAbsmax || EPI == kEpiAddBF16Gelu) {
     for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
@@ -263,6 +286,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -271,66 +295,100 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // ---------------- TMA producer ----------------
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = cid; tile < p.num_tiles && ok; tile += ncl) {
         const int m_blk = tile / p.num_n_blk;
         const int n_blk = tile - m_blk * p.num_n_blk;
+        const int a_row = m_blk * kTileRows + (int)rank * BM;
+        const int b_row = n_blk * BN + (int)rank * (BN / CG);
         for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          const int s = it % kStages;
+          const uint32_t ph = (uint32_t)(it / kStages) & 1u;
           if (!mbar_wait(&empty_bar[s], ph ^ 1u, kErrProducer)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, m_blk * BM);
-          tma_load_2d(sa + A_BYTES, &tmB, &full_bar[s], kb * BK, n_blk * BN);
+          uint8_t* sa = smem + s * kStageBytes;
+          if constexpr (CG == 2) {
+            if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kStageBytes);  // both CTAs' bytes
+            const uint32_t bar0 = mapa_shared(&full_bar[s], 0);
+            tma_load_2d_pair(sa, &tmA, bar0, kb * BK, a_row);
+            tma_load_2d_pair(sa + A_BYTES, &tmB, bar0, kb * BK, b_row);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+            tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, a_row);
+            tma_load_2d(sa + A_BYTES, &tmB, &full_bar[s], kb * BK, b_row);
+          }
         }
       }
-      // Let every copy this thread issued land before the CTA can exit.
-      for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
-        mbar_wait(&full_bar[j % STAGES], (uint32_t)(j / STAGES) & 1u, kErrDrain, 200000000ull);
+      // Let every copy this thread issued land before the CTA can exit: its
+      // full barrier (CG = 1), or the release of the stage by the MMA that read
+      // it (CG = 2: the full barrier is rank 0's).
+      for (int j = (it > kStages ? it - kStages : 0); j < it; ++j) {
+        if constexpr (CG == 2)
+          mbar_wait(&empty_bar[j % kStages], (uint32_t)(j / kStages) & 1u, kErrDrain, 200000000ull);
+        else
+          mbar_wait(&full_bar[j % kStages], (uint32_t)(j / kStages) & 1u, kErrDrain, 200000000ull);
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (rank 0 of a pair) ----------------
       int it = 0;
       int tcount = 0;
       bool ok = true;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tcount) {
+      for (int tile = cid; tile < p.num_tiles && ok; tile += ncl, ++tcount) {
         const int acc = tcount & 1;
         const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
         if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, kErrMmaAcc)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          const int s = it % kStages;
+          const uint32_t ph = (uint32_t)(it / kStages) & 1u;
           if (!mbar_wait(&full_bar[s], ph, kErrMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t a_addr = smem_u32(smem + s * kStageBytes);
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
-            if constexpr (kBF16Mma)
+            const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (CG == 2)
+              umma_i8_pair(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                           IDESC_I8_PAIR, accum);
+            else if constexpr (kBF16Mma)
               umma_bf16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC_BF16,
-                        (kb > 0 || kk > 0) ? 1u : 0u);
+                        accum);
             else
               umma_i8(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC_I8,
-                      (kb > 0 || kk > 0) ? 1u : 0u);
+                      accum);
           }
           issued = true;
-          umma_commit(&empty_bar[s]);
+          if constexpr (CG == 2) {  // the stage is free in both CTAs
+            umma_commit_pair(mapa_shared(&empty_bar[s], 0));
+            umma_commit_pair(mapa_shared(&empty_bar[s], 1));
+          } else {
+            umma_commit(&empty_bar[s]);
+          }
         }
-        if (ok) umma_commit(&tfull_bar[acc]);
+        if (ok) {
+          if constexpr (CG == 2) {  // accumulator ready in both CTAs
+            umma_commit_pair(mapa_shared(&tfull_bar[acc], 0));
+            umma_commit_pair(mapa_shared(&tfull_bar[acc], 1));
+          } else {
+            umma_commit(&tfull_bar[acc]);
+          }
+        }
       }
       if (issued) {
         // All MMAs this thread issued complete before TMEM can be released.
-        umma_commit(drain_bar);
+        if constexpr (CG == 2)
+          umma_commit_pair(mapa_shared(drain_bar, 0));
+        else
+          umma_commit(drain_bar);
         mbar_wait(drain_bar, 0u, kErrDrain, 200000000ull);
       }
     }
@@ -349,12 +407,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t in_phase = 0;
     bool in_pending = false;  // an input-box load was issued and not yet waited for
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++tcount) {
+    for (int tile = cid; tile < p.num_tiles && ok; tile += ncl, ++tcount) {
       const int m_blk = tile / p.num_n_blk;
       const int n_blk = tile - m_blk * p.num_n_blk;
       const int acc = tcount & 1;
       const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
-      const int row = m_blk * BM + quarter * 32 + lane;
+      const int row0 = m_blk * kTileRows + (int)rank * BM;  // this CTA's first row of the tile
+      const int row = row0 + quarter * 32 + lane;
       const int col_base = n_blk * BN + half * 128;
       if constexpr (EPI != kEpiI32 && !kBF16Mma) {
         // stage this tile's per-column operands while the MMAs run
@@ -377,7 +436,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (EPI != kEpiI32 && !kBF16Mma) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
-      const int box_row0 = m_blk * BM + quarter * 32;
+      const int box_row0 = row0 + quarter * 32;
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         uint32_t r[32];
@@ -428,7 +487,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {  // release the accumulator on the MMA issuer's barrier
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(mapa_shared(&tempty_bar[acc], 0));
+        else
+          mbar_arrive(&tempty_bar[acc]);
+      }
       if constexpr (EPI == kEpiGeluAbsmax) {
         if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, amax_bits << 16);
       }
@@ -444,9 +508,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync_all();  // the pair's MMAs, remote arrivals and epilogues are all done
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -458,19 +526,49 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
                         (uint32_t)BK, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int EPI>
+template <int EPI, int CG>
 cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
                        const KParams& kp, int grid, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_i8_kernel<EPI, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  gemm_i8_kernel<EPI><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, tr, kp);
-  return cudaGetLastError();
+  if constexpr (CG == 1) {
+    gemm_i8_kernel<EPI, 1><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, tr, kp);
+    return cudaGetLastError();
+  } else {
+    // a persistent grid must be fully resident: clamp to the clusters of two
+    // 227 KB CTAs the device can co-schedule
+    static int max_clusters[64] = {0};
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (dev >= 0 && dev < 64 && max_clusters[dev] == 0) {
+      cfg.gridDim = dim3((unsigned)grid, 1, 1);
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, gemm_i8_kernel<EPI, 2>, &cfg);
+      if (e != cudaSuccess) return e;
+      if (n < 1) return cudaErrorNotSupported;
+      max_clusters[dev] = n;
+    }
+    if (dev >= 0 && dev < 64 && grid > 2 * max_clusters[dev]) grid = 2 * max_clusters[dev];
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<EPI, 2>, ta, tb, to, tr, kp);
+  }
 }
 
 }  // namespace
@@ -536,9 +634,17 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
         !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.w, (uint64_t)a.k, (uint64_t)a.n,
                         (uint64_t)a.ldw * 2, BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
-  } else if (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN)) {
-    return cudaErrorInvalidValue;
   }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = num_sms(dev);
+  // CTA pairs (256 x 256 tiles, cta_group::2) for the int8 GEMMs with enough
+  // tiles to give every SM pair work; single CTAs otherwise.
+  const int64_t n_blk = (a.n + BN - 1) / BN;
+  const bool pair = !bf16_in && ((a.m + 2 * BM - 1) / (2 * BM)) * n_blk >= sms / 2;
+  const int cg = pair ? 2 : 1;
+  if (!bf16_in && (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN / cg)))
+    return cudaErrorInvalidValue;
   if (a.epilogue == kEpiI32) {
     to = tb;  // unused: int32 results are stored directly
   } else if (!encode_tmap_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
@@ -556,10 +662,10 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.m = (int)a.m;
   kp.n = (int)a.n;
   kp.k = (int)a.k;
-  kp.num_n_blk = (int)((a.n + BN - 1) / BN);
+  kp.num_n_blk = (int)n_blk;
   const int64_t k_per_blk = BK / esz;
   kp.num_k_blk = (int)((a.k + k_per_blk - 1) / k_per_blk);
-  const int64_t num_m_blk = (a.m + BM - 1) / BM;
+  const int64_t num_m_blk = (a.m + cg * BM - 1) / (cg * BM);
   const int64_t tiles = num_m_blk * kp.num_n_blk;
   if (tiles > (1ll << 30)) return cudaErrorNotSupported;
   kp.num_tiles = (int)tiles;
@@ -573,16 +679,24 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.out = a.out;
   kp.ldo = a.ldo;
   kp.row_absmax = a.row_absmax;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int grid = (int)std::min<int64_t>(tiles, (int64_t)num_sms(dev));
+  if (pair) {
+    const int grid = 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2));
+    switch (a.epilogue) {
+      case kEpiI32: return launch_epi<kEpiI32, 2>(ta, tb, to, tr, kp, grid, stream);
+      case kEpiBF16: return launch_epi<kEpiBF16, 2>(ta, tb, to, tr, kp, grid, stream);
+      case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, 2>(ta, tb, to, tr, kp, grid, stream);
+      case kEpiGatedResidual: return launch_epi<kEpiGatedResidual, 2>(ta, tb, to, tr, kp, grid, stream);
+      default: return cudaErrorNotSupported;
+    }
+  }
+  const int grid = (int)std::min<int64_t>(tiles, (int64_t)sms);
   switch (a.epilogue) {
-    case kEpiI32: return launch_epi<kEpiI32>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiBF16: return launch_epi<kEpiBF16>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiAddBF16: return launch_epi<kEpiAddBF16>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiAddBF16Gelu: return launch_epi<kEpiAddBF16Gelu>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiI32: return launch_epi<kEpiI32, 1>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiBF16: return launch_epi<kEpiBF16, 1>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, 1>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual, 1>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiAddBF16: return launch_epi<kEpiAddBF16, 1>(ta, tb, to, tr, kp, grid, stream);
+    case kEpiAddBF16Gelu: return launch_epi<kEpiAddBF16Gelu, 1>(ta, tb, to, tr, kp, grid, stream);
     default: return cudaErrorNotSupported;
   }
 }

@@ -62,7 +62,8 @@ __global__ void dequant_int4_scalar_kernel(const uint8_t* __restrict__ qd, const
 // ConvRot-256 + row quantization. One CTA per row; each half-warp rotates one
 // 256-group, lane li holding elements 16 li .. 16 li + 15. The regular Hadamard
 // H4^(x)4 acts on the four base-4 digits of the in-group index independently
-// (y_j = S - 2 v_(3-j), S the sum of the four values on that digit's axis):
+// (y_j = S - 2 v_(3-j), S the sum of the four values on that digit's axis;
+// S - 2 v is one fused multiply-add, exact in its product since 2 v is):
 // digits 0-1 are lane-local; a transpose through shared memory (each lane then
 // holds indices li + 16 e) makes digits 2-3 lane-local. The sums are formed in
 // the fixed order (v0 + v1) + (v2 + v3); the 1/16 normalisation is exact. The
@@ -79,8 +80,8 @@ __device__ __forceinline__ void h4_digit_lo(float (&v)[16]) {  // digit over ind
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
     const float s = __fadd_rn(__fadd_rn(v[4 * a], v[4 * a + 1]), __fadd_rn(v[4 * a + 2], v[4 * a + 3]));
-    const float t0 = __fsub_rn(s, 2.0f * v[4 * a + 3]), t1 = __fsub_rn(s, 2.0f * v[4 * a + 2]);
-    const float t2 = __fsub_rn(s, 2.0f * v[4 * a + 1]), t3 = __fsub_rn(s, 2.0f * v[4 * a]);
+    const float t0 = __fmaf_rn(-2.0f, v[4 * a + 3], s), t1 = __fmaf_rn(-2.0f, v[4 * a + 2], s);
+    const float t2 = __fmaf_rn(-2.0f, v[4 * a + 1], s), t3 = __fmaf_rn(-2.0f, v[4 * a], s);
     v[4 * a] = t0; v[4 * a + 1] = t1; v[4 * a + 2] = t2; v[4 * a + 3] = t3;
   }
 }
@@ -88,8 +89,8 @@ __device__ __forceinline__ void h4_digit_hi(float (&v)[16]) {  // digit over ind
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     const float s = __fadd_rn(__fadd_rn(v[b], v[4 + b]), __fadd_rn(v[8 + b], v[12 + b]));
-    const float t0 = __fsub_rn(s, 2.0f * v[12 + b]), t1 = __fsub_rn(s, 2.0f * v[8 + b]);
-    const float t2 = __fsub_rn(s, 2.0f * v[4 + b]), t3 = __fsub_rn(s, 2.0f * v[b]);
+    const float t0 = __fmaf_rn(-2.0f, v[12 + b], s), t1 = __fmaf_rn(-2.0f, v[8 + b], s);
+    const float t2 = __fmaf_rn(-2.0f, v[4 + b], s), t3 = __fmaf_rn(-2.0f, v[b], s);
     v[b] = t0; v[4 + b] = t1; v[8 + b] = t2; v[12 + b] = t3;
   }
 }
