@@ -45,8 +45,11 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
 }
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// two floats -> bf16x2 (lo in the low half), each rounded to nearest even: one cvt
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  return (uint32_t)bf16_bits(lo) | ((uint32_t)bf16_bits(hi) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // ---------------------------------------------------------------------------

@@ -21,8 +21,7 @@
 // two bf16 values is exact, and the fp32 sum of two bf16 values rounds to the
 // same bf16 value as the exact sum).
 // RoPE: y0 = t00*x0 + t01*x1, y1 = t10*x0 + t11*x1 (fp32, two products and one
-// add, no fusion: scalar __fmul_rn / __fadd_rn), bf16 store; table fp32
-// [m, rot_dim/2, 2, 2].
+// add, no fusion), bf16 store; table fp32 [m, rot_dim/2, 2, 2].
 //
 // B200 design: a persistent CTA per SM streams tokens through a shared-memory
 // ring with asynchronous copies (no multicast): one producer thread loads a
@@ -38,11 +37,13 @@
 // coefficients are read once per token and its rotation partner (vector
 // v +- rot_dim/16 of the same head) is one shuffle away. Per-column weights,
 // bf16(1 + scale) and shift are staged in shared memory once per CTA. The
-// normalisation products use the packed f32x2 multiply of sm_100 (two IEEE
-// round-to-nearest products per instruction). The RoPE sums stay scalar: a
-// packed multiply followed by a packed add was measured to round like a fused
-// multiply-add (last-bit differences in about 1 of 10^5 outputs), even with
-// contraction disabled.
+// normalisation and RoPE products use the packed f32x2 multiply of sm_100
+// (two IEEE round-to-nearest products per instruction). The RoPE sums stay
+// scalar: a packed multiply followed by a packed add was measured to round like
+// a fused multiply-add (last-bit differences in about 1 of 10^5 outputs), even
+// with contraction disabled. Row weights are staged as fp32 pairs, and the
+// 24-head (3072-wide) case is a separate instantiation without per-vector
+// predicates.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -155,19 +156,20 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
       : "memory");
 }
 
-template <int VPL, bool ROW_SPAN, bool MODULATE, bool FULL_ROT>
+// EXACT: heads * 16 == 32 * VPL, every lane's VPL vectors exist (no predicates).
+template <int VPL, bool ROW_SPAN, bool MODULATE, bool FULL_ROT, bool EXACT>
 __global__ void __launch_bounds__(kNRThreads, 1)
     adaln_rms_rope_kernel(const __grid_constant__ CUtensorMap tm_table, const NRParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int nvec = p.heads * 16;
+  const int nvec = EXACT ? 32 * VPL : p.heads * 16;
   const int S = p.stages;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty_bar = full_bar + kMaxStages;
-  uint4* cst = reinterpret_cast<uint4*>(smem + 256);
-  // ROW_SPAN: per-vector weights of Q (cst[0, nvec)) and K (cst[nvec, 2 nvec))
-  uint4* m_s = cst + (ROW_SPAN ? 2 : 0) * nvec;                // MODULATE: bf16(1 + scale)
-  uint4* sh_s = m_s + nvec;                                    // MODULATE: shift
+  // ROW_SPAN: fp32 weights of Q (wf[0, nvec)) and K (wf[nvec, 2 nvec)), 8 per vector
+  float4* wf = reinterpret_cast<float4*>(smem + 256);
+  uint4* m_s = reinterpret_cast<uint4*>(wf + (ROW_SPAN ? 4 : 0) * nvec);  // MODULATE: bf16(1 + scale)
+  uint4* sh_s = m_s + nvec;                                                 // MODULATE: shift
   uint8_t* ring = smem + p.ring_off;
   const int stage_bytes = p.stage_bytes;
 
@@ -186,8 +188,12 @@ __global__ void __launch_bounds__(kNRThreads, 1)
   }
   for (int i = threadIdx.x; i < nvec; i += kNRThreads) {
     if (ROW_SPAN) {
-      cst[i] = ldg_nc_v4(p.w[0] + 8 * i);
-      cst[nvec + i] = ldg_nc_v4(p.w[1] + 8 * i);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const uint4 w = ldg_nc_v4(p.w[t] + 8 * i);
+        wf[(t * nvec + i) * 2] = make_float4(bf16_lo(w.x), bf16_hi(w.x), bf16_lo(w.y), bf16_hi(w.y));
+        wf[(t * nvec + i) * 2 + 1] = make_float4(bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w));
+      }
     }
     if (MODULATE) {
       const uint4 sc = ldg_nc_v4(p.scale + 8 * i);
@@ -234,7 +240,7 @@ __global__ void __launch_bounds__(kNRThreads, 1)
   const int partner = (lane & 16) | (role == 0 ? hv + half_v : (role == 1 ? hv - half_v : hv));
   const int pair0 = 8 * (role == 0 ? hv : (role == 1 ? hv - half_v : 0));
 
-  const uint4* w_row = cst + t * nvec;
+  const float4* w_row = wf + 2 * t * nvec;
   uint4 whead = make_uint4(0, 0, 0, 0);
   if (!ROW_SPAN) whead = ldg_nc_v4(p.w[t] + 8 * hv);
   __nv_bfloat16* const ybase = p.y[t];
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(kNRThreads, 1)
 #pragma unroll
       for (int jj = 0; jj < VPL; ++jj) {
         const int vi = lane + 32 * jj;
-        sumsq8_fast(vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0), acc);
+        sumsq8_fast((EXACT || vi < nvec) ? xs[vi] : make_uint4(0, 0, 0, 0), acc);
       }
       double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
@@ -283,7 +289,7 @@ __global__ void __launch_bounds__(kNRThreads, 1)
 #pragma unroll 1
         for (int jj = 0; jj < VPL; ++jj) {
           const int vi = lane + 32 * jj;
-          sumsq8_exact(vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0), ex);
+          sumsq8_exact((EXACT || vi < nvec) ? xs[vi] : make_uint4(0, 0, 0, 0), ex);
         }
         double se = (ex[0] + ex[1]) + (ex[2] + ex[3]);
 #pragma unroll
@@ -295,7 +301,7 @@ __global__ void __launch_bounds__(kNRThreads, 1)
 #pragma unroll
       for (int jj = 0; jj < (ROW_SPAN ? 1 : VPL); ++jj) {
         const int vi = lane + 32 * jj;
-        const uint4 xv = vi < nvec ? xs[vi] : make_uint4(0, 0, 0, 0);
+        const uint4 xv = (EXACT || vi < nvec) ? xs[vi] : make_uint4(0, 0, 0, 0);
         double acc[4] = {0.0, 0.0, 0.0, 0.0};
         sumsq8_fast(xv, acc);
         double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
@@ -321,11 +327,19 @@ __global__ void __launch_bounds__(kNRThreads, 1)
 #pragma unroll
     for (int jj = 0; jj < VPL; ++jj) {
       const int vi = lane + 32 * jj;
-      const bool ok = vi < nvec;
+      const bool ok = EXACT || vi < nvec;
       const int vc = ok ? vi : 0;
       const float rs = rstd[ROW_SPAN ? 0 : jj];
       const uint64_t rs2 = f2_pack(rs, rs);
-      const uint4 wv = ROW_SPAN ? w_row[vc] : whead;
+      uint64_t wpair[4];  // fp32 weight pairs of this vector
+      if (ROW_SPAN) {
+        const float4 w0 = w_row[2 * vc], w1 = w_row[2 * vc + 1];
+        wpair[0] = f2_pack(w0.x, w0.y); wpair[1] = f2_pack(w0.z, w0.w);
+        wpair[2] = f2_pack(w1.x, w1.y); wpair[3] = f2_pack(w1.z, w1.w);
+      } else {
+        wpair[0] = bf16x2_to_f2(whead.x); wpair[1] = bf16x2_to_f2(whead.y);
+        wpair[2] = bf16x2_to_f2(whead.z); wpair[3] = bf16x2_to_f2(whead.w);
+      }
       uint4 mv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
       if (MODULATE) {
         mv = m_s[vc];
@@ -333,26 +347,24 @@ __global__ void __launch_bounds__(kNRThreads, 1)
       }
       const uint4 xv = xs[vc];
       const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
-      const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
       const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mv);
       const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
       uint32_t h[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        h[e] = f2_to_bf16x2(f2_mul(f2_mul(bf16x2_to_f2(xw[e]), rs2), bf16x2_to_f2(ww[e])));
+        h[e] = f2_to_bf16x2(f2_mul(f2_mul(bf16x2_to_f2(xw[e]), rs2), wpair[e]));
         if (MODULATE) h[e] = bf2_add(bf2_mul(h[e], mw[e]), sw[e]);
       }
       uint32_t o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const uint32_t pw = __shfl_sync(0xffffffffu, h[e], partner);
-        float a0, a1, b0, b1;
-        f2_unpack(A[e], a0, a1);
-        f2_unpack(B[e], b0, b1);
-        // scalar round-to-nearest products and add: never contracted into an FMA
-        const float r0 = __fadd_rn(__fmul_rn(a0, bf16_lo(h[e])), __fmul_rn(b0, bf16_lo(pw)));
-        const float r1 = __fadd_rn(__fmul_rn(a1, bf16_hi(h[e])), __fmul_rn(b1, bf16_hi(pw)));
-        o[e] = pack_bf16(r0, r1);
+        // packed round-to-nearest products, scalar adds (a packed add after a
+        // packed multiply was measured to round like a fused multiply-add)
+        float p0, p1, q0, q1;
+        f2_unpack(f2_mul(A[e], bf16x2_to_f2(h[e])), p0, p1);
+        f2_unpack(f2_mul(B[e], bf16x2_to_f2(pw)), q0, q1);
+        o[e] = pack_bf16(__fadd_rn(p0, q0), __fadd_rn(p1, q1));
         if (!FULL_ROT && role == 2) o[e] = h[e];
       }
       if (ok) stg_v4(yr + 8 * vi, make_uint4(o[0], o[1], o[2], o[3]));
@@ -363,13 +375,13 @@ __global__ void __launch_bounds__(kNRThreads, 1)
 }
 
 int ring_offset(int nvec, bool row, bool mod) {
-  const int n_cst = ((row ? 2 : 0) + (mod ? 2 : 0)) * nvec;
-  return (256 + n_cst * 16 + 1023) & ~1023;
+  const int cst_bytes = (row ? 2 * nvec * 32 : 0) + (mod ? 2 * nvec * 16 : 0);
+  return (256 + cst_bytes + 1023) & ~1023;
 }
 
-template <int VPL, bool ROW, bool MOD, bool FULL>
+template <int VPL, bool ROW, bool MOD, bool FULL, bool EXACT>
 cudaError_t launch_one(const CUtensorMap& tm, const NRParams& p, int smem, cudaStream_t st) {
-  auto kern = adaln_rms_rope_kernel<VPL, ROW, MOD, FULL>;
+  auto kern = adaln_rms_rope_kernel<VPL, ROW, MOD, FULL, EXACT>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -383,15 +395,15 @@ cudaError_t launch_one(const CUtensorMap& tm, const NRParams& p, int smem, cudaS
   return cudaGetLastError();
 }
 
-template <int VPL>
+template <int VPL, bool EXACT>
 cudaError_t launch_vpl(const CUtensorMap& tm, const NRParams& p, bool row, bool mod, bool full, int smem,
                        cudaStream_t st) {
   if (row) {
-    if (mod) return full ? launch_one<VPL, true, true, true>(tm, p, smem, st) : launch_one<VPL, true, true, false>(tm, p, smem, st);
-    return full ? launch_one<VPL, true, false, true>(tm, p, smem, st) : launch_one<VPL, true, false, false>(tm, p, smem, st);
+    if (mod) return full ? launch_one<VPL, true, true, true, EXACT>(tm, p, smem, st) : launch_one<VPL, true, true, false, EXACT>(tm, p, smem, st);
+    return full ? launch_one<VPL, true, false, true, EXACT>(tm, p, smem, st) : launch_one<VPL, true, false, false, EXACT>(tm, p, smem, st);
   }
-  if (mod) return full ? launch_one<VPL, false, true, true>(tm, p, smem, st) : launch_one<VPL, false, true, false>(tm, p, smem, st);
-  return full ? launch_one<VPL, false, false, true>(tm, p, smem, st) : launch_one<VPL, false, false, false>(tm, p, smem, st);
+  if (mod) return full ? launch_one<VPL, false, true, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, true, false, EXACT>(tm, p, smem, st);
+  return full ? launch_one<VPL, false, false, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, false, false, EXACT>(tm, p, smem, st);
 }
 
 }  // namespace
@@ -453,10 +465,11 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const bool full = rot == 128;
   const int vpl = (int)((a.heads * 16 + 31) / 32);
-  if (vpl <= 4) return launch_vpl<4>(tm, p, row, mod, full, smem, stream);
-  if (vpl <= 8) return launch_vpl<8>(tm, p, row, mod, full, smem, stream);
-  if (vpl <= 12) return launch_vpl<12>(tm, p, row, mod, full, smem, stream);
-  return launch_vpl<16>(tm, p, row, mod, full, smem, stream);
+  if (a.heads == 24) return launch_vpl<12, true>(tm, p, row, mod, full, smem, stream);  // 3072-wide rows
+  if (vpl <= 4) return launch_vpl<4, false>(tm, p, row, mod, full, smem, stream);
+  if (vpl <= 8) return launch_vpl<8, false>(tm, p, row, mod, full, smem, stream);
+  if (vpl <= 12) return launch_vpl<12, false>(tm, p, row, mod, full, smem, stream);
+  return launch_vpl<16, false>(tm, p, row, mod, full, smem, stream);
 }
 
 }  // namespace h3
