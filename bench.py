@@ -62,17 +62,23 @@ def load_traffic():
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi SM clocks and throttle reasons around the timed region.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Samples carry nvidia-smi's timestamp; ``mark_start``/``mark_end`` bracket the
+    timed region on the host clock, and the summary keeps the samples inside it
+    (or the one nearest to it when the region is shorter than the sampling
+    period)."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int, period_ms: int = 100):
+    def __init__(self, index: int, period_ms: int = 20):
         self.index = index
         self.period_ms = period_ms
         self.proc = None
         self.lines = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -90,6 +96,14 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark_start(self):
+        import datetime
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        import datetime
+        self.t1 = datetime.datetime.now()
+
     def __exit__(self, *exc):
         if self.proc is not None:
             time.sleep(0.15)
@@ -100,25 +114,30 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons, power = [], None, set(), []
+        import datetime
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        samples = []
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-                power.append(float(parts[3]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                samples.append((ts, float(parts[2]), float(parts[3]), float(parts[4]),
+                                [nm for nm, v in zip(names, parts[6:10]) if v.lower() == "active"]))
             except ValueError:
                 continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
+        if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm), "power_w_max": max(power) if power else None}
+        inside = samples
+        if self.t0 is not None and self.t1 is not None:
+            inside = [s for s in samples if self.t0 <= s[0] <= self.t1]
+            if not inside:  # region shorter than the sampling period: nearest sample
+                mid = self.t0 + (self.t1 - self.t0) / 2
+                inside = [min(samples, key=lambda s: abs((s[0] - mid).total_seconds()))]
+        reasons = sorted({r for s in inside for r in s[4]})
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": inside[0][2], "reasons": reasons,
+                "samples": len(inside), "power_w_max": max(s[3] for s in inside), "period_ms": self.period_ms}
 
 
 # ---------------------------------------------------------------------------
@@ -258,11 +277,13 @@ def run_ours(args, rank, world, local_rank):
     with ClockSampler(local_rank) as clk:
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
+        clk.mark_start()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
         ev1.record(stream)
         ev1.synchronize()
+        clk.mark_end()
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     if world > 1:
