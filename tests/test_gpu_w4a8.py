@@ -90,3 +90,46 @@ def test_fused_w4a8_mlp_matches_op_chain_and_oracle():
     r2 = res.cuda()
     h3b200.fused_gated_mlp_w4a8(r2, x.cuda(), wt, gate.cuda(), out=r2)
     np.testing.assert_array_equal(t2u(r2), t2u(out))
+
+
+def test_w4a8_linear_cta_pair_path_matches_single_cta_and_oracle():
+    """Large M takes the CTA-pair GEMM (cta_group::2, correction MMA over both CTAs' rows);
+    row slices of <= 256 rows take the single-CTA GEMM. The tensor-core correction sums
+    each output element in the same k order on both paths, so they agree bit for bit;
+    a row subset is checked against the oracle within the north-star tolerance."""
+    gen = torch.Generator().manual_seed(41)
+    m, k, n = 2048, 3072, 3072
+    w = randn_bf16((n, k), gen, std=0.02)
+    x = randn_bf16((m, k), gen).cuda()
+    q, s_rel, s_ch, corr = h3b200.quantize_w4a8_weight(w.cuda(), 128)
+    grid = h3b200.dequant_int4_grouped_to_int8(q, s_rel, 128)
+    y = h3b200.w4a8_int8_linear(x, q, s_rel, s_ch, correction=corr, group_size=128, grid=grid)
+    parts = [h3b200.w4a8_int8_linear(x[s:s + 200], q, s_rel, s_ch, correction=corr, group_size=128, grid=grid)
+             for s in range(0, m, 200)]
+    assert h3b200.device_status(0) == 0
+    np.testing.assert_array_equal(t2u(y), t2u(torch.cat(parts)))
+    rows = slice(1000, 1064)
+    o = O.w4a8_int8_linear_quantized(t2u(x[rows]), np_(q), np_(s_rel), np_(s_ch), t2u(corr), 128, 256)
+    rel, mx = rel_l2(t2u(y[rows]), o)
+    assert rel <= 2e-3 and mx <= 2e-2
+
+
+def test_fused_w4a8_mlp_cta_pair_path_matches_op_chain():
+    """Config-2 shapes (d 3072, ffn 12288) at 2048 tokens: both fused GEMMs (correction + GELU,
+    correction + gated residual) run on CTA pairs; the result equals the chain of single ops."""
+    gen = torch.Generator().manual_seed(43)
+    d, ffn, m = 3072, 12288, 2048
+    w1 = randn_bf16((ffn, d), gen, std=0.02).cuda()
+    w2 = randn_bf16((d, ffn), gen, std=0.02).cuda()
+    x = randn_bf16((m, d), gen).cuda()
+    gate = randn_bf16((d,), gen).cuda()
+    res = randn_bf16((m, d), gen).cuda()
+    wt = h3b200.W4A8MLPWeights.from_float(w1, w2)
+    out = h3b200.fused_gated_mlp_w4a8(res, x, wt, gate)
+    h = h3b200.w4a8_int8_linear(x, wt.q1, wt.s_rel1, wt.s_ch1, correction=wt.corr1, group_size=128)
+    y = h3b200.w4a8_int8_linear(h, wt.q2, wt.s_rel2, wt.s_ch2, correction=wt.corr2, group_size=128,
+                                input_act="gelu_tanh")
+    assert h3b200.device_status(0) == 0
+    f = O.bf16_to_f32
+    expect = O.f32_to_bf16(f(t2u(res)) + f(t2u(y)) * f(t2u(gate))[None, :])
+    np.testing.assert_array_equal(t2u(out), expect)

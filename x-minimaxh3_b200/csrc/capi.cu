@@ -288,26 +288,26 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
   cudaStream_t st = S(stream);
   cudaError_t e = h3::launch_quantize_convrot(x, ldx, m, k, act, xq, xs, correction ? sx : nullptr, group_size, kp, st);
   if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: convrot quantize");
-  h3::GemmArgs g;
-  g.a = xq; g.w = grid; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
-  g.epilogue = h3::kEpiBF16; g.a_scale = xs; g.w_scale = s_channel; g.w_scale_per_channel = 1;
-  g.out = out; g.ldo = n;
-  e = h3::launch_gemm_i8(g, st);
-  if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: gemm");
   if (correction != nullptr) {
     e = h3::launch_correction_transpose(correction, groups, n, kp, corr_t, st);
     if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction layout");
-    e = h3::launch_w4a8_correction(sx, corr_t, kp, m, n, out, n, false, st);
-    if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear: correction");
   }
-  return H3B200_OK;
+  // GEMM with the dequant epilogue; the asymmetric correction is fused into it
+  h3::GemmArgs g;
+  g.a = xq; g.w = grid; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = correction ? h3::kEpiBF16Corr : h3::kEpiBF16;
+  g.a_scale = xs; g.w_scale = s_channel; g.w_scale_per_channel = 1;
+  g.out = out; g.ldo = n;
+  g.sx = sx; g.corr_t = corr_t; g.kp = kp;
+  e = h3::launch_gemm_i8(g, st);
+  return from_cuda(e, "w4a8_int8_linear: gemm");
 }
 
 
 int64_t h3b200_fused_gated_mlp_w4a8_workspace_bytes(int64_t m, int64_t d, int64_t ffn, int64_t group_size) {
   if (m < 0 || d <= 0 || ffn <= 0 || group_size <= 0) return 0;
   const int64_t kp1 = h3::correction_kpad(d / group_size), kp2 = h3::correction_kpad(ffn / group_size);
-  return round_up(ffn * d, 256) * 2 + round_up(m * d, 256) * 3 + round_up(m * 4, 256) * 2 +
+  return round_up(ffn * d, 256) * 2 + round_up(m * d, 256) + round_up(m * 4, 256) * 2 +
          round_up(m * kp1 * 2, 256) + round_up(ffn * kp1 * 2, 256) + round_up(m * ffn * 2, 256) +
          round_up(m * ffn, 256) + round_up(m * kp2 * 2, 256) + round_up(d * kp2 * 2, 256) + 4096;
 }
@@ -341,7 +341,6 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   float* xs2 = static_cast<float*>(c.take(m * 4));
   void* sx2 = c.take(m * kp2 * 2);
   void* ct2 = c.take(d * kp2 * 2);
-  void* y = c.take(m * d * 2);
   if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: workspace too small");
   cudaStream_t st = S(stream);
   cudaError_t e = h3::launch_dequant_int4(qdata1, s_rel1, ffn, d, group_size, grid1, st);
@@ -351,35 +350,37 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   // fc1: ConvRot-quantize x, GEMM, asymmetric correction
   e = h3::launch_quantize_convrot(x, ldx, m, d, H3B200_ACT_NONE, xq, xs, correction1 ? sx1 : nullptr, group_size, kp1, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize x");
-  h3::GemmArgs g1;
-  g1.a = xq; g1.w = grid1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
-  g1.epilogue = h3::kEpiBF16; g1.a_scale = xs; g1.w_scale = s_channel1; g1.w_scale_per_channel = 1;
-  g1.out = h; g1.ldo = ffn;
-  e = h3::launch_gemm_i8(g1, st);
-  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1");
   if (correction1) {
     e = h3::launch_correction_transpose(correction1, ng1, ffn, kp1, ct1, st);
-    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx1, ct1, kp1, m, ffn, h, ffn, true, st);  // + GELU
-    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1 correction");
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1 correction layout");
   }
-  // fc2: ConvRot-quantize gelu(h), GEMM, correction, gated residual
-  // gelu(h) was applied by the fc1 correction epilogue; without a correction the quantizer applies it
+  // fc1 GEMM: dequant, asymmetric correction and GELU in the epilogue (without
+  // a correction the plain dequant epilogue runs and the fc2 quantizer applies the GELU)
+  h3::GemmArgs g1;
+  g1.a = xq; g1.w = grid1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
+  g1.epilogue = correction1 ? h3::kEpiBF16CorrGelu : h3::kEpiBF16;
+  g1.a_scale = xs; g1.w_scale = s_channel1; g1.w_scale_per_channel = 1;
+  g1.out = h; g1.ldo = ffn;
+  g1.sx = sx1; g1.corr_t = ct1; g1.kp = kp1;
+  e = h3::launch_gemm_i8(g1, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc1");
+  // fc2: ConvRot-quantize gelu(h); GEMM with dequant, correction and gated residual in the epilogue
   e = h3::launch_quantize_convrot(h, ffn, m, ffn, correction1 ? H3B200_ACT_NONE : H3B200_ACT_GELU_TANH, q2, xs2,
                                   correction2 ? sx2 : nullptr, group_size, kp2, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: quantize gelu(h)");
-  h3::GemmArgs g2;
-  g2.a = q2; g2.w = grid2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
-  g2.epilogue = h3::kEpiBF16; g2.a_scale = xs2; g2.w_scale = s_channel2; g2.w_scale_per_channel = 1;
-  g2.out = y; g2.ldo = d;
-  e = h3::launch_gemm_i8(g2, st);
-  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2");
   if (correction2) {
     e = h3::launch_correction_transpose(correction2, ng2, d, kp2, ct2, st);
-    if (e == cudaSuccess) e = h3::launch_w4a8_correction(sx2, ct2, kp2, m, d, y, d, false, st);
-    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2 correction");
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: fc2 correction layout");
   }
-  e = h3::launch_gated_residual_bf16(y, d, gate, residual, ldr, out, ldo, m, d, st);
-  return from_cuda(e, "fused_gated_mlp_w4a8: gated residual");
+  h3::GemmArgs g2;
+  g2.a = q2; g2.w = grid2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
+  g2.epilogue = correction2 ? h3::kEpiGatedResidualCorr : h3::kEpiGatedResidual;
+  g2.a_scale = xs2; g2.w_scale = s_channel2; g2.w_scale_per_channel = 1;
+  g2.gate = gate; g2.residual = residual; g2.ldr = ldr;
+  g2.out = out; g2.ldo = ldo;
+  g2.sx = sx2; g2.corr_t = ct2; g2.kp = kp2;
+  e = h3::launch_gemm_i8(g2, st);
+  return from_cuda(e, "fused_gated_mlp_w4a8: fc2");
 }
 }  // extern "C"
 

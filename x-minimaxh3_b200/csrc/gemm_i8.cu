@@ -13,18 +13,22 @@
 //   warp 1      MMA issuer: 4 x tcgen05.mma.cta_group::1.kind::i8 (128x256x32)
 //               per stage into a TMEM accumulator; tcgen05.commit frees the
 //               stage and, after the last k-block, publishes the accumulator.
-//               (The kEpiAddBF16 variant is a bf16 GEMM: kind::f16, 128x256x16,
-//               the same 128-byte k-block rows and fp32 accumulators.)
 //   warp 2      TMEM allocator (512 columns = two 128x256 s32 accumulators).
 //   warps 4-11  epilogue: tcgen05.ld 32 columns at a time, fused dequant /
 //               activation / gated residual; each warp stages its 32x32 bf16
 //               result in shared memory (64-byte swizzle, conflict-free) and one
 //               lane writes it with a TMA tensor store (int32 results use
-//               128-bit global stores). Epilogues that read a bf16 tensor of
-//               the output's shape (residual, or the output itself for
-//               kEpiAddBF16) TMA-load its 32x32 box into the same staging box
-//               first. The two accumulators let the epilogue
-//               of tile i overlap the mainloop of tile i+1.
+//               128-bit global stores). The gated-residual epilogues TMA-load
+//               the residual's 32x32 box into the same staging box first. The
+//               two accumulators let the epilogue of tile i overlap the
+//               mainloop of tile i+1.
+// W4A8 epilogues (kEpi*Corr) add the asymmetric correction sx . corr_t^T, a
+// rank-kp bf16 product (kp <= 128), on the tensor cores inside the same TMEM
+// accumulator: a first epilogue pass replaces each int32 accumulator by its
+// dequantized bf16 value as fp32 (tcgen05.st); one epilogue thread then issues
+// kind::f16 MMAs that accumulate sx[rows, :kp] . corr_t[cols, :kp]^T onto it,
+// their operands TMA-loaded into shared memory reserved for them (the stage
+// ring shrinks to make room); a second pass reads the corrected sums.
 // Tiles are visited n-fastest so that the concurrently running CTAs share the
 // same A rows and the whole weight stays resident in the 126 MB L2.
 // No cluster multicast is used anywhere (the same binary runs in multi-GPU jobs).
@@ -48,6 +52,8 @@ constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint32_t IDESC_I8 = umma_idesc_i8(BM, BN);
 constexpr uint32_t IDESC_I8_PAIR = umma_idesc_i8(2 * BM, BN);  // cta_group::2: 256 x 256 per CTA pair
 constexpr uint32_t IDESC_BF16 = umma_idesc_bf16(BM, BN);
+constexpr uint32_t IDESC_BF16_PAIR = umma_idesc_bf16(2 * BM, BN);
+constexpr int kMaxCorrKp = 128;  // correction groups (padded) held in shared memory
 constexpr int BAR_BYTES = 256;
 constexpr int STAGE_OPS_BYTES = NUM_EPI_WARPS * 2 * 128 * 4;   // per-warp column scales + bias/gate
 constexpr int GELU_TAB_BYTES = 2 * 19 * 128 * 2;
@@ -61,7 +67,7 @@ static_assert(SMEM_BYTES <= 232448, "GEMM shared memory exceeds the 227 KB per-b
 
 // status codes recorded when a bounded wait expires
 constexpr unsigned kErrProducer = 0x101, kErrMmaAcc = 0x102, kErrMmaFull = 0x103, kErrEpi = 0x104,
-                   kErrDrain = 0x105, kErrEpiIn = 0x106;
+                   kErrDrain = 0x105, kErrEpiIn = 0x106, kErrCorr = 0x107;
 
 struct KParams {
   int m, n, k;
@@ -76,7 +82,13 @@ struct KParams {
   void* out;
   int64_t ldo;
   float* row_absmax;
+  int corr_kb;  // 64-group k-blocks of the correction operands (kEpi*Corr)
 };
+
+template <int EPI>
+constexpr bool is_corr_epi() {
+  return EPI == kEpiBF16Corr || EPI == kEpiBF16CorrGelu || EPI == kEpiGatedResidualCorr;
+}
 
 // Exact bf16 tanh-GELU by table. The activation input is a bf16 value, so the
 // GELU is a function on at most 65,536 inputs. Every CTA of the GELU variant
@@ -109,9 +121,37 @@ __device__ __forceinline__ uint32_t gelu_lookup(uint32_t hb, const uint16_t* tab
   return bf16_bits(gelu_tanh_exact(__uint_as_float(hb << 16)));
 }
 
+// GELU of 16 packed bf16 pairs, in place.
+__device__ __forceinline__ void gelu_pairs(uint32_t (&ob)[16], const uint16_t* gtab) {
+  bool miss = false;
+  uint32_t g[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    g[j] = gelu_lookup_fast(ob[j] & 0xFFFFu, gtab, miss) | (gelu_lookup_fast(ob[j] >> 16, gtab, miss) << 16);
+  if (miss) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) g[j] = gelu_lookup(ob[j] & 0xFFFFu, gtab) | (gelu_lookup(ob[j] >> 16, gtab) << 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) ob[j] = g[j];
+}
+
 // Dequantized bf16 bits of the 32 accumulators of one chunk (GELU variant input).
 __device__ __forceinline__ uint32_t dequant_bits(uint32_t acc, float xs, float ws) {
   return bf16_bits(__fmul_rn(__int2float_rn((int)acc), __fmul_rn(xs, ws)));
+}
+
+// First pass of the W4A8 epilogues: each int32 accumulator of the chunk becomes
+// its dequantized bf16 value bf16(acc * (xs * ws)), held as fp32 bits.
+__device__ __forceinline__ void dequant_to_f32(uint32_t (&r)[32], float xs, const float* ws_s) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
+    r[4 * q + 0] = dequant_bits(r[4 * q + 0], xs, w4.x) << 16;
+    r[4 * q + 1] = dequant_bits(r[4 * q + 1], xs, w4.y) << 16;
+    r[4 * q + 2] = dequant_bits(r[4 * q + 2], xs, w4.z) << 16;
+    r[4 * q + 3] = dequant_bits(r[4 * q + 3], xs, w4.w) << 16;
+  }
 }
 
 // fc1 chunk: out bits (packed pairs) = gelu(bf16(acc * (xs * ws))); chunk absmax bits.
@@ -159,8 +199,9 @@ __device__ __forceinline__ void store_i32_chunk(const KParams& p, int row, int c
 
 // bf16 results (packed pairs) of one 32-column chunk of one accumulator row.
 // ws_s / aux_s: this warp's staged per-column weight scales and bias-or-gate
-// (fp32) for the chunk; in_w: the row's 32 bf16 input values (residual, or the
-// output being accumulated into) for the epilogues that read one.
+// (fp32) for the chunk; in_w: the row's 32 bf16 residual values for the
+// gated-residual epilogues. For the W4A8 epilogues r holds the fp32 sums
+// dequant + correction of the second pass.
 template <int EPI>
 __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t (&r)[32], float xs,
                                                 const float* ws_s, const float* aux_s, const uint16_t* gtab,
@@ -168,23 +209,20 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
                                                 uint32_t (&ob)[16]) {
   if constexpr (EPI == kEpiGeluAbsmax) {
     gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
-  } else if constexpr (EPI == kEpiAddBF16 || EPI == kEpiAddBF16Gelu) {
+  } else if constexpr (is_corr_epi<EPI>()) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      ob[j] = pack_bf16(__fadd_rn(bf16_lo(in_w[j]), __uint_as_float(r[2 * j])),
-                        __fadd_rn(bf16_hi(in_w[j]), __uint_as_float(r[2 * j + 1])));
-    if constexpr (EPI == kEpiAddBF16Gelu) {
-      bool miss = false;
-      uint32_t g[16];
+    for (int j = 0; j < 16; ++j) ob[j] = pack_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+    if constexpr (EPI == kEpiBF16CorrGelu) gelu_pairs(ob, gtab);
+    if constexpr (EPI == kEpiGatedResidualCorr) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        g[j] = gelu_lookup_fast(ob[j] & 0xFFFFu, gtab, miss) | (gelu_lookup_fast(ob[j] >> 16, gtab, miss) << 16);
-      if (miss) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) g[j] = gelu_lookup(ob[j] & 0xFFFFu, gtab) | (gelu_lookup(ob[j] >> 16, gtab) << 16);
+      for (int q = 0; q < 8; ++q) {
+        const float4 a4 = *reinterpret_cast<const float4*>(aux_s + 4 * q);
+        const uint32_t y0 = ob[2 * q], y1 = ob[2 * q + 1], r0 = in_w[2 * q], r1 = in_w[2 * q + 1];
+        ob[2 * q] = pack_bf16(__fadd_rn(bf16_lo(r0), __fmul_rn(bf16_lo(y0), a4.x)),
+                              __fadd_rn(bf16_hi(r0), __fmul_rn(bf16_hi(y0), a4.y)));
+        ob[2 * q + 1] = pack_bf16(__fadd_rn(bf16_lo(r1), __fmul_rn(bf16_lo(y1), a4.z)),
+                                  __fadd_rn(bf16_hi(r1), __fmul_rn(bf16_hi(y1), a4.w)));
       }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) ob[j] = g[j];
     }
   } else {
 #pragma unroll
@@ -226,14 +264,21 @@ template <int EPI, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
                    const KParams p) {
-  constexpr bool kBF16Mma = EPI == kEpiAddBF16 || EPI == kEpiAddBF16Gelu;
-  constexpr bool kInBox = EPI == kEpiGatedResidual || kBF16Mma;
-  static_assert(CG == 1 || (CG == 2 && !kBF16Mma), "CTA pairs run the int8 MMA only");
-  constexpr int kStages = CG == 2 ? 6 : STAGES;
+  constexpr bool kCorr = is_corr_epi<EPI>();
+  constexpr bool kInBox = EPI == kEpiGatedResidual || EPI == kEpiGatedResidualCorr;
   constexpr int kBBytes = B_BYTES / CG;
   constexpr int kStageBytes = A_BYTES + kBBytes;
-  static_assert(kStages * kStageBytes <= OFF_BAR, "stage ring overflows its region");
+  // W4A8 correction operands for one tile: sx rows [BM x kMaxCorrKp] and
+  // corr_t rows [BN / CG x kMaxCorrKp], bf16, as 64-group k-blocks
+  constexpr int kCorrSxBytes = kCorr ? BM * kMaxCorrKp * 2 : 0;
+  constexpr int kCorrCtBytes = kCorr ? (BN / CG) * kMaxCorrKp * 2 : 0;
+  constexpr int kStagesMax = CG == 2 ? 6 : STAGES;
+  constexpr int kStagesFit = (OFF_BAR - kCorrSxBytes - kCorrCtBytes) / kStageBytes;
+  constexpr int kStages = kStagesMax < kStagesFit ? kStagesMax : kStagesFit;
+  constexpr int kOffCorr = kStages * kStageBytes;
+  static_assert(kStages >= 2 && kOffCorr + kCorrSxBytes + kCorrCtBytes <= OFF_BAR, "stage ring overflows its region");
   constexpr int kTileRows = BM * CG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -245,10 +290,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull_bar = empty_bar + kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint64_t* in_bar = drain_bar + 1;  // [NUM_EPI_WARPS]: input-box loads of the epilogue warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(in_bar + NUM_EPI_WARPS);
+  uint64_t* in_bar = drain_bar + 1;                   // [NUM_EPI_WARPS]: input-box loads of the epilogue warps
+  uint64_t* corr_full_bar = in_bar + NUM_EPI_WARPS;   // correction operands landed (rank 0 counts both CTAs)
+  uint64_t* dq_bar = corr_full_bar + 1;               // first epilogue pass written back (rank 0, all warps)
+  uint64_t* cf_bar = dq_bar + 1;                      // correction MMAs complete (each CTA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cf_bar + 1);
   float* ops_smem = reinterpret_cast<float*>(smem + OFF_OPS);
   uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + OFF_GELU);
+  uint8_t* corr_sx = smem + kOffCorr;
+  uint8_t* corr_ct = corr_sx + kCorrSxBytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -264,12 +314,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     for (int w = 0; w < NUM_EPI_WARPS; ++w) mbar_init(&in_bar[w], 1);
+    mbar_init(corr_full_bar, 1);
+    mbar_init(dq_bar, NUM_EPI_WARPS * CG);
+    mbar_init(cf_bar, 1);
     fence_barrier_init();
     fence_proxy_async_shared();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (EPI != kEpiI32) tma_prefetch_desc(&tmO);
     if (kInBox) tma_prefetch_desc(&tmR);
+    if (kCorr) {
+      tma_prefetch_desc(&tmS);
+      tma_prefetch_desc(&tmC);
+    }
   }
   if (warp == 2) {
     if constexpr (CG == 2) {
@@ -280,7 +337,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tmem_relinquish();
     }
   }
-  if constexpr (EPI == kEpiGeluAbsmax || EPI == kEpiAddBF16Gelu) {
+  if constexpr (EPI == kEpiGeluAbsmax || EPI == kEpiBF16CorrGelu) {
     for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
       gelu_tab[i] = (uint16_t)bf16_bits(gelu_tanh_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
   }
@@ -340,7 +397,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = cid; tile < p.num_tiles && ok; tile += ncl, ++tcount) {
         const int acc = tcount & 1;
         const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
-        if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, kErrMmaAcc)) break;
+        const bool freed = CG == 2 ? mbar_wait_cluster(&tempty_bar[acc], acc_ph ^ 1u, kErrMmaAcc)
+                                   : mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, kErrMmaAcc);
+        if (!freed) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
@@ -359,9 +418,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if constexpr (CG == 2)
               umma_i8_pair(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
                            IDESC_I8_PAIR, accum);
-            else if constexpr (kBF16Mma)
-              umma_bf16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC_BF16,
-                        accum);
             else
               umma_i8(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), IDESC_I8,
                       accum);
@@ -403,6 +459,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // row `lane` of the box, 16-byte chunk q, at the 64-byte-swizzle position q ^ ((lane >> 1) & 3)
     uint8_t* box_row = box + lane * 64;
     const int box_sw = (lane >> 1) & 3;
+    const bool corr_thread = kCorr && ew == 0 && lane == 0;  // loads the correction operands, issues its MMAs
     int tcount = 0;
     uint32_t in_phase = 0;
     bool in_pending = false;  // an input-box load was issued and not yet waited for
@@ -415,7 +472,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int row0 = m_blk * kTileRows + (int)rank * BM;  // this CTA's first row of the tile
       const int row = row0 + quarter * 32 + lane;
       const int col_base = n_blk * BN + half * 128;
-      if constexpr (EPI != kEpiI32 && !kBF16Mma) {
+      if constexpr (kCorr) {
+        // This tile's correction operands. The previous tile's correction MMAs
+        // have completed (its cf_bar phase), so their buffers are free.
+        if (corr_thread) {
+          const uint32_t bytes = (uint32_t)p.corr_kb * (uint32_t)(BM + BN / CG) * 128u;
+          if constexpr (CG == 2) {
+            if (rank == 0) mbar_arrive_expect_tx(corr_full_bar, 2 * bytes);  // both CTAs' bytes
+            const uint32_t bar0 = mapa_shared(corr_full_bar, 0);
+            for (int kb = 0; kb < p.corr_kb; ++kb) {
+              tma_load_2d_pair(corr_sx + kb * (BM * 128), &tmS, bar0, kb * 64, row0);
+              tma_load_2d_pair(corr_ct + kb * ((BN / CG) * 128), &tmC, bar0, kb * 64,
+                               n_blk * BN + (int)rank * (BN / CG));
+            }
+          } else {
+            mbar_arrive_expect_tx(corr_full_bar, bytes);
+            for (int kb = 0; kb < p.corr_kb; ++kb) {
+              tma_load_2d(corr_sx + kb * (BM * 128), &tmS, corr_full_bar, kb * 64, row0);
+              tma_load_2d(corr_ct + kb * (BN * 128), &tmC, corr_full_bar, kb * 64, n_blk * BN);
+            }
+          }
+        }
+      }
+      if constexpr (EPI != kEpiI32) {
         // stage this tile's per-column operands while the MMAs run
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -425,7 +504,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
           float a = 0.0f;
           if (EPI == kEpiBF16 && p.bias != nullptr && cok) a = __bfloat162float(p.bias[col]);
-          if (EPI == kEpiGatedResidual && cok) a = __bfloat162float(p.gate[col]);
+          if (kInBox && cok) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
         }
         __syncwarp();
@@ -433,10 +512,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
       tc_fence_after();
       float xs = 0.0f;
-      if constexpr (EPI != kEpiI32 && !kBF16Mma) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
+      if constexpr (EPI != kEpiI32) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
       const int box_row0 = row0 + quarter * 32;
+      if constexpr (kCorr) {
+        // pass 1: the dequantized values replace the int32 accumulators
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c, r);
+          tmem_wait_ld();
+          dequant_to_f32(r, xs, ws_s + c);
+          tmem_st32(taddr + c, r);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 2)
+            mbar_arrive_cluster(mapa_shared(dq_bar, 0));
+          else
+            mbar_arrive(dq_bar);
+        }
+        const uint32_t ph = (uint32_t)tcount & 1u;
+        if (corr_thread && rank == 0) {
+          // D[rows, cols] += sx[rows, :kp] . corr_t[cols, :kp]^T: kind::f16, fp32 accumulate
+          const bool ready = (CG == 2 ? mbar_wait_cluster(dq_bar, ph, kErrCorr) : mbar_wait(dq_bar, ph, kErrCorr)) &&
+                             mbar_wait(corr_full_bar, ph, kErrCorr);
+          if (ready) {
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+            for (int kb = 0; kb < p.corr_kb; ++kb) {
+              const uint32_t a_addr = smem_u32(corr_sx + kb * (BM * 128));
+              const uint32_t b_addr = smem_u32(corr_ct + kb * ((BN / CG) * 128));
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                if constexpr (CG == 2)
+                  umma_bf16_pair(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                                 IDESC_BF16_PAIR, 1u);
+                else
+                  umma_bf16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                            IDESC_BF16, 1u);
+              }
+            }
+            if constexpr (CG == 2) {
+              umma_commit_pair(mapa_shared(cf_bar, 0));
+              umma_commit_pair(mapa_shared(cf_bar, 1));
+            } else {
+              umma_commit(cf_bar);
+            }
+          }
+        }
+        if (!mbar_wait(cf_bar, ph, kErrEpi)) break;
+        tc_fence_after();
+      }
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         uint32_t r[32];
@@ -526,9 +656,12 @@ bool make_tmap_i8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
                         (uint32_t)BK, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+struct TensorMaps {
+  CUtensorMap a, b, out, res, sx, corr;
+};
+
 template <int EPI, int CG>
-cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
-                       const KParams& kp, int grid, cudaStream_t stream) {
+cudaError_t launch_epi(const TensorMaps& t, const KParams& kp, int grid, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -539,7 +672,7 @@ cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     attr_set[dev] = true;
   }
   if constexpr (CG == 1) {
-    gemm_i8_kernel<EPI, 1><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, to, tr, kp);
+    gemm_i8_kernel<EPI, 1><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(t.a, t.b, t.out, t.res, t.sx, t.corr, kp);
     return cudaGetLastError();
   } else {
     // a persistent grid must be fully resident: clamp to the clusters of two
@@ -567,7 +700,21 @@ cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (dev >= 0 && dev < 64 && grid > 2 * max_clusters[dev]) grid = 2 * max_clusters[dev];
     cfg.gridDim = dim3((unsigned)grid, 1, 1);
     cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-    return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<EPI, 2>, ta, tb, to, tr, kp);
+    return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<EPI, 2>, t.a, t.b, t.out, t.res, t.sx, t.corr, kp);
+  }
+}
+
+template <int CG>
+cudaError_t launch_cg(int epilogue, const TensorMaps& t, const KParams& kp, int grid, cudaStream_t stream) {
+  switch (epilogue) {
+    case kEpiI32: return launch_epi<kEpiI32, CG>(t, kp, grid, stream);
+    case kEpiBF16: return launch_epi<kEpiBF16, CG>(t, kp, grid, stream);
+    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, CG>(t, kp, grid, stream);
+    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual, CG>(t, kp, grid, stream);
+    case kEpiBF16Corr: return launch_epi<kEpiBF16Corr, CG>(t, kp, grid, stream);
+    case kEpiBF16CorrGelu: return launch_epi<kEpiBF16CorrGelu, CG>(t, kp, grid, stream);
+    case kEpiGatedResidualCorr: return launch_epi<kEpiGatedResidualCorr, CG>(t, kp, grid, stream);
+    default: return cudaErrorNotSupported;
   }
 }
 
@@ -616,55 +763,59 @@ int num_sms(int device) {
 
 cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   if (a.m <= 0 || a.n <= 0) return cudaSuccess;
-  const bool bf16_in = a.epilogue == kEpiAddBF16 || a.epilogue == kEpiAddBF16Gelu;  // bf16 operands, kind::f16
-  const int64_t esz = bf16_in ? 2 : 1;
-  if (a.k <= 0 || (a.k * esz) % 16 != 0 || a.n % 8 != 0 || (a.lda * esz) % 16 != 0 || (a.ldw * esz) % 16 != 0 ||
-      a.m > (1ll << 30) || a.n > (1ll << 30) || a.k > (1ll << 30))
+  if (a.k <= 0 || a.k % 16 != 0 || a.n % 8 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.m > (1ll << 30) ||
+      a.n > (1ll << 30) || a.k > (1ll << 30))
     return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
       (reinterpret_cast<uintptr_t>(a.out) & 15) || a.ldo % 8 != 0)
     return cudaErrorNotSupported;
-  if (a.epilogue == kEpiGatedResidual && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0))
+  const bool gated = a.epilogue == kEpiGatedResidual || a.epilogue == kEpiGatedResidualCorr;
+  if (gated && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0)) return cudaErrorNotSupported;
+  const bool corr = a.epilogue == kEpiBF16Corr || a.epilogue == kEpiBF16CorrGelu || a.epilogue == kEpiGatedResidualCorr;
+  if (corr && (a.sx == nullptr || a.corr_t == nullptr || a.kp <= 0 || a.kp % 64 != 0 || a.kp > kMaxCorrKp ||
+               (reinterpret_cast<uintptr_t>(a.sx) & 15) || (reinterpret_cast<uintptr_t>(a.corr_t) & 15)))
     return cudaErrorNotSupported;
-  CUtensorMap ta, tb, to, tr;
-  if (bf16_in) {
-    // 64 bf16 (128 bytes) per k-block row, 128-byte swizzle: the same smem tiles as the int8 path
-    if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.a, (uint64_t)a.k, (uint64_t)a.m,
-                        (uint64_t)a.lda * 2, BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.w, (uint64_t)a.k, (uint64_t)a.n,
-                        (uint64_t)a.ldw * 2, BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B))
-      return cudaErrorInvalidValue;
-  }
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
-  // CTA pairs (256 x 256 tiles, cta_group::2) for the int8 GEMMs with enough
-  // tiles to give every SM pair work; single CTAs otherwise.
+  // CTA pairs (256 x 256 tiles, cta_group::2) for the GEMMs with enough tiles
+  // to give every SM pair work; single CTAs otherwise.
   const int64_t n_blk = (a.n + BN - 1) / BN;
-  const bool pair = !bf16_in && ((a.m + 2 * BM - 1) / (2 * BM)) * n_blk >= sms / 2;
+  const bool pair = ((a.m + 2 * BM - 1) / (2 * BM)) * n_blk >= sms / 2;
   const int cg = pair ? 2 : 1;
-  if (!bf16_in && (!make_tmap_i8(&ta, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&tb, a.w, a.n, a.k, a.ldw, BN / cg)))
+  TensorMaps t;
+  if (!make_tmap_i8(&t.a, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&t.b, a.w, a.n, a.k, a.ldw, BN / cg))
     return cudaErrorInvalidValue;
   if (a.epilogue == kEpiI32) {
-    to = tb;  // unused: int32 results are stored directly
-  } else if (!encode_tmap_2d(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
+    t.out = t.b;  // unused: int32 results are stored directly
+  } else if (!encode_tmap_2d(&t.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
                              (uint64_t)a.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return cudaErrorInvalidValue;
   }
-  if (a.epilogue == kEpiGatedResidual) {
-    if (!encode_tmap_2d(&tr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.residual, (uint64_t)a.n, (uint64_t)a.m,
+  if (gated) {
+    if (!encode_tmap_2d(&t.res, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.residual, (uint64_t)a.n, (uint64_t)a.m,
                         (uint64_t)a.ldr * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return cudaErrorInvalidValue;
   } else {
-    tr = to;  // kEpiAddBF16 reads the output it accumulates into; unused otherwise
+    t.res = t.out;  // unused
+  }
+  if (corr) {
+    // 64 groups (128 bytes) per k-block row, 128-byte swizzle: the UMMA operand layout of the mainloop tiles
+    if (!encode_tmap_2d(&t.sx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.sx, (uint64_t)a.kp, (uint64_t)a.m,
+                        (uint64_t)a.kp * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap_2d(&t.corr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.corr_t, (uint64_t)a.kp, (uint64_t)a.n,
+                        (uint64_t)a.kp * 2, 64, BN / cg, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  } else {
+    t.sx = t.a;  // unused
+    t.corr = t.a;
   }
   KParams kp;
   kp.m = (int)a.m;
   kp.n = (int)a.n;
   kp.k = (int)a.k;
   kp.num_n_blk = (int)n_blk;
-  const int64_t k_per_blk = BK / esz;
-  kp.num_k_blk = (int)((a.k + k_per_blk - 1) / k_per_blk);
+  kp.num_k_blk = (int)((a.k + BK - 1) / BK);
   const int64_t num_m_blk = (a.m + cg * BM - 1) / (cg * BM);
   const int64_t tiles = num_m_blk * kp.num_n_blk;
   if (tiles > (1ll << 30)) return cudaErrorNotSupported;
@@ -679,26 +830,9 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.out = a.out;
   kp.ldo = a.ldo;
   kp.row_absmax = a.row_absmax;
-  if (pair) {
-    const int grid = 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2));
-    switch (a.epilogue) {
-      case kEpiI32: return launch_epi<kEpiI32, 2>(ta, tb, to, tr, kp, grid, stream);
-      case kEpiBF16: return launch_epi<kEpiBF16, 2>(ta, tb, to, tr, kp, grid, stream);
-      case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, 2>(ta, tb, to, tr, kp, grid, stream);
-      case kEpiGatedResidual: return launch_epi<kEpiGatedResidual, 2>(ta, tb, to, tr, kp, grid, stream);
-      default: return cudaErrorNotSupported;
-    }
-  }
-  const int grid = (int)std::min<int64_t>(tiles, (int64_t)sms);
-  switch (a.epilogue) {
-    case kEpiI32: return launch_epi<kEpiI32, 1>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiBF16: return launch_epi<kEpiBF16, 1>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, 1>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual, 1>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiAddBF16: return launch_epi<kEpiAddBF16, 1>(ta, tb, to, tr, kp, grid, stream);
-    case kEpiAddBF16Gelu: return launch_epi<kEpiAddBF16Gelu, 1>(ta, tb, to, tr, kp, grid, stream);
-    default: return cudaErrorNotSupported;
-  }
+  kp.corr_kb = corr ? (int)(a.kp / 64) : 0;
+  if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
+  return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }
 
 }  // namespace h3

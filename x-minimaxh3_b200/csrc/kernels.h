@@ -13,14 +13,16 @@ enum GemmEpilogue : int {
   kEpiBF16 = 1,            // bf16(acc * (xs * ws)) (+ bf16 bias)
   kEpiGeluAbsmax = 2,      // a = gelu(bf16(acc * (xs * ws))) stored bf16, row absmax of |a| via atomicMax
   kEpiGatedResidual = 3,   // out = bf16(residual + bf16(acc * (xs * ws)) * gate)
-  kEpiAddBF16 = 4,         // bf16 x bf16 -> fp32 GEMM (kind::f16): out = bf16(out + acc), in place
-                           // (the W4A8 asymmetric correction sx[m, g] . corr[g, n] added to a linear's output)
-  kEpiAddBF16Gelu = 5,     // as kEpiAddBF16, then out = tanh-GELU(out) (exact bf16)
+  // W4A8 linears with the asymmetric correction fused into the INT8 GEMM:
+  //   y = bf16(bf16(acc * (xs * ws)) + sum_g sx[m, g] * corr_t[n, g])   (fp32 sum, one rounding)
+  kEpiBF16Corr = 4,          // out = y
+  kEpiBF16CorrGelu = 5,      // out = tanh-GELU(y) (exact bf16)
+  kEpiGatedResidualCorr = 6, // out = bf16(residual + y * gate)
 };
 
 struct GemmArgs {
-  const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes (kEpiAddBF16: bf16, lda elements)
-  const int8_t* w = nullptr;  // [n, k] int8, row stride ldw bytes (kEpiAddBF16: bf16, ldw elements)
+  const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes
+  const int8_t* w = nullptr;  // [n, k] int8, row stride ldw bytes
   int64_t m = 0, n = 0, k = 0;
   int64_t lda = 0, ldw = 0;
   int epilogue = kEpiBF16;
@@ -34,9 +36,11 @@ struct GemmArgs {
   void* out = nullptr;  // bf16 or int32 [m, ldo]
   int64_t ldo = 0;
   float* row_absmax = nullptr;              // fp32 [m], must start at 0 (values are non-negative)
-  const int32_t* group_sums = nullptr;      // int32 [m, k/group]
-  const void* correction = nullptr;         // bf16 [k/group, n]
-  int64_t groups = 0;
+  // W4A8 correction operands (kEpi*Corr): sx bf16 [m, kp], corr_t bf16 [n, kp],
+  // both zero for group index >= groups; kp a multiple of 64, at most 128.
+  const void* sx = nullptr;
+  const void* corr_t = nullptr;
+  int64_t kp = 0;
 };
 
 cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,
@@ -75,11 +79,7 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
 // corr_t[n, kp] (bf16) = correction[g, n] transposed, zero for g >= groups
 cudaError_t launch_correction_transpose(const void* corr, int64_t groups, int64_t n, int64_t kp, void* corr_t,
                                         cudaStream_t stream);
-// out[m, n] = bf16(out + sx . corr_t^T) (tcgen05 kind::f16 GEMM, K = kp), then gelu(out) when `gelu`
-cudaError_t launch_w4a8_correction(const void* sx, const void* corr_t, int64_t kp, int64_t m, int64_t n, void* out,
-                                   int64_t ldo, bool gelu, cudaStream_t stream);
-
-// K padding of the correction GEMM: groups rounded up to 64 (one 128-byte bf16 k-block)
+// K padding of the correction operands: groups rounded up to 64 (one 128-byte bf16 k-block)
 inline int64_t correction_kpad(int64_t groups) { return (groups + 63) / 64 * 64; }
 
 int num_sms(int device);
@@ -88,11 +88,6 @@ int num_sms(int device);
 // synchronously on `stream`); cudaErrorStreamCaptureUnsupported if that first
 // use happens inside a stream capture.
 cudaError_t ensure_gelu_table(cudaStream_t stream);
-
-// out = bf16(residual + y * gate) (fp32 math, one rounding), bf16 [m, n] rows.
-cudaError_t launch_gated_residual_bf16(const void* y, int64_t ldy, const void* gate, const void* residual,
-                                       int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
-                                       cudaStream_t stream);
 
 // 2-D tiled TMA descriptor (no interleave, 256-byte L2 promotion, no OOB fill);
 // false when the driver's encoder is unavailable or rejects the layout.

@@ -256,27 +256,6 @@ __global__ void gelu_table_init_kernel() {
   if (i < 65536u) g_gelu_bf16[i] = bf16_bits(gelu_tanh_exact(__uint_as_float(i << 16)));
 }
 
-// out = bf16(residual + y * gate), 8 columns per thread
-__global__ void gated_residual_bf16_kernel(const __nv_bfloat16* y, int64_t ldy, const __nv_bfloat16* __restrict__ gate,
-                                           const __nv_bfloat16* residual, int64_t ldr, __nv_bfloat16* out,
-                                           int64_t ldo, int64_t m, int64_t n) {
-  const int64_t per_row = n / 8;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= m * per_row) return;
-  const int64_t row = idx / per_row;
-  const int64_t c = (idx - row * per_row) * 8;
-  const uint4 yv = ldg_v4(y + row * ldy + c);
-  const uint4 rv = ldg_v4(residual + row * ldr + c);
-  const uint4 gv = ldg_nc_v4(gate + c);
-  const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e)
-    o[e] = pack_bf16(__fadd_rn(bf16_lo(rw[e]), __fmul_rn(bf16_lo(yw[e]), bf16_lo(gw[e]))),
-                     __fadd_rn(bf16_hi(rw[e]), __fmul_rn(bf16_hi(yw[e]), bf16_hi(gw[e]))));
-  stg_v4(out + row * ldo + c, make_uint4(o[0], o[1], o[2], o[3]));
-}
-
 }  // namespace
 
 __device__ uint16_t g_gelu_bf16[65536];
@@ -298,21 +277,6 @@ cudaError_t ensure_gelu_table(cudaStream_t stream) {
   if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
   ready[dev] = true;
   return cudaSuccess;
-}
-
-cudaError_t launch_gated_residual_bf16(const void* y, int64_t ldy, const void* gate, const void* residual,
-                                       int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
-                                       cudaStream_t stream) {
-  if (m == 0 || n == 0) return cudaSuccess;
-  if (n % 8 || ldy % 8 || ldr % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(y) & 15) ||
-      (reinterpret_cast<uintptr_t>(residual) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
-      (reinterpret_cast<uintptr_t>(gate) & 15))
-    return cudaErrorNotSupported;
-  const int64_t total = m * (n / 8);
-  gated_residual_bf16_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(y), ldy, static_cast<const __nv_bfloat16*>(gate),
-      static_cast<const __nv_bfloat16*>(residual), ldr, static_cast<__nv_bfloat16*>(out), ldo, m, n);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,

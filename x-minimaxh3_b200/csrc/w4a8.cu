@@ -1,8 +1,9 @@
 // W4A8 pieces: int4 -> int8 grid decode, ConvRot-256 rotation + row
 // quantization (emitting the asymmetric-correction operand
-// sx[m, g] = bf16(bf16(sum_{k in g} q) * bf16(xs))), and the correction itself,
-// out += sx . corr, run as a tcgen05 bf16 GEMM (gemm_i8.cu, kEpiAddBF16) against
-// the transposed, zero-padded correction matrix.
+// sx[m, g] = bf16(bf16(sum_{k in g} q) * bf16(xs))), and the transposed,
+// zero-padded correction matrix. The correction itself, out += sx . corr, is
+// accumulated on the tensor cores inside the INT8 GEMM's epilogue (gemm_i8.cu,
+// kEpi*Corr).
 //
 // Reference: comfy_kitchen W4A8 (backends/eager/w4a8_int8.py:344-363 decode;
 // backends/cuda/ops/w4a8_gemm.cu:36-90; ConvRot quantizer
@@ -271,17 +272,6 @@ cudaError_t launch_correction_transpose(const void* corr, int64_t groups, int64_
   correction_transpose_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(corr), groups, n, kp, static_cast<__nv_bfloat16*>(corr_t));
   return cudaGetLastError();
-}
-
-cudaError_t launch_w4a8_correction(const void* sx, const void* corr_t, int64_t kp, int64_t m, int64_t n, void* out,
-                                   int64_t ldo, bool gelu, cudaStream_t stream) {
-  GemmArgs g;
-  g.a = static_cast<const int8_t*>(sx);
-  g.w = static_cast<const int8_t*>(corr_t);
-  g.m = m; g.n = n; g.k = kp; g.lda = kp; g.ldw = kp;
-  g.epilogue = gelu ? kEpiAddBF16Gelu : kEpiAddBF16;
-  g.out = out; g.ldo = ldo;
-  return launch_gemm_i8(g, stream);
 }
 
 }  // namespace h3
