@@ -32,6 +32,23 @@ def test_convrot_quantize_vs_golden(golden):
     np.testing.assert_array_equal(np_(xs)[same], g["xs"][same])
 
 
+@pytest.mark.parametrize("m,k,ldx", [(1001, 3072, 3072), (37, 12288, 12288), (250, 6144, 6208), (13, 1024, 1024),
+                                     (29, 2048, 2048), (45, 4096, 4096), (7, 2304, 2304)])
+def test_convrot_quantize_shapes_vs_oracle(m, k, ldx):
+    """Every row-team size of the persistent ConvRot quantizer (K = 1024 T, T | 12), row counts that
+    leave a stage partly filled, strided rows, and a K outside that family (the per-row kernel).
+    (The correction operand it also emits is checked through the W4A8 linear and MLP tests.)"""
+    gen = torch.Generator().manual_seed(k + m)
+    xfull = randn_bf16((m, ldx), gen)
+    x = xfull[:, :k]
+    q, xs = h3b200.quantize_int8_rowwise_convrot(xfull.cuda()[:, :k], 256)
+    oq, os_ = O.quantize_int8_rowwise(O.rotate_activation(t2u(x.contiguous()), 256))
+    rows = (np_(q) == oq).all(-1)
+    assert rows.mean() >= 0.9                    # fp32 butterfly vs exact rotation: rare bf16 flips
+    assert np.abs(np_(q).astype(np.int32) - oq).max() <= 1
+    np.testing.assert_array_equal(np_(xs).reshape(-1)[rows], os_.reshape(-1)[rows])
+
+
 def test_convrot_quantize_vs_oracle_large():
     gen = torch.Generator().manual_seed(31)
     x = randn_bf16((2000, 12288), gen)

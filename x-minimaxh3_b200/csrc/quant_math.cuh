@@ -1,15 +1,14 @@
 // Row-quantization arithmetic shared by the quantizer kernels (plain and
 // ConvRot): the reference's q = clamp(rne(bf16(x / bf16(scale))), -128, 127)
 // (backends/eager/quantization.py:815-826, 857-875) evaluated with a
-// correctly rounded reciprocal and an exact-division fallback near bf16
-// rounding midpoints, on packed f32x2 / bf16x2 operations.
+// correctly rounded reciprocal (which rounds like the division on every bf16
+// operand pair; the argument is in quantize.cu), on packed f32x2 / bf16x2
+// operations.
 #pragma once
 
 #include "common.cuh"
 
 namespace h3 {
-
-constexpr uint32_t kMidWin = 8;
 
 // bf16(scale) as the divisor, with torch.finfo(bf16).tiny for a zero
 __device__ __forceinline__ float quant_divisor(float scale) {
@@ -53,38 +52,22 @@ __device__ __forceinline__ uint32_t bf16x2_clamp_i8(uint32_t b) {  // clamp both
   return r;
 }
 
-// True when fp32 bits t have their low 16 bits within kMidWin of 0x8000 (a bf16
-// rounding midpoint): (t << 16) + ((kMidWin - 0x8000) << 16) < (2 kMidWin + 1) << 16.
-__device__ __forceinline__ bool near_midpoint(uint32_t t) {
-  return t * 65536u + ((kMidWin - 0x8000u) << 16) < ((2u * kMidWin + 1u) << 16);
-}
-
-// 8 bf16 (one 16-byte vector) -> 8 int8 packed in a uint2, for r = rcp_rn(sb);
-// the same result as quant_one on each element. Per pair: packed product,
-// midpoint test, bf16x2 rounding and clamp, then round-to-nearest-even to an
-// integer by adding 1.5 * 2^23 (the integer lands in the low byte of the sum).
-__device__ __forceinline__ uint2 quant_vec8(const uint4& v, float sb, float r) {
+// 8 bf16 (one 16-byte vector) -> 8 int8 packed in a uint2, for r = rcp_rn(sb).
+// Per pair: packed product, bf16x2 rounding and clamp, then round-to-nearest-
+// even to an integer by adding 1.5 * 2^23 (the integer lands in the low byte
+// of the sum).
+__device__ __forceinline__ uint2 quant_vec8(const uint4& v, float r) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   const uint64_t r2 = f2_dup(r);
-  uint32_t b[4];
-  bool amb = false;
+  const uint64_t magic = f2_dup(12582912.0f);  // 1.5 * 2^23
+  uint32_t q[8];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     uint32_t t0, t1;
     f2_bits(f2_mul(bf16x2_to_f2(w[e]), r2), t0, t1);
-    amb |= near_midpoint(t0) | near_midpoint(t1);
-    b[e] = bf16x2_from_bits(t0, t1);
+    const uint32_t b = bf16x2_clamp_i8(bf16x2_from_bits(t0, t1));
+    f2_bits(f2_add(bf16x2_to_f2(b), magic), q[2 * e], q[2 * e + 1]);
   }
-  if (amb) {  // rare: recompute this vector's quotients with the IEEE division
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      b[e] = bf16x2_from_bits(__float_as_uint(__fdiv_rn(bf16_lo(w[e]), sb)),
-                              __float_as_uint(__fdiv_rn(bf16_hi(w[e]), sb)));
-  }
-  const uint64_t magic = f2_dup(12582912.0f);  // 1.5 * 2^23
-  uint32_t q[8];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) f2_bits(f2_add(bf16x2_to_f2(bf16x2_clamp_i8(b[e])), magic), q[2 * e], q[2 * e + 1]);
   const uint32_t lo = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
   const uint32_t hi = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
   return make_uint2(lo, hi);

@@ -8,13 +8,16 @@
 //   sb     = bf16(scale)                          scale as the bf16 operand
 //   q      = clamp(rne(bf16(x / sb)), -128, 127)
 //
-// Division. The fp32 quotient x / sb is only needed up to which side of a bf16
-// rounding midpoint it falls on. t = x * rcp(sb), with rcp correctly rounded,
-// is within 2 ulp of the correctly rounded quotient, and bf16 rounding changes
-// only where the low 16 bits of the fp32 value cross 0x8000. So t is used
-// directly unless its low 16 bits lie within kMidWin of 0x8000, in which case
-// the quotient is recomputed with an IEEE division (about 5e-5 of elements).
-// Exhaustively equal to the division on every (bf16 x, bf16 scale) pair.
+// Division. Only the bf16 rounding of the quotient x / sb matters, and
+// t = x * rcp(sb) (rcp correctly rounded, sb >= bf16(1e-30) so rcp is finite)
+// lies within 2 ulp of the exact quotient. That never moves it across a bf16
+// rounding midpoint: with x = a 2^i and sb = b 2^j for integer mantissas
+// 1 <= a, b <= 255, the ratio a / b is more than 128 fp32 ulp away from every
+// bf16 midpoint of its binade (checked for all 255 x 255 mantissa pairs: the
+// midpoints have 9 significant bits, and no ratio of two 8-bit integers comes
+// that close to one). The product therefore rounds to the same bf16 as the division, as
+// an exhaustive sweep over all finite bf16 x and all normal bf16 divisors
+// confirms (2.1e9 pairs, no exception).
 //
 // B200 layout: rows of up to 4096 elements go one warp per row (the row stays
 // in registers between the absmax and the quantize pass; no block barrier);
@@ -114,7 +117,7 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_warp_kernel(const __n
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int vi = lane + 32 * j;
-    if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant_vec8(v[j], sb, r);
+    if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant_vec8(v[j], r);
   }
   if (lane == 0) scale[row] = s;
 }
@@ -158,7 +161,7 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_vec_kernel(const __nv
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t vi = threadIdx.x + (int64_t)j * kQThreads;
-    if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant_vec8(v[j], sb, r);
+    if (vi < nvec) *reinterpret_cast<uint2*>(qr + vi * 8) = quant_vec8(v[j], r);
   }
   if (threadIdx.x == 0) scale[row] = s;
 }
