@@ -7,7 +7,7 @@ with the GELU + row-absmax epilogue; ``fc1_bf16`` / ``fc1_i32``: the same GEMM w
 the plain dequant or the int32 epilogue), ``requant`` (fc2 input quantizer with a
 given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
 ``mlp`` (the whole fused MLP call), ``mlp_w4a8`` (the config-2 W4A8 MLP call),
-``convrot`` (ConvRot-256 + row quantization of a K = 12288 bf16 input) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
+``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
 Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
 norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
 runs the kernels it needs to build its inputs, then launches the kernel under
@@ -78,9 +78,9 @@ def run(case: str, m: int, iters: int, report: bool = False):
         qo, ko = torch.empty_like(q), torch.empty_like(k)
         ms = _timed(lambda: ops.adaln_rms_rope_(q, k, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko),
                     iters, report)
-    elif case == "convrot":
+    elif case in ("convrot", "convrot_x"):
         g = torch.Generator(device=dev).manual_seed(6)
-        a = torch.randn(m, D_FFN, generator=g, device=dev).to(torch.bfloat16)
+        a = torch.randn(m, D_FFN if case == "convrot" else D_MODEL, generator=g, device=dev).to(torch.bfloat16)
         ms = _timed(lambda: ops.quantize_int8_rowwise_convrot(a, 256), iters, report)
     elif case == "mlp_w4a8":
         g = torch.Generator(device=dev).manual_seed(3)
@@ -134,7 +134,7 @@ def run(case: str, m: int, iters: int, report: bool = False):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", nargs="+", choices=["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp",
-                                                "mlp_w4a8", "convrot", "norm_rope"])
+                                                "mlp_w4a8", "convrot", "convrot_x", "norm_rope"])
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="report the mean CUDA-event time per launch")
