@@ -13,7 +13,7 @@
  *    non-zero status leaves a message in h3b200_last_error(). No C++
  *    exception crosses this boundary and nothing falls back to another path.
  *  - Activation codes follow comfy_kitchen backends/cuda/input_act_codes.h:13
- *    (0 none, 1 gelu_tanh); dtype codes follow eager/quantization.py:34-40
+ *    (0 none, 1 gelu_tanh, 2 swiglu); dtype codes follow eager/quantization.py:34-40
  *    (0 fp32, 1 fp16, 2 bf16).
  */
 #ifndef H3B200_H_
@@ -41,7 +41,7 @@ enum {
   H3B200_ERR_DEVICE = 4       /* a kernel recorded a device-side failure (bounded wait expired) */
 };
 
-enum { H3B200_ACT_NONE = 0, H3B200_ACT_GELU_TANH = 1 };
+enum { H3B200_ACT_NONE = 0, H3B200_ACT_GELU_TANH = 1, H3B200_ACT_SWIGLU = 2 };
 enum { H3B200_DTYPE_F32 = 0, H3B200_DTYPE_F16 = 1, H3B200_DTYPE_BF16 = 2, H3B200_DTYPE_I32 = 3 };
 
 /* Library identification and diagnostics. */
@@ -56,9 +56,20 @@ H3B200_API int h3b200_device_status(int device, unsigned int* status, int clear)
  * Elementwise pre-quantization activation on bf16 (y may alias x).
  * Replaces apply_input_act (backends/_activations.py:40-53; gelu_tanh =
  * torch.nn.functional.gelu(approximate="tanh")); bit-identical to the
- * reference's CPU result for every bf16 input.
+ * reference's CPU result for every bf16 input. act = H3B200_ACT_SWIGLU is
+ * row-structured and goes through h3b200_swiglu.
  */
 H3B200_API int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act, h3b200_stream_t stream);
+
+/*
+ * SwiGLU input activation: y[m, k] = silu(x[:, :k]) * x[:, k:2k] (bf16).
+ * Replaces apply_input_act(x, "swiglu") (backends/_activations.py:40-53:
+ * gate, up = x.chunk(2, -1); silu(gate).mul_(up)); bit-identical to the
+ * reference's CPU result (silu exact on every bf16 input, the product rounded
+ * once). x rows are [gate | up] at stride ldx >= 2k; y rows at stride ldy >= k.
+ */
+H3B200_API int h3b200_swiglu(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, int64_t k,
+                             h3b200_stream_t stream);
 
 /*
  * Per-token absmax INT8 quantizer.
@@ -67,6 +78,9 @@ H3B200_API int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act
  * kernel backends/cuda/ops/int8_linear.cu:157-200).
  * x: bf16 [m, k] with row stride ldx elements; act applied to x first
  * (backends/_activations.py:40-53). q: int8 [m, k] contiguous; scale: fp32 [m].
+ * For act = H3B200_ACT_SWIGLU the rows of x are [gate | up], 2k wide
+ * (ldx >= 2k), and the activated k-wide row is quantized; the same holds for
+ * every entry point below that takes an act code, except the fused MLPs.
  */
 H3B200_API int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ldx, int act, int8_t* q,
                                  float* scale, h3b200_stream_t stream);

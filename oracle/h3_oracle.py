@@ -19,6 +19,10 @@ documented where they occur:
   uses a double-precision tanh rounded to fp32 plus the same saturation; the
   golden table ``tests/golden/gelu_tanh_bf16_all.npz`` pins it on all 65,536
   bf16 inputs.
+* ``torch.nn.functional.silu`` (the gate of ``input_act="swiglu"``) on CPU
+  evaluates ``x / (1 + exp(-x))`` in fp32 with SLEEF ``expf_u10``. The oracle
+  uses a double-precision exp rounded to fp32; ``tests/golden/silu_bf16_all.npz``
+  pins it on all 65,536 bf16 inputs.
 * ``torch.nn.functional.rms_norm`` sums x^2 in fp32 in an ISA-dependent order.
   The oracle sums in float64 and rounds the mean to fp32 once (error below the
   reference's own), so rare last-bit differences against the reference remain
@@ -35,6 +39,9 @@ __all__ = [
     "quantize_int8_rowwise",
     "quantize_int8_rowwise_given_absmax",
     "gelu_tanh_bf16",
+    "silu_bf16",
+    "swiglu_bf16",
+    "apply_input_act",
     "int8_matmul_accumulate",
     "dequant_epilogue",
     "int8_linear",
@@ -162,6 +169,44 @@ def gelu_tanh_bf16(x_bf16: np.ndarray) -> np.ndarray:
     return f32_to_bf16(out)
 
 
+def silu_bf16(x_bf16: np.ndarray) -> np.ndarray:
+    """SiLU of bf16 values, returned as bf16 bits.
+
+    ``apply_input_act(x, "swiglu")`` backends/_activations.py:50-52 calls
+    ``torch.nn.functional.silu(gate)``; on a bf16 CPU tensor torch 2.11 (ATen silu
+    kernel, reduced-float path) computes ``x / (1 + exp(-x))`` in fp32 and stores
+    bf16. Restated with a double exp rounded to fp32."""
+    x = bf16_to_f32(x_bf16)
+    with np.errstate(all="ignore"):
+        e = np.exp(-x.astype(np.float64)).astype(np.float32)
+        d = (F32(1.0) + e).astype(np.float32)
+        r = (x / d).astype(np.float32)
+    return f32_to_bf16(r)
+
+
+def swiglu_bf16(x_bf16: np.ndarray) -> np.ndarray:
+    """``silu(gate).mul_(up)`` on the ``[gate | up]`` halves of the last dim
+    (backends/_activations.py:50-52): bf16 silu, then the bf16 product (exact in
+    fp32, rounded once). Returns bf16 bits, half as wide."""
+    x = np.asarray(x_bf16, np.uint16)
+    k = x.shape[-1] // 2
+    s = bf16_to_f32(silu_bf16(x[..., :k]))
+    u = bf16_to_f32(x[..., k:2 * k])
+    return f32_to_bf16((s * u).astype(np.float32))
+
+
+def apply_input_act(x_bf16: np.ndarray, input_act) -> np.ndarray:
+    """``apply_input_act`` backends/_activations.py:40-53 on bf16 bits."""
+    x = np.asarray(x_bf16, np.uint16)
+    if input_act in (None, "none"):
+        return x
+    if input_act == "gelu_tanh":
+        return gelu_tanh_bf16(x)
+    if input_act == "swiglu":
+        return swiglu_bf16(x)
+    raise ValueError(f"unsupported input_act {input_act!r}")
+
+
 # ---------------------------------------------------------------------------
 # INT8 GEMM + dequant epilogue
 # ---------------------------------------------------------------------------
@@ -209,11 +254,7 @@ def int8_linear(x_bf16, w_i8, w_scale, bias_bf16=None, input_act=None):
 
     eager/quantization.py:971-1056: optional activation on the bf16 input,
     per-row quantization, int32 GEMM, dequant epilogue. Returns bf16 bits."""
-    x = np.asarray(x_bf16, np.uint16)
-    if input_act == "gelu_tanh":
-        x = gelu_tanh_bf16(x)
-    elif input_act not in (None, "none"):
-        raise ValueError(f"unsupported input_act {input_act!r}")
+    x = apply_input_act(x_bf16, input_act)
     q, s = quantize_int8_rowwise(x)
     acc = int8_matmul_accumulate(q, w_i8)
     return dequant_epilogue(acc, s, w_scale, bias_bf16)

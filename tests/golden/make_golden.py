@@ -31,6 +31,7 @@ def b16(t: torch.Tensor) -> np.ndarray:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", nargs="*", default=None, help="write only these fixtures (names without .npz)")
     args = ap.parse_args()
     ref = os.path.abspath(args.reference)
     sys.path.insert(0, os.path.join(ref, "backends", "turbo", "vendor"))
@@ -174,7 +175,31 @@ def main() -> None:
         "acc": acc4.numpy(), "y_eager": b16(y4),
     }
 
+    # 7. SiLU on every bf16 bit pattern (the swiglu gate, up = 1 so the product is exact).
+    ones = torch.ones(65536, dtype=torch.bfloat16)
+    out["silu_bf16_all"] = {"y": b16(apply_input_act(torch.cat([allb, ones]).reshape(1, -1), "swiglu").reshape(-1))}
+
+    # 8. SwiGLU input activation into an INT8 linear (x rows [gate | up], K = 512, N = 192),
+    #    plain and ConvRot (weights rotated offline by the reference's own helper).
+    gs_ = torch.Generator().manual_seed(6)
+    xs_ = (torch.randn(64, 1024, generator=gs_) * 2).to(torch.bfloat16)
+    wsw = (torch.randn(192, 512, generator=gs_) * 0.02).to(torch.bfloat16)
+    swq, sws = eq.quantize_int8_rowwise(wsw)
+    sws = sws.reshape(-1)
+    act = apply_input_act(xs_, "swiglu")
+    aq, as_ = eq.quantize_int8_rowwise(act)
+    ysw = eq.int8_linear(xs_, swq, sws, None, torch.bfloat16, input_act="swiglu")
+    cwq, cws = eq.quantize_int8_convrot_weight(wsw, 256)
+    cws = cws.reshape(-1)
+    ysc = eq.int8_linear(xs_, cwq, cws, None, torch.bfloat16, convrot=True, convrot_groupsize=256, input_act="swiglu")
+    out["swiglu_linear"] = {
+        "x": b16(xs_), "wq": swq.numpy(), "ws": sws.numpy(), "act": b16(act), "aq": aq.numpy(), "as": as_.numpy(),
+        "y": b16(ysw), "wq_convrot": cwq.numpy(), "ws_convrot": cws.numpy(), "y_convrot": b16(ysc),
+    }
+
     for name, arrays in out.items():
+        if args.only is not None and name not in args.only:
+            continue
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **arrays)
         print(f"wrote {path} ({os.path.getsize(path)} bytes)")

@@ -174,3 +174,29 @@ def test_torch_port_matches_golden(golden):
                               _t(g["scale"]), _t(g["shift"]))
     np.testing.assert_array_equal(_u(qo), g["q_out"])
     np.testing.assert_array_equal(_u(ko), g["k_out"])
+
+
+def test_silu_all_bf16_bit_exact(golden):
+    ref = golden("silu_bf16_all")["y"]
+    allx = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    mine = O.silu_bf16(allx)
+    finite = np.isfinite(O.bf16_to_f32(allx))
+    assert int((mine[finite] != ref[finite]).sum()) == 0
+    assert np.isnan(O.bf16_to_f32(mine[np.isnan(O.bf16_to_f32(allx))])).all()
+
+
+def test_swiglu_linear_bit_exact(golden):
+    """SwiGLU input activation: the activated rows, their quantization and the plain
+    INT8 linear are bit-exact; the ConvRot variant (bf16 rotation matmul in the
+    reference) agrees within the float tolerance."""
+    g = golden("swiglu_linear")
+    a = O.apply_input_act(g["x"], "swiglu")
+    np.testing.assert_array_equal(a, g["act"])
+    q, s = O.quantize_int8_rowwise(a)
+    np.testing.assert_array_equal(q, g["aq"])
+    np.testing.assert_array_equal(s, g["as"])
+    np.testing.assert_array_equal(O.int8_linear(g["x"], g["wq"], g["ws"], input_act="swiglu"), g["y"])
+    qc, sc = O.quantize_int8_rowwise(O.rotate_activation(a, 256))
+    yc = O.dequant_epilogue(O.int8_matmul_accumulate(qc, g["wq_convrot"]), sc, g["ws_convrot"])
+    yf, rf = O.bf16_to_f32(yc).astype(np.float64), O.bf16_to_f32(g["y_convrot"]).astype(np.float64)
+    assert np.linalg.norm(yf - rf) / np.linalg.norm(rf) <= 1e-2 and np.abs(yf - rf).max() <= 2e-2

@@ -53,6 +53,9 @@ struct Carver {
 
 }  // namespace
 
+// Raw input columns per activated column: 2 for SwiGLU ([gate | up] rows), else 1.
+static int64_t act_width(int act) { return act == H3B200_ACT_SWIGLU ? 2 : 1; }
+
 extern "C" {
 
 const char* h3b200_version(void) { return "h3b200 0.1.0 (sm_100a)"; }
@@ -76,16 +79,25 @@ int h3b200_device_status(int device, unsigned int* status, int clear) {
 
 int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act, h3b200_stream_t stream) {
   if (n < 0) return fail(H3B200_ERR_INVALID, "apply_input_act: negative size");
+  if (act == H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "apply_input_act: swiglu halves each row; use h3b200_swiglu");
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "apply_input_act: unsupported act code %d", act);
   if (n > 0 && (x == nullptr || y == nullptr)) return fail(H3B200_ERR_INVALID, "apply_input_act: NULL pointer");
   if (n > (1ll << 40)) return fail(H3B200_ERR_UNSUPPORTED, "apply_input_act: n too large");
   return from_cuda(h3::launch_apply_act(x, y, n, act, S(stream)), "apply_input_act");
 }
 
+int h3b200_swiglu(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, int64_t k, h3b200_stream_t stream) {
+  if (m < 0 || k < 0 || ldx < 2 * k || ldy < k) return fail(H3B200_ERR_INVALID, "swiglu: bad shape m=%lld k=%lld ldx=%lld ldy=%lld (ldx >= 2k, ldy >= k)", (long long)m, (long long)k, (long long)ldx, (long long)ldy);
+  if (m == 0 || k == 0) return H3B200_OK;
+  if (x == nullptr || y == nullptr) return fail(H3B200_ERR_INVALID, "swiglu: NULL pointer");
+  if (m * k > (1ll << 40)) return fail(H3B200_ERR_UNSUPPORTED, "swiglu: too large");
+  return from_cuda(h3::launch_swiglu_rows(x, ldx, y, ldy, m, k, S(stream)), "swiglu");
+}
+
 int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ldx, int act, int8_t* q, float* scale,
                                  h3b200_stream_t stream) {
-  if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: bad shape m=%lld k=%lld ldx=%lld", (long long)m, (long long)k, (long long)ldx);
-  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: unsupported act code %d", act);
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: unsupported act code %d", act);
+  if (m < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: bad shape m=%lld k=%lld ldx=%lld (act %d reads %lld columns)", (long long)m, (long long)k, (long long)ldx, act, (long long)(k * act_width(act)));
   if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: NULL pointer");
   if (m > 0x7fffffffll) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise: m too large");
   return from_cuda(h3::launch_quantize_rows(x, ldx, m, k, act, nullptr, q, scale, S(stream)), "quantize_int8_rowwise");
@@ -165,7 +177,7 @@ int64_t h3b200_int8_linear_workspace_bytes(int64_t m, int64_t k) {
 int h3b200_int8_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale, int64_t w_scale_numel,
                        const void* bias, int act, void* out, int64_t m, int64_t n, int64_t k, void* workspace,
                        int64_t workspace_bytes, h3b200_stream_t stream) {
-  if (m < 0 || n < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "int8_linear: bad shape");
+  if (m < 0 || n < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "int8_linear: bad shape");
   if (m == 0 || n == 0) return H3B200_OK;
   if (workspace == nullptr || workspace_bytes < h3b200_int8_linear_workspace_bytes(m, k)) return fail(H3B200_ERR_INVALID, "int8_linear: workspace too small (need %lld bytes)", (long long)h3b200_int8_linear_workspace_bytes(m, k));
   Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
@@ -250,10 +262,10 @@ int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const float* s_rel,
 
 int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, int64_t k, int64_t ldx, int64_t group_size,
                                          int act, int8_t* q, float* scale, h3b200_stream_t stream) {
-  if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: bad shape");
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: unsupported act %d", act);
+  if (m < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: bad shape");
   if (group_size != 256) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_convrot: only group_size 256 is built (got %lld)", (long long)group_size);
   if (k % 256) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: ConvRot group size 256 does not divide input features %lld", (long long)k);
-  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: unsupported act %d", act);
   if (m == 0) return H3B200_OK;
   if (!x || !q || !scale) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: NULL pointer");
   return from_cuda(h3::launch_quantize_convrot(x, ldx, m, k, act, q, scale, nullptr, 0, 0, S(stream)), "quantize_int8_rowwise_convrot");
@@ -268,7 +280,8 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
                             const void* correction, int64_t group_size, int64_t convrot_group, int act, void* out,
                             int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                             h3b200_stream_t stream) {
-  if (m < 0 || n < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: bad shape");
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: unsupported act code %d", act);
+  if (m < 0 || n < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: bad shape");
   if (group_size < 4 || k % 16 || k % group_size || k % convrot_group || (16 % group_size && group_size % 16))
     return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: K=%lld must be divisible by 16, group_size=%lld, and convrot_groupsize=%lld", (long long)k, (long long)group_size, (long long)convrot_group);
   if (convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: only convrot_groupsize 256 is built");

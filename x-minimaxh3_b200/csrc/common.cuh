@@ -96,6 +96,42 @@ extern __device__ uint16_t g_gelu_bf16[65536];
 __device__ __forceinline__ uint32_t gelu_bf16_bits(uint32_t xbits16) { return g_gelu_bf16[xbits16 & 0xFFFFu]; }
 
 // ---------------------------------------------------------------------------
+// SiLU on a bf16 input, bit-identical to the reference's CPU result.
+//
+// apply_input_act(x, "swiglu") (backends/_activations.py:40-53) evaluates
+// torch.nn.functional.silu(gate) on bf16 CPU tensors as x / (1 + exp(-x)) in
+// fp32 (ATen silu kernel, reduced-float path) and stores bf16. The result
+// here uses the same rounded operations; exp comes from expf (documented max
+// error 2 ulp) and the bf16 result is accepted when a +-4 ulp band around it
+// rounds to one bf16 value (x / (1 + e) is monotone in e), otherwise exp is
+// recomputed in double precision and rounded to fp32 (the correctly rounded
+// value; it matches the reference on all 65,536 inputs).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float silu_exact(float x) {
+  const float e = expf(-x);
+  const float r = __fdiv_rn(x, __fadd_rn(1.0f, e));
+  const float de = fabsf(e) * 4.8e-7f + 1e-45f;
+  const float ra = __fdiv_rn(x, __fadd_rn(1.0f, __fsub_rn(e, de)));
+  const float rb = __fdiv_rn(x, __fadd_rn(1.0f, __fadd_rn(e, de)));
+  if (bf16_bits(ra) == bf16_bits(rb)) return r;
+  const float ec = (float)exp(-(double)x);
+  return __fdiv_rn(x, __fadd_rn(1.0f, ec));
+}
+
+// Exact SiLU of every bf16 input, filled once per device by ensure_act_table().
+extern __device__ uint16_t g_silu_bf16[65536];
+
+__device__ __forceinline__ uint32_t silu_bf16_bits(uint32_t xbits16) { return g_silu_bf16[xbits16 & 0xFFFFu]; }
+
+// SwiGLU of packed bf16 pairs (gate g, up u): bf16(bf16(silu(g)) * u) per half,
+// torch's silu(gate).mul_(up); a product of two bf16 values is exact in fp32,
+// so it is rounded once.
+__device__ __forceinline__ uint32_t swiglu_bf16x2(uint32_t g, uint32_t u) {
+  const uint32_t s = silu_bf16_bits(g) | (silu_bf16_bits(g >> 16) << 16);
+  return pack_bf16(__fmul_rn(bf16_lo(s), bf16_lo(u)), __fmul_rn(bf16_hi(s), bf16_hi(u)));
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier (shared::cta) with bounded waits
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

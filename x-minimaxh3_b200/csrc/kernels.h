@@ -47,6 +47,8 @@ cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, c
                                           const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,
                                           int64_t n, cudaStream_t stream);
 cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream);
+// Row quantizer of the activated row (width k; for act = SwiGLU the raw row is
+// [gate | up], 2 k wide, at stride ldx >= 2 k).
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
                                  int8_t* q, float* scale, cudaStream_t stream);
 
@@ -88,6 +90,11 @@ int num_sms(int device);
 // synchronously on `stream`); cudaErrorStreamCaptureUnsupported if that first
 // use happens inside a stream capture.
 cudaError_t ensure_gelu_table(cudaStream_t stream);
+// The same for the table of `act` (GELU or SiLU; no-op for other codes).
+cudaError_t ensure_act_table(int act, cudaStream_t stream);
+// y[m, k] = silu(x[:, :k]) * x[:, k:2k] per row (bf16)
+cudaError_t launch_swiglu_rows(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, int64_t k,
+                               cudaStream_t stream);
 
 // 2-D tiled TMA descriptor (no interleave, 256-byte L2 promotion, no OOB fill);
 // false when the driver's encoder is unavailable or rejects the layout.

@@ -62,6 +62,29 @@ __device__ __forceinline__ void apply_act_vec(uint4& v, int act) {
   for (int e = 0; e < 4; ++e) w[e] = gelu_bf16_bits(w[e]) | (gelu_bf16_bits(w[e] >> 16) << 16);
 }
 
+// The 8 activated values at vector index vi of an activated row of width k:
+// the row itself for elementwise activations; for SwiGLU the raw row is
+// [gate | up], 2 k wide, and the value is silu(gate) * up.
+__device__ __forceinline__ uint4 load_act_vec(const __nv_bfloat16* xr, int64_t k, int64_t vi, int act) {
+  uint4 v = ldg_nc_v4(xr + vi * 8);
+  if (act == H3B200_ACT_SWIGLU) {
+    const uint4 u = ldg_nc_v4(xr + k + vi * 8);
+    v = make_uint4(swiglu_bf16x2(v.x, u.x), swiglu_bf16x2(v.y, u.y), swiglu_bf16x2(v.z, u.z), swiglu_bf16x2(v.w, u.w));
+  } else {
+    apply_act_vec(v, act);
+  }
+  return v;
+}
+
+// One activated value (scalar paths).
+__device__ __forceinline__ float act_value(const __nv_bfloat16* xr, int64_t k, int64_t i, int act) {
+  if (act == H3B200_ACT_SWIGLU) {
+    const float s = __uint_as_float(silu_bf16_bits(__bfloat16_as_ushort(xr[i])) << 16);
+    return bf16_round(__fmul_rn(s, __bfloat162float(xr[k + i])));
+  }
+  return act_apply(__bfloat162float(xr[i]), act);
+}
+
 __device__ __forceinline__ float row_scale(float rowmax) { return fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f); }
 
 __device__ __forceinline__ float block_max(float v, float* red) {
@@ -92,12 +115,7 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_warp_kernel(const __n
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int vi = lane + 32 * j;
-    v[j] = vi < nvec ? ldg_nc_v4(xr + vi * 8) : make_uint4(0, 0, 0, 0);
-  }
-  if (act != H3B200_ACT_NONE) {
-#pragma unroll
-    for (int j = 0; j < VPL; ++j)
-      if (lane + 32 * j < nvec) apply_act_vec(v[j], act);
+    v[j] = vi < nvec ? load_act_vec(xr, k, vi, act) : make_uint4(0, 0, 0, 0);
   }
   float rowmax;
   if (GIVEN_ABSMAX) {
@@ -138,12 +156,7 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_vec_kernel(const __nv
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t vi = threadIdx.x + (int64_t)j * kQThreads;
-    v[j] = vi < nvec ? ldg_nc_v4(xr + vi * 8) : make_uint4(0, 0, 0, 0);
-  }
-  if (act != H3B200_ACT_NONE) {
-#pragma unroll
-    for (int j = 0; j < VPT; ++j)
-      if (threadIdx.x + (int64_t)j * kQThreads < nvec) apply_act_vec(v[j], act);
+    v[j] = vi < nvec ? load_act_vec(xr, k, vi, act) : make_uint4(0, 0, 0, 0);
   }
   float rowmax;
   if (GIVEN_ABSMAX) {
@@ -181,12 +194,12 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_scalar_kernel(const _
     rowmax = absmax_in[row];
   } else {
     float amax = 0.0f;
-    for (int64_t i = threadIdx.x; i < k; i += kQThreads) amax = fmaxf(amax, fabsf(act_apply(__bfloat162float(xr[i]), act)));
+    for (int64_t i = threadIdx.x; i < k; i += kQThreads) amax = fmaxf(amax, fabsf(act_value(xr, k, i, act)));
     rowmax = block_max(amax, red);
   }
   const float s = row_scale(rowmax);
   const float sb = quant_divisor(s);
-  for (int64_t i = threadIdx.x; i < k; i += kQThreads) q[row * k + i] = quant_one(act_apply(__bfloat162float(xr[i]), act), sb);
+  for (int64_t i = threadIdx.x; i < k; i += kQThreads) q[row * k + i] = quant_one(act_value(xr, k, i, act), sb);
   if (threadIdx.x == 0) scale[row] = s;
 }
 
@@ -225,6 +238,15 @@ __global__ void apply_act_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloa
   if (i < n) y[i] = __float2bfloat16_rn(act_apply(__bfloat162float(x[i]), act));
 }
 
+// y[m, k] = silu(x[:, :k]) * x[:, k:2k] (bf16, the reference's two roundings)
+__global__ void swiglu_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y,
+                                   int64_t ldy, int64_t m, int64_t k) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m * k) return;
+  const int64_t row = i / k, col = i - row * k;
+  y[row * ldy + col] = __float2bfloat16_rn(act_value(x + row * ldx, k, col, H3B200_ACT_SWIGLU));
+}
+
 // out = bf16(residual + bf16(float(acc) * (xs[row] * ws[col])) * gate[col]); 8 columns per thread.
 __global__ void dequant_gated_residual_kernel(const int32_t* __restrict__ acc, const float* __restrict__ xs,
                                               const float* __restrict__ ws, const __nv_bfloat16* __restrict__ gate,
@@ -254,33 +276,42 @@ __global__ void dequant_gated_residual_kernel(const int32_t* __restrict__ acc, c
   stg_v4(out + row * ldo + c, make_uint4(o[0], o[1], o[2], o[3]));
 }
 
-__global__ void gelu_table_init_kernel() {
+__global__ void act_table_init_kernel(int act) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < 65536u) g_gelu_bf16[i] = bf16_bits(gelu_tanh_exact(__uint_as_float(i << 16)));
+  if (i >= 65536u) return;
+  const float x = __uint_as_float(i << 16);
+  if (act == H3B200_ACT_SWIGLU)
+    g_silu_bf16[i] = bf16_bits(silu_exact(x));
+  else
+    g_gelu_bf16[i] = bf16_bits(gelu_tanh_exact(x));
 }
 
 }  // namespace
 
 __device__ uint16_t g_gelu_bf16[65536];
+__device__ uint16_t g_silu_bf16[65536];
 
-cudaError_t ensure_gelu_table(cudaStream_t stream) {
+cudaError_t ensure_act_table(int act, cudaStream_t stream) {
+  if (act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return cudaSuccess;
   static std::mutex mu;
-  static bool ready[64] = {false};
+  static bool ready[64][3] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
-  if (ready[dev]) return cudaSuccess;
+  if (ready[dev][act]) return cudaSuccess;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if ((e = cudaStreamIsCapturing(stream, &cap)) != cudaSuccess) return e;
   if (cap != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
-  gelu_table_init_kernel<<<256, 256, 0, stream>>>();
+  act_table_init_kernel<<<256, 256, 0, stream>>>(act);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return e;
-  ready[dev] = true;
+  ready[dev][act] = true;
   return cudaSuccess;
 }
+
+cudaError_t ensure_gelu_table(cudaStream_t stream) { return ensure_act_table(H3B200_ACT_GELU_TANH, stream); }
 
 cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,
                                           const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,
@@ -297,8 +328,20 @@ cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, c
   return cudaGetLastError();
 }
 
+cudaError_t launch_swiglu_rows(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, int64_t k,
+                               cudaStream_t stream) {
+  if (m == 0 || k == 0) return cudaSuccess;
+  const cudaError_t e = ensure_act_table(H3B200_ACT_SWIGLU, stream);
+  if (e != cudaSuccess) return e;
+  const int64_t n = m * k;
+  swiglu_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), ldx,
+                                                                     static_cast<__nv_bfloat16*>(y), ldy, m, k);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
+  if (act == H3B200_ACT_SWIGLU) return cudaErrorNotSupported;  // row-structured: launch_swiglu_rows
   if (act == H3B200_ACT_GELU_TANH) {
     const cudaError_t e = ensure_gelu_table(stream);
     if (e != cudaSuccess) return e;
@@ -311,8 +354,8 @@ cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStr
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
                                  int8_t* q, float* scale, cudaStream_t stream) {
   if (m == 0) return cudaSuccess;
-  if (act == H3B200_ACT_GELU_TANH) {
-    const cudaError_t e = ensure_gelu_table(stream);
+  {
+    const cudaError_t e = ensure_act_table(act, stream);
     if (e != cudaSuccess) return e;
   }
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);

@@ -132,6 +132,14 @@ __global__ void __launch_bounds__(kCvThreadsMax) quantize_convrot_kernel(const _
       const __nv_bfloat16* src = x + row * ldx + (int64_t)g * 256 + 16 * li;
       raw[0] = ldg_nc_v4(src);
       raw[1] = ldg_nc_v4(src + 8);
+      if (act == H3B200_ACT_SWIGLU) {  // [gate | up] raw row: silu(gate) * up, exact bf16
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint4 u = ldg_nc_v4(src + k + 8 * hh);
+          raw[hh] = make_uint4(swiglu_bf16x2(raw[hh].x, u.x), swiglu_bf16x2(raw[hh].y, u.y),
+                               swiglu_bf16x2(raw[hh].z, u.z), swiglu_bf16x2(raw[hh].w, u.w));
+        }
+      }
     }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -547,12 +555,14 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
     return cudaErrorNotSupported;
   if (sx != nullptr && (sum_group < 16 || sum_group > 256 || 256 % sum_group || kp < k / sum_group))
     return cudaErrorNotSupported;
-  if (act == H3B200_ACT_GELU_TANH) {
-    const cudaError_t e = ensure_gelu_table(stream);
+  {
+    const cudaError_t e = ensure_act_table(act, stream);
     if (e != cudaSuccess) return e;
   }
   const int64_t rppw = k / 1536;
-  if (k % 1536 == 0 && (rppw == 2 || rppw == 4 || rppw == 8)) {
+  // the persistent kernel's stages hold one activated-width row, so SwiGLU rows
+  // ([gate | up], twice as wide) take the per-row kernel
+  if (k % 1536 == 0 && (rppw == 2 || rppw == 4 || rppw == 8) && act != H3B200_ACT_SWIGLU) {
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64][9] = {};

@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libh3b200.so")
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_LAUNCH, ERR_DEVICE = 0, 1, 2, 3, 4
-ACT_NONE, ACT_GELU_TANH = 0, 1
+ACT_NONE, ACT_GELU_TANH, ACT_SWIGLU = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_I32 = 0, 1, 2, 3
 
 _p = ctypes.c_void_p
@@ -29,6 +29,7 @@ SIGNATURES = {
     "h3b200_last_error": (ctypes.c_char_p, []),
     "h3b200_device_status": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint), _i32]),
     "h3b200_apply_input_act": (_i32, [_p, _p, _i64, _i32, _p]),
+    "h3b200_swiglu": (_i32, [_p, _i64, _p, _i64, _i64, _i64, _p]),
     "h3b200_quantize_int8_rowwise": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _p, _p]),
     "h3b200_quantize_int8_rowwise_absmax": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p, _p]),
     "h3b200_int8_mm": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p]),

@@ -36,11 +36,11 @@ __all__ = [
     "input_act_code",
 ]
 
-_ACT = {None: _lib.ACT_NONE, "none": _lib.ACT_NONE, "gelu_tanh": _lib.ACT_GELU_TANH}
+_ACT = {None: _lib.ACT_NONE, "none": _lib.ACT_NONE, "gelu_tanh": _lib.ACT_GELU_TANH, "swiglu": _lib.ACT_SWIGLU}
 
 
 def input_act_code(input_act) -> int:
-    """Kernel code for ``input_act`` (backends/_activations.py:19-33); swiglu is not built."""
+    """Kernel code for ``input_act`` (backends/_activations.py:19-33)."""
     try:
         return _ACT[input_act]
     except KeyError:
@@ -73,15 +73,35 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+def input_act_width(input_act) -> int:
+    """Raw input columns per activated column (backends/_activations.py:36-38): 2 for swiglu."""
+    return 2 if input_act_code(input_act) == _lib.ACT_SWIGLU else 1
+
+
+def _act_k(x: torch.Tensor, input_act) -> int:
+    """Width of the activated row of x."""
+    w = input_act_width(input_act)
+    if x.shape[-1] % w:
+        raise ValueError(f"swiglu needs an even last dimension ([gate | up]), got {x.shape[-1]}")
+    return x.shape[-1] // w
+
+
 def apply_input_act(x: torch.Tensor, input_act) -> torch.Tensor:
     """Pre-quantization activation (backends/_activations.py:40-53), bit-identical to
-    the reference's CPU ``gelu(approximate="tanh")`` for every bf16 input."""
+    the reference's CPU result for every bf16 input: ``gelu(approximate="tanh")``, or
+    for ``swiglu`` ``silu(gate) * up`` of the ``[gate | up]`` halves of the last dim."""
     _need_cuda(x)
     code = input_act_code(input_act)
     if code == _lib.ACT_NONE:
         return x
     if x.dtype != torch.bfloat16:
         raise ValueError("apply_input_act expects bf16")
+    if code == _lib.ACT_SWIGLU:
+        k = _act_k(x, input_act)
+        x2, ldx = _rows(x)
+        y = torch.empty((x2.shape[0], k), dtype=torch.bfloat16, device=x.device)
+        _lib.call("h3b200_swiglu", x2.data_ptr(), ldx, y.data_ptr(), k, x2.shape[0], k, _stream(x))
+        return y.reshape(*x.shape[:-1], k)
     xc = x.contiguous()
     y = torch.empty_like(xc)
     _lib.call("h3b200_apply_input_act", xc.data_ptr(), y.data_ptr(), xc.numel(), code, _stream(x))
@@ -104,13 +124,14 @@ def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int | None = 0, 
     _need_cuda(x)
     if x.dtype != torch.bfloat16:
         raise ValueError(f"quantize_int8_rowwise expects bf16, got {x.dtype}")
+    k = _act_k(x, input_act)
     x2, ldx = _rows(x)
-    m, k = x2.shape
+    m = x2.shape[0]
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
     _lib.call("h3b200_quantize_int8_rowwise", x2.data_ptr(), m, k, ldx, input_act_code(input_act), q.data_ptr(),
               s.data_ptr(), _stream(x))
-    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+    return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
 
 
 def quantize_int8_rowwise_absmax(x: torch.Tensor, absmax: torch.Tensor):
@@ -245,15 +266,16 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         out_dtype = torch.bfloat16
     if out_dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
         raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
-    if x.shape[-1] != weight.shape[-1]:
-        raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {weight.shape[-1]}")
+    k = _act_k(x, input_act)  # swiglu: x rows are [gate | up], 2 K wide
+    if k != weight.shape[-1]:
+        raise ValueError(f"Input and weight inner dimensions must match, got {k} and {weight.shape[-1]}")
     act = input_act_code(input_act)
     n = weight.shape[0]
     if convrot:
         xq, xs = quantize_int8_rowwise_convrot(x, convrot_groupsize, input_act)
         return int8_linear_prequantized(xq, xs, weight, weight_scale, bias, out_dtype)
     x2, ldx = _rows(x)
-    m, k = x2.shape
+    m = x2.shape[0]
     w = weight.contiguous()
     ws = _weight_scale(weight_scale, n, x.device)
     b = None if bias is None else bias.to(device=x.device, dtype=torch.bfloat16).contiguous()
@@ -471,13 +493,14 @@ def quantize_int8_rowwise_convrot(x: torch.Tensor, convrot_groupsize: int = 256,
     _need_cuda(x)
     if x.dtype != torch.bfloat16:
         raise ValueError("x must be bf16")
+    k = _act_k(x, input_act)
     x2, ldx = _rows(x)
-    m, k = x2.shape
+    m = x2.shape[0]
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
     _lib.call("h3b200_quantize_int8_rowwise_convrot", x2.data_ptr(), m, k, ldx, convrot_groupsize,
               input_act_code(input_act), q.data_ptr(), s.data_ptr(), _stream(x))
-    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+    return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
 
 
 def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, s_channel: torch.Tensor,
@@ -500,8 +523,8 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
         raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
     n, kh = qdata.shape
     k = kh * 2
-    if x.shape[-1] != k:
-        raise ValueError(f"Input K={x.shape[-1]} does not match qdata K={k}")
+    if _act_k(x, input_act) != k:
+        raise ValueError(f"Input K={_act_k(x, input_act)} (after input_act) does not match qdata K={k}")
     if grid is None:
         grid = dequant_int4_grouped_to_int8(qdata, s_rel, group_size)
     groups = k // group_size
