@@ -121,7 +121,8 @@ H3B200_API int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_
  * exposed so each stage can be launched and timed on its own.
  * epilogue: 0 int32 out; 1 bf16 dequant (+bias); 2 dequant -> tanh-GELU -> bf16
  * out with the per-row absmax of |out| atomically max-reduced into row_absmax
- * (fp32 [m], caller zero-fills); 3 out = bf16(residual + dequant * gate).
+ * (fp32 [m], caller zero-fills); 3 out = bf16(residual + y * gate) with
+ * y = dequant, or bf16(dequant + bias) when bias is given.
  * Arithmetic as h3b200_int8_linear_prequantized / h3b200_fused_gated_mlp.
  * Replaces the reference's CUTLASS EVT GEMM (backends/cuda/ops/cutlass_gemm_int8.cu:242-324)
  * and the experimental fc2 + dequant + gate + residual Triton epilogue
@@ -249,8 +250,8 @@ H3B200_API int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, in
  * grid: int8 [n, k] decoded weight (h3b200_dequant_int4_grouped_to_int8);
  * s_channel: fp32 [n]; correction: bf16 [k/group, n] or NULL (symmetric).
  * workspace: h3b200_w4a8_linear_workspace_bytes(m, n, k, group) bytes. The
- * correction runs as a bf16 tensor-core GEMM (fp32 accumulation), at most 128
- * groups.
+ * correction is accumulated on the tensor cores inside the INT8 GEMM's
+ * epilogue (bf16 operands, fp32 accumulation), at most 128 groups.
  */
 H3B200_API int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group_size);
 H3B200_API int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
@@ -282,6 +283,34 @@ H3B200_API int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int
                                            int64_t ldo, int64_t m, int64_t d, int64_t ffn, int64_t group_size,
                                            int act, void* workspace, int64_t workspace_bytes,
                                            h3b200_stream_t stream);
+
+/*
+ * Fused gated SwiGLU INT8 MLP, the H3 production path (hidden d, fc1 out 2 ffn):
+ *   raw = int8_linear(x, W1, s1, b1, convrot = fc1_convrot_group);
+ *   y   = int8_linear(raw, W2, s2, b2, convrot = 256, input_act = "swiglu");
+ *   out[t] = residual[t] + y[t] * gate[row_map[t]]   (bf16 addcmul per token)
+ * Drop-in for try_fused_gated_mlp's INT8 path (h3serve/native_engine/model/
+ * fused_mlp.py:269-426: fc1 :366, fused-act fc2 :393-405, per-segment
+ * addcmul :410-424, segment row map _segment_row_map :34-55) with
+ * int8_linear as in eager/quantization.py:971-1056 (ConvRot weights are
+ * rotated offline along their input dimension).
+ * x, residual, out: bf16 [m, d] (out may alias residual); W1 int8 [2 ffn, d]
+ * ([gate | up] output rows), s1 fp32 [2 ffn] or [1], b1 bf16 [2 ffn] or NULL;
+ * W2 int8 [d, ffn], s2 fp32 [d] or [1], b2 bf16 [d] or NULL.
+ * gate: bf16 [d] when row_map is NULL, else bf16 [rows, ldg] and row_map
+ * int32 [m] gives each token's modulation row. fc1_convrot_group: 0 or 256.
+ * ffn (and d with fc1 ConvRot) multiples of 256. Tokens are processed in
+ * chunks of chunk_tokens; workspace:
+ * h3b200_fused_gated_mlp_swiglu_workspace_bytes(min(chunk_tokens, m), d, ffn).
+ */
+H3B200_API int64_t h3b200_fused_gated_mlp_swiglu_workspace_bytes(int64_t chunk_tokens, int64_t d, int64_t ffn);
+H3B200_API int h3b200_fused_gated_mlp_swiglu(const void* x, int64_t ldx, const int8_t* w1, const float* s1,
+                                             int64_t s1_numel, const void* b1, const int8_t* w2, const float* s2,
+                                             int64_t s2_numel, const void* b2, const void* gate, int64_t ldg,
+                                             const int32_t* row_map, const void* residual, int64_t ldr, void* out,
+                                             int64_t ldo, int64_t m, int64_t d, int64_t ffn,
+                                             int64_t fc1_convrot_group, int64_t chunk_tokens, void* workspace,
+                                             int64_t workspace_bytes, h3b200_stream_t stream);
 
 #ifdef __cplusplus
 }

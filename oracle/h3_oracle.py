@@ -47,6 +47,7 @@ __all__ = [
     "int8_linear",
     "gated_residual",
     "w8a8_gelu_mlp",
+    "swiglu_mlp",
     "rms_norm_row",
     "rms_adaln",
     "rope_split_half",
@@ -294,6 +295,27 @@ def w8a8_gelu_mlp(x_bf16, w1_i8, s1, w2_i8, s2, gate_bf16, residual_bf16, return
 # ---------------------------------------------------------------------------
 # (c) AdaLN-modulate + RMSNorm + split-half RoPE
 # ---------------------------------------------------------------------------
+
+
+def swiglu_mlp(x_bf16, w1q, s1, b1_bf16, w2q, s2, b2_bf16, gate_rows_bf16, row_map, residual_bf16,
+               fc1_convrot=True, return_intermediates=False):
+    """H3 SwiGLU MLP, the INT8 path of ``try_fused_gated_mlp``
+    (h3serve/native_engine/model/fused_mlp.py:366-424): ``raw = int8_linear(x, W1, s1, b1,
+    convrot=fc1_convrot)``; ``y = int8_linear(raw, W2, s2, b2, convrot=True,
+    input_act="swiglu")``; ``out[t] = residual[t] + y[t] * gate[row_map[t]]`` (the
+    per-segment ``addcmul_``). ConvRot uses the exact rotation (``rotate_activation``).
+    Returns bf16 bits."""
+    xr = rotate_activation(x_bf16, 256) if fc1_convrot else np.asarray(x_bf16, np.uint16)
+    q1, xs1 = quantize_int8_rowwise(xr)
+    raw = dequant_epilogue(int8_matmul_accumulate(q1, w1q), xs1, s1, b1_bf16)
+    a = rotate_activation(swiglu_bf16(raw), 256)
+    q2, xs2 = quantize_int8_rowwise(a)
+    y = dequant_epilogue(int8_matmul_accumulate(q2, w2q), xs2, s2, b2_bf16)
+    g = bf16_to_f32(np.asarray(gate_rows_bf16, np.uint16).reshape(-1, y.shape[-1])[np.asarray(row_map)])
+    out = f32_to_bf16((bf16_to_f32(residual_bf16) + (bf16_to_f32(y) * g).astype(np.float32)).astype(np.float32))
+    if return_intermediates:
+        return out, {"raw": raw, "y": y}
+    return out
 
 
 def _rms_rstd(xf: np.ndarray, eps: float) -> np.ndarray:

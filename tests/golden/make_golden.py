@@ -197,6 +197,34 @@ def main() -> None:
         "y": b16(ysw), "wq_convrot": cwq.numpy(), "ws_convrot": cws.numpy(), "y_convrot": b16(ysc),
     }
 
+    # 9. H3 SwiGLU MLP at reduced width (d=256, ffn=512, M=96): ConvRot INT8 fc1 with bias,
+    #    fused-act ConvRot fc2 with bias, gated residual over three modulation segments
+    #    (the INT8 path of try_fused_gated_mlp, h3serve/native_engine/model/fused_mlp.py:366-424).
+    gq = torch.Generator().manual_seed(7)
+    d9, f9, m9 = 256, 512, 96
+    w91 = (torch.randn(2 * f9, d9, generator=gq) * 0.02).to(torch.bfloat16)
+    w92 = (torch.randn(d9, f9, generator=gq) * 0.02).to(torch.bfloat16)
+    b91 = (torch.randn(2 * f9, generator=gq) * 0.1).to(torch.bfloat16)
+    b92 = (torch.randn(d9, generator=gq) * 0.1).to(torch.bfloat16)
+    x9 = torch.randn(m9, d9, generator=gq).to(torch.bfloat16)
+    r9 = torch.randn(m9, d9, generator=gq).to(torch.bfloat16)
+    g9 = torch.randn(3, d9, generator=gq).to(torch.bfloat16)
+    segs = ((0, 40, 2), (40, 70, 0), (70, 96, 1))
+    w91q, s91 = eq.quantize_int8_convrot_weight(w91, 256)
+    w92q, s92 = eq.quantize_int8_convrot_weight(w92, 256)
+    s91, s92 = s91.reshape(-1), s92.reshape(-1)
+    raw9 = eq.int8_linear(x9, w91q, s91, b91, torch.bfloat16, convrot=True, convrot_groupsize=256)
+    proj9 = eq.int8_linear(raw9, w92q, s92, b92, torch.bfloat16, convrot=True, convrot_groupsize=256,
+                           input_act="swiglu")
+    out9 = r9.clone()
+    for a9, z9, row9 in segs:
+        out9[a9:z9].addcmul_(proj9[a9:z9], g9[row9])
+    out["swiglu_mlp_small"] = {
+        "w1": b16(w91), "w2": b16(w92), "b1": b16(b91), "b2": b16(b92), "x": b16(x9), "residual": b16(r9),
+        "gate": b16(g9), "segments": np.array(segs, dtype=np.int64), "w1q": w91q.numpy(), "s1": s91.numpy(),
+        "w2q": w92q.numpy(), "s2": s92.numpy(), "raw": b16(raw9), "proj": b16(proj9), "out": b16(out9),
+    }
+
     for name, arrays in out.items():
         if args.only is not None and name not in args.only:
             continue

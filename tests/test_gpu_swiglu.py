@@ -72,3 +72,69 @@ def test_swiglu_convrot_quantizer_vs_oracle():
     assert rows.mean() >= 0.9                    # fp32 butterfly vs exact rotation: rare bf16 flips
     assert np.abs(np_(q).astype(np.int32) - oq).max() <= 1
     assert h3b200.device_status(0) == 0
+
+
+def _chain(x, wt, gate_rows, row_map, res):
+    """The reference's composition through h3b200's single ops, gated residual in numpy fp32."""
+    raw = h3b200.int8_linear(x, wt.w1q, wt.s1, wt.b1, convrot=wt.fc1_convrot)
+    y = h3b200.int8_linear(raw, wt.w2q, wt.s2, wt.b2, convrot=True, input_act="swiglu")
+    f = O.bf16_to_f32
+    g = f(t2u(gate_rows)).reshape(-1, y.shape[-1])[row_map]
+    return O.f32_to_bf16(f(t2u(res)) + f(t2u(y)) * g)
+
+
+def test_convrot_weight_prep_vs_reference(golden):
+    """Offline ConvRot weight rotation + per-channel quantization against the reference's
+    quantize_int8_convrot_weight (its rotation is a bf16 CPU matmul: rare last-bit flips)."""
+    g = golden("swiglu_mlp_small")
+    for w, wq_ref, s_ref in ((g["w1"], g["w1q"], g["s1"]), (g["w2"], g["w2q"], g["s2"])):
+        wq, s = h3b200.quantize_int8_convrot_weight(u2t(w))
+        same = (np_(wq) == wq_ref).all(-1)
+        assert same.mean() >= 0.95
+        assert np.abs(np_(wq).astype(np.int32) - wq_ref).max() <= 1
+        np.testing.assert_array_equal(np_(s)[same], s_ref[same])
+
+
+def test_swiglu_mlp_vs_reference_and_chain(golden):
+    g = golden("swiglu_mlp_small")
+    wt = h3b200.SwiGLUMLPWeights(torch.from_numpy(g["w1q"]).cuda(), torch.from_numpy(g["s1"]).cuda(),
+                                 torch.from_numpy(g["w2q"]).cuda(), torch.from_numpy(g["s2"]).cuda(),
+                                 u2t(g["b1"]), u2t(g["b2"]))
+    segs = [tuple(int(v) for v in s) for s in g["segments"]]
+    x, res, gate = u2t(g["x"]), u2t(g["residual"]), u2t(g["gate"])
+    out = h3b200.fused_gated_mlp_swiglu(res, x, wt, gate, segments=segs)
+    assert h3b200.device_status(0) == 0
+    rel, mx = rel_l2(t2u(out), g["out"])
+    assert rel <= 1e-2 and mx <= 2e-2
+    row_map = np.concatenate([np.full(b - a, r) for a, b, r in segs])
+    np.testing.assert_array_equal(t2u(out), _chain(x, wt, gate, row_map, res))
+    ref = O.swiglu_mlp(g["x"], g["w1q"], g["s1"], g["b1"], g["w2q"], g["s2"], g["b2"], g["gate"], row_map,
+                       g["residual"])
+    rel, mx = rel_l2(t2u(out), ref)
+    assert rel <= 1e-2 and mx <= 2e-2
+
+
+def test_swiglu_mlp_h3_dims_chunked_in_place():
+    """H3 dims (d 5,376, fc1 28,672, ffn 14,336) at 600 tokens (CTA-pair GEMMs), two modulation
+    segments and biases: equal to the op chain bit for bit, the same in 256-token chunks, and
+    in place on the residual."""
+    gen = torch.Generator().manual_seed(61)
+    d, ffn, m = 5376, 14336, 600
+    w1 = randn_bf16((2 * ffn, d), gen, std=0.02).cuda()
+    w2 = randn_bf16((d, ffn), gen, std=0.02).cuda()
+    b1 = randn_bf16((2 * ffn,), gen, std=0.1).cuda()
+    b2 = randn_bf16((d,), gen, std=0.1).cuda()
+    x = randn_bf16((m, d), gen).cuda()
+    res = randn_bf16((m, d), gen).cuda()
+    gate = randn_bf16((2, d), gen).cuda()
+    segs = [(0, 217, 1), (217, m, 0)]
+    wt = h3b200.SwiGLUMLPWeights.from_float(w1, w2, b1, b2)
+    out = h3b200.fused_gated_mlp_swiglu(res, x, wt, gate, segments=segs)
+    assert h3b200.device_status(0) == 0
+    row_map = np.concatenate([np.full(b - a, r) for a, b, r in segs])
+    np.testing.assert_array_equal(t2u(out), _chain(x, wt, gate, row_map, res))
+    chunked = h3b200.fused_gated_mlp_swiglu(res, x, wt, gate, segments=segs, chunk_tokens=256)
+    np.testing.assert_array_equal(t2u(chunked), t2u(out))
+    r2 = res.clone()
+    h3b200.fused_gated_mlp_swiglu(r2, x, wt, gate, segments=segs, out=r2, chunk_tokens=256)
+    np.testing.assert_array_equal(t2u(r2), t2u(out))

@@ -200,3 +200,15 @@ def test_swiglu_linear_bit_exact(golden):
     yc = O.dequant_epilogue(O.int8_matmul_accumulate(qc, g["wq_convrot"]), sc, g["ws_convrot"])
     yf, rf = O.bf16_to_f32(yc).astype(np.float64), O.bf16_to_f32(g["y_convrot"]).astype(np.float64)
     assert np.linalg.norm(yf - rf) / np.linalg.norm(rf) <= 1e-2 and np.abs(yf - rf).max() <= 2e-2
+
+
+def test_swiglu_mlp_oracle_vs_reference(golden):
+    """H3 SwiGLU MLP with biases and three modulation segments: the oracle composition (exact
+    ConvRot rotation) against the reference's own chain, within the north-star tolerance."""
+    g = golden("swiglu_mlp_small")
+    row_map = np.concatenate([np.full(b - a, r) for a, b, r in g["segments"]])
+    out, it = O.swiglu_mlp(g["x"], g["w1q"], g["s1"], g["b1"], g["w2q"], g["s2"], g["b2"], g["gate"], row_map,
+                           g["residual"], return_intermediates=True)
+    for mine, ref in ((it["raw"], g["raw"]), (it["y"], g["proj"]), (out, g["out"])):
+        a, b = O.bf16_to_f32(mine).astype(np.float64), O.bf16_to_f32(ref).astype(np.float64)
+        assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-2 and np.abs(a - b).max() <= 2e-2

@@ -317,6 +317,71 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
 }
 
 
+int64_t h3b200_fused_gated_mlp_swiglu_workspace_bytes(int64_t chunk_tokens, int64_t d, int64_t ffn) {
+  if (chunk_tokens <= 0 || d <= 0 || ffn <= 0) return 0;
+  const int64_t c = chunk_tokens;
+  return round_up(c * d, 256) + round_up(c * 4, 256) * 2 + round_up(c * 2 * ffn * 2, 256) + round_up(c * ffn, 256) +
+         1024;
+}
+
+int h3b200_fused_gated_mlp_swiglu(const void* x, int64_t ldx, const int8_t* w1, const float* s1, int64_t s1_numel,
+                                  const void* b1, const int8_t* w2, const float* s2, int64_t s2_numel, const void* b2,
+                                  const void* gate, int64_t ldg, const int32_t* row_map, const void* residual,
+                                  int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t d, int64_t ffn,
+                                  int64_t fc1_convrot_group, int64_t chunk_tokens, void* workspace,
+                                  int64_t workspace_bytes, h3b200_stream_t stream) {
+  if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d || chunk_tokens <= 0)
+    return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: bad shape m=%lld d=%lld ffn=%lld chunk=%lld", (long long)m, (long long)d, (long long)ffn, (long long)chunk_tokens);
+  if (fc1_convrot_group != 0 && fc1_convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_swiglu: fc1 ConvRot group must be 0 (off) or 256, got %lld", (long long)fc1_convrot_group);
+  if (d % 256 && fc1_convrot_group) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: ConvRot group 256 does not divide d=%lld", (long long)d);
+  if (ffn % 256) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: fc2 ConvRot group 256 does not divide ffn=%lld", (long long)ffn);
+  if (d % 16) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_swiglu: needs d %% 16 == 0");
+  if (s1_numel != 1 && s1_numel != 2 * ffn) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: fc1 scale must be scalar or [2*ffn]");
+  if (s2_numel != 1 && s2_numel != d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: fc2 scale must be scalar or [d]");
+  if (row_map != nullptr && ldg < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: gate row stride %lld < d", (long long)ldg);
+  if (m == 0) return H3B200_OK;
+  if (!x || !w1 || !s1 || !w2 || !s2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: NULL pointer");
+  const int64_t chunk = std::min(chunk_tokens, m);
+  const int64_t need = h3b200_fused_gated_mlp_swiglu_workspace_bytes(chunk, d, ffn);
+  if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: workspace too small (need %lld bytes for %lld-token chunks)", (long long)need, (long long)chunk);
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* xq = static_cast<int8_t*>(c.take(chunk * d));
+  float* xs = static_cast<float*>(c.take(chunk * 4));
+  void* raw = c.take(chunk * 2 * ffn * 2);
+  int8_t* q2 = static_cast<int8_t*>(c.take(chunk * ffn));
+  float* xs2 = static_cast<float*>(c.take(chunk * 4));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: workspace too small");
+  cudaStream_t st = S(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* rb = static_cast<const __nv_bfloat16*>(residual);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  for (int64_t s0 = 0; s0 < m; s0 += chunk) {
+    const int64_t mc = std::min(chunk, m - s0);
+    // fc1: (ConvRot-)quantize x, GEMM, dequant (+ bias) -> raw [mc, 2 ffn] = [gate | up]
+    cudaError_t e = fc1_convrot_group
+                        ? h3::launch_quantize_convrot(xb + s0 * ldx, ldx, mc, d, H3B200_ACT_NONE, xq, xs, nullptr, 0, 0, st)
+                        : h3::launch_quantize_rows(xb + s0 * ldx, ldx, mc, d, H3B200_ACT_NONE, nullptr, xq, xs, st);
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: quantize x");
+    h3::GemmArgs g1;
+    g1.a = xq; g1.w = w1; g1.m = mc; g1.n = 2 * ffn; g1.k = d; g1.lda = d; g1.ldw = d;
+    g1.epilogue = h3::kEpiBF16; g1.a_scale = xs; g1.w_scale = s1; g1.w_scale_per_channel = s1_numel > 1 ? 1 : 0;
+    g1.bias = b1; g1.out = raw; g1.ldo = 2 * ffn;
+    e = h3::launch_gemm_i8(g1, st);
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: fc1");
+    // fc2: SwiGLU + ConvRot-256 + quantize, GEMM, dequant (+ bias), gated residual per modulation row
+    e = h3::launch_quantize_convrot(raw, 2 * ffn, mc, ffn, H3B200_ACT_SWIGLU, q2, xs2, nullptr, 0, 0, st);
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: quantize swiglu(raw)");
+    h3::GemmArgs g2;
+    g2.a = q2; g2.w = w2; g2.m = mc; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
+    g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = s2; g2.w_scale_per_channel = s2_numel > 1 ? 1 : 0;
+    g2.bias = b2; g2.gate = gate; g2.row_map = row_map ? row_map + s0 : nullptr; g2.ldg = ldg;
+    g2.residual = rb + s0 * ldr; g2.ldr = ldr; g2.out = ob + s0 * ldo; g2.ldo = ldo;
+    e = h3::launch_gemm_i8(g2, st);
+    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: fc2");
+  }
+  return H3B200_OK;
+}
+
 int64_t h3b200_fused_gated_mlp_w4a8_workspace_bytes(int64_t m, int64_t d, int64_t ffn, int64_t group_size) {
   if (m < 0 || d <= 0 || ffn <= 0 || group_size <= 0) return 0;
   const int64_t kp1 = h3::correction_kpad(d / group_size), kp2 = h3::correction_kpad(ffn / group_size);

@@ -83,6 +83,8 @@ struct KParams {
   int64_t ldo;
   float* row_absmax;
   int corr_kb;  // 64-group k-blocks of the correction operands (kEpi*Corr)
+  const int32_t* row_map;  // kEpiGatedResidual: gate row of each output row (nullptr: gate is one row)
+  int64_t ldg;             // row stride of the gate rows (elements)
 };
 
 template <int EPI>
@@ -202,10 +204,14 @@ __device__ __forceinline__ void store_i32_chunk(const KParams& p, int row, int c
 // (fp32) for the chunk; in_w: the row's 32 bf16 residual values for the
 // gated-residual epilogues. For the W4A8 epilogues r holds the fp32 sums
 // dequant + correction of the second pass.
+// For kEpiGatedResidual, bias_s holds the staged bias (when p.bias is set) and
+// gw the row's own 32 gate values (when p.row_map is set; else aux_s has the
+// single gate row).
 template <int EPI>
 __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t (&r)[32], float xs,
                                                 const float* ws_s, const float* aux_s, const uint16_t* gtab,
                                                 uint32_t& amax_bits, const uint32_t (&in_w)[16],
+                                                const float* bias_s, const uint32_t (&gw)[16],
                                                 uint32_t (&ob)[16]) {
   if constexpr (EPI == kEpiGeluAbsmax) {
     gelu_chunk(r, xs, ws_s, gtab, ob, amax_bits);
@@ -240,9 +246,12 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
           if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
         }
         if constexpr (EPI == kEpiGatedResidual) {
+          if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), bias_s[j]));
           const uint32_t rw = in_w[j >> 1];
           const float rv = (j & 1) ? bf16_hi(rw) : bf16_lo(rw);
-          b = bf16_bits(__fadd_rn(rv, __fmul_rn(__uint_as_float(b << 16), av[e])));
+          float gv = av[e];
+          if (p.row_map != nullptr) gv = (j & 1) ? bf16_hi(gw[j >> 1]) : bf16_lo(gw[j >> 1]);
+          b = bf16_bits(__fadd_rn(rv, __fmul_rn(__uint_as_float(b << 16), gv)));
         }
         hb[e] = b;
       }
@@ -455,6 +464,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int half = ew >> 2;              // columns [128*half, 128*half + 128)
     float* ws_s = ops_smem + ew * 256;     // this warp's 128 column scales ...
     float* aux_s = ws_s + 128;             // ... and 128 bias / gate values
+    // kEpiGatedResidual with a bias: 128 staged bias values per warp in the GELU
+    // table's region (unused by this epilogue)
+    float* bias_s = reinterpret_cast<float*>(gelu_tab) + ew * 128;
     uint8_t* box = smem + OFF_EPI + ew * EPI_STAGE_BYTES;  // this warp's 32x32 bf16 output box
     // row `lane` of the box, 16-byte chunk q, at the 64-byte-swizzle position q ^ ((lane >> 1) & 3)
     uint8_t* box_row = box + lane * 64;
@@ -504,8 +516,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
           float a = 0.0f;
           if (EPI == kEpiBF16 && p.bias != nullptr && cok) a = __bfloat162float(p.bias[col]);
-          if (kInBox && cok) a = __bfloat162float(p.gate[col]);
+          if (kInBox && cok && (EPI != kEpiGatedResidual || p.row_map == nullptr)) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
+          if (EPI == kEpiGatedResidual && p.bias != nullptr) bias_s[c] = cok ? __bfloat162float(p.bias[col]) : 0.0f;
         }
         __syncwarp();
       }
@@ -600,8 +613,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) in_w[j] = 0u;
           }
+          uint32_t gw[16];  // the row's gate values (kEpiGatedResidual with a row map)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) gw[j] = 0u;
+          if constexpr (EPI == kEpiGatedResidual) {
+            if (p.row_map != nullptr && row < p.m) {
+              const __nv_bfloat16* grow = p.gate + (int64_t)__ldg(p.row_map + row) * p.ldg + col_base + c;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (col_base + c + 8 * q < p.n) {
+                  const uint4 v = __ldg(reinterpret_cast<const uint4*>(grow + 8 * q));
+                  gw[4 * q] = v.x; gw[4 * q + 1] = v.y; gw[4 * q + 2] = v.z; gw[4 * q + 3] = v.w;
+                }
+              }
+            }
+          }
           uint32_t ob[16];
-          epilogue_values<EPI>(p, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, in_w, ob);
+          epilogue_values<EPI>(p, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, in_w, bias_s + c, gw, ob);
           __syncwarp();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -771,6 +799,9 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
     return cudaErrorNotSupported;
   const bool gated = a.epilogue == kEpiGatedResidual || a.epilogue == kEpiGatedResidualCorr;
   if (gated && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0)) return cudaErrorNotSupported;
+  if (a.row_map != nullptr && (a.epilogue != kEpiGatedResidual || a.ldg < a.n || a.ldg % 8 != 0 ||
+                               (reinterpret_cast<uintptr_t>(a.gate) & 15)))
+    return cudaErrorNotSupported;
   const bool corr = a.epilogue == kEpiBF16Corr || a.epilogue == kEpiBF16CorrGelu || a.epilogue == kEpiGatedResidualCorr;
   if (corr && (a.sx == nullptr || a.corr_t == nullptr || a.kp <= 0 || a.kp % 64 != 0 || a.kp > kMaxCorrKp ||
                (reinterpret_cast<uintptr_t>(a.sx) & 15) || (reinterpret_cast<uintptr_t>(a.corr_t) & 15)))
@@ -831,6 +862,8 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.ldo = a.ldo;
   kp.row_absmax = a.row_absmax;
   kp.corr_kb = corr ? (int)(a.kp / 64) : 0;
+  kp.row_map = a.epilogue == kEpiGatedResidual ? a.row_map : nullptr;
+  kp.ldg = a.ldg;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

@@ -12,7 +12,7 @@ enum GemmEpilogue : int {
   kEpiI32 = 0,             // raw int32 accumulators
   kEpiBF16 = 1,            // bf16(acc * (xs * ws)) (+ bf16 bias)
   kEpiGeluAbsmax = 2,      // a = gelu(bf16(acc * (xs * ws))) stored bf16, row absmax of |a| via atomicMax
-  kEpiGatedResidual = 3,   // out = bf16(residual + bf16(acc * (xs * ws)) * gate)
+  kEpiGatedResidual = 3,   // out = bf16(residual + y * gate), y = bf16(acc * (xs * ws)) (+ bias, rounded)
   // W4A8 linears with the asymmetric correction fused into the INT8 GEMM:
   //   y = bf16(bf16(acc * (xs * ws)) + sum_g sx[m, g] * corr_t[n, g])   (fp32 sum, one rounding)
   kEpiBF16Corr = 4,          // out = y
@@ -30,7 +30,9 @@ struct GemmArgs {
   const float* w_scale = nullptr;  // [n] or [1]
   int w_scale_per_channel = 1;
   const void* bias = nullptr;      // bf16 [n]
-  const void* gate = nullptr;      // bf16 [n]
+  const void* gate = nullptr;      // bf16 [n], or [rows, ldg] with row_map
+  const int32_t* row_map = nullptr;  // kEpiGatedResidual: gate row of each output row [m] (modulation segments)
+  int64_t ldg = 0;
   const void* residual = nullptr;  // bf16 [m, ldr]
   int64_t ldr = 0;
   void* out = nullptr;  // bf16 or int32 [m, ldo]

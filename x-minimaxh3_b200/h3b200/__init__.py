@@ -16,8 +16,10 @@ from .ops import (  # noqa: F401
     adaln_rms_rope_,
     dequant_int4_grouped_to_int8,
     fused_gated_mlp,
+    fused_gated_mlp_swiglu,
     fused_gated_mlp_w4a8,
     input_act_code,
+    input_act_width,
     int8_gemm_fused,
     int8_linear,
     int8_linear_prequantized,
@@ -27,11 +29,20 @@ from .ops import (  # noqa: F401
     quantize_int8_rowwise_convrot,
     rms_rope_split_half,
     rms_rope_split_half_,
+    segment_row_map,
     w4a8_int8_linear,
 )
 from .pipeline import fused_gated_mlp_host  # noqa: F401
 from .rope import rope_grid_table  # noqa: F401
-from .weights import quantize_int8_weight, quantize_w4a8_weight, W4A8MLPWeights, W8A8MLPWeights  # noqa: F401
+from .weights import (  # noqa: F401
+    SwiGLUMLPWeights,
+    W4A8MLPWeights,
+    W8A8MLPWeights,
+    quantize_int8_convrot_weight,
+    quantize_int8_weight,
+    quantize_w4a8_weight,
+    rotate_weight,
+)
 
 __version__ = "0.1.0"
 

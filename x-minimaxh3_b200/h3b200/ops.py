@@ -503,6 +503,70 @@ def quantize_int8_rowwise_convrot(x: torch.Tensor, convrot_groupsize: int = 256,
     return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
 
 
+def segment_row_map(length: int, segments, device) -> torch.Tensor:
+    """int32 [length]: the modulation row of each token, from ``(start, stop, row)`` segments
+    that partition ``[0, length)`` in order (``_segment_row_map``,
+    h3serve/native_engine/model/fused_mlp.py:34-55, same validation)."""
+    host = torch.empty(length, dtype=torch.int32)
+    previous = 0
+    for start, stop, row in ((int(a), int(b), int(r)) for a, b, r in segments):
+        if start != previous or stop <= start:
+            raise ValueError("modulation segments must be an ordered partition")
+        host[start:stop] = row
+        previous = stop
+    if previous != length:
+        raise ValueError("modulation segments do not cover the packed sequence")
+    return host.to(device)
+
+
+def fused_gated_mlp_swiglu(residual: torch.Tensor, hidden: torch.Tensor, weights, gate: torch.Tensor,
+                           segments=None, out: torch.Tensor | None = None, chunk_tokens: int = 8192,
+                           workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The H3 SwiGLU MLP with the gated residual per modulation segment.
+
+    Drop-in for the INT8 path of ``try_fused_gated_mlp`` (h3serve/native_engine/model/
+    fused_mlp.py:269-426): ``raw = fc1(hidden)`` (ConvRot INT8 linear, fc1 bias),
+    ``y = int8_linear(raw, W2, s2, b2, convrot=True, input_act="swiglu")``, then
+    ``residual[a:b].addcmul_(y[a:b], gate[row])`` for each ``(a, b, row)`` in
+    ``segments`` (``gate`` [rows, d]); with ``segments=None`` ``gate`` is one row [d].
+    ``weights`` is a :class:`h3b200.SwiGLUMLPWeights`; ``out`` may be ``residual``."""
+    _need_cuda(residual, hidden, gate)
+    for name, t in (("residual", residual), ("hidden", hidden), ("gate", gate)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16, got {t.dtype}")
+    x2, ldx = _rows(hidden)
+    r2, ldr = _rows(residual)
+    m, d = x2.shape
+    ffn = weights.ffn
+    if weights.d != d or r2.shape != x2.shape:
+        raise ValueError(f"hidden/residual [M, {d}] do not match the weights (d={weights.d})")
+    if segments is None:
+        g = gate.reshape(-1).contiguous()
+        if g.numel() != d:
+            raise ValueError(f"gate must have {d} elements when no segments are given")
+        row_map, ldg = None, d
+    else:
+        g = gate.reshape(-1, d).contiguous()
+        row_map = segment_row_map(m, segments, hidden.device)
+        if m and int(row_map.max()) >= g.shape[0]:
+            raise ValueError(f"a segment names gate row {int(row_map.max())}, gate has {g.shape[0]} rows")
+        ldg = d
+    if out is None:
+        out = torch.empty_like(r2)
+    o2, ldo = _rows(out)
+    chunk = max(1, min(int(chunk_tokens), m)) if m else 1
+    nbytes = int(_lib.load().h3b200_fused_gated_mlp_swiglu_workspace_bytes(chunk, d, ffn))
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
+    s1 = weights.s1.to(torch.float32).contiguous()
+    s2 = weights.s2.to(torch.float32).contiguous()
+    _lib.call("h3b200_fused_gated_mlp_swiglu", x2.data_ptr(), ldx, weights.w1q.data_ptr(), s1.data_ptr(),
+              s1.numel(), _ptr(weights.b1), weights.w2q.data_ptr(), s2.data_ptr(), s2.numel(), _ptr(weights.b2),
+              g.data_ptr(), ldg, _ptr(row_map), r2.data_ptr(), ldr, o2.data_ptr(), ldo, m, d, ffn,
+              256 if weights.fc1_convrot else 0, chunk, workspace.data_ptr(), workspace.numel(), _stream(hidden))
+    return out
+
+
 def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, s_channel: torch.Tensor,
                      codebook: torch.Tensor | None = None, correction: torch.Tensor | None = None,
                      bias: torch.Tensor | None = None, group_size: int = 16, convrot_groupsize: int = 256,

@@ -10,6 +10,10 @@ scale_dtype=float32)``, backends/eager/w4a8_int8.py:315-341 -> :122-209):
 ConvRot-256 rotation of W, per-group min/max to uint4, fp32 ``s_rel`` and
 ``s_channel``, bf16 ``correction``. This is offline preparation written with
 torch tensor operations (it runs once per weight, on any device).
+
+ConvRot INT8 weights (the H3 SwiGLU MLP) are rotated along their input dimension
+by the regular Hadamard-256 and then quantized per output channel
+(``quantize_int8_convrot_weight``, backends/eager/quantization.py:898-906).
 """
 
 from __future__ import annotations
@@ -120,3 +124,51 @@ class W4A8MLPWeights:
     @property
     def ffn(self) -> int:
         return self.q1.shape[0]
+
+
+def rotate_weight(w: torch.Tensor, group_size: int = 256) -> torch.Tensor:
+    """Offline ConvRot rotation ``W @ H^T`` per input group (tensor/int8_utils.py:41-55),
+    summed exactly and rounded to bf16 as the reference's bf16 matmul result is stored."""
+    n, k = w.shape
+    if k % group_size:
+        raise ValueError(f"in_features {k} not divisible by group_size {group_size}")
+    hm = regular_hadamard(group_size, w.device)
+    wr = (w.to(torch.float64).reshape(n, k // group_size, group_size) @ hm.T).reshape(n, k)
+    return wr.to(torch.float32).to(torch.bfloat16)
+
+
+def quantize_int8_convrot_weight(w: torch.Tensor, group_size: int = 256):
+    """bf16 [N, K] -> (int8 [N, K], fp32 per-channel scale [N]) of the rotated weight
+    (``quantize_int8_convrot_weight`` eager/quantization.py:898-906)."""
+    return quantize_int8_weight(rotate_weight(w, group_size))
+
+
+@dataclass
+class SwiGLUMLPWeights:
+    """One H3 SwiGLU MLP: fc1 [2 ffn, d] ([gate | up] output rows), fc2 [d, ffn], INT8 with
+    per-channel fp32 scales and optional bf16 biases. fc2 is always ConvRot-rotated (the
+    reference's fused fc2 requires it, fused_mlp.py:306-312); fc1 is when ``fc1_convrot``."""
+
+    w1q: torch.Tensor
+    s1: torch.Tensor
+    w2q: torch.Tensor
+    s2: torch.Tensor
+    b1: torch.Tensor | None = None
+    b2: torch.Tensor | None = None
+    fc1_convrot: bool = True
+
+    @classmethod
+    def from_float(cls, w1: torch.Tensor, w2: torch.Tensor, b1: torch.Tensor | None = None,
+                   b2: torch.Tensor | None = None, fc1_convrot: bool = True) -> "SwiGLUMLPWeights":
+        w1q, s1 = quantize_int8_convrot_weight(w1) if fc1_convrot else quantize_int8_weight(w1)
+        w2q, s2 = quantize_int8_convrot_weight(w2)
+        cast = (lambda b: None if b is None else b.to(torch.bfloat16).contiguous())
+        return cls(w1q, s1, w2q, s2, cast(b1), cast(b2), fc1_convrot)
+
+    @property
+    def d(self) -> int:
+        return self.w1q.shape[1]
+
+    @property
+    def ffn(self) -> int:
+        return self.w1q.shape[0] // 2
