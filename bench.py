@@ -367,6 +367,33 @@ def run_ours(args, rank, world, local_rank):
     w4_ms = timed(k_w4a8, 10, stream)
     del work4, x3
 
+    # ---- H3 SwiGLU MLP at the H3 dims (d 5,376, fc1 out 28,672, ffn 14,336): ConvRot fc1 + bias,
+    #      SwiGLU+ConvRot fc2 + bias, gated residual; 8,192-token chunks as in the reference ----
+    H3_D, H3_FFN = 5376, 14336
+    g5 = torch.Generator(device=dev).manual_seed(8)
+    w1f = (torch.randn(2 * H3_FFN, H3_D, generator=g5, device=dev) * 0.02).to(torch.bfloat16)
+    w2f = (torch.randn(H3_D, H3_FFN, generator=g5, device=dev) * 0.02).to(torch.bfloat16)
+    b1f = (torch.randn(2 * H3_FFN, generator=g5, device=dev) * 0.1).to(torch.bfloat16)
+    b2f = (torch.randn(H3_D, generator=g5, device=dev) * 0.1).to(torch.bfloat16)
+    wsw = h3b200.SwiGLUMLPWeights.from_float(w1f, w2f, b1f, b2f)
+    del w1f, w2f
+    x5 = torch.randn(M_TOKENS, H3_D, generator=g5, device=dev).to(torch.bfloat16)
+    r5 = torch.randn(M_TOKENS, H3_D, generator=g5, device=dev).to(torch.bfloat16)
+    o5 = torch.empty_like(r5)
+    gate5 = torch.randn(2, H3_D, generator=g5, device=dev).to(torch.bfloat16)
+    segs5 = [(0, 1024, 1), (1024, M_TOKENS, 0)]   # a conditioning prefix with its own modulation row
+    wsb5 = int(h3b200.library().h3b200_fused_gated_mlp_swiglu_workspace_bytes(8192, H3_D, H3_FFN))
+    work5 = torch.empty(wsb5, dtype=torch.uint8, device=dev)
+
+    def k_swiglu():
+        h3b200.fused_gated_mlp_swiglu(r5, x5, wsw, gate5, segments=segs5, out=o5, workspace=work5)
+
+    for _ in range(3):
+        k_swiglu()
+    sw_ms = timed(k_swiglu, 10, stream)
+    sw_ops = 2 * H3_D * 2 * H3_FFN + 2 * H3_FFN * H3_D   # int8 ops per token
+    del work5, x5, r5, o5, wsw
+
     # ---- config 4: long-video DiT-block slice (norm-RoPE then W8A8 MLP) on this rank's token shard ----
     from h3b200 import parallel as PAR
 
@@ -473,6 +500,9 @@ def run_ours(args, rank, world, local_rank):
                 **{k: {"ms": v} for k, v in comp_ms.items()},
                 "fc2_gemm_gated_residual_tops": fc2_ops / (comp_ms["fc2_gemm_gated_residual"] * 1e-3) / 1e12,
                 "cublaslt_int8_8192_tops": lib_int8_tops,
+                "h3_swiglu_mlp": {"d": H3_D, "ffn": H3_FFN, "tokens": M_TOKENS, "ms": sw_ms,
+                                  "tokens_per_s": M_TOKENS / (sw_ms * 1e-3),
+                                  "int8_tops": M_TOKENS * sw_ops / (sw_ms * 1e-3) / 1e12},
                 "w4a8_mlp_cfg2": {"ms": w4_ms, "tokens_per_s": M_TOKENS / (w4_ms * 1e-3),
                                   "int8_tops": M_TOKENS * OPS_PER_TOKEN / (w4_ms * 1e-3) / 1e12,
                                   "weights": "asymmetric int4, group 128, ConvRot-256, decoded per call"},
