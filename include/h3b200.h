@@ -42,7 +42,7 @@ enum {
 };
 
 enum { H3B200_ACT_NONE = 0, H3B200_ACT_GELU_TANH = 1, H3B200_ACT_SWIGLU = 2 };
-enum { H3B200_DTYPE_F32 = 0, H3B200_DTYPE_F16 = 1, H3B200_DTYPE_BF16 = 2, H3B200_DTYPE_I32 = 3 };
+enum { H3B200_DTYPE_F32 = 0, H3B200_DTYPE_F16 = 1, H3B200_DTYPE_BF16 = 2, H3B200_DTYPE_I32 = 3, H3B200_DTYPE_E4M3 = 5 };
 
 /* Library identification and diagnostics. */
 H3B200_API const char* h3b200_version(void);
@@ -230,6 +230,21 @@ H3B200_API int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const fl
                                         int64_t group_size, int8_t* out, h3b200_stream_t stream);
 
 /*
+ * The same decode for every scale type and level table of the reference:
+ * q = clamp(rne(level(u) * s_rel[row, group]), -127, 127) with level(u) = u - 8
+ * (codebook NULL) or codebook[u] (16 fp32 levels, the H3 release format's
+ * Lloyd-Max table). s_rel_dtype: H3B200_DTYPE_F32 (fp32 [n, k/group]) or
+ * H3B200_DTYPE_E4M3 (float8_e4m3fn bytes [n, k/group], widened exactly).
+ * group_size 4, 8 or a multiple of 16. NaN scales decode to 0.
+ * Replaces launch_dequant_int4_grouped_to_int8 and
+ * launch_dequant_int4_grouped_to_int8_e4m3 (backends/cuda/ops/w4a8_gemm.cu:92-121,
+ * kernel :36-90; eager _dequant_int4_grouped_to_int8 eager/w4a8_int8.py:344-363).
+ */
+H3B200_API int h3b200_dequant_int4_grouped_to_int8_ex(const int8_t* qdata, const void* s_rel, int s_rel_dtype,
+                                                      const float* codebook, int64_t n, int64_t k, int64_t group_size,
+                                                      int8_t* out, h3b200_stream_t stream);
+
+/*
  * ConvRot (regular Hadamard, group 256) + per-row INT8 quantization, with an
  * optional activation applied first.
  * Replaces _C.quantize_int8_rowwise_convrot / quantize_int8_rowwise_convrot64
@@ -248,14 +263,17 @@ H3B200_API int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, in
  * Replaces comfy_kitchen w4a8_int8_linear (tensor/w4a8_int8.py:89-115; CUDA
  * backends/cuda/__init__.py:2139-2298, asymmetric correction :2294-2297).
  * grid: int8 [n, k] decoded weight (h3b200_dequant_int4_grouped_to_int8);
- * s_channel: fp32 [n]; correction: bf16 [k/group, n] or NULL (symmetric).
+ * s_channel: fp32 [n]; correction: bf16 [k/group, n] or NULL (symmetric);
+ * bias: bf16 [n] or NULL, symmetric weights only (then the call is
+ * int8_linear(x, grid, s_channel, bias, convrot=True), eager/w4a8_int8.py:494-508).
  * workspace: h3b200_w4a8_linear_workspace_bytes(m, n, k, group) bytes. The
  * correction is accumulated on the tensor cores inside the INT8 GEMM's
  * epilogue (bf16 operands, fp32 accumulation), at most 128 groups.
  */
 H3B200_API int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group_size);
 H3B200_API int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
-                            const void* correction, int64_t group_size, int64_t convrot_group, int act, void* out,
+                            const void* correction, const void* bias, int64_t group_size, int64_t convrot_group,
+                            int act, void* out,
                             int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                             h3b200_stream_t stream);
 
@@ -311,6 +329,36 @@ H3B200_API int h3b200_fused_gated_mlp_swiglu(const void* x, int64_t ldx, const i
                                              int64_t ldo, int64_t m, int64_t d, int64_t ffn,
                                              int64_t fc1_convrot_group, int64_t chunk_tokens, void* workspace,
                                              int64_t workspace_bytes, h3b200_stream_t stream);
+
+/*
+ * The H3 SwiGLU MLP on W4A8 weights in the H3 release format (group 16,
+ * fp8-e4m3 s_rel, 16-level codebook, symmetric; ConvRot-256 on both linears):
+ *   raw = w4a8_linear(x, W1, b1); y = w4a8_linear(silu(raw_gate) * raw_up, W2, b2);
+ *   out[t] = residual[t] + y[t] * gate[row_map[t]]
+ * with w4a8_linear(v, W, b) = int8_linear(v, decode(W), s_channel, b, convrot=True).
+ * Drop-in for try_fused_gated_mlp's W4A8 path, _chunked_module_gated_mlp
+ * (h3serve/native_engine/model/fused_mlp.py:222-266) over ConvRotW4A8Linear
+ * modules (quantization.py:416-600) bound to comfy_kitchen.w4a8_int8_linear
+ * (quantization.py:64-95). Both int4 weights are decoded once per call into
+ * the workspace (h3b200_dequant_int4_grouped_to_int8_ex), then the token
+ * chunks run as h3b200_fused_gated_mlp_swiglu with fc1 ConvRot on.
+ * qdata1 int8 [2 ffn, d/2], s_rel1 [2 ffn, d/group], s_channel1 fp32 [2 ffn],
+ * codebook1 fp32 [16] or NULL, b1 bf16 [2 ffn] or NULL; qdata2 int8 [d, ffn/2],
+ * s_rel2 [d, ffn/group], s_channel2 fp32 [d], codebook2, b2 bf16 [d] or NULL;
+ * s_rel_dtype H3B200_DTYPE_F32 or H3B200_DTYPE_E4M3 (both weights). Other
+ * arguments as h3b200_fused_gated_mlp_swiglu. workspace:
+ * h3b200_fused_gated_mlp_swiglu_w4a8_workspace_bytes(min(chunk_tokens, m), d, ffn).
+ */
+H3B200_API int64_t h3b200_fused_gated_mlp_swiglu_w4a8_workspace_bytes(int64_t chunk_tokens, int64_t d, int64_t ffn);
+H3B200_API int h3b200_fused_gated_mlp_swiglu_w4a8(const void* x, int64_t ldx, const int8_t* qdata1,
+                                                  const void* s_rel1, const float* s_channel1, const float* codebook1,
+                                                  const void* b1, const int8_t* qdata2, const void* s_rel2,
+                                                  const float* s_channel2, const float* codebook2, const void* b2,
+                                                  int s_rel_dtype, int64_t group_size, const void* gate, int64_t ldg,
+                                                  const int32_t* row_map, const void* residual, int64_t ldr,
+                                                  void* out, int64_t ldo, int64_t m, int64_t d, int64_t ffn,
+                                                  int64_t chunk_tokens, void* workspace, int64_t workspace_bytes,
+                                                  h3b200_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -58,6 +58,9 @@ __all__ = [
     "build_hadamard",
     "rotate_activation",
     "decode_int4_grouped_to_int8",
+    "e4m3_to_f32",
+    "w4a8_symmetric_linear",
+    "w4a8_swiglu_mlp",
     "w4a8_int8_linear_quantized",
     "w4a8_quantize_weight",
     "GELU_TANH_SATURATION",
@@ -460,21 +463,68 @@ def rotate_activation(x_bf16, group_size: int = 256) -> np.ndarray:
     return f32_to_bf16(y.astype(np.float32))
 
 
-def decode_int4_grouped_to_int8(qdata_i8, s_rel_f32, group_size: int) -> np.ndarray:
-    """Decode packed uint4 to the int8 grid: ``clamp(rne((u - 8) * s_rel), -127, 127)``.
+def e4m3_to_f32(bits_u8) -> np.ndarray:
+    """Widen OCP FP8 E4M3 (``torch.float8_e4m3fn``) bit patterns to fp32 exactly.
+
+    Format definition: sign bit, 4-bit exponent with bias 7, 3-bit mantissa,
+    subnormals ``m * 2^-9`` at exponent 0, no infinities, ``S.1111.111`` is NaN."""
+    b = np.asarray(bits_u8, np.uint8).astype(np.int64)
+    e = (b >> 3) & 0xF
+    m = (b & 7).astype(np.float64)
+    mag = np.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * np.exp2(e - 7.0))
+    mag = np.where((b & 0x7F) == 0x7F, np.nan, mag)
+    return np.where(b & 0x80, -mag, mag).astype(np.float32)
+
+
+def decode_int4_grouped_to_int8(qdata_i8, s_rel, group_size: int, codebook=None) -> np.ndarray:
+    """Decode packed uint4 to the int8 grid: ``clamp(rne(level(u) * s_rel), -127, 127)``,
+    ``level(u) = u - 8`` or ``codebook[u]``.
 
     ``_dequant_int4_grouped_to_int8`` eager/w4a8_int8.py:344-363 (even column =
-    low nibble; fp32 ``s_rel`` per (row, group)); CUDA twin
-    backends/cuda/ops/w4a8_gemm.cu:36-90."""
+    low nibble; ``s_rel`` per (row, group) as fp32, or as fp8-e4m3 given here as its
+    uint8 bit patterns and widened exactly); CUDA twin backends/cuda/ops/w4a8_gemm.cu:36-121."""
     p = np.asarray(qdata_i8).view(np.uint8).astype(np.int32)
     n, kh = p.shape
     k = kh * 2
     u = np.empty((n, k), dtype=np.int32)
     u[:, 0::2] = p & 0xF
     u[:, 1::2] = (p >> 4) & 0xF
-    vals = (u.astype(np.float32) - F32(8.0)).reshape(n, k // group_size, group_size)
-    vals = (vals * np.asarray(s_rel_f32, np.float32)[..., None]).astype(np.float32)
+    s = np.asarray(s_rel)
+    s = e4m3_to_f32(s) if s.dtype == np.uint8 else s.astype(np.float32)
+    if codebook is None:
+        lv = u.astype(np.float32) - F32(8.0)
+    else:
+        lv = np.asarray(codebook, np.float32)[u]
+    vals = (lv.reshape(n, k // group_size, group_size) * s[..., None]).astype(np.float32)
     return np.clip(np.rint(vals), -127, 127).astype(np.int8).reshape(n, k)
+
+
+def w4a8_symmetric_linear(x_bf16, qdata_i8, s_rel, s_channel, codebook=None, bias_bf16=None, group_size=16,
+                          input_act=None):
+    """Symmetric W4A8 linear (no correction): the H3 release format.
+
+    ``w4a8_int8_linear`` eager/w4a8_int8.py:494-508: decode the int4 weight to the
+    int8 grid, then ``int8_linear(x, grid, s_channel, bias, convrot=True)`` (ConvRot-256
+    rotation of the activation, exact here, then row quantization, int32 GEMM,
+    dequant, bias). Returns bf16 bits."""
+    grid = decode_int4_grouped_to_int8(qdata_i8, s_rel, group_size, codebook)
+    xr = rotate_activation(apply_input_act(x_bf16, input_act), 256)
+    q, xs = quantize_int8_rowwise(xr)
+    return dequant_epilogue(int8_matmul_accumulate(q, grid), xs, s_channel, bias_bf16)
+
+
+def w4a8_swiglu_mlp(x_bf16, w4, gate_rows_bf16, row_map, residual_bf16, return_intermediates=False):
+    """H3 SwiGLU MLP on W4A8 weights: ``_chunked_module_gated_mlp``
+    (h3serve/native_engine/model/fused_mlp.py:222-266) with the W4A8 kernel
+    binding: ``raw = fc1(x)``, ``y = fc2(silu(gate).mul_(up))``,
+    ``out[t] = residual[t] + y[t] * gate[row_map[t]]``. ``w4`` maps ``q1, s_rel1,
+    s_ch1, codebook1, b1, q2, ...`` and ``group_size``; per token the result equals
+    ``swiglu_mlp`` on the decoded grids."""
+    gs = int(w4["group_size"])
+    g1 = decode_int4_grouped_to_int8(w4["q1"], w4["s_rel1"], gs, w4.get("codebook1"))
+    g2 = decode_int4_grouped_to_int8(w4["q2"], w4["s_rel2"], gs, w4.get("codebook2"))
+    return swiglu_mlp(x_bf16, g1, w4["s_ch1"], w4.get("b1"), g2, w4["s_ch2"], w4.get("b2"), gate_rows_bf16,
+                      row_map, residual_bf16, fc1_convrot=True, return_intermediates=return_intermediates)
 
 
 def w4a8_int8_linear_quantized(x_bf16, qdata_i8, s_rel, s_channel, correction_bf16, group_size=128,

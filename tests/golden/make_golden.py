@@ -225,6 +225,107 @@ def main() -> None:
         "w2q": w92q.numpy(), "s2": s92.numpy(), "raw": b16(raw9), "proj": b16(proj9), "out": b16(out9),
     }
 
+    # 10. H3 release W4A8 format (quantize_w4a8_int8_weight defaults: group 16, symmetric,
+    #     fp8-e4m3 s_rel, 16-level codebook, no correction; ConvRot-256).
+    #     a) Gaussian weight (fixed codebook), its decode and its linear with a bias through
+    #        the top-level comfy_kitchen.w4a8_int8_linear (tensor/w4a8_int8.py:89-115);
+    #     b) a weight whose rotated groups are heavy-tailed (v^3 rotated back by H), so the
+    #        codebook is fitted, with more elements than the kurtosis and fit samples;
+    #     c) decode-only cases for the other group sizes, fp32 scales and the uniform
+    #        symmetric branch;
+    #     d) a reduced-width W4 SwiGLU MLP (d=256, ffn=512, M=96, biases, three modulation
+    #        segments, 64-token chunks) through the reference's own W4A8 driver
+    #        _chunked_module_gated_mlp (h3serve/native_engine/model/fused_mlp.py:222-266)
+    #        with the production binding comfy_kitchen_w4a8_kernel (quantization.py:64-95).
+    import types
+
+    import comfy_kitchen as ck
+    from h3serve.native_engine.model import fused_mlp as h3fused
+    from h3serve.native_engine.model import quantization as h3quant
+
+    def u8(t):
+        return t.contiguous().view(torch.uint8).numpy().copy()
+
+    gh = torch.Generator().manual_seed(8)
+    wa = (torch.randn(384, 512, generator=gh) * 0.02).to(torch.bfloat16)
+    xa = torch.randn(80, 512, generator=gh).to(torch.bfloat16)
+    ba = (torch.randn(384, generator=gh) * 0.1).to(torch.bfloat16)
+    qa, sra, sca, ca, cba = ew4.quantize_w4a8_int8_weight(wa)
+    assert ca is None and cba is not None and sra.dtype == torch.float8_e4m3fn
+    grida = ew4._dequant_int4_grouped_to_int8(qa, sra, cba, 16)
+    ya = ck.w4a8_int8_linear(xa, qa, sra, sca, cba, None, ba, 16, 256, torch.bfloat16)
+    h10 = _build_hadamard(256, dtype=torch.float32)
+    zb = torch.randn(1088, 512, generator=gh)
+    wb = ((zb * zb * zb * 0.01).reshape(1088, 2, 256) @ h10).reshape(1088, 512).to(torch.bfloat16)
+    qb, srb, scb, cb_, cbb = ew4.quantize_w4a8_int8_weight(wb)
+    fixed = torch.tensor(ew4._FIXED_LUT)
+    assert not torch.equal(cbb, fixed), "the heavy-tailed case must take the fitted codebook"
+    gridb = ew4._dequant_int4_grouped_to_int8(qb, srb, cbb, 16)
+    arrays10 = {
+        "w_a": b16(wa), "x_a": b16(xa), "b_a": b16(ba), "q_a": qa.numpy(), "s_rel_a": u8(sra), "s_ch_a": sca.numpy(),
+        "codebook_a": cba.numpy(), "grid_a": grida.numpy(), "y_a": b16(ya),
+        "w_b": b16(wb), "q_b": qb.numpy(), "s_rel_b": u8(srb), "s_ch_b": scb.numpy(), "codebook_b": cbb.numpy(),
+        "grid_b": gridb.numpy(),
+    }
+    wc = (torch.randn(64, 512, generator=gh) * 0.02).to(torch.bfloat16)
+    for tag, gsz, sdt, use_cb in (("g4_e4m3_cb", 4, torch.float8_e4m3fn, True), ("g8_e4m3_cb", 8, torch.float8_e4m3fn, True),
+                                  ("g32_f32_cb", 32, torch.float32, True), ("g16_f32_uni", 16, torch.float32, False),
+                                  ("g8_e4m3_uni", 8, torch.float8_e4m3fn, False)):
+        qc, src_, scc, cc, cbc = ew4.quantize_w4a8_int8_weight(wc, gsz, 256, True, sdt, use_cb)
+        assert cc is None and (cbc is not None) == use_cb
+        arrays10[f"q_{tag}"] = qc.numpy()
+        arrays10[f"s_rel_{tag}"] = u8(src_) if sdt != torch.float32 else src_.numpy()
+        arrays10[f"s_ch_{tag}"] = scc.numpy()
+        if use_cb:
+            arrays10[f"codebook_{tag}"] = cbc.numpy()
+        arrays10[f"grid_{tag}"] = ew4._dequant_int4_grouped_to_int8(qc, src_, cbc, gsz).numpy()
+    arrays10["w_c"] = b16(wc)
+    d10, f10, m10 = 256, 512, 96
+    w101 = (torch.randn(2 * f10, d10, generator=gh) * 0.02).to(torch.bfloat16)
+    w102 = (torch.randn(d10, f10, generator=gh) * 0.02).to(torch.bfloat16)
+    b101 = (torch.randn(2 * f10, generator=gh) * 0.1).to(torch.bfloat16)
+    b102 = (torch.randn(d10, generator=gh) * 0.1).to(torch.bfloat16)
+    x10 = torch.randn(m10, d10, generator=gh).to(torch.bfloat16)
+    r10 = torch.randn(m10, d10, generator=gh).to(torch.bfloat16)
+    g10 = torch.randn(3, d10, generator=gh).to(torch.bfloat16)
+    segs10 = ((0, 40, 2), (40, 70, 0), (70, 96, 1))
+    p1 = ew4.quantize_w4a8_int8_weight(w101)
+    p2 = ew4.quantize_w4a8_int8_weight(w102)
+
+    def w4_linear(prep, bias):
+        def run(v):
+            return h3quant.comfy_kitchen_w4a8_kernel(v, prep[0], prep[1], prep[2], prep[4], prep[3], bias, 16, 256,
+                                                     v.dtype)
+        return run
+
+    mlp10 = types.SimpleNamespace(fc1=w4_linear(p1, b101), fc2=w4_linear(p2, b102))
+    out10 = r10.clone()
+    h3fused._chunked_module_gated_mlp(out10, x10, mlp10, g10, segs10, chunk_tokens=64)
+    raw10 = mlp10.fc1(x10)
+    arrays10.update({
+        "mlp_w1": b16(w101), "mlp_w2": b16(w102), "mlp_b1": b16(b101), "mlp_b2": b16(b102), "mlp_x": b16(x10),
+        "mlp_residual": b16(r10), "mlp_gate": b16(g10), "mlp_segments": np.array(segs10, dtype=np.int64),
+        "mlp_q1": p1[0].numpy(), "mlp_s_rel1": u8(p1[1]), "mlp_s_ch1": p1[2].numpy(), "mlp_codebook1": p1[4].numpy(),
+        "mlp_q2": p2[0].numpy(), "mlp_s_rel2": u8(p2[1]), "mlp_s_ch2": p2[2].numpy(), "mlp_codebook2": p2[4].numpy(),
+        "mlp_raw": b16(raw10), "mlp_out": b16(out10),
+    })
+    #     e) a heavy-tailed [640, 8192] weight regenerated from its seed by the test (too big
+    #        to store): more rows than the codebook row sample (rows are then strided) and two
+    #        preparation chunks; SHA-256 digests of the weight and of the outputs.
+    import hashlib
+
+    def digest(t):
+        return np.frombuffer(hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).digest(), np.uint8)
+
+    ge = torch.Generator().manual_seed(9)
+    ze = torch.randn(640, 8192, generator=ge)
+    we = ((ze * ze * ze * 0.01).reshape(640, 32, 256) @ h10).reshape(640, 8192).to(torch.bfloat16)
+    qe, sre, sce, _, cbe = ew4.quantize_w4a8_int8_weight(we)
+    assert not torch.equal(cbe, fixed)
+    arrays10.update({"big_seed": np.array(9), "big_w_sha": digest(we), "big_q_sha": digest(qe),
+                     "big_s_rel_sha": digest(sre), "big_s_ch": sce.numpy(), "big_codebook": cbe.numpy()})
+    out["w4a8_h3"] = arrays10
+
     for name, arrays in out.items():
         if args.only is not None and name not in args.only:
             continue

@@ -250,14 +250,25 @@ int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk
   return from_cuda(h3::launch_adaln_rms_rope(a, S(stream)), "adaln_rms_rope");
 }
 
-int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k,
-                                        int64_t group_size, int8_t* out, h3b200_stream_t stream) {
+int h3b200_dequant_int4_grouped_to_int8_ex(const int8_t* qdata, const void* s_rel, int s_rel_dtype,
+                                           const float* codebook, int64_t n, int64_t k, int64_t group_size,
+                                           int8_t* out, h3b200_stream_t stream) {
   if (n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: negative shape");
   if (group_size < 4 || k % 16 || k % group_size || (16 % group_size && group_size % 16))
     return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: K=%lld must be divisible by 16 and group_size=%lld; group_size must be >=4 and divide 16 or be a multiple of 16", (long long)k, (long long)group_size);
+  if (s_rel_dtype != H3B200_DTYPE_F32 && s_rel_dtype != H3B200_DTYPE_E4M3)
+    return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: s_rel dtype code must be 0 (float32) or 5 (float8_e4m3fn), got %d", s_rel_dtype);
   if (n == 0 || k == 0) return H3B200_OK;
   if (!qdata || !s_rel || !out) return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: NULL pointer");
-  return from_cuda(h3::launch_dequant_int4(qdata, s_rel, n, k, group_size, out, S(stream)), "dequant_int4_grouped_to_int8");
+  return from_cuda(h3::launch_dequant_int4(qdata, s_rel, s_rel_dtype == H3B200_DTYPE_E4M3, codebook, n, k, group_size,
+                                           out, S(stream)),
+                   "dequant_int4_grouped_to_int8");
+}
+
+int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k,
+                                        int64_t group_size, int8_t* out, h3b200_stream_t stream) {
+  return h3b200_dequant_int4_grouped_to_int8_ex(qdata, s_rel, H3B200_DTYPE_F32, nullptr, n, k, group_size, out,
+                                                stream);
 }
 
 int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, int64_t k, int64_t ldx, int64_t group_size,
@@ -277,7 +288,8 @@ int64_t h3b200_w4a8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int6
 }
 
 int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, const float* s_channel,
-                            const void* correction, int64_t group_size, int64_t convrot_group, int act, void* out,
+                            const void* correction, const void* bias, int64_t group_size, int64_t convrot_group,
+                            int act, void* out,
                             int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                             h3b200_stream_t stream) {
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: unsupported act code %d", act);
@@ -286,6 +298,7 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
     return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: K=%lld must be divisible by 16, group_size=%lld, and convrot_groupsize=%lld", (long long)k, (long long)group_size, (long long)convrot_group);
   if (convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: only convrot_groupsize 256 is built");
   if (correction != nullptr && (group_size % 8 || 256 % group_size)) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: asymmetric correction needs group_size dividing 256");
+  if (correction != nullptr && bias != nullptr) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: a bias is built for symmetric weights (no correction) only");
   if (m == 0 || n == 0) return H3B200_OK;
   if (!x || !grid || !s_channel || !out) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: NULL pointer");
   if (n % 8) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: needs n %% 8 == 0");
@@ -310,7 +323,7 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
   g.a = xq; g.w = grid; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
   g.epilogue = correction ? h3::kEpiBF16Corr : h3::kEpiBF16;
   g.a_scale = xs; g.w_scale = s_channel; g.w_scale_per_channel = 1;
-  g.out = out; g.ldo = n;
+  g.bias = bias; g.out = out; g.ldo = n;
   g.sx = sx; g.corr_t = corr_t; g.kp = kp;
   e = h3::launch_gemm_i8(g, st);
   return from_cuda(e, "w4a8_int8_linear: gemm");
@@ -324,62 +337,142 @@ int64_t h3b200_fused_gated_mlp_swiglu_workspace_bytes(int64_t chunk_tokens, int6
          1024;
 }
 
+}  // extern "C"
+
+namespace {
+
+struct SwiGLUMlp {
+  const void* x; int64_t ldx;
+  const int8_t* w1; const float* s1; int64_t s1_numel; const void* b1;
+  const int8_t* w2; const float* s2; int64_t s2_numel; const void* b2;
+  const void* gate; int64_t ldg; const int32_t* row_map;
+  const void* residual; int64_t ldr; void* out; int64_t ldo;
+  int64_t m, d, ffn, fc1_convrot_group, chunk_tokens;
+};
+
+// Shape and pointer checks shared by the INT8 and W4A8 SwiGLU MLPs (the weight
+// pointers are checked by the callers).
+int check_swiglu_mlp(const SwiGLUMlp& a, const char* who) {
+  if (a.m < 0 || a.d <= 0 || a.ffn <= 0 || a.ldx < a.d || a.ldr < a.d || a.ldo < a.d || a.chunk_tokens <= 0)
+    return fail(H3B200_ERR_INVALID, "%s: bad shape m=%lld d=%lld ffn=%lld chunk=%lld", who, (long long)a.m, (long long)a.d, (long long)a.ffn, (long long)a.chunk_tokens);
+  if (a.fc1_convrot_group != 0 && a.fc1_convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "%s: fc1 ConvRot group must be 0 (off) or 256, got %lld", who, (long long)a.fc1_convrot_group);
+  if (a.d % 256 && a.fc1_convrot_group) return fail(H3B200_ERR_INVALID, "%s: ConvRot group 256 does not divide d=%lld", who, (long long)a.d);
+  if (a.ffn % 256) return fail(H3B200_ERR_INVALID, "%s: fc2 ConvRot group 256 does not divide ffn=%lld", who, (long long)a.ffn);
+  if (a.d % 16) return fail(H3B200_ERR_UNSUPPORTED, "%s: needs d %% 16 == 0", who);
+  if (a.s1_numel != 1 && a.s1_numel != 2 * a.ffn) return fail(H3B200_ERR_INVALID, "%s: fc1 scale must be scalar or [2*ffn]", who);
+  if (a.s2_numel != 1 && a.s2_numel != a.d) return fail(H3B200_ERR_INVALID, "%s: fc2 scale must be scalar or [d]", who);
+  if (a.row_map != nullptr && a.ldg < a.d) return fail(H3B200_ERR_INVALID, "%s: gate row stride %lld < d", who, (long long)a.ldg);
+  if (a.m > 0 && (!a.x || !a.gate || !a.residual || !a.out)) return fail(H3B200_ERR_INVALID, "%s: NULL pointer", who);
+  return H3B200_OK;
+}
+
+// Per chunk of tokens: (ConvRot-)quantize x -> fc1 GEMM (dequant + bias) ->
+// SwiGLU + ConvRot-256 + quantize -> fc2 GEMM (dequant + bias + gated residual
+// by modulation row). `work` holds at least
+// h3b200_fused_gated_mlp_swiglu_workspace_bytes(min(chunk, m), d, ffn) bytes.
+int run_swiglu_mlp(const SwiGLUMlp& a, void* work, int64_t work_bytes, cudaStream_t st, const char* who) {
+  const int64_t m = a.m, d = a.d, ffn = a.ffn;
+  const int64_t chunk = std::min(a.chunk_tokens, m);
+  Carver c{static_cast<uint8_t*>(work), work_bytes};
+  int8_t* xq = static_cast<int8_t*>(c.take(chunk * d));
+  float* xs = static_cast<float*>(c.take(chunk * 4));
+  void* raw = c.take(chunk * 2 * ffn * 2);
+  int8_t* q2 = static_cast<int8_t*>(c.take(chunk * ffn));
+  float* xs2 = static_cast<float*>(c.take(chunk * 4));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "%s: workspace too small", who);
+  const auto* xb = static_cast<const __nv_bfloat16*>(a.x);
+  const auto* rb = static_cast<const __nv_bfloat16*>(a.residual);
+  auto* ob = static_cast<__nv_bfloat16*>(a.out);
+  for (int64_t s0 = 0; s0 < m; s0 += chunk) {
+    const int64_t mc = std::min(chunk, m - s0);
+    // fc1: (ConvRot-)quantize x, GEMM, dequant (+ bias) -> raw [mc, 2 ffn] = [gate | up]
+    cudaError_t e = a.fc1_convrot_group
+                        ? h3::launch_quantize_convrot(xb + s0 * a.ldx, a.ldx, mc, d, H3B200_ACT_NONE, xq, xs, nullptr, 0, 0, st)
+                        : h3::launch_quantize_rows(xb + s0 * a.ldx, a.ldx, mc, d, H3B200_ACT_NONE, nullptr, xq, xs, st);
+    if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: quantize x");
+    h3::GemmArgs g1;
+    g1.a = xq; g1.w = a.w1; g1.m = mc; g1.n = 2 * ffn; g1.k = d; g1.lda = d; g1.ldw = d;
+    g1.epilogue = h3::kEpiBF16; g1.a_scale = xs; g1.w_scale = a.s1; g1.w_scale_per_channel = a.s1_numel > 1 ? 1 : 0;
+    g1.bias = a.b1; g1.out = raw; g1.ldo = 2 * ffn;
+    e = h3::launch_gemm_i8(g1, st);
+    if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: fc1");
+    // fc2: SwiGLU + ConvRot-256 + quantize, GEMM, dequant (+ bias), gated residual per modulation row
+    e = h3::launch_quantize_convrot(raw, 2 * ffn, mc, ffn, H3B200_ACT_SWIGLU, q2, xs2, nullptr, 0, 0, st);
+    if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: quantize swiglu(raw)");
+    h3::GemmArgs g2;
+    g2.a = q2; g2.w = a.w2; g2.m = mc; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
+    g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = a.s2; g2.w_scale_per_channel = a.s2_numel > 1 ? 1 : 0;
+    g2.bias = a.b2; g2.gate = a.gate; g2.row_map = a.row_map ? a.row_map + s0 : nullptr; g2.ldg = a.ldg;
+    g2.residual = rb + s0 * a.ldr; g2.ldr = a.ldr; g2.out = ob + s0 * a.ldo; g2.ldo = a.ldo;
+    e = h3::launch_gemm_i8(g2, st);
+    if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: fc2");
+  }
+  return H3B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int h3b200_fused_gated_mlp_swiglu(const void* x, int64_t ldx, const int8_t* w1, const float* s1, int64_t s1_numel,
                                   const void* b1, const int8_t* w2, const float* s2, int64_t s2_numel, const void* b2,
                                   const void* gate, int64_t ldg, const int32_t* row_map, const void* residual,
                                   int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t d, int64_t ffn,
                                   int64_t fc1_convrot_group, int64_t chunk_tokens, void* workspace,
                                   int64_t workspace_bytes, h3b200_stream_t stream) {
-  if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d || chunk_tokens <= 0)
-    return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: bad shape m=%lld d=%lld ffn=%lld chunk=%lld", (long long)m, (long long)d, (long long)ffn, (long long)chunk_tokens);
-  if (fc1_convrot_group != 0 && fc1_convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_swiglu: fc1 ConvRot group must be 0 (off) or 256, got %lld", (long long)fc1_convrot_group);
-  if (d % 256 && fc1_convrot_group) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: ConvRot group 256 does not divide d=%lld", (long long)d);
-  if (ffn % 256) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: fc2 ConvRot group 256 does not divide ffn=%lld", (long long)ffn);
-  if (d % 16) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_swiglu: needs d %% 16 == 0");
-  if (s1_numel != 1 && s1_numel != 2 * ffn) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: fc1 scale must be scalar or [2*ffn]");
-  if (s2_numel != 1 && s2_numel != d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: fc2 scale must be scalar or [d]");
-  if (row_map != nullptr && ldg < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: gate row stride %lld < d", (long long)ldg);
+  const SwiGLUMlp a{x, ldx, w1, s1, s1_numel, b1, w2, s2, s2_numel, b2, gate, ldg, row_map, residual, ldr, out, ldo,
+                    m, d, ffn, fc1_convrot_group, chunk_tokens};
+  if (int rc = check_swiglu_mlp(a, "fused_gated_mlp_swiglu")) return rc;
   if (m == 0) return H3B200_OK;
-  if (!x || !w1 || !s1 || !w2 || !s2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: NULL pointer");
+  if (!w1 || !s1 || !w2 || !s2) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: NULL pointer");
   const int64_t chunk = std::min(chunk_tokens, m);
   const int64_t need = h3b200_fused_gated_mlp_swiglu_workspace_bytes(chunk, d, ffn);
   if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: workspace too small (need %lld bytes for %lld-token chunks)", (long long)need, (long long)chunk);
+  return run_swiglu_mlp(a, workspace, workspace_bytes, S(stream), "fused_gated_mlp_swiglu");
+}
+
+int64_t h3b200_fused_gated_mlp_swiglu_w4a8_workspace_bytes(int64_t chunk_tokens, int64_t d, int64_t ffn) {
+  if (chunk_tokens <= 0 || d <= 0 || ffn <= 0) return 0;
+  return round_up(2 * ffn * d, 256) + round_up(d * ffn, 256) +
+         h3b200_fused_gated_mlp_swiglu_workspace_bytes(chunk_tokens, d, ffn) + 256;
+}
+
+int h3b200_fused_gated_mlp_swiglu_w4a8(const void* x, int64_t ldx, const int8_t* qdata1, const void* s_rel1,
+                                       const float* s_channel1, const float* codebook1, const void* b1,
+                                       const int8_t* qdata2, const void* s_rel2, const float* s_channel2,
+                                       const float* codebook2, const void* b2, int s_rel_dtype, int64_t group_size,
+                                       const void* gate, int64_t ldg, const int32_t* row_map, const void* residual,
+                                       int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t d, int64_t ffn,
+                                       int64_t chunk_tokens, void* workspace, int64_t workspace_bytes,
+                                       h3b200_stream_t stream) {
+  const char* who = "fused_gated_mlp_swiglu_w4a8";
+  if (group_size < 4 || (16 % group_size && group_size % 16) || d % group_size || ffn % group_size)
+    return fail(H3B200_ERR_INVALID, "%s: group_size=%lld must be >=4, divide 16 or be a multiple of 16, and divide d and ffn", who, (long long)group_size);
+  if (s_rel_dtype != H3B200_DTYPE_F32 && s_rel_dtype != H3B200_DTYPE_E4M3)
+    return fail(H3B200_ERR_INVALID, "%s: s_rel dtype code must be 0 (float32) or 5 (float8_e4m3fn), got %d", who, s_rel_dtype);
+  const SwiGLUMlp a0{x, ldx, nullptr, s_channel1, 2 * ffn, b1, nullptr, s_channel2, d, b2, gate, ldg, row_map,
+                     residual, ldr, out, ldo, m, d, ffn, 256, chunk_tokens};
+  if (int rc = check_swiglu_mlp(a0, who)) return rc;
+  if (m == 0) return H3B200_OK;
+  if (!qdata1 || !s_rel1 || !s_channel1 || !qdata2 || !s_rel2 || !s_channel2) return fail(H3B200_ERR_INVALID, "%s: NULL pointer", who);
+  const int64_t chunk = std::min(chunk_tokens, m);
+  const int64_t need = h3b200_fused_gated_mlp_swiglu_w4a8_workspace_bytes(chunk, d, ffn);
+  if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "%s: workspace too small (need %lld bytes for %lld-token chunks)", who, (long long)need, (long long)chunk);
   Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
-  int8_t* xq = static_cast<int8_t*>(c.take(chunk * d));
-  float* xs = static_cast<float*>(c.take(chunk * 4));
-  void* raw = c.take(chunk * 2 * ffn * 2);
-  int8_t* q2 = static_cast<int8_t*>(c.take(chunk * ffn));
-  float* xs2 = static_cast<float*>(c.take(chunk * 4));
-  if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_swiglu: workspace too small");
+  int8_t* grid1 = static_cast<int8_t*>(c.take(2 * ffn * d));
+  int8_t* grid2 = static_cast<int8_t*>(c.take(d * ffn));
+  c.off = round_up(c.off, 256);
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "%s: workspace too small", who);
   cudaStream_t st = S(stream);
-  const auto* xb = static_cast<const __nv_bfloat16*>(x);
-  const auto* rb = static_cast<const __nv_bfloat16*>(residual);
-  auto* ob = static_cast<__nv_bfloat16*>(out);
-  for (int64_t s0 = 0; s0 < m; s0 += chunk) {
-    const int64_t mc = std::min(chunk, m - s0);
-    // fc1: (ConvRot-)quantize x, GEMM, dequant (+ bias) -> raw [mc, 2 ffn] = [gate | up]
-    cudaError_t e = fc1_convrot_group
-                        ? h3::launch_quantize_convrot(xb + s0 * ldx, ldx, mc, d, H3B200_ACT_NONE, xq, xs, nullptr, 0, 0, st)
-                        : h3::launch_quantize_rows(xb + s0 * ldx, ldx, mc, d, H3B200_ACT_NONE, nullptr, xq, xs, st);
-    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: quantize x");
-    h3::GemmArgs g1;
-    g1.a = xq; g1.w = w1; g1.m = mc; g1.n = 2 * ffn; g1.k = d; g1.lda = d; g1.ldw = d;
-    g1.epilogue = h3::kEpiBF16; g1.a_scale = xs; g1.w_scale = s1; g1.w_scale_per_channel = s1_numel > 1 ? 1 : 0;
-    g1.bias = b1; g1.out = raw; g1.ldo = 2 * ffn;
-    e = h3::launch_gemm_i8(g1, st);
-    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: fc1");
-    // fc2: SwiGLU + ConvRot-256 + quantize, GEMM, dequant (+ bias), gated residual per modulation row
-    e = h3::launch_quantize_convrot(raw, 2 * ffn, mc, ffn, H3B200_ACT_SWIGLU, q2, xs2, nullptr, 0, 0, st);
-    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: quantize swiglu(raw)");
-    h3::GemmArgs g2;
-    g2.a = q2; g2.w = w2; g2.m = mc; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
-    g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = s2; g2.w_scale_per_channel = s2_numel > 1 ? 1 : 0;
-    g2.bias = b2; g2.gate = gate; g2.row_map = row_map ? row_map + s0 : nullptr; g2.ldg = ldg;
-    g2.residual = rb + s0 * ldr; g2.ldr = ldr; g2.out = ob + s0 * ldo; g2.ldo = ldo;
-    e = h3::launch_gemm_i8(g2, st);
-    if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu: fc2");
-  }
-  return H3B200_OK;
+  const bool e4m3 = s_rel_dtype == H3B200_DTYPE_E4M3;
+  // the int4 weights are decoded once per call; every token chunk's GEMMs read the grids
+  cudaError_t e = h3::launch_dequant_int4(qdata1, s_rel1, e4m3, codebook1, 2 * ffn, d, group_size, grid1, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu_w4a8: decode W1");
+  e = h3::launch_dequant_int4(qdata2, s_rel2, e4m3, codebook2, d, ffn, group_size, grid2, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_swiglu_w4a8: decode W2");
+  SwiGLUMlp a = a0;
+  a.w1 = grid1; a.w2 = grid2;
+  return run_swiglu_mlp(a, static_cast<uint8_t*>(workspace) + c.off, workspace_bytes - c.off, st, who);
 }
 
 int64_t h3b200_fused_gated_mlp_w4a8_workspace_bytes(int64_t m, int64_t d, int64_t ffn, int64_t group_size) {
@@ -421,9 +514,9 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
   void* ct2 = c.take(d * kp2 * 2);
   if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: workspace too small");
   cudaStream_t st = S(stream);
-  cudaError_t e = h3::launch_dequant_int4(qdata1, s_rel1, ffn, d, group_size, grid1, st);
+  cudaError_t e = h3::launch_dequant_int4(qdata1, s_rel1, false, nullptr, ffn, d, group_size, grid1, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: decode W1");
-  e = h3::launch_dequant_int4(qdata2, s_rel2, d, ffn, group_size, grid2, st);
+  e = h3::launch_dequant_int4(qdata2, s_rel2, false, nullptr, d, ffn, group_size, grid2, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp_w4a8: decode W2");
   // fc1: ConvRot-quantize x, GEMM, asymmetric correction
   e = h3::launch_quantize_convrot(x, ldx, m, d, H3B200_ACT_NONE, xq, xs, correction1 ? sx1 : nullptr, group_size, kp1, st);

@@ -74,8 +74,9 @@ struct NormRopeArgs {
 };
 cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream);
 
-cudaError_t launch_dequant_int4(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k, int64_t group,
-                                int8_t* out, cudaStream_t stream);
+// int4 -> int8 grid; s_rel fp32 or (s_rel_e4m3) fp8-e4m3 bytes; codebook: 16 fp32 levels or nullptr (u - 8)
+cudaError_t launch_dequant_int4(const int8_t* qdata, const void* s_rel, bool s_rel_e4m3, const float* codebook,
+                                int64_t n, int64_t k, int64_t group, int8_t* out, cudaStream_t stream);
 // ConvRot-256 + row quantization; with sx != nullptr also writes the correction
 // operand sx (bf16 [m, kp], zero beyond k / sum_group).
 cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64_t k, int act, int8_t* q,

@@ -20,45 +20,88 @@ namespace h3 {
 namespace {
 
 // ---------------------------------------------------------------------------
-// Decode: 16 outputs per thread (8 packed bytes), group_size % 16 == 0.
-// q = clamp(rne((u - 8) * s_rel), -127, 127); even column = low nibble.
+// Decode: q = clamp(rne(level(u) * s), -127, 127) with level(u) = u - 8 or a
+// 16-entry fp32 codebook, s the row's group scale (fp32, or fp8-e4m3 bytes),
+// even column in the low nibble. The product is one fp32 multiply and the
+// rounding is cvt.rni (NaN -> 0), then an integer clamp.
 // ---------------------------------------------------------------------------
-__global__ void dequant_int4_kernel(const uint8_t* __restrict__ qd, const float* __restrict__ s_rel, int64_t n,
-                                    int64_t k, int64_t group, int8_t* __restrict__ out) {
-  const int64_t per_row = k / 16;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= n * per_row) return;
-  const int64_t row = idx / per_row;
-  const int64_t c16 = (idx - row * per_row) * 16;
-  const float s = s_rel[row * (k / group) + c16 / group];
-  const uint2 pk = *reinterpret_cast<const uint2*>(qd + row * (k / 2) + c16 / 2);
+
+// OCP FP8 E4M3 (float8_e4m3fn) -> fp32, exact: exponent bias 7 -> 127 is a
+// shift of the 7 magnitude bits by 20 plus 120 << 23; exponent 0 is m * 2^-9;
+// S.1111.111 is NaN.
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  const uint32_t mag = b & 0x7Fu;
+  float v = mag >= 8u ? __uint_as_float((mag << 20) + (120u << 23)) : (float)mag * 0.001953125f;
+  if (mag == 0x7Fu) v = __uint_as_float(0x7FC00000u);
+  return (b & 0x80u) ? -v : v;
+}
+
+template <bool E4M3>
+__device__ __forceinline__ float group_scale(const void* s_rel, int64_t i) {
+  if constexpr (E4M3) return e4m3_to_f32(static_cast<const uint8_t*>(s_rel)[i]);
+  else return static_cast<const float*>(s_rel)[i];
+}
+
+__device__ __forceinline__ uint32_t decode_one(float level, float s) {
+  const int v = __float2int_rn(__fmul_rn(level, s));
+  return (uint32_t)(uint8_t)(int8_t)max(-127, min(127, v));
+}
+
+// 16 outputs per thread (8 packed bytes, one 16-byte store). Group sizes 4, 8
+// or a multiple of 16, so the 16 columns use 4, 2 or 1 group scales. Index
+// arithmetic is 32-bit (the launcher guarantees n * k / 16 < 2^31); byte
+// offsets are formed in 64 bits.
+template <bool E4M3, bool CODEBOOK>
+__global__ void __launch_bounds__(256) dequant_int4_kernel(const uint8_t* __restrict__ qd,
+                                                           const void* __restrict__ s_rel,
+                                                           const float* __restrict__ codebook, int n, int k,
+                                                           int group, int8_t* __restrict__ out) {
+  __shared__ float lv_s[16];
+  if constexpr (CODEBOOK) {
+    if (threadIdx.x < 16) lv_s[threadIdx.x] = codebook[threadIdx.x];
+    __syncthreads();
+  }
+  const uint32_t per_row = (uint32_t)k >> 4;
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint32_t)n * per_row) return;
+  const uint32_t row = idx / per_row;
+  const uint32_t c16 = (idx - row * per_row) << 4;
+  const int64_t sbase = (int64_t)row * (uint32_t)(k / group) + c16 / (uint32_t)group;
+  const int per_scale = group >= 16 ? 16 : group;   // columns sharing one scale
+  float s[4];
+  s[0] = group_scale<E4M3>(s_rel, sbase);
+  s[1] = s[2] = s[3] = s[0];
+  if (per_scale < 16) {
+    s[1] = group_scale<E4M3>(s_rel, sbase + 1);
+    if (per_scale < 8) {
+      s[2] = group_scale<E4M3>(s_rel, sbase + 2);
+      s[3] = group_scale<E4M3>(s_rel, sbase + 3);
+    }
+  }
+  const uint2 pk = __ldg(reinterpret_cast<const uint2*>(qd + (int64_t)row * (k >> 1) + (c16 >> 1)));
   const uint32_t w[2] = {pk.x, pk.y};
   uint32_t o[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int b = 0; b < 8; ++b) {
-    const uint32_t byte = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float u = (float)((byte >> (4 * h)) & 0xFu) - 8.0f;
-      float v = rintf(__fmul_rn(u, s));
-      v = fminf(fmaxf(v, -127.0f), 127.0f);
-      const int e = 2 * b + h;
-      o[e >> 2] |= (uint32_t)(uint8_t)(int8_t)(int)v << (8 * (e & 3));
-    }
+  for (int e = 0; e < 16; ++e) {
+    const uint32_t u = (w[e >> 3] >> (4 * (e & 7))) & 0xFu;
+    const float level = CODEBOOK ? lv_s[u] : (float)u - 8.0f;
+    const float sc = per_scale == 16 ? s[0] : (per_scale == 8 ? s[e >> 3] : s[e >> 2]);
+    o[e >> 2] |= decode_one(level, sc) << (8 * (e & 3));
   }
-  *reinterpret_cast<uint4*>(out + row * k + c16) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(out + (int64_t)row * k + c16) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Generic decode (any group size dividing k).
-__global__ void dequant_int4_scalar_kernel(const uint8_t* __restrict__ qd, const float* __restrict__ s_rel,
-                                           int64_t n, int64_t k, int64_t group, int8_t* __restrict__ out) {
+// One output per thread, for buffers without the 8/16-byte alignment above.
+template <bool E4M3, bool CODEBOOK>
+__global__ void dequant_int4_scalar_kernel(const uint8_t* __restrict__ qd, const void* __restrict__ s_rel,
+                                           const float* __restrict__ codebook, int64_t n, int64_t k, int64_t group,
+                                           int8_t* __restrict__ out) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= n * k) return;
   const int64_t row = idx / k, col = idx - row * k;
-  const uint32_t byte = qd[row * (k / 2) + col / 2];
-  const float u = (float)((byte >> (4 * (col & 1))) & 0xFu) - 8.0f;
-  float v = rintf(__fmul_rn(u, s_rel[row * (k / group) + col / group]));
-  out[idx] = (int8_t)(int)fminf(fmaxf(v, -127.0f), 127.0f);
+  const uint32_t u = (qd[row * (k / 2) + col / 2] >> (4 * (col & 1))) & 0xFu;
+  const float level = CODEBOOK ? codebook[u] : (float)u - 8.0f;
+  out[idx] = (int8_t)decode_one(level, group_scale<E4M3>(s_rel, row * (k / group) + col / group));
 }
 
 // ---------------------------------------------------------------------------
@@ -533,18 +576,24 @@ __global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * cr_teams<PPW>()), 1)
 
 }  // namespace
 
-cudaError_t launch_dequant_int4(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k, int64_t group,
-                                int8_t* out, cudaStream_t stream) {
+cudaError_t launch_dequant_int4(const int8_t* qdata, const void* s_rel, bool s_rel_e4m3, const float* codebook,
+                                int64_t n, int64_t k, int64_t group, int8_t* out, cudaStream_t stream) {
   if (n == 0 || k == 0) return cudaSuccess;
+  if (k % 16 || group < 4 || k % group || (16 % group && group % 16)) return cudaErrorNotSupported;
   const uint8_t* qd = reinterpret_cast<const uint8_t*>(qdata);
-  if (group % 16 == 0 && k % 16 == 0 && !(reinterpret_cast<uintptr_t>(qdata) & 7) &&
-      !(reinterpret_cast<uintptr_t>(out) & 15)) {
-    const int64_t total = n * (k / 16);
-    dequant_int4_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(qd, s_rel, n, k, group, out);
+  const bool vec = !(reinterpret_cast<uintptr_t>(qdata) & 7) && !(reinterpret_cast<uintptr_t>(out) & 15) &&
+                   n * (k / 16) < (int64_t(1) << 31) && k < (int64_t(1) << 31);
+  const int64_t total = vec ? n * (k / 16) : n * k;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+#define H3_DEQ(E, C)                                                                                         \
+  (vec ? dequant_int4_kernel<E, C><<<grid, 256, 0, stream>>>(qd, s_rel, codebook, (int)n, (int)k, (int)group, out) \
+       : dequant_int4_scalar_kernel<E, C><<<grid, 256, 0, stream>>>(qd, s_rel, codebook, n, k, group, out))
+  if (s_rel_e4m3) {
+    if (codebook) H3_DEQ(true, true); else H3_DEQ(true, false);
   } else {
-    const int64_t total = n * k;
-    dequant_int4_scalar_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(qd, s_rel, n, k, group, out);
+    if (codebook) H3_DEQ(false, true); else H3_DEQ(false, false);
   }
+#undef H3_DEQ
   return cudaGetLastError();
 }
 

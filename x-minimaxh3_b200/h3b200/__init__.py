@@ -17,6 +17,7 @@ from .ops import (  # noqa: F401
     dequant_int4_grouped_to_int8,
     fused_gated_mlp,
     fused_gated_mlp_swiglu,
+    fused_gated_mlp_swiglu_w4a8,
     fused_gated_mlp_w4a8,
     input_act_code,
     input_act_width,
@@ -36,10 +37,12 @@ from .pipeline import fused_gated_mlp_host  # noqa: F401
 from .rope import rope_grid_table  # noqa: F401
 from .weights import (  # noqa: F401
     SwiGLUMLPWeights,
+    W4A8SwiGLUMLPWeights,
     W4A8MLPWeights,
     W8A8MLPWeights,
     quantize_int8_convrot_weight,
     quantize_int8_weight,
+    quantize_w4a8_int8_weight,
     quantize_w4a8_weight,
     rotate_weight,
 )

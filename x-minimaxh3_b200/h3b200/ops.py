@@ -26,6 +26,7 @@ __all__ = [
     "dequant_gated_residual",
     "fused_gated_mlp",
     "fused_gated_mlp_w4a8",
+    "fused_gated_mlp_swiglu_w4a8",
     "adaln_rms_rope",
     "adaln_rms_rope_",
     "rms_rope_split_half",
@@ -470,20 +471,42 @@ def rms_rope_split_half(q, k, freqs_cis, q_scale, k_scale=None, epsilon: float =
 # ---------------------------------------------------------------------------
 
 
-def dequant_int4_grouped_to_int8(qdata: torch.Tensor, s_rel: torch.Tensor, group_size: int) -> torch.Tensor:
-    """Decode packed uint4 to the int8 grid (eager/w4a8_int8.py:344-363; CUDA w4a8_gemm.cu:36-90)."""
+_S_REL_DTYPE_CODES = {torch.float32: 0, torch.float8_e4m3fn: 5}   # eager/quantization.py:34-40 codes
+
+
+def _s_rel_code(s_rel: torch.Tensor) -> int:
+    code = _S_REL_DTYPE_CODES.get(s_rel.dtype)
+    if code is None:
+        raise ValueError(f"s_rel must be float32 or float8_e4m3fn, got {s_rel.dtype}")
+    return code
+
+
+def _codebook(codebook, device):
+    if codebook is None:
+        return None
+    cb = codebook.to(device=device, dtype=torch.float32).contiguous()
+    if tuple(cb.shape) != (16,):
+        raise ValueError(f"codebook must have shape (16,), got {tuple(cb.shape)}")
+    return cb
+
+
+def dequant_int4_grouped_to_int8(qdata: torch.Tensor, s_rel: torch.Tensor, group_size: int,
+                                 codebook: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode packed uint4 to the int8 grid, ``clamp(rne(level(u) * s_rel), -127, 127)`` with
+    ``level(u) = u - 8`` or ``codebook[u]``; ``s_rel`` fp32 or float8_e4m3fn
+    (eager/w4a8_int8.py:344-363; CUDA w4a8_gemm.cu:36-121)."""
     _need_cuda(qdata, s_rel)
-    if s_rel.dtype != torch.float32:
-        raise NotImplementedError("h3b200 builds fp32 s_rel only (no fp8-e4m3 scales, no codebook)")
+    code = _s_rel_code(s_rel)
     qd = qdata.contiguous()
     n, kh = qd.shape
     k = kh * 2
     sr = s_rel.contiguous()
     if tuple(sr.shape) != (n, k // group_size):
         raise ValueError(f"s_rel must have shape {(n, k // group_size)}, got {tuple(sr.shape)}")
+    cb = _codebook(codebook, qd.device)
     out = torch.empty((n, k), dtype=torch.int8, device=qd.device)
-    _lib.call("h3b200_dequant_int4_grouped_to_int8", qd.data_ptr(), sr.data_ptr(), n, k, group_size, out.data_ptr(),
-              _stream(qd))
+    _lib.call("h3b200_dequant_int4_grouped_to_int8_ex", qd.data_ptr(), sr.data_ptr(), code, _ptr(cb), n, k,
+              group_size, out.data_ptr(), _stream(qd))
     return out
 
 
@@ -519,6 +542,33 @@ def segment_row_map(length: int, segments, device) -> torch.Tensor:
     return host.to(device)
 
 
+def _gate_rows(gate: torch.Tensor, segments, m: int, d: int, device):
+    """(gate rows [rows, d] contiguous, int32 row map [m] or None, row stride) of a gated
+    residual: one row [d] without segments, else the ``(start, stop, row)`` partition."""
+    if segments is None:
+        g = gate.reshape(-1).contiguous()
+        if g.numel() != d:
+            raise ValueError(f"gate must have {d} elements when no segments are given")
+        return g, None, d
+    g = gate.reshape(-1, d).contiguous()
+    row_map = segment_row_map(m, segments, device)
+    if m and int(row_map.max()) >= g.shape[0]:
+        raise ValueError(f"a segment names gate row {int(row_map.max())}, gate has {g.shape[0]} rows")
+    return g, row_map, d
+
+
+def _mlp_io(residual, hidden, gate, d_w):
+    _need_cuda(residual, hidden, gate)
+    for name, t in (("residual", residual), ("hidden", hidden), ("gate", gate)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16, got {t.dtype}")
+    x2, ldx = _rows(hidden)
+    r2, ldr = _rows(residual)
+    if x2.shape[1] != d_w or r2.shape != x2.shape:
+        raise ValueError(f"hidden/residual [M, {x2.shape[1]}] do not match the weights (d={d_w})")
+    return x2, ldx, r2, ldr
+
+
 def fused_gated_mlp_swiglu(residual: torch.Tensor, hidden: torch.Tensor, weights, gate: torch.Tensor,
                            segments=None, out: torch.Tensor | None = None, chunk_tokens: int = 8192,
                            workspace: torch.Tensor | None = None) -> torch.Tensor:
@@ -530,27 +580,10 @@ def fused_gated_mlp_swiglu(residual: torch.Tensor, hidden: torch.Tensor, weights
     ``residual[a:b].addcmul_(y[a:b], gate[row])`` for each ``(a, b, row)`` in
     ``segments`` (``gate`` [rows, d]); with ``segments=None`` ``gate`` is one row [d].
     ``weights`` is a :class:`h3b200.SwiGLUMLPWeights`; ``out`` may be ``residual``."""
-    _need_cuda(residual, hidden, gate)
-    for name, t in (("residual", residual), ("hidden", hidden), ("gate", gate)):
-        if t.dtype != torch.bfloat16:
-            raise ValueError(f"{name} must be bf16, got {t.dtype}")
-    x2, ldx = _rows(hidden)
-    r2, ldr = _rows(residual)
+    x2, ldx, r2, ldr = _mlp_io(residual, hidden, gate, weights.d)
     m, d = x2.shape
     ffn = weights.ffn
-    if weights.d != d or r2.shape != x2.shape:
-        raise ValueError(f"hidden/residual [M, {d}] do not match the weights (d={weights.d})")
-    if segments is None:
-        g = gate.reshape(-1).contiguous()
-        if g.numel() != d:
-            raise ValueError(f"gate must have {d} elements when no segments are given")
-        row_map, ldg = None, d
-    else:
-        g = gate.reshape(-1, d).contiguous()
-        row_map = segment_row_map(m, segments, hidden.device)
-        if m and int(row_map.max()) >= g.shape[0]:
-            raise ValueError(f"a segment names gate row {int(row_map.max())}, gate has {g.shape[0]} rows")
-        ldg = d
+    g, row_map, ldg = _gate_rows(gate, segments, m, d, hidden.device)
     if out is None:
         out = torch.empty_like(r2)
     o2, ldo = _rows(out)
@@ -567,6 +600,51 @@ def fused_gated_mlp_swiglu(residual: torch.Tensor, hidden: torch.Tensor, weights
     return out
 
 
+def fused_gated_mlp_swiglu_w4a8(residual: torch.Tensor, hidden: torch.Tensor, weights, gate: torch.Tensor,
+                                segments=None, out: torch.Tensor | None = None, chunk_tokens: int = 8192,
+                                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The H3 SwiGLU MLP on W4A8 weights (H3 release format: group 16, fp8-e4m3 ``s_rel``,
+    16-level codebook, symmetric, ConvRot-256), gated residual per modulation segment.
+
+    Drop-in for the W4A8 path of ``try_fused_gated_mlp``, ``_chunked_module_gated_mlp``
+    (h3serve/native_engine/model/fused_mlp.py:222-266) over ``ConvRotW4A8Linear`` modules
+    bound to ``comfy_kitchen.w4a8_int8_linear`` (quantization.py:64-95, 416-600):
+    ``raw = fc1(hidden)``, ``y = fc2(silu(raw_gate) * raw_up)``, then the per-segment
+    ``addcmul_``. ``weights`` is a :class:`h3b200.W4A8SwiGLUMLPWeights`; both int4 weights
+    are decoded once per call into the workspace; ``out`` may be ``residual``."""
+    x2, ldx, r2, ldr = _mlp_io(residual, hidden, gate, weights.d)
+    m, d = x2.shape
+    ffn = weights.ffn
+    if weights.s_rel1.dtype != weights.s_rel2.dtype:
+        raise ValueError("fc1 and fc2 s_rel must have the same dtype")
+    code = _s_rel_code(weights.s_rel1)
+    gsz = int(weights.group_size)
+    for name, t, shape in (("s_rel1", weights.s_rel1, (2 * ffn, d // gsz)), ("s_rel2", weights.s_rel2, (d, ffn // gsz)),
+                           ("s_ch1", weights.s_ch1, (2 * ffn,)), ("s_ch2", weights.s_ch2, (d,)),
+                           ("q2", weights.q2, (d, ffn // 2))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {shape}, got {tuple(t.shape)}")
+    g, row_map, ldg = _gate_rows(gate, segments, m, d, hidden.device)
+    if out is None:
+        out = torch.empty_like(r2)
+    o2, ldo = _rows(out)
+    chunk = max(1, min(int(chunk_tokens), m)) if m else 1
+    nbytes = int(_lib.load().h3b200_fused_gated_mlp_swiglu_w4a8_workspace_bytes(chunk, d, ffn))
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
+    c = lambda t: t.contiguous()  # noqa: E731
+    sc1 = weights.s_ch1.to(torch.float32).contiguous()
+    sc2 = weights.s_ch2.to(torch.float32).contiguous()
+    cb1 = _codebook(weights.codebook1, hidden.device)
+    cb2 = _codebook(weights.codebook2, hidden.device)
+    q1, q2, sr1, sr2 = c(weights.q1), c(weights.q2), c(weights.s_rel1), c(weights.s_rel2)
+    _lib.call("h3b200_fused_gated_mlp_swiglu_w4a8", x2.data_ptr(), ldx, q1.data_ptr(), sr1.data_ptr(),
+              sc1.data_ptr(), _ptr(cb1), _ptr(weights.b1), q2.data_ptr(), sr2.data_ptr(), sc2.data_ptr(), _ptr(cb2),
+              _ptr(weights.b2), code, gsz, g.data_ptr(), ldg, _ptr(row_map), r2.data_ptr(), ldr, o2.data_ptr(), ldo,
+              m, d, ffn, chunk, workspace.data_ptr(), workspace.numel(), _stream(hidden))
+    return out
+
+
 def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, s_channel: torch.Tensor,
                      codebook: torch.Tensor | None = None, correction: torch.Tensor | None = None,
                      bias: torch.Tensor | None = None, group_size: int = 16, convrot_groupsize: int = 256,
@@ -574,15 +652,14 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
                      input_act=None) -> torch.Tensor:
     """W4A8 linear (``comfy_kitchen`` w4a8_int8_linear, tensor/w4a8_int8.py:89-115; CUDA
     backends/cuda/__init__.py:2139-2298): ConvRot-quantize x, INT8 GEMM against
-    the decoded int8 grid, dequant by ``s_channel``, asymmetric group correction.
+    the decoded int8 grid, dequant by ``s_channel``, then the asymmetric group
+    correction (``correction`` given) or the bias (symmetric weights: the call is
+    ``int8_linear(x, grid, s_channel, bias, convrot=True)``, eager/w4a8_int8.py:494-508).
+    ``s_rel`` fp32 or float8_e4m3fn; ``codebook`` the 16 levels of the H3 release format.
 
     ``grid`` is the decoded weight from :func:`dequant_int4_grouped_to_int8`;
     pass it to keep the decode out of the per-call path (weights are static)."""
     _need_cuda(x, qdata, s_rel, s_channel)
-    if codebook is not None:
-        raise NotImplementedError("codebook W4A8 is not built in h3b200")
-    if bias is not None:
-        raise NotImplementedError("bias is not built for W4A8")
     if out_dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
         raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
     n, kh = qdata.shape
@@ -590,13 +667,20 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     if _act_k(x, input_act) != k:
         raise ValueError(f"Input K={_act_k(x, input_act)} (after input_act) does not match qdata K={k}")
     if grid is None:
-        grid = dequant_int4_grouped_to_int8(qdata, s_rel, group_size)
+        grid = dequant_int4_grouped_to_int8(qdata, s_rel, group_size, codebook)
     groups = k // group_size
     corr = None
     if correction is not None:
+        if bias is not None:
+            raise NotImplementedError("h3b200 builds a bias for symmetric W4A8 weights (no correction) only")
         if tuple(correction.shape) != (groups, n):
             raise ValueError(f"correction must have shape {(groups, n)}, got {tuple(correction.shape)}")
         corr = correction.to(torch.bfloat16).contiguous()
+    b = None
+    if bias is not None:
+        b = bias.to(torch.bfloat16).contiguous().reshape(-1)
+        if b.numel() != n:
+            raise ValueError(f"bias must have {n} elements, got {b.numel()}")
     sch = s_channel.to(torch.float32).contiguous()
     if tuple(sch.shape) != (n,):
         raise ValueError(f"s_channel must have shape {(n,)}, got {tuple(sch.shape)}")
@@ -606,6 +690,6 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     nbytes = int(_lib.load().h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size))
     work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
     _lib.call("h3b200_w4a8_int8_linear", x2.data_ptr(), ldx, grid.contiguous().data_ptr(), sch.data_ptr(), _ptr(corr),
-              group_size, convrot_groupsize, input_act_code(input_act), out.data_ptr(), m, n, k, work.data_ptr(),
-              nbytes, _stream(x))
+              _ptr(b), group_size, convrot_groupsize, input_act_code(input_act), out.data_ptr(), m, n, k,
+              work.data_ptr(), nbytes, _stream(x))
     return out.reshape(*x.shape[:-1], n)

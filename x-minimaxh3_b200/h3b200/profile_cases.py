@@ -8,6 +8,9 @@ the plain dequant or the int32 epilogue), ``requant`` (fc2 input quantizer with 
 given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
 ``mlp`` (the whole fused MLP call), ``mlp_w4a8`` (the config-2 W4A8 MLP call), ``mlp_swiglu``
 (the H3 SwiGLU MLP at d 5,376 / ffn 14,336, ConvRot fc1 and fc2, 8,192-token chunks),
+``mlp_swiglu_w4`` (the same MLP on W4A8 weights in the H3 release format: group 16,
+fp8-e4m3 scales, codebook; both weights decoded per call), ``decode_w4`` (that
+format's int4 -> int8 decode of the fc1 weight, 28,672 x 5,376),
 ``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
 Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
 norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
@@ -96,6 +99,21 @@ def run(case: str, m: int, iters: int, report: bool = False):
         res = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
         out = torch.empty_like(res)
         ms = _timed(lambda: h3b200.fused_gated_mlp_swiglu(res, x, wt, gate, out=out), iters, report)
+    elif case in ("mlp_swiglu_w4", "decode_w4"):
+        g = torch.Generator(device=dev).manual_seed(9)
+        d, ffn = 5376, 14336
+        w1 = (torch.randn(2 * ffn, d, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn(d, ffn, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w4 = h3b200.W4A8SwiGLUMLPWeights.from_float(w1, w2)
+        del w1, w2
+        if case == "decode_w4":
+            ms = _timed(lambda: ops.dequant_int4_grouped_to_int8(w4.q1, w4.s_rel1, 16, w4.codebook1), iters, report)
+        else:
+            x = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+            gate = torch.randn(d, generator=g, device=dev).to(torch.bfloat16)
+            res = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty_like(res)
+            ms = _timed(lambda: h3b200.fused_gated_mlp_swiglu_w4a8(res, x, w4, gate, out=out), iters, report)
     elif case == "mlp_w4a8":
         g = torch.Generator(device=dev).manual_seed(3)
         w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
@@ -148,7 +166,8 @@ def run(case: str, m: int, iters: int, report: bool = False):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", nargs="+", choices=["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp",
-                                                "mlp_w4a8", "mlp_swiglu", "convrot", "convrot_x", "norm_rope"])
+                                                "mlp_w4a8", "mlp_swiglu", "mlp_swiglu_w4", "decode_w4", "convrot",
+                                                "convrot_x", "norm_rope"])
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="report the mean CUDA-event time per launch")
