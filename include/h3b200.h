@@ -220,6 +220,64 @@ H3B200_API int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, 
                           int64_t rot_dim, int norm_span, float eps, h3b200_stream_t stream);
 
 /*
+ * Per-head RMSNorm + partial split-half RoPE on one tensor (k == NULL) or two,
+ * over strided bf16 [m, heads, head_dim] views: element strides token (_st)
+ * and head (_sh), unit stride on head_dim. Outputs may alias the inputs (in
+ * place) or be other views, e.g. an HND-backed NHD view of an attention
+ * buffer [heads, tokens, head_dim] (qo_st = head_dim, qo_sh = tokens * head_dim).
+ *   h = bf16((x / sqrt(mean(x^2) + eps)) * w)   (w: bf16 [head_dim] per tensor)
+ *   y[i] = t00 h[i] + t01 h[i + r/2], y[i + r/2] = t10 h[i] + t11 h[i + r/2]  (i < r/2)
+ *   y[i] = h[i] for i >= r = rot_dim (0: head_dim)
+ * freqs: rows of [r/2, 2, 2] values, dtype code 0 (float32), 1 (float16) or
+ * 2 (bfloat16; widened to fp32), at element stride f_st per token and f_sh
+ * per head (0 = one row shared by all heads); freqs NULL: RMSNorm only (the
+ * reference's q_norm / k_norm without frequencies). head_dim 128, rot_dim a
+ * multiple of 16; pointers 16-byte aligned, strides multiples of 8 elements.
+ * Replaces launch_rms_rope_kernel with split_half = true and has_k = false
+ * (single side) or true (backends/cuda/ops/rms_rope.cu:36-229, launcher
+ * :353-384), as bound by h3serve/native_engine/model/single_qknorm_rope.py:
+ * 37-63 (_try_apply_single_qknorm_rope_out :69-181, the HND target :209-236);
+ * eager semantics backends/eager/rope.py:67-92.
+ */
+H3B200_API int h3b200_qknorm_rope_strided(const void* q, int64_t q_st, int64_t q_sh, void* q_out, int64_t qo_st,
+                                          int64_t qo_sh, const void* q_weight, const void* k, int64_t k_st,
+                                          int64_t k_sh, void* k_out, int64_t ko_st, int64_t ko_sh,
+                                          const void* k_weight, const void* freqs, int freqs_dtype, int64_t f_st,
+                                          int64_t f_sh, int64_t m, int64_t heads, int64_t head_dim,
+                                          int64_t rot_dim, float eps, h3b200_stream_t stream);
+
+/*
+ * Q/K/V projection of one token chunk with QK-norm + partial RoPE into the
+ * attention layout, from an activation quantized once (ConvRot or plain,
+ * h3b200_quantize_int8_rowwise_convrot / h3b200_quantize_int8_rowwise):
+ *   proj = int8_linear_prequantized(xq, x_scale, W[rows of sections], w_scale, bias)
+ *   Q -> q_out, K -> k_out: per-head RMSNorm (q/k norm weight, bf16 [head_dim])
+ *        and split-half RoPE as h3b200_qknorm_rope_strided (freqs NULL: RMSNorm only)
+ *   V -> v_out unchanged
+ * Sections [sec_begin, sec_end) of {0: Q, 1: K, 2: V}: (0, 3) all three,
+ * (1, 3) the K/V build, (0, 1) a query chunk. w_qkv: int8 [3 heads head_dim, k]
+ * (rows Q | K | V), w_scale fp32 [3 heads head_dim] or [1], bias bf16
+ * [3 heads head_dim] or NULL; xq int8 [m, k], x_scale fp32 [m]. Outputs are
+ * [m, heads, head_dim] views with element strides token (_st) and head (_sh),
+ * e.g. HND buffers (st = head_dim, sh = tokens * head_dim). workspace:
+ * h3b200_qkv_qknorm_rope_workspace_bytes(m, heads, head_dim, sec_begin, sec_end).
+ * Replaces the H3 long-sequence attention build
+ * (h3serve/native_engine/model/layers.py:445-641: prepare_output_slices /
+ * forward_prepared_output_slice, quantization.py:340-415, with
+ * try_apply_single_qknorm_rope_to_hnd for K and Q and the V copy into HND).
+ */
+H3B200_API int64_t h3b200_qkv_qknorm_rope_workspace_bytes(int64_t m, int64_t heads, int64_t head_dim, int sec_begin,
+                                                         int sec_end);
+H3B200_API int h3b200_qkv_qknorm_rope(const int8_t* xq, const float* x_scale, int64_t m, int64_t k,
+                                      const int8_t* w_qkv, const float* w_scale, int64_t w_scale_numel,
+                                      const void* bias, int64_t heads, int64_t head_dim, int sec_begin, int sec_end,
+                                      const void* q_norm_weight, const void* k_norm_weight, const void* freqs,
+                                      int freqs_dtype, int64_t f_st, int64_t f_sh, int64_t rot_dim, float eps,
+                                      void* q_out, int64_t q_st, int64_t q_sh, void* k_out, int64_t k_st,
+                                      int64_t k_sh, void* v_out, int64_t v_st, int64_t v_sh, void* workspace,
+                                      int64_t workspace_bytes, h3b200_stream_t stream);
+
+/*
  * W4A8: decode packed uint4 weights to the int8 grid,
  * clamp(rne((u - 8) * s_rel[row, group]), -127, 127), even column = low nibble.
  * Replaces _C.dequant_int4_grouped_to_int8 (dlpack_bindings.cpp:2781-2790;

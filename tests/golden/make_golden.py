@@ -326,6 +326,33 @@ def main() -> None:
                      "big_s_rel_sha": digest(sre), "big_s_ch": sce.numpy(), "big_codebook": cbe.numpy()})
     out["w4a8_h3"] = arrays10
 
+    # 11. H3 QK-norm + partial RoPE at the H3 head layout (56 heads x 128, rot_dim 96 = 3 axes
+    #     x 16 pairs, eps 1e-5), table from H3's own rope_frequencies / rope_rotation_table
+    #     (layers.py:51-69) on a (t, h, w) grid, fp32 and bf16. Reference outputs: comfy eager
+    #     rms_rope_split_half (fp32 table), the same with the bf16 table, and H3's CPU
+    #     single-side path _apply_single_qknorm_rope (layers.py:152-231, bf16 table) for Q and K.
+    gr = torch.Generator().manual_seed(10)
+    m11, h11 = 16, 56
+    inv11 = 1.0 / (10000.0 ** (torch.arange(0, 32, 2, dtype=torch.float32) / 32.0))
+    tt, hh, ww = torch.meshgrid(torch.arange(2) + 3, torch.arange(2) + 17, torch.arange(4) + 29, indexing="ij")
+    pos11 = torch.stack([tt.reshape(-1), hh.reshape(-1), ww.reshape(-1)], dim=-1)
+    ang11 = h3layers.rope_frequencies(pos11, inv11)
+    tab32 = h3layers.rope_rotation_table(ang11, torch.float32)
+    tab16 = h3layers.rope_rotation_table(ang11, torch.bfloat16)
+    q11 = (torch.randn(m11, h11, 128, generator=gr) * 1.5).to(torch.bfloat16)
+    k11 = (torch.randn(m11, h11, 128, generator=gr) * 0.7).to(torch.bfloat16)
+    wq11 = (1 + 0.02 * torch.randn(128, generator=gr)).to(torch.bfloat16)
+    wk11 = (1 + 0.02 * torch.randn(128, generator=gr)).to(torch.bfloat16)
+    q32, k32 = erope.rms_rope_split_half(q11.unsqueeze(0), k11.unsqueeze(0), tab32, wq11, wk11, 1e-5, 96)
+    q16, k16 = erope.rms_rope_split_half(q11.unsqueeze(0), k11.unsqueeze(0), tab16, wq11, wk11, 1e-5, 96)
+    qh3 = h3layers._apply_single_qknorm_rope(q11, weight=wq11, frequencies=tab16, eps=1e-5, query_slot=True)
+    kh3 = h3layers._apply_single_qknorm_rope(k11, weight=wk11, frequencies=tab16, eps=1e-5, query_slot=False)
+    out["qknorm_rope_h3"] = {
+        "q": b16(q11), "k": b16(k11), "wq": b16(wq11), "wk": b16(wk11), "table_f32": tab32.reshape(m11, 48, 2, 2).numpy(),
+        "table_bf16": b16(tab16.reshape(m11, 48, 2, 2)), "q_f32tab": b16(q32[0]), "k_f32tab": b16(k32[0]),
+        "q_bf16tab": b16(q16[0]), "k_bf16tab": b16(k16[0]), "q_h3": b16(qh3), "k_h3": b16(kh3),
+    }
+
     for name, arrays in out.items():
         if args.only is not None and name not in args.only:
             continue

@@ -250,6 +250,89 @@ int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk
   return from_cuda(h3::launch_adaln_rms_rope(a, S(stream)), "adaln_rms_rope");
 }
 
+int h3b200_qknorm_rope_strided(const void* q, int64_t q_st, int64_t q_sh, void* q_out, int64_t qo_st,
+                               int64_t qo_sh, const void* q_weight, const void* k, int64_t k_st, int64_t k_sh,
+                               void* k_out, int64_t ko_st, int64_t ko_sh, const void* k_weight, const void* freqs,
+                               int freqs_dtype, int64_t f_st, int64_t f_sh, int64_t m, int64_t heads,
+                               int64_t head_dim, int64_t rot_dim, float eps, h3b200_stream_t stream) {
+  const char* who = "qknorm_rope_strided";
+  if (m < 0 || heads <= 0 || head_dim <= 0) return fail(H3B200_ERR_INVALID, "%s: bad shape", who);
+  const int64_t rot = rot_dim == 0 ? head_dim : rot_dim;
+  if (rot < 0 || rot > head_dim || rot % 4) return fail(H3B200_ERR_INVALID, "%s: rot_dim %lld invalid for head_dim %lld", who, (long long)rot_dim, (long long)head_dim);
+  if (head_dim != 128 || rot % 16) return fail(H3B200_ERR_UNSUPPORTED, "%s: head_dim 128 with rot_dim a multiple of 16 is built (got %lld, %lld)", who, (long long)head_dim, (long long)rot);
+  if (freqs_dtype != H3B200_DTYPE_F32 && freqs_dtype != H3B200_DTYPE_BF16 && freqs_dtype != H3B200_DTYPE_F16)
+    return fail(H3B200_ERR_INVALID, "%s: freqs dtype code must be 0 (float32), 1 (float16) or 2 (bfloat16), got %d", who, freqs_dtype);
+  if (f_st < 0 || f_sh < 0) return fail(H3B200_ERR_INVALID, "%s: negative table stride", who);
+  if (m == 0) return H3B200_OK;
+  if (!q || !q_out || !q_weight || (k && (!k_out || !k_weight))) return fail(H3B200_ERR_INVALID, "%s: NULL pointer", who);
+  h3::QKNormRopeArgs a;
+  a.x[0] = q; a.y[0] = q_out; a.w[0] = q_weight; a.xs_t[0] = q_st; a.xs_h[0] = q_sh; a.ys_t[0] = qo_st; a.ys_h[0] = qo_sh;
+  a.tensors = k ? 2 : 1;
+  if (k) {
+    a.x[1] = k; a.y[1] = k_out; a.w[1] = k_weight; a.xs_t[1] = k_st; a.xs_h[1] = k_sh; a.ys_t[1] = ko_st; a.ys_h[1] = ko_sh;
+  }
+  a.freqs = freqs;
+  a.table_dtype = freqs_dtype == H3B200_DTYPE_F32 ? 0 : (freqs_dtype == H3B200_DTYPE_BF16 ? 1 : 2);
+  a.fs_t = f_st; a.fs_h = f_sh;
+  a.m = m; a.heads = heads; a.head_dim = head_dim; a.rot_dim = rot; a.eps = eps;
+  return from_cuda(h3::launch_qk_rms_rope(a, S(stream)), who);
+}
+
+int64_t h3b200_qkv_qknorm_rope_workspace_bytes(int64_t m, int64_t heads, int64_t head_dim, int sec_begin,
+                                              int sec_end) {
+  if (m < 0 || heads <= 0 || head_dim <= 0 || sec_begin < 0 || sec_end > 3 || sec_begin >= sec_end) return 0;
+  return round_up(m * (sec_end - sec_begin) * heads * head_dim * 2, 256) + 256;
+}
+
+int h3b200_qkv_qknorm_rope(const int8_t* xq, const float* x_scale, int64_t m, int64_t k, const int8_t* w_qkv,
+                           const float* w_scale, int64_t w_scale_numel, const void* bias, int64_t heads,
+                           int64_t head_dim, int sec_begin, int sec_end, const void* q_norm_weight,
+                           const void* k_norm_weight, const void* freqs, int freqs_dtype, int64_t f_st, int64_t f_sh,
+                           int64_t rot_dim, float eps, void* q_out, int64_t q_st, int64_t q_sh, void* k_out,
+                           int64_t k_st, int64_t k_sh, void* v_out, int64_t v_st, int64_t v_sh, void* workspace,
+                           int64_t workspace_bytes, h3b200_stream_t stream) {
+  const char* who = "qkv_qknorm_rope";
+  if (m < 0 || k <= 0 || heads <= 0 || head_dim != 128) return fail(H3B200_ERR_INVALID, "%s: bad shape (head_dim must be 128)", who);
+  if (sec_begin < 0 || sec_end > 3 || sec_begin >= sec_end) return fail(H3B200_ERR_INVALID, "%s: section range [%d, %d) is not a non-empty part of Q|K|V", who, sec_begin, sec_end);
+  const int64_t inner = heads * head_dim;
+  if (w_scale_numel != 1 && w_scale_numel != 3 * inner) return fail(H3B200_ERR_INVALID, "%s: weight scale must be scalar or [3 * heads * head_dim]", who);
+  const bool has_q = sec_begin == 0, has_k = sec_begin <= 1 && sec_end >= 2, has_v = sec_end == 3;
+  if ((has_q && (!q_out || !q_norm_weight)) || (has_k && (!k_out || !k_norm_weight)) || (has_v && !v_out))
+    return fail(H3B200_ERR_INVALID, "%s: an output or norm weight of a requested section is NULL", who);
+  if (m == 0) return H3B200_OK;
+  if (!xq || !x_scale || !w_qkv || !w_scale) return fail(H3B200_ERR_INVALID, "%s: NULL pointer", who);
+  if (k % 16) return fail(H3B200_ERR_UNSUPPORTED, "%s: needs k %% 16 == 0", who);
+  const int64_t need = h3b200_qkv_qknorm_rope_workspace_bytes(m, heads, head_dim, sec_begin, sec_end);
+  if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "%s: workspace too small (need %lld bytes)", who, (long long)need);
+  cudaStream_t st = S(stream);
+  const int64_t n = (sec_end - sec_begin) * inner;
+  auto* proj = static_cast<__nv_bfloat16*>(workspace);
+  // the requested Q/K/V rows of the projection: dequant (+ bias) into [m, n] bf16
+  h3::GemmArgs g;
+  g.a = xq; g.w = w_qkv + sec_begin * inner * k; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = h3::kEpiBF16; g.a_scale = x_scale;
+  g.w_scale = w_scale_numel == 1 ? w_scale : w_scale + sec_begin * inner;
+  g.w_scale_per_channel = w_scale_numel == 1 ? 0 : 1;
+  g.bias = bias ? static_cast<const __nv_bfloat16*>(bias) + sec_begin * inner : nullptr;
+  g.out = proj; g.ldo = n;
+  cudaError_t e = h3::launch_gemm_i8(g, st);
+  if (e != cudaSuccess) return from_cuda(e, "qkv_qknorm_rope: projection");
+  // QK-norm + RoPE of the Q and K sections (one launch for both) into the caller's views
+  if (has_q || has_k) {
+    const int rc = h3b200_qknorm_rope_strided(
+        has_q ? proj : proj + (1 - sec_begin) * inner, n, head_dim, has_q ? q_out : k_out, has_q ? q_st : k_st,
+        has_q ? q_sh : k_sh, has_q ? q_norm_weight : k_norm_weight, has_q && has_k ? proj + inner : nullptr, n,
+        head_dim, has_q && has_k ? k_out : nullptr, k_st, k_sh, k_norm_weight, freqs, freqs_dtype, f_st, f_sh, m,
+        heads, head_dim, rot_dim, eps, stream);
+    if (rc != H3B200_OK) return rc;
+  }
+  if (has_v) {
+    e = h3::launch_copy_heads(proj + (2 - sec_begin) * inner, n, head_dim, v_out, v_st, v_sh, m, heads, st);
+    if (e != cudaSuccess) return from_cuda(e, "qkv_qknorm_rope: V layout");
+  }
+  return H3B200_OK;
+}
+
 int h3b200_dequant_int4_grouped_to_int8_ex(const int8_t* qdata, const void* s_rel, int s_rel_dtype,
                                            const float* codebook, int64_t n, int64_t k, int64_t group_size,
                                            int8_t* out, h3b200_stream_t stream) {

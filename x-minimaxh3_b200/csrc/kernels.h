@@ -74,6 +74,27 @@ struct NormRopeArgs {
 };
 cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream);
 
+// Per-head RMSNorm + partial split-half RoPE over strided [m, heads, 128] bf16
+// views (x[t] -> y[t], t < tensors; in place when x == y). Table rows
+// [rot/2, 2, 2] of fp32 (0), bf16 (1) or fp16 (2) at token stride fs_t and
+// head stride fs_h (0: one row per token) in elements.
+struct QKNormRopeArgs {
+  const void* x[2] = {nullptr, nullptr};
+  void* y[2] = {nullptr, nullptr};
+  const void* w[2] = {nullptr, nullptr};
+  int64_t xs_t[2] = {0, 0}, xs_h[2] = {0, 0}, ys_t[2] = {0, 0}, ys_h[2] = {0, 0};
+  const void* freqs = nullptr;
+  int table_dtype = 0;
+  int64_t fs_t = 0, fs_h = 0;
+  int64_t m = 0, heads = 0, head_dim = 128, rot_dim = 0;
+  int tensors = 1;
+  float eps = 1e-6f;
+};
+cudaError_t launch_qk_rms_rope(const QKNormRopeArgs& a, cudaStream_t stream);
+// y[t, h, :] = x[t, h, :] over strided [m, heads, 128] bf16 views
+cudaError_t launch_copy_heads(const void* x, int64_t xs_t, int64_t xs_h, void* y, int64_t ys_t, int64_t ys_h,
+                              int64_t m, int64_t heads, cudaStream_t stream);
+
 // int4 -> int8 grid; s_rel fp32 or (s_rel_e4m3) fp8-e4m3 bytes; codebook: 16 fp32 levels or nullptr (u - 8)
 cudaError_t launch_dequant_int4(const int8_t* qdata, const void* s_rel, bool s_rel_e4m3, const float* codebook,
                                 int64_t n, int64_t k, int64_t group, int8_t* out, cudaStream_t stream);

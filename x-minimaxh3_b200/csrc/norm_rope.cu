@@ -406,7 +406,221 @@ cudaError_t launch_vpl(const CUtensorMap& tm, const NRParams& p, bool row, bool 
   return full ? launch_one<VPL, false, false, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, false, false, EXACT>(tm, p, smem, st);
 }
 
+// ---------------------------------------------------------------------------
+// Per-head QK-norm + partial split-half RoPE over strided [tokens, heads, 128]
+// views, one tensor (single side) or two (Q and K), for any head count and
+// for outputs laid out for attention (HND-backed NHD views).
+//
+// Reference: launch_rms_rope_kernel with has_k = false / true and
+// split_half = true (backends/cuda/ops/rms_rope.cu:36-229, launcher :353-384),
+// called by single_qknorm_rope.py:69-181 (in place) and :209-236 (into an
+// HND-backed view); math as the eager rms_rope_split_half
+// (backends/eager/rope.py:67-92): rstd = 1 / sqrt(mean(x^2) + eps) in fp32,
+// h = bf16((x * rstd) * w), y0 = t00 h0 + t01 h1, y1 = t10 h0 + t11 h1 in fp32
+// (two products and one add), bf16; dims >= rot_dim are normalised only. A
+// bf16 or fp16 table is widened to fp32, as the reference's CUDA kernel does.
+//
+// Layout: one warp per token, two heads at a time (half-warp hsel takes head
+// 2 i + hsel), lane (l mod 16) owns dims 8 (l mod 16) .. + 7 as one 16-byte
+// vector; its RoPE partner is (l mod 16) +- rot_dim / 16, one shuffle away.
+// The rotation coefficients of the lane's 8 pairs are read once per token
+// (once per head when the table has a head stride). Heads of the second
+// tensor follow those of the first in the same loop, so the paired form reads
+// each table row once for Q and K.
+// ---------------------------------------------------------------------------
+constexpr int kQKWarpsPerBlock = 8;
+
+struct QKParams {
+  const __nv_bfloat16* x[2];
+  __nv_bfloat16* y[2];
+  int64_t xs_t[2], xs_h[2], ys_t[2], ys_h[2];  // element strides: token, head
+  const __nv_bfloat16* w[2];
+  const void* freqs;
+  int64_t fs_t, fs_h;  // table element strides: token, head (0: shared by the heads)
+  int64_t m;
+  int heads;
+  int half_v;  // rot_dim / 16: vectors in each rotation half
+  int nt;      // tensors: 1 or 2
+  float eps;
+};
+
+// fp32 coefficients (A for the lane's own value, B for the partner's) of the
+// lane's 8 pairs starting at pair0 of a table row; TAB: 0 fp32, 1 bf16, 2 fp16.
+template <int TAB>
+__device__ __forceinline__ void rope_coeffs(const void* row, int pair0, int role, uint64_t (&A)[4], uint64_t (&B)[4]) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float c[2][4];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int pr = pair0 + 2 * e + u;
+      if constexpr (TAB == 0) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(row) + pr);
+        c[u][0] = v.x; c[u][1] = v.y; c[u][2] = v.z; c[u][3] = v.w;
+      } else {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(row) + pr);
+        if constexpr (TAB == 1) {
+          c[u][0] = bf16_lo(v.x); c[u][1] = bf16_hi(v.x); c[u][2] = bf16_lo(v.y); c[u][3] = bf16_hi(v.y);
+        } else {
+          c[u][0] = __half2float(__ushort_as_half((unsigned short)(v.x & 0xFFFFu)));
+          c[u][1] = __half2float(__ushort_as_half((unsigned short)(v.x >> 16)));
+          c[u][2] = __half2float(__ushort_as_half((unsigned short)(v.y & 0xFFFFu)));
+          c[u][3] = __half2float(__ushort_as_half((unsigned short)(v.y >> 16)));
+        }
+      }
+    }
+    // role 0 (x0): t00 * x0 + t01 * x1; role 1 (x1): t11 * x1 + t10 * x0
+    A[e] = role == 0 ? f2_pack(c[0][0], c[1][0]) : f2_pack(c[0][3], c[1][3]);
+    B[e] = role == 0 ? f2_pack(c[0][1], c[1][1]) : f2_pack(c[0][2], c[1][2]);
+  }
+}
+
+template <int TAB>
+__global__ void __launch_bounds__(32 * kQKWarpsPerBlock) qk_rms_rope_kernel(const QKParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (int64_t)blockIdx.x * kQKWarpsPerBlock + (threadIdx.x >> 5);
+  if (tok >= p.m) return;  // warp-uniform
+  const int hv = lane & 15;
+  const int hsel = lane >> 4;
+  const int half_v = p.half_v;
+  const int role = hv < half_v ? 0 : (hv < 2 * half_v ? 1 : 2);  // first half, second half, pass-through
+  const int partner = (lane & 16) | (role == 0 ? hv + half_v : (role == 1 ? hv - half_v : hv));
+  const int pair0 = 8 * (role == 0 ? hv : (role == 1 ? hv - half_v : 0));
+  constexpr int kTabElemBytes = TAB == 0 ? 4 : 2;
+  const uint8_t* trow = static_cast<const uint8_t*>(p.freqs) + tok * p.fs_t * kTabElemBytes;
+
+  uint64_t A[4], B[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) A[e] = B[e] = 0;
+  if (role != 2 && p.fs_h == 0) rope_coeffs<TAB>(trow, pair0, role, A, B);
+  uint64_t wp[2][4];  // the lane's 8 weights of each tensor as fp32 pairs
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const uint4 w = t < p.nt ? ldg_nc_v4(p.w[t] + 8 * hv) : make_uint4(0, 0, 0, 0);
+    wp[t][0] = bf16x2_to_f2(w.x); wp[t][1] = bf16x2_to_f2(w.y);
+    wp[t][2] = bf16x2_to_f2(w.z); wp[t][3] = bf16x2_to_f2(w.w);
+  }
+
+  const int total = p.nt * p.heads;
+#pragma unroll 2
+  for (int base = 0; base < total; base += 2) {
+    const int hh = base + hsel;
+    const bool ok = hh < total;
+    const int hc = ok ? hh : base;  // an existing head for the half-warp past the end
+    const int t = hc >= p.heads ? 1 : 0;
+    const int h = hc - t * p.heads;
+    const uint4 xv = ldg_v4(p.x[t] + tok * p.xs_t[t] + h * p.xs_h[t] + 8 * hv);
+    if (role != 2 && p.fs_h != 0) rope_coeffs<TAB>(trow + h * p.fs_h * kTabElemBytes, pair0, role, A, B);
+    // sum of squares over the head's 128 values (16 lanes), double
+    double acc[4] = {0.0, 0.0, 0.0, 0.0};
+    sumsq8_fast(xv, acc);
+    double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    float ms = (float)(sum / 128.0);
+    const bool bad = !isfinite(ms);
+    if (__any_sync(0xffffffffu, bad)) {  // inf / NaN / huge: exact conversions
+      double ex[4] = {0.0, 0.0, 0.0, 0.0};
+      sumsq8_exact(xv, ex);
+      double se = (ex[0] + ex[1]) + (ex[2] + ex[3]);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+      if (bad) ms = (float)(se / 128.0);
+    }
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+    const uint64_t rs2 = f2_pack(rs, rs);
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t hb[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) hb[e] = f2_to_bf16x2(f2_mul(f2_mul(bf16x2_to_f2(xw[e]), rs2), wp[t][e]));
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t pw = __shfl_sync(0xffffffffu, hb[e], partner);
+      float p0, p1, q0, q1;
+      f2_unpack(f2_mul(A[e], bf16x2_to_f2(hb[e])), p0, p1);
+      f2_unpack(f2_mul(B[e], bf16x2_to_f2(pw)), q0, q1);
+      o[e] = role == 2 ? hb[e] : pack_bf16(__fadd_rn(p0, q0), __fadd_rn(p1, q1));
+    }
+    if (ok) stg_v4(p.y[t] + tok * p.ys_t[t] + h * p.ys_h[t] + 8 * hv, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+// y[t, h, :] = x[t, h, :] for [m, heads, 128] bf16 views (16-byte vectors; one
+// thread per vector, 16 per head).
+__global__ void __launch_bounds__(256) copy_heads_kernel(const __nv_bfloat16* __restrict__ x, int64_t xs_t,
+                                                         int64_t xs_h, __nv_bfloat16* __restrict__ y, int64_t ys_t,
+                                                         int64_t ys_h, int64_t m, int heads) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m * heads * 16) return;
+  const int v = (int)(i & 15);
+  const int64_t th = i >> 4;
+  const int64_t t = th / heads;
+  const int h = (int)(th - t * heads);
+  stg_v4(y + t * ys_t + h * ys_h + 8 * v, ldg_nc_v4(x + t * xs_t + h * xs_h + 8 * v));
+}
+
 }  // namespace
+
+cudaError_t launch_copy_heads(const void* x, int64_t xs_t, int64_t xs_h, void* y, int64_t ys_t, int64_t ys_h,
+                              int64_t m, int64_t heads, cudaStream_t stream) {
+  if (m == 0) return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15) || xs_t % 8 || xs_h % 8 ||
+      ys_t % 8 || ys_h % 8 || heads <= 0 || heads > (1 << 20))
+    return cudaErrorNotSupported;
+  const int64_t total = m * heads * 16;
+  copy_heads_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), xs_t, xs_h, static_cast<__nv_bfloat16*>(y), ys_t, ys_h, m, (int)heads);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qk_rms_rope(const QKNormRopeArgs& a, cudaStream_t stream) {
+  if (a.m == 0) return cudaSuccess;
+  const int64_t rot = a.rot_dim == 0 ? 128 : a.rot_dim;
+  if (a.head_dim != 128 || rot % 16 || rot <= 0 || rot > 128 || a.heads <= 0 || a.heads > (1 << 20) ||
+      (a.tensors != 1 && a.tensors != 2) || a.table_dtype < 0 || a.table_dtype > 2)
+    return cudaErrorNotSupported;
+  auto al16 = [](const void* ptr) { return ptr != nullptr && !(reinterpret_cast<uintptr_t>(ptr) & 15); };
+  QKParams p;
+  for (int t = 0; t < 2; ++t) {
+    const bool on = t < a.tensors;
+    if (on && (!al16(a.x[t]) || !al16(a.y[t]) || !al16(a.w[t]) || a.xs_t[t] % 8 || a.xs_h[t] % 8 ||
+               a.ys_t[t] % 8 || a.ys_h[t] % 8))
+      return cudaErrorNotSupported;
+    p.x[t] = static_cast<const __nv_bfloat16*>(on ? a.x[t] : a.x[0]);
+    p.y[t] = static_cast<__nv_bfloat16*>(on ? a.y[t] : a.y[0]);
+    p.w[t] = static_cast<const __nv_bfloat16*>(on ? a.w[t] : a.w[0]);
+    p.xs_t[t] = on ? a.xs_t[t] : a.xs_t[0];
+    p.xs_h[t] = on ? a.xs_h[t] : a.xs_h[0];
+    p.ys_t[t] = on ? a.ys_t[t] : a.ys_t[0];
+    p.ys_h[t] = on ? a.ys_h[t] : a.ys_h[0];
+  }
+  const int tab_bytes = a.table_dtype == 0 ? 4 : 2;
+  // table rows: [rot/2, 2, 2] contiguous, each row start 16-byte (fp32) / 8-byte (16-bit) aligned;
+  // no table: RMSNorm only (every lane passes its normalised values through)
+  const bool rope = a.freqs != nullptr;
+  if (rope && ((reinterpret_cast<uintptr_t>(a.freqs) % (2 * tab_bytes * 2)) || (a.fs_t * tab_bytes) % (4 * tab_bytes) ||
+               (a.fs_h * tab_bytes) % (4 * tab_bytes) || a.fs_t < 0 || a.fs_h < 0))
+    return cudaErrorNotSupported;
+  p.freqs = a.freqs;
+  p.fs_t = rope ? a.fs_t : 0;
+  p.fs_h = rope ? a.fs_h : 0;
+  p.m = a.m;
+  p.heads = (int)a.heads;
+  p.half_v = rope ? (int)(rot / 16) : 0;
+  p.nt = a.tensors;
+  p.eps = a.eps;
+  const int64_t blocks = (a.m + kQKWarpsPerBlock - 1) / kQKWarpsPerBlock;
+  if (blocks > 0x7FFFFFFF) return cudaErrorNotSupported;
+  const dim3 grid((unsigned)blocks), block(32 * kQKWarpsPerBlock);
+  if (a.table_dtype == 0)
+    qk_rms_rope_kernel<0><<<grid, block, 0, stream>>>(p);
+  else if (a.table_dtype == 1)
+    qk_rms_rope_kernel<1><<<grid, block, 0, stream>>>(p);
+  else
+    qk_rms_rope_kernel<2><<<grid, block, 0, stream>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   if (a.m == 0) return cudaSuccess;

@@ -30,6 +30,10 @@ from .ops import (  # noqa: F401
     quantize_int8_rowwise_convrot,
     rms_rope_split_half,
     rms_rope_split_half_,
+    qknorm_rope_strided_,
+    single_qknorm_rope_,
+    single_qknorm_rope_to_hnd,
+    qkv_qknorm_rope,
     segment_row_map,
     w4a8_int8_linear,
 )

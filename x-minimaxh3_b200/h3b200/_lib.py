@@ -47,6 +47,12 @@ SIGNATURES = {
     "h3b200_adaln_rms_rope": (_i32, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                      _i64, _i32, _f32, _p]),
     "h3b200_dequant_int4_grouped_to_int8": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p]),
+    "h3b200_qkv_qknorm_rope_workspace_bytes": (_i64, [_i64, _i64, _i64, _i32, _i32]),
+    "h3b200_qkv_qknorm_rope": (_i32, [_p, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i64, _i32, _i32, _p, _p, _p, _i32,
+                                      _i64, _i64, _i64, _f32, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p,
+                                      _i64, _p]),
+    "h3b200_qknorm_rope_strided": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _i64, _p, _i64, _i64, _p, _p,
+                                          _i32, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p]),
     "h3b200_quantize_int8_rowwise_convrot": (_i32, [_p, _i64, _i64, _i64, _i64, _i32, _p, _p, _p]),
     "h3b200_w4a8_linear_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "h3b200_dequant_int4_grouped_to_int8_ex": (_i32, [_p, _p, _i32, _p, _i64, _i64, _i64, _p, _p]),

@@ -31,6 +31,10 @@ __all__ = [
     "adaln_rms_rope_",
     "rms_rope_split_half",
     "rms_rope_split_half_",
+    "qknorm_rope_strided_",
+    "single_qknorm_rope_",
+    "single_qknorm_rope_to_hnd",
+    "qkv_qknorm_rope",
     "dequant_int4_grouped_to_int8",
     "quantize_int8_rowwise_convrot",
     "w4a8_int8_linear",
@@ -455,15 +459,205 @@ def adaln_rms_rope(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=N
                            q_out=torch.empty_like(q), k_out=torch.empty_like(k))
 
 
+_TABLE_DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}   # eager/quantization.py:34-40
+
+
+def _nhd(t: torch.Tensor, name: str) -> torch.Tensor:
+    """[1, T, H, D] / [T, H, D] bf16 with unit stride on D -> [T, H, D] view."""
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise ValueError(f"{name}: batch dimension must be 1 (packed token layout)")
+        t = t[0]
+    if t.dim() != 3:
+        raise ValueError(f"{name}: expected [T, H, D] or [1, T, H, D], got {tuple(t.shape)}")
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bf16, got {t.dtype}")
+    if t.stride(2) != 1:
+        raise ValueError(f"{name}: head_dim must have unit stride")
+    return t
+
+
+def _rope_rows(frequencies: torch.Tensor, tokens: int, heads: int, pairs: int):
+    """Rotation table [1, 1|T, 1|H, P, 2, 2] (or [T, P, 2, 2]) with P >= pairs -> (table with
+    contiguous [P, 2, 2] rows, token stride, head stride) in elements (0 = broadcast)."""
+    f = frequencies
+    if f.dim() == 4:
+        f = f.unsqueeze(0).unsqueeze(2)
+    if f.dim() != 6 or tuple(f.shape[-2:]) != (2, 2):
+        raise ValueError(f"frequencies must be [1, 1|T, 1|H, P, 2, 2], got {tuple(frequencies.shape)}")
+    if f.shape[0] != 1 or f.shape[1] not in (1, tokens) or f.shape[2] not in (1, heads) or f.shape[3] < pairs:
+        raise ValueError(f"frequencies {tuple(frequencies.shape)} do not cover {tokens} tokens x {heads} heads x "
+                         f"{pairs} pairs")
+    if f.dtype not in _TABLE_DTYPE_CODES:
+        raise ValueError(f"frequencies must be float32, float16 or bfloat16, got {f.dtype}")
+    if f.stride(5) != 1 or f.stride(4) != 2 or f.stride(3) != 4:
+        f = f.contiguous()
+    return f, (f.stride(1) if f.shape[1] != 1 else 0), (f.stride(2) if f.shape[2] != 1 else 0)
+
+
+def qknorm_rope_strided_(q: torch.Tensor, q_weight: torch.Tensor, frequencies: torch.Tensor, eps: float = 1e-6,
+                         rot_dim: int = 0, q_out: torch.Tensor | None = None, k: torch.Tensor | None = None,
+                         k_weight: torch.Tensor | None = None, k_out: torch.Tensor | None = None):
+    """Per-head RMSNorm + partial split-half RoPE on Q (and K when given) over strided
+    [T, H, 128] views, writing ``q_out`` / ``k_out`` (default: in place), which may be
+    HND-backed views. The reference launcher ``launch_rms_rope_kernel`` with
+    ``split_half=True`` and ``has_k`` (backends/cuda/ops/rms_rope.cu:36-229); eager math
+    backends/eager/rope.py:67-92. Returns (q_out, k_out)."""
+    _need_cuda(q, q_weight, frequencies)
+    q3 = _nhd(q, "q")
+    t, h, d = q3.shape
+    qo3 = _nhd(q if q_out is None else q_out, "q_out")
+    if qo3.shape != q3.shape:
+        raise ValueError("q_out must have q's [T, H, D] shape")
+    rd = d if rot_dim in (0, None) else int(rot_dim)
+    f, fst, fsh = _rope_rows(frequencies, t, h, rd // 2)
+    wq = q_weight.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+    if wq.numel() != d:
+        raise ValueError(f"q_weight must have {d} elements")
+    k3 = ko3 = wk = None
+    if k is not None:
+        k3 = _nhd(k, "k")
+        ko3 = _nhd(k if k_out is None else k_out, "k_out")
+        if k3.shape != q3.shape or ko3.shape != q3.shape:
+            raise ValueError("k and k_out must have q's [T, H, D] shape")
+        wk = (q_weight if k_weight is None else k_weight).to(device=q.device, dtype=torch.bfloat16).reshape(-1)
+        wk = wk.contiguous()
+        if wk.numel() != d:
+            raise ValueError(f"k_weight must have {d} elements")
+    kp = (lambda v, i: 0 if v is None else v.stride(i))  # noqa: E731
+    _lib.call("h3b200_qknorm_rope_strided", q3.data_ptr(), q3.stride(0), q3.stride(1), qo3.data_ptr(), qo3.stride(0),
+              qo3.stride(1), wq.data_ptr(), _ptr(k3), kp(k3, 0), kp(k3, 1), _ptr(ko3), kp(ko3, 0), kp(ko3, 1), _ptr(wk),
+              f.data_ptr(), _TABLE_DTYPE_CODES[f.dtype], fst, fsh, t, h, d, rd, float(eps), _stream(q))
+    q_res = q if q_out is None else q_out
+    k_res = None if k is None else (k if k_out is None else k_out)
+    return q_res, k_res
+
+
+def single_qknorm_rope_(value: torch.Tensor, *, weight: torch.Tensor, frequencies: torch.Tensor,
+                        eps: float) -> torch.Tensor:
+    """Single-side QK-norm + split-half RoPE in place on ``value`` [T, H, D]
+    (``try_apply_single_qknorm_rope_``, h3serve/native_engine/model/single_qknorm_rope.py:
+    190-206): ``rot_dim = 2 * frequencies.shape[-3]``. Raises where the reference returns
+    False."""
+    qknorm_rope_strided_(value, weight, frequencies, eps, 2 * int(frequencies.shape[-3]))
+    return value
+
+
+def single_qknorm_rope_to_hnd(value: torch.Tensor, output_nhd_view: torch.Tensor, *, weight: torch.Tensor,
+                              frequencies: torch.Tensor, eps: float) -> torch.Tensor:
+    """Single-side QK-norm + split-half RoPE from logical NHD ``value`` [T, H, D] into an
+    HND-backed NHD view (``try_apply_single_qknorm_rope_to_hnd``,
+    single_qknorm_rope.py:209-236: strides ``(D, >= T*D, 1)``, a multiple of D)."""
+    t, h, d = value.shape
+    s = tuple(int(v) for v in output_nhd_view.stride())
+    if output_nhd_view.is_contiguous() or s[0] != d or s[1] < t * d or s[1] % d or s[2] != 1:
+        raise ValueError(f"output view strides {s} are not an HND-backed [T, H, D] view")
+    qknorm_rope_strided_(value, weight, frequencies, eps, 2 * int(frequencies.shape[-3]), q_out=output_nhd_view)
+    return output_nhd_view
+
+
+_QKV_SECTIONS = {"qkv": (0, 3), "qk": (0, 2), "kv": (1, 3), "q": (0, 1), "k": (1, 2), "v": (2, 3)}
+
+
+def qkv_qknorm_rope(xq: torch.Tensor, x_scale: torch.Tensor, w_qkv: torch.Tensor, w_scale: torch.Tensor,
+                    bias: torch.Tensor | None, heads: int, q_norm_weight: torch.Tensor | None,
+                    k_norm_weight: torch.Tensor | None, frequencies: torch.Tensor | None, eps: float,
+                    sections: str = "qkv", q_out=None, k_out=None, v_out=None, workspace=None):
+    """Q/K/V projection of a token chunk with QK-norm + partial split-half RoPE, written into the
+    attention layout.
+
+    ``xq``/``x_scale``: the chunk's activation quantized once (``quantize_int8_rowwise_convrot``,
+    the reference's ``prepare_output_slices``, h3serve/native_engine/model/quantization.py:
+    340-375); ``w_qkv`` int8 [3 H 128, K] with rows Q | K | V and its per-row ``w_scale`` /
+    ``bias``. ``sections`` picks the output rows computed, as ``forward_prepared_output_slice``
+    does (:377-415): "qkv", "kv" (the K/V build), "q" (a query chunk), ... Q and K get per-head
+    RMSNorm with their norm weights and, when ``frequencies`` is given, split-half RoPE over
+    ``2 * frequencies.shape[-3]`` dims (layers.py:445-641 with
+    ``try_apply_single_qknorm_rope_to_hnd``); V is copied. Outputs default to fresh HND
+    buffers [H, m, 128]; any [m, H, 128] view (unit stride on the last dim) is accepted.
+    Returns the (q, k, v) [m, H, 128] views (None for sections not computed)."""
+    _need_cuda(xq, x_scale, w_qkv, w_scale)
+    if sections not in _QKV_SECTIONS:
+        raise ValueError(f"sections must be one of {sorted(_QKV_SECTIONS)}, got {sections!r}")
+    s0, s1 = _QKV_SECTIONS[sections]
+    if xq.dtype != torch.int8 or xq.dim() != 2 or xq.stride(1) != 1 or xq.stride(0) != xq.shape[1]:
+        raise ValueError("xq must be a contiguous int8 [m, K] tensor")
+    m, k = xq.shape
+    inner = int(heads) * 128
+    if w_qkv.dtype != torch.int8 or tuple(w_qkv.shape) != (3 * inner, k) or not w_qkv.is_contiguous():
+        raise ValueError(f"w_qkv must be a contiguous int8 [{3 * inner}, {k}] tensor")
+    xs = x_scale.to(torch.float32).reshape(-1).contiguous()
+    ws = w_scale.to(torch.float32).reshape(-1).contiguous()
+    if xs.numel() != m or ws.numel() not in (1, 3 * inner):
+        raise ValueError("x_scale must have m values and w_scale 1 or 3 * heads * 128")
+    b = None
+    if bias is not None:
+        b = bias.to(torch.bfloat16).reshape(-1).contiguous()
+        if b.numel() != 3 * inner:
+            raise ValueError(f"bias must have {3 * inner} values")
+    f, fst, fsh, fcode, rot = None, 0, 0, 0, 0
+    if frequencies is not None:
+        rot = 2 * int(frequencies.shape[-3])
+        f, fst, fsh = _rope_rows(frequencies, m, int(heads), rot // 2)
+        fcode = _TABLE_DTYPE_CODES[f.dtype]
+    outs = []
+    for sec, view, nw in ((0, q_out, q_norm_weight), (1, k_out, k_norm_weight), (2, v_out, None)):
+        if not s0 <= sec < s1:
+            outs.append((None, None))
+            continue
+        if view is None:
+            view = torch.empty(int(heads), m, 128, dtype=torch.bfloat16, device=xq.device).permute(1, 0, 2)
+        view3 = _nhd(view, ("q_out", "k_out", "v_out")[sec])
+        if tuple(view3.shape) != (m, int(heads), 128):
+            raise ValueError(f"output view must be [{m}, {heads}, 128], got {tuple(view3.shape)}")
+        w = None
+        if sec < 2:
+            if nw is None:
+                raise ValueError("q_norm_weight / k_norm_weight are required for the Q / K sections")
+            w = nw.to(device=xq.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+            if w.numel() != 128:
+                raise ValueError("norm weights must have 128 values")
+        outs.append((view3, w))
+    nbytes = int(_lib.load().h3b200_qkv_qknorm_rope_workspace_bytes(m, int(heads), 128, s0, s1))
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=xq.device)
+    (qv, qw), (kv, kw), (vv, _) = outs
+    st = (lambda v, i: 0 if v is None else v.stride(i))  # noqa: E731
+    _lib.call("h3b200_qkv_qknorm_rope", xq.data_ptr(), xs.data_ptr(), m, k, w_qkv.data_ptr(), ws.data_ptr(),
+              ws.numel(), _ptr(b), int(heads), 128, s0, s1, _ptr(qw), _ptr(kw), _ptr(f), fcode, fst, fsh, rot,
+              float(eps), _ptr(qv), st(qv, 0), st(qv, 1), _ptr(kv), st(kv, 0), st(kv, 1), _ptr(vv), st(vv, 0),
+              st(vv, 1), workspace.data_ptr(), workspace.numel(), _stream(xq))
+    return qv, kv, vv
+
+
+def _persistent_norm_rope_fits(q, k, freqs_cis) -> bool:
+    """The persistent norm-RoPE kernel takes contiguous heads (at most 32 of 128) and an fp32
+    table with one row per token; other layouts go to the strided kernel."""
+    try:
+        q3, k3 = _nhd(q, "q"), _nhd(k, "k")
+    except ValueError:
+        return False
+    return (q3.shape[1] <= 32 and q3.shape[2] == 128 and q3.stride(1) == 128 and k3.stride(1) == 128
+            and freqs_cis.dtype == torch.float32 and freqs_cis.numel() // (freqs_cis.shape[-3] * 4) == q3.shape[0])
+
+
 def rms_rope_split_half_(q, k, freqs_cis, q_scale, k_scale=None, epsilon: float = 1e-6, rot_dim: int = 0):
     """In-place per-head RMSNorm + split-half RoPE (``comfy_kitchen.rms_rope_split_half_``,
-    __init__.py:566-580; CUDA backends/cuda/ops/rms_rope.cu:36-229)."""
-    return adaln_rms_rope_(q, k, freqs_cis, q_scale, k_scale, None, None, epsilon, "head", rot_dim)
+    __init__.py:566-580; CUDA backends/cuda/ops/rms_rope.cu:36-229). Up to 32 contiguous
+    heads with an fp32 per-token table run on the persistent norm-RoPE kernel; any other
+    head count, stride or table dtype (e.g. H3's 56 heads, bf16 table) on the strided one."""
+    if _persistent_norm_rope_fits(q, k, freqs_cis):
+        return adaln_rms_rope_(q, k, freqs_cis, q_scale, k_scale, None, None, epsilon, "head", rot_dim)
+    return qknorm_rope_strided_(q, q_scale, freqs_cis, epsilon, rot_dim, k=k,
+                                k_weight=q_scale if k_scale is None else k_scale)
 
 
 def rms_rope_split_half(q, k, freqs_cis, q_scale, k_scale=None, epsilon: float = 1e-6, rot_dim: int = 0):
     """Out-of-place ``comfy_kitchen.rms_rope_split_half`` (__init__.py:549-563)."""
-    return adaln_rms_rope(q, k, freqs_cis, q_scale, k_scale, None, None, epsilon, "head", rot_dim)
+    if _persistent_norm_rope_fits(q, k, freqs_cis):
+        return adaln_rms_rope(q, k, freqs_cis, q_scale, k_scale, None, None, epsilon, "head", rot_dim)
+    return qknorm_rope_strided_(q, q_scale, freqs_cis, epsilon, rot_dim, q_out=torch.empty_like(q), k=k,
+                                k_weight=q_scale if k_scale is None else k_scale, k_out=torch.empty_like(k))
 
 
 # ---------------------------------------------------------------------------

@@ -10,7 +10,10 @@ given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
 (the H3 SwiGLU MLP at d 5,376 / ffn 14,336, ConvRot fc1 and fc2, 8,192-token chunks),
 ``mlp_swiglu_w4`` (the same MLP on W4A8 weights in the H3 release format: group 16,
 fp8-e4m3 scales, codebook; both weights decoded per call), ``decode_w4`` (that
-format's int4 -> int8 decode of the fc1 weight, 28,672 x 5,376),
+format's int4 -> int8 decode of the fc1 weight, 28,672 x 5,376), ``qknorm_h3``
+(single-side QK-norm + partial RoPE of H3 K, 56 heads, rot 96, bf16 table, into an
+HND buffer), ``qkv_h3`` (the H3 Q/K/V projection of M tokens, hidden 5,376, with
+QK-norm + RoPE into HND buffers, from a ConvRot-quantized activation),
 ``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
 Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
 norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
@@ -114,6 +117,27 @@ def run(case: str, m: int, iters: int, report: bool = False):
             res = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
             out = torch.empty_like(res)
             ms = _timed(lambda: h3b200.fused_gated_mlp_swiglu_w4a8(res, x, w4, gate, out=out), iters, report)
+    elif case in ("qknorm_h3", "qkv_h3"):
+        g = torch.Generator(device=dev).manual_seed(10)
+        heads, d = 56, 5376
+        freqs = torch.randn(1, m, 1, 48, 2, 2, generator=g, device=dev).to(torch.bfloat16)
+        kn = (1 + 0.02 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+        if case == "qknorm_h3":
+            k = torch.randn(m, heads, 128, generator=g, device=dev).to(torch.bfloat16)
+            k_hnd = torch.empty(heads, m, 128, dtype=torch.bfloat16, device=dev).permute(1, 0, 2)
+            ms = _timed(lambda: ops.single_qknorm_rope_to_hnd(k, k_hnd, weight=kn, frequencies=freqs, eps=1e-5),
+                        iters, report)
+        else:
+            w = (torch.randn(3 * heads * 128, d, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            wq_, ws = h3b200.quantize_int8_convrot_weight(w)
+            del w
+            hidden = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+            xq, xs = ops.quantize_int8_rowwise_convrot(hidden, 256)
+            outs = [torch.empty(heads, m, 128, dtype=torch.bfloat16, device=dev).permute(1, 0, 2) for _ in range(3)]
+            work = torch.empty(int(h3b200.library().h3b200_qkv_qknorm_rope_workspace_bytes(m, heads, 128, 0, 3)),
+                               dtype=torch.uint8, device=dev)
+            ms = _timed(lambda: ops.qkv_qknorm_rope(xq, xs, wq_, ws, None, heads, kn, kn, freqs, 1e-5, "qkv",
+                                                    *outs, workspace=work), iters, report)
     elif case == "mlp_w4a8":
         g = torch.Generator(device=dev).manual_seed(3)
         w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
@@ -166,7 +190,8 @@ def run(case: str, m: int, iters: int, report: bool = False):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", nargs="+", choices=["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp",
-                                                "mlp_w4a8", "mlp_swiglu", "mlp_swiglu_w4", "decode_w4", "convrot",
+                                                "mlp_w4a8", "mlp_swiglu", "mlp_swiglu_w4", "decode_w4", "qknorm_h3",
+                                                "qkv_h3", "convrot",
                                                 "convrot_x", "norm_rope"])
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=3)
