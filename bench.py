@@ -404,7 +404,47 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(3):
         k_swiglu_w4()
     sw4_ms = timed(k_swiglu_w4, 10, stream)
-    del work5, x5, r5, o5, wsw4
+    del work5, r5, o5, wsw4
+
+    # ---- H3 attention build: Q/K/V projection (hidden 5,376 -> 3 x 56 heads x 128, ConvRot INT8)
+    #      from the activation quantized once, per-head QK-norm + RoPE over 96 dims (bf16 table)
+    #      into HND attention buffers, 8,192-token chunks as the reference's projection chunks ----
+    H3_HEADS = 56
+    g6 = torch.Generator(device=dev).manual_seed(10)
+    wqkv = (torch.randn(3 * H3_HEADS * 128, H3_D, generator=g6, device=dev) * 0.02).to(torch.bfloat16)
+    wqkv_q, wqkv_s = h3b200.quantize_int8_convrot_weight(wqkv)
+    del wqkv
+    bqkv = (torch.randn(3 * H3_HEADS * 128, generator=g6, device=dev) * 0.1).to(torch.bfloat16)
+    qn6 = (1 + 0.02 * torch.randn(128, generator=g6, device=dev)).to(torch.bfloat16)
+    kn6 = (1 + 0.02 * torch.randn(128, generator=g6, device=dev)).to(torch.bfloat16)
+    tab6 = rope_grid_table((21, 39, 40), dims=(32, 32, 32), device=dev).to(torch.bfloat16)
+    tab6 = tab6.reshape(1, M_TOKENS, 1, 48, 2, 2)
+    hnd6 = [torch.empty(H3_HEADS, M_TOKENS, 128, dtype=torch.bfloat16, device=dev) for _ in range(3)]
+    chunk6 = 8192
+    work6 = torch.empty(int(h3b200.library().h3b200_qkv_qknorm_rope_workspace_bytes(chunk6, H3_HEADS, 128, 0, 3)),
+                        dtype=torch.uint8, device=dev)
+
+    def k_qkv():
+        xq6, xs6 = ops.quantize_int8_rowwise_convrot(x5, 256)
+        for a in range(0, M_TOKENS, chunk6):
+            b = min(M_TOKENS, a + chunk6)
+            ops.qkv_qknorm_rope(xq6[a:b], xs6[a:b], wqkv_q, wqkv_s, bqkv, H3_HEADS, qn6, kn6, tab6[:, a:b], 1e-5,
+                                "qkv", *(h[:, a:b].permute(1, 0, 2) for h in hnd6), workspace=work6)
+
+    for _ in range(3):
+        k_qkv()
+    qkv_ms = timed(k_qkv, 10, stream)
+    qkv_ops = 2 * H3_D * 3 * H3_HEADS * 128   # int8 ops per token
+    k6 = torch.randn(M_TOKENS, H3_HEADS, 128, generator=g6, device=dev).to(torch.bfloat16)
+
+    def k_qk1():
+        ops.single_qknorm_rope_to_hnd(k6, hnd6[1].permute(1, 0, 2), weight=kn6, frequencies=tab6, eps=1e-5)
+
+    for _ in range(3):
+        k_qk1()
+    qk1_ms = timed(k_qk1, 20, stream)
+    qk1_bytes = M_TOKENS * H3_HEADS * 128 * 2 * 2
+    del work6, hnd6, k6, wqkv_q, x5
 
     # ---- config 4: long-video DiT-block slice (norm-RoPE then W8A8 MLP) on this rank's token shard ----
     from h3b200 import parallel as PAR
@@ -520,6 +560,15 @@ def run_ours(args, rank, world, local_rank):
                                        "int8_tops": M_TOKENS * sw_ops / (sw4_ms * 1e-3) / 1e12,
                                        "weights": "H3 release W4A8: int4 group 16, fp8-e4m3 s_rel, 16-level "
                                                   "codebook, ConvRot-256; both weights decoded per call"},
+                "h3_qkv_qknorm_rope_hnd": {"heads": H3_HEADS, "d": H3_D, "tokens": M_TOKENS, "ms": qkv_ms,
+                                           "tokens_per_s": M_TOKENS / (qkv_ms * 1e-3),
+                                           "int8_tops": M_TOKENS * qkv_ops / (qkv_ms * 1e-3) / 1e12,
+                                           "path": "ConvRot quantize once; per 8,192-token chunk INT8 GEMM [Q|K|V], "
+                                                   "QK-norm + RoPE(96) of Q and K into HND, V into HND"},
+                "h3_single_qknorm_rope_hnd": {"heads": H3_HEADS, "tokens": M_TOKENS, "ms": qk1_ms,
+                                              "achieved": qk1_bytes / (qk1_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                                              "unit": "GB/s", "frac": qk1_bytes / (qk1_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                              "bytes_per_token": H3_HEADS * 128 * 2 * 2},
                 "w4a8_mlp_cfg2": {"ms": w4_ms, "tokens_per_s": M_TOKENS / (w4_ms * 1e-3),
                                   "int8_tops": M_TOKENS * OPS_PER_TOKEN / (w4_ms * 1e-3) / 1e12,
                                   "weights": "asymmetric int4, group 128, ConvRot-256, decoded per call"},

@@ -250,3 +250,29 @@ def test_qkv_norm_only_and_caller_views():
     np.testing.assert_array_equal(t2u(v_hnd[:, 20:20 + m].permute(1, 0, 2)),
                                   t2u(proj[:, 2 * inner:]).reshape(m, heads, 128))
     assert bool((k_hnd[:, :20] == 3.0).all()) and bool((v_hnd[:, 20 + m:] == 3.0).all())
+
+
+@pytest.mark.parametrize("rot,per_head_table,nhd_out", [(96, False, True), (128, False, False), (64, False, True),
+                                                         (16, False, False), (96, True, False)])
+def test_qkv_fused_and_three_kernel_paths_match_op_chain(rot, per_head_table, nhd_out):
+    """The fused GEMM epilogue (per-token table, rot a multiple of 32) and the three-kernel path
+    (rot 16, or a table row per head) give the op chain's bits, into HND or NHD outputs."""
+    m, heads, k = 333, 6, 768
+    inner = heads * 128
+    xq, xs, wq_, ws, bias, qn, kn, _ = _qkv_case(m, heads, k, rot + per_head_table)
+    gen = torch.Generator(device="cuda").manual_seed(rot)
+    freqs = torch.randn(1, m, heads if per_head_table else 1, rot // 2, 2, 2, generator=gen, device="cuda")
+    if nhd_out:
+        bufs = [torch.empty(m, heads, 128, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    else:
+        bufs = [torch.empty(heads, m, 128, dtype=torch.bfloat16, device="cuda").permute(1, 0, 2) for _ in range(3)]
+    q, kk, v = h3b200.qkv_qknorm_rope(xq, xs, wq_, ws, bias, heads, qn, kn, freqs, 1e-5, "qkv", *bufs)
+    assert h3b200.device_status(0) == 0
+    proj = h3b200.int8_linear_prequantized(xq, xs, wq_, ws, bias)
+    pq = proj[:, :inner].reshape(m, heads, 128)
+    pk = proj[:, inner:2 * inner].reshape(m, heads, 128)
+    rq, rk = h3b200.qknorm_rope_strided_(pq, qn, freqs, 1e-5, rot, q_out=torch.empty_like(pq), k=pk, k_weight=kn,
+                                         k_out=torch.empty_like(pk))
+    np.testing.assert_array_equal(t2u(q), t2u(rq))
+    np.testing.assert_array_equal(t2u(kk), t2u(rk))
+    np.testing.assert_array_equal(t2u(v), t2u(proj[:, 2 * inner:].reshape(m, heads, 128)))

@@ -281,7 +281,10 @@ int h3b200_qknorm_rope_strided(const void* q, int64_t q_st, int64_t q_sh, void* 
 int64_t h3b200_qkv_qknorm_rope_workspace_bytes(int64_t m, int64_t heads, int64_t head_dim, int sec_begin,
                                               int sec_end) {
   if (m < 0 || heads <= 0 || head_dim <= 0 || sec_begin < 0 || sec_end > 3 || sec_begin >= sec_end) return 0;
-  return round_up(m * (sec_end - sec_begin) * heads * head_dim * 2, 256) + 256;
+  // the larger of the projection buffer (three-kernel path) and the transposed
+  // rotation table (fused path: at most head_dim / 2 pairs x 16 bytes per token)
+  return std::max(round_up(m * (sec_end - sec_begin) * heads * head_dim * 2, 256),
+                  round_up(m * (head_dim / 2) * 16, 256)) + 256;
 }
 
 int h3b200_qkv_qknorm_rope(const int8_t* xq, const float* x_scale, int64_t m, int64_t k, const int8_t* w_qkv,
@@ -306,6 +309,38 @@ int h3b200_qkv_qknorm_rope(const int8_t* xq, const float* x_scale, int64_t m, in
   if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "%s: workspace too small (need %lld bytes)", who, (long long)need);
   cudaStream_t st = S(stream);
   const int64_t n = (sec_end - sec_begin) * inner;
+  // Fused path: one GEMM whose epilogue normalises, rotates and stores every head
+  // straight into the caller's views (per-token table, rotation a multiple of 32 dims).
+  const int64_t rot = freqs ? (rot_dim == 0 ? head_dim : rot_dim) : 0;
+  void* const outs[3] = {q_out, k_out, v_out};
+  const int64_t sts[3] = {q_st, k_st, v_st}, shs[3] = {q_sh, k_sh, v_sh};
+  bool fused = (freqs == nullptr || (f_sh == 0 && rot % 32 == 0 && rot >= 32 && rot <= 128)) && !(k % 16);
+  for (int s = sec_begin; s < sec_end; ++s)
+    fused = fused && !(reinterpret_cast<uintptr_t>(outs[s]) & 15) && sts[s] > 0 && shs[s] > 0 && sts[s] % 8 == 0 &&
+            shs[s] % 8 == 0;
+  if (fused) {
+    float4* rope_t = nullptr;
+    if (freqs) {
+      if (freqs_dtype != H3B200_DTYPE_F32 && freqs_dtype != H3B200_DTYPE_BF16 && freqs_dtype != H3B200_DTYPE_F16)
+        return fail(H3B200_ERR_INVALID, "%s: freqs dtype code must be 0, 1 or 2, got %d", who, freqs_dtype);
+      rope_t = static_cast<float4*>(workspace);
+      const int tab = freqs_dtype == H3B200_DTYPE_F32 ? 0 : (freqs_dtype == H3B200_DTYPE_BF16 ? 1 : 2);
+      cudaError_t e = h3::launch_rope_table_transpose(freqs, tab, f_st, m, (int)(rot / 2), rope_t, st);
+      if (e != cudaSuccess) return from_cuda(e, "qkv_qknorm_rope: rotation table");
+    }
+    h3::GemmArgs g;
+    g.a = xq; g.w = w_qkv + sec_begin * inner * k; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+    g.epilogue = h3::kEpiQKV; g.a_scale = x_scale;
+    g.w_scale = w_scale_numel == 1 ? w_scale : w_scale + sec_begin * inner;
+    g.w_scale_per_channel = w_scale_numel == 1 ? 0 : 1;
+    g.bias = bias ? static_cast<const __nv_bfloat16*>(bias) + sec_begin * inner : nullptr;
+    g.qkv_heads = heads; g.qkv_sec0 = sec_begin; g.qkv_rot = (int)rot; g.rope_t = rope_t; g.qk_eps = eps;
+    g.qk_w[0] = q_norm_weight; g.qk_w[1] = k_norm_weight;
+    for (int s = 0; s < 3; ++s) {
+      g.qkv_out[s] = outs[s]; g.qkv_st[s] = sts[s]; g.qkv_sh[s] = shs[s];
+    }
+    return from_cuda(h3::launch_gemm_i8(g, st), "qkv_qknorm_rope: fused projection");
+  }
   auto* proj = static_cast<__nv_bfloat16*>(workspace);
   // the requested Q/K/V rows of the projection: dequant (+ bias) into [m, n] bf16
   h3::GemmArgs g;

@@ -34,6 +34,7 @@
 // No cluster multicast is used anywhere (the same binary runs in multi-GPU jobs).
 #include "common.cuh"
 #include "kernels.h"
+#include "quant_math.cuh"
 
 namespace h3 {
 
@@ -85,6 +86,12 @@ struct KParams {
   int corr_kb;  // 64-group k-blocks of the correction operands (kEpi*Corr)
   const int32_t* row_map;  // kEpiGatedResidual: gate row of each output row (nullptr: gate is one row)
   int64_t ldg;             // row stride of the gate rows (elements)
+  // kEpiQKV (see GemmArgs): output maps tmO / tmR / tmS are sections Q / K / V;
+  // bit s of qkv_hmaj: section s's map is (dim, head, token) instead of (dim, token, head)
+  int qkv_inner, qkv_sec0, qkv_rot, qkv_hmaj;
+  const __nv_bfloat16* qk_w[2];
+  const float4* rope_t;
+  float qk_eps;
 };
 
 template <int EPI>
@@ -258,6 +265,43 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
       ob[2 * q] = hb[0] | (hb[1] << 16);
       ob[2 * q + 1] = hb[2] | (hb[3] << 16);
     }
+  }
+}
+
+// ---- kEpiQKV helpers: one thread holds one head (128 values) of one token ----
+// |bf16| of the low / high half of w as a double, built from its bits (exact for
+// normal values; zero and subnormals become a value below 2^-126 whose square
+// cannot change the fp32 mean; non-finite rows are re-summed exactly)
+__device__ __forceinline__ double qkv_abs_lo(uint32_t w) {
+  return __hiloint2double((int)(((w & 0x7FFFu) << 13) + 0x38000000u), 0);
+}
+__device__ __forceinline__ double qkv_abs_hi(uint32_t w) {
+  return __hiloint2double((int)(((w >> 3) & 0x0FFFE000u) + 0x38000000u), 0);
+}
+
+__device__ __forceinline__ uint64_t qkv_f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+// split-half RoPE over dims [0, 2R) of the head held as bf16 pairs h[j] = (2j, 2j + 1):
+// y_i = t00 h_i + t01 h_{i+R}, y_{i+R} = t10 h_i + t11 h_{i+R} (fp32, two rounded
+// products and one add, then bf16). rt: rows of pair p at rt[p * m], this token's
+// column `row` (coalesced across the warp's 32 consecutive tokens).
+template <int R>
+__device__ __forceinline__ void qkv_rope(uint32_t (&h)[64], const float4* __restrict__ rt, int64_t m, int row) {
+  const bool live = row < m;
+#pragma unroll
+  for (int i = 0; i < R; i += 2) {
+    const float4 ta = live ? __ldg(rt + (int64_t)i * m + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 tb = live ? __ldg(rt + (int64_t)(i + 1) * m + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t x0w = h[i / 2], x1w = h[(i + R) / 2];
+    const float a0 = bf16_lo(x0w), a1 = bf16_hi(x0w), b0 = bf16_lo(x1w), b1 = bf16_hi(x1w);
+    h[i / 2] = pack_bf16(__fadd_rn(__fmul_rn(ta.x, a0), __fmul_rn(ta.y, b0)),
+                         __fadd_rn(__fmul_rn(tb.x, a1), __fmul_rn(tb.y, b1)));
+    h[(i + R) / 2] = pack_bf16(__fadd_rn(__fmul_rn(ta.z, a0), __fmul_rn(ta.w, b0)),
+                               __fadd_rn(__fmul_rn(tb.z, a1), __fmul_rn(tb.w, b1)));
   }
 }
 
@@ -515,10 +559,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const bool cok = col < p.n;
           ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
           float a = 0.0f;
-          if (EPI == kEpiBF16 && p.bias != nullptr && cok) a = __bfloat162float(p.bias[col]);
+          if ((EPI == kEpiBF16 || EPI == kEpiQKV) && p.bias != nullptr && cok) a = __bfloat162float(p.bias[col]);
           if (kInBox && cok && (EPI != kEpiGatedResidual || p.row_map == nullptr)) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
           if (EPI == kEpiGatedResidual && p.bias != nullptr) bias_s[c] = cok ? __bfloat162float(p.bias[col]) : 0.0f;
+          if constexpr (EPI == kEpiQKV) {  // this head's RMSNorm weight (Q and K sections)
+            const int sec = p.qkv_sec0 + col_base / p.qkv_inner;
+            bias_s[c] = sec < 2 ? __bfloat162float(p.qk_w[sec][c]) : 0.0f;
+          }
         }
         __syncwarp();
       }
@@ -529,6 +577,98 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
       const int box_row0 = row0 + quarter * 32;
+      if constexpr (EPI == kEpiQKV) {
+        // The warp's 128 columns are one head of one section; each thread holds its
+        // token's head in registers: dequant (+ bias), then for Q / K the RMSNorm over
+        // the 128 values (sum of squares in double, in-thread) and the RoPE pairs,
+        // then four 32x32 boxes stored by TMA into the section's [m, heads, 128] view.
+        const bool live_cols = col_base < p.n;  // warp-uniform
+        const int sec = p.qkv_sec0 + col_base / p.qkv_inner;
+        const int head = (col_base % p.qkv_inner) >> 7;
+        uint32_t h[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + 32 * c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            uint32_t b0 = dequant_bits(r[2 * j], xs, ws_s[32 * c + 2 * j]);
+            uint32_t b1 = dequant_bits(r[2 * j + 1], xs, ws_s[32 * c + 2 * j + 1]);
+            if (p.bias != nullptr) {
+              b0 = bf16_bits(__fadd_rn(__uint_as_float(b0 << 16), aux_s[32 * c + 2 * j]));
+              b1 = bf16_bits(__fadd_rn(__uint_as_float(b1 << 16), aux_s[32 * c + 2 * j + 1]));
+            }
+            h[16 * c + j] = b0 | (b1 << 16);
+          }
+        }
+        // the accumulator is in registers: release it to the MMA issuer
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 2)
+            mbar_arrive_cluster(mapa_shared(&tempty_bar[acc], 0));
+          else
+            mbar_arrive(&tempty_bar[acc]);
+        }
+        if (!live_cols || box_row0 >= p.m) continue;  // warp-uniform: nothing of this head to store
+        if (sec < 2) {
+          double sq[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const double a = qkv_abs_lo(h[j]), b = qkv_abs_hi(h[j]);
+            sq[j & 3] = fma(a, a, sq[j & 3]);
+            sq[j & 3] = fma(b, b, sq[j & 3]);
+          }
+          float ms = (float)(((sq[0] + sq[1]) + (sq[2] + sq[3])) * 0.0078125);
+          if (!isfinite(ms)) {  // inf / NaN / huge: exact conversions
+            double se = 0.0;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const double a = (double)bf16_lo(h[j]), b = (double)bf16_hi(h[j]);
+              se = fma(a, a, se);
+              se = fma(b, b, se);
+            }
+            ms = (float)(se * 0.0078125);
+          }
+          const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.qk_eps)));
+          const uint64_t rs2 = f2_dup(rs);
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            uint32_t lo, hi;
+            f2_bits(f2_mul(f2_mul(bf16x2_to_f2(h[j]), rs2), qkv_f2(bias_s[2 * j], bias_s[2 * j + 1])), lo, hi);
+            h[j] = bf16x2_from_bits(lo, hi);
+          }
+          switch (p.qkv_rot) {
+            case 32: qkv_rope<16>(h, p.rope_t, p.m, row); break;
+            case 64: qkv_rope<32>(h, p.rope_t, p.m, row); break;
+            case 96: qkv_rope<48>(h, p.rope_t, p.m, row); break;
+            case 128: qkv_rope<64>(h, p.rope_t, p.m, row); break;
+            default: break;  // RMSNorm only
+          }
+        }
+        const CUtensorMap* omap = sec == 0 ? &tmO : (sec == 1 ? &tmR : &tmS);
+        const bool hmaj = (p.qkv_hmaj >> sec) & 1;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(box_row + ((q ^ box_sw) << 4)) =
+                make_uint4(h[16 * c + 4 * q], h[16 * c + 4 * q + 1], h[16 * c + 4 * q + 2], h[16 * c + 4 * q + 3]);
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            if (hmaj)
+              tma_store_3d(omap, box, 32 * c, head, box_row0);   // tokens >= m are clipped
+            else
+              tma_store_3d(omap, box, 32 * c, box_row0, head);
+            bulk_commit_group();
+          }
+        }
+        continue;
+      }
       if constexpr (kCorr) {
         // pass 1: the dequantized values replace the int32 accumulators
 #pragma unroll 1
@@ -742,6 +882,7 @@ cudaError_t launch_cg(int epilogue, const TensorMaps& t, const KParams& kp, int 
     case kEpiBF16Corr: return launch_epi<kEpiBF16Corr, CG>(t, kp, grid, stream);
     case kEpiBF16CorrGelu: return launch_epi<kEpiBF16CorrGelu, CG>(t, kp, grid, stream);
     case kEpiGatedResidualCorr: return launch_epi<kEpiGatedResidualCorr, CG>(t, kp, grid, stream);
+    case kEpiQKV: return launch_epi<kEpiQKV, CG>(t, kp, grid, stream);
     default: return cudaErrorNotSupported;
   }
 }
@@ -778,6 +919,20 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D tiled map over bf16 [d2][d1][d0] with byte strides s1, s2 (box b0 x b1 x b2)
+bool encode_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                         uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+  cuuint64_t strides[2] = {(cuuint64_t)s1, (cuuint64_t)s2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int num_sms(int device) {
   static int cache[64] = {0};
   if (device < 0 || device >= 64) return 148;
@@ -794,9 +949,24 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   if (a.k <= 0 || a.k % 16 != 0 || a.n % 8 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.m > (1ll << 30) ||
       a.n > (1ll << 30) || a.k > (1ll << 30))
     return cudaErrorNotSupported;
+  const bool qkv = a.epilogue == kEpiQKV;
   if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15) ||
-      (reinterpret_cast<uintptr_t>(a.out) & 15) || a.ldo % 8 != 0)
+      (!qkv && ((reinterpret_cast<uintptr_t>(a.out) & 15) || a.ldo % 8 != 0)))
     return cudaErrorNotSupported;
+  int qkv_hmaj = 0;
+  if (qkv) {
+    const int64_t inner = a.qkv_heads * 128;
+    const int nsec = inner > 0 ? (int)(a.n / inner) : 0;
+    if (a.qkv_heads <= 0 || a.n % inner != 0 || a.qkv_sec0 < 0 || a.qkv_sec0 + nsec > 3 || nsec < 1 ||
+        inner > (1ll << 30) || (a.rope_t == nullptr ? a.qkv_rot != 0 : (a.qkv_rot % 32 || a.qkv_rot < 32 || a.qkv_rot > 128)))
+      return cudaErrorNotSupported;
+    for (int s = a.qkv_sec0; s < a.qkv_sec0 + nsec; ++s) {
+      if (a.qkv_out[s] == nullptr || (reinterpret_cast<uintptr_t>(a.qkv_out[s]) & 15) || a.qkv_st[s] % 8 ||
+          a.qkv_sh[s] % 8 || a.qkv_st[s] <= 0 || a.qkv_sh[s] <= 0 || (s < 2 && a.qk_w[s] == nullptr))
+        return cudaErrorNotSupported;
+      if (a.qkv_sh[s] < a.qkv_st[s]) qkv_hmaj |= 1 << s;  // heads inside a token row: (dim, head, token) order
+    }
+  }
   const bool gated = a.epilogue == kEpiGatedResidual || a.epilogue == kEpiGatedResidualCorr;
   if (gated && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0)) return cudaErrorNotSupported;
   if (a.row_map != nullptr && (a.epilogue != kEpiGatedResidual || a.ldg < a.n || a.ldg % 8 != 0 ||
@@ -817,13 +987,31 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   TensorMaps t;
   if (!make_tmap_i8(&t.a, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&t.b, a.w, a.n, a.k, a.ldw, BN / cg))
     return cudaErrorInvalidValue;
-  if (a.epilogue == kEpiI32) {
+  if (qkv) {
+    // one [m, heads, 128] map per present section, boxes of 32 dims x 32 tokens
+    CUtensorMap* maps[3] = {&t.out, &t.res, &t.sx};
+    const int nsec = (int)(a.n / (a.qkv_heads * 128));
+    for (int s = 0; s < 3; ++s) {
+      const int src_s = (s >= a.qkv_sec0 && s < a.qkv_sec0 + nsec) ? s : a.qkv_sec0;  // absent: any valid map
+      const bool hm = (qkv_hmaj >> src_s) & 1;
+      const uint64_t st = (uint64_t)a.qkv_st[src_s] * 2, sh = (uint64_t)a.qkv_sh[src_s] * 2;
+      // (dim, token, head) with boxes 32 x 32 x 1, or (dim, head, token) with 32 x 1 x 32:
+      // either way a box is 32 token rows of 64 bytes in shared memory
+      if (!(hm ? encode_tmap_3d_bf16(maps[s], a.qkv_out[src_s], 128, (uint64_t)a.qkv_heads, (uint64_t)a.m, sh, st,
+                                     32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+               : encode_tmap_3d_bf16(maps[s], a.qkv_out[src_s], 128, (uint64_t)a.m, (uint64_t)a.qkv_heads, st, sh,
+                                     32, 32, 1, CU_TENSOR_MAP_SWIZZLE_64B)))
+        return cudaErrorInvalidValue;
+    }
+  } else if (a.epilogue == kEpiI32) {
     t.out = t.b;  // unused: int32 results are stored directly
   } else if (!encode_tmap_2d(&t.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
                              (uint64_t)a.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return cudaErrorInvalidValue;
   }
-  if (gated) {
+  if (qkv) {
+    // t.res holds the K map
+  } else if (gated) {
     if (!encode_tmap_2d(&t.res, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.residual, (uint64_t)a.n, (uint64_t)a.m,
                         (uint64_t)a.ldr * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return cudaErrorInvalidValue;
@@ -837,9 +1025,11 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
         !encode_tmap_2d(&t.corr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.corr_t, (uint64_t)a.kp, (uint64_t)a.n,
                         (uint64_t)a.kp * 2, 64, BN / cg, CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
-  } else {
+  } else if (!qkv) {
     t.sx = t.a;  // unused
     t.corr = t.a;
+  } else {
+    t.corr = t.a;  // unused; t.sx holds the V map
   }
   KParams kp;
   kp.m = (int)a.m;
@@ -864,6 +1054,14 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.corr_kb = corr ? (int)(a.kp / 64) : 0;
   kp.row_map = a.epilogue == kEpiGatedResidual ? a.row_map : nullptr;
   kp.ldg = a.ldg;
+  kp.qkv_inner = qkv ? (int)(a.qkv_heads * 128) : 1;
+  kp.qkv_sec0 = a.qkv_sec0;
+  kp.qkv_rot = a.rope_t != nullptr ? a.qkv_rot : 0;
+  kp.qkv_hmaj = qkv_hmaj;
+  kp.qk_w[0] = static_cast<const __nv_bfloat16*>(a.qk_w[0]);
+  kp.qk_w[1] = static_cast<const __nv_bfloat16*>(a.qk_w[1]);
+  kp.rope_t = a.rope_t;
+  kp.qk_eps = a.qk_eps;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

@@ -18,6 +18,9 @@ enum GemmEpilogue : int {
   kEpiBF16Corr = 4,          // out = y
   kEpiBF16CorrGelu = 5,      // out = tanh-GELU(y) (exact bf16)
   kEpiGatedResidualCorr = 6, // out = bf16(residual + y * gate)
+  // Q/K/V projection into attention layouts: y = bf16(bf16(acc * (xs * ws)) + bias);
+  // Q and K heads get per-head RMSNorm and partial split-half RoPE, V is stored as is.
+  kEpiQKV = 7,
 };
 
 struct GemmArgs {
@@ -43,7 +46,26 @@ struct GemmArgs {
   const void* sx = nullptr;
   const void* corr_t = nullptr;
   int64_t kp = 0;
+  // kEpiQKV: GEMM column c is dim c % 128 of head (c % inner) / 128 of section
+  // sec0 + c / inner (0 Q, 1 K, 2 V), inner = heads * 128. Section s writes
+  // [m, heads, 128] bf16 at qkv_out[s] with element strides token qkv_st[s] and
+  // head qkv_sh[s] (16-byte multiples). qk_w: bf16 [128] RMSNorm weights of Q and
+  // K; rope_t: the rotation rows transposed to [qkv_rot / 2][m] x {t00, t01, t10, t11}
+  // fp32 (nullptr: RMSNorm only); qkv_rot a multiple of 32, at most 128.
+  int64_t qkv_heads = 0;
+  int qkv_sec0 = 0;
+  int qkv_rot = 0;
+  void* qkv_out[3] = {nullptr, nullptr, nullptr};
+  int64_t qkv_st[3] = {0, 0, 0}, qkv_sh[3] = {0, 0, 0};
+  const void* qk_w[2] = {nullptr, nullptr};
+  const float4* rope_t = nullptr;
+  float qk_eps = 1e-6f;
 };
+
+// rope_t[p, t] = {t00, t01, t10, t11} of pair p < pairs of token t, fp32, from
+// table rows [pairs, 2, 2] at element stride fs_t (table dtype 0 fp32, 1 bf16, 2 fp16)
+cudaError_t launch_rope_table_transpose(const void* freqs, int table_dtype, int64_t fs_t, int64_t m, int pairs,
+                                        float4* rope_t, cudaStream_t stream);
 
 cudaError_t launch_dequant_gated_residual(const int32_t* acc, const float* xs, const float* ws, const void* gate,
                                           const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,

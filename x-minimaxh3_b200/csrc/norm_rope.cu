@@ -429,6 +429,10 @@ cudaError_t launch_vpl(const CUtensorMap& tm, const NRParams& p, bool row, bool 
 // each table row once for Q and K.
 // ---------------------------------------------------------------------------
 constexpr int kQKWarpsPerBlock = 8;
+// per-warp cp.async ring depth (stages - 1 warp iterations in flight): 32 KB of
+// static shared memory per block either way
+template <int LPH>
+constexpr int qk_stages() { return LPH == 16 ? 8 : 4; }
 
 struct QKParams {
   const __nv_bfloat16* x[2];
@@ -439,15 +443,15 @@ struct QKParams {
   int64_t fs_t, fs_h;  // table element strides: token, head (0: shared by the heads)
   int64_t m;
   int heads;
-  int half_v;  // rot_dim / 16: vectors in each rotation half
+  int half_v;  // rot_dim / 16: 16-byte vectors in each rotation half (0: no rotation)
   int nt;      // tensors: 1 or 2
   float eps;
 };
 
-// fp32 coefficients (A for the lane's own value, B for the partner's) of the
-// lane's 8 pairs starting at pair0 of a table row; TAB: 0 fp32, 1 bf16, 2 fp16.
+// fp32 coefficients (A for the lane's own value, B for the partner's) of 8 pairs
+// starting at pair0 of a table row; TAB: 0 fp32, 1 bf16, 2 fp16.
 template <int TAB>
-__device__ __forceinline__ void rope_coeffs(const void* row, int pair0, int role, uint64_t (&A)[4], uint64_t (&B)[4]) {
+__device__ __forceinline__ void rope_coeffs(const void* row, int pair0, int role, uint64_t* A, uint64_t* B) {
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     float c[2][4];
@@ -475,74 +479,128 @@ __device__ __forceinline__ void rope_coeffs(const void* row, int pair0, int role
   }
 }
 
-template <int TAB>
+// LPH lanes per head: 16 (one 16-byte vector per lane, two heads per warp
+// iteration) or 8 (two vectors per lane, four heads per iteration; needs the
+// rotation halves to be whole lanes, rot_dim % 32 == 0). Lane (l mod LPH)
+// owns dims 8 VPL (l mod LPH) .. + 8 VPL - 1; its RoPE partner holds the dims
+// rot_dim / 2 away, one shuffle across the head's lanes.
+template <int TAB, int LPH>
 __global__ void __launch_bounds__(32 * kQKWarpsPerBlock) qk_rms_rope_kernel(const QKParams p) {
+  constexpr int VPL = 16 / LPH;   // vectors per lane per head
+  constexpr int HPI = 32 / LPH;   // heads per warp iteration
+  constexpr int S = qk_stages<LPH>();
   const int lane = threadIdx.x & 31;
   const int64_t tok = (int64_t)blockIdx.x * kQKWarpsPerBlock + (threadIdx.x >> 5);
   if (tok >= p.m) return;  // warp-uniform
-  const int hv = lane & 15;
-  const int hsel = lane >> 4;
-  const int half_v = p.half_v;
-  const int role = hv < half_v ? 0 : (hv < 2 * half_v ? 1 : 2);  // first half, second half, pass-through
-  const int partner = (lane & 16) | (role == 0 ? hv + half_v : (role == 1 ? hv - half_v : hv));
-  const int pair0 = 8 * (role == 0 ? hv : (role == 1 ? hv - half_v : 0));
+  const int hv = lane % LPH;
+  const int hsel = lane / LPH;
+  const int half_l = p.half_v / VPL;  // lanes per rotation half
+  const int role = hv < half_l ? 0 : (hv < 2 * half_l ? 1 : 2);  // first half, second half, pass-through
+  const int partner = (lane - hv) + (role == 0 ? hv + half_l : (role == 1 ? hv - half_l : hv));
+  const int pair0 = 8 * VPL * (role == 0 ? hv : (role == 1 ? hv - half_l : 0));
   constexpr int kTabElemBytes = TAB == 0 ? 4 : 2;
   const uint8_t* trow = static_cast<const uint8_t*>(p.freqs) + tok * p.fs_t * kTabElemBytes;
 
-  uint64_t A[4], B[4];
+  uint64_t A[4 * VPL], B[4 * VPL];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) A[e] = B[e] = 0;
-  if (role != 2 && p.fs_h == 0) rope_coeffs<TAB>(trow, pair0, role, A, B);
-  uint64_t wp[2][4];  // the lane's 8 weights of each tensor as fp32 pairs
+  for (int e = 0; e < 4 * VPL; ++e) A[e] = B[e] = 0;
+  if (role != 2 && p.fs_h == 0) {
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const uint4 w = t < p.nt ? ldg_nc_v4(p.w[t] + 8 * hv) : make_uint4(0, 0, 0, 0);
-    wp[t][0] = bf16x2_to_f2(w.x); wp[t][1] = bf16x2_to_f2(w.y);
-    wp[t][2] = bf16x2_to_f2(w.z); wp[t][3] = bf16x2_to_f2(w.w);
+    for (int v = 0; v < VPL; ++v) rope_coeffs<TAB>(trow, pair0 + 8 * v, role, A + 4 * v, B + 4 * v);
+  }
+  // the lane's weights of each tensor (bf16 pairs; widened where used)
+  uint4 wv0[VPL], wv1[VPL];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) {
+    wv0[v] = ldg_nc_v4(p.w[0] + 8 * (VPL * hv + v));
+    wv1[v] = p.nt > 1 ? ldg_nc_v4(p.w[1] + 8 * (VPL * hv + v)) : wv0[v];
   }
 
   const int total = p.nt * p.heads;
-#pragma unroll 2
-  for (int base = 0; base < total; base += 2) {
-    const int hh = base + hsel;
+  const int iters = (total + HPI - 1) / HPI;
+  // this token's rows of each tensor (lane offset included); selects, not
+  // runtime-indexed arrays, so everything stays in registers
+  const __nv_bfloat16* const xrow0 = p.x[0] + tok * p.xs_t[0] + 8 * VPL * hv;
+  const __nv_bfloat16* const xrow1 = p.x[1] + tok * p.xs_t[1] + 8 * VPL * hv;
+  __nv_bfloat16* const yrow0 = p.y[0] + tok * p.ys_t[0] + 8 * VPL * hv;
+  __nv_bfloat16* const yrow1 = p.y[1] + tok * p.ys_t[1] + 8 * VPL * hv;
+  const int64_t xsh0 = p.xs_h[0], xsh1 = p.xs_h[1], ysh0 = p.ys_h[0], ysh1 = p.ys_h[1];
+  // Each lane streams its own bytes of head HPI i + hsel into a per-warp
+  // shared-memory ring with cp.async, S - 1 iterations ahead, and reads back
+  // only what it copied itself (cp.async.wait_group orders it, no barrier).
+  // The heads read ahead are never the ones being written, so in place is exact.
+  __shared__ __align__(16) uint4 ring_s[kQKWarpsPerBlock][S][32 * VPL];
+  uint4* const ring = &ring_s[threadIdx.x >> 5][0][lane * VPL];
+  auto issue = [&](int it) {
+    const int hh = HPI * it + hsel;
+    if (it < iters && hh < total) {
+      const __nv_bfloat16* src = hh >= p.heads ? xrow1 + (int64_t)(hh - p.heads) * xsh1 : xrow0 + (int64_t)hh * xsh0;
+#pragma unroll
+      for (int v = 0; v < VPL; ++v)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(ring + (it & (S - 1)) * 32 * VPL + v)),
+                     "l"(src + 8 * v)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int i = 0; i < S - 1; ++i) issue(i);
+  for (int it = 0; it < iters; ++it) {
+    issue(it + S - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(S - 1) : "memory");
+    const int hh = HPI * it + hsel;
     const bool ok = hh < total;
-    const int hc = ok ? hh : base;  // an existing head for the half-warp past the end
+    uint4 xv[VPL];
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) xv[v] = ok ? ring[(it & (S - 1)) * 32 * VPL + v] : make_uint4(0, 0, 0, 0);
+    const int hc = ok ? hh : total - 1;
     const int t = hc >= p.heads ? 1 : 0;
     const int h = hc - t * p.heads;
-    const uint4 xv = ldg_v4(p.x[t] + tok * p.xs_t[t] + h * p.xs_h[t] + 8 * hv);
-    if (role != 2 && p.fs_h != 0) rope_coeffs<TAB>(trow + h * p.fs_h * kTabElemBytes, pair0, role, A, B);
-    // sum of squares over the head's 128 values (16 lanes), double
+    if (role != 2 && p.fs_h != 0) {
+#pragma unroll
+      for (int v = 0; v < VPL; ++v)
+        rope_coeffs<TAB>(trow + h * p.fs_h * kTabElemBytes, pair0 + 8 * v, role, A + 4 * v, B + 4 * v);
+    }
+    // sum of squares over the head's 128 values (LPH lanes), double
     double acc[4] = {0.0, 0.0, 0.0, 0.0};
-    sumsq8_fast(xv, acc);
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) sumsq8_fast(xv[v], acc);
     double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    float ms = (float)(sum / 128.0);
+    for (int o = LPH / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    float ms = (float)(sum * 0.0078125);   // / 128, exact
     const bool bad = !isfinite(ms);
     if (__any_sync(0xffffffffu, bad)) {  // inf / NaN / huge: exact conversions
       double ex[4] = {0.0, 0.0, 0.0, 0.0};
-      sumsq8_exact(xv, ex);
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) sumsq8_exact(xv[v], ex);
       double se = (ex[0] + ex[1]) + (ex[2] + ex[3]);
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
-      if (bad) ms = (float)(se / 128.0);
+      for (int o = LPH / 2; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+      if (bad) ms = (float)(se * 0.0078125);
     }
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
     const uint64_t rs2 = f2_pack(rs, rs);
-    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-    uint32_t hb[4];
+    __nv_bfloat16* const dst = (t ? yrow1 : yrow0) + (int64_t)h * (t ? ysh1 : ysh0);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) hb[e] = f2_to_bf16x2(f2_mul(f2_mul(bf16x2_to_f2(xw[e]), rs2), wp[t][e]));
-    uint32_t o[4];
+    for (int v = 0; v < VPL; ++v) {
+      const uint32_t xw[4] = {xv[v].x, xv[v].y, xv[v].z, xv[v].w};
+      const uint4 wv = t ? wv1[v] : wv0[v];
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t hb[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const uint32_t pw = __shfl_sync(0xffffffffu, hb[e], partner);
-      float p0, p1, q0, q1;
-      f2_unpack(f2_mul(A[e], bf16x2_to_f2(hb[e])), p0, p1);
-      f2_unpack(f2_mul(B[e], bf16x2_to_f2(pw)), q0, q1);
-      o[e] = role == 2 ? hb[e] : pack_bf16(__fadd_rn(p0, q0), __fadd_rn(p1, q1));
+      for (int e = 0; e < 4; ++e) hb[e] = f2_to_bf16x2(f2_mul(f2_mul(bf16x2_to_f2(xw[e]), rs2), bf16x2_to_f2(ww[e])));
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t pw = __shfl_sync(0xffffffffu, hb[e], partner);
+        float p0, p1, q0, q1;
+        f2_unpack(f2_mul(A[4 * v + e], bf16x2_to_f2(hb[e])), p0, p1);
+        f2_unpack(f2_mul(B[4 * v + e], bf16x2_to_f2(pw)), q0, q1);
+        o[e] = role == 2 ? hb[e] : pack_bf16(__fadd_rn(p0, q0), __fadd_rn(p1, q1));
+      }
+      if (ok) stg_v4(dst + 8 * v, make_uint4(o[0], o[1], o[2], o[3]));
     }
-    if (ok) stg_v4(p.y[t] + tok * p.ys_t[t] + h * p.ys_h[t] + 8 * hv, make_uint4(o[0], o[1], o[2], o[3]));
   }
 }
 
@@ -560,7 +618,50 @@ __global__ void __launch_bounds__(256) copy_heads_kernel(const __nv_bfloat16* __
   stg_v4(y + t * ys_t + h * ys_h + 8 * v, ldg_nc_v4(x + t * xs_t + h * xs_h + 8 * v));
 }
 
+// rope_t[p * m + t] = row p of token t's table as fp32 {t00, t01, t10, t11}
+template <int TAB>
+__global__ void __launch_bounds__(256) rope_table_transpose_kernel(const void* __restrict__ freqs, int64_t fs_t,
+                                                                   int64_t m, int pairs, float4* __restrict__ rope_t) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // i = p * m + t: coalesced stores
+  if (i >= m * pairs) return;
+  const int p = (int)(i / m);
+  const int64_t t = i - (int64_t)p * m;
+  float4 v;
+  if constexpr (TAB == 0) {
+    v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(freqs) + t * fs_t) + p);
+  } else {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(freqs) + t * fs_t) + p);
+    if constexpr (TAB == 1) {
+      v = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+    } else {
+      v = make_float4(__half2float(__ushort_as_half((unsigned short)(u.x & 0xFFFFu))),
+                      __half2float(__ushort_as_half((unsigned short)(u.x >> 16))),
+                      __half2float(__ushort_as_half((unsigned short)(u.y & 0xFFFFu))),
+                      __half2float(__ushort_as_half((unsigned short)(u.y >> 16))));
+    }
+  }
+  rope_t[i] = v;
+}
+
 }  // namespace
+
+cudaError_t launch_rope_table_transpose(const void* freqs, int table_dtype, int64_t fs_t, int64_t m, int pairs,
+                                        float4* rope_t, cudaStream_t stream) {
+  if (m == 0 || pairs == 0) return cudaSuccess;
+  const int tab_bytes = table_dtype == 0 ? 4 : 2;
+  if (freqs == nullptr || table_dtype < 0 || table_dtype > 2 || pairs < 0 || fs_t < 0 ||
+      (reinterpret_cast<uintptr_t>(freqs) % (4 * tab_bytes)) || (fs_t % 4) || (reinterpret_cast<uintptr_t>(rope_t) & 15))
+    return cudaErrorNotSupported;
+  const int64_t total = m * pairs;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  if (table_dtype == 0)
+    rope_table_transpose_kernel<0><<<grid, 256, 0, stream>>>(freqs, fs_t, m, pairs, rope_t);
+  else if (table_dtype == 1)
+    rope_table_transpose_kernel<1><<<grid, 256, 0, stream>>>(freqs, fs_t, m, pairs, rope_t);
+  else
+    rope_table_transpose_kernel<2><<<grid, 256, 0, stream>>>(freqs, fs_t, m, pairs, rope_t);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_copy_heads(const void* x, int64_t xs_t, int64_t xs_h, void* y, int64_t ys_t, int64_t ys_h,
                               int64_t m, int64_t heads, cudaStream_t stream) {
@@ -613,12 +714,18 @@ cudaError_t launch_qk_rms_rope(const QKNormRopeArgs& a, cudaStream_t stream) {
   const int64_t blocks = (a.m + kQKWarpsPerBlock - 1) / kQKWarpsPerBlock;
   if (blocks > 0x7FFFFFFF) return cudaErrorNotSupported;
   const dim3 grid((unsigned)blocks), block(32 * kQKWarpsPerBlock);
+  // eight lanes per head when the rotation halves are whole lanes of 16 dims
+  const bool lph8 = p.half_v % 2 == 0;
+#define H3_QK(TAB)                                                               \
+  (lph8 ? qk_rms_rope_kernel<TAB, 8><<<grid, block, 0, stream>>>(p)              \
+        : qk_rms_rope_kernel<TAB, 16><<<grid, block, 0, stream>>>(p))
   if (a.table_dtype == 0)
-    qk_rms_rope_kernel<0><<<grid, block, 0, stream>>>(p);
+    H3_QK(0);
   else if (a.table_dtype == 1)
-    qk_rms_rope_kernel<1><<<grid, block, 0, stream>>>(p);
+    H3_QK(1);
   else
-    qk_rms_rope_kernel<2><<<grid, block, 0, stream>>>(p);
+    H3_QK(2);
+#undef H3_QK
   return cudaGetLastError();
 }
 
