@@ -29,8 +29,9 @@
 // kind::f16 MMAs that accumulate sx[rows, :kp] . corr_t[cols, :kp]^T onto it,
 // their operands TMA-loaded into shared memory reserved for them (the stage
 // ring shrinks to make room); a second pass reads the corrected sums.
-// Tiles are visited n-fastest so that the concurrently running CTAs share the
-// same A rows and the whole weight stays resident in the 126 MB L2.
+// Tiles are visited N-fastest when the weight fits in L2 (it stays resident and
+// the running CTAs share A rows), else in groups of 8 M-blocks with M fastest
+// inside a group (the weight streams past L2 once per group; see tile_coords).
 // No cluster multicast is used anywhere (the same binary runs in multi-GPU jobs).
 #include "common.cuh"
 #include "kernels.h"
@@ -73,6 +74,7 @@ constexpr unsigned kErrProducer = 0x101, kErrMmaAcc = 0x102, kErrMmaFull = 0x103
 struct KParams {
   int m, n, k;
   int num_n_blk, num_k_blk, num_tiles;
+  int num_m_blk, group_m;  // tile order: groups of group_m M-blocks (see tile_coords)
   const float* a_scale;
   const float* w_scale;
   int w_pc;
@@ -268,6 +270,22 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
   }
 }
 
+// Tile order of the persistent walkers: groups of group_m M-blocks; inside a group
+// the M-block changes fastest, then the N-block. With group_m = 1 (weights up to
+// 64 MB) this is N-fastest: the running CTAs share one A row block and the whole
+// weight stays resident in L2. For a larger weight (the H3 projections, 77-154 MB)
+// group_m = 8: the running CTAs cover about 8 M-blocks x (CTAs / 8) N-blocks, the
+// group's activation rows stay in L2 and the weight streams past once per group,
+// num_m_blk / 8 times instead of once per M-block.
+__device__ __forceinline__ void tile_coords(int tile, const KParams& p, int& m_blk, int& n_blk) {
+  const int per_group = p.group_m * p.num_n_blk;
+  const int g = tile / per_group;
+  const int rem = tile - g * per_group;
+  const int gm = min(p.group_m, p.num_m_blk - g * p.group_m);  // the last group may be shorter
+  n_blk = rem / gm;
+  m_blk = g * p.group_m + (rem - n_blk * gm);
+}
+
 // ---- kEpiQKV helpers: one thread holds one head (128 values) of one token ----
 // |bf16| of the low / high half of w as a double, built from its bits (exact for
 // normal values; zero and subnormals become a value below 2^-126 whose square
@@ -406,8 +424,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int tile = cid; tile < p.num_tiles && ok; tile += ncl) {
-        const int m_blk = tile / p.num_n_blk;
-        const int n_blk = tile - m_blk * p.num_n_blk;
+        int m_blk, n_blk;
+        tile_coords(tile, p, m_blk, n_blk);
         const int a_row = m_blk * kTileRows + (int)rank * BM;
         const int b_row = n_blk * BN + (int)rank * (BN / CG);
         for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
@@ -521,8 +539,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bool in_pending = false;  // an input-box load was issued and not yet waited for
     bool ok = true;
     for (int tile = cid; tile < p.num_tiles && ok; tile += ncl, ++tcount) {
-      const int m_blk = tile / p.num_n_blk;
-      const int n_blk = tile - m_blk * p.num_n_blk;
+      int m_blk, n_blk;
+      tile_coords(tile, p, m_blk, n_blk);
       const int acc = tcount & 1;
       const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
       const int row0 = m_blk * kTileRows + (int)rank * BM;  // this CTA's first row of the tile
@@ -1041,6 +1059,10 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   const int64_t tiles = num_m_blk * kp.num_n_blk;
   if (tiles > (1ll << 30)) return cudaErrorNotSupported;
   kp.num_tiles = (int)tiles;
+  kp.num_m_blk = (int)num_m_blk;
+  // a weight that fits comfortably in the 126 MB L2 stays resident with N-fastest
+  // order (group of one M-block); a larger one streams past once per group of 8
+  kp.group_m = a.n * a.k <= (64ll << 20) ? 1 : (int)std::min<int64_t>(num_m_blk, 8);
   kp.a_scale = a.a_scale;
   kp.w_scale = a.w_scale;
   kp.w_pc = a.w_scale_per_channel;
