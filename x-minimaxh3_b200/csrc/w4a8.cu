@@ -350,12 +350,13 @@ __global__ void correction_transpose_kernel(const __nv_bfloat16* __restrict__ co
 }
 
 // ---------------------------------------------------------------------------
-// ConvRot-256 + row quantization, persistent, for K = 1536 PPW (PPW = 2, 4, 8:
-// K = 3072, 6144, 12288). One CTA per SM: a producer warp streams rows into a
+// ConvRot-256 + row quantization, persistent, for rows of ng 256-groups (K = 256 ng,
+// ng <= 12 NP; NP = 1..4 covers K up to 12288). One CTA per SM: a producer warp streams rows into a
 // ring of one-row stages (cp.async.bulk, completion counted on mbarriers);
 // 12 consumer warps form 4 teams of 3, each team taking every 4th row of the
 // CTA, so that 4 rows are in flight at different points of their work. The
-// team's 6 half-warps take PPW groups each and rotate them two at a time in
+// team's 6 half-warps take 2 NP group slots each (slots past ng hold zeros and are
+// never stored) and rotate them two at a time in
 // lock step (group a in the low, group b in the high half of packed f32x2
 // registers) with the butterflies, transposes and summation order of
 // quantize_convrot_kernel; the 1/16 normalisation is folded exactly into the
@@ -431,21 +432,15 @@ __device__ __forceinline__ void h4x2_hi(uint64_t (&P)[16]) {
 }
 
 // Consumer teams of a CTA (12 consumer warps); 4 rows in flight.
-template <int PPW>
-constexpr int cr_teams() {
-  return kCrTeams;
-}
-
-template <int PPW>
-__global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * cr_teams<PPW>()), 1)
+template <int NP>
+__global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * kCrTeams), 1)
     convrot_ring_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t m, int act,
                         int8_t* __restrict__ q, float* __restrict__ scale, __nv_bfloat16* __restrict__ sx,
-                        int sum_group, int64_t kp, int stages) {
-  constexpr int K = 1536 * PPW;
-  constexpr int ROW_BYTES = 2 * K;
+                        int sum_group, int64_t kp, int stages, int ng) {
+  const int K = 256 * ng;
+  const int ROW_BYTES = 2 * K;
   constexpr int HALF_GROUPS = 2 * kCrTeamWarps;  // half-warps of a team
-  constexpr int TEAMS = cr_teams<PPW>();
-  constexpr int NP = PPW / 2;                     // group pairs per half-warp
+  constexpr int TEAMS = kCrTeams;                // NP: group pairs per half-warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
@@ -518,14 +513,16 @@ __global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * cr_teams<PPW>()), 1)
 #pragma unroll 1
     for (int pr = 0; pr < NP; ++pr) {
       const int ga = hw + HALF_GROUPS * pr, gb = ga + HALF_GROUPS * NP;
-      uint8_t* sa = const_cast<uint8_t*>(st) + ga * 512 + li * 32;
-      uint8_t* sb = const_cast<uint8_t*>(st) + gb * 512 + li * 32;
+      const bool oka = ga < ng, okb = gb < ng;  // slots past the row hold zeros
+      uint8_t* sa = const_cast<uint8_t*>(st) + (oka ? ga : 0) * 512 + li * 32;
+      uint8_t* sb = const_cast<uint8_t*>(st) + (okb ? gb : 0) * 512 + li * 32;
       uint32_t wa[8], wb[8];
       {
-        const uint4 a0 = *reinterpret_cast<const uint4*>(sa + 16 * c1);
-        const uint4 a1 = *reinterpret_cast<const uint4*>(sa + 16 - 16 * c1);
-        const uint4 b0 = *reinterpret_cast<const uint4*>(sb + 16 * c1);
-        const uint4 b1 = *reinterpret_cast<const uint4*>(sb + 16 - 16 * c1);
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        const uint4 a0 = oka ? *reinterpret_cast<const uint4*>(sa + 16 * c1) : z;
+        const uint4 a1 = oka ? *reinterpret_cast<const uint4*>(sa + 16 - 16 * c1) : z;
+        const uint4 b0 = okb ? *reinterpret_cast<const uint4*>(sb + 16 * c1) : z;
+        const uint4 b1 = okb ? *reinterpret_cast<const uint4*>(sb + 16 - 16 * c1) : z;
         wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w; wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
         wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w; wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
       }
@@ -575,11 +572,19 @@ __global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * cr_teams<PPW>()), 1)
         wab[e] = pack_bf16(a, b);
         amax = __vmaxu2(amax, wab[e] & 0x7FFF7FFFu);  // per-half running max of |bf16|
       }
-      if (NP > 1) {
-        *reinterpret_cast<uint4*>(sa) = make_uint4(wab[0], wab[1], wab[2], wab[3]);
-        *reinterpret_cast<uint4*>(sa + 16) = make_uint4(wab[4], wab[5], wab[6], wab[7]);
-        *reinterpret_cast<uint4*>(sb) = make_uint4(wab[8], wab[9], wab[10], wab[11]);
-        *reinterpret_cast<uint4*>(sb + 16) = make_uint4(wab[12], wab[13], wab[14], wab[15]);
+      if (NP > 1) {  // park the pair in this lane's own slots of the groups it read
+        if (okb) {     // the 16 (a, b) words span both 32-byte slots
+          *reinterpret_cast<uint4*>(sa) = make_uint4(wab[0], wab[1], wab[2], wab[3]);
+          *reinterpret_cast<uint4*>(sa + 16) = make_uint4(wab[4], wab[5], wab[6], wab[7]);
+          *reinterpret_cast<uint4*>(sb) = make_uint4(wab[8], wab[9], wab[10], wab[11]);
+          *reinterpret_cast<uint4*>(sb + 16) = make_uint4(wab[12], wab[13], wab[14], wab[15]);
+        } else if (oka) {  // empty b slot: group a's 16 values (the low halves) fit its own slot
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[i] = __byte_perm(wab[2 * i], wab[2 * i + 1], 0x5410);
+          *reinterpret_cast<uint4*>(sa) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(sa + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+        }
       }
     }
     // row absmax over the team
@@ -601,14 +606,25 @@ __global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * cr_teams<PPW>()), 1)
 #pragma unroll 1
     for (int pr = 0; pr < NP; ++pr) {
       const int ga = hw + HALF_GROUPS * pr, gb = ga + HALF_GROUPS * NP;
+      const bool oka = ga < ng, okb = gb < ng;
       if (NP > 1) {
-        const uint8_t* sa = st + ga * 512 + li * 32;
-        const uint8_t* sb = st + gb * 512 + li * 32;
-        const uint4 a0 = *reinterpret_cast<const uint4*>(sa), a1 = *reinterpret_cast<const uint4*>(sa + 16);
-        const uint4 b0 = *reinterpret_cast<const uint4*>(sb), b1 = *reinterpret_cast<const uint4*>(sb + 16);
-        wab[0] = a0.x; wab[1] = a0.y; wab[2] = a0.z; wab[3] = a0.w; wab[4] = a1.x; wab[5] = a1.y; wab[6] = a1.z;
-        wab[7] = a1.w; wab[8] = b0.x; wab[9] = b0.y; wab[10] = b0.z; wab[11] = b0.w; wab[12] = b1.x; wab[13] = b1.y;
-        wab[14] = b1.z; wab[15] = b1.w;
+        const uint8_t* sa = st + (oka ? ga : 0) * 512 + li * 32;
+        const uint8_t* sb = st + (okb ? gb : 0) * 512 + li * 32;
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        const uint4 a0 = oka ? *reinterpret_cast<const uint4*>(sa) : z, a1 = oka ? *reinterpret_cast<const uint4*>(sa + 16) : z;
+        if (okb) {
+          const uint4 b0 = *reinterpret_cast<const uint4*>(sb), b1 = *reinterpret_cast<const uint4*>(sb + 16);
+          wab[0] = a0.x; wab[1] = a0.y; wab[2] = a0.z; wab[3] = a0.w; wab[4] = a1.x; wab[5] = a1.y; wab[6] = a1.z;
+          wab[7] = a1.w; wab[8] = b0.x; wab[9] = b0.y; wab[10] = b0.z; wab[11] = b0.w; wab[12] = b1.x; wab[13] = b1.y;
+          wab[14] = b1.z; wab[15] = b1.w;
+        } else {  // group a's values only (b is an empty slot: zeros in the high halves)
+          const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            wab[2 * i] = w[i] & 0xFFFFu;
+            wab[2 * i + 1] = w[i] >> 16;
+          }
+        }
       }
       // quantize in the transposed order; bytes land in natural order in the byte tile
 #pragma unroll
@@ -625,13 +641,14 @@ __global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * cr_teams<PPW>()), 1)
 #pragma unroll
       for (int pg = 0; pg < 2; ++pg) {
         const int g = pg ? gb : ga;
+        const bool live = g < ng;  // an empty slot stores nothing (its lanes still take part in the shuffles)
         const uint4 v = *reinterpret_cast<const uint4*>(bt + pg * 256 + 16 * li);
-        stg_v4(q + row * K + g * 256 + 16 * li, v);
+        if (live) stg_v4(q + row * K + g * 256 + 16 * li, v);
         if (sx != nullptr) {  // all lanes shuffle; partners stay inside the half-warp (offsets < 16)
           int isum = __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
                             __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0))));
           for (int o = 1; o < lanes_per_sum; o <<= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-          if ((li % lanes_per_sum) == 0)
+          if (live && (li % lanes_per_sum) == 0)
             sx[row * kp + (g * 256 + 16 * li) / sum_group] =
                 __float2bfloat16_rn(__fmul_rn(bf16_round((float)isum), bf16_round(s_row)));
         }
@@ -688,10 +705,11 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
     const cudaError_t e = ensure_act_table(act, stream);
     if (e != cudaSuccess) return e;
   }
-  const int64_t rppw = k / 1536;
+  const int64_t ngroups = k / 256;
+  const int64_t np = (ngroups + 2 * 6 - 1) / (2 * 6);  // group pairs per half-warp of a 6-half-warp team
   // the persistent kernel's stages hold one activated-width row, so SwiGLU rows
   // ([gate | up], twice as wide) take the per-row kernel
-  if (k % 1536 == 0 && (rppw == 2 || rppw == 4 || rppw == 8) && act != H3B200_ACT_SWIGLU) {
+  if (np >= 1 && np <= 4 && act != H3B200_ACT_SWIGLU) {
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64][9] = {};
@@ -703,20 +721,21 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
     __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
     const int sg = sx != nullptr ? (int)sum_group : 16;
     auto go = [&](auto kern) -> cudaError_t {
-      if (dev >= 0 && dev < 64 && !attr_set[dev][rppw]) {
+      if (dev >= 0 && dev < 64 && !attr_set[dev][np]) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kCrSmemLimit);
         if (e != cudaSuccess) return e;
-        attr_set[dev][rppw] = true;
+        attr_set[dev][np] = true;
       }
       const int threads = 32 * (1 + kCrConsumers);
-      kern<<<grid, threads, smem, stream>>>(xb, ldx, m, act, q, scale, sxb, sg, kp, stages);
+      kern<<<grid, threads, smem, stream>>>(xb, ldx, m, act, q, scale, sxb, sg, kp, stages, (int)ngroups);
       return cudaGetLastError();
     };
     if (stages >= 2 * kCrTeams) {  // two stages per team at least
-      switch (rppw) {
+      switch (np) {
+        case 1: return go(convrot_ring_kernel<1>);
         case 2: return go(convrot_ring_kernel<2>);
+        case 3: return go(convrot_ring_kernel<3>);
         case 4: return go(convrot_ring_kernel<4>);
-        case 8: return go(convrot_ring_kernel<8>);
         default: break;
       }
     }
