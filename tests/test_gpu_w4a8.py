@@ -34,11 +34,14 @@ def test_convrot_quantize_vs_golden(golden):
 
 @pytest.mark.parametrize("m,k,ldx", [(1001, 3072, 3072), (37, 12288, 12288), (250, 6144, 6208), (13, 1024, 1024),
                                      (29, 2048, 2048), (45, 4096, 4096), (7, 2304, 2304), (300, 5376, 5376),
-                                     (3, 256, 256), (61, 9216, 9216), (40, 11008, 11008), (9, 14336, 14336)])
+                                     (3, 256, 256), (61, 9216, 9216), (40, 11008, 11008), (9, 14336, 14336),
+                                     (401, 12544, 12544), (1500, 14336, 14336), (77, 15360, 15424),
+                                     (5, 15616, 15616)])
 def test_convrot_quantize_shapes_vs_oracle(m, k, ldx):
-    """The persistent ConvRot quantizer for every group-pair count (1-4 pairs per half-warp, rows of
-    1 to 48 groups, partly filled slots such as H3's 21 groups), row counts that leave a stage
-    partly filled, strided rows, and K = 14336 (56 groups: the per-row kernel).
+    """The persistent ConvRot quantizer for every group-pair count (1-5 pairs per half-warp, rows of
+    1 to 60 groups, partly filled slots such as H3's 21 groups), row counts that leave a stage
+    partly filled, strided rows, 7-stage rings that wrap many times (1,500 rows of H3's 56-group
+    fc2 input), and K = 15616 (61 groups: the per-row kernel).
     (The correction operand it also emits is checked through the W4A8 linear and MLP tests.)"""
     gen = torch.Generator().manual_seed(k + m)
     xfull = randn_bf16((m, ldx), gen)

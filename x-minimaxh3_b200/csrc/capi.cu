@@ -494,7 +494,7 @@ int run_swiglu_mlp(const SwiGLUMlp& a, void* work, int64_t work_bytes, cudaStrea
   Carver c{static_cast<uint8_t*>(work), work_bytes};
   int8_t* xq = static_cast<int8_t*>(c.take(chunk * d));
   float* xs = static_cast<float*>(c.take(chunk * 4));
-  void* raw = c.take(chunk * 2 * ffn * 2);
+  void* hbuf = c.take(chunk * 2 * ffn * 2);
   int8_t* q2 = static_cast<int8_t*>(c.take(chunk * ffn));
   float* xs2 = static_cast<float*>(c.take(chunk * 4));
   if (!c.ok) return fail(H3B200_ERR_INVALID, "%s: workspace too small", who);
@@ -503,20 +503,22 @@ int run_swiglu_mlp(const SwiGLUMlp& a, void* work, int64_t work_bytes, cudaStrea
   auto* ob = static_cast<__nv_bfloat16*>(a.out);
   for (int64_t s0 = 0; s0 < m; s0 += chunk) {
     const int64_t mc = std::min(chunk, m - s0);
-    // fc1: (ConvRot-)quantize x, GEMM, dequant (+ bias) -> raw [mc, 2 ffn] = [gate | up]
+    // fc1: (ConvRot-)quantize x, GEMM with the SwiGLU epilogue: the gate and up halves
+    // of each output column are dequantized (+ bias) and combined in the same tile,
+    // h [mc, ffn] = bf16(silu(gate) * up)
     cudaError_t e = a.fc1_convrot_group
                         ? h3::launch_quantize_convrot(xb + s0 * a.ldx, a.ldx, mc, d, H3B200_ACT_NONE, xq, xs, nullptr, 0, 0, st)
                         : h3::launch_quantize_rows(xb + s0 * a.ldx, a.ldx, mc, d, H3B200_ACT_NONE, nullptr, xq, xs, st);
     if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: quantize x");
     h3::GemmArgs g1;
     g1.a = xq; g1.w = a.w1; g1.m = mc; g1.n = 2 * ffn; g1.k = d; g1.lda = d; g1.ldw = d;
-    g1.epilogue = h3::kEpiBF16; g1.a_scale = xs; g1.w_scale = a.s1; g1.w_scale_per_channel = a.s1_numel > 1 ? 1 : 0;
-    g1.bias = a.b1; g1.out = raw; g1.ldo = 2 * ffn;
+    g1.epilogue = h3::kEpiSwiGLU; g1.a_scale = xs; g1.w_scale = a.s1; g1.w_scale_per_channel = a.s1_numel > 1 ? 1 : 0;
+    g1.bias = a.b1; g1.out = hbuf; g1.ldo = ffn;
     e = h3::launch_gemm_i8(g1, st);
     if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: fc1");
-    // fc2: SwiGLU + ConvRot-256 + quantize, GEMM, dequant (+ bias), gated residual per modulation row
-    e = h3::launch_quantize_convrot(raw, 2 * ffn, mc, ffn, H3B200_ACT_SWIGLU, q2, xs2, nullptr, 0, 0, st);
-    if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: quantize swiglu(raw)");
+    // fc2: ConvRot-256 + quantize h, GEMM, dequant (+ bias), gated residual per modulation row
+    e = h3::launch_quantize_convrot(hbuf, ffn, mc, ffn, H3B200_ACT_NONE, q2, xs2, nullptr, 0, 0, st);
+    if (e != cudaSuccess) return from_cuda(e, "swiglu mlp: quantize h");
     h3::GemmArgs g2;
     g2.a = q2; g2.w = a.w2; g2.m = mc; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
     g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = a.s2; g2.w_scale_per_channel = a.s2_numel > 1 ? 1 : 0;

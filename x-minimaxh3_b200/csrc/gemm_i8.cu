@@ -94,6 +94,7 @@ struct KParams {
   const __nv_bfloat16* qk_w[2];
   const float4* rope_t;
   float qk_eps;
+  int up_row;  // kEpiSwiGLU: first up row of W (the output width f)
 };
 
 template <int EPI>
@@ -130,6 +131,14 @@ __device__ __forceinline__ uint32_t gelu_lookup(uint32_t hb, const uint16_t* tab
   const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
   if (rel < kGeluNE) return tab[(hb >> 15) * (kGeluNE * 128) + rel * 128 + (hb & 0x7Fu)];
   return bf16_bits(gelu_tanh_exact(__uint_as_float(hb << 16)));
+}
+
+// SiLU by the same table layout (kEpiSwiGLU fills it with silu_exact); inputs
+// outside it read the device-wide table of every bf16 input.
+__device__ __forceinline__ uint32_t silu_lookup(uint32_t hb, const uint16_t* tab) {
+  const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
+  if (rel < kGeluNE) return tab[(hb >> 15) * (kGeluNE * 128) + rel * 128 + (hb & 0x7Fu)];
+  return silu_bf16_bits(hb);
 }
 
 // GELU of 16 packed bf16 pairs, in place.
@@ -412,6 +421,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
       gelu_tab[i] = (uint16_t)bf16_bits(gelu_tanh_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
   }
+  if constexpr (EPI == kEpiSwiGLU) {  // SiLU of |x| in [2^-16, 8), both signs
+    for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
+      gelu_tab[i] = (uint16_t)bf16_bits(silu_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
+  }
   tc_fence_before();
   __syncthreads();
   if constexpr (CG == 2) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
@@ -427,7 +440,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int m_blk, n_blk;
         tile_coords(tile, p, m_blk, n_blk);
         const int a_row = m_blk * kTileRows + (int)rank * BM;
-        const int b_row = n_blk * BN + (int)rank * (BN / CG);
+        // kEpiSwiGLU: a tile is 128 output columns; its B rows are the 128 gate rows
+        // then the 128 up rows of those columns (rank 1 of a pair loads the up rows)
+        const int b_row = EPI == kEpiSwiGLU ? n_blk * (BN / 2) + (int)rank * p.up_row
+                                            : n_blk * BN + (int)rank * (BN / CG);
         for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (uint32_t)(it / kStages) & 1u;
@@ -445,6 +461,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
             tma_load_2d(sa, &tmA, &full_bar[s], kb * BK, a_row);
             tma_load_2d(sa + A_BYTES, &tmB, &full_bar[s], kb * BK, b_row);
+            if constexpr (EPI == kEpiSwiGLU)  // 128-row box: the up rows fill B rows [128, 256)
+              tma_load_2d(sa + A_BYTES + (BN / 2) * BK, &tmB, &full_bar[s], kb * BK, b_row + p.up_row);
           }
         }
       }
@@ -545,7 +563,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t acc_ph = (uint32_t)(tcount >> 1) & 1u;
       const int row0 = m_blk * kTileRows + (int)rank * BM;  // this CTA's first row of the tile
       const int row = row0 + quarter * 32 + lane;
-      const int col_base = n_blk * BN + half * 128;
+      // kEpiSwiGLU: output columns [64 half, 64 half + 64) of the tile's 128
+      const int col_base = EPI == kEpiSwiGLU ? n_blk * (BN / 2) + half * 64 : n_blk * BN + half * 128;
       if constexpr (kCorr) {
         // This tile's correction operands. The previous tile's correction MMAs
         // have completed (its cf_bar phase), so their buffers are free.
@@ -573,11 +592,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int c = lane + 32 * i;
-          const int col = col_base + c;
+          // kEpiSwiGLU: entries [0, 64) are the warp's gate columns, [64, 128) their up rows
+          const int col = EPI == kEpiSwiGLU ? col_base + (c & 63) : col_base + c;
+          const int wrow = EPI == kEpiSwiGLU && c >= 64 ? col + p.up_row : col;  // row of W
           const bool cok = col < p.n;
-          ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? col : 0)) : 0.0f;
+          ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? wrow : 0)) : 0.0f;
           float a = 0.0f;
-          if ((EPI == kEpiBF16 || EPI == kEpiQKV) && p.bias != nullptr && cok) a = __bfloat162float(p.bias[col]);
+          if ((EPI == kEpiBF16 || EPI == kEpiQKV || EPI == kEpiSwiGLU) && p.bias != nullptr && cok)
+            a = __bfloat162float(p.bias[wrow]);
           if (kInBox && cok && (EPI != kEpiGatedResidual || p.row_map == nullptr)) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
           if (EPI == kEpiGatedResidual && p.bias != nullptr) bias_s[c] = cok ? __bfloat162float(p.bias[col]) : 0.0f;
@@ -595,7 +617,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
       const int box_row0 = row0 + quarter * 32;
-      if constexpr (EPI == kEpiQKV) {
+      if constexpr (EPI == kEpiSwiGLU) {
+        // Accumulator columns [0, 128) are the gate and [128, 256) the up projection
+        // of the tile's 128 output columns; this warp combines its 64 of them.
+        const uint32_t tg = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 64);
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tg + c, rg);
+          tmem_ld32(tg + 128 + c, ru);
+          tmem_wait_ld();
+          if (col_base + c >= p.n || box_row0 >= p.m) continue;  // warp-uniform: nothing to store
+          if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
+          uint32_t ob[16];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {  // 4 columns: one float4 of each staged operand
+            const float4 wg = *reinterpret_cast<const float4*>(ws_s + c + 4 * q);
+            const float4 wu = *reinterpret_cast<const float4*>(ws_s + 64 + c + 4 * q);
+            const float wgv[4] = {wg.x, wg.y, wg.z, wg.w}, wuv[4] = {wu.x, wu.y, wu.z, wu.w};
+            float bgv[4] = {0.f, 0.f, 0.f, 0.f}, buv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (p.bias != nullptr) {
+              const float4 bg = *reinterpret_cast<const float4*>(aux_s + c + 4 * q);
+              const float4 bu = *reinterpret_cast<const float4*>(aux_s + 64 + c + 4 * q);
+              bgv[0] = bg.x; bgv[1] = bg.y; bgv[2] = bg.z; bgv[3] = bg.w;
+              buv[0] = bu.x; buv[1] = bu.y; buv[2] = bu.z; buv[3] = bu.w;
+            }
+            uint32_t hb[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t g = dequant_bits(rg[4 * q + e], xs, wgv[e]), u = dequant_bits(ru[4 * q + e], xs, wuv[e]);
+              if (p.bias != nullptr) {
+                g = bf16_bits(__fadd_rn(__uint_as_float(g << 16), bgv[e]));
+                u = bf16_bits(__fadd_rn(__uint_as_float(u << 16), buv[e]));
+              }
+              // bf16(bf16(silu(g)) * u): the product of two bf16 values is exact in fp32
+              hb[e] = bf16_bits(__fmul_rn(__uint_as_float(silu_lookup(g, gelu_tab) << 16), __uint_as_float(u << 16)));
+            }
+            ob[2 * q] = hb[0] | (hb[1] << 16);
+            ob[2 * q + 1] = hb[2] | (hb[3] << 16);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(box_row + ((q ^ box_sw) << 4)) =
+                make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]);
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, box, col_base + c, box_row0);  // rows >= m and columns >= n are clipped
+            bulk_commit_group();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {  // release the accumulator on the MMA issuer's barrier
+          if constexpr (CG == 2)
+            mbar_arrive_cluster(mapa_shared(&tempty_bar[acc], 0));
+          else
+            mbar_arrive(&tempty_bar[acc]);
+        }
+      } else if constexpr (EPI == kEpiQKV) {
         // The warp's 128 columns are one head of one section; each thread holds its
         // token's head in registers: dequant (+ bias), then for Q / K the RMSNorm over
         // the 128 values (sum of squares in double, in-thread) and the RoPE pairs,
@@ -685,132 +766,132 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bulk_commit_group();
           }
         }
-        continue;
-      }
-      if constexpr (kCorr) {
-        // pass 1: the dequantized values replace the int32 accumulators
-#pragma unroll 1
+      } else {
+        if constexpr (kCorr) {
+          // pass 1: the dequantized values replace the int32 accumulators
+  #pragma unroll 1
+          for (int c = 0; c < 128; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(taddr + c, r);
+            tmem_wait_ld();
+            dequant_to_f32(r, xs, ws_s + c);
+            tmem_st32(taddr + c, r);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 2)
+              mbar_arrive_cluster(mapa_shared(dq_bar, 0));
+            else
+              mbar_arrive(dq_bar);
+          }
+          const uint32_t ph = (uint32_t)tcount & 1u;
+          if (corr_thread && rank == 0) {
+            // D[rows, cols] += sx[rows, :kp] . corr_t[cols, :kp]^T: kind::f16, fp32 accumulate
+            const bool ready = (CG == 2 ? mbar_wait_cluster(dq_bar, ph, kErrCorr) : mbar_wait(dq_bar, ph, kErrCorr)) &&
+                               mbar_wait(corr_full_bar, ph, kErrCorr);
+            if (ready) {
+              tc_fence_after();
+              const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+              for (int kb = 0; kb < p.corr_kb; ++kb) {
+                const uint32_t a_addr = smem_u32(corr_sx + kb * (BM * 128));
+                const uint32_t b_addr = smem_u32(corr_ct + kb * ((BN / CG) * 128));
+  #pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  if constexpr (CG == 2)
+                    umma_bf16_pair(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                                   IDESC_BF16_PAIR, 1u);
+                  else
+                    umma_bf16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                              IDESC_BF16, 1u);
+                }
+              }
+              if constexpr (CG == 2) {
+                umma_commit_pair(mapa_shared(cf_bar, 0));
+                umma_commit_pair(mapa_shared(cf_bar, 1));
+              } else {
+                umma_commit(cf_bar);
+              }
+            }
+          }
+          if (!mbar_wait(cf_bar, ph, kErrEpi)) break;
+          tc_fence_after();
+        }
+  #pragma unroll 1
         for (int c = 0; c < 128; c += 32) {
           uint32_t r[32];
           tmem_ld32(taddr + c, r);
           tmem_wait_ld();
-          dequant_to_f32(r, xs, ws_s + c);
-          tmem_st32(taddr + c, r);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if constexpr (CG == 2)
-            mbar_arrive_cluster(mapa_shared(dq_bar, 0));
-          else
-            mbar_arrive(dq_bar);
-        }
-        const uint32_t ph = (uint32_t)tcount & 1u;
-        if (corr_thread && rank == 0) {
-          // D[rows, cols] += sx[rows, :kp] . corr_t[cols, :kp]^T: kind::f16, fp32 accumulate
-          const bool ready = (CG == 2 ? mbar_wait_cluster(dq_bar, ph, kErrCorr) : mbar_wait(dq_bar, ph, kErrCorr)) &&
-                             mbar_wait(corr_full_bar, ph, kErrCorr);
-          if (ready) {
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-            for (int kb = 0; kb < p.corr_kb; ++kb) {
-              const uint32_t a_addr = smem_u32(corr_sx + kb * (BM * 128));
-              const uint32_t b_addr = smem_u32(corr_ct + kb * ((BN / CG) * 128));
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                if constexpr (CG == 2)
-                  umma_bf16_pair(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
-                                 IDESC_BF16_PAIR, 1u);
-                else
-                  umma_bf16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
-                            IDESC_BF16, 1u);
-              }
-            }
-            if constexpr (CG == 2) {
-              umma_commit_pair(mapa_shared(cf_bar, 0));
-              umma_commit_pair(mapa_shared(cf_bar, 1));
-            } else {
-              umma_commit(cf_bar);
-            }
-          }
-        }
-        if (!mbar_wait(cf_bar, ph, kErrEpi)) break;
-        tc_fence_after();
-      }
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c, r);
-        tmem_wait_ld();
-        if (col_base + c >= p.n) continue;  // warp-uniform
-        if constexpr (EPI == kEpiI32) {
-          store_i32_chunk(p, row, col_base + c, r);
-        } else {
-          if (box_row0 >= p.m) continue;      // warp-uniform: no row of this box exists
-          if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
-          uint32_t in_w[16];
-          if constexpr (kInBox) {
-            if (lane == 0) {
-              mbar_arrive_expect_tx(&in_bar[ew], EPI_STAGE_BYTES);
-              tma_load_2d(box, &tmR, &in_bar[ew], col_base + c, box_row0);
-            }
-            in_pending = true;
-            if (!mbar_wait(&in_bar[ew], in_phase, kErrEpiIn)) {
-              ok = false;
-              break;
-            }
-            in_pending = false;
-            in_phase ^= 1u;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 v = *reinterpret_cast<const uint4*>(box_row + ((q ^ box_sw) << 4));
-              in_w[4 * q] = v.x; in_w[4 * q + 1] = v.y; in_w[4 * q + 2] = v.z; in_w[4 * q + 3] = v.w;
-            }
+          if (col_base + c >= p.n) continue;  // warp-uniform
+          if constexpr (EPI == kEpiI32) {
+            store_i32_chunk(p, row, col_base + c, r);
           } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) in_w[j] = 0u;
-          }
-          uint32_t gw[16];  // the row's gate values (kEpiGatedResidual with a row map)
-#pragma unroll
-          for (int j = 0; j < 16; ++j) gw[j] = 0u;
-          if constexpr (EPI == kEpiGatedResidual) {
-            if (p.row_map != nullptr && row < p.m) {
-              const __nv_bfloat16* grow = p.gate + (int64_t)__ldg(p.row_map + row) * p.ldg + col_base + c;
-#pragma unroll
+            if (box_row0 >= p.m) continue;      // warp-uniform: no row of this box exists
+            if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
+            uint32_t in_w[16];
+            if constexpr (kInBox) {
+              if (lane == 0) {
+                mbar_arrive_expect_tx(&in_bar[ew], EPI_STAGE_BYTES);
+                tma_load_2d(box, &tmR, &in_bar[ew], col_base + c, box_row0);
+              }
+              in_pending = true;
+              if (!mbar_wait(&in_bar[ew], in_phase, kErrEpiIn)) {
+                ok = false;
+                break;
+              }
+              in_pending = false;
+              in_phase ^= 1u;
+  #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                if (col_base + c + 8 * q < p.n) {
-                  const uint4 v = __ldg(reinterpret_cast<const uint4*>(grow + 8 * q));
-                  gw[4 * q] = v.x; gw[4 * q + 1] = v.y; gw[4 * q + 2] = v.z; gw[4 * q + 3] = v.w;
+                const uint4 v = *reinterpret_cast<const uint4*>(box_row + ((q ^ box_sw) << 4));
+                in_w[4 * q] = v.x; in_w[4 * q + 1] = v.y; in_w[4 * q + 2] = v.z; in_w[4 * q + 3] = v.w;
+              }
+            } else {
+  #pragma unroll
+              for (int j = 0; j < 16; ++j) in_w[j] = 0u;
+            }
+            uint32_t gw[16];  // the row's gate values (kEpiGatedResidual with a row map)
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) gw[j] = 0u;
+            if constexpr (EPI == kEpiGatedResidual) {
+              if (p.row_map != nullptr && row < p.m) {
+                const __nv_bfloat16* grow = p.gate + (int64_t)__ldg(p.row_map + row) * p.ldg + col_base + c;
+  #pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  if (col_base + c + 8 * q < p.n) {
+                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(grow + 8 * q));
+                    gw[4 * q] = v.x; gw[4 * q + 1] = v.y; gw[4 * q + 2] = v.z; gw[4 * q + 3] = v.w;
+                  }
                 }
               }
             }
-          }
-          uint32_t ob[16];
-          epilogue_values<EPI>(p, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, in_w, bias_s + c, gw, ob);
-          __syncwarp();
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(box_row + ((q ^ box_sw) << 4)) =
-                make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]);
-          fence_proxy_async_shared();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmO, box, col_base + c, box_row0);  // rows >= m and columns >= n are clipped
-            bulk_commit_group();
+            uint32_t ob[16];
+            epilogue_values<EPI>(p, r, xs, ws_s + c, aux_s + c, gelu_tab, amax_bits, in_w, bias_s + c, gw, ob);
+            __syncwarp();
+  #pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(box_row + ((q ^ box_sw) << 4)) =
+                  make_uint4(ob[4 * q], ob[4 * q + 1], ob[4 * q + 2], ob[4 * q + 3]);
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmO, box, col_base + c, box_row0);  // rows >= m and columns >= n are clipped
+              bulk_commit_group();
+            }
           }
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {  // release the accumulator on the MMA issuer's barrier
-        if constexpr (CG == 2)
-          mbar_arrive_cluster(mapa_shared(&tempty_bar[acc], 0));
-        else
-          mbar_arrive(&tempty_bar[acc]);
-      }
-      if constexpr (EPI == kEpiGeluAbsmax) {
-        if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, amax_bits << 16);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {  // release the accumulator on the MMA issuer's barrier
+          if constexpr (CG == 2)
+            mbar_arrive_cluster(mapa_shared(&tempty_bar[acc], 0));
+          else
+            mbar_arrive(&tempty_bar[acc]);
+        }
+        if constexpr (EPI == kEpiGeluAbsmax) {
+          if (row < p.m) atomicMax(reinterpret_cast<unsigned int*>(p.row_absmax) + row, amax_bits << 16);
+        }
       }
     }
     if constexpr (kInBox) {
@@ -901,6 +982,7 @@ cudaError_t launch_cg(int epilogue, const TensorMaps& t, const KParams& kp, int 
     case kEpiBF16CorrGelu: return launch_epi<kEpiBF16CorrGelu, CG>(t, kp, grid, stream);
     case kEpiGatedResidualCorr: return launch_epi<kEpiGatedResidualCorr, CG>(t, kp, grid, stream);
     case kEpiQKV: return launch_epi<kEpiQKV, CG>(t, kp, grid, stream);
+    case kEpiSwiGLU: return launch_epi<kEpiSwiGLU, CG>(t, kp, grid, stream);
     default: return cudaErrorNotSupported;
   }
 }
@@ -985,6 +1067,14 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
       if (a.qkv_sh[s] < a.qkv_st[s]) qkv_hmaj |= 1 << s;  // heads inside a token row: (dim, head, token) order
     }
   }
+  // kEpiSwiGLU: W's n rows are [gate | up]; the output is n / 2 columns wide
+  const bool swiglu = a.epilogue == kEpiSwiGLU;
+  if (swiglu && a.n % 16 != 0) return cudaErrorNotSupported;
+  const int64_t n_out = swiglu ? a.n / 2 : a.n;
+  if (swiglu) {
+    const cudaError_t e = ensure_act_table(H3B200_ACT_SWIGLU, stream);
+    if (e != cudaSuccess) return e;
+  }
   const bool gated = a.epilogue == kEpiGatedResidual || a.epilogue == kEpiGatedResidualCorr;
   if (gated && ((reinterpret_cast<uintptr_t>(a.residual) & 15) || a.ldr % 8 != 0)) return cudaErrorNotSupported;
   if (a.row_map != nullptr && (a.epilogue != kEpiGatedResidual || a.ldg < a.n || a.ldg % 8 != 0 ||
@@ -999,11 +1089,11 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   const int sms = num_sms(dev);
   // CTA pairs (256 x 256 tiles, cta_group::2) for the GEMMs with enough tiles
   // to give every SM pair work; single CTAs otherwise.
-  const int64_t n_blk = (a.n + BN - 1) / BN;
+  const int64_t n_blk = swiglu ? (n_out + BN / 2 - 1) / (BN / 2) : (a.n + BN - 1) / BN;
   const bool pair = ((a.m + 2 * BM - 1) / (2 * BM)) * n_blk >= sms / 2;
   const int cg = pair ? 2 : 1;
   TensorMaps t;
-  if (!make_tmap_i8(&t.a, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&t.b, a.w, a.n, a.k, a.ldw, BN / cg))
+  if (!make_tmap_i8(&t.a, a.a, a.m, a.k, a.lda, BM) || !make_tmap_i8(&t.b, a.w, a.n, a.k, a.ldw, swiglu ? BN / 2 : BN / cg))
     return cudaErrorInvalidValue;
   if (qkv) {
     // one [m, heads, 128] map per present section, boxes of 32 dims x 32 tokens
@@ -1023,7 +1113,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
     }
   } else if (a.epilogue == kEpiI32) {
     t.out = t.b;  // unused: int32 results are stored directly
-  } else if (!encode_tmap_2d(&t.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)a.n, (uint64_t)a.m,
+  } else if (!encode_tmap_2d(&t.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)n_out, (uint64_t)a.m,
                              (uint64_t)a.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return cudaErrorInvalidValue;
   }
@@ -1051,7 +1141,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   }
   KParams kp;
   kp.m = (int)a.m;
-  kp.n = (int)a.n;
+  kp.n = (int)n_out;
   kp.k = (int)a.k;
   kp.num_n_blk = (int)n_blk;
   kp.num_k_blk = (int)((a.k + BK - 1) / BK);
@@ -1084,6 +1174,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.qk_w[1] = static_cast<const __nv_bfloat16*>(a.qk_w[1]);
   kp.rope_t = a.rope_t;
   kp.qk_eps = a.qk_eps;
+  kp.up_row = swiglu ? (int)n_out : 0;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

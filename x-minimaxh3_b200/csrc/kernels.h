@@ -21,6 +21,10 @@ enum GemmEpilogue : int {
   // Q/K/V projection into attention layouts: y = bf16(bf16(acc * (xs * ws)) + bias);
   // Q and K heads get per-head RMSNorm and partial split-half RoPE, V is stored as is.
   kEpiQKV = 7,
+  // kEpiSwiGLU: W holds n = 2 f rows, gate rows [0, f) then up rows [f, 2 f);
+  // out [m, f] = bf16(silu(g) * u) with g, u = bf16(acc * (xs * ws)) (+ bf16 bias,
+  // rounded), the reference's fc1 -> silu(gate).mul_(up) in one pass
+  kEpiSwiGLU = 8,
 };
 
 struct GemmArgs {

@@ -709,7 +709,7 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
   const int64_t np = (ngroups + 2 * 6 - 1) / (2 * 6);  // group pairs per half-warp of a 6-half-warp team
   // the persistent kernel's stages hold one activated-width row, so SwiGLU rows
   // ([gate | up], twice as wide) take the per-row kernel
-  if (np >= 1 && np <= 4 && act != H3B200_ACT_SWIGLU) {
+  if (np >= 1 && np <= 5 && act != H3B200_ACT_SWIGLU) {
     int dev = 0;
     cudaGetDevice(&dev);
     static bool attr_set[64][9] = {};
@@ -730,12 +730,17 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
       kern<<<grid, threads, smem, stream>>>(xb, ldx, m, act, q, scale, sxb, sg, kp, stages, (int)ngroups);
       return cudaGetLastError();
     };
-    if (stages >= 2 * kCrTeams) {  // two stages per team at least
+    // A team waits for row j after consuming its row j - teams; the producer fills in
+    // order, so with stages >= teams the stage's previous row (j - stages) has landed
+    // and the parity wait cannot pass on the phase before it. Rows of up to 48
+    // groups get 8 or more stages; 49-60 groups (H3's 56-group fc2 input) 7 or 8.
+    if (stages >= kCrTeams) {
       switch (np) {
         case 1: return go(convrot_ring_kernel<1>);
         case 2: return go(convrot_ring_kernel<2>);
         case 3: return go(convrot_ring_kernel<3>);
         case 4: return go(convrot_ring_kernel<4>);
+        case 5: return go(convrot_ring_kernel<5>);
         default: break;
       }
     }
