@@ -133,14 +133,6 @@ __device__ __forceinline__ uint32_t gelu_lookup(uint32_t hb, const uint16_t* tab
   return bf16_bits(gelu_tanh_exact(__uint_as_float(hb << 16)));
 }
 
-// SiLU by the same table layout (kEpiSwiGLU fills it with silu_exact); inputs
-// outside it read the device-wide table of every bf16 input.
-__device__ __forceinline__ uint32_t silu_lookup(uint32_t hb, const uint16_t* tab) {
-  const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
-  if (rel < kGeluNE) return tab[(hb >> 15) * (kGeluNE * 128) + rel * 128 + (hb & 0x7Fu)];
-  return silu_bf16_bits(hb);
-}
-
 // GELU of 16 packed bf16 pairs, in place.
 __device__ __forceinline__ void gelu_pairs(uint32_t (&ob)[16], const uint16_t* gtab) {
   bool miss = false;
@@ -421,10 +413,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
       gelu_tab[i] = (uint16_t)bf16_bits(gelu_tanh_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
   }
-  if constexpr (EPI == kEpiSwiGLU) {  // SiLU of |x| in [2^-16, 8), both signs
-    for (int i = threadIdx.x; i < kGeluEntries; i += NUM_THREADS)
-      gelu_tab[i] = (uint16_t)bf16_bits(silu_exact(__uint_as_float(gelu_table_bits((uint32_t)i) << 16)));
-  }
   tc_fence_before();
   __syncthreads();
   if constexpr (CG == 2) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
@@ -651,7 +639,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 u = bf16_bits(__fadd_rn(__uint_as_float(u << 16), buv[e]));
               }
               // bf16(bf16(silu(g)) * u): the product of two bf16 values is exact in fp32
-              hb[e] = bf16_bits(__fmul_rn(__uint_as_float(silu_lookup(g, gelu_tab) << 16), __uint_as_float(u << 16)));
+              hb[e] = bf16_bits(__fmul_rn(__uint_as_float(silu_bf16_fast(g) << 16), __uint_as_float(u << 16)));
             }
             ob[2 * q] = hb[0] | (hb[1] << 16);
             ob[2 * q + 1] = hb[2] | (hb[3] << 16);

@@ -79,7 +79,7 @@ __device__ __forceinline__ uint4 load_act_vec(const __nv_bfloat16* xr, int64_t k
 // One activated value (scalar paths).
 __device__ __forceinline__ float act_value(const __nv_bfloat16* xr, int64_t k, int64_t i, int act) {
   if (act == H3B200_ACT_SWIGLU) {
-    const float s = __uint_as_float(silu_bf16_bits(__bfloat16_as_ushort(xr[i])) << 16);
+    const float s = __uint_as_float(silu_bf16_fast(__bfloat16_as_ushort(xr[i])) << 16);
     return bf16_round(__fmul_rn(s, __bfloat162float(xr[k + i])));
   }
   return act_apply(__bfloat162float(xr[i]), act);
