@@ -97,3 +97,27 @@ def test_contract_errors():
         h3b200.int8_linear(x, torch.zeros(8, 32, dtype=torch.int8, device="cuda"), torch.ones(8, device="cuda"))
     with pytest.raises(ValueError, match="scalar or per-output-channel"):
         h3b200.int8_linear(x, torch.zeros(8, 64, dtype=torch.int8, device="cuda"), torch.ones(3, device="cuda"))
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 512, 256), (600, 12288, 128)])
+def test_gelu_absmax_epilogue_outside_the_table(m, n, k):
+    """The fc1 epilogue (dequant -> tanh-GELU -> bf16, row absmax) on rows whose values fall
+    outside the shared-memory table: zero rows, a tiny row scale (|x| < 2^-16), a large one
+    (|x| >= 8, both signs), beside ordinary rows; single CTAs and CTA pairs. Output bits and
+    row absmax equal the oracle's."""
+    gen = torch.Generator().manual_seed(m + n + k)
+    a = rand_i8((m, k), gen)
+    a[::7] = 0                                                  # acc = 0: gelu(+0) = +0
+    w = rand_i8((n, k), gen)
+    xs = torch.full((m,), 1e-4, dtype=torch.float32)
+    xs[1::5] = 1e-9                                            # |x| < 2^-16: 0.5 x
+    xs[2::5] = 1.0                                             # |x| >= 8: x or -0
+    ws = (torch.rand(n, generator=gen) * 1e-3 + 1e-4).to(torch.float32)
+    amax = torch.zeros(m, dtype=torch.float32, device="cuda")
+    out = h3b200.ops.int8_gemm_fused(a.cuda(), w.cuda(), h3b200.ops.EPI_GELU_ABSMAX, xs.cuda(), ws.cuda(),
+                                     row_absmax=amax)
+    acc = O.int8_matmul_accumulate(np_(a), np_(w))
+    ref = O.gelu_tanh_bf16(O.dequant_epilogue(acc, np_(xs), np_(ws)))
+    np.testing.assert_array_equal(t2u(out), ref)
+    np.testing.assert_array_equal(np_(amax), np.abs(O.bf16_to_f32(ref)).max(axis=1))
+    assert h3b200.device_status(0) == 0

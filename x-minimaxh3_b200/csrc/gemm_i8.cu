@@ -108,8 +108,9 @@ constexpr bool is_corr_epi() {
 // reference, verified on all bf16 inputs) for |x| in [2^-16, 8) and both signs
 // (2 x 19 binades x 128 mantissas). The lookup itself is branch-free (the
 // index is clamped into the table); a lane whose chunk holds an input outside
-// that range (rare: zero, tiny, huge, non-finite) recomputes the chunk with
-// gelu_tanh_exact.
+// that range (zero, |x| < 2^-16 or >= 8, non-finite) recomputes the chunk
+// through gelu_lookup, whose closed forms leave only subnormal and non-finite
+// inputs to gelu_tanh_exact.
 constexpr uint32_t kGeluE0 = 111;   // exponent field of 2^-16
 constexpr uint32_t kGeluNE = 19;    // binades 2^-16 .. 2^2
 constexpr int kGeluEntries = 2 * kGeluNE * 128;
@@ -120,27 +121,41 @@ __device__ __forceinline__ uint32_t gelu_table_bits(uint32_t i) {
   return (sgn << 15) | ((kGeluE0 + rem / 128) << 7) | (rem & 127u);
 }
 
-// Table lookup; sets `miss` when hb is outside the table's range.
-__device__ __forceinline__ uint32_t gelu_lookup_fast(uint32_t hb, const uint16_t* tab, bool& miss) {
-  const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
-  miss |= rel >= kGeluNE;
-  return tab[(hb >> 15) * (kGeluNE * 128) + min(rel, kGeluNE - 1) * 128 + (hb & 0x7Fu)];
+constexpr uint32_t kGeluHalf = kGeluNE * 128;  // entries per sign
+constexpr uint32_t kGeluBase = kGeluE0 << 7;   // |x| bits of 2^-16
+
+// Table lookup. Inside the table the entry of |x| is its bits minus those of 2^-16
+// (binade and mantissa are consecutive in the encoding); `span` collects that
+// unclamped offset, so span >= kGeluHalf afterwards flags an input outside it.
+__device__ __forceinline__ uint32_t gelu_lookup_fast(uint32_t hb, const uint16_t* tab, uint32_t& span) {
+  const uint32_t u = (hb & 0x7FFFu) - kGeluBase;  // wraps below 2^-16
+  span = max(span, u);
+  return tab[((hb >> 15) & 1u) * kGeluHalf + min(u, kGeluHalf - 1u)];
 }
 
+// The exact value of any bf16 input. Outside the table the reference's result has
+// a closed form (checked against its all-inputs fixture): +-0 -> +-0; 2^-125 <= |x|
+// < 2^-16 -> 0.5 x exactly (the tanh term is below half an ulp); |x| >= 8 -> x or -0
+// (its tanh is exactly +-1). Only subnormal and non-finite inputs are evaluated.
 __device__ __forceinline__ uint32_t gelu_lookup(uint32_t hb, const uint16_t* tab) {
-  const uint32_t rel = ((hb >> 7) & 0xFFu) - kGeluE0;
-  if (rel < kGeluNE) return tab[(hb >> 15) * (kGeluNE * 128) + rel * 128 + (hb & 0x7Fu)];
+  hb &= 0xFFFFu;
+  const uint32_t u = (hb & 0x7FFFu) - kGeluBase;
+  if (u < kGeluHalf) return tab[(hb >> 15) * kGeluHalf + u];
+  const uint32_t e = (hb >> 7) & 0xFFu;
+  if ((hb & 0x7FFFu) == 0u) return hb;
+  if (e >= 2u && e < kGeluE0) return hb - 0x80u;
+  if (e >= kGeluE0 + kGeluNE && e < 255u) return (hb & 0x8000u) ? 0x8000u : hb;
   return bf16_bits(gelu_tanh_exact(__uint_as_float(hb << 16)));
 }
 
 // GELU of 16 packed bf16 pairs, in place.
 __device__ __forceinline__ void gelu_pairs(uint32_t (&ob)[16], const uint16_t* gtab) {
-  bool miss = false;
+  uint32_t span = 0u;
   uint32_t g[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j)
-    g[j] = gelu_lookup_fast(ob[j] & 0xFFFFu, gtab, miss) | (gelu_lookup_fast(ob[j] >> 16, gtab, miss) << 16);
-  if (miss) {
+    g[j] = gelu_lookup_fast(ob[j] & 0xFFFFu, gtab, span) | (gelu_lookup_fast(ob[j] >> 16, gtab, span) << 16);
+  if (span >= kGeluHalf) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) g[j] = gelu_lookup(ob[j] & 0xFFFFu, gtab) | (gelu_lookup(ob[j] >> 16, gtab) << 16);
   }
@@ -166,37 +181,49 @@ __device__ __forceinline__ void dequant_to_f32(uint32_t (&r)[32], float xs, cons
   }
 }
 
+// Two dequantized values bf16(acc * (xs * ws)) as a packed bf16 pair (f32x2 products,
+// the same roundings as dequant_bits).
+__device__ __forceinline__ uint32_t dequant_pair(uint32_t a0, uint32_t a1, float xs, float w0, float w1) {
+  uint64_t w, a;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(w) : "f"(w0), "f"(w1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(__int2float_rn((int)a0)), "f"(__int2float_rn((int)a1)));
+  uint32_t lo, hi;
+  f2_bits(f2_mul(a, f2_mul(f2_dup(xs), w)), lo, hi);
+  return bf16x2_from_bits(lo, hi);
+}
+
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // fc1 chunk: out bits (packed pairs) = gelu(bf16(acc * (xs * ws))); chunk absmax bits.
 __device__ __forceinline__ void gelu_chunk(const uint32_t (&r)[32], float xs, const float* ws_s, const uint16_t* gtab,
                                            uint32_t (&ob)[16], uint32_t& amax_bits) {
-  bool miss = false;
-  uint32_t cmax = 0u;
+  uint32_t span = 0u, cmax = 0u;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
-    const uint32_t g0 = gelu_lookup_fast(dequant_bits(r[4 * q + 0], xs, w4.x), gtab, miss);
-    const uint32_t g1 = gelu_lookup_fast(dequant_bits(r[4 * q + 1], xs, w4.y), gtab, miss);
-    const uint32_t g2 = gelu_lookup_fast(dequant_bits(r[4 * q + 2], xs, w4.z), gtab, miss);
-    const uint32_t g3 = gelu_lookup_fast(dequant_bits(r[4 * q + 3], xs, w4.w), gtab, miss);
-    ob[2 * q] = g0 | (g1 << 16);
-    ob[2 * q + 1] = g2 | (g3 << 16);
-    cmax = max(cmax, max(max(g0 & 0x7FFFu, g1 & 0x7FFFu), max(g2 & 0x7FFFu, g3 & 0x7FFFu)));
+    const uint32_t h01 = dequant_pair(r[4 * q + 0], r[4 * q + 1], xs, w4.x, w4.y);
+    const uint32_t h23 = dequant_pair(r[4 * q + 2], r[4 * q + 3], xs, w4.z, w4.w);
+    ob[2 * q] = gelu_lookup_fast(h01, gtab, span) | (gelu_lookup_fast(h01 >> 16, gtab, span) << 16);
+    ob[2 * q + 1] = gelu_lookup_fast(h23, gtab, span) | (gelu_lookup_fast(h23 >> 16, gtab, span) << 16);
+    cmax = max_u16x2(cmax, max_u16x2(ob[2 * q] & 0x7FFF7FFFu, ob[2 * q + 1] & 0x7FFF7FFFu));
   }
-  if (miss) {
+  if (span >= kGeluHalf) {  // an input outside the table: the exact path for the chunk
     cmax = 0u;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const float4 w4 = *reinterpret_cast<const float4*>(ws_s + 4 * q);
-      const uint32_t g0 = gelu_lookup(dequant_bits(r[4 * q + 0], xs, w4.x), gtab);
-      const uint32_t g1 = gelu_lookup(dequant_bits(r[4 * q + 1], xs, w4.y), gtab);
-      const uint32_t g2 = gelu_lookup(dequant_bits(r[4 * q + 2], xs, w4.z), gtab);
-      const uint32_t g3 = gelu_lookup(dequant_bits(r[4 * q + 3], xs, w4.w), gtab);
-      ob[2 * q] = g0 | (g1 << 16);
-      ob[2 * q + 1] = g2 | (g3 << 16);
-      cmax = max(cmax, max(max(g0 & 0x7FFFu, g1 & 0x7FFFu), max(g2 & 0x7FFFu, g3 & 0x7FFFu)));
+      const uint32_t h01 = dequant_pair(r[4 * q + 0], r[4 * q + 1], xs, w4.x, w4.y);
+      const uint32_t h23 = dequant_pair(r[4 * q + 2], r[4 * q + 3], xs, w4.z, w4.w);
+      ob[2 * q] = gelu_lookup(h01, gtab) | (gelu_lookup(h01 >> 16, gtab) << 16);
+      ob[2 * q + 1] = gelu_lookup(h23, gtab) | (gelu_lookup(h23 >> 16, gtab) << 16);
+      cmax = max_u16x2(cmax, max_u16x2(ob[2 * q] & 0x7FFF7FFFu, ob[2 * q + 1] & 0x7FFF7FFFu));
     }
   }
-  amax_bits = max(amax_bits, cmax);
+  amax_bits = max(amax_bits, max(cmax & 0xFFFFu, cmax >> 16));
 }
 
 // int32 accumulators of one 32-column chunk of one row, 128-bit stores.
