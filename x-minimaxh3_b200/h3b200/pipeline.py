@@ -8,6 +8,13 @@ residual) and the device-to-host copy of chunk i-1 run at the same time. The
 MLP is per-token, so the chunked result is bit-identical to one call over all
 tokens. Device staging buffers are allocated once per (device, d, chunk) and
 reused.
+
+The copies in dominate (x and residual: 4 bytes per element against 2 out), so
+the call lasts about as long as the host-to-device stream plus whatever follows
+its last copy: the last chunk's MLP and its copy out, which nothing overlaps.
+The tokens after the last full chunk are therefore cut into halving pieces
+(4,088 -> 2,048 + 1,024 + 512 + 504), which shrinks that tail to the smallest
+piece's.
 """
 
 from __future__ import annotations
@@ -44,6 +51,23 @@ def _staging(device: torch.device, d: int, chunk: int, slots: int) -> _Staging:
     return st
 
 
+def _chunk_sizes(m: int, chunk: int, min_piece: int = 256) -> list[int]:
+    """Full chunks, then the remainder (at most one chunk) in halving pieces of at
+    least ``min_piece`` tokens (multiples of 16)."""
+    sizes = []
+    rest = m
+    while rest > chunk:
+        sizes.append(chunk)
+        rest -= chunk
+    while rest > 2 * min_piece:
+        piece = -(-(rest // 2) // 16) * 16
+        sizes.append(piece)
+        rest -= piece
+    if rest > 0:
+        sizes.append(rest)
+    return sizes
+
+
 def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Tensor, s1: torch.Tensor,
                          w2q: torch.Tensor, s2: torch.Tensor, gate: torch.Tensor, out: torch.Tensor | None = None,
                          chunk_tokens: int = 4096, slots: int = 3, synchronize: bool = True) -> torch.Tensor:
@@ -74,9 +98,9 @@ def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torc
     cur = torch.cuda.current_stream(dev)
     for s in (st.h2d, st.comp, st.d2h):
         s.wait_stream(cur)
-    for i, lo in enumerate(range(0, m, chunk)):
-        hi = min(m, lo + chunk)
-        n = hi - lo
+    lo = 0
+    for i, n in enumerate(_chunk_sizes(m, chunk)):
+        hi = lo + n
         k = i % slots
         xb, rb = st.x[k][:n], st.r[k][:n]
         with torch.cuda.stream(st.h2d):
@@ -96,6 +120,7 @@ def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torc
             out[lo:hi].copy_(rb, non_blocking=True)
             st.free[k].record(st.d2h)
         st.used[k] = True
+        lo = hi
     cur.wait_stream(st.d2h)
     if synchronize:
         cur.synchronize()
