@@ -451,7 +451,8 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
 int64_t h3b200_fused_gated_mlp_swiglu_workspace_bytes(int64_t chunk_tokens, int64_t d, int64_t ffn) {
   if (chunk_tokens <= 0 || d <= 0 || ffn <= 0) return 0;
   const int64_t c = chunk_tokens;
-  return round_up(c * d, 256) + round_up(c * 4, 256) * 2 + round_up(c * 2 * ffn * 2, 256) + round_up(c * ffn, 256) +
+  // xq, xs, h = silu(gate) * up (bf16 [c, ffn], written by fc1's epilogue), q2, xs2
+  return round_up(c * d, 256) + round_up(c * 4, 256) * 2 + round_up(c * ffn * 2, 256) + round_up(c * ffn, 256) +
          1024;
 }
 
@@ -494,7 +495,7 @@ int run_swiglu_mlp(const SwiGLUMlp& a, void* work, int64_t work_bytes, cudaStrea
   Carver c{static_cast<uint8_t*>(work), work_bytes};
   int8_t* xq = static_cast<int8_t*>(c.take(chunk * d));
   float* xs = static_cast<float*>(c.take(chunk * 4));
-  void* hbuf = c.take(chunk * 2 * ffn * 2);
+  void* hbuf = c.take(chunk * ffn * 2);
   int8_t* q2 = static_cast<int8_t*>(c.take(chunk * ffn));
   float* xs2 = static_cast<float*>(c.take(chunk * 4));
   if (!c.ok) return fail(H3B200_ERR_INVALID, "%s: workspace too small", who);
