@@ -141,6 +141,196 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
+# profiling cases: one kernel (or one fused call) of the hot path on a chosen
+# token count, for ncu captures.
+#
+#     python bench.py --case CASE [CASE ...] [--tokens M] [--iters N] [--time]
+#
+# CASE is one of ``quantize`` (fc1 input quantizer, K = 3072), ``fc1`` (INT8 GEMM
+# with the GELU + row-absmax epilogue; ``fc1_bf16`` / ``fc1_i32``: the same GEMM with
+# the plain dequant or the int32 epilogue), ``requant`` (fc2 input quantizer with a
+# given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
+# ``mlp`` (the whole fused MLP call), ``mlp_w4a8`` (the config-2 W4A8 MLP call), ``mlp_swiglu``
+# (the H3 SwiGLU MLP at d 5,376 / ffn 14,336, ConvRot fc1 and fc2, 8,192-token chunks),
+# ``mlp_swiglu_w4`` (the same MLP on W4A8 weights in the H3 release format: group 16,
+# fp8-e4m3 scales, codebook; both weights decoded per call), ``decode_w4`` (that
+# format's int4 -> int8 decode of the fc1 weight, 28,672 x 5,376), ``qknorm_h3``
+# (single-side QK-norm + partial RoPE of H3 K, 56 heads, rot 96, bf16 table, into an
+# HND buffer), ``qkv_h3`` (the H3 Q/K/V projection of M tokens, hidden 5,376, with
+# QK-norm + RoPE into HND buffers, from a ConvRot-quantized activation),
+# ``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
+# Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
+# norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
+# runs the kernels it needs to build its inputs, then launches the kernel under
+# study ``--iters`` times, so a profiler can skip the set-up launches by kernel
+# name; ``--time`` also reports the mean CUDA-event time of those launches. The
+# process exits non-zero if a kernel reports an error.
+# ---------------------------------------------------------------------------
+
+CASES = ["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp", "mlp_w4a8", "mlp_swiglu",
+         "mlp_swiglu_w4", "decode_w4", "qknorm_h3", "qkv_h3", "convrot", "convrot_x", "norm_rope"]
+
+
+def _case_mlp_inputs(m: int, dev):
+    import torch
+
+    import h3b200
+
+    g = torch.Generator(device=dev).manual_seed(2)
+    w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(D_MODEL, D_FFN, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wt = h3b200.W8A8MLPWeights.from_float(w1, w2)
+    x = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+    gate = torch.randn(D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+    res = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+    return wt, x, gate, res
+
+
+def _case_case_timed(fn, iters: int, report: bool):
+    import torch
+
+    if not report:
+        for _ in range(iters):
+            fn()
+        return None
+    fn()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def run_case(case: str, m: int, iters: int, report: bool = False):
+    """Run one profiling case (see CASES); returns the mean CUDA-event ms per launch with ``report``."""
+    import torch
+
+    import h3b200
+    from h3b200 import ops
+    from h3b200.rope import rope_grid_table
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    h3b200.library()
+    if case == "norm_rope":
+        g = torch.Generator(device=dev).manual_seed(4)
+        q = torch.randn(m, 24, 128, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.randn(m, 24, 128, generator=g, device=dev).to(torch.bfloat16)
+        sh = (torch.randn(3072, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        sc = (torch.randn(3072, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        wq = (1 + 0.02 * torch.randn(3072, generator=g, device=dev)).to(torch.bfloat16)
+        wk = (1 + 0.02 * torch.randn(3072, generator=g, device=dev)).to(torch.bfloat16)
+        grid_t = max(1, (m + 39 * 40 - 1) // (39 * 40))
+        table = rope_grid_table((grid_t, 39, 40), device=dev)[:m].contiguous()
+        qo, ko = torch.empty_like(q), torch.empty_like(k)
+        ms = _case_timed(lambda: ops.adaln_rms_rope_(q, k, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko),
+                    iters, report)
+    elif case in ("convrot", "convrot_x"):
+        g = torch.Generator(device=dev).manual_seed(6)
+        a = torch.randn(m, D_FFN if case == "convrot" else D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+        ms = _case_timed(lambda: ops.quantize_int8_rowwise_convrot(a, 256), iters, report)
+    elif case == "mlp_swiglu":
+        # H3 SwiGLU MLP at the H3 dims: d 5,376, fc1 out 28,672 ([gate | up]), ffn 14,336
+        g = torch.Generator(device=dev).manual_seed(8)
+        d, ffn = 5376, 14336
+        w1 = (torch.randn(2 * ffn, d, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn(d, ffn, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wt = h3b200.SwiGLUMLPWeights.from_float(w1, w2)
+        del w1, w2
+        x = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+        gate = torch.randn(d, generator=g, device=dev).to(torch.bfloat16)
+        res = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(res)
+        ms = _case_timed(lambda: h3b200.fused_gated_mlp_swiglu(res, x, wt, gate, out=out), iters, report)
+    elif case in ("mlp_swiglu_w4", "decode_w4"):
+        g = torch.Generator(device=dev).manual_seed(9)
+        d, ffn = 5376, 14336
+        w1 = (torch.randn(2 * ffn, d, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn(d, ffn, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w4 = h3b200.W4A8SwiGLUMLPWeights.from_float(w1, w2)
+        del w1, w2
+        if case == "decode_w4":
+            ms = _case_timed(lambda: ops.dequant_int4_grouped_to_int8(w4.q1, w4.s_rel1, 16, w4.codebook1), iters, report)
+        else:
+            x = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+            gate = torch.randn(d, generator=g, device=dev).to(torch.bfloat16)
+            res = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty_like(res)
+            ms = _case_timed(lambda: h3b200.fused_gated_mlp_swiglu_w4a8(res, x, w4, gate, out=out), iters, report)
+    elif case in ("qknorm_h3", "qkv_h3"):
+        g = torch.Generator(device=dev).manual_seed(10)
+        heads, d = 56, 5376
+        freqs = torch.randn(1, m, 1, 48, 2, 2, generator=g, device=dev).to(torch.bfloat16)
+        kn = (1 + 0.02 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+        if case == "qknorm_h3":
+            k = torch.randn(m, heads, 128, generator=g, device=dev).to(torch.bfloat16)
+            k_hnd = torch.empty(heads, m, 128, dtype=torch.bfloat16, device=dev).permute(1, 0, 2)
+            ms = _case_timed(lambda: ops.single_qknorm_rope_to_hnd(k, k_hnd, weight=kn, frequencies=freqs, eps=1e-5),
+                        iters, report)
+        else:
+            w = (torch.randn(3 * heads * 128, d, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            wq_, ws = h3b200.quantize_int8_convrot_weight(w)
+            del w
+            hidden = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+            xq, xs = ops.quantize_int8_rowwise_convrot(hidden, 256)
+            outs = [torch.empty(heads, m, 128, dtype=torch.bfloat16, device=dev).permute(1, 0, 2) for _ in range(3)]
+            work = torch.empty(int(h3b200.library().h3b200_qkv_qknorm_rope_workspace_bytes(m, heads, 128, 0, 3)),
+                               dtype=torch.uint8, device=dev)
+            ms = _case_timed(lambda: ops.qkv_qknorm_rope(xq, xs, wq_, ws, None, heads, kn, kn, freqs, 1e-5, "qkv",
+                                                    *outs, workspace=work), iters, report)
+    elif case == "mlp_w4a8":
+        g = torch.Generator(device=dev).manual_seed(3)
+        w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn(D_MODEL, D_FFN, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        w4 = h3b200.W4A8MLPWeights.from_float(w1, w2, 128)
+        x = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+        gate = torch.randn(D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+        res = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(res)
+        ms = _case_timed(lambda: h3b200.fused_gated_mlp_w4a8(res, x, w4, gate, out=out), iters, report)
+    else:
+        wt, x, gate, res = _case_mlp_inputs(m, dev)
+        xq, xs = ops.quantize_int8_rowwise(x)
+        amax = torch.zeros(m, dtype=torch.float32, device=dev)
+        act = torch.empty(m, D_FFN, dtype=torch.bfloat16, device=dev)
+        out = torch.empty_like(res)
+
+        def fc1():
+            ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_GELU_ABSMAX, xs, wt.s1, out=act, row_absmax=amax)
+
+        if case == "quantize":
+            ms = _case_timed(lambda: ops.quantize_int8_rowwise(x), iters, report)
+        elif case == "fc1":
+            ms = _case_timed(fc1, iters, report)   # row absmax only grows: re-running on the same inputs is idempotent
+        elif case == "fc1_bf16":
+            ms = _case_timed(lambda: ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_BF16, xs, wt.s1, out=act), iters, report)
+        elif case == "fc1_i32":
+            acc = torch.empty(m, D_FFN, dtype=torch.int32, device=dev)
+            ms = _case_timed(lambda: ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_I32, out=acc), iters, report)
+        elif case in ("requant", "fc2"):
+            fc1()
+            if case == "requant":
+                ms = _case_timed(lambda: ops.quantize_int8_rowwise_absmax(act, amax), iters, report)
+            else:
+                q2, xs2 = ops.quantize_int8_rowwise_absmax(act, amax)
+                ms = _case_timed(lambda: ops.int8_gemm_fused(q2, wt.w2q, ops.EPI_GATED_RESIDUAL, xs2, wt.s2, gate=gate,
+                                                        residual=res, out=out), iters, report)
+        elif case == "mlp":
+            ms = _case_timed(lambda: h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=out), iters,
+                        report)
+        else:
+            raise SystemExit(f"unknown case {case!r}")
+    torch.cuda.synchronize()
+    st = h3b200.device_status(0)
+    if st != 0:
+        raise SystemExit(f"device status {st:#x}")
+    return ms
+
+
+# ---------------------------------------------------------------------------
 # reference arm / CPU baseline
 # ---------------------------------------------------------------------------
 
@@ -161,8 +351,30 @@ def _cpu_mlp_inputs(rows, seed=2):
     return x, w1q, s1.reshape(-1), w2q, s2.reshape(-1), gate, res
 
 
-def cpu_mlp_tokens_per_s(rows: int, repeats: int = 3):
-    """Median tokens/s of the torch-CPU port of the reference eager MLP on `rows` tokens."""
+CPU_ROWS = 2048          # config-1 tokens per CPU sample (per-token math, so a row sample is representative)
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_protocol() -> dict:
+    """Host description recorded beside every CPU number."""
+    import torch
+
+    return {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "cpu_model": cpu_model()}
+
+
+def cpu_mlp_tokens_per_s(rows: int = CPU_ROWS, repeats: int = 3):
+    """Median tokens/s of the torch-CPU port of the reference eager MLP on `rows` tokens
+    (1 warm-up, median of `repeats`), all host threads."""
     import torch
 
     from oracle import torch_port as P
@@ -186,25 +398,22 @@ def run_reference(args, rank, world):
     from oracle import torch_port as P
 
     torch.set_num_threads(os.cpu_count() or 1)
-    # size the per-step token sample so the whole run stays within ~2 minutes
-    probe_rows = 64
-    x, w1q, s1, w2q, s2, gate, res = _cpu_mlp_inputs(probe_rows)
-    P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
-    t0 = time.perf_counter()
-    P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
-    per_row = (time.perf_counter() - t0) / probe_rows
-    budget = 100.0 / max(1, args.steps + args.warmup)
-    rows = int(max(16, min(2048, budget / max(per_row, 1e-9))))
+    # the same sample as our arm's cpu_baseline: 2,048 config-1 tokens per step (about 0.15 s of
+    # CPU work on a 16-thread host, so 200 steps stay within a minute or two)
+    rows = CPU_ROWS
     x, w1q, s1, w2q, s2, gate, res = _cpu_mlp_inputs(rows)
-    for _ in range(args.warmup):
+    for _ in range(max(1, args.warmup)):
         P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
-    t0 = time.perf_counter()
+    per_step = []
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         P.w8a8_gelu_mlp(x, w1q, s1, w2q, s2, gate, res)
-    dt = time.perf_counter() - t0
+        per_step.append(time.perf_counter() - t0)
+    dt = sum(per_step)
     value = rows * args.steps / dt
     cores = torch.get_num_threads()
-    sample = f"{rows} of {M_TOKENS} config-1 tokens per step (per-token math; torch-CPU port of the eager path)"
+    sample = (f"{rows} of {M_TOKENS} config-1 tokens per step (per-token math; torch-CPU port of the eager path); "
+              f"median step {rows / statistics.median(per_step):.0f} tokens/s")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
@@ -212,7 +421,8 @@ def run_reference(args, rank, world):
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
         "config": {"workload": "cfg1 fused W8A8 tanh-GELU DiT MLP, d=3072 ffn=12288", "tokens_per_step": rows,
                    "parallelism": "host cores"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample,
+                         **cpu_protocol()},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "int8_tops": value * OPS_PER_TOKEN / 1e12,
     }
@@ -291,9 +501,27 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    status = h3b200.device_status(local_rank)
     ms_per_step = ms / args.steps
     value = world * M_TOKENS * args.steps / (ms / 1e3)
+
+    # ---- the same step over a timed region of at least 1.5 s (steady state under the power cap) ----
+    sus_steps = max(args.steps, int(1500.0 / max(ms_per_step, 1e-3)) + 1)
+    with ClockSampler(local_rank, period_ms=100) as clk_sus:
+        ev0.record(stream)
+        clk_sus.mark_start()
+        for _ in range(sus_steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+        clk_sus.mark_end()
+    sus_ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([sus_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sus_ms = float(t.item())
+    sustained = {"steps": sus_steps, "ms_per_step": sus_ms / sus_steps,
+                 "tokens_per_s": world * M_TOKENS * sus_steps / (sus_ms / 1e3), "clocks": clk_sus.summary()}
+    status = h3b200.device_status(local_rank)
 
     # ---- per-kernel timing of the same step (events around each launch) ----
     xq = torch.empty(M_TOKENS, D_MODEL, dtype=torch.int8, device=dev)
@@ -526,10 +754,11 @@ def run_ours(args, rank, world, local_rank):
     # ---- CPU baseline (rank 0, N = 1 only) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = 512
-        v, cores = cpu_mlp_tokens_per_s(rows)
+        v, cores = cpu_mlp_tokens_per_s(CPU_ROWS)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{rows} config-1 tokens, median of 3 after 1 warm-up (torch-CPU port of the eager path)"}
+               "sample": f"{CPU_ROWS} config-1 tokens, median of 3 after 1 warm-up (torch-CPU port of the eager "
+                         "path; the reference arm runs the same 2,048-token sample per step)",
+               **cpu_protocol()}
 
     if rank == 0:
         clocks = clk.summary()
@@ -549,6 +778,7 @@ def run_ours(args, rank, world, local_rank):
                                         "tcgen05 kind::i8 issues at twice the kind::f16 rate",
                          "traffic": traffic.get("fc1_gemm_gelu_absmax")},
             "components": {
+                "sustained_step": sustained,
                 **{k: {"ms": v} for k, v in comp_ms.items()},
                 "fc2_gemm_gated_residual_tops": fc2_ops / (comp_ms["fc2_gemm_gated_residual"] * 1e-3) / 1e12,
                 "cublaslt_int8_8192_tops": lib_int8_tops,
@@ -590,6 +820,11 @@ def run_ours(args, rank, world, local_rank):
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    final = h3b200.device_status(local_rank)
+    if status or final:
+        print(f"bench: device status {max(status, final):#x}: a bounded device wait expired; numbers are not valid",
+              file=sys.stderr, flush=True)
+        return 3
     return 0
 
 
@@ -600,7 +835,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", nargs="+", choices=CASES, help="run profiling cases instead of the benchmark")
+    ap.add_argument("--tokens", type=int, default=8192, help="tokens per profiling case")
+    ap.add_argument("--iters", type=int, default=3, help="launches of the studied kernel per profiling case")
+    ap.add_argument("--time", action="store_true", help="report the mean CUDA-event ms per launch of each case")
     args = ap.parse_args()
+    if args.case:
+        for case in args.case:
+            ms = run_case(case, args.tokens, args.iters, args.time)
+            extra = f" mean {ms:.4f} ms per launch" if ms is not None else ""
+            print(f"profile case {case} tokens={args.tokens} iters={args.iters}: ok{extra}", flush=True)
+        return 0
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -12,6 +12,14 @@
  *  - Every entry point returns an int status (H3B200_OK on success). A
  *    non-zero status leaves a message in h3b200_last_error(). No C++
  *    exception crosses this boundary and nothing falls back to another path.
+ *  - Every wait inside a kernel is bounded. A wait that expires records a code
+ *    in the device status word and in a mapped host copy of it; from then on
+ *    every launching entry point on that device returns H3B200_ERR_DEVICE
+ *    without launching, until h3b200_device_status(device, &s, 1) clears it.
+ *    Errors are reported asynchronously, like CUDA's: calls queued before the
+ *    failure became visible return H3B200_OK but their outputs are not valid.
+ *    The host copy is set up by the first call on each device that is not
+ *    made under stream capture.
  *  - Activation codes follow comfy_kitchen backends/cuda/input_act_codes.h:13
  *    (0 none, 1 gelu_tanh, 2 swiglu); dtype codes follow eager/quantization.py:34-40
  *    (0 fp32, 1 fp16, 2 bf16).
@@ -38,7 +46,7 @@ enum {
   H3B200_ERR_INVALID = 1,     /* shape / stride / alignment / code outside the contract */
   H3B200_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
   H3B200_ERR_LAUNCH = 3,      /* CUDA runtime error at launch */
-  H3B200_ERR_DEVICE = 4       /* a kernel recorded a device-side failure (bounded wait expired) */
+  H3B200_ERR_DEVICE = 4       /* a kernel recorded a device-side failure (bounded wait expired); refused until cleared */
 };
 
 enum { H3B200_ACT_NONE = 0, H3B200_ACT_GELU_TANH = 1, H3B200_ACT_SWIGLU = 2 };
@@ -51,6 +59,15 @@ H3B200_API const char* h3b200_last_error(void);
 /* Reads (and optionally clears) the device status word of `device`, where
  * kernels record bounded-wait timeouts. Synchronises that device. */
 H3B200_API int h3b200_device_status(int device, unsigned int* status, int clear);
+/* Reads the mapped host copy of the status word of `device` without
+ * synchronising (0 until a failure has become visible to the host). No
+ * counterpart in the reference, whose kernels have no bounded waits. */
+H3B200_API int h3b200_device_status_nowait(int device, unsigned int* status);
+/* Test hook: launches one thread that waits, with limit timeout_ns (1 us to
+ * 1 s), on a barrier nothing arrives at, so the wait expires and the kernel
+ * records status 0x7E57 and returns. Exercises the failure reporting above
+ * without a fault or a hang. No counterpart in the reference. */
+H3B200_API int h3b200_selftest_expire_wait(int64_t timeout_ns, h3b200_stream_t stream);
 
 /*
  * Elementwise pre-quantization activation on bf16 (y may alias x).
@@ -168,9 +185,13 @@ H3B200_API int h3b200_int8_linear(const void* x, int64_t ldx, const int8_t* w, c
  * loading the library holds until exit, and no memory is allocated.
  * Limit: round_up(m * k, 256) + 4 * m must fit in that array (e.g. m <= 2600 at
  * k = 3072); larger calls are rejected with H3B200_ERR_INVALID. The first call
- * on a device looks up the array's device address with that device current;
- * make that first call before any stream capture. All calls share the array:
- * calls that overlap on the GPU race on it. Same arithmetic and result as
+ * on a device looks up the array's device address with that device current and
+ * fills the device's tanh-GELU table (synchronising `stream` once), whatever
+ * `act` it asks for; make that first call before any stream capture. All calls
+ * share the array: calls that overlap on the GPU race on it. The cached address
+ * belongs to the device's current context: after cudaDeviceReset this library's
+ * per-device state (this address, its activation tables, the status mirror) is
+ * stale, so do not call it again in that process. Same arithmetic and result as
  * h3b200_int8_linear; the caller still passes x, w, scales, bias and out.
  */
 H3B200_API int64_t h3b200_int8_linear_noalloc_max_scratch_bytes(void);

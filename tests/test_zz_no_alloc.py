@@ -22,24 +22,26 @@ from h3b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
-def _linear_with_workspace(lib, x, w, ws, stream):
+def _linear_with_workspace(lib, x, w, ws, stream, bias=None, act=0):
     m, k = x.shape
     n = w.shape[0]
     out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     nbytes = int(lib.h3b200_int8_linear_workspace_bytes(m, k))
     work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
-    rc = lib.h3b200_int8_linear(x.data_ptr(), x.stride(0), w.data_ptr(), ws.data_ptr(), ws.numel(), None, 0,
-                                out.data_ptr(), m, n, k, work.data_ptr(), nbytes, stream)
+    rc = lib.h3b200_int8_linear(x.data_ptr(), x.stride(0), w.data_ptr(), ws.data_ptr(), ws.numel(),
+                                None if bias is None else bias.data_ptr(), act, out.data_ptr(), m, n, k,
+                                work.data_ptr(), nbytes, stream)
     assert rc == 0, lib.h3b200_last_error()
     return out
 
 
-def _linear_noalloc(lib, x, w, ws, stream):
+def _linear_noalloc(lib, x, w, ws, stream, bias=None, act=0):
     m, k = x.shape
     n = w.shape[0]
     out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
-    rc = lib.h3b200_int8_linear_noalloc(x.data_ptr(), x.stride(0), w.data_ptr(), ws.data_ptr(), ws.numel(), None,
-                                        0, out.data_ptr(), m, n, k, stream)
+    rc = lib.h3b200_int8_linear_noalloc(x.data_ptr(), x.stride(0), w.data_ptr(), ws.data_ptr(), ws.numel(),
+                                        None if bias is None else bias.data_ptr(), act, out.data_ptr(), m, n, k,
+                                        stream)
     assert rc == 0, lib.h3b200_last_error()
     return out
 
@@ -54,6 +56,22 @@ def test_noalloc_matches_workspace_entry_point_two_calls():
         x = torch.randn(rows, 3072, generator=gen).to(torch.bfloat16).cuda()
         ref = _linear_with_workspace(lib, x, w, ws, stream)
         got = _linear_noalloc(lib, x, w, ws, stream)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+def test_noalloc_gelu_input_and_bias_match_workspace_entry_point():
+    """tanh-GELU on the input and a bias in the epilogue, two calls in a row, bit for bit."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    gen = torch.Generator().manual_seed(78)
+    w = torch.randint(-127, 128, (512, 1024), generator=gen, dtype=torch.int16).to(torch.int8).cuda()
+    ws = (torch.rand(512, generator=gen) * 1e-3).cuda()
+    bias = (torch.randn(512, generator=gen) * 0.1).to(torch.bfloat16).cuda()
+    for rows in (1000, 64):
+        x = (torch.randn(rows, 1024, generator=gen) * 2).to(torch.bfloat16).cuda()
+        ref = _linear_with_workspace(lib, x, w, ws, stream, bias, _lib.ACT_GELU_TANH)
+        got = _linear_noalloc(lib, x, w, ws, stream, bias, _lib.ACT_GELU_TANH)
         torch.cuda.synchronize()
         assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
 

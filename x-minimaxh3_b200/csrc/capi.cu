@@ -4,7 +4,10 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <string.h>
+
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -51,6 +54,83 @@ struct Carver {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Host mirror of the device status word. A kernel whose bounded wait expires
+// records a code in g_status (device memory) and, through g_status_host, in one
+// word of mapped pinned host memory per device. Every launching entry point
+// reads that word first (no synchronisation) and refuses with
+// H3B200_ERR_DEVICE while it is set: outputs of kernels that ran after the
+// failure are not valid, and they must not be mistaken for results. The mirror
+// is set up by the first call on each device that is not under stream capture
+// (it writes a device symbol); h3b200_device_status(.., clear = 1) resets both.
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+std::mutex g_mirror_mu;
+unsigned int* g_mirror = nullptr;  // kMaxDevices words, cudaHostAllocMapped | Portable
+std::atomic<bool> g_mirror_ready[kMaxDevices];
+
+void status_mirror_setup(int dev, cudaStream_t stream) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return;
+  std::lock_guard<std::mutex> lock(g_mirror_mu);
+  if (g_mirror_ready[dev].load(std::memory_order_acquire)) return;
+  if (g_mirror == nullptr) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, kMaxDevices * sizeof(unsigned int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();
+      return;  // no mirror: failures still show in h3b200_device_status
+    }
+    memset(p, 0, kMaxDevices * sizeof(unsigned int));
+    g_mirror = static_cast<unsigned int*>(p);
+  }
+  void* dptr = nullptr;
+  if (cudaHostGetDevicePointer(&dptr, g_mirror + dev, 0) != cudaSuccess ||
+      cudaMemcpyToSymbol(h3::g_status_host, &dptr, sizeof(dptr)) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  g_mirror_ready[dev].store(true, std::memory_order_release);
+}
+
+unsigned int status_mirror_read(int dev) {
+  if (g_mirror == nullptr || !g_mirror_ready[dev].load(std::memory_order_acquire)) return 0u;
+  return *reinterpret_cast<volatile unsigned int*>(g_mirror + dev);
+}
+
+// First statement of every launching entry point.
+int status_guard(const char* what, h3b200_stream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return H3B200_OK;  // the launch itself reports the device error
+  }
+  if (!g_mirror_ready[dev].load(std::memory_order_acquire)) status_mirror_setup(dev, reinterpret_cast<cudaStream_t>(stream));
+  const unsigned int code = status_mirror_read(dev);
+  if (code != 0u)
+    return fail(H3B200_ERR_DEVICE,
+                "%s: refused: a bounded device wait on device %d expired earlier (status 0x%x); outputs of calls "
+                "since then are not valid; read and clear it with h3b200_device_status(device, &status, 1)",
+                what, dev, code);
+  return H3B200_OK;
+}
+
+#define H3_GUARD(what, stream)                                        \
+  do {                                                                \
+    if (const int rc_ = status_guard(what, stream)) return rc_;       \
+  } while (0)
+
+// Test-only: one thread waits on a shared-memory mbarrier that nothing arrives
+// at, with the given limit, so that the bounded wait expires and the kernel
+// records kErrSelftest and returns. No copy or MMA is in flight.
+constexpr unsigned kErrSelftest = 0x7E57u;
+__global__ void selftest_expire_kernel(unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  h3::mbar_init(&bar, 1);
+  h3::fence_barrier_init();
+  h3::mbar_wait(&bar, 0u, kErrSelftest, timeout_ns);
+}
+
 }  // namespace
 
 // Raw input columns per activated column: 2 for SwiGLU ([gate | up] rows), else 1.
@@ -72,12 +152,29 @@ int h3b200_device_status(int device, unsigned int* status, int clear) {
   if (e == cudaSuccess && clear) {
     unsigned int zero = 0;
     e = cudaMemcpyToSymbol(h3::g_status, &zero, sizeof(unsigned int));
+    if (e == cudaSuccess && device >= 0 && device < kMaxDevices && g_mirror != nullptr)
+      *reinterpret_cast<volatile unsigned int*>(g_mirror + device) = 0u;
   }
   cudaSetDevice(prev);
   return from_cuda(e, "device_status");
 }
 
+int h3b200_device_status_nowait(int device, unsigned int* status) {
+  if (status == nullptr) return fail(H3B200_ERR_INVALID, "device_status_nowait: status is NULL");
+  if (device < 0 || device >= kMaxDevices) return fail(H3B200_ERR_INVALID, "device_status_nowait: bad device %d", device);
+  *status = status_mirror_read(device);
+  return H3B200_OK;
+}
+
+int h3b200_selftest_expire_wait(int64_t timeout_ns, h3b200_stream_t stream) {
+  H3_GUARD("selftest_expire_wait", stream);
+  if (timeout_ns < 1000 || timeout_ns > 1000000000) return fail(H3B200_ERR_INVALID, "selftest_expire_wait: timeout must be within [1 us, 1 s]");
+  selftest_expire_kernel<<<1, 32, 0, S(stream)>>>((unsigned long long)timeout_ns);
+  return from_cuda(cudaGetLastError(), "selftest_expire_wait");
+}
+
 int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act, h3b200_stream_t stream) {
+  H3_GUARD("apply_input_act", stream);
   if (n < 0) return fail(H3B200_ERR_INVALID, "apply_input_act: negative size");
   if (act == H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "apply_input_act: swiglu halves each row; use h3b200_swiglu");
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "apply_input_act: unsupported act code %d", act);
@@ -87,6 +184,7 @@ int h3b200_apply_input_act(const void* x, void* y, int64_t n, int act, h3b200_st
 }
 
 int h3b200_swiglu(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, int64_t k, h3b200_stream_t stream) {
+  H3_GUARD("swiglu", stream);
   if (m < 0 || k < 0 || ldx < 2 * k || ldy < k) return fail(H3B200_ERR_INVALID, "swiglu: bad shape m=%lld k=%lld ldx=%lld ldy=%lld (ldx >= 2k, ldy >= k)", (long long)m, (long long)k, (long long)ldx, (long long)ldy);
   if (m == 0 || k == 0) return H3B200_OK;
   if (x == nullptr || y == nullptr) return fail(H3B200_ERR_INVALID, "swiglu: NULL pointer");
@@ -96,6 +194,7 @@ int h3b200_swiglu(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, i
 
 int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ldx, int act, int8_t* q, float* scale,
                                  h3b200_stream_t stream) {
+  H3_GUARD("quantize_int8_rowwise", stream);
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: unsupported act code %d", act);
   if (m < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: bad shape m=%lld k=%lld ldx=%lld (act %d reads %lld columns)", (long long)m, (long long)k, (long long)ldx, act, (long long)(k * act_width(act)));
   if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise: NULL pointer");
@@ -105,6 +204,7 @@ int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ld
 
 int h3b200_quantize_int8_rowwise_absmax(const void* x, const float* absmax, int64_t m, int64_t k, int64_t ldx,
                                         int8_t* q, float* scale, h3b200_stream_t stream) {
+  H3_GUARD("quantize_int8_rowwise_absmax", stream);
   if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_absmax: bad shape");
   if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr || absmax == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_absmax: NULL pointer");
   if (m > 0x7fffffffll) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_absmax: m too large");
@@ -113,6 +213,7 @@ int h3b200_quantize_int8_rowwise_absmax(const void* x, const float* absmax, int6
 
 int h3b200_int8_mm(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k, int32_t* out,
                    h3b200_stream_t stream) {
+  H3_GUARD("int8_mm", stream);
   if (m < 0 || n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "int8_mm: negative shape");
   if (m == 0 || n == 0) return H3B200_OK;
   if (a == nullptr || w == nullptr || out == nullptr) return fail(H3B200_ERR_INVALID, "int8_mm: NULL pointer");
@@ -126,6 +227,7 @@ int h3b200_int8_mm(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64
 int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_scale, const int8_t* w, const float* w_scale,
                                     int64_t w_scale_numel, const void* bias, int out_dtype, void* out, int64_t m,
                                     int64_t n, int64_t k, h3b200_stream_t stream) {
+  H3_GUARD("int8_linear_prequantized", stream);
   if (m < 0 || n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: negative shape");
   if (out_dtype != H3B200_DTYPE_BF16) return fail(H3B200_ERR_UNSUPPORTED, "int8_linear_prequantized: only bf16 output is built (got code %d)", out_dtype);
   if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: weight scale must be scalar or per-output-channel, got %lld for n=%lld", (long long)w_scale_numel, (long long)n);
@@ -144,6 +246,7 @@ int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t* w, int64_
                            int64_t k, int epilogue, const float* a_scale, const float* w_scale,
                            int64_t w_scale_numel, const void* bias, const void* gate, const void* residual,
                            int64_t ldr, void* out, int64_t ldo, float* row_absmax, h3b200_stream_t stream) {
+  H3_GUARD("int8_gemm_fused", stream);
   if (m < 0 || n < 0 || k < 0 || lda < k || ldw < k || ldo < n) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: bad shape");
   if (epilogue < h3::kEpiI32 || epilogue > h3::kEpiGatedResidual) return fail(H3B200_ERR_INVALID, "int8_gemm_fused: unknown epilogue %d", epilogue);
   if (m == 0 || n == 0) return H3B200_OK;
@@ -164,6 +267,7 @@ int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t* w, int64_
 int h3b200_dequant_gated_residual(const int32_t* acc, const float* x_scale, const float* w_scale, const void* gate,
                                   const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
                                   h3b200_stream_t stream) {
+  H3_GUARD("dequant_gated_residual", stream);
   if (m < 0 || n < 0 || ldr < n || ldo < n) return fail(H3B200_ERR_INVALID, "dequant_gated_residual: bad shape");
   if (m == 0 || n == 0) return H3B200_OK;
   if (!acc || !x_scale || !w_scale || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "dequant_gated_residual: NULL pointer");
@@ -177,6 +281,7 @@ int64_t h3b200_int8_linear_workspace_bytes(int64_t m, int64_t k) {
 int h3b200_int8_linear(const void* x, int64_t ldx, const int8_t* w, const float* w_scale, int64_t w_scale_numel,
                        const void* bias, int act, void* out, int64_t m, int64_t n, int64_t k, void* workspace,
                        int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("int8_linear", stream);
   if (m < 0 || n < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "int8_linear: bad shape");
   if (m == 0 || n == 0) return H3B200_OK;
   if (workspace == nullptr || workspace_bytes < h3b200_int8_linear_workspace_bytes(m, k)) return fail(H3B200_ERR_INVALID, "int8_linear: workspace too small (need %lld bytes)", (long long)h3b200_int8_linear_workspace_bytes(m, k));
@@ -197,6 +302,7 @@ int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const f
                            const float* s2, const void* gate, const void* residual, int64_t ldr, void* out,
                            int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
                            int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("fused_gated_mlp", stream);
   if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: bad shape m=%lld d=%lld ffn=%lld", (long long)m, (long long)d, (long long)ffn);
   if (act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp: only act=gelu_tanh (1) is built, got %d", act);
   if (m == 0) return H3B200_OK;
@@ -236,6 +342,7 @@ int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk
                           void* k_out, int64_t ldko, const float* freqs, const void* q_weight, const void* k_weight,
                           const void* scale, const void* shift, int64_t m, int64_t heads, int64_t head_dim,
                           int64_t rot_dim, int norm_span, float eps, h3b200_stream_t stream) {
+  H3_GUARD("adaln_rms_rope", stream);
   if (m < 0 || heads <= 0 || head_dim <= 0) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: bad shape");
   if (norm_span != 0 && norm_span != 1) return fail(H3B200_ERR_INVALID, "adaln_rms_rope: norm_span must be 0 (row) or 1 (head)");
   const int64_t rot = rot_dim == 0 ? head_dim : rot_dim;
@@ -255,6 +362,7 @@ int h3b200_qknorm_rope_strided(const void* q, int64_t q_st, int64_t q_sh, void* 
                                void* k_out, int64_t ko_st, int64_t ko_sh, const void* k_weight, const void* freqs,
                                int freqs_dtype, int64_t f_st, int64_t f_sh, int64_t m, int64_t heads,
                                int64_t head_dim, int64_t rot_dim, float eps, h3b200_stream_t stream) {
+  H3_GUARD("qknorm_rope_strided", stream);
   const char* who = "qknorm_rope_strided";
   if (m < 0 || heads <= 0 || head_dim <= 0) return fail(H3B200_ERR_INVALID, "%s: bad shape", who);
   const int64_t rot = rot_dim == 0 ? head_dim : rot_dim;
@@ -294,6 +402,7 @@ int h3b200_qkv_qknorm_rope(const int8_t* xq, const float* x_scale, int64_t m, in
                            int64_t rot_dim, float eps, void* q_out, int64_t q_st, int64_t q_sh, void* k_out,
                            int64_t k_st, int64_t k_sh, void* v_out, int64_t v_st, int64_t v_sh, void* workspace,
                            int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("qkv_qknorm_rope", stream);
   const char* who = "qkv_qknorm_rope";
   if (m < 0 || k <= 0 || heads <= 0 || head_dim != 128) return fail(H3B200_ERR_INVALID, "%s: bad shape (head_dim must be 128)", who);
   if (sec_begin < 0 || sec_end > 3 || sec_begin >= sec_end) return fail(H3B200_ERR_INVALID, "%s: section range [%d, %d) is not a non-empty part of Q|K|V", who, sec_begin, sec_end);
@@ -371,6 +480,7 @@ int h3b200_qkv_qknorm_rope(const int8_t* xq, const float* x_scale, int64_t m, in
 int h3b200_dequant_int4_grouped_to_int8_ex(const int8_t* qdata, const void* s_rel, int s_rel_dtype,
                                            const float* codebook, int64_t n, int64_t k, int64_t group_size,
                                            int8_t* out, h3b200_stream_t stream) {
+  H3_GUARD("dequant_int4_grouped_to_int8_ex", stream);
   if (n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: negative shape");
   if (group_size < 4 || k % 16 || k % group_size || (16 % group_size && group_size % 16))
     return fail(H3B200_ERR_INVALID, "dequant_int4_grouped_to_int8: K=%lld must be divisible by 16 and group_size=%lld; group_size must be >=4 and divide 16 or be a multiple of 16", (long long)k, (long long)group_size);
@@ -385,12 +495,14 @@ int h3b200_dequant_int4_grouped_to_int8_ex(const int8_t* qdata, const void* s_re
 
 int h3b200_dequant_int4_grouped_to_int8(const int8_t* qdata, const float* s_rel, int64_t n, int64_t k,
                                         int64_t group_size, int8_t* out, h3b200_stream_t stream) {
+  H3_GUARD("dequant_int4_grouped_to_int8", stream);
   return h3b200_dequant_int4_grouped_to_int8_ex(qdata, s_rel, H3B200_DTYPE_F32, nullptr, n, k, group_size, out,
                                                 stream);
 }
 
 int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, int64_t k, int64_t ldx, int64_t group_size,
                                          int act, int8_t* q, float* scale, h3b200_stream_t stream) {
+  H3_GUARD("quantize_int8_rowwise_convrot", stream);
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: unsupported act %d", act);
   if (m < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_convrot: bad shape");
   if (group_size != 256) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_convrot: only group_size 256 is built (got %lld)", (long long)group_size);
@@ -410,6 +522,7 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
                             int act, void* out,
                             int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                             h3b200_stream_t stream) {
+  H3_GUARD("w4a8_int8_linear", stream);
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: unsupported act code %d", act);
   if (m < 0 || n < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: bad shape");
   if (group_size < 4 || k % 16 || k % group_size || k % convrot_group || (16 % group_size && group_size % 16))
@@ -541,6 +654,7 @@ int h3b200_fused_gated_mlp_swiglu(const void* x, int64_t ldx, const int8_t* w1, 
                                   int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t d, int64_t ffn,
                                   int64_t fc1_convrot_group, int64_t chunk_tokens, void* workspace,
                                   int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("fused_gated_mlp_swiglu", stream);
   const SwiGLUMlp a{x, ldx, w1, s1, s1_numel, b1, w2, s2, s2_numel, b2, gate, ldg, row_map, residual, ldr, out, ldo,
                     m, d, ffn, fc1_convrot_group, chunk_tokens};
   if (int rc = check_swiglu_mlp(a, "fused_gated_mlp_swiglu")) return rc;
@@ -566,6 +680,7 @@ int h3b200_fused_gated_mlp_swiglu_w4a8(const void* x, int64_t ldx, const int8_t*
                                        int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t d, int64_t ffn,
                                        int64_t chunk_tokens, void* workspace, int64_t workspace_bytes,
                                        h3b200_stream_t stream) {
+  H3_GUARD("fused_gated_mlp_swiglu_w4a8", stream);
   const char* who = "fused_gated_mlp_swiglu_w4a8";
   if (group_size < 4 || (16 % group_size && group_size % 16) || d % group_size || ffn % group_size)
     return fail(H3B200_ERR_INVALID, "%s: group_size=%lld must be >=4, divide 16 or be a multiple of 16, and divide d and ffn", who, (long long)group_size);
@@ -610,6 +725,7 @@ int h3b200_fused_gated_mlp_w4a8(const void* x, int64_t ldx, const int8_t* qdata1
                                 const void* gate, const void* residual, int64_t ldr, void* out, int64_t ldo,
                                 int64_t m, int64_t d, int64_t ffn, int64_t group_size, int act, void* workspace,
                                 int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("fused_gated_mlp_w4a8", stream);
   if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_w4a8: bad shape m=%lld d=%lld ffn=%lld", (long long)m, (long long)d, (long long)ffn);
   if (act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_w4a8: only act=gelu_tanh (1) is built, got %d", act);
   if (group_size < 16 || group_size % 16 || 256 % group_size) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp_w4a8: group_size must be 16..256 and divide 256, got %lld", (long long)group_size);
@@ -698,22 +814,20 @@ __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {nullptr};
 
-// Device address of the scratch array on `device`. The first call on a device
-// looks it up with that device current (cudaGetSymbolAddress); later calls use
-// the cached address. Host code must never pass g_noalloc_scratch itself to a
-// kernel: on the host that name is only a stand-in, not a device address.
-cudaError_t noalloc_scratch(int device, void** out) {
+// Device address of the scratch array on the current device `device`. The first
+// call on a device looks it up (cudaGetSymbolAddress, with that device current)
+// and also fills the device's exact tanh-GELU table, which synchronises
+// `stream` once; later calls use the cached address and launch only. Host code
+// must never pass g_noalloc_scratch itself to a kernel: on the host that name is
+// only a stand-in, not a device address.
+cudaError_t noalloc_scratch(int device, cudaStream_t stream, void** out) {
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_ptr[device] == nullptr) {
-    int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return e;
-    if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (prev != device) cudaSetDevice(prev);
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return e;
+    if ((e = h3::ensure_act_table(H3B200_ACT_GELU_TANH, stream)) != cudaSuccess) return e;
     g_noalloc_ptr[device] = p;
   }
   *out = g_noalloc_ptr[device];
@@ -729,6 +843,7 @@ int64_t h3b200_int8_linear_noalloc_max_scratch_bytes(void) { return kNoAllocScra
 int h3b200_int8_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, const float* w_scale,
                                int64_t w_scale_numel, const void* bias, int act, void* out, int64_t m, int64_t n,
                                int64_t k, h3b200_stream_t stream) {
+  H3_GUARD("int8_linear_noalloc", stream);
   if (m < 0 || n < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: bad shape");
   if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: unsupported act code %d", act);
   if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "int8_linear_noalloc: weight scale must be scalar or per-output-channel");
@@ -746,7 +861,7 @@ int h3b200_int8_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, cons
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   void* base = nullptr;
-  if (e == cudaSuccess) e = noalloc_scratch(dev, &base);
+  if (e == cudaSuccess) e = noalloc_scratch(dev, S(stream), &base);
   if (e != cudaSuccess) return from_cuda(e, "int8_linear_noalloc: scratch set-up");
   int8_t* xq = static_cast<int8_t*>(base);
   float* xs = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + q_bytes);

@@ -14,9 +14,13 @@ namespace h3 {
 // ---------------------------------------------------------------------------
 // Device status word. 0 = healthy; the first failing wait records its code.
 // Every spin-wait in this library is bounded; on timeout the kernel records a
-// code here and unwinds instead of hanging the GPU.
+// code here and unwinds instead of hanging the GPU. The first recorder also
+// writes the code to a mapped pinned host word (g_status_host, set up per device
+// by the C-ABI layer), so the host sees the failure without synchronising and
+// every later entry point refuses to launch until the status is cleared.
 // ---------------------------------------------------------------------------
 extern __device__ unsigned int g_status;
+extern __device__ unsigned int* g_status_host;
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s per wait
 
@@ -27,7 +31,13 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 __device__ __forceinline__ void set_status(unsigned int code) {
-  atomicCAS(&g_status, 0u, code);
+  if (atomicCAS(&g_status, 0u, code) == 0u) {
+    unsigned int* h = *((unsigned int* volatile*)&g_status_host);
+    if (h != nullptr) {
+      *((volatile unsigned int*)h) = code;
+      __threadfence_system();
+    }
+  }
 }
 
 __device__ __forceinline__ bool status_bad() {

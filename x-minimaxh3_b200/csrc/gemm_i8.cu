@@ -40,6 +40,7 @@
 namespace h3 {
 
 __device__ unsigned int g_status = 0u;
+__device__ unsigned int* g_status_host = nullptr;
 
 namespace {
 

@@ -15,6 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libh3b200.so")
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_LAUNCH, ERR_DEVICE = 0, 1, 2, 3, 4
+STATUS_SELFTEST = 0x7E57
 ACT_NONE, ACT_GELU_TANH, ACT_SWIGLU = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_I32 = 0, 1, 2, 3
 
@@ -28,6 +29,8 @@ SIGNATURES = {
     "h3b200_version": (ctypes.c_char_p, []),
     "h3b200_last_error": (ctypes.c_char_p, []),
     "h3b200_device_status": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint), _i32]),
+    "h3b200_device_status_nowait": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint)]),
+    "h3b200_selftest_expire_wait": (_i32, [_i64, _p]),
     "h3b200_apply_input_act": (_i32, [_p, _p, _i64, _i32, _p]),
     "h3b200_swiglu": (_i32, [_p, _i64, _p, _i64, _i64, _i64, _p]),
     "h3b200_quantize_int8_rowwise": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _p, _p]),
@@ -112,3 +115,22 @@ def device_status(device: int, clear: bool = False) -> int:
     v = ctypes.c_uint(0)
     check(load().h3b200_device_status(device, ctypes.byref(v), 1 if clear else 0), "h3b200_device_status")
     return int(v.value)
+
+
+def device_status_nowait(device: int) -> int:
+    """Status word as last written to its mapped host copy (no synchronisation)."""
+    v = ctypes.c_uint(0)
+    check(load().h3b200_device_status_nowait(device, ctypes.byref(v)), "h3b200_device_status_nowait")
+    return int(v.value)
+
+
+def check_device(device: int, what: str) -> None:
+    """Raise if a bounded wait on ``device`` has expired. Reads the mapped host copy
+    of the status word, so call it after synchronising with the work to check.
+
+    Called at the sync points of the host pipeline and the bench, so a failure
+    inside a kernel is never reported as a result."""
+    code = device_status_nowait(device)
+    if code:
+        raise RuntimeError(f"{what}: a bounded device wait expired on device {device} (status {code:#x}); "
+                           "outputs since then are not valid")

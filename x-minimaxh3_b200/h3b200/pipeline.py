@@ -6,8 +6,10 @@ three CUDA streams: host-to-device copies of chunk i+1, the fused MLP of chunk
 i (``fused_gated_mlp``: quantize -> fc1 + GELU -> requant -> fc2 + gated
 residual) and the device-to-host copy of chunk i-1 run at the same time. The
 MLP is per-token, so the chunked result is bit-identical to one call over all
-tokens. Device staging buffers are allocated once per (device, d, chunk) and
-reused.
+tokens. Device staging buffers (token slots, streams, events and the MLP
+workspace) are allocated once per (device, d, ffn, chunk, slots) and reused;
+calls that share them from several host threads are serialised by a lock held
+while their work is queued (the streams and events then order it on the GPU).
 
 The copies in dominate (x and residual: 4 bytes per element against 2 out), so
 the call lasts about as long as the host-to-device stream plus whatever follows
@@ -30,7 +32,9 @@ _cache: dict = {}
 
 
 class _Staging:
-    def __init__(self, device: torch.device, d: int, chunk: int, slots: int):
+    def __init__(self, device: torch.device, d: int, ffn: int, chunk: int, slots: int):
+        from . import _lib
+        self.lock = threading.Lock()
         self.x = [torch.empty(chunk, d, dtype=torch.bfloat16, device=device) for _ in range(slots)]
         self.r = [torch.empty(chunk, d, dtype=torch.bfloat16, device=device) for _ in range(slots)]
         self.h2d = torch.cuda.Stream(device)
@@ -38,15 +42,16 @@ class _Staging:
         self.d2h = torch.cuda.Stream(device)
         self.free = [torch.cuda.Event() for _ in range(slots)]
         self.used = [False] * slots
-        self.workspace = None
+        nbytes = int(_lib.load().h3b200_fused_gated_mlp_workspace_bytes(chunk, d, ffn))
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
 
 
-def _staging(device: torch.device, d: int, chunk: int, slots: int) -> _Staging:
-    key = (device.index, d, chunk, slots)
+def _staging(device: torch.device, d: int, ffn: int, chunk: int, slots: int) -> _Staging:
+    key = (device.index, d, ffn, chunk, slots)
     with _cache_lock:
         st = _cache.get(key)
         if st is None:
-            st = _Staging(device, d, chunk, slots)
+            st = _Staging(device, d, ffn, chunk, slots)
             _cache[key] = st
     return st
 
@@ -94,8 +99,19 @@ def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torc
         raise ValueError("out must be a host bf16 tensor shaped like residual")
     dev = w1q.device
     chunk = min(chunk_tokens, m) if m > 0 else 1
-    st = _staging(dev, d, chunk, slots)
-    cur = torch.cuda.current_stream(dev)
+    st = _staging(dev, d, w1q.shape[0], chunk, slots)
+    with st.lock:
+        _queue(st, residual, hidden, w1q, s1, w2q, s2, gate, out, m, chunk, slots)
+    if synchronize:
+        torch.cuda.current_stream(dev).synchronize()
+        from . import _lib
+        _lib.check_device(dev.index, "fused_gated_mlp_host")
+    return out
+
+
+def _queue(st: _Staging, residual, hidden, w1q, s1, w2q, s2, gate, out, m: int, chunk: int, slots: int) -> None:
+    """Queue the chunked copies and MLPs of one call on the staging streams."""
+    cur = torch.cuda.current_stream(w1q.device)
     for s in (st.h2d, st.comp, st.d2h):
         s.wait_stream(cur)
     lo = 0
@@ -110,10 +126,6 @@ def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torc
             rb.copy_(residual[lo:hi], non_blocking=True)
         st.comp.wait_stream(st.h2d)
         with torch.cuda.stream(st.comp):
-            if st.workspace is None:
-                from . import _lib
-                nbytes = int(_lib.load().h3b200_fused_gated_mlp_workspace_bytes(chunk, d, w1q.shape[0]))
-                st.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
             fused_gated_mlp(rb, xb, w1q, s1, w2q, s2, gate, out=rb, workspace=st.workspace)
         st.d2h.wait_stream(st.comp)
         with torch.cuda.stream(st.d2h):
@@ -122,6 +134,3 @@ def fused_gated_mlp_host(residual: torch.Tensor, hidden: torch.Tensor, w1q: torc
         st.used[k] = True
         lo = hi
     cur.wait_stream(st.d2h)
-    if synchronize:
-        cur.synchronize()
-    return out
