@@ -186,7 +186,7 @@ def _case_mlp_inputs(m: int, dev):
     return wt, x, gate, res
 
 
-def _case_case_timed(fn, iters: int, report: bool):
+def _case_timed(fn, iters: int, report: bool):
     import torch
 
     if not report:
