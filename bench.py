@@ -158,8 +158,10 @@ class ClockSampler:
 # (single-side QK-norm + partial RoPE of H3 K, 56 heads, rot 96, bf16 table, into an
 # HND buffer), ``qkv_h3`` (the H3 Q/K/V projection of M tokens, hidden 5,376, with
 # QK-norm + RoPE into HND buffers, from a ConvRot-quantized activation),
-# ``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input) or ``norm_rope`` (AdaLN + RMSNorm + RoPE on
-# Q and K, 24 heads x 128). Shapes are those of the config-1 MLP and config-3
+# ``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input),
+# ``norm_rope`` (AdaLN + RMSNorm + RoPE on Q and K, 24 heads x 128) or
+# ``rms_adaln`` / ``rms_adaln_h3`` (standalone RMS-AdaLN on a [M, 3072] hidden stream with one
+# modulation row / on H3's [M, 5376] with three segments). Shapes are those of the config-1 MLP and config-3
 # norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
 # runs the kernels it needs to build its inputs, then launches the kernel under
 # study ``--iters`` times, so a profiler can skip the set-up launches by kernel
@@ -168,7 +170,8 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 CASES = ["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp", "mlp_w4a8", "mlp_swiglu",
-         "mlp_swiglu_w4", "decode_w4", "qknorm_h3", "qkv_h3", "convrot", "convrot_x", "norm_rope"]
+         "mlp_swiglu_w4", "decode_w4", "qknorm_h3", "qkv_h3", "convrot", "convrot_x", "norm_rope", "rms_adaln",
+         "rms_adaln_h3"]
 
 
 def _case_mlp_inputs(m: int, dev):
@@ -228,6 +231,19 @@ def run_case(case: str, m: int, iters: int, report: bool = False):
         qo, ko = torch.empty_like(q), torch.empty_like(k)
         ms = _case_timed(lambda: ops.adaln_rms_rope_(q, k, table, wq, wk, sc, sh, 1e-6, "row", 0, q_out=qo, k_out=ko),
                     iters, report)
+    elif case in ("rms_adaln", "rms_adaln_h3"):
+        import types
+
+        g = torch.Generator(device=dev).manual_seed(4)
+        d = 3072 if case == "rms_adaln" else 5376
+        x = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        proj = (torch.randn(3, 6 * d, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        norm = types.SimpleNamespace(weight=(1 + 0.02 * torch.randn(d, generator=g, device=dev)).to(torch.bfloat16),
+                                     eps=1e-6)
+        segs = [(0, m, 0)] if case == "rms_adaln" else [(0, m // 8, 2), (m // 8, m // 4, 1), (m // 4, m, 0)]
+        ms = _case_timed(lambda: ops.rms_adaln_segmented(x, norm, proj[:, :d], proj[:, d:2 * d], segs, out=y),
+                         iters, report)
     elif case in ("convrot", "convrot_x"):
         g = torch.Generator(device=dev).manual_seed(6)
         a = torch.randn(m, D_FFN if case == "convrot" else D_MODEL, generator=g, device=dev).to(torch.bfloat16)
@@ -577,6 +593,38 @@ def run_ours(args, rank, world, local_rank):
     nr_ms = timed(k_nr, 50, stream)
     nr_bytes = M_TOKENS * NR_BYTES_PER_TOKEN
 
+    # ---- standalone RMS-AdaLN on the hidden stream, HBM-bound: config-3 shape [32,760, 3,072] with one
+    #      modulation row, and H3's width 5,376 with three modulation segments (kernels.py:7586) ----
+    import types
+
+    xa = torch.randn(M_TOKENS, D_MODEL, generator=gn, device=dev).to(torch.bfloat16)
+    ya = torch.empty_like(xa)
+    norm_a = types.SimpleNamespace(weight=wq, eps=1e-6)
+
+    def k_ra():
+        ops.rms_adaln_segmented(xa, norm_a, sh.reshape(1, -1), sc.reshape(1, -1), [(0, M_TOKENS, 0)], out=ya)
+
+    for _ in range(3):
+        k_ra()
+    ra_ms = timed(k_ra, 50, stream)
+    ra_bytes = M_TOKENS * D_MODEL * 4
+    del xa, ya
+    xh = torch.randn(M_TOKENS, 5376, generator=gn, device=dev).to(torch.bfloat16)
+    yh = torch.empty_like(xh)
+    projh = (torch.randn(3, 6 * 5376, generator=gn, device=dev) * 0.1).to(torch.bfloat16)
+    norm_h = types.SimpleNamespace(weight=(1 + 0.02 * torch.randn(5376, generator=gn, device=dev)).to(torch.bfloat16),
+                                   eps=1e-6)
+    segs_h = [(0, 1024, 2), (1024, 2048, 1), (2048, M_TOKENS, 0)]
+
+    def k_ra_h3():
+        ops.rms_adaln_segmented(xh, norm_h, projh[:, :5376], projh[:, 5376:2 * 5376], segs_h, out=yh)
+
+    for _ in range(3):
+        k_ra_h3()
+    rah_ms = timed(k_ra_h3, 50, stream)
+    rah_bytes = M_TOKENS * 5376 * 4
+    del xh, yh
+
     # ---- config 2: fused W4A8 MLP (reference's asymmetric group-128 format, int4 at rest) ----
     g3 = torch.Generator(device=dev).manual_seed(3)
     w1f = (torch.randn(D_FFN, D_MODEL, generator=g3, device=dev) * 0.02).to(torch.bfloat16)
@@ -805,6 +853,15 @@ def run_ours(args, rank, world, local_rank):
                 "long_video_block_cfg4": {"tokens_total": M4, "tokens_this_rank": m4, "ms": blk_ms,
                                           "tokens_per_s": M4 / (blk_ms * 1e-3),
                                           "mode": f"token-shard x{world} (norm-RoPE + W8A8 MLP per rank)"},
+                "rms_adaln_cfg3": {"ms": ra_ms, "achieved": ra_bytes / (ra_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                                   "unit": "GB/s", "frac": ra_bytes / (ra_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                   "bytes_per_token": D_MODEL * 4, "tokens": M_TOKENS,
+                                   "form": "RMSNorm(weight) -> *(1+scale) -> +shift, one modulation row"},
+                "rms_adaln_h3_3seg": {"ms": rah_ms, "achieved": rah_bytes / (rah_ms * 1e-3) / 1e9,
+                                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                      "frac": rah_bytes / (rah_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                      "bytes_per_token": 5376 * 4, "tokens": M_TOKENS,
+                                      "form": "H3 width 5,376, three modulation segments (strided split_adaln views)"},
                 "norm_rope_cfg3": {"ms": nr_ms, "achieved": nr_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                    "frac": nr_gbs / peaks["hbm_gbs"], "bytes_per_token": NR_BYTES_PER_TOKEN,
                                    "table_bytes_per_token": NR_TABLE_BYTES_PER_TOKEN,

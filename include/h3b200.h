@@ -216,6 +216,44 @@ H3B200_API int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* 
                            const float* s2, const void* gate, const void* residual, int64_t ldr, void* out,
                            int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
                            int64_t workspace_bytes, h3b200_stream_t stream);
+/*
+ * The same MLP with per-token gate rows: out[t] = residual[t] + y[t] * gate_rows[row_map[t]]
+ * -- the per-modulation-segment addcmul_ of try_fused_gated_mlp
+ * (h3serve/native_engine/model/fused_mlp.py:414-425 via _segment_row_map :34-55;
+ * _gated_residual layers.py:937-953). gate_rows: bf16 rows at stride ldg
+ * (>= d, a multiple of 8); row_map: int32 [m] on the device, every value a
+ * valid row. Same workspace as h3b200_fused_gated_mlp.
+ */
+H3B200_API int h3b200_fused_gated_mlp_segmented(const void* x, int64_t ldx, const int8_t* w1, const float* s1,
+                                                const int8_t* w2, const float* s2, const void* gate_rows,
+                                                int64_t ldg, const int32_t* row_map, const void* residual,
+                                                int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t d,
+                                                int64_t ffn, int act, void* workspace, int64_t workspace_bytes,
+                                                h3b200_stream_t stream);
+
+/*
+ * RMS-AdaLN on the hidden stream, with per-token modulation rows:
+ *   h   = bf16((x / sqrt(mean(x^2) + eps)) * w)   (no weight: bf16(x / sqrt(..)))
+ *   out = bf16(bf16(h * bf16(1 + scale[r])) + shift[r])
+ * r = row_map[t] (int32 [m] on the device; values outside [0, mod_rows) are
+ * clamped), or, with row_map NULL, t / tokens_per_row (tokens_per_row <= 0:
+ * row 0 for every token). scale == shift == NULL gives the plain RMSNorm.
+ * Replaces H3's rms_adaln(value, norm, shift, scale, segments)
+ * (h3serve/native_engine/model/kernels.py:7586-7634: F.rms_norm with the
+ * module weight, then per segment mul_(1 + scale[row]).add_(shift[row]) in bf16;
+ * its Triton _segmented_rms_adaln_kernel, backends/original/kernels/
+ * fused_norm_rope.py:12-44, keeps the same three bf16 steps) and comfy_kitchen's
+ * rms_adaln(x, scale, shift, eps) (__init__.py:130-150; eager
+ * backends/eager/adaln.py:17-20, no weight; per-sample [B, 1, D] modulation is
+ * tokens_per_row = T, like its CUDA kernel's scale_group, cuda/ops/adaln.cu:104-199).
+ * x, out: bf16 [m, d] at row strides ldx / ldo (out may alias x); norm_weight:
+ * bf16 [d] or NULL; scale / shift: bf16 [mod_rows, d] at row strides
+ * ld_scale / ld_shift. d % 8 == 0, d <= 8192, 16-byte aligned rows.
+ */
+H3B200_API int h3b200_rms_adaln(const void* x, int64_t ldx, const void* norm_weight, const void* scale,
+                                int64_t ld_scale, const void* shift, int64_t ld_shift, int64_t mod_rows,
+                                const int32_t* row_map, int64_t tokens_per_row, float eps, void* out, int64_t ldo,
+                                int64_t m, int64_t d, h3b200_stream_t stream);
 
 /*
  * Fused (AdaLN-modulate +) RMSNorm + split-half RoPE on Q and K.
@@ -239,6 +277,21 @@ H3B200_API int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, 
                           void* k_out, int64_t ldko, const float* freqs, const void* q_weight, const void* k_weight,
                           const void* scale, const void* shift, int64_t m, int64_t heads, int64_t head_dim,
                           int64_t rot_dim, int norm_span, float eps, h3b200_stream_t stream);
+/*
+ * h3b200_adaln_rms_rope (row span) with a modulation row per token: token t
+ * uses scale / shift row row_map[t] (int32 [m] on the device, clamped to
+ * [0, mod_rows)), or t / tokens_per_row when row_map is NULL -- H3's segmented
+ * rms_adaln (kernels.py:7586-7634, per-segment scale[row] / shift[row],
+ * layers.py:909-934 _scale_shift) fused with the RoPE. scale / shift: bf16
+ * [mod_rows, heads*head_dim] at row strides ld_scale / ld_shift (multiples of 8).
+ */
+H3B200_API int h3b200_adaln_rms_rope_segmented(const void* q, int64_t ldq, const void* k, int64_t ldk, void* q_out,
+                                               int64_t ldqo, void* k_out, int64_t ldko, const float* freqs,
+                                               const void* q_weight, const void* k_weight, const void* scale,
+                                               int64_t ld_scale, const void* shift, int64_t ld_shift,
+                                               int64_t mod_rows, const int32_t* row_map, int64_t tokens_per_row,
+                                               int64_t m, int64_t heads, int64_t head_dim, int64_t rot_dim,
+                                               float eps, h3b200_stream_t stream);
 
 /*
  * Per-head RMSNorm + partial split-half RoPE on one tensor (k == NULL) or two,

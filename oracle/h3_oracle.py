@@ -50,6 +50,8 @@ __all__ = [
     "swiglu_mlp",
     "rms_norm_row",
     "rms_adaln",
+    "rms_adaln_rows",
+    "rms_norm_noaffine",
     "rope_split_half",
     "adaln_rms_rope",
     "rms_rope_split_half",
@@ -337,6 +339,36 @@ def rms_norm_row(x_bf16, weight_bf16, eps=1e-6):
     rstd = _rms_rstd(xf, eps)
     w = bf16_to_f32(weight_bf16)
     return f32_to_bf16(((xf * rstd).astype(np.float32) * w).astype(np.float32))
+
+
+def rms_norm_noaffine(x_bf16, eps=1e-6):
+    """``F.rms_norm(x, (D,), eps=eps)`` without a weight on bf16: ``bf16(x * rstd)``
+    (comfy_kitchen backends/eager/adaln.py:17-20)."""
+    xf = bf16_to_f32(x_bf16)
+    return f32_to_bf16((xf * _rms_rstd(xf, eps)).astype(np.float32))
+
+
+def rms_adaln_rows(x_bf16, weight_bf16, scale_rows_bf16, shift_rows_bf16, row_map, eps=1e-6):
+    """RMS-AdaLN with a modulation row per token.
+
+    H3 ``rms_adaln(value, norm, shift, scale, segments)`` eager branch
+    (h3serve/native_engine/model/kernels.py:7623-7634): ``hidden = norm(value)``
+    (``F.rms_norm`` with the module weight, layers.py:39-48), then for each segment
+    ``hidden[start:stop].mul_(1.0 + scale[row].to(bf16)).add_(shift[row].to(bf16))``.
+    ``weight_bf16=None`` is comfy_kitchen's weightless ``rms_adaln``
+    (backends/eager/adaln.py:17-20). x: bf16 [M, D]; scale/shift rows: bf16 [R, D];
+    row_map: int [M] (the segment row of each token). Returns bf16 bits."""
+    if weight_bf16 is None:
+        h = bf16_to_f32(rms_norm_noaffine(x_bf16, eps))
+    else:
+        h = bf16_to_f32(rms_norm_row(x_bf16, weight_bf16, eps))
+    rm = np.asarray(row_map, np.int64)
+    sc = bf16_to_f32(np.asarray(scale_rows_bf16, np.uint16).reshape(-1, h.shape[-1]))[rm]
+    sh = bf16_to_f32(np.asarray(shift_rows_bf16, np.uint16).reshape(-1, h.shape[-1]))[rm]
+    one_plus = _bf16_round((F32(1.0) + sc).astype(np.float32))
+    h = _bf16_round((h * one_plus).astype(np.float32))
+    h = _bf16_round((h + sh).astype(np.float32))
+    return f32_to_bf16(h)
 
 
 def rms_adaln(x_bf16, weight_bf16, scale_bf16, shift_bf16, eps=1e-6):

@@ -353,6 +353,46 @@ def main() -> None:
         "q_bf16tab": b16(q16[0]), "k_bf16tab": b16(k16[0]), "q_h3": b16(qh3), "k_h3": b16(kh3),
     }
 
+    # 12. RMS-AdaLN on the hidden stream.
+    #  (a) H3 rms_adaln(value, norm, shift, scale, segments) (kernels.py:7586-7634, eager branch on
+    #      CPU) at the H3 width 5,376 with three modulation segments: an RMSNorm module with an fp32
+    #      weight (cast to bf16 in its forward), shift/scale as the fp32 [rows, hidden] views that
+    #      split_adaln cuts from a [1, 18 * hidden] projection (cast by .to(bf16)), and edge rows
+    #      (zero, tiny, one huge value, constant).
+    #  (b) comfy_kitchen rms_adaln(x, scale, shift, eps) (eager/adaln.py:17-20, no weight) with
+    #      per-sample [B, 1, D] modulation.
+    import importlib
+
+    from h3serve.native_engine.model import kernels as h3kernels
+
+    eadaln = importlib.import_module("comfy_kitchen.backends.eager.adaln")  # the package re-exports a function
+
+    gm = torch.Generator().manual_seed(12)
+    m12, d12 = 96, 5376
+    v12 = (torch.randn(m12, d12, generator=gm) * 1.3).to(torch.bfloat16)
+    v12[4] = 0
+    v12[9] = (v12[9].float() * 1e-30).to(torch.bfloat16)
+    v12[11, 5] = 3.0e38
+    v12[17] = -2.0
+    norm12 = h3layers.RMSNorm(d12, eps=1e-6)
+    with torch.no_grad():
+        norm12.weight.copy_(1 + 0.05 * torch.randn(d12, generator=gm))
+    proj = torch.randn(1, 18 * d12, generator=gm) * 0.2
+    shift_a, scale_a = h3layers.split_adaln(proj, hidden_size=d12)[:2]
+    segs12 = ((0, 25, 2), (25, 60, 0), (60, m12, 1))
+    o12 = h3kernels.rms_adaln(v12.clone(), norm12, shift_a, scale_a, segs12)
+    xb = torch.randn(2, 48, 3072, generator=gm).to(torch.bfloat16)
+    scb = (torch.randn(2, 1, 3072, generator=gm) * 0.1).to(torch.bfloat16)
+    shb = (torch.randn(2, 1, 3072, generator=gm) * 0.1).to(torch.bfloat16)
+    ob = eadaln.rms_adaln(xb, scb, shb, 1e-6)
+    assert o12.dtype == torch.bfloat16 and ob.dtype == torch.bfloat16
+    out["rms_adaln"] = {
+        "x_h3": b16(v12), "w_h3": b16(norm12.weight.detach().to(torch.bfloat16)),
+        "shift_rows": shift_a.contiguous().numpy(), "scale_rows": scale_a.contiguous().numpy(),
+        "segments": np.array(segs12, dtype=np.int64), "eps_h3": np.float32(norm12.eps), "out_h3": b16(o12),
+        "x_cf": b16(xb), "scale_cf": b16(scb), "shift_cf": b16(shb), "out_cf": b16(ob),
+    }
+
     for name, arrays in out.items():
         if args.only is not None and name not in args.only:
             continue

@@ -212,3 +212,23 @@ def test_swiglu_mlp_oracle_vs_reference(golden):
     for mine, ref in ((it["raw"], g["raw"]), (it["y"], g["proj"]), (out, g["out"])):
         a, b = O.bf16_to_f32(mine).astype(np.float64), O.bf16_to_f32(ref).astype(np.float64)
         assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-2 and np.abs(a - b).max() <= 2e-2
+
+
+def test_rms_adaln_oracle_pinned_to_reference(golden):
+    """RMS-AdaLN on the hidden stream, bit-exact against the reference's eager outputs:
+    H3's segmented rms_adaln at width 5,376 (three segments, module weight, fp32 modulation
+    rows cast to bf16, zero / tiny / huge / constant rows) and comfy_kitchen's weightless
+    rms_adaln with per-sample [B, 1, D] modulation."""
+    import warnings
+
+    g = golden("rms_adaln")
+    row_map = np.concatenate([np.full(b - a, r) for a, b, r in g["segments"]])
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", RuntimeWarning)   # the huge row's mean overflows fp32, as in the reference
+        out = O.rms_adaln_rows(g["x_h3"], g["w_h3"], O.f32_to_bf16(g["scale_rows"]), O.f32_to_bf16(g["shift_rows"]),
+                               row_map, float(g["eps_h3"]))
+    np.testing.assert_array_equal(out, g["out_h3"])
+    b, t, d = g["x_cf"].shape
+    out_cf = O.rms_adaln_rows(g["x_cf"].reshape(-1, d), None, g["scale_cf"].reshape(b, d),
+                              g["shift_cf"].reshape(b, d), np.repeat(np.arange(b), t), 1e-6)
+    np.testing.assert_array_equal(out_cf, g["out_cf"].reshape(-1, d))

@@ -298,17 +298,22 @@ int64_t h3b200_fused_gated_mlp_workspace_bytes(int64_t m, int64_t d, int64_t ffn
   return round_up(m * d, 256) + round_up(m * 4, 256) * 3 + round_up(m * ffn * 2, 256) + round_up(m * ffn, 256) + 1024;
 }
 
-int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const int8_t* w2,
-                           const float* s2, const void* gate, const void* residual, int64_t ldr, void* out,
-                           int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
-                           int64_t workspace_bytes, h3b200_stream_t stream) {
-  H3_GUARD("fused_gated_mlp", stream);
-  if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: bad shape m=%lld d=%lld ffn=%lld", (long long)m, (long long)d, (long long)ffn);
-  if (act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp: only act=gelu_tanh (1) is built, got %d", act);
+}  // extern "C"
+
+// The W8A8 MLP of h3b200_fused_gated_mlp(_segmented): gate is one row [d] (row_map
+// nullptr) or rows at stride ldg selected per token by row_map.
+static int fused_gated_mlp_impl(const char* what, const void* x, int64_t ldx, const int8_t* w1, const float* s1,
+                                const int8_t* w2, const float* s2, const void* gate, int64_t ldg,
+                                const int32_t* row_map, const void* residual, int64_t ldr, void* out, int64_t ldo,
+                                int64_t m, int64_t d, int64_t ffn, int act, void* workspace, int64_t workspace_bytes,
+                                h3b200_stream_t stream) {
+  if (m < 0 || d <= 0 || ffn <= 0 || ldx < d || ldr < d || ldo < d) return fail(H3B200_ERR_INVALID, "%s: bad shape m=%lld d=%lld ffn=%lld", what, (long long)m, (long long)d, (long long)ffn);
+  if (act != H3B200_ACT_GELU_TANH) return fail(H3B200_ERR_UNSUPPORTED, "%s: only act=gelu_tanh (1) is built, got %d", what, act);
+  if (row_map != nullptr && (ldg < d || ldg % 8)) return fail(H3B200_ERR_INVALID, "%s: gate row stride %lld must be >= d and a multiple of 8", what, (long long)ldg);
   if (m == 0) return H3B200_OK;
-  if (!x || !w1 || !s1 || !w2 || !s2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: NULL pointer");
-  if (d % 16 || ffn % 16) return fail(H3B200_ERR_UNSUPPORTED, "fused_gated_mlp: needs d %% 16 == 0 and ffn %% 16 == 0");
-  if (workspace == nullptr || workspace_bytes < h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn)) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: workspace too small (need %lld bytes)", (long long)h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn));
+  if (!x || !w1 || !s1 || !w2 || !s2 || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "%s: NULL pointer", what);
+  if (d % 16 || ffn % 16) return fail(H3B200_ERR_UNSUPPORTED, "%s: needs d %% 16 == 0 and ffn %% 16 == 0", what);
+  if (workspace == nullptr || workspace_bytes < h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn)) return fail(H3B200_ERR_INVALID, "%s: workspace too small (need %lld bytes)", what, (long long)h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn));
   Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
   int8_t* xq = static_cast<int8_t*>(c.take(m * d));
   float* xs = static_cast<float*>(c.take(m * 4));
@@ -316,11 +321,11 @@ int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const f
   float* xs2 = static_cast<float*>(c.take(m * 4));
   void* a = c.take(m * ffn * 2);
   int8_t* q2 = static_cast<int8_t*>(c.take(m * ffn));
-  if (!c.ok) return fail(H3B200_ERR_INVALID, "fused_gated_mlp: workspace too small");
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "%s: workspace too small", what);
   cudaStream_t st = S(stream);
-  int rc = h3b200_quantize_int8_rowwise(x, m, d, ldx, H3B200_ACT_NONE, xq, xs, stream);
-  if (rc != H3B200_OK) return rc;
-  cudaError_t e = cudaMemsetAsync(amax, 0, m * 4, st);
+  cudaError_t e = h3::launch_quantize_rows(x, ldx, m, d, H3B200_ACT_NONE, nullptr, xq, xs, st);
+  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: quantize x");
+  e = cudaMemsetAsync(amax, 0, m * 4, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: memset");
   h3::GemmArgs g1;
   g1.a = xq; g1.w = w1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
@@ -333,9 +338,53 @@ int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const f
   h3::GemmArgs g2;
   g2.a = q2; g2.w = w2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
   g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = s2; g2.w_scale_per_channel = 1;
-  g2.gate = gate; g2.residual = residual; g2.ldr = ldr; g2.out = out; g2.ldo = ldo;
+  g2.gate = gate; g2.row_map = row_map; g2.ldg = row_map != nullptr ? ldg : 0;
+  g2.residual = residual; g2.ldr = ldr; g2.out = out; g2.ldo = ldo;
   e = h3::launch_gemm_i8(g2, st);
   return from_cuda(e, "fused_gated_mlp: fc2");
+}
+
+extern "C" {
+
+int h3b200_fused_gated_mlp(const void* x, int64_t ldx, const int8_t* w1, const float* s1, const int8_t* w2,
+                           const float* s2, const void* gate, const void* residual, int64_t ldr, void* out,
+                           int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
+                           int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("fused_gated_mlp", stream);
+  return fused_gated_mlp_impl("fused_gated_mlp", x, ldx, w1, s1, w2, s2, gate, 0, nullptr, residual, ldr, out, ldo,
+                              m, d, ffn, act, workspace, workspace_bytes, stream);
+}
+
+int h3b200_fused_gated_mlp_segmented(const void* x, int64_t ldx, const int8_t* w1, const float* s1,
+                                     const int8_t* w2, const float* s2, const void* gate_rows, int64_t ldg,
+                                     const int32_t* row_map, const void* residual, int64_t ldr, void* out,
+                                     int64_t ldo, int64_t m, int64_t d, int64_t ffn, int act, void* workspace,
+                                     int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("fused_gated_mlp_segmented", stream);
+  if (m > 0 && row_map == nullptr) return fail(H3B200_ERR_INVALID, "fused_gated_mlp_segmented: row_map is NULL");
+  return fused_gated_mlp_impl("fused_gated_mlp_segmented", x, ldx, w1, s1, w2, s2, gate_rows, ldg, row_map, residual,
+                              ldr, out, ldo, m, d, ffn, act, workspace, workspace_bytes, stream);
+}
+
+int h3b200_rms_adaln(const void* x, int64_t ldx, const void* norm_weight, const void* scale, int64_t ld_scale,
+                     const void* shift, int64_t ld_shift, int64_t mod_rows, const int32_t* row_map,
+                     int64_t tokens_per_row, float eps, void* out, int64_t ldo, int64_t m, int64_t d,
+                     h3b200_stream_t stream) {
+  H3_GUARD("rms_adaln", stream);
+  if (m < 0 || d <= 0 || ldx < d || ldo < d) return fail(H3B200_ERR_INVALID, "rms_adaln: bad shape m=%lld d=%lld ldx=%lld ldo=%lld", (long long)m, (long long)d, (long long)ldx, (long long)ldo);
+  if ((scale == nullptr) != (shift == nullptr)) return fail(H3B200_ERR_INVALID, "rms_adaln: scale and shift must be given together");
+  if (scale != nullptr && (mod_rows <= 0 || ld_scale < d || ld_shift < d)) return fail(H3B200_ERR_INVALID, "rms_adaln: modulation needs mod_rows >= 1 and row strides >= d");
+  if (!(eps >= 0.0f)) return fail(H3B200_ERR_INVALID, "rms_adaln: eps must be >= 0");
+  if (m == 0) return H3B200_OK;
+  if (x == nullptr || out == nullptr) return fail(H3B200_ERR_INVALID, "rms_adaln: NULL pointer");
+  if (d % 8 || d > 8192 || ldx % 8 || ldo % 8 || (scale != nullptr && (ld_scale % 8 || ld_shift % 8)))
+    return fail(H3B200_ERR_UNSUPPORTED, "rms_adaln: needs d %% 8 == 0, d <= 8192 and row strides that are multiples of 8 elements");
+  h3::RmsAdalnArgs a;
+  a.x = x; a.ldx = ldx; a.y = out; a.ldy = ldo; a.weight = norm_weight;
+  a.scale = scale; a.lds = ld_scale; a.shift = shift; a.ldh = ld_shift;
+  a.row_map = row_map; a.tokens_per_row = tokens_per_row; a.rows = scale != nullptr ? mod_rows : 0;
+  a.m = m; a.d = d; a.eps = eps;
+  return from_cuda(h3::launch_rms_adaln(a, S(stream)), "rms_adaln");
 }
 
 int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk, void* q_out, int64_t ldqo,
@@ -355,6 +404,29 @@ int h3b200_adaln_rms_rope(const void* q, int64_t ldq, const void* k, int64_t ldk
   a.freqs = freqs; a.q_weight = q_weight; a.k_weight = k_weight; a.scale = scale; a.shift = shift;
   a.m = m; a.heads = heads; a.head_dim = head_dim; a.rot_dim = rot; a.norm_span = norm_span; a.eps = eps;
   return from_cuda(h3::launch_adaln_rms_rope(a, S(stream)), "adaln_rms_rope");
+}
+
+int h3b200_adaln_rms_rope_segmented(const void* q, int64_t ldq, const void* k, int64_t ldk, void* q_out,
+                                    int64_t ldqo, void* k_out, int64_t ldko, const float* freqs,
+                                    const void* q_weight, const void* k_weight, const void* scale,
+                                    int64_t ld_scale, const void* shift, int64_t ld_shift, int64_t mod_rows,
+                                    const int32_t* row_map, int64_t tokens_per_row, int64_t m, int64_t heads,
+                                    int64_t head_dim, int64_t rot_dim, float eps, h3b200_stream_t stream) {
+  H3_GUARD("adaln_rms_rope_segmented", stream);
+  if (m < 0 || heads <= 0 || head_dim <= 0) return fail(H3B200_ERR_INVALID, "adaln_rms_rope_segmented: bad shape");
+  const int64_t rot = rot_dim == 0 ? head_dim : rot_dim;
+  if (rot < 0 || rot > head_dim || rot % 2) return fail(H3B200_ERR_INVALID, "adaln_rms_rope_segmented: rot_dim %lld invalid for head_dim %lld", (long long)rot_dim, (long long)head_dim);
+  if (scale == nullptr || shift == nullptr || mod_rows < 1) return fail(H3B200_ERR_INVALID, "adaln_rms_rope_segmented: scale, shift and mod_rows >= 1 are required");
+  const int64_t w = heads * head_dim;
+  if (ld_scale < w || ld_shift < w) return fail(H3B200_ERR_INVALID, "adaln_rms_rope_segmented: modulation row strides must be >= heads * head_dim");
+  if (ldq < w || ldk < w || ldqo < w || ldko < w) return fail(H3B200_ERR_INVALID, "adaln_rms_rope_segmented: token stride smaller than a row");
+  if (m == 0) return H3B200_OK;
+  h3::NormRopeArgs a;
+  a.q = q; a.k = k; a.q_out = q_out; a.k_out = k_out; a.ldq = ldq; a.ldk = ldk; a.ldqo = ldqo; a.ldko = ldko;
+  a.freqs = freqs; a.q_weight = q_weight; a.k_weight = k_weight; a.scale = scale; a.shift = shift;
+  a.row_map = row_map; a.tokens_per_row = tokens_per_row; a.mod_rows = mod_rows; a.lds = ld_scale; a.ldh = ld_shift;
+  a.m = m; a.heads = heads; a.head_dim = head_dim; a.rot_dim = rot; a.norm_span = 0; a.eps = eps;
+  return from_cuda(h3::launch_adaln_rms_rope(a, S(stream)), "adaln_rms_rope_segmented");
 }
 
 int h3b200_qknorm_rope_strided(const void* q, int64_t q_st, int64_t q_sh, void* q_out, int64_t qo_st,

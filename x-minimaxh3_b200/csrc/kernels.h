@@ -94,6 +94,11 @@ struct NormRopeArgs {
   const void* k_weight = nullptr;
   const void* scale = nullptr;
   const void* shift = nullptr;
+  // Per-token modulation rows (row span only): with row_map (int32 [m]), tokens_per_row > 0 or
+  // mod_rows > 1, token t uses row row_map[t] (clamped) or t / tokens_per_row of scale / shift
+  // at row strides lds / ldh; otherwise scale / shift are one row.
+  const int32_t* row_map = nullptr;
+  int64_t tokens_per_row = 0, mod_rows = 1, lds = 0, ldh = 0;
   int64_t m = 0, heads = 0, head_dim = 0, rot_dim = 0;
   int norm_span = 0;
   float eps = 1e-6f;
@@ -142,6 +147,27 @@ int num_sms(int device);
 cudaError_t ensure_gelu_table(cudaStream_t stream);
 // The same for the table of `act` (GELU or SiLU; no-op for other codes).
 cudaError_t ensure_act_table(int act, cudaStream_t stream);
+
+// Standalone RMS-AdaLN (adaln.cu): y = bf16(bf16(bf16((x * rstd) * w) * bf16(1 + scale[r])) + shift[r]),
+// r = row_map[t] (clamped to [0, rows)), else t / tokens_per_row (<= 0: 0). weight may be nullptr
+// (no affine weight); scale == shift == nullptr is a plain RMSNorm. y may alias x.
+struct RmsAdalnArgs {
+  const void* x = nullptr;
+  int64_t ldx = 0;
+  void* y = nullptr;
+  int64_t ldy = 0;
+  const void* weight = nullptr;
+  const void* scale = nullptr;
+  int64_t lds = 0;
+  const void* shift = nullptr;
+  int64_t ldh = 0;
+  const int32_t* row_map = nullptr;
+  int64_t tokens_per_row = 0;
+  int64_t rows = 0;
+  int64_t m = 0, d = 0;
+  float eps = 1e-6f;
+};
+cudaError_t launch_rms_adaln(const RmsAdalnArgs& a, cudaStream_t stream);
 // y[m, k] = silu(x[:, :k]) * x[:, k:2k] per row (bf16)
 cudaError_t launch_swiglu_rows(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t m, int64_t k,
                                cudaStream_t stream);

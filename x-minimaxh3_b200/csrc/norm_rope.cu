@@ -46,6 +46,7 @@
 // predicates.
 #include "common.cuh"
 #include "kernels.h"
+#include "norm_math.cuh"
 
 namespace h3 {
 namespace {
@@ -64,6 +65,10 @@ struct NRParams {
   const float* freqs;
   const __nv_bfloat16* scale;
   const __nv_bfloat16* shift;
+  // per-token modulation rows (MOD == 2): row_map[t] (clamped to [0, mod_rows)), else
+  // t / tokens_per_row (<= 0: row 0); row strides lds / ldh elements
+  const int32_t* row_map;
+  int64_t tokens_per_row, mod_rows, lds, ldh;
   int64_t m;
   int heads;
   int half_v;     // rot_dim / 16: vectors in each rotation half
@@ -104,49 +109,6 @@ __device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) {
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(w << 16), "r"(w & 0xFFFF0000u));
   return r;
 }
-__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-// |bf16| of the low / high half of w as a double: exponent rebiased by
-// 1023 - 127 = 896, mantissa moved to the top of the double's fraction.
-__device__ __forceinline__ double abs_lo_as_double(uint32_t w) {
-  return __hiloint2double((int)(((w & 0x7FFFu) << 13) + 0x38000000u), 0);
-}
-__device__ __forceinline__ double abs_hi_as_double(uint32_t w) {
-  return __hiloint2double((int)(((w >> 3) & 0x0FFFE000u) + 0x38000000u), 0);
-}
-
-// sum of squares of the 8 bf16 values of v (fast: integer-built doubles)
-__device__ __forceinline__ void sumsq8_fast(const uint4& v, double (&acc)[4]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const double a = abs_lo_as_double(w[e]);
-    const double b = abs_hi_as_double(w[e]);
-    acc[e] = fma(a, a, acc[e]);
-    acc[e] = fma(b, b, acc[e]);
-  }
-}
-// the same with exact conversions (inf / NaN aware)
-__device__ __forceinline__ void sumsq8_exact(const uint4& v, double (&acc)[4]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const double a = (double)bf16_lo(w[e]);
-    const double b = (double)bf16_hi(w[e]);
-    acc[e] = fma(a, a, acc[e]);
-    acc[e] = fma(b, b, acc[e]);
-  }
-}
-
 // ---- bulk copy global -> shared, completion counted on an mbarrier ---------
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -157,7 +119,9 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
 }
 
 // EXACT: heads * 16 == 32 * VPL, every lane's VPL vectors exist (no predicates).
-template <int VPL, bool ROW_SPAN, bool MODULATE, bool FULL_ROT, bool EXACT>
+// MOD: 0 no modulation, 1 one row (bf16(1 + scale) and shift staged in shared
+// memory), 2 a row per token (read through the read-only L1 path).
+template <int VPL, bool ROW_SPAN, int MOD, bool FULL_ROT, bool EXACT>
 __global__ void __launch_bounds__(kNRThreads, 1)
     adaln_rms_rope_kernel(const __grid_constant__ CUtensorMap tm_table, const NRParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -168,8 +132,9 @@ __global__ void __launch_bounds__(kNRThreads, 1)
   uint64_t* empty_bar = full_bar + kMaxStages;
   // ROW_SPAN: fp32 weights of Q (wf[0, nvec)) and K (wf[nvec, 2 nvec)), 8 per vector
   float4* wf = reinterpret_cast<float4*>(smem + 256);
-  uint4* m_s = reinterpret_cast<uint4*>(wf + (ROW_SPAN ? 4 : 0) * nvec);  // MODULATE: bf16(1 + scale)
-  uint4* sh_s = m_s + nvec;                                                 // MODULATE: shift
+  constexpr bool MODULATE = MOD != 0;
+  uint4* m_s = reinterpret_cast<uint4*>(wf + (ROW_SPAN ? 4 : 0) * nvec);  // MOD 1: bf16(1 + scale)
+  uint4* sh_s = m_s + nvec;                                                 // MOD 1: shift
   uint8_t* ring = smem + p.ring_off;
   const int stage_bytes = p.stage_bytes;
 
@@ -195,7 +160,7 @@ __global__ void __launch_bounds__(kNRThreads, 1)
         wf[(t * nvec + i) * 2 + 1] = make_float4(bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w));
       }
     }
-    if (MODULATE) {
+    if (MOD == 1) {
       const uint4 sc = ldg_nc_v4(p.scale + 8 * i);
       const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sc);
       uint4 mv;
@@ -324,6 +289,15 @@ __global__ void __launch_bounds__(kNRThreads, 1)
     // ---- normalise, modulate, rotate, store ----
     const int64_t tok = blockIdx.x + j * G;
     __nv_bfloat16* yr = ybase + tok * ldy;
+    const __nv_bfloat16* scr = nullptr;
+    const __nv_bfloat16* shr = nullptr;
+    if (MOD == 2) {
+      int64_t r = p.row_map != nullptr ? (int64_t)__ldg(p.row_map + tok)
+                                       : (p.tokens_per_row > 0 ? tok / p.tokens_per_row : 0);
+      r = r < 0 ? 0 : (r >= p.mod_rows ? p.mod_rows - 1 : r);  // rows outside the table are clamped
+      scr = p.scale + r * p.lds;
+      shr = p.shift + r * p.ldh;
+    }
 #pragma unroll
     for (int jj = 0; jj < VPL; ++jj) {
       const int vi = lane + 32 * jj;
@@ -341,9 +315,14 @@ __global__ void __launch_bounds__(kNRThreads, 1)
         wpair[2] = bf16x2_to_f2(whead.z); wpair[3] = bf16x2_to_f2(whead.w);
       }
       uint4 mv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
-      if (MODULATE) {
+      if (MOD == 1) {
         mv = m_s[vc];
         sv = sh_s[vc];
+      } else if (MOD == 2) {
+        const uint4 sc = ldg_nc_v4(scr + 8 * vc);
+        mv = make_uint4(bf2_add(sc.x, 0x3F803F80u), bf2_add(sc.y, 0x3F803F80u), bf2_add(sc.z, 0x3F803F80u),
+                        bf2_add(sc.w, 0x3F803F80u));  // bf16(1 + scale)
+        sv = ldg_nc_v4(shr + 8 * vc);
       }
       const uint4 xv = xs[vc];
       const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
@@ -379,7 +358,7 @@ int ring_offset(int nvec, bool row, bool mod) {
   return (256 + cst_bytes + 1023) & ~1023;
 }
 
-template <int VPL, bool ROW, bool MOD, bool FULL, bool EXACT>
+template <int VPL, bool ROW, int MOD, bool FULL, bool EXACT>
 cudaError_t launch_one(const CUtensorMap& tm, const NRParams& p, int smem, cudaStream_t st) {
   auto kern = adaln_rms_rope_kernel<VPL, ROW, MOD, FULL, EXACT>;
   static bool attr_set[64] = {false};
@@ -399,11 +378,11 @@ template <int VPL, bool EXACT>
 cudaError_t launch_vpl(const CUtensorMap& tm, const NRParams& p, bool row, bool mod, bool full, int smem,
                        cudaStream_t st) {
   if (row) {
-    if (mod) return full ? launch_one<VPL, true, true, true, EXACT>(tm, p, smem, st) : launch_one<VPL, true, true, false, EXACT>(tm, p, smem, st);
-    return full ? launch_one<VPL, true, false, true, EXACT>(tm, p, smem, st) : launch_one<VPL, true, false, false, EXACT>(tm, p, smem, st);
+    if (mod) return full ? launch_one<VPL, true, 1, true, EXACT>(tm, p, smem, st) : launch_one<VPL, true, 1, false, EXACT>(tm, p, smem, st);
+    return full ? launch_one<VPL, true, 0, true, EXACT>(tm, p, smem, st) : launch_one<VPL, true, 0, false, EXACT>(tm, p, smem, st);
   }
-  if (mod) return full ? launch_one<VPL, false, true, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, true, false, EXACT>(tm, p, smem, st);
-  return full ? launch_one<VPL, false, false, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, false, false, EXACT>(tm, p, smem, st);
+  if (mod) return full ? launch_one<VPL, false, 1, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, 1, false, EXACT>(tm, p, smem, st);
+  return full ? launch_one<VPL, false, 0, true, EXACT>(tm, p, smem, st) : launch_one<VPL, false, 0, false, EXACT>(tm, p, smem, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -743,6 +722,11 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   if (mod && (a.shift == nullptr || (reinterpret_cast<uintptr_t>(a.scale) & 15) ||
               (reinterpret_cast<uintptr_t>(a.shift) & 15)))
     return cudaErrorNotSupported;
+  // a modulation row per token (row map or token groups): row span only, rows read through L1
+  const bool mod_rows = mod && (a.row_map != nullptr || a.tokens_per_row > 0 || a.mod_rows > 1);
+  if (mod_rows && (a.norm_span != 0 || a.mod_rows < 1 || a.lds % 8 || a.ldh % 8 ||
+                   a.lds < a.heads * a.head_dim || a.ldh < a.heads * a.head_dim))
+    return cudaErrorNotSupported;
   NRParams p;
   p.x[0] = static_cast<const __nv_bfloat16*>(a.q);
   p.x[1] = static_cast<const __nv_bfloat16*>(a.k);
@@ -757,6 +741,11 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   p.freqs = a.freqs;
   p.scale = static_cast<const __nv_bfloat16*>(a.scale);
   p.shift = static_cast<const __nv_bfloat16*>(a.shift);
+  p.row_map = a.row_map;
+  p.tokens_per_row = a.tokens_per_row;
+  p.mod_rows = a.mod_rows < 1 ? 1 : a.mod_rows;
+  p.lds = a.lds;
+  p.ldh = a.ldh;
   p.m = a.m;
   p.heads = (int)a.heads;
   p.half_v = (int)(rot / 16);
@@ -768,7 +757,7 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
   const int nvec = (int)(a.heads * 16);
   p.tab_off = (2 * p.row_bytes + 1023) & ~1023;
   p.stage_bytes = (p.tab_off + p.nseg * 128 + 1023) & ~1023;
-  p.ring_off = ring_offset(nvec, row, mod);
+  p.ring_off = ring_offset(nvec, row, mod && !mod_rows);
   // deepest ring (a multiple of the pair count, so each stage always serves the same pair) that fits
   int stages = 0;
   for (int s = kMaxStages; s >= kPairs; s -= kPairs)
@@ -786,6 +775,11 @@ cudaError_t launch_adaln_rms_rope(const NormRopeArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const bool full = rot == 128;
   const int vpl = (int)((a.heads * 16 + 31) / 32);
+  if (mod_rows) {
+    if (a.heads == 24)
+      return full ? launch_one<12, true, 2, true, true>(tm, p, smem, stream) : launch_one<12, true, 2, false, true>(tm, p, smem, stream);
+    return full ? launch_one<16, true, 2, true, false>(tm, p, smem, stream) : launch_one<16, true, 2, false, false>(tm, p, smem, stream);
+  }
   if (a.heads == 24) return launch_vpl<12, true>(tm, p, row, mod, full, smem, stream);  // 3072-wide rows
   if (vpl <= 4) return launch_vpl<4, false>(tm, p, row, mod, full, smem, stream);
   if (vpl <= 8) return launch_vpl<8, false>(tm, p, row, mod, full, smem, stream);

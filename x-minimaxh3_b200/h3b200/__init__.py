@@ -28,6 +28,8 @@ from .ops import (  # noqa: F401
     quantize_int8_rowwise,
     quantize_int8_rowwise_absmax,
     quantize_int8_rowwise_convrot,
+    rms_adaln,
+    rms_adaln_segmented,
     rms_rope_split_half,
     rms_rope_split_half_,
     qknorm_rope_strided_,

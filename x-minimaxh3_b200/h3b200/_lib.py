@@ -47,6 +47,11 @@ SIGNATURES = {
     "h3b200_fused_gated_mlp_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "h3b200_fused_gated_mlp": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32,
                                       _p, _i64, _p]),
+    "h3b200_fused_gated_mlp_segmented": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _i64, _p, _i64, _i64,
+                                                _i64, _i64, _i32, _p, _i64, _p]),
+    "h3b200_rms_adaln": (_i32, [_p, _i64, _p, _p, _i64, _p, _i64, _i64, _p, _i64, _f32, _p, _i64, _i64, _i64, _p]),
+    "h3b200_adaln_rms_rope_segmented": (_i32, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _p, _i64, _p,
+                                               _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _f32, _p]),
     "h3b200_adaln_rms_rope": (_i32, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                      _i64, _i32, _f32, _p]),
     "h3b200_dequant_int4_grouped_to_int8": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p]),

@@ -29,6 +29,8 @@ __all__ = [
     "fused_gated_mlp_swiglu_w4a8",
     "adaln_rms_rope",
     "adaln_rms_rope_",
+    "rms_adaln",
+    "rms_adaln_segmented",
     "rms_rope_split_half",
     "rms_rope_split_half_",
     "qknorm_rope_strided_",
@@ -294,12 +296,16 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
 
 def fused_gated_mlp(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Tensor, s1: torch.Tensor,
                     w2q: torch.Tensor, s2: torch.Tensor, gate: torch.Tensor, act: str = "gelu_tanh",
-                    out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                    out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                    segments=None) -> torch.Tensor:
     """``residual + int8_linear(act(int8_linear(hidden, w1q, s1)), w2q, s2) * gate`` in one launch chain.
 
     Drop-in for ``try_fused_gated_mlp`` (h3serve/native_engine/model/fused_mlp.py:269-426;
-    composition :393-425) with one modulation row (``gate`` [d]) and the tanh-GELU
-    activation. ``out`` may be ``residual`` (in-place ``addcmul_``)."""
+    composition :393-425) with the tanh-GELU activation. ``gate`` is one modulation row [d],
+    or with ``segments`` (``(start, stop, row)`` runs partitioning the tokens, the reference's
+    modulation segments, ``_segment_row_map`` :34-55) rows [rows, d]: token t is gated by
+    ``gate[row of t]`` (the per-segment ``addcmul_``, layers.py:937-953). ``out`` may be
+    ``residual`` (in-place ``addcmul_``)."""
     _need_cuda(residual, hidden, w1q, w2q, gate)
     if act != "gelu_tanh":
         raise NotImplementedError(f"fused_gated_mlp builds act='gelu_tanh' only, got {act!r}")
@@ -314,9 +320,7 @@ def fused_gated_mlp(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Ten
         raise ValueError(f"weights must be w1 [ffn, d] and w2 [d, ffn], got {tuple(w1q.shape)} and {tuple(w2q.shape)}")
     if r2.shape != x2.shape:
         raise ValueError("residual and hidden must have the same shape")
-    g = gate.reshape(-1).contiguous()
-    if g.numel() != d:
-        raise ValueError(f"gate must have {d} elements (one modulation row)")
+    g, row_map, ldg = _gate_rows(gate, segments, m, d, hidden.device)
     ws1 = _weight_scale(s1, ffn, hidden.device)
     ws2 = _weight_scale(s2, d, hidden.device)
     if ws1.numel() != ffn or ws2.numel() != d:
@@ -327,9 +331,15 @@ def fused_gated_mlp(residual: torch.Tensor, hidden: torch.Tensor, w1q: torch.Ten
     nbytes = int(_lib.load().h3b200_fused_gated_mlp_workspace_bytes(m, d, ffn))
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
-    _lib.call("h3b200_fused_gated_mlp", x2.data_ptr(), ldx, w1q.contiguous().data_ptr(), ws1.data_ptr(),
-              w2q.contiguous().data_ptr(), ws2.data_ptr(), g.data_ptr(), r2.data_ptr(), ldr, o2.data_ptr(), ldo,
-              m, d, ffn, _lib.ACT_GELU_TANH, workspace.data_ptr(), workspace.numel(), _stream(hidden))
+    if row_map is None:
+        _lib.call("h3b200_fused_gated_mlp", x2.data_ptr(), ldx, w1q.contiguous().data_ptr(), ws1.data_ptr(),
+                  w2q.contiguous().data_ptr(), ws2.data_ptr(), g.data_ptr(), r2.data_ptr(), ldr, o2.data_ptr(), ldo,
+                  m, d, ffn, _lib.ACT_GELU_TANH, workspace.data_ptr(), workspace.numel(), _stream(hidden))
+    else:
+        _lib.call("h3b200_fused_gated_mlp_segmented", x2.data_ptr(), ldx, w1q.contiguous().data_ptr(),
+                  ws1.data_ptr(), w2q.contiguous().data_ptr(), ws2.data_ptr(), g.data_ptr(), ldg, row_map.data_ptr(),
+                  r2.data_ptr(), ldr, o2.data_ptr(), ldo, m, d, ffn, _lib.ACT_GELU_TANH, workspace.data_ptr(),
+                  workspace.numel(), _stream(hidden))
     return out
 
 
@@ -403,15 +413,18 @@ def _freqs(freqs_cis: torch.Tensor, m: int, half: int) -> torch.Tensor:
 
 
 def adaln_rms_rope_(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=None, eps: float = 1e-6,
-                    norm_span: str = "row", rot_dim: int = 0, q_out=None, k_out=None):
+                    norm_span: str = "row", rot_dim: int = 0, q_out=None, k_out=None, segments=None):
     """Fused AdaLN-modulate + RMSNorm + split-half RoPE on Q and K, in place by default.
 
     ``norm_span="row"``: RMSNorm over heads*head_dim with [H*D] weights, then
     ``*(1 + scale)`` and ``+ shift`` (bf16 after each) -- the eager order of H3's
     ``rms_adaln`` (h3serve/native_engine/model/kernels.py:7586-7634) -- then
-    per-head split-half RoPE (eager/rope.py:39-42). ``norm_span="head"``:
-    per-head RMSNorm with [D] weights (``rms_rope_split_half``, eager/rope.py:67-143),
-    optional modulation after it. Returns (q_out, k_out)."""
+    per-head split-half RoPE (eager/rope.py:39-42). ``scale``/``shift`` are one row
+    [H*D], or with ``segments`` (``(start, stop, row)`` runs partitioning the tokens,
+    the reference's modulation segments) rows [rows, H*D] selected per token.
+    ``norm_span="head"``: per-head RMSNorm with [D] weights (``rms_rope_split_half``,
+    eager/rope.py:67-143), optional single-row modulation after it.
+    Returns (q_out, k_out)."""
     _need_cuda(q, k, freqs_cis, q_weight)
     if k_weight is None:
         k_weight = q_weight
@@ -441,10 +454,27 @@ def adaln_rms_rope_(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=
     if scale is not None or shift is not None:
         if scale is None or shift is None:
             raise ValueError("scale and shift must be given together")
+        if segments is not None:
+            if span != 0:
+                raise NotImplementedError("per-segment modulation is built for norm_span='row'")
+            sc = _mod_rows(scale, h * d, q.device, "scale")
+            sh = _mod_rows(shift, h * d, q.device, "shift")
+            row_map = segment_row_map(m, segments, q.device)
+            if m and max(int(r) for _, _, r in segments) >= min(sc.shape[0], sh.shape[0]):
+                raise ValueError("a segment names a modulation row outside scale/shift")
+            f = _freqs(freqs_cis, m, rd // 2)
+            _lib.call("h3b200_adaln_rms_rope_segmented", q3.data_ptr(), ldq, k3.data_ptr(), ldk, qo3.data_ptr(),
+                      ldqo, ko3.data_ptr(), ldko, f.data_ptr(), wq.data_ptr(), wk.data_ptr(), sc.data_ptr(),
+                      sc.stride(0) if sc.shape[0] > 1 else h * d, sh.data_ptr(),
+                      sh.stride(0) if sh.shape[0] > 1 else h * d, min(sc.shape[0], sh.shape[0]),
+                      row_map.data_ptr(), 0, m, h, d, rd, float(eps), _stream(q))
+            return q_out, k_out
         sc = scale.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
         sh = shift.to(device=q.device, dtype=torch.bfloat16).reshape(-1).contiguous()
         if sc.numel() != h * d or sh.numel() != h * d:
             raise ValueError(f"scale/shift must have {h * d} elements (one modulation row)")
+    elif segments is not None:
+        raise ValueError("segments need scale and shift")
     f = _freqs(freqs_cis, m, rd // 2)
     _lib.call("h3b200_adaln_rms_rope", q3.data_ptr(), ldq, k3.data_ptr(), ldk, qo3.data_ptr(), ldqo, ko3.data_ptr(),
               ldko, f.data_ptr(), wq.data_ptr(), wk.data_ptr(), _ptr(sc), _ptr(sh), m, h, d, rd, span, float(eps),
@@ -452,11 +482,118 @@ def adaln_rms_rope_(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=
     return q_out, k_out
 
 
+def _mod_rows(t, d: int, device, name: str) -> torch.Tensor:
+    """Modulation rows as bf16 [rows, d] with unit column stride (a strided row view is kept)."""
+    if t.shape[-1] != d:
+        raise ValueError(f"{name} must have {d} features in its last dimension, got {tuple(t.shape)}")
+    r = t.reshape(-1, d) if t.dim() != 2 else t
+    r = r.to(device=device, dtype=torch.bfloat16)
+    if r.stride(-1) != 1 or (r.shape[0] > 1 and (r.stride(0) < d or r.stride(0) % 8)) or r.data_ptr() % 16:
+        r = r.contiguous()
+    return r
+
+
+def _rms_adaln_launch(x2, ldx, weight, sc, sh, row_map, tokens_per_row, eps, out2, ldo):
+    m, d = x2.shape
+    lds = sc.stride(0) if sc is not None and sc.shape[0] > 1 else d
+    ldh = sh.stride(0) if sh is not None and sh.shape[0] > 1 else d
+    _lib.call("h3b200_rms_adaln", x2.data_ptr(), ldx, _ptr(weight), _ptr(sc), lds, _ptr(sh), ldh,
+              0 if sc is None else sc.shape[0], _ptr(row_map), int(tokens_per_row), float(eps), out2.data_ptr(),
+              ldo, m, d, _stream(x2))
+
+
+def rms_adaln(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """``rmsnorm(x) * (1 + scale) + shift`` without an affine weight, bf16 after each step.
+
+    comfy_kitchen ``rms_adaln(x, scale, shift, eps)`` (``__init__.py:130-150``; eager
+    ``backends/eager/adaln.py:17-20``). ``x`` bf16 ``[..., D]``; ``scale`` / ``shift`` bf16 and
+    broadcastable to ``x`` with a full last dimension D: one row ``[D]``, per-sample rows such as
+    ``[B, 1, D]``, or one row per token. Each token's modulation row is found from the broadcast
+    shape (a row map, or ``tokens_per_row`` for the per-sample case); nothing is expanded."""
+    _need_cuda(x, scale, shift)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("rms_adaln expects bf16 x")
+    if scale.dtype != torch.bfloat16 or shift.dtype != torch.bfloat16:
+        raise NotImplementedError("rms_adaln builds bf16 scale/shift (other dtypes promote the result in eager)")
+    d = x.shape[-1]
+    if scale.shape != shift.shape:
+        raise ValueError(f"scale {tuple(scale.shape)} and shift {tuple(shift.shape)} must have the same shape")
+    if scale.shape[-1] != d or scale.dim() > x.dim():
+        raise ValueError(f"scale/shift {tuple(scale.shape)} do not broadcast to x {tuple(x.shape)} with a full "
+                         "last dimension")
+    lead_x = tuple(x.shape[:-1])
+    lead_s = (1,) * (x.dim() - scale.dim()) + tuple(scale.shape[:-1])
+    for a, b in zip(lead_s, lead_x):
+        if a not in (1, b):
+            raise ValueError(f"scale/shift {tuple(scale.shape)} do not broadcast to x {tuple(x.shape)}")
+    x2, ldx = _rows(x)
+    n = x2.shape[0]
+    sc = _mod_rows(scale, d, x.device, "scale")
+    sh = _mod_rows(shift, d, x.device, "shift")
+    row_map, tpr = None, 0
+    rows = sc.shape[0]
+    if rows > 1:
+        # the dims scale/shift vary along: a contiguous run of leading 1s then full dims means one
+        # row per tokens_per_row tokens; anything else takes an explicit row map
+        varying = [i for i, a in enumerate(lead_s) if a != 1]
+        tail = 1
+        for b in lead_x[varying[-1] + 1:]:
+            tail *= b
+        if varying == list(range(varying[0], varying[-1] + 1)) and all(lead_s[i] == lead_x[i] for i in varying) \
+                and all(a == 1 for a in lead_s[:varying[0]]) and all(b == 1 for b in lead_x[:varying[0]]):
+            tpr = tail
+        else:
+            idx = torch.arange(rows, dtype=torch.int32, device=x.device).reshape(lead_s)
+            row_map = idx.expand(lead_x).reshape(-1).contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    o2, ldo = _rows(out)
+    _rms_adaln_launch(x2, ldx, None, sc, sh, row_map, tpr, eps, o2, ldo)
+    return out
+
+
+def rms_adaln_segmented(value: torch.Tensor, norm, shift: torch.Tensor, scale: torch.Tensor, segments,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """H3's ``rms_adaln(value, norm, shift, scale, segments)``
+    (h3serve/native_engine/model/kernels.py:7586-7634), same argument order.
+
+    ``hidden = norm(value)`` (``F.rms_norm`` with ``norm.weight`` cast to bf16 and ``norm.eps``;
+    ``norm=None`` or a norm without weight: no affine weight), then for every
+    ``(start, stop, row)`` segment ``hidden[start:stop].mul_(1.0 + scale[row].to(bf16))
+    .add_(shift[row].to(bf16))`` -- one pass over ``value`` [M, D] bf16. ``shift``/``scale`` are
+    [rows, D] (the strided views ``split_adaln`` returns are read in place when bf16). The segments
+    must partition ``[0, M)`` in order (same validation as the reference). ``out`` may be
+    ``value``."""
+    _need_cuda(value, shift, scale)
+    if value.dtype != torch.bfloat16 or value.dim() != 2:
+        raise ValueError("rms_adaln_segmented expects a 2-D bf16 value [tokens, hidden]")
+    m, d = value.shape
+    weight = getattr(norm, "weight", None) if norm is not None else None
+    eps = float(getattr(norm, "eps", 1e-6)) if norm is not None else 1e-6
+    w = None
+    if weight is not None:
+        w = weight.detach().to(device=value.device, dtype=torch.bfloat16).reshape(-1).contiguous()
+        if w.numel() != d:
+            raise ValueError(f"norm weight has {w.numel()} elements, value has {d} features")
+    sc = _mod_rows(scale, d, value.device, "scale")
+    sh = _mod_rows(shift, d, value.device, "shift")
+    row_map = segment_row_map(m, segments, value.device)
+    if m and int(max(r for _, _, r in segments)) >= min(sc.shape[0], sh.shape[0]):
+        raise ValueError("a segment names a modulation row outside scale/shift")
+    x2, ldx = _rows(value)
+    if out is None:
+        out = torch.empty_like(x2)
+    o2, ldo = _rows(out)
+    _rms_adaln_launch(x2, ldx, w, sc, sh, row_map, 0, eps, o2, ldo)
+    return out
+
+
 def adaln_rms_rope(q, k, freqs_cis, q_weight, k_weight=None, scale=None, shift=None, eps: float = 1e-6,
-                   norm_span: str = "row", rot_dim: int = 0):
+                   norm_span: str = "row", rot_dim: int = 0, segments=None):
     """Out-of-place variant of :func:`adaln_rms_rope_`."""
     return adaln_rms_rope_(q, k, freqs_cis, q_weight, k_weight, scale, shift, eps, norm_span, rot_dim,
-                           q_out=torch.empty_like(q), k_out=torch.empty_like(k))
+                           q_out=torch.empty_like(q), k_out=torch.empty_like(k), segments=segments)
 
 
 _TABLE_DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}   # eager/quantization.py:34-40
@@ -720,20 +857,38 @@ def quantize_int8_rowwise_convrot(x: torch.Tensor, convrot_groupsize: int = 256,
     return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
 
 
+_ROW_MAPS: dict = {}
+_ROW_MAPS_MAX = 64
+
+
 def segment_row_map(length: int, segments, device) -> torch.Tensor:
     """int32 [length]: the modulation row of each token, from ``(start, stop, row)`` segments
     that partition ``[0, length)`` in order (``_segment_row_map``,
-    h3serve/native_engine/model/fused_mlp.py:34-55, same validation)."""
+    h3serve/native_engine/model/fused_mlp.py:34-55, same validation).
+
+    A model calls this with the same few layouts in every block and step, so the device
+    maps are cached per (length, segments, device) and must not be written by callers."""
+    segs = tuple((int(a), int(b), int(r)) for a, b, r in segments)
+    key = (int(length), segs, str(torch.device(device)))
+    hit = _ROW_MAPS.get(key)
+    if hit is not None:
+        return hit
     host = torch.empty(length, dtype=torch.int32)
     previous = 0
-    for start, stop, row in ((int(a), int(b), int(r)) for a, b, r in segments):
+    for start, stop, row in segs:
         if start != previous or stop <= start:
             raise ValueError("modulation segments must be an ordered partition")
+        if row < 0:
+            raise ValueError("modulation rows must be non-negative")
         host[start:stop] = row
         previous = stop
     if previous != length:
         raise ValueError("modulation segments do not cover the packed sequence")
-    return host.to(device)
+    dev_map = host.to(device)
+    if len(_ROW_MAPS) >= _ROW_MAPS_MAX:
+        _ROW_MAPS.pop(next(iter(_ROW_MAPS)))
+    _ROW_MAPS[key] = dev_map
+    return dev_map
 
 
 def _gate_rows(gate: torch.Tensor, segments, m: int, d: int, device):
