@@ -59,6 +59,7 @@ __all__ = [
     "rope_grid_table",
     "build_hadamard",
     "rotate_activation",
+    "f64_to_bf16",
     "decode_int4_grouped_to_int8",
     "e4m3_to_f32",
     "w4a8_symmetric_linear",
@@ -86,8 +87,9 @@ def f32_to_bf16(f: np.ndarray) -> np.ndarray:
 
     Same rounding as torch's ``c10::BFloat16`` conversion (NaN -> 0x7FC0)."""
     f = np.ascontiguousarray(f, dtype=np.float32)
-    u = f.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    u = f.view(np.uint32)
+    # uint32 arithmetic: only NaN patterns (patched below) can wrap
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
     nan = np.isnan(f)
     if nan.any():
         r[nan] = 0x7FC0
@@ -480,19 +482,144 @@ def build_hadamard(size: int = 256) -> np.ndarray:
     return h / np.sqrt(size)
 
 
+def f64_to_bf16(y) -> np.ndarray:
+    """Round float64 values to bf16 (round-to-nearest-even, one rounding), uint16 patterns.
+
+    In the fp32 normal range the value is first rounded to fp32 with round-to-odd (the
+    dropped bits OR-ed into the last kept bit; 24 bits > 8 + 1, so the following
+    nearest-even rounding to bf16 is the correctly rounded one); other values take
+    exact integer arithmetic on the binary64 fields: 8 significant bits in the bf16
+    normal range, units of 2^-133 below it, inf on overflow, 0x7FC0 for NaN."""
+    y = np.ascontiguousarray(y, dtype=np.float64)
+    w = y.view(np.uint32).reshape(y.shape + (2,))       # little-endian halves: [..., 0] low, [..., 1] high
+    lo, hi = w[..., 0], w[..., 1]
+    ef = (hi >> np.uint32(20)) & np.uint32(0x7FF)
+    f32 = (hi & np.uint32(0x80000000)) | ((ef - np.uint32(896)) << np.uint32(23)) | \
+        ((hi & np.uint32(0xFFFFF)) << np.uint32(3)) | (lo >> np.uint32(29))
+    f32 |= ((lo & np.uint32((1 << 29) - 1)) != 0).astype(np.uint32)
+    out = f32_to_bf16(f32.view(np.float32))
+    slow = np.nonzero((ef < np.uint32(1023 - 126)) | (ef > np.uint32(1023 + 127)))
+    if slow[0].size:
+        out[slow] = _f64_to_bf16_general(y[slow])
+    return out
+
+
+def _f64_to_bf16_general(y) -> np.ndarray:
+    y = np.ascontiguousarray(y, dtype=np.float64)
+    u = y.view(np.uint64)
+    sign = ((u >> np.uint64(63)) << np.uint64(15)).astype(np.uint64)
+    ef = ((u >> np.uint64(52)) & np.uint64(0x7FF)).astype(np.int64)
+    frac = (u & np.uint64((1 << 52) - 1)).astype(np.uint64)
+    mfull = np.where(ef > 0, frac | np.uint64(1 << 52), frac)        # value = mfull * 2^(max(ef,1) - 1075)
+    e_unb = np.maximum(ef, 1) - 1075                                 # weight exponent of mfull's bit 0
+    top = np.frexp(mfull.astype(np.float64))[1].astype(np.int64) - 1   # exact: mfull < 2^53
+    top = np.where(mfull > 0, top, 0)
+    e_top = top + e_unb                                              # weight exponent of the leading bit
+    # bf16 keeps bits down to weight 2^(e_top - 7) (normal) or 2^-133 (subnormal)
+    keep_w = np.where(e_top >= -126, e_top - 7, -133)
+    shift = keep_w - e_unb                                           # bits of mfull dropped (can be <= 0)
+    # mfull < 2^53, so a drop of 54 or more bits leaves less than half a unit: zero
+    sh = np.clip(shift, 0, 54).astype(np.uint64)
+    q = np.where(shift >= 54, np.uint64(0), mfull >> sh)
+    rem = mfull & ((np.uint64(1) << sh) - np.uint64(1))
+    half = np.where(shift > 0, np.uint64(1) << np.clip(shift - 1, 0, 53).astype(np.uint64), np.uint64(0))
+    up = (shift > 0) & (shift < 54) & ((rem > half) | ((rem == half) & ((q & np.uint64(1)) == 1)))
+    q = np.where(shift < 0, mfull << np.clip(-shift, 0, 63).astype(np.uint64), q) + up.astype(np.uint64)
+    normal = e_top >= -126
+    e_out = np.where(normal & (q == 256), e_top + 1, e_top)
+    q = np.where(normal & (q == 256), np.uint64(128), q)
+    bits = np.where(normal, ((e_out + 127).astype(np.uint64) << np.uint64(7)) | (q & np.uint64(0x7F)), q)
+    bits = np.where(normal & (e_out + 127 >= 255), np.uint64(0x7F80), bits)
+    bits = np.where(mfull == 0, np.uint64(0), bits)
+    bits = np.where(ef == 0x7FF, np.uint64(0x7F80), bits)
+    r = (bits | sign).astype(np.uint16)
+    nan = np.isnan(y)
+    if nan.any():
+        r[nan] = 0x7FC0
+    return r
+
+
+def _bf16_from_fraction(v) -> int:
+    """Correctly rounded bf16 (RNE) of an exact rational value, as a bit pattern."""
+    from fractions import Fraction
+
+    if v == 0:
+        return 0
+    sign = 0x8000 if v < 0 else 0
+    a = -v if v < 0 else v
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    while Fraction(2) ** e > a:
+        e -= 1
+    while Fraction(2) ** (e + 1) <= a:
+        e += 1
+    lsb = e - 7 if e >= -126 else -133
+    scaled = a / Fraction(2) ** lsb
+    q, r = divmod(scaled.numerator, scaled.denominator)
+    r2 = 2 * r
+    if r2 > scaled.denominator or (r2 == scaled.denominator and q & 1):
+        q += 1
+    if e >= -126:
+        if q == 256:
+            q, e = 128, e + 1
+        if e + 127 >= 255:
+            return sign | 0x7F80
+        return sign | ((e + 127) << 7) | (q & 0x7F)
+    return sign | q
+
+
+def _rotate_group_exact(xg: np.ndarray) -> np.ndarray:
+    """Exact rotation of one 256-group (bf16 bit patterns) with IEEE rules for inf / NaN."""
+    from fractions import Fraction
+
+    f = bf16_to_f32(xg).astype(np.float64)
+    n = f.shape[0]
+    h = np.sign(build_hadamard(n)).astype(np.int64)
+    out = np.zeros(n, np.uint16)
+    if np.isnan(f).any():
+        out[:] = 0x7FC0
+        return out
+    fin = np.isfinite(f)
+    vals = [Fraction(float(v)) for v in np.where(fin, f, 0.0)]
+    for j in range(n):
+        col = h[:, j]
+        pinf = bool(((f == np.inf) & (col > 0)).any() or ((f == -np.inf) & (col < 0)).any())
+        ninf = bool(((f == np.inf) & (col < 0)).any() or ((f == -np.inf) & (col > 0)).any())
+        if pinf or ninf:
+            out[j] = 0x7FC0 if (pinf and ninf) else (0x7F80 if pinf else 0xFF80)
+            continue
+        tot = sum((vals[i] if col[i] > 0 else -vals[i]) for i in range(n) if fin[i] and f[i] != 0)
+        out[j] = _bf16_from_fraction(Fraction(tot) / int(round(n ** 0.5)))   # H = H4^(x)k / sqrt(n), n a power of 4
+    return out
+
+
 def rotate_activation(x_bf16, group_size: int = 256) -> np.ndarray:
     """ConvRot online rotation ``x_grouped @ H`` per group, bf16 out (tensor/int8_utils.py:58-74).
 
-    The reference runs a bf16 matmul with fp32 accumulation; the oracle forms the
-    exact sum in float64 and rounds to fp32 then bf16, so last-bit differences
-    against the reference are possible and checked under tolerance."""
-    x = bf16_to_f32(x_bf16).astype(np.float64)
-    k = x.shape[-1]
+    The reference runs a bf16 matmul with fp32 accumulation in its BLAS order; the
+    oracle defines the rotation as the correctly rounded bf16 of the exact sum
+    ``sum_i x_i H[i][j]`` (H = H4^(x)4 / 16), which is what the reference's fp32 sums
+    approximate. Groups whose float64 sums are exact (exponent spread of the nonzero
+    inputs at most 37 bits, |x| < 2^124, finite) are summed in float64 and rounded once;
+    the rest are summed exactly with rationals."""
+    xb = np.ascontiguousarray(np.asarray(x_bf16, np.uint16))
+    k = xb.shape[-1]
     if k % group_size:
         raise ValueError(f"features {k} not divisible by group_size {group_size}")
+    g = xb.reshape(-1, group_size)
+    x = bf16_to_f32(g).astype(np.float64)
     hm = build_hadamard(group_size)
-    y = (x.reshape(-1, k // group_size, group_size) @ hm).reshape(x.shape)
-    return f32_to_bf16(y.astype(np.float32))
+    y = f64_to_bf16(x @ hm)
+    a = (g & 0x7FFF).astype(np.int64)
+    fld = a >> 7
+    fmax = fld.max(axis=1)
+    nz = a != 0
+    fmin = np.where(nz, np.maximum(fld, 1), 1 << 20).min(axis=1)
+    fmin = np.where(nz.any(axis=1), fmin, fmax)
+    exact = (a.max(axis=1) < 0x7D80) & (fmax - np.maximum(fmin, 1) <= 37)
+    exact |= ~nz.any(axis=1)
+    for r in np.nonzero(~exact)[0]:
+        y[r] = _rotate_group_exact(g[r])
+    return y.reshape(xb.shape)
 
 
 def e4m3_to_f32(bits_u8) -> np.ndarray:

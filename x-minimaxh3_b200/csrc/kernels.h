@@ -129,8 +129,10 @@ cudaError_t launch_copy_heads(const void* x, int64_t xs_t, int64_t xs_h, void* y
 // int4 -> int8 grid; s_rel fp32 or (s_rel_e4m3) fp8-e4m3 bytes; codebook: 16 fp32 levels or nullptr (u - 8)
 cudaError_t launch_dequant_int4(const int8_t* qdata, const void* s_rel, bool s_rel_e4m3, const float* codebook,
                                 int64_t n, int64_t k, int64_t group, int8_t* out, cudaStream_t stream);
-// ConvRot-256 + row quantization; with sx != nullptr also writes the correction
-// operand sx (bf16 [m, kp], zero beyond k / sum_group).
+// ConvRot-256 + row quantization with the rotation correctly rounded (convrot.cu);
+// with sx != nullptr also writes the correction operand sx (bf16 [m, kp], zero
+// beyond k / sum_group). k a multiple of 256, at most convrot_max_k(act).
+int64_t convrot_max_k(int act);
 cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64_t k, int act, int8_t* q,
                                     float* scale, void* sx, int64_t sum_group, int64_t kp, cudaStream_t stream);
 // corr_t[n, kp] (bf16) = correction[g, n] transposed, zero for g >= groups

@@ -1,7 +1,7 @@
-// W4A8 pieces: int4 -> int8 grid decode, ConvRot-256 rotation + row
-// quantization (emitting the asymmetric-correction operand
-// sx[m, g] = bf16(bf16(sum_{k in g} q) * bf16(xs))), and the transposed,
-// zero-padded correction matrix. The correction itself, out += sx . corr, is
+// W4A8 pieces: int4 -> int8 grid decode and the transposed, zero-padded
+// correction matrix (the ConvRot-256 activation quantizer, which also emits the
+// asymmetric-correction operand sx[m, g] = bf16(bf16(sum_{k in g} q) * bf16(xs)),
+// is in convrot.cu). The correction itself, out += sx . corr, is
 // accumulated on the tensor cores inside the INT8 GEMM's epilogue (gemm_i8.cu,
 // kEpi*Corr).
 //
@@ -180,166 +180,6 @@ __global__ void dequant_int4_scalar_kernel(const uint8_t* __restrict__ qd, const
   out[idx] = (int8_t)decode_one(level, group_scale<E4M3>(s_rel, row * (k / group) + col / group));
 }
 
-// ---------------------------------------------------------------------------
-// ConvRot-256 + row quantization. One CTA per row; each half-warp rotates one
-// 256-group, lane li holding elements 16 li .. 16 li + 15. The regular Hadamard
-// H4^(x)4 acts on the four base-4 digits of the in-group index independently
-// (y_j = S - 2 v_(3-j), S the sum of the four values on that digit's axis;
-// S - 2 v is one fused multiply-add, exact in its product since 2 v is):
-// digits 0-1 are lane-local; a transpose through shared memory (each lane then
-// holds indices li + 16 e) makes digits 2-3 lane-local. The sums are formed in
-// the fixed order (v0 + v1) + (v2 + v3); the 1/16 normalisation is exact. The
-// rotated value is rounded to bf16 (the reference's bf16 rotation matmul
-// output); once the row absmax is known a second transpose restores the
-// contiguous order and the row is quantized exactly like quantize_int8_rowwise,
-// with 16-byte stores. The optional correction operand is
-// sx[row, g] = bf16(bf16(sum of the int8 over group g) * bf16(xs)).
-// Shared memory per warp: 16 rows x 32 floats; half h's 16 values of row r sit
-// in 16-byte chunk (4 h + c) ^ (r & 7) of the row, so row-wise 16-byte accesses
-// and column-wise 4-byte accesses are both free of bank conflicts.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void h4_digit_lo(float (&v)[16]) {  // digit over index bits 0-1
-#pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    const float s = __fadd_rn(__fadd_rn(v[4 * a], v[4 * a + 1]), __fadd_rn(v[4 * a + 2], v[4 * a + 3]));
-    const float t0 = __fmaf_rn(-2.0f, v[4 * a + 3], s), t1 = __fmaf_rn(-2.0f, v[4 * a + 2], s);
-    const float t2 = __fmaf_rn(-2.0f, v[4 * a + 1], s), t3 = __fmaf_rn(-2.0f, v[4 * a], s);
-    v[4 * a] = t0; v[4 * a + 1] = t1; v[4 * a + 2] = t2; v[4 * a + 3] = t3;
-  }
-}
-__device__ __forceinline__ void h4_digit_hi(float (&v)[16]) {  // digit over index bits 2-3
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const float s = __fadd_rn(__fadd_rn(v[b], v[4 + b]), __fadd_rn(v[8 + b], v[12 + b]));
-    const float t0 = __fmaf_rn(-2.0f, v[12 + b], s), t1 = __fmaf_rn(-2.0f, v[8 + b], s);
-    const float t2 = __fmaf_rn(-2.0f, v[4 + b], s), t3 = __fmaf_rn(-2.0f, v[b], s);
-    v[b] = t0; v[4 + b] = t1; v[8 + b] = t2; v[12 + b] = t3;
-  }
-}
-// word address (floats) of (row r, value c) of half h in a warp's transpose tile
-__device__ __forceinline__ int tr_addr(int r, int h, int c) {
-  return r * 32 + ((((h << 2) + (c >> 2)) ^ (r & 7)) << 2) + (c & 3);
-}
-
-constexpr int kCvThreadsMax = 256;
-
-template <int PPW>
-__global__ void __launch_bounds__(kCvThreadsMax) quantize_convrot_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                         int64_t ldx, int64_t m, int64_t k, int act,
-                                                                         int8_t* __restrict__ q,
-                                                                         float* __restrict__ scale,
-                                                                         __nv_bfloat16* __restrict__ sx,
-                                                                         int64_t sum_group, int64_t kp) {
-  __shared__ __align__(16) float tile[kCvThreadsMax / 32][16 * 32];
-  __shared__ float red[kCvThreadsMax / 32];
-  const int64_t row = blockIdx.x;
-  if (row >= m) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  const int h = lane >> 4, li = lane & 15;
-  const int ngroups = (int)(k / 256);
-  float* tw = tile[warp];
-  uint32_t vals[PPW][8];  // rotated bf16 pairs, transposed order: lane holds indices li + 16 e
-  uint32_t amax_bits = 0u;
-#pragma unroll
-  for (int t = 0; t < PPW; ++t) {
-    const int g = 2 * (warp + nwarps * t) + h;
-    const bool ok = g < ngroups;
-    float v[16];
-    uint4 raw[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    if (ok) {
-      const __nv_bfloat16* src = x + row * ldx + (int64_t)g * 256 + 16 * li;
-      raw[0] = ldg_nc_v4(src);
-      raw[1] = ldg_nc_v4(src + 8);
-      if (act == H3B200_ACT_SWIGLU) {  // [gate | up] raw row: silu(gate) * up, exact bf16
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const uint4 u = ldg_nc_v4(src + k + 8 * hh);
-          raw[hh] = make_uint4(swiglu_bf16x2(raw[hh].x, u.x), swiglu_bf16x2(raw[hh].y, u.y),
-                               swiglu_bf16x2(raw[hh].z, u.z), swiglu_bf16x2(raw[hh].w, u.w));
-        }
-      }
-    }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      uint32_t w[4] = {raw[hh].x, raw[hh].y, raw[hh].z, raw[hh].w};
-      if (act == H3B200_ACT_GELU_TANH) {  // exact bf16 GELU from the device table
-#pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = gelu_bf16_bits(w[e]) | (gelu_bf16_bits(w[e] >> 16) << 16);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        v[8 * hh + 2 * e] = bf16_lo(w[e]);
-        v[8 * hh + 2 * e + 1] = bf16_hi(w[e]);
-      }
-    }
-    h4_digit_lo(v);
-    h4_digit_hi(v);
-    // transpose: write row li (16-byte chunks), read column li
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<float4*>(tw + tr_addr(li, h, 4 * c)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < 16; ++e) v[e] = tw[tr_addr(e, h, li)];
-    __syncwarp();
-    h4_digit_lo(v);
-    h4_digit_hi(v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const uint32_t pb = pack_bf16(v[2 * e] * 0.0625f, v[2 * e + 1] * 0.0625f);
-      vals[t][e] = pb;
-      if (ok) amax_bits = __vmaxu2(amax_bits, pb & 0x7FFF7FFFu);  // per-half running max of |bf16|
-    }
-  }
-  amax_bits = max(amax_bits & 0xFFFFu, amax_bits >> 16);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax_bits = max(amax_bits, __shfl_xor_sync(0xffffffffu, amax_bits, o));
-  if (lane == 0) red[warp] = __uint_as_float(amax_bits << 16);
-  __syncthreads();
-  float rowmax = red[0];
-  for (int i = 1; i < nwarps; ++i) rowmax = fmaxf(rowmax, red[i]);
-  const float s = fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f);
-  const float sb = quant_divisor(s);
-  const float rcp = __frcp_rn(sb);
-  const int lanes_per_sum = (int)(sum_group / 16);
-#pragma unroll
-  for (int t = 0; t < PPW; ++t) {
-    const int g = 2 * (warp + nwarps * t) + h;
-    // back to contiguous order: write column li, read row li
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      tw[tr_addr(2 * e, h, li)] = bf16_lo(vals[t][e]);
-      tw[tr_addr(2 * e + 1, h, li)] = bf16_hi(vals[t][e]);
-    }
-    __syncwarp();
-    uint32_t pw[8];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float4 f = *reinterpret_cast<const float4*>(tw + tr_addr(li, h, 4 * c));
-      pw[2 * c] = pack_bf16(f.x, f.y);
-      pw[2 * c + 1] = pack_bf16(f.z, f.w);
-    }
-    __syncwarp();
-    const bool ok = g < ngroups;  // the same for the 16 lanes of a half-warp
-    const uint2 q0 = quant_vec8(make_uint4(pw[0], pw[1], pw[2], pw[3]), rcp);
-    const uint2 q1 = quant_vec8(make_uint4(pw[4], pw[5], pw[6], pw[7]), rcp);
-    if (ok) *reinterpret_cast<uint4*>(q + row * k + (int64_t)g * 256 + 16 * li) = make_uint4(q0.x, q0.y, q1.x, q1.y);
-    if (sx != nullptr) {  // all lanes shuffle; partners stay inside the half-warp (offsets < 16)
-      int isum = __dp4a((int)q0.x, 0x01010101, __dp4a((int)q0.y, 0x01010101,
-                        __dp4a((int)q1.x, 0x01010101, __dp4a((int)q1.y, 0x01010101, 0))));
-      for (int o = 1; o < lanes_per_sum; o <<= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-      if (ok && (li % lanes_per_sum) == 0)
-        sx[row * kp + ((int64_t)g * 256 + 16 * li) / sum_group] =
-            __float2bfloat16_rn(__fmul_rn(bf16_round((float)isum), bf16_round(s)));
-    }
-  }
-  if (sx != nullptr) {  // zero the K padding of the correction operand
-    for (int64_t i = k / sum_group + threadIdx.x; i < kp; i += blockDim.x) sx[row * kp + i] = __float2bfloat16_rn(0.0f);
-  }
-  if (threadIdx.x == 0) scale[row] = s;
-}
-
 // corrT[n, kp] = correction[g, n] for g < groups, 0 for groups <= g < kp
 __global__ void correction_transpose_kernel(const __nv_bfloat16* __restrict__ corr, int64_t groups, int64_t n,
                                             int64_t kp, __nv_bfloat16* __restrict__ corr_t) {
@@ -347,324 +187,6 @@ __global__ void correction_transpose_kernel(const __nv_bfloat16* __restrict__ co
   if (i >= n * kp) return;
   const int64_t col = i / kp, g = i - col * kp;
   corr_t[i] = g < groups ? corr[g * n + col] : __float2bfloat16_rn(0.0f);
-}
-
-// ---------------------------------------------------------------------------
-// ConvRot-256 + row quantization, persistent, for rows of ng 256-groups (K = 256 ng,
-// ng <= 12 NP; NP = 1..4 covers K up to 12288). One CTA per SM: a producer warp streams rows into a
-// ring of one-row stages (cp.async.bulk, completion counted on mbarriers);
-// 12 consumer warps form 4 teams of 3, each team taking every 4th row of the
-// CTA, so that 4 rows are in flight at different points of their work. The
-// team's 6 half-warps take 2 NP group slots each (slots past ng hold zeros and are
-// never stored) and rotate them two at a time in
-// lock step (group a in the low, group b in the high half of packed f32x2
-// registers) with the butterflies, transposes and summation order of
-// quantize_convrot_kernel; the 1/16 normalisation is folded exactly into the
-// last butterfly ((s - 2 v) / 16 = fma(-1/8, v, s / 16), both scalings
-// exact). The rotated bf16 pairs wait (in registers for a single pair, else in
-// the lane's own slots of the stage) until the team's row absmax (met on an
-// mbarrier, bounded wait) is known. The
-// int8 values are then formed in the transposed order, stored byte by byte
-// into shared memory in natural order and written to HBM with 16-byte stores;
-// the correction operand sx is summed from those bytes as in
-// quantize_convrot_kernel.
-// ---------------------------------------------------------------------------
-constexpr int kCrConsumers = 12;
-constexpr int kCrTeamWarps = 3;
-constexpr int kCrTeams = kCrConsumers / kCrTeamWarps;
-constexpr int kCrMaxStages = 24;
-constexpr int kCrTileBytes = 2048;  // per consumer warp: float transpose tile / byte tile
-constexpr int kCrOffRed = 512;      // after the mbarriers
-constexpr int kCrOffTiles = 1024;
-constexpr int kCrOffRing = kCrOffTiles + kCrConsumers * kCrTileBytes;
-constexpr int kCrSmemLimit = 232448;
-constexpr unsigned kErrCrProducer = 0x301, kErrCrFull = 0x302, kErrCrTeam = 0x303, kErrCrDrain = 0x304;
-
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void sts_u8(void* p, uint32_t v) {
-  asm volatile("st.shared.u8 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
-}
-
-// The H4 butterflies of h4_digit_lo / h4_digit_hi on two groups at once. LAST:
-// the output is scaled by 1/16 (exact).
-template <bool LAST>
-__device__ __forceinline__ void h4x2_lo(uint64_t (&P)[16]) {
-  const uint64_t m2 = f2_dup(LAST ? -0.125f : -2.0f);
-#pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    uint64_t s = f2_add(f2_add(P[4 * a], P[4 * a + 1]), f2_add(P[4 * a + 2], P[4 * a + 3]));
-    if (LAST) s = f2_mul(s, f2_dup(0.0625f));
-    const uint64_t t0 = f2_fma(m2, P[4 * a + 3], s), t1 = f2_fma(m2, P[4 * a + 2], s);
-    const uint64_t t2 = f2_fma(m2, P[4 * a + 1], s), t3 = f2_fma(m2, P[4 * a], s);
-    P[4 * a] = t0; P[4 * a + 1] = t1; P[4 * a + 2] = t2; P[4 * a + 3] = t3;
-  }
-}
-template <bool LAST>
-__device__ __forceinline__ void h4x2_hi(uint64_t (&P)[16]) {
-  const uint64_t m2 = f2_dup(LAST ? -0.125f : -2.0f);
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    uint64_t s = f2_add(f2_add(P[b], P[4 + b]), f2_add(P[8 + b], P[12 + b]));
-    if (LAST) s = f2_mul(s, f2_dup(0.0625f));
-    const uint64_t t0 = f2_fma(m2, P[12 + b], s), t1 = f2_fma(m2, P[8 + b], s);
-    const uint64_t t2 = f2_fma(m2, P[4 + b], s), t3 = f2_fma(m2, P[b], s);
-    P[b] = t0; P[4 + b] = t1; P[8 + b] = t2; P[12 + b] = t3;
-  }
-}
-
-// Consumer teams of a CTA (12 consumer warps); 4 rows in flight.
-template <int NP>
-__global__ void __launch_bounds__(32 * (1 + kCrTeamWarps * kCrTeams), 1)
-    convrot_ring_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t m, int act,
-                        int8_t* __restrict__ q, float* __restrict__ scale, __nv_bfloat16* __restrict__ sx,
-                        int sum_group, int64_t kp, int stages, int ng) {
-  const int K = 256 * ng;
-  const int ROW_BYTES = 2 * K;
-  constexpr int HALF_GROUPS = 2 * kCrTeamWarps;  // half-warps of a team
-  constexpr int TEAMS = kCrTeams;                // NP: group pairs per half-warp
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty_bar = full_bar + kCrMaxStages;
-  uint64_t* team_bar = empty_bar + kCrMaxStages;  // [TEAMS]
-  uint32_t* red = reinterpret_cast<uint32_t*>(smem + kCrOffRed);  // [TEAMS][2][kCrTeamWarps] row-max bits
-  uint8_t* ring = smem + kCrOffRing;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t G = gridDim.x;
-  const int64_t cnt = m > (int64_t)blockIdx.x ? (m - blockIdx.x + G - 1) / G : 0;  // rows of this CTA
-  const int S = stages;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kCrTeamWarps);
-    }
-    for (int t = 0; t < TEAMS; ++t) mbar_init(&team_bar[t], kCrTeamWarps);
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- producer ----------------
-      int64_t j = 0;
-      for (; j < cnt; ++j) {
-        const int s = (int)(j % S);
-        const uint32_t use = (uint32_t)(j / S);
-        if (!mbar_wait(&empty_bar[s], (use & 1u) ^ 1u, kErrCrProducer)) break;
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)ROW_BYTES);
-        bulk_g2s(ring + (size_t)s * ROW_BYTES, x + (blockIdx.x + j * G) * ldx, (uint32_t)ROW_BYTES, &full_bar[s]);
-      }
-      // every copy issued lands before the CTA may exit
-      for (int64_t i = (j > S ? j - S : 0); i < j; ++i)
-        mbar_wait(&full_bar[i % S], (uint32_t)(i / S) & 1u, kErrCrDrain, 200000000ull);
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  const int cw = warp - 1;
-  const int team = cw / kCrTeamWarps, tw = cw - team * kCrTeamWarps;
-  const int h = lane >> 4, li = lane & 15;
-  const int hw = 2 * tw + h;  // half-warp within the team: groups hw + 6 i
-  // The lane's 32 bytes of a group are read as two 16-byte halves, the upper
-  // one first in lanes with bit 2 set, so that the 8 lanes of a quarter-warp
-  // hit distinct banks. Registers 0-7 then hold indices 8 c1 .. 8 c1 + 7: the
-  // H4 butterflies commute with that relabelling (flipping index bit 3 maps a
-  // digit d to d ^ 2 on inputs and outputs alike), so only the transpose
-  // write addresses depend on it.
-  const int c1 = (li >> 2) & 1;
-  uint8_t* tile = smem + kCrOffTiles + cw * kCrTileBytes;
-  float* tf = reinterpret_cast<float*>(tile);
-  uint8_t* bt = tile + h * 528;  // byte tile: group a [0, 256), group b [256, 512)
-  uint32_t* rteam = red + team * (2 * kCrTeamWarps);
-  const int lanes_per_sum = sum_group / 16;
-  const uint64_t magic = f2_dup(12582912.0f);  // 1.5 * 2^23
-  uint32_t team_phase = 0;
-  for (int64_t j = team; j < cnt; j += TEAMS) {
-    const int s = (int)(j % S);
-    const int64_t row = blockIdx.x + j * G;
-    if (!mbar_wait(&full_bar[s], (uint32_t)(j / S) & 1u, kErrCrFull)) break;
-    const uint8_t* st = ring + (size_t)s * ROW_BYTES;
-    uint32_t amax = 0u;
-    // per pair: bf16 (group a, group b) of index li + 16 e. One pair stays in
-    // registers; with more, each waits in this lane's own 32-byte slots of the
-    // stage (only this lane reads them back) until the row absmax is known.
-    uint32_t wab[16];
-#pragma unroll 1
-    for (int pr = 0; pr < NP; ++pr) {
-      const int ga = hw + HALF_GROUPS * pr, gb = ga + HALF_GROUPS * NP;
-      const bool oka = ga < ng, okb = gb < ng;  // slots past the row hold zeros
-      uint8_t* sa = const_cast<uint8_t*>(st) + (oka ? ga : 0) * 512 + li * 32;
-      uint8_t* sb = const_cast<uint8_t*>(st) + (okb ? gb : 0) * 512 + li * 32;
-      uint32_t wa[8], wb[8];
-      {
-        const uint4 z = make_uint4(0, 0, 0, 0);
-        const uint4 a0 = oka ? *reinterpret_cast<const uint4*>(sa + 16 * c1) : z;
-        const uint4 a1 = oka ? *reinterpret_cast<const uint4*>(sa + 16 - 16 * c1) : z;
-        const uint4 b0 = okb ? *reinterpret_cast<const uint4*>(sb + 16 * c1) : z;
-        const uint4 b1 = okb ? *reinterpret_cast<const uint4*>(sb + 16 - 16 * c1) : z;
-        wa[0] = a0.x; wa[1] = a0.y; wa[2] = a0.z; wa[3] = a0.w; wa[4] = a1.x; wa[5] = a1.y; wa[6] = a1.z; wa[7] = a1.w;
-        wb[0] = b0.x; wb[1] = b0.y; wb[2] = b0.z; wb[3] = b0.w; wb[4] = b1.x; wb[5] = b1.y; wb[6] = b1.z; wb[7] = b1.w;
-      }
-      if (act == H3B200_ACT_GELU_TANH) {  // exact bf16 GELU from the device table
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          wa[e] = gelu_bf16_bits(wa[e]) | (gelu_bf16_bits(wa[e] >> 16) << 16);
-          wb[e] = gelu_bf16_bits(wb[e]) | (gelu_bf16_bits(wb[e] >> 16) << 16);
-        }
-      }
-      uint64_t P[16];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        P[2 * e] = f2_make(bf16_lo(wa[e]), bf16_lo(wb[e]));
-        P[2 * e + 1] = f2_make(bf16_hi(wa[e]), bf16_hi(wb[e]));
-      }
-      h4x2_lo<false>(P);
-      h4x2_hi<false>(P);
-      // transpose each group: write row li, read column li (lane then holds indices li + 16 e)
-      float va[16], vb[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) f2_split(P[e], va[e], vb[e]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<float4*>(tf + tr_addr(li, h, 4 * (c ^ (2 * c1)))) =
-            make_float4(va[4 * c], va[4 * c + 1], va[4 * c + 2], va[4 * c + 3]);
-      __syncwarp();
-#pragma unroll
-      for (int e = 0; e < 16; ++e) va[e] = tf[tr_addr(e, h, li)];
-      __syncwarp();
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<float4*>(tf + tr_addr(li, h, 4 * (c ^ (2 * c1)))) =
-            make_float4(vb[4 * c], vb[4 * c + 1], vb[4 * c + 2], vb[4 * c + 3]);
-      __syncwarp();
-#pragma unroll
-      for (int e = 0; e < 16; ++e) vb[e] = tf[tr_addr(e, h, li)];
-      __syncwarp();
-#pragma unroll
-      for (int e = 0; e < 16; ++e) P[e] = f2_make(va[e], vb[e]);
-      h4x2_lo<false>(P);
-      h4x2_hi<true>(P);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        float a, b;
-        f2_split(P[e], a, b);
-        wab[e] = pack_bf16(a, b);
-        amax = __vmaxu2(amax, wab[e] & 0x7FFF7FFFu);  // per-half running max of |bf16|
-      }
-      if (NP > 1) {  // park the pair in this lane's own slots of the groups it read
-        if (okb) {     // the 16 (a, b) words span both 32-byte slots
-          *reinterpret_cast<uint4*>(sa) = make_uint4(wab[0], wab[1], wab[2], wab[3]);
-          *reinterpret_cast<uint4*>(sa + 16) = make_uint4(wab[4], wab[5], wab[6], wab[7]);
-          *reinterpret_cast<uint4*>(sb) = make_uint4(wab[8], wab[9], wab[10], wab[11]);
-          *reinterpret_cast<uint4*>(sb + 16) = make_uint4(wab[12], wab[13], wab[14], wab[15]);
-        } else if (oka) {  // empty b slot: group a's 16 values (the low halves) fit its own slot
-          uint32_t w[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = __byte_perm(wab[2 * i], wab[2 * i + 1], 0x5410);
-          *reinterpret_cast<uint4*>(sa) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(sa + 16) = make_uint4(w[4], w[5], w[6], w[7]);
-        }
-      }
-    }
-    // row absmax over the team
-    amax = max(amax & 0xFFFFu, amax >> 16);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    uint32_t* rr = rteam + (team_phase & 1u) * kCrTeamWarps;
-    if (lane == 0) {
-      rr[tw] = amax;
-      mbar_arrive(&team_bar[team]);
-    }
-    if (!mbar_wait(&team_bar[team], team_phase & 1u, kErrCrTeam)) break;
-    ++team_phase;
-    uint32_t rowbits = rr[0];
-#pragma unroll
-    for (int i = 1; i < kCrTeamWarps; ++i) rowbits = max(rowbits, rr[i]);
-    const float s_row = fmaxf(__fdiv_rn(__uint_as_float(rowbits << 16), 127.0f), 1e-30f);
-    const uint64_t r2 = f2_dup(__frcp_rn(quant_divisor(s_row)));
-#pragma unroll 1
-    for (int pr = 0; pr < NP; ++pr) {
-      const int ga = hw + HALF_GROUPS * pr, gb = ga + HALF_GROUPS * NP;
-      const bool oka = ga < ng, okb = gb < ng;
-      if (NP > 1) {
-        const uint8_t* sa = st + (oka ? ga : 0) * 512 + li * 32;
-        const uint8_t* sb = st + (okb ? gb : 0) * 512 + li * 32;
-        const uint4 z = make_uint4(0, 0, 0, 0);
-        const uint4 a0 = oka ? *reinterpret_cast<const uint4*>(sa) : z, a1 = oka ? *reinterpret_cast<const uint4*>(sa + 16) : z;
-        if (okb) {
-          const uint4 b0 = *reinterpret_cast<const uint4*>(sb), b1 = *reinterpret_cast<const uint4*>(sb + 16);
-          wab[0] = a0.x; wab[1] = a0.y; wab[2] = a0.z; wab[3] = a0.w; wab[4] = a1.x; wab[5] = a1.y; wab[6] = a1.z;
-          wab[7] = a1.w; wab[8] = b0.x; wab[9] = b0.y; wab[10] = b0.z; wab[11] = b0.w; wab[12] = b1.x; wab[13] = b1.y;
-          wab[14] = b1.z; wab[15] = b1.w;
-        } else {  // group a's values only (b is an empty slot: zeros in the high halves)
-          const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            wab[2 * i] = w[i] & 0xFFFFu;
-            wab[2 * i + 1] = w[i] >> 16;
-          }
-        }
-      }
-      // quantize in the transposed order; bytes land in natural order in the byte tile
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        uint32_t t0, t1;
-        f2_bits(f2_mul(bf16x2_to_f2(wab[e]), r2), t0, t1);
-        const uint32_t b = bf16x2_clamp_i8(bf16x2_from_bits(t0, t1));
-        uint32_t qa, qb;
-        f2_bits(f2_add(bf16x2_to_f2(b), magic), qa, qb);  // the integers sit in the low bytes
-        sts_u8(bt + li + 16 * e, qa);
-        sts_u8(bt + 256 + li + 16 * e, qb);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int pg = 0; pg < 2; ++pg) {
-        const int g = pg ? gb : ga;
-        const bool live = g < ng;  // an empty slot stores nothing (its lanes still take part in the shuffles)
-        const uint4 v = *reinterpret_cast<const uint4*>(bt + pg * 256 + 16 * li);
-        if (live) stg_v4(q + row * K + g * 256 + 16 * li, v);
-        if (sx != nullptr) {  // all lanes shuffle; partners stay inside the half-warp (offsets < 16)
-          int isum = __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
-                            __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0))));
-          for (int o = 1; o < lanes_per_sum; o <<= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-          if (live && (li % lanes_per_sum) == 0)
-            sx[row * kp + (g * 256 + 16 * li) / sum_group] =
-                __float2bfloat16_rn(__fmul_rn(bf16_round((float)isum), bf16_round(s_row)));
-        }
-      }
-      __syncwarp();  // the byte tile is reused
-    }
-    // the stage was written here (parked pairs) and is refilled by the async proxy next
-    fence_proxy_async_shared();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);  // this warp is done with the stage
-    if (tw == 0) {
-      if (lane == 0) scale[row] = s_row;
-      if (sx != nullptr)  // zero the K padding of the correction operand
-        for (int64_t i = K / sum_group + lane; i < kp; i += 32) sx[row * kp + i] = __float2bfloat16_rn(0.0f);
-    }
-  }
 }
 
 }  // namespace
@@ -691,73 +213,6 @@ cudaError_t launch_dequant_int4(const int8_t* qdata, const void* s_rel, bool s_r
   }
 #undef H3_DEQ
 #undef H3_DEQ_V
-  return cudaGetLastError();
-}
-
-cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64_t k, int act, int8_t* q,
-                                    float* scale, void* sx, int64_t sum_group, int64_t kp, cudaStream_t stream) {
-  if (m == 0) return cudaSuccess;
-  if (k % 256 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 15))
-    return cudaErrorNotSupported;
-  if (sx != nullptr && (sum_group < 16 || sum_group > 256 || 256 % sum_group || kp < k / sum_group))
-    return cudaErrorNotSupported;
-  {
-    const cudaError_t e = ensure_act_table(act, stream);
-    if (e != cudaSuccess) return e;
-  }
-  const int64_t ngroups = k / 256;
-  const int64_t np = (ngroups + 2 * 6 - 1) / (2 * 6);  // group pairs per half-warp of a 6-half-warp team
-  // the persistent kernel's stages hold one activated-width row, so SwiGLU rows
-  // ([gate | up], twice as wide) take the per-row kernel
-  if (np >= 1 && np <= 5 && act != H3B200_ACT_SWIGLU) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    static bool attr_set[64][9] = {};
-    const int64_t row_bytes = 2 * k;
-    const int stages = (int)std::min<int64_t>(kCrMaxStages, (kCrSmemLimit - 1024 - kCrOffRing) / row_bytes);
-    const int smem = 1024 + kCrOffRing + stages * (int)row_bytes;
-    const unsigned grid = (unsigned)std::min<int64_t>(m, (int64_t)num_sms(dev));
-    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
-    __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
-    const int sg = sx != nullptr ? (int)sum_group : 16;
-    auto go = [&](auto kern) -> cudaError_t {
-      if (dev >= 0 && dev < 64 && !attr_set[dev][np]) {
-        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kCrSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_set[dev][np] = true;
-      }
-      const int threads = 32 * (1 + kCrConsumers);
-      kern<<<grid, threads, smem, stream>>>(xb, ldx, m, act, q, scale, sxb, sg, kp, stages, (int)ngroups);
-      return cudaGetLastError();
-    };
-    // A team waits for row j after consuming its row j - teams; the producer fills in
-    // order, so with stages >= teams the stage's previous row (j - stages) has landed
-    // and the parity wait cannot pass on the phase before it. Rows of up to 48
-    // groups get 8 or more stages; 49-60 groups (H3's 56-group fc2 input) 7 or 8.
-    if (stages >= kCrTeams) {
-      switch (np) {
-        case 1: return go(convrot_ring_kernel<1>);
-        case 2: return go(convrot_ring_kernel<2>);
-        case 3: return go(convrot_ring_kernel<3>);
-        case 4: return go(convrot_ring_kernel<4>);
-        case 5: return go(convrot_ring_kernel<5>);
-        default: break;
-      }
-    }
-  }
-  const int64_t pairs = (k / 256 + 1) / 2;
-  const int64_t nwarps = pairs < 8 ? pairs : 8;
-  const int64_t ppw = (pairs + nwarps - 1) / nwarps;
-  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
-  __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
-  dim3 grid((unsigned)m), block((unsigned)(32 * nwarps));
-  switch (ppw) {
-    case 1: quantize_convrot_kernel<1><<<grid, block, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp); break;
-    case 2: quantize_convrot_kernel<2><<<grid, block, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp); break;
-    case 3: quantize_convrot_kernel<3><<<grid, block, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp); break;
-    case 4: quantize_convrot_kernel<4><<<grid, block, 0, stream>>>(xb, ldx, m, k, act, q, scale, sxb, sum_group, kp); break;
-    default: return cudaErrorNotSupported;  // k > 32768
-  }
   return cudaGetLastError();
 }
 
