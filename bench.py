@@ -754,6 +754,57 @@ def run_ours(args, rank, world, local_rank):
         blk_ms = float(t.item())
     del q4, k4, x4, r4, o4, table4, work5
 
+    # ---- config 4, tensor-parallel MLP: all 196,560 tokens replicated on every rank, W1 rows and
+    #      W2 columns split N ways (fc1 -> all-reduce(MAX) of the row absmax -> requant -> fc2 int32
+    #      partials -> reduce-scatter + epilogue on owned rows + bf16 all-gather, or int32 all-reduce),
+    #      8,192-token chunks; strong scaling (total work fixed) ----
+    gt = torch.Generator(device=dev).manual_seed(6)      # the same replicated inputs on every rank
+    xt = torch.randn(M4, D_MODEL, generator=gt, device=dev).to(torch.bfloat16)
+    rt = torch.randn(M4, D_MODEL, generator=gt, device=dev).to(torch.bfloat16)
+    ot = torch.empty_like(rt)
+    tp_shard = PAR.TPShard.from_full(wt.w1q, wt.s1, wt.w2q, wt.s2, world, rank)
+    TP_CHUNK = 8192
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    tp_ms = {}
+    for coll in (PAR.COLLECTIVES if world > 1 else PAR.COLLECTIVES[:1]):
+        def k_tp(coll=coll):
+            PAR.tp_gated_mlp(xt, rt, gate, tp_shard, chunk_tokens=TP_CHUNK, out=ot, collective=coll)
+
+        k_tp()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        tp_ms[coll] = max_over_ranks(timed(k_tp, 3, stream))
+    # the collectives of one TP step alone (same sizes, same order), to see what bounds the curve
+    tp_coll_ms = None
+    if world > 1:
+        nchunk = -(-M4 // TP_CHUNK)
+        am_t = torch.zeros(TP_CHUNK, dtype=torch.float32, device=dev)
+        acc_t = torch.zeros(TP_CHUNK, D_MODEL, dtype=torch.int32, device=dev)
+        part_t = torch.empty(TP_CHUNK // world, D_MODEL, dtype=torch.int32, device=dev)
+        loc_t = torch.empty(TP_CHUNK // world, D_MODEL, dtype=torch.bfloat16, device=dev)
+        gat_t = torch.empty(TP_CHUNK, D_MODEL, dtype=torch.bfloat16, device=dev)
+
+        def k_coll():
+            for _ in range(nchunk):
+                dist.all_reduce(am_t, op=dist.ReduceOp.MAX)
+                dist.reduce_scatter_tensor(part_t, acc_t, op=dist.ReduceOp.SUM)
+                dist.all_gather_into_tensor(gat_t, loc_t)
+
+        k_coll()
+        torch.cuda.synchronize()
+        dist.barrier()
+        tp_coll_ms = max_over_ranks(timed(k_coll, 3, stream))
+        del am_t, acc_t, part_t, loc_t, gat_t
+    del xt, rt, ot, tp_shard
+
     # ---- library INT8 reference: cuBLASLt through torch._int_mm, 8192^3, same box and run ----
     lib_int8_tops = None
     try:
@@ -850,6 +901,13 @@ def run_ours(args, rank, world, local_rank):
                 "w4a8_mlp_cfg2": {"ms": w4_ms, "tokens_per_s": M_TOKENS / (w4_ms * 1e-3),
                                   "int8_tops": M_TOKENS * OPS_PER_TOKEN / (w4_ms * 1e-3) / 1e12,
                                   "weights": "asymmetric int4, group 128, ConvRot-256, decoded per call"},
+                "tp_mlp_cfg4": {"tokens_total": M4, "tensor_parallel": world, "chunk_tokens": TP_CHUNK,
+                                "ms": tp_ms["reduce_scatter"], "tokens_per_s": M4 / (tp_ms["reduce_scatter"] * 1e-3),
+                                "int8_tops": M4 * OPS_PER_TOKEN / (tp_ms["reduce_scatter"] * 1e-3) / 1e12,
+                                "collective": "int32 reduce-scatter + bf16 all-gather (NCCL), absmax all-reduce(MAX)",
+                                "all_reduce_variant_ms": tp_ms.get("all_reduce"),
+                                "collectives_alone_ms": tp_coll_ms,
+                                "scaling": "strong (196,560 tokens in total at every N)"},
                 "long_video_block_cfg4": {"tokens_total": M4, "tokens_this_rank": m4, "ms": blk_ms,
                                           "tokens_per_s": M4 / (blk_ms * 1e-3),
                                           "mode": f"token-shard x{world} (norm-RoPE + W8A8 MLP per rank)"},

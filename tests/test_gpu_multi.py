@@ -1,8 +1,8 @@
-"""GPU parity on 2 GPUs (NCCL): tensor-parallel MLP and token sharding vs one GPU.
+"""GPU parity on 2 or 4 GPUs (NCCL): tensor-parallel MLP and token sharding vs one GPU.
 
 Each rank runs in its own spawned process with one GPU. The tensor-parallel MLP
 (fc1 column-split, all-reduce(MAX) of the row absmax, fc2 row-split, int32
-all-reduce(SUM)) and the token-sharded MLP must both reproduce the single-GPU
+reduce-scatter + bf16 all-gather, or int32 all-reduce) and the token-sharded MLP must both reproduce the single-GPU
 fused MLP bit for bit. Skipped when fewer than 2 GPUs are visible.
 """
 
@@ -49,14 +49,16 @@ def _worker(rank, world, port, outdir):
         ref = h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate)
 
         shard = P.TPShard.from_full(wt.w1q, wt.s1, wt.w2q, wt.s2, world, rank)
-        tp = P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=384)
+        # chunks of 383 rows (383, 383, 234): reduce-scatter rows padded to the world size
+        tp = all(bool(torch.equal(P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=383, collective=c), ref))
+                 for c in P.COLLECTIVES)
 
         lo, hi = P.shard_range(m, world, rank)
         local = P.token_sharded_mlp(x[lo:hi], res[lo:hi], gate, wt.w1q, wt.s1, wt.w2q, wt.s2)
         ts = P.gather_tokens(local, m)
         torch.cuda.synchronize()
         ok = {
-            "tp": bool(torch.equal(tp, ref)),
+            "tp": tp,
             "token_shard": bool(torch.equal(ts, ref)),
             "status": h3b200.device_status(rank),
         }
@@ -66,14 +68,15 @@ def _worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-def test_tp_mlp_and_token_sharding_two_gpus(tmp_path):
+def test_tp_mlp_and_token_sharding_multi_gpu(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
+    world = 4 if torch.cuda.device_count() >= 4 else 2
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -82,6 +85,6 @@ def test_tp_mlp_and_token_sharding_two_gpus(tmp_path):
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    for r in range(2):
+    for r in range(world):
         res = eval((tmp_path / f"rank{r}.txt").read_text())
         assert res == {"tp": True, "token_shard": True, "status": 0}, (r, res)

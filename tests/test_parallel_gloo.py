@@ -108,11 +108,16 @@ def _worker(rank, world, port, mode, q):
         ops = OracleOps()
         x, res, gate, w1q, s1, w2q, s2 = _inputs()
         m = x.shape[0]
-        if mode == "tp":
+        if mode.startswith("tp"):
+            # 96 tokens in chunks of 37 (37, 37, 22 rows): no chunk splits evenly over 2 or 4
+            # ranks, so the reduce-scatter pads rows and the gather copies back
             shard = P.TPShard.from_full(w1q, s1, w2q, s2, world, rank)
-            out = P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=40, ops=ops)
             full = ops.fused_mlp(res, x, w1q, s1, w2q, s2, gate, torch.empty_like(res))
-            q.put((rank, bool(torch.equal(out.view(torch.int16), full.view(torch.int16)))))
+            ok = True
+            for coll in P.COLLECTIVES:
+                out = P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=37, ops=ops, collective=coll)
+                ok = ok and bool(torch.equal(out.view(torch.int16), full.view(torch.int16)))
+            q.put((rank, ok))
         elif mode == "dp":
             lo, hi = P.shard_range(m, world, rank)
             y = P.token_sharded_mlp(x[lo:hi], res[lo:hi], gate, w1q, s1, w2q, s2, ops=ops)
@@ -176,6 +181,27 @@ def test_shard_range_covers_tokens():
 def test_tensor_parallel_mlp_bit_exact_two_ranks():
     res = _run("tp")
     assert res == {0: True, 1: True}
+
+
+def test_tensor_parallel_mlp_bit_exact_four_ranks():
+    """ffn 512 over 4 ranks (128 columns each), ragged chunks of 37 and 22 rows."""
+    res = _run("tp", world=4)
+    assert res == {0: True, 1: True, 2: True, 3: True}
+
+
+def test_tensor_parallel_mlp_without_process_group():
+    """One rank and no process group: the same chunked path, no collective."""
+    _paths()
+    from h3b200 import parallel as P
+
+    ops = OracleOps()
+    x, res, gate, w1q, s1, w2q, s2 = _inputs(m=50)
+    shard = P.TPShard.from_full(w1q, s1, w2q, s2, 1, 0)
+    out = P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=16, ops=ops)
+    full = ops.fused_mlp(res, x, w1q, s1, w2q, s2, gate, torch.empty_like(res))
+    assert torch.equal(out.view(torch.int16), full.view(torch.int16))
+    with pytest.raises(ValueError):
+        P.tp_gated_mlp(x, res, gate, shard, ops=ops, collective="ring")
 
 
 def test_token_sharded_mlp_bit_exact_two_ranks():

@@ -44,6 +44,9 @@ namespace {
 #ifndef CV_TEAM_WARPS
 #define CV_TEAM_WARPS 6
 #endif
+#ifndef CV_MAXNREG
+#define CV_MAXNREG 128
+#endif
 constexpr int kCvTeams = 2;
 constexpr int kCvTeamWarps = CV_TEAM_WARPS;
 constexpr int kCvConsumers = kCvTeams * kCvTeamWarps;  // 12
@@ -65,18 +68,6 @@ __device__ __forceinline__ void cv_bulk_g2s(void* smem_dst, const void* gsrc, ui
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ uint32_t lds_u16(const void* p) {
-  uint32_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
-  return v;
-}
-__device__ __forceinline__ void sts_f64(void* p, double v) {
-  asm volatile("st.shared.f64 [%0], %1;" ::"r"(smem_u32(p)), "d"(v) : "memory");
-}
-__device__ __forceinline__ void lds_f64x2(const void* p, double& a, double& b) {
-  asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(a), "=d"(b) : "r"(smem_u32(p)));
-}
-
 // activation applied to one bf16 input (low 16 bits): GELU from the exact table,
 // SwiGLU = bf16(silu(gate) * up) (the product of two bf16 values is exact in fp32)
 template <int ACT>
@@ -152,14 +143,16 @@ __device__ __forceinline__ Words8 cv_group_slow(const uint8_t* st, int K, int g,
 }
 
 template <int GPH, int ACT>
-__global__ void __maxnreg__(128)
+__global__ void __maxnreg__(CV_MAXNREG)
     convrot_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t m, int8_t* __restrict__ q,
                    float* __restrict__ scale, __nv_bfloat16* __restrict__ sx, int sum_group, int64_t kp, int stages,
                    int ng) {
   const int K = 256 * ng;
   const int row_bytes = (ACT == H3B200_ACT_SWIGLU ? 4 : 2) * K;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 16-byte alignment is all this kernel needs (bulk copies, f64 pairs, mbarriers); the
+  // array is used directly so the compiler keeps every access in the shared space
+  extern __shared__ __align__(128) uint8_t cv_smem[];
+  uint8_t* smem = cv_smem;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty_bar = full_bar + kCvMaxStages;
   uint64_t* team_bar = empty_bar + kCvMaxStages;  // [kCvTeams]
@@ -223,63 +216,91 @@ __global__ void __maxnreg__(128)
     for (int i = 0; i < GPH; ++i) {
       const int g = hw + kCvHalfWarps * i;
       const bool ok = g < ng;  // the same for the 16 lanes of a half-warp; empty slots carry zeros
-      const uint8_t* col = st + (ok ? g : 0) * 512 + 2 * li;
+      // register e holds row e ^ h of column li: row e + h (e even) or e - h (e odd)
+      const uint16_t* col_even = reinterpret_cast<const uint16_t*>(st + (ok ? g : 0) * 512 + 2 * li) + 16 * h;
+      const uint16_t* col_odd = col_even - 32 * h;
       uint32_t v[16];
-      uint32_t kmax = 0u, kmin = 0xFFFFFFFFu;  // |x| bits << 17: max, and min of (that - 1)
+      float xf[16];
+      // |x| statistics of this lane's 16 inputs (a bf16 is the high half of its fp32):
+      // the largest and the smallest, zeros included. Both drop NaN; a NaN input makes
+      // every output of its group NaN on either path, and a NaN bf16 quantizes the same
+      // whatever its payload, so NaN needs no exact path.
+      float fmx = 0.0f, fmn = __uint_as_float(0x7F800000u);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        const int r = e ^ h;  // register e holds row e ^ h of column li
+        const uint16_t* p = (e & 1 ? col_odd : col_even) + 16 * e;
         uint32_t a = 0u;
         if (ok) {
-          const uint32_t gate = lds_u16(col + 32 * r);
-          const uint32_t up = ACT == H3B200_ACT_SWIGLU ? lds_u16(col + 2 * K + 32 * r) : 0u;
+          const uint32_t gate = p[0];
+          const uint32_t up = ACT == H3B200_ACT_SWIGLU ? p[K] : 0u;
           a = cv_act<ACT>(gate, up);
         }
         v[e] = a;
-        const uint32_t key = a * 131072u;  // magnitude bits at the top, sign dropped
-        kmax = max(kmax, key);
-        kmin = min(kmin, key - 1u);         // a zero wraps to the largest value
+        xf[e] = __uint_as_float(a << 16);
+        fmx = fmaxf(fmx, fabsf(xf[e]));
+        fmn = fminf(fmn, fabsf(xf[e]));
       }
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) {
-        kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
-        kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+      if (!ok) {  // an empty slot does not constrain the other half-warp's group
+        fmx = 0.0f;
+        fmn = __uint_as_float(0x7F800000u);
       }
-      const uint32_t min1 = (kmin >> 17) == 0x7FFFu ? 0xFFFFFFFFu : (kmin >> 17);
-      const bool slow_h = ok && !cv::fast_path_ok(kmax >> 17, min1);
-      // the exchange is warp-synchronous: if either half-warp's group needs the exact
-      // integer path, both groups of this slot take it
-      if (!__any_sync(0xffffffffu, slow_h)) {
-        double d[16];
+      // One exactness test for the slot's two groups (both half-warps): the exponent
+      // spread over both is at least each group's own, so passing it proves both exact.
+      const uint32_t umax = __reduce_max_sync(0xffffffffu, __float_as_uint(fmx));
+      uint32_t umin = __reduce_min_sync(0xffffffffu, __float_as_uint(fmn));
+      uint32_t min1;
+      if (umin != 0u) {
+        min1 = (umin >> 16) - 1u;  // umin = 0x7F800000 (no valid input) passes through fast_path_ok's inf check
+      } else {  // a zero among the inputs: the smallest nonzero magnitude, zeros wrapping to the top
+        uint32_t m1 = 0xFFFFFFFFu;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) d[e] = cv::bf16_double(v[e]);
+        for (int e = 0; e < 16; ++e) m1 = min(m1, (v[e] & 0x7FFFu) - 1u);
+        min1 = __reduce_min_sync(0xffffffffu, ok ? m1 : 0xFFFFFFFFu);
+      }
+      if (!cv::fast_path_ok(umax >> 16, min1)) {
+        // rare: the per-group test decides which of the two groups need the exact path
+        uint32_t kmax = 0u, kmin = 0xFFFFFFFFu;
 #pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) cv::h4<false>(d[4 * a4], d[4 * a4 + 1], d[4 * a4 + 2], d[4 * a4 + 3]);
-#pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) cv::h4<false>(d[a4], d[4 + a4], d[8 + a4], d[12 + a4]);
-        // exchange: this lane holds column li (register e = row e ^ h); it reads back row li.
-        // Row e ^ h is row e + 1 (e even) or e - 1 (e odd) in the second half-warp.
-#pragma unroll
-        for (int e = 0; e < 16; ++e) sts_f64((e & 1 ? wr_odd : wr_even) + e * cv::kXRow, d[e]);
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 8; ++k) lds_f64x2(rd_row + 16 * k, d[2 * k], d[2 * k + 1]);
-        __syncwarp();  // the tile is rewritten for the next group
-#pragma unroll
-        for (int b4 = 0; b4 < 4; ++b4) cv::h4<false>(d[4 * b4], d[4 * b4 + 1], d[4 * b4 + 2], d[4 * b4 + 3]);
-#pragma unroll
-        for (int b4 = 0; b4 < 4; ++b4) cv::h4<true>(d[b4], d[4 + b4], d[8 + b4], d[12 + b4]);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t mag = pack_bf16(cv::bits_float(cv::rto21_abs_bits(d[2 * k])),
-                                         cv::bits_float(cv::rto21_abs_bits(d[2 * k + 1])));
-          park[i][k] = mag | cv::bf16_pair_signs(cv::double_hi(d[2 * k]), cv::double_hi(d[2 * k + 1]));
+        for (int e = 0; e < 16; ++e) {
+          kmax = max(kmax, v[e] & 0x7FFFu);
+          kmin = min(kmin, (v[e] & 0x7FFFu) - 1u);
         }
-      } else {
-        if (ok) slow_mask |= 1u << i;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) park[i][k] = 0u;  // filled below
+        for (int o = 1; o < 16; o <<= 1) {
+          kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+          kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+        }
+        if (ok && !cv::fast_path_ok(kmax, kmin)) slow_mask |= 1u << i;
       }
+      // Fast path for both groups of the slot (a group marked slow gets its values
+      // replaced below). The exchange is warp-synchronous.
+      double d[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) d[e] = (double)xf[e];
+#pragma unroll
+      for (int a4 = 0; a4 < 4; ++a4) cv::h4<false>(d[4 * a4], d[4 * a4 + 1], d[4 * a4 + 2], d[4 * a4 + 3]);
+#pragma unroll
+      for (int a4 = 0; a4 < 4; ++a4) cv::h4<false>(d[a4], d[4 + a4], d[8 + a4], d[12 + a4]);
+      // exchange: this lane holds column li (register e = row e ^ h); it reads back row li.
+      // Row e ^ h is row e + 1 (e even) or e - 1 (e odd) in the second half-warp.
+#pragma unroll
+      for (int e = 0; e < 16; ++e) *reinterpret_cast<double*>((e & 1 ? wr_odd : wr_even) + e * cv::kXRow) = d[e];
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const double2 t = *reinterpret_cast<const double2*>(rd_row + 16 * k);
+        d[2 * k] = t.x;
+        d[2 * k + 1] = t.y;
+      }
+      __syncwarp();  // the tile is rewritten for the next group
+#pragma unroll
+      for (int b4 = 0; b4 < 4; ++b4) cv::h4<false>(d[4 * b4], d[4 * b4 + 1], d[4 * b4 + 2], d[4 * b4 + 3]);
+#pragma unroll
+      for (int b4 = 0; b4 < 4; ++b4) cv::h4<true>(d[b4], d[4 + b4], d[8 + b4], d[12 + b4]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        park[i][k] = pack_bf16(cv::bits_float(cv::rto21_signed_bits(d[2 * k])),
+                               cv::bits_float(cv::rto21_signed_bits(d[2 * k + 1])));
     }
     if (__any_sync(0xffffffffu, slow_mask != 0u)) {
       // Exact integer path for the marked groups, one group slot at a time for the whole

@@ -102,6 +102,14 @@ CV_HD uint32_t rto21_abs_bits(double ys) {
   split_double(ys, hi, lo);
   return (hi << 3) + (lo != 0u ? 1u : 0u);
 }
+// The same pattern with the sign of y: (hi * 8 + sticky) keeps the exponent field
+// (its top bit, hi's bit 28, is zero for |y| < 2^128) and 20 mantissa bits; the sticky
+// bit is min(lo, 1). Rounding it to bf16 (nearest even) gives the correctly rounded bf16 of y.
+CV_HD uint32_t rto21_signed_bits(double ys) {
+  uint32_t hi, lo;
+  split_double(ys, hi, lo);
+  return (hi * 8u + (lo < 1u ? lo : 1u)) | (hi & 0x80000000u);
+}
 // sign bits of two scaled doubles (high words hi0, hi1) at bits 15 and 31
 CV_HD uint32_t bf16_pair_signs(uint32_t hi0, uint32_t hi1) {
 #if defined(__CUDA_ARCH__)

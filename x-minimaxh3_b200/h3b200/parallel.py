@@ -14,10 +14,12 @@ Two modes:
   of an fp32 [M] vector, after which every rank quantizes with the global scale
   (so the int8 activations are the single-GPU ones). fc2 is row-split along
   its K = ffn: each rank produces partial int32 accumulators, summed exactly by
-  an all-reduce(SUM) over int32, followed by the dequant + gated-residual
-  epilogue. The output is bit-identical to the single-GPU fused MLP.
-  Tokens are processed in chunks; the collectives of chunk i run
-  asynchronously while chunk i+1 computes.
+  a reduce-scatter(SUM) over int32 by rows, each rank runs the dequant +
+  gated-residual epilogue on its rows, and an all-gather returns the bf16 rows
+  (or, optionally, an int32 all-reduce and the whole epilogue on every rank).
+  The output is bit-identical to the single-GPU fused MLP. Tokens are processed
+  in chunks; the reduction of chunk i runs asynchronously while chunk i+1
+  computes.
 
 The kernel calls go through an ``ops`` object (default: the CUDA kernels of
 this package) so the orchestration can be exercised on CPU ranks in tests.
@@ -102,31 +104,107 @@ class TPShard:
         return cls(w1q[lo:hi].contiguous(), s1[lo:hi].contiguous(), w2q[:, lo:hi].contiguous(), s2.contiguous())
 
 
+def _world(group=None) -> tuple[int, int]:
+    """(world size, rank) of ``group``; (1, 0) when no process group is initialised."""
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+COLLECTIVES = ("reduce_scatter", "all_reduce")
+
+
 def tp_gated_mlp(x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor, shard: TPShard,
-                 group=None, chunk_tokens: int = 8192, ops=None, out: torch.Tensor | None = None) -> torch.Tensor:
+                 group=None, chunk_tokens: int = 8192, ops=None, out: torch.Tensor | None = None,
+                 collective: str = "reduce_scatter") -> torch.Tensor:
     """Tensor-parallel fused gated W8A8 MLP; ``x``/``residual`` [M, d] are replicated on every rank.
 
-    Every rank takes the same collective steps in the same order (two
-    all-reduces per chunk), so the ranks stay matched in every path."""
+    Per token chunk: quantize x, fc1 on this rank's W1 rows with the GELU + row-absmax
+    epilogue, all-reduce(MAX) of the fp32 row absmax (so every rank requantizes with the
+    global scale, as the single-GPU MLP does), requantize, fc2 on this rank's W2 columns
+    into int32 partial sums, then the exact int32 reduction across ranks:
+
+    * ``collective="reduce_scatter"`` (default): reduce-scatter the int32 partials by
+      rows, run the dequant + gated-residual epilogue on the owned rows only, and
+      all-gather the bf16 output rows (6 bytes per output element cross the links
+      instead of the all-reduce's 8, and each rank runs 1/world of the epilogue);
+    * ``collective="all_reduce"``: all-reduce the int32 partials, every rank runs the
+      whole epilogue.
+
+    The reduction of chunk i runs asynchronously while chunk i+1 computes; chunk i's
+    epilogue runs right after chunk i+1's fc2 is issued, so at most two chunks' partial
+    sums are alive at once. Every rank takes the same collective steps in the same
+    order. The output equals the single-GPU fused MLP bit for bit (int32 sums are exact
+    in any order). With no process group (or one rank) no collective is issued."""
+    if collective not in COLLECTIVES:
+        raise ValueError(f"collective must be one of {COLLECTIVES}, got {collective!r}")
     ops = ops or CudaOps()
+    world, rank = _world(group)
     m = x.shape[0]
     if out is None:
         out = torch.empty_like(residual)
-    pending = []
+    prev = None
     for lo in range(0, m, chunk_tokens):
         hi = min(m, lo + chunk_tokens)
-        xq, xs = ops.quantize(x[lo:hi])
-        absmax = torch.zeros(hi - lo, dtype=torch.float32, device=x.device)
-        a = ops.fc1_gelu_absmax(xq, xs, shard.w1q, shard.s1, absmax)
-        dist.all_reduce(absmax, op=dist.ReduceOp.MAX, group=group)
-        q2, xs2 = ops.quantize_absmax(a, absmax)
-        acc = ops.gemm_i32(q2, shard.w2q)
-        work = dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=group, async_op=True)
-        pending.append((lo, hi, acc, xs2, work))
-    for lo, hi, acc, xs2, work in pending:
-        work.wait()
-        ops.dequant_gated_residual(acc, xs2, shard.s2, gate, residual[lo:hi], out[lo:hi])
+        cur = _tp_chunk_partials(x, shard, lo, hi, world, group, ops, collective)
+        if prev is not None:
+            _tp_chunk_finish(prev, residual, gate, shard, out, world, rank, group, ops)
+        prev = cur
+    if prev is not None:
+        _tp_chunk_finish(prev, residual, gate, shard, out, world, rank, group, ops)
     return out
+
+
+def _tp_chunk_partials(x, shard, lo, hi, world, group, ops, collective):
+    """fc1 -> absmax all-reduce -> requant -> fc2 partials of one chunk, reduction launched."""
+    xq, xs = ops.quantize(x[lo:hi])
+    absmax = torch.zeros(hi - lo, dtype=torch.float32, device=x.device)
+    a = ops.fc1_gelu_absmax(xq, xs, shard.w1q, shard.s1, absmax)
+    if world > 1:
+        dist.all_reduce(absmax, op=dist.ReduceOp.MAX, group=group)
+    q2, xs2 = ops.quantize_absmax(a, absmax)
+    del a, xq
+    acc = ops.gemm_i32(q2, shard.w2q)
+    c = hi - lo
+    st = {"lo": lo, "hi": hi, "xs2": xs2, "acc": acc, "work": None, "part": None, "rows_pad": c}
+    if world == 1:
+        return st
+    if collective == "all_reduce":
+        st["work"] = dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=group, async_op=True)
+        return st
+    cp = -(-c // world) * world               # rows padded to a multiple of the world size
+    if cp != c:
+        padded = torch.zeros(cp, acc.shape[1], dtype=acc.dtype, device=acc.device)
+        padded[:c] = acc
+        acc = st["acc"] = padded
+    part = torch.empty(cp // world, acc.shape[1], dtype=acc.dtype, device=acc.device)
+    st["work"] = dist.reduce_scatter_tensor(part, acc, op=dist.ReduceOp.SUM, group=group, async_op=True)
+    st["part"], st["rows_pad"] = part, cp
+    return st
+
+
+def _tp_chunk_finish(st, residual, gate, shard, out, world, rank, group, ops):
+    """Wait for one chunk's reduction, run its epilogue, gather the output rows if scattered."""
+    lo, hi = st["lo"], st["hi"]
+    if st["work"] is not None:
+        st["work"].wait()
+    if st["part"] is None:                     # one rank, or the all-reduced partials
+        ops.dequant_gated_residual(st["acc"], st["xs2"], shard.s2, gate, residual[lo:hi], out[lo:hi])
+        return
+    c, cp = hi - lo, st["rows_pad"]
+    per = cp // world
+    r0, r1 = rank * per, min(c, (rank + 1) * per)
+    local = torch.empty(per, out.shape[1], dtype=out.dtype, device=out.device)
+    if r1 > r0:
+        ops.dequant_gated_residual(st["part"][: r1 - r0], st["xs2"][r0:r1], shard.s2, gate,
+                                   residual[lo + r0:lo + r1], local[: r1 - r0])
+    dst = out[lo:hi]
+    direct = cp == c and dst.is_contiguous()
+    if not direct:
+        dst = torch.empty(cp, out.shape[1], dtype=out.dtype, device=out.device)
+    dist.all_gather_into_tensor(dst, local, group=group)
+    if not direct:
+        out[lo:hi].copy_(dst[:c])
 
 
 def token_sharded_mlp(x_shard, residual_shard, gate, w1q, s1, w2q, s2, ops=None, out=None):
