@@ -13,12 +13,13 @@
 // is one well-defined function of the input. Input activations (tanh-GELU, or
 // SwiGLU of [gate | up] rows) are applied exactly before the rotation.
 //
-// B200 design: a persistent CTA per SM. A producer thread streams rows into a
-// shared-memory ring of one-row stages with cp.async.bulk (no multicast); two
-// teams of six consumer warps take alternate rows (the ring has an even number
-// of stages, so each stage always serves the same team and a team waits for a
-// stage's next fill only after consuming its previous one). A team's 12
-// half-warps split the row's 256-groups (GPH per half-warp). Per group, lane l of
+// B200 design: a persistent CTA per SM with two teams of TW warps (6 for rows of up
+// to 24 groups, 8 above: 12 or 16 warps); the teams take alternate rows. Rows stream into a shared-memory ring of one-row
+// stages with cp.async.bulk (no multicast), issued by each team's first lane for
+// its own rows (the ring has an even number of stages, so each stage always
+// serves the same team; a stage is refilled as soon as the team's row-absmax
+// barrier shows every warp has read it). A team's 2 TW half-warps split the row's
+// 256-groups (GPH per half-warp). Per group, lane l of
 // a half-warp reads column l of the group's 16 x 16 matrix (natural index
 // 16 a + b: a = high base-4 digits, b = low) with 2-byte loads (the second
 // half-warp reads rows in the order a ^ 1, which keeps the two half-warps on
@@ -41,25 +42,16 @@
 namespace h3 {
 namespace {
 
-#ifndef CV_TEAM_WARPS
-#define CV_TEAM_WARPS 6
-#endif
-#ifndef CV_MAXNREG
-#define CV_MAXNREG 128
-#endif
+// TW warps per team (6 or 8): 12 or 16 warps per CTA, at most 4 per SM sub-partition
 constexpr int kCvTeams = 2;
-constexpr int kCvTeamWarps = CV_TEAM_WARPS;
-constexpr int kCvConsumers = kCvTeams * kCvTeamWarps;  // 12
-constexpr int kCvThreads = 32 * (1 + kCvConsumers);     // producer warp + consumers
-constexpr int kCvHalfWarps = 2 * kCvTeamWarps;          // half-warps per team
-constexpr int kCvMaxGph = 8;                            // groups per half-warp: K <= 12 * 8 * 256
+constexpr int kCvMaxGph = 6;  // groups per half-warp: K <= 16 * 6 * 256
 constexpr int kCvMaxStages = 16;
 constexpr int kCvTileBytes = 2 * 16 * cv::kXRow;  // per consumer warp: one padded double tile per half-warp
 constexpr int kCvOffRed = 512;      // [team][phase][warp] row-max words, after the mbarriers
 constexpr int kCvOffTiles = 1024;
-constexpr int kCvOffRing = kCvOffTiles + kCvConsumers * kCvTileBytes;
+constexpr int cv_off_ring(int tw) { return kCvOffTiles + kCvTeams * tw * kCvTileBytes; }
 constexpr int kCvSmemLimit = 232448;
-constexpr unsigned kErrCvProducer = 0x311, kErrCvFull = 0x312, kErrCvTeam = 0x313, kErrCvDrain = 0x314;
+constexpr unsigned kErrCvFull = 0x312, kErrCvTeam = 0x313, kErrCvDrain = 0x314;
 
 __device__ __forceinline__ void cv_bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -142,8 +134,8 @@ __device__ __forceinline__ Words8 cv_group_slow(const uint8_t* st, int K, int g,
   return r;
 }
 
-template <int GPH, int ACT>
-__global__ void __maxnreg__(CV_MAXNREG)
+template <int TW, int GPH, int ACT>
+__global__ void __maxnreg__(128)
     convrot_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t m, int8_t* __restrict__ q,
                    float* __restrict__ scale, __nv_bfloat16* __restrict__ sx, int sum_group, int64_t kp, int stages,
                    int ng) {
@@ -154,67 +146,58 @@ __global__ void __maxnreg__(CV_MAXNREG)
   extern __shared__ __align__(128) uint8_t cv_smem[];
   uint8_t* smem = cv_smem;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty_bar = full_bar + kCvMaxStages;
-  uint64_t* team_bar = empty_bar + kCvMaxStages;  // [kCvTeams]
+  uint64_t* team_bar = full_bar + kCvMaxStages;  // [kCvTeams]
   uint32_t* red = reinterpret_cast<uint32_t*>(smem + kCvOffRed);
-  uint8_t* ring = smem + kCvOffRing;
+  uint8_t* ring = smem + cv_off_ring(TW);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t G = gridDim.x;
   const int64_t cnt = m > (int64_t)blockIdx.x ? (m - blockIdx.x + G - 1) / G : 0;  // rows of this CTA
   const int S = stages;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kCvTeamWarps);
-    }
-    for (int t = 0; t < kCvTeams; ++t) mbar_init(&team_bar[t], kCvTeamWarps);
+    for (int s = 0; s < S; ++s) mbar_init(&full_bar[s], 1);
+    for (int t = 0; t < kCvTeams; ++t) mbar_init(&team_bar[t], TW);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- producer ----------------
-      int64_t j = 0;
-      for (; j < cnt; ++j) {
-        const int s = (int)(j % S);
-        const uint32_t use = (uint32_t)(j / S);
-        if (!mbar_wait(&empty_bar[s], (use & 1u) ^ 1u, kErrCvProducer)) break;
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)row_bytes);
-        cv_bulk_g2s(ring + (size_t)s * row_bytes, x + (blockIdx.x + j * G) * ldx, (uint32_t)row_bytes,
-                    &full_bar[s]);
-      }
-      // every copy issued lands before the CTA may exit
-      for (int64_t i = (j > S ? j - S : 0); i < j; ++i)
-        mbar_wait(&full_bar[i % S], (uint32_t)(i / S) & 1u, kErrCvDrain, 200000000ull);
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  const int cw = warp - 1;
-  const int team = cw / kCvTeamWarps, tw = cw - team * kCvTeamWarps;
+  const int cw = warp;
+  const int team = cw / TW, tw = cw - team * TW;
+  // The first lane of each team fills that team's stages: S is even, so stage j % S
+  // always holds rows of team j % 2. Rows team, team + 2, ... below S first; then row
+  // j + S as soon as the team has read row j (its row-absmax barrier completes after
+  // every warp of the team has read the stage), overlapping the quantization of row j.
+  const bool leader = tw == 0 && lane == 0;
+  auto fill = [&](int64_t j) {
+    const int s = (int)(j % S);
+    mbar_arrive_expect_tx(&full_bar[s], (uint32_t)row_bytes);
+    cv_bulk_g2s(ring + (size_t)s * row_bytes, x + (blockIdx.x + j * G) * ldx, (uint32_t)row_bytes, &full_bar[s]);
+  };
+  int64_t filled = team;  // (leader) next row of the team to fill
+  if (leader)
+    for (; filled < cnt && filled < S; filled += kCvTeams) fill(filled);
   const int h = lane >> 4, li = lane & 15;
-  const int hw = 2 * tw + h;  // groups hw, hw + 12, ...
+  const int hw = 2 * tw + h;  // groups hw, hw + 2 TW, ...
   uint8_t* tile = smem + kCvOffTiles + cw * kCvTileBytes + h * (16 * cv::kXRow);
   uint8_t* const wr_even = tile + cv::xtile_off(h, li);         // row e ^ h for even e: e + h
   uint8_t* const wr_odd = tile + cv::xtile_off(0, li) - h * cv::kXRow;  // odd e: e - h
   const uint8_t* const rd_row = tile + cv::xtile_pair_off(li, 0);
-  uint32_t* rteam = red + team * (2 * kCvTeamWarps);
+  uint32_t* rteam = red + team * (2 * TW);
   const int lanes_per_sum = sum_group / 16;
   uint32_t team_phase = 0;
+  int64_t waited = team;  // next row of the team whose fill has not been waited for
   for (int64_t j = team; j < cnt; j += kCvTeams) {
     const int s = (int)(j % S);
     const int64_t row = blockIdx.x + j * G;
     if (!mbar_wait(&full_bar[s], (uint32_t)(j / S) & 1u, kErrCvFull)) break;
+    waited = j + kCvTeams;
     const uint8_t* st = ring + (size_t)s * row_bytes;
     uint32_t park[GPH][8];
     uint32_t amax = 0u;
     uint32_t slow_mask = 0u;  // groups of this half-warp that take the exact integer path
 #pragma unroll
     for (int i = 0; i < GPH; ++i) {
-      const int g = hw + kCvHalfWarps * i;
+      const int g = hw + 2 * TW * i;
       const bool ok = g < ng;  // the same for the 16 lanes of a half-warp; empty slots carry zeros
       // register e holds row e ^ h of column li: row e + h (e even) or e - h (e odd)
       const uint16_t* col_even = reinterpret_cast<const uint16_t*>(st + (ok ? g : 0) * 512 + 2 * li) + 16 * h;
@@ -229,12 +212,8 @@ __global__ void __maxnreg__(CV_MAXNREG)
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const uint16_t* p = (e & 1 ? col_odd : col_even) + 16 * e;
-        uint32_t a = 0u;
-        if (ok) {
-          const uint32_t gate = p[0];
-          const uint32_t up = ACT == H3B200_ACT_SWIGLU ? p[K] : 0u;
-          a = cv_act<ACT>(gate, up);
-        }
+        // an empty slot reads group 0 (valid memory); its values are never used
+        const uint32_t a = cv_act<ACT>(p[0], ACT == H3B200_ACT_SWIGLU ? (uint32_t)p[K] : 0u);
         v[e] = a;
         xf[e] = __uint_as_float(a << 16);
         fmx = fmaxf(fmx, fabsf(xf[e]));
@@ -310,7 +289,7 @@ __global__ void __maxnreg__(CV_MAXNREG)
 #pragma unroll 1
       for (int i = 0; i < GPH; ++i) {
         const bool mine = (slow_mask >> i) & 1u;
-        const int g = hw + kCvHalfWarps * i;
+        const int g = hw + 2 * TW * i;
         Words8 r = {{0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u}};
         if (mine) r = cv_group_slow<ACT>(st, K, g, li);
         __syncwarp();
@@ -324,7 +303,7 @@ __global__ void __maxnreg__(CV_MAXNREG)
 #pragma unroll
       for (int i = 0; i < GPH; ++i)
         if ((slow_mask >> i) & 1u) {
-          const uint8_t* src = st + (hw + kCvHalfWarps * i) * 512 + 32 * li;
+          const uint8_t* src = st + (hw + 2 * TW * i) * 512 + 32 * li;
           const uint4 a = *reinterpret_cast<const uint4*>(src), b = *reinterpret_cast<const uint4*>(src + 16);
           park[i][0] = a.x; park[i][1] = a.y; park[i][2] = a.z; park[i][3] = a.w;
           park[i][4] = b.x; park[i][5] = b.y; park[i][6] = b.z; park[i][7] = b.w;
@@ -333,33 +312,34 @@ __global__ void __maxnreg__(CV_MAXNREG)
     }
 #pragma unroll
     for (int i = 0; i < GPH; ++i)
-      if (hw + kCvHalfWarps * i < ng) {
+      if (hw + 2 * TW * i < ng) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) amax = bf16x2_absmax(amax, park[i][k]);
       }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);  // this warp's reads of the stage are done
-
-    // row absmax over the team
+    // row absmax over the team (its barrier also marks every read of the stage done)
     amax &= 0x7FFF7FFFu;
     amax = max(amax & 0xFFFFu, amax >> 16);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    uint32_t* rr = rteam + (team_phase & 1u) * kCvTeamWarps;
+    uint32_t* rr = rteam + (team_phase & 1u) * TW;
     if (lane == 0) {
       rr[tw] = amax;
       mbar_arrive(&team_bar[team]);
     }
     if (!mbar_wait(&team_bar[team], team_phase & 1u, kErrCvTeam)) break;
     ++team_phase;
+    if (leader && j + S < cnt) {
+      fill(j + S);
+      filled = j + S + kCvTeams;
+    }
     uint32_t rowbits = rr[0];
 #pragma unroll
-    for (int t = 1; t < kCvTeamWarps; ++t) rowbits = max(rowbits, rr[t]);
+    for (int t = 1; t < TW; ++t) rowbits = max(rowbits, rr[t]);
     const float s_row = fmaxf(__fdiv_rn(__uint_as_float(rowbits << 16), 127.0f), 1e-30f);
     const float rcp = __frcp_rn(quant_divisor(s_row));
 #pragma unroll
     for (int i = 0; i < GPH; ++i) {
-      const int g = hw + kCvHalfWarps * i;
+      const int g = hw + 2 * TW * i;
       const bool ok = g < ng;
       const uint32_t w0[4] = {park[i][0], park[i][1], park[i][2], park[i][3]};
       const uint32_t w1[4] = {park[i][4], park[i][5], park[i][6], park[i][7]};
@@ -381,35 +361,45 @@ __global__ void __maxnreg__(CV_MAXNREG)
         for (int64_t i2 = K / sum_group + lane; i2 < kp; i2 += 32) sx[row * kp + i2] = __float2bfloat16_rn(0.0f);
     }
   }
+  // every copy this team's leader issued lands before the CTA may exit (rows left
+  // unconsumed only after a bounded wait failed)
+  if (leader)
+    for (int64_t i = waited; i < filled; i += kCvTeams)
+      mbar_wait(&full_bar[i % S], (uint32_t)(i / S) & 1u, kErrCvDrain, 200000000ull);
 }
 
-template <int GPH>
+template <int TW, int GPH>
 cudaError_t cv_launch(int act, const __nv_bfloat16* x, int64_t ldx, int64_t m, int8_t* q, float* scale,
                       __nv_bfloat16* sx, int sum_group, int64_t kp, int stages, int ng, int smem, unsigned grid,
                       cudaStream_t stream) {
+  constexpr int threads = 32 * kCvTeams * TW;
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kCvSmemLimit);
     if (e != cudaSuccess) return e;
     cudaFuncAttributes fa;
     if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
-    // 13 warps need one SM sub-partition (a quarter of the register file) to hold 4 of
-    // them, hence the 128-register limit on the kernel
-    if (fa.maxThreadsPerBlock < kCvThreads) return cudaErrorLaunchOutOfResources;
-    kern<<<grid, kCvThreads, smem, stream>>>(x, ldx, m, q, scale, sx, sum_group, kp, stages, ng);
+    // 16 warps put 4 on each SM sub-partition (a quarter of the register file), hence
+    // the 128-register limit on the kernel
+    if (fa.maxThreadsPerBlock < threads) return cudaErrorLaunchOutOfResources;
+    kern<<<grid, threads, smem, stream>>>(x, ldx, m, q, scale, sx, sum_group, kp, stages, ng);
     return cudaGetLastError();
   };
-  if (act == H3B200_ACT_GELU_TANH) return go(convrot_kernel<GPH, H3B200_ACT_GELU_TANH>);
-  if (act == H3B200_ACT_SWIGLU) return go(convrot_kernel<GPH, H3B200_ACT_SWIGLU>);
-  return go(convrot_kernel<GPH, H3B200_ACT_NONE>);
+  if (act == H3B200_ACT_GELU_TANH) return go(convrot_kernel<TW, GPH, H3B200_ACT_GELU_TANH>);
+  if (act == H3B200_ACT_SWIGLU) return go(convrot_kernel<TW, GPH, H3B200_ACT_SWIGLU>);
+  return go(convrot_kernel<TW, GPH, H3B200_ACT_NONE>);
 }
+
+// Team size for a row of ng groups: rows of up to 24 groups keep every half-warp of
+// 6-warp teams busy (more warps would idle); longer rows use 8-warp teams (16 warps).
+int cv_team_warps(int64_t ng) { return ng <= 24 ? 6 : 8; }
 
 }  // namespace
 
 int64_t convrot_max_k(int act) {
-  // rows of at most 12 half-warps x 8 groups, and at least two stages of the raw row in shared memory
-  const int64_t by_regs = (int64_t)kCvHalfWarps * kCvMaxGph * 256;
+  // rows of at most 16 half-warps x 6 groups, and at least two stages of the raw row in shared memory
+  const int64_t by_regs = (int64_t)kCvTeams * 8 * kCvMaxGph * 256;
   const int64_t per_elem = act == H3B200_ACT_SWIGLU ? 4 : 2;
-  const int64_t by_smem = ((kCvSmemLimit - 1024 - kCvOffRing) / 2 / per_elem) / 256 * 256;
+  const int64_t by_smem = ((kCvSmemLimit - 1024 - cv_off_ring(8)) / 2 / per_elem) / 256 * 256;
   return std::min(by_regs, by_smem);
 }
 
@@ -426,26 +416,29 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
     if (e != cudaSuccess) return e;
   }
   const int ng = (int)(k / 256);
-  const int gph = (ng + kCvHalfWarps - 1) / kCvHalfWarps;
+  const int tw = cv_team_warps(ng);
+  const int gph = (ng + 2 * tw - 1) / (2 * tw);
   const int64_t row_bytes = (act == H3B200_ACT_SWIGLU ? 4 : 2) * k;
-  int stages = (int)std::min<int64_t>(kCvMaxStages, (kCvSmemLimit - 1024 - kCvOffRing) / row_bytes);
+  int stages = (int)std::min<int64_t>(kCvMaxStages, (kCvSmemLimit - 1024 - cv_off_ring(tw)) / row_bytes);
   stages &= ~1;  // even: each stage serves one team
   if (stages < 2) return cudaErrorNotSupported;
-  const int smem = 1024 + kCvOffRing + stages * (int)row_bytes;
+  const int smem = 1024 + cv_off_ring(tw) + stages * (int)row_bytes;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned grid = (unsigned)std::min<int64_t>(m, (int64_t)num_sms(dev));
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
   __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
   const int sg = sx != nullptr ? (int)sum_group : 16;
+  if (tw == 6) {
+    if (gph == 1) return cv_launch<6, 1>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    return cv_launch<6, 2>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+  }
   switch (gph) {
-    case 1: return cv_launch<1>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    case 2: return cv_launch<2>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    case 3: return cv_launch<3>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    case 4: return cv_launch<4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    case 5: return cv_launch<5>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    case 6: return cv_launch<6>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    default: return cv_launch<8>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    case 2: return cv_launch<8, 2>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    case 3: return cv_launch<8, 3>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    case 4: return cv_launch<8, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    case 5: return cv_launch<8, 5>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    default: return cv_launch<8, 6>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
   }
 }
 
