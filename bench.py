@@ -149,7 +149,8 @@ class ClockSampler:
 # CASE is one of ``quantize`` (fc1 input quantizer, K = 3072), ``fc1`` (INT8 GEMM
 # with the GELU + row-absmax epilogue; ``fc1_bf16`` / ``fc1_i32``: the same GEMM with
 # the plain dequant or the int32 epilogue), ``requant`` (fc2 input quantizer with a
-# given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue),
+# given absmax, K = 12288), ``fc2`` (INT8 GEMM with the gated-residual epilogue), ``fc2_rq``
+# (the same GEMM quantizing its bf16 input itself, as the fused MLP runs it),
 # ``mlp`` (the whole fused MLP call), ``mlp_w4a8`` (the config-2 W4A8 MLP call), ``mlp_swiglu``
 # (the H3 SwiGLU MLP at d 5,376 / ffn 14,336, ConvRot fc1 and fc2, 8,192-token chunks),
 # ``mlp_swiglu_w4`` (the same MLP on W4A8 weights in the H3 release format: group 16,
@@ -169,7 +170,7 @@ class ClockSampler:
 # process exits non-zero if a kernel reports an error.
 # ---------------------------------------------------------------------------
 
-CASES = ["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "mlp", "mlp_w4a8", "mlp_swiglu",
+CASES = ["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "fc2_rq", "mlp", "mlp_w4a8", "mlp_swiglu",
          "mlp_swiglu_w4", "decode_w4", "qknorm_h3", "qkv_h3", "convrot", "convrot_x", "norm_rope", "rms_adaln",
          "rms_adaln_h3"]
 
@@ -326,9 +327,14 @@ def run_case(case: str, m: int, iters: int, report: bool = False):
         elif case == "fc1_i32":
             acc = torch.empty(m, D_FFN, dtype=torch.int32, device=dev)
             ms = _case_timed(lambda: ops.int8_gemm_fused(xq, wt.w1q, ops.EPI_I32, out=acc), iters, report)
-        elif case in ("requant", "fc2"):
+        elif case in ("requant", "fc2", "fc2_rq"):
             fc1()
-            if case == "requant":
+            if case == "fc2_rq":
+                work = torch.empty(int(h3b200.library().h3b200_requant_gemm_workspace_bytes(m, D_FFN)),
+                                   dtype=torch.uint8, device=dev)
+                ms = _case_timed(lambda: h3b200.requant_gemm_gated_residual(act, amax, wt.w2q, wt.s2, gate, res,
+                                                                            out=out, workspace=work), iters, report)
+            elif case == "requant":
                 ms = _case_timed(lambda: ops.quantize_int8_rowwise_absmax(act, amax), iters, report)
             else:
                 q2, xs2 = ops.quantize_int8_rowwise_absmax(act, amax)
@@ -562,11 +568,20 @@ def run_ours(args, rank, world, local_rank):
     def k_fc2():
         ops.int8_gemm_fused(q2, wt.w2q, ops.EPI_GATED_RESIDUAL, xs2, wt.s2, gate=gate, residual=res, out=out)
 
-    for f in (k_quant, k_fc1, k_requant, k_fc2):
+    rq_work = torch.empty(int(lib.h3b200_requant_gemm_workspace_bytes(M_TOKENS, D_FFN)), dtype=torch.uint8,
+                          device=dev)
+
+    def k_fc2_rq():
+        h3b200.requant_gemm_gated_residual(act, amax, wt.w2q, wt.s2, gate, res, out=out, workspace=rq_work)
+
+    for f in (k_quant, k_fc1, k_requant, k_fc2, k_fc2_rq):
         f()
     reps = 20
+    # the step runs quantize_x, fc1 and fc2_requant_gated_residual (fc2 quantizing its input
+    # itself); the separate requant kernel and plain fc2 are timed for comparison
     comp_ms = {name: timed(f, reps, stream) for name, f in
-               (("quantize_x", k_quant), ("fc1_gemm_gelu_absmax", k_fc1), ("requant_fc2_input", k_requant),
+               (("quantize_x", k_quant), ("fc1_gemm_gelu_absmax", k_fc1),
+                ("fc2_requant_gated_residual", k_fc2_rq), ("requant_fc2_input", k_requant),
                 ("fc2_gemm_gated_residual", k_fc2))}
     fc1_ops = 2.0 * M_TOKENS * D_MODEL * D_FFN
     fc2_ops = fc1_ops

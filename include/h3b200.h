@@ -152,6 +152,30 @@ H3B200_API int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t
                                       float* row_absmax, h3b200_stream_t stream);
 
 /*
+ * fc2 of the fused MLP with the requantization of its input inside the GEMM:
+ *   q, xs = quantize_int8_rowwise(h)   with max |h[row, :]| given in h_absmax[row]
+ *   out   = bf16(residual + bf16(bf16(float(q . W^T) * (xs * w_scale)) (+ bias)) * gate)
+ * the requant -> int8_linear -> addcmul_ chain of the reference's fused MLP
+ * (h3serve/native_engine/model/fused_mlp.py:414-425; quantize_int8_rowwise
+ * backends/eager/quantization.py:857-875). h_absmax is what epilogue 2 of
+ * h3b200_int8_gemm_fused reduces. The GEMM's spare warps quantize h's rows into
+ * the workspace in row order while the tensor cores run; tiles wait (bounded)
+ * for their rows. gate is one row [n] (row_map NULL) or rows at stride ldg
+ * selected per output row by row_map. Bit-identical to
+ * h3b200_quantize_int8_rowwise_absmax followed by epilogue 3.
+ * workspace: h3b200_requant_gemm_workspace_bytes(m, k) bytes, 256-byte aligned.
+ * k % 16 == 0, n % 8 == 0, ldh % 8 == 0, h 16-byte aligned; out may alias residual.
+ */
+H3B200_API int64_t h3b200_requant_gemm_workspace_bytes(int64_t m, int64_t k);
+H3B200_API int h3b200_requant_gemm_gated_residual(const void* h, int64_t ldh, const float* h_absmax,
+                                                  const int8_t* w, const float* w_scale, int64_t w_scale_numel,
+                                                  const void* bias, const void* gate, int64_t ldg,
+                                                  const int32_t* row_map, const void* residual, int64_t ldr,
+                                                  void* out, int64_t ldo, int64_t m, int64_t n, int64_t k,
+                                                  void* workspace, int64_t workspace_bytes,
+                                                  h3b200_stream_t stream);
+
+/*
  * Dequant + gated residual on reduced int32 accumulators (tensor-parallel fc2):
  * out = bf16(residual + bf16(float(acc) * (x_scale[row] * w_scale[col])) * gate[col]).
  * The same arithmetic as epilogue 3 of h3b200_int8_gemm_fused, for when the

@@ -264,6 +264,39 @@ int h3b200_int8_gemm_fused(const int8_t* a, int64_t lda, const int8_t* w, int64_
   return from_cuda(h3::launch_gemm_i8(g, S(stream)), "int8_gemm_fused");
 }
 
+int64_t h3b200_requant_gemm_workspace_bytes(int64_t m, int64_t k) {
+  return round_up(m * k, 256) + round_up(h3::requant_ready_count(m) * 4, 256) + 256;
+}
+
+int h3b200_requant_gemm_gated_residual(const void* h, int64_t ldh, const float* h_absmax, const int8_t* w,
+                                       const float* w_scale, int64_t w_scale_numel, const void* bias,
+                                       const void* gate, int64_t ldg, const int32_t* row_map, const void* residual,
+                                       int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n, int64_t k,
+                                       void* workspace, int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("requant_gemm_gated_residual", stream);
+  if (m < 0 || n < 0 || k < 0 || ldh < k || ldr < n || ldo < n) return fail(H3B200_ERR_INVALID, "requant_gemm_gated_residual: bad shape");
+  if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "requant_gemm_gated_residual: weight scale must be scalar or per-output-channel");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!h || !h_absmax || !w || !w_scale || !gate || !residual || !out) return fail(H3B200_ERR_INVALID, "requant_gemm_gated_residual: NULL pointer");
+  if (row_map != nullptr && (ldg < n || ldg % 8)) return fail(H3B200_ERR_INVALID, "requant_gemm_gated_residual: gate row stride %lld must be >= n and a multiple of 8", (long long)ldg);
+  if (k % 16 || n % 8 || ldh % 8) return fail(H3B200_ERR_UNSUPPORTED, "requant_gemm_gated_residual: needs k %% 16 == 0, n %% 8 == 0 and ldh %% 8 == 0");
+  if (workspace == nullptr || workspace_bytes < h3b200_requant_gemm_workspace_bytes(m, k)) return fail(H3B200_ERR_INVALID, "requant_gemm_gated_residual: workspace too small (need %lld bytes)", (long long)h3b200_requant_gemm_workspace_bytes(m, k));
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* q = static_cast<int8_t*>(c.take(m * k));
+  unsigned int* ready = static_cast<unsigned int*>(c.take(h3::requant_ready_count(m) * 4));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "requant_gemm_gated_residual: workspace too small");
+  cudaStream_t st = S(stream);
+  cudaError_t e = cudaMemsetAsync(ready, 0, (size_t)(h3::requant_ready_count(m) * 4), st);
+  if (e != cudaSuccess) return from_cuda(e, "requant_gemm_gated_residual: memset");
+  h3::GemmArgs g;
+  g.a = q; g.w = w; g.m = m; g.n = n; g.k = k; g.lda = k; g.ldw = k;
+  g.epilogue = h3::kEpiGatedResidual; g.w_scale = w_scale; g.w_scale_per_channel = (w_scale_numel == n && n > 1) ? 1 : 0;
+  g.requant_src = h; g.requant_lds = ldh; g.requant_ready = ready; g.row_absmax = const_cast<float*>(h_absmax);
+  g.bias = bias; g.gate = gate; g.row_map = row_map; g.ldg = row_map != nullptr ? ldg : 0;
+  g.residual = residual; g.ldr = ldr; g.out = out; g.ldo = ldo;
+  return from_cuda(h3::launch_gemm_i8(g, st), "requant_gemm_gated_residual");
+}
+
 int h3b200_dequant_gated_residual(const int32_t* acc, const float* x_scale, const float* w_scale, const void* gate,
                                   const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int64_t n,
                                   h3b200_stream_t stream) {
@@ -318,14 +351,18 @@ static int fused_gated_mlp_impl(const char* what, const void* x, int64_t ldx, co
   int8_t* xq = static_cast<int8_t*>(c.take(m * d));
   float* xs = static_cast<float*>(c.take(m * 4));
   float* amax = static_cast<float*>(c.take(m * 4));
-  float* xs2 = static_cast<float*>(c.take(m * 4));
+  // the fc2 kernel requantizes fc1's output itself; this slot holds its block counters
+  unsigned int* ready = static_cast<unsigned int*>(c.take(m * 4));
   void* a = c.take(m * ffn * 2);
   int8_t* q2 = static_cast<int8_t*>(c.take(m * ffn));
   if (!c.ok) return fail(H3B200_ERR_INVALID, "%s: workspace too small", what);
   cudaStream_t st = S(stream);
   cudaError_t e = h3::launch_quantize_rows(x, ldx, m, d, H3B200_ACT_NONE, nullptr, xq, xs, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: quantize x");
-  e = cudaMemsetAsync(amax, 0, m * 4, st);
+  // one memset zeroes the row absmax and the counters that follow it
+  const int64_t zero_bytes = reinterpret_cast<uint8_t*>(ready + h3::requant_ready_count(m)) -
+                             reinterpret_cast<uint8_t*>(amax);
+  e = cudaMemsetAsync(amax, 0, (size_t)zero_bytes, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: memset");
   h3::GemmArgs g1;
   g1.a = xq; g1.w = w1; g1.m = m; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
@@ -333,15 +370,14 @@ static int fused_gated_mlp_impl(const char* what, const void* x, int64_t ldx, co
   g1.out = a; g1.ldo = ffn; g1.row_absmax = amax;
   e = h3::launch_gemm_i8(g1, st);
   if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: fc1");
-  e = h3::launch_quantize_rows(a, ffn, m, ffn, H3B200_ACT_NONE, amax, q2, xs2, st);
-  if (e != cudaSuccess) return from_cuda(e, "fused_gated_mlp: requant");
   h3::GemmArgs g2;
   g2.a = q2; g2.w = w2; g2.m = m; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
-  g2.epilogue = h3::kEpiGatedResidual; g2.a_scale = xs2; g2.w_scale = s2; g2.w_scale_per_channel = 1;
+  g2.epilogue = h3::kEpiGatedResidual; g2.w_scale = s2; g2.w_scale_per_channel = 1;
+  g2.requant_src = a; g2.requant_lds = ffn; g2.requant_ready = ready; g2.row_absmax = amax;
   g2.gate = gate; g2.row_map = row_map; g2.ldg = row_map != nullptr ? ldg : 0;
   g2.residual = residual; g2.ldr = ldr; g2.out = out; g2.ldo = ldo;
   e = h3::launch_gemm_i8(g2, st);
-  return from_cuda(e, "fused_gated_mlp: fc2");
+  return from_cuda(e, "fused_gated_mlp: fc2 (with the requantization of its input)");
 }
 
 extern "C" {

@@ -96,6 +96,14 @@ struct KParams {
   const float4* rope_t;
   float qk_eps;
   int up_row;  // kEpiSwiGLU: first up row of W (the output width f)
+  // in-kernel requantization of A (kEpiGatedResidual, GemmArgs::requant_src)
+  const __nv_bfloat16* rq_src;
+  int64_t rq_lds;
+  int8_t* rq_dst;
+  unsigned int* rq_ready;     // one count of finished units per block of tile rows (zero at launch)
+  unsigned int* rq_horizon;   // highest block the tiles have asked for (zero at launch)
+  int64_t rq_units;           // m * rq_upr
+  int rq_upr;                 // units of kRqUnit elements per row
 };
 
 template <int EPI>
@@ -315,6 +323,152 @@ __device__ __forceinline__ void tile_coords(int tile, const KParams& p, int& m_b
   m_blk = g * p.group_m + (rem - n_blk * gm);
 }
 
+// ---- in-kernel requantization of A (fc2 of the fused MLP, kEpiGatedResidualRq) ----
+// The A operand of fc2 is quantize_int8_rowwise(gelu(fc1)) with the row absmax that
+// fc1's epilogue already reduced. Instead of a separate pass, the CTAs' non-MMA warps
+// produce it while the tensor cores run: warps 2-3 (idle otherwise) and the eight
+// epilogue warps whenever their next accumulator is not ready yet (fc2's epilogue is
+// short next to its mainloop). A unit is kRqUnit consecutive elements of one row;
+// unit u belongs to quantizing warp u mod (kRqSlots * CTAs), so each warp walks the rows
+// in order. A unit's 16-byte vectors and its row absmax are loaded at once, quantized
+// like quantize_int8_rowwise and stored, and the unit is counted for its block of tile
+// rows; the TMA producer loads a tile's A rows only once that block's count is
+// complete. A warp takes its next unit only while that unit's block is at most `lead`
+// blocks past the highest block the tiles have asked for, so quantized rows wait in L2
+// briefly. No quantizing warp holds a unit while waiting on anything, units of blocks
+// the tiles already asked for are never held back, and an epilogue warp whose tile
+// waits for A has its accumulator not ready, so it quantizes: the dependency cannot
+// deadlock (the persistent grid is resident).
+constexpr int kRqUnit = 4096;      // elements per unit: 16 vectors of 8 per lane
+constexpr int kRqSlots = 2 + NUM_EPI_WARPS;
+constexpr unsigned kErrRequant = 0x108;
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned int* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned int* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// non-blocking test of a barrier phase
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Blocks the quantizing warps may run ahead of the tiles: the blocks of the first wave of
+// tiles (ncl walkers) plus two.
+__device__ __forceinline__ int requant_lead(const KParams& p, int ncl) {
+  int mb_first = 0;
+  for (int t = 0; t < ncl && t < p.num_tiles; ++t) {
+    int mb, nb;
+    tile_coords(t, p, mb, nb);
+    mb_first = max(mb_first, mb);
+  }
+  return mb_first + 2;
+}
+
+// One quantizing warp's walk over its units.
+struct RqCursor {
+  int64_t u;       // next unit of this warp
+  int64_t stride;  // kRqSlots * CTAs
+  int lead;
+  unsigned hz;     // lane 0's last view of the tiles' horizon
+};
+
+// Quantize and count unit c.u if its block is inside the window (lane 0 refreshes its
+// view of the horizon only when the cached one says no). Returns false when the warp
+// has no unit left or the window is closed.
+template <int TILE_ROWS>
+__device__ __forceinline__ bool requant_step(const KParams& p, RqCursor& c, int lane) {
+  if (c.u >= p.rq_units) return false;
+  const int row = (int)(c.u / p.rq_upr);
+  uint32_t go = 1u;
+  if (lane == 0 && row / TILE_ROWS > (int)c.hz + c.lead) {
+    c.hz = ld_relaxed_gpu(p.rq_horizon);
+    go = row / TILE_ROWS <= (int)c.hz + c.lead ? 1u : 0u;
+  }
+  if (__shfl_sync(0xffffffffu, go, 0) == 0u) return false;
+  const int c0 = (int)(c.u - (int64_t)row * p.rq_upr) * kRqUnit;
+  const int lim = p.k - c0;  // elements of the row from c0 on
+  const __nv_bfloat16* src = p.rq_src + (int64_t)row * p.rq_lds + c0;
+  int8_t* dst = p.rq_dst + (int64_t)row * p.k + c0;
+  const float am = __ldg(p.row_absmax + row);
+  uint4 v[kRqUnit / 256];
+#pragma unroll
+  for (int j = 0; j < kRqUnit / 256; ++j) {
+    const int e = 8 * (lane + 32 * j);
+    v[j] = e < lim ? ldg_nc_v4(src + e) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  const float r = __frcp_rn(quant_divisor(row_scale(am)));
+#pragma unroll
+  for (int j = 0; j < kRqUnit / 256; ++j) {
+    const int e = 8 * (lane + 32 * j);
+    if (e < lim) *reinterpret_cast<uint2*>(dst + e) = quant_vec8(v[j], r);
+  }
+  // these generic-proxy stores are read by TMA (async proxy) after the count: fence
+  // them towards the async proxy, then release the count at GPU scope
+  fence_proxy_async_global();
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    atomicAdd(p.rq_ready + row / TILE_ROWS, 1u);
+  }
+  c.u += c.stride;
+  return true;
+}
+
+// Every remaining unit of the warp, waiting (bounded) whenever the window is closed.
+template <int TILE_ROWS>
+__device__ __forceinline__ void requant_finish(const KParams& p, RqCursor& c, int lane) {
+  unsigned long long t0 = 0ull;
+  while (c.u < p.rq_units) {
+    if (requant_step<TILE_ROWS>(p, c, lane)) {
+      t0 = 0ull;
+      continue;
+    }
+    if (t0 == 0ull) t0 = global_ns();
+    __nanosleep(256);
+    if (status_bad()) return;
+    if (global_ns() - t0 > kWaitTimeoutNs) {
+      set_status(kErrRequant);
+      return;
+    }
+  }
+}
+
+// Producer side: wait (bounded) until block b's A rows are all written.
+__device__ __forceinline__ bool requant_wait(const KParams& p, int b, int tile_rows) {
+  const unsigned need = (unsigned)(min(tile_rows, p.m - b * tile_rows) * p.rq_upr);
+  const unsigned int* c = p.rq_ready + b;
+  if (ld_acquire_gpu(c) < need) {
+    const unsigned long long t0 = global_ns();
+    while (ld_acquire_gpu(c) < need) {
+      __nanosleep(256);
+      if (status_bad()) return false;
+      if (global_ns() - t0 > kWaitTimeoutNs) {
+        set_status(kErrRequant);
+        return false;
+      }
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
+
 // ---- kEpiQKV helpers: one thread holds one head (128 values) of one token ----
 // |bf16| of the low / high half of w as a double, built from its bits (exact for
 // normal values; zero and subnormals become a value below 2^-126 whose square
@@ -360,12 +514,15 @@ __device__ __forceinline__ void qkv_rope(uint32_t (&h)[64], const float4* __rest
 // full barrier, each commit of rank 0 arrives on the barriers of both CTAs, and
 // rank r's TMEM receives output rows [128 r, 128 r + 128) of the tile. Both
 // epilogues release an accumulator on rank 0's barrier.
-template <int EPI, int CG>
+template <int EPI_ID, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
                    const KParams p) {
+  // kEpiGatedResidualRq: the gated-residual epilogue on an A operand this kernel quantizes
+  constexpr bool kRq = EPI_ID == kEpiGatedResidualRq;
+  constexpr int EPI = kRq ? kEpiGatedResidual : EPI_ID;
   constexpr bool kCorr = is_corr_epi<EPI>();
   constexpr bool kInBox = EPI == kEpiGatedResidual || EPI == kEpiGatedResidualCorr;
   constexpr int kBBytes = B_BYTES / CG;
@@ -447,6 +604,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  RqCursor rq{};  // warps 2-11: this warp's units of A (kEpiGatedResidualRq)
+  if constexpr (kRq) {
+    if (warp >= 2) {
+      rq.u = (int64_t)blockIdx.x * kRqSlots + (warp - 2);
+      rq.stride = (int64_t)gridDim.x * kRqSlots;
+      rq.lead = requant_lead(p, ncl);
+      rq.hz = 0u;
+      if (warp < EPI_WARP0) requant_finish<kTileRows>(p, rq, lane);
+    }
+  }
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
@@ -460,6 +628,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // then the 128 up rows of those columns (rank 1 of a pair loads the up rows)
         const int b_row = EPI == kEpiSwiGLU ? n_blk * (BN / 2) + (int)rank * p.up_row
                                             : n_blk * BN + (int)rank * (BN / CG);
+        if constexpr (kRq) {
+          atomicMax(p.rq_horizon, (unsigned)m_blk);
+          if (!requant_wait(p, m_blk, kTileRows)) break;  // A rows not written in time
+        }
         for (int kb = 0; kb < p.num_k_blk; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (uint32_t)(it / kStages) & 1u;
@@ -626,10 +798,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
       }
+      if constexpr (kRq) {
+        // quantize this warp's units of A while the accumulator is not ready
+        for (;;) {
+          const uint32_t ready = mbar_test(&tfull_bar[acc], acc_ph) ? 1u : 0u;
+          if (__shfl_sync(0xffffffffu, ready, 0) != 0u) break;
+          if (!requant_step<kTileRows>(p, rq, lane)) break;
+        }
+      }
       if (!mbar_wait(&tfull_bar[acc], acc_ph, kErrEpi)) break;
       tc_fence_after();
       float xs = 0.0f;
-      if constexpr (EPI != kEpiI32) xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
+      if constexpr (kRq) {  // A was quantized in this kernel: its row scale from the row absmax
+        xs = (row < p.m) ? row_scale(__ldg(p.row_absmax + row)) : 0.0f;
+      } else if constexpr (EPI != kEpiI32) {
+        xs = (row < p.m) ? __ldg(p.a_scale + row) : 0.0f;
+      }
       uint32_t amax_bits = 0u;
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + half * 128);
       const int box_row0 = row0 + quarter * 32;
@@ -910,6 +1094,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    if constexpr (kRq) requant_finish<kTileRows>(p, rq, lane);  // units other tiles may still need
     if constexpr (kInBox) {
       if (in_pending) mbar_wait(&in_bar[ew], in_phase, kErrDrain, 200000000ull);  // let a late box land
     }
@@ -993,7 +1178,9 @@ cudaError_t launch_cg(int epilogue, const TensorMaps& t, const KParams& kp, int 
     case kEpiI32: return launch_epi<kEpiI32, CG>(t, kp, grid, stream);
     case kEpiBF16: return launch_epi<kEpiBF16, CG>(t, kp, grid, stream);
     case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, CG>(t, kp, grid, stream);
-    case kEpiGatedResidual: return launch_epi<kEpiGatedResidual, CG>(t, kp, grid, stream);
+    case kEpiGatedResidual:
+      if (kp.rq_src != nullptr) return launch_epi<kEpiGatedResidualRq, CG>(t, kp, grid, stream);
+      return launch_epi<kEpiGatedResidual, CG>(t, kp, grid, stream);
     case kEpiBF16Corr: return launch_epi<kEpiBF16Corr, CG>(t, kp, grid, stream);
     case kEpiBF16CorrGelu: return launch_epi<kEpiBF16CorrGelu, CG>(t, kp, grid, stream);
     case kEpiGatedResidualCorr: return launch_epi<kEpiGatedResidualCorr, CG>(t, kp, grid, stream);
@@ -1096,6 +1283,11 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   if (a.row_map != nullptr && (a.epilogue != kEpiGatedResidual || a.ldg < a.n || a.ldg % 8 != 0 ||
                                (reinterpret_cast<uintptr_t>(a.gate) & 15)))
     return cudaErrorNotSupported;
+  if (a.requant_src != nullptr &&
+      (a.epilogue != kEpiGatedResidual || a.lda != a.k || a.k % 8 != 0 || a.requant_lds < a.k ||
+       a.requant_lds % 8 != 0 || (reinterpret_cast<uintptr_t>(a.requant_src) & 15) || a.row_absmax == nullptr ||
+       a.requant_ready == nullptr))
+    return cudaErrorNotSupported;
   const bool corr = a.epilogue == kEpiBF16Corr || a.epilogue == kEpiBF16CorrGelu || a.epilogue == kEpiGatedResidualCorr;
   if (corr && (a.sx == nullptr || a.corr_t == nullptr || a.kp <= 0 || a.kp % 64 != 0 || a.kp > kMaxCorrKp ||
                (reinterpret_cast<uintptr_t>(a.sx) & 15) || (reinterpret_cast<uintptr_t>(a.corr_t) & 15)))
@@ -1191,6 +1383,13 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.rope_t = a.rope_t;
   kp.qk_eps = a.qk_eps;
   kp.up_row = swiglu ? (int)n_out : 0;
+  kp.rq_src = static_cast<const __nv_bfloat16*>(a.requant_src);
+  kp.rq_lds = a.requant_lds;
+  kp.rq_dst = const_cast<int8_t*>(a.a);
+  kp.rq_ready = a.requant_ready;
+  kp.rq_horizon = a.requant_ready == nullptr ? nullptr : a.requant_ready + (a.m + 127) / 128;
+  kp.rq_upr = (int)((a.k + kRqUnit - 1) / kRqUnit);
+  kp.rq_units = a.m * kp.rq_upr;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

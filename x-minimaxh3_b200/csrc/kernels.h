@@ -25,6 +25,9 @@ enum GemmEpilogue : int {
   // out [m, f] = bf16(silu(g) * u) with g, u = bf16(acc * (xs * ws)) (+ bf16 bias,
   // rounded), the reference's fc1 -> silu(gate).mul_(up) in one pass
   kEpiSwiGLU = 8,
+  // internal: kEpiGatedResidual whose A operand the kernel quantizes itself
+  // (GemmArgs::requant_src); chosen by launch_gemm_i8, not by callers
+  kEpiGatedResidualRq = 9,
 };
 
 struct GemmArgs {
@@ -64,7 +67,20 @@ struct GemmArgs {
   const void* qk_w[2] = {nullptr, nullptr};
   const float4* rope_t = nullptr;
   float qk_eps = 1e-6f;
+  // kEpiGatedResidual with requant_src set: A is not an input but is produced by the
+  // same kernel. Its rows are quantize_int8_rowwise of the bf16 rows requant_src
+  // [m, k] (row stride requant_lds) with the row absmax given in row_absmax (fc1's
+  // epilogue atomics), written into a (lda == k); requant_ready holds one counter per
+  // block of tile rows and must be zero at launch. a_scale is not read: the epilogue
+  // takes the row scale from row_absmax.
+  const void* requant_src = nullptr;
+  int64_t requant_lds = 0;
+  unsigned int* requant_ready = nullptr;
 };
+
+// 32-bit words requant_ready needs for m rows: one counter per 128-row block (enough
+// for both tile shapes), then the progress word of the tiles.
+inline int64_t requant_ready_count(int64_t m) { return (m + 127) / 128 + 1; }
 
 // rope_t[p, t] = {t00, t01, t10, t11} of pair p < pairs of token t, fp32, from
 // table rows [pairs, 2, 2] at element stride fs_t (table dtype 0 fp32, 1 bf16, 2 fp16)

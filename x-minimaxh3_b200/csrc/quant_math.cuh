@@ -10,6 +10,9 @@
 
 namespace h3 {
 
+// The stored per-row scale: max(absmax / 127, 1e-30) in fp32
+__device__ __forceinline__ float row_scale(float rowmax) { return fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f); }
+
 // bf16(scale) as the divisor, with torch.finfo(bf16).tiny for a zero
 __device__ __forceinline__ float quant_divisor(float scale) {
   float sb = bf16_round(scale);

@@ -85,8 +85,6 @@ __device__ __forceinline__ float act_value(const __nv_bfloat16* xr, int64_t k, i
   return act_apply(__bfloat162float(xr[i]), act);
 }
 
-__device__ __forceinline__ float row_scale(float rowmax) { return fmaxf(__fdiv_rn(rowmax, 127.0f), 1e-30f); }
-
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

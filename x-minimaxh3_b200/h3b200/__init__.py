@@ -22,6 +22,7 @@ from .ops import (  # noqa: F401
     input_act_code,
     input_act_width,
     int8_gemm_fused,
+    requant_gemm_gated_residual,
     int8_linear,
     int8_linear_prequantized,
     mm_int8,

@@ -39,6 +39,9 @@ SIGNATURES = {
     "h3b200_int8_linear_prequantized": (_i32, [_p, _p, _p, _p, _i64, _p, _i32, _p, _i64, _i64, _i64, _p]),
     "h3b200_int8_gemm_fused": (_i32, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _p, _p, _i64, _p,
                                       _i64, _p, _p]),
+    "h3b200_requant_gemm_workspace_bytes": (_i64, [_i64, _i64]),
+    "h3b200_requant_gemm_gated_residual": (_i32, [_p, _i64, _p, _p, _p, _i64, _p, _p, _i64, _p, _p, _i64, _p, _i64,
+                                                  _i64, _i64, _i64, _p, _i64, _p]),
     "h3b200_dequant_gated_residual": (_i32, [_p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _p]),
     "h3b200_int8_linear_workspace_bytes": (_i64, [_i64, _i64]),
     "h3b200_int8_linear": (_i32, [_p, _i64, _p, _p, _i64, _p, _i32, _p, _i64, _i64, _i64, _p, _i64, _p]),

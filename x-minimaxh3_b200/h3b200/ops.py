@@ -241,6 +241,38 @@ def int8_gemm_fused(a: torch.Tensor, w: torch.Tensor, epilogue: int, a_scale=Non
     return out
 
 
+def requant_gemm_gated_residual(h: torch.Tensor, h_absmax: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor,
+                                gate: torch.Tensor, residual: torch.Tensor, out: torch.Tensor | None = None,
+                                bias: torch.Tensor | None = None, row_map: torch.Tensor | None = None,
+                                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """fc2 of the fused MLP with its input requantization inside the GEMM:
+    ``residual + bf16(int8_linear_prequantized(quantize_int8_rowwise(h))) * gate``, where
+    ``h_absmax[row]`` is max |h[row, :]| (the fc1 GELU epilogue's row absmax). ``gate`` is
+    one row [n], or rows [R, n] picked per output row by the int32 ``row_map``."""
+    _need_cuda(h, h_absmax, w, w_scale, gate, residual)
+    h2, ldh = _rows(h)
+    m, k = h2.shape
+    n = w.shape[0]
+    ws = _weight_scale(w_scale, n, h.device)
+    amax = h_absmax.reshape(-1).to(torch.float32).contiguous()
+    r2, ldr = _rows(residual)
+    if out is None:
+        out = torch.empty_like(r2)
+    o2, ldo = _rows(out)
+    if row_map is not None:
+        g2, ldg = _rows(gate)
+        rm = row_map.to(torch.int32).contiguous()
+    else:
+        g2, ldg, rm = gate.reshape(-1).contiguous(), 0, None
+    need = int(_lib.load().h3b200_requant_gemm_workspace_bytes(m, k))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=h.device)
+    _lib.call("h3b200_requant_gemm_gated_residual", h2.data_ptr(), ldh, amax.data_ptr(), w.data_ptr(), ws.data_ptr(),
+              ws.numel(), _ptr(bias), g2.data_ptr(), ldg, _ptr(rm), r2.data_ptr(), ldr, o2.data_ptr(), ldo, m, n, k,
+              workspace.data_ptr(), workspace.numel(), _stream(h))
+    return out
+
+
 def dequant_gated_residual(acc: torch.Tensor, x_scale: torch.Tensor, w_scale: torch.Tensor, gate: torch.Tensor,
                            residual: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``residual + bf16(acc * (x_scale * w_scale)) * gate`` on (cross-rank reduced) int32 accumulators."""
