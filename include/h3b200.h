@@ -103,6 +103,19 @@ H3B200_API int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k,
                                  float* scale, h3b200_stream_t stream);
 
 /*
+ * quantize_int8_rowwise(x, stochastic_rounding=seed) with seed > 0: the same row
+ * scale, then q = clamp(floor(bf16(bf16(x / bf16(scale)) + u)), -128, 127) with the
+ * counter-based noise of the reference's CUDA kernel (backends/cuda/ops/int8_linear.cu:
+ * 78-90, 186-193): u = bf16(float(pcg_hash(lo32(i + seed) ^ hi32(i + seed)) >> 8) * 2^-24)
+ * for element i = row * k + col. Replaces the stochastic branch of _round_int8
+ * (backends/eager/quantization.py:821-826), whose eager noise comes from torch.rand
+ * and is generator-specific. Arguments as h3b200_quantize_int8_rowwise.
+ */
+H3B200_API int h3b200_quantize_int8_rowwise_stochastic(const void* x, int64_t m, int64_t k, int64_t ldx, int act,
+                                                       int64_t seed, int8_t* q, float* scale,
+                                                       h3b200_stream_t stream);
+
+/*
  * Quantizer body with a precomputed per-row absmax (fp32 [m]); same arithmetic
  * as h3b200_quantize_int8_rowwise. Used for fc2's input after the fc1 epilogue
  * has reduced the row absmax (the reference quantizes the activated fc1 output
@@ -420,8 +433,13 @@ H3B200_API int h3b200_quantize_int8_rowwise_convrot(const void* x, int64_t m, in
  * backends/cuda/__init__.py:2139-2298, asymmetric correction :2294-2297).
  * grid: int8 [n, k] decoded weight (h3b200_dequant_int4_grouped_to_int8);
  * s_channel: fp32 [n]; correction: bf16 [k/group, n] or NULL (symmetric);
- * bias: bf16 [n] or NULL, symmetric weights only (then the call is
- * int8_linear(x, grid, s_channel, bias, convrot=True), eager/w4a8_int8.py:494-508).
+ * bias: bf16 [n] or NULL. Symmetric weights: the call is
+ * int8_linear(x, grid, s_channel, bias, convrot=True) (eager/w4a8_int8.py:494-508).
+ * With a correction the bias joins the dequantized value before the correction is
+ * added: out = bf16(bf16(bf16(acc * (xs * s_channel)) + bias) + corr), the order of the
+ * reference's CUDA path (bias in the dequant epilogue, then out.addmm_(sx, correction),
+ * backends/cuda/__init__.py:2265-2297); the eager path (a bf16 F.linear on the
+ * dequantized weight, eager/w4a8_int8.py:481-492) agrees within the tolerances.
  * workspace: h3b200_w4a8_linear_workspace_bytes(m, n, k, group) bytes. The
  * correction is accumulated on the tensor cores inside the INT8 GEMM's
  * epilogue (bf16 operands, fp32 accumulation), at most 128 groups.

@@ -38,6 +38,8 @@ __all__ = [
     "f32_to_bf16",
     "quantize_int8_rowwise",
     "quantize_int8_rowwise_given_absmax",
+    "quantize_int8_rowwise_stochastic",
+    "stochastic_noise_bf16",
     "gelu_tanh_bf16",
     "silu_bf16",
     "swiglu_bf16",
@@ -141,6 +143,51 @@ def quantize_int8_rowwise_given_absmax(x_bf16: np.ndarray, absmax: np.ndarray):
     Same arithmetic as ``quantize_int8_rowwise``; the fused MLP computes the
     absmax inside the fc1 epilogue and quantizes fc2's input with it."""
     return _quantize_rows(bf16_to_f32(x_bf16), np.asarray(absmax, np.float32))
+
+
+def _pcg_hash_u32(x: np.ndarray) -> np.ndarray:
+    """PCG-based integer hash (Jarzynski & Olano, JCGT 2020) on uint32 arrays, the
+    ``pcg_hash`` of backends/cuda/ops/int8_linear.cu:78-82."""
+    x = np.asarray(x, dtype=np.uint32)
+    state = x * np.uint32(747796405) + np.uint32(2891336453)
+    word = ((state >> ((state >> np.uint32(28)) + np.uint32(4))) ^ state) * np.uint32(277803737)
+    return (word >> np.uint32(22)) ^ word
+
+
+def stochastic_noise_bf16(idx: np.ndarray, seed: int) -> np.ndarray:
+    """Noise of element ``idx`` for stochastic rounding (fp32 value of a bf16 in [0, 1]):
+    ``bf16(float(pcg_hash(lo32(idx + seed) ^ hi32(idx + seed)) >> 8) * 2^-24)``,
+    ``stochastic_rng_value`` backends/cuda/ops/int8_linear.cu:84-90."""
+    key = np.asarray(idx, dtype=np.uint64) + np.uint64(seed)
+    folded = ((key & np.uint64(0xFFFFFFFF)) ^ (key >> np.uint64(32))).astype(np.uint32)
+    u = (_pcg_hash_u32(folded) >> np.uint32(8)).astype(np.float32) * np.float32(2.0 ** -24)
+    return _bf16_round(u.astype(np.float32))
+
+
+def quantize_int8_rowwise_stochastic(x_bf16: np.ndarray, seed: int):
+    """``quantize_int8_rowwise(x, stochastic_rounding=seed)`` for seed > 0 on [M, K] bf16.
+
+    Row scale as ``quantize_int8_rowwise`` (eager/quantization.py:870-873); then the
+    rounding of the reference's CUDA kernel (backends/cuda/ops/int8_linear.cu:186-193,
+    noise :84-90): ``q = clamp(floor(bf16(bf16(x / bf16(scale)) + u)), -128, 127)`` with
+    ``u`` the counter-based noise of element ``row * K + col``. (The eager branch,
+    eager/quantization.py:821-826, adds ``torch.rand`` noise from a seeded generator,
+    which is device-specific; the CUDA kernel's noise is a function of the index.)
+    Parity unpinned: the reference's CUDA kernel cannot be built or run here.
+    Returns (int8 [M, K], fp32 scale [M, 1])."""
+    xf = bf16_to_f32(x_bf16)
+    m, k = xf.shape
+    absmax = np.abs(xf).max(axis=-1, keepdims=True) if k else np.zeros((m, 1), np.float32)
+    scale = np.maximum((absmax.astype(np.float32) / F32(127.0)).astype(np.float32), F32(1e-30)).astype(np.float32)
+    sb = _bf16_round(scale)
+    sb = np.where(sb == 0, np.float32(np.finfo(np.float32).tiny), sb).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        quo = _bf16_round((xf / sb).astype(np.float32))
+        u = stochastic_noise_bf16(np.arange(m * k, dtype=np.uint64).reshape(m, k), seed)
+        v = np.floor(_bf16_round((quo + u).astype(np.float32)))
+    # fminf(127, fmaxf(-128, v)): a NaN becomes -128, as in the CUDA kernel
+    q = np.fmin(np.fmax(v, np.float32(-128.0)), np.float32(127.0)).astype(np.int8)
+    return q, scale
 
 
 # ---------------------------------------------------------------------------
@@ -687,7 +734,7 @@ def w4a8_swiglu_mlp(x_bf16, w4, gate_rows_bf16, row_map, residual_bf16, return_i
 
 
 def w4a8_int8_linear_quantized(x_bf16, qdata_i8, s_rel, s_channel, correction_bf16, group_size=128,
-                               convrot_groupsize=256, return_intermediates=False):
+                               convrot_groupsize=256, return_intermediates=False, bias_bf16=None):
     """W4A8 linear with quantized activations (the reference's CUDA route).
 
     backends/cuda/__init__.py:2139-2298 for asymmetric weights: ConvRot-rotate and
@@ -696,12 +743,14 @@ def w4a8_int8_linear_quantized(x_bf16, qdata_i8, s_rel, s_channel, correction_bf
     ``out + bf16(bf16(sum_g xq) * bf16(xs)) @ correction`` (:2294-2297) accumulated
     in fp32 and rounded once. The eager reference (eager/w4a8_int8.py:481-492)
     instead dequantizes the weight to bf16 and runs a bf16 ``F.linear`` on the
-    unquantized input; the two agree within the float tolerance."""
+    unquantized input; the two agree within the float tolerance. A bias joins the
+    dequantized value before the correction (the CUDA route's order: bias in the
+    dequant epilogue, then ``out.addmm_``), rounded to bf16 as the linear's bias is."""
     xr = rotate_activation(x_bf16, convrot_groupsize)
     xq, xs = quantize_int8_rowwise(xr)
     wgrid = decode_int4_grouped_to_int8(qdata_i8, s_rel, group_size)
     acc = int8_matmul_accumulate(xq, wgrid)
-    out = bf16_to_f32(dequant_epilogue(acc, xs, s_channel))
+    out = bf16_to_f32(dequant_epilogue(acc, xs, s_channel, bias_bf16))
     if correction_bf16 is not None:
         m, k = xq.shape
         gs = xq.astype(np.int32).reshape(m, k // group_size, group_size).sum(-1)

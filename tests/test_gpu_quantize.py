@@ -61,3 +61,19 @@ def test_quantize_given_absmax():
 def test_quantize_empty_rows():
     q, s = h3b200.quantize_int8_rowwise(torch.empty(0, 64, dtype=torch.bfloat16, device="cuda"))
     assert q.shape == (0, 64) and s.shape == (0, 1)
+
+
+@pytest.mark.parametrize("m,k,seed", [(300, 3072, 1), (7, 40, 99), (64, 12288, 2 ** 40 + 5), (1, 8, 3)])
+def test_quantize_stochastic_vs_oracle(m, k, seed):
+    gen = torch.Generator().manual_seed(m + k)
+    x = randn_bf16((m, k), gen, std=3.0)
+    x[0, : min(k, 4)] = 0.0
+    if m > 2:
+        x[2] = 0.0                                   # a zero row: scale 1e-30, divisor bf16 tiny
+    q, s = h3b200.quantize_int8_rowwise(x.cuda(), stochastic_rounding=seed)
+    oq, os_ = O.quantize_int8_rowwise_stochastic(t2u(x), seed)
+    np.testing.assert_array_equal(np_(q), oq)
+    np.testing.assert_array_equal(np_(s), os_)
+    q0, _ = h3b200.quantize_int8_rowwise(x.cuda())
+    if m * k > 1000:
+        assert (np_(q) != np_(q0)).mean() > 0.1      # rounding differs from nearest-even

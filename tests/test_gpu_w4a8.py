@@ -84,7 +84,7 @@ def _extreme_rows(k, seed):
     of 2^-84, exact cancellations, zeros; each row's other groups are ordinary."""
     rng = np.random.default_rng(seed)
     rows = O.f32_to_bf16(rng.standard_normal((8, k)).astype(np.float32))
-    b = lambda v: O.f32_to_bf16(np.float32(v))
+    b = lambda v: O.f32_to_bf16(np.array([v], np.float32))[0]
     g = lambda r, i: (r, slice(256 * i, 256 * i + 256))
     rows[g(0, 0)][5] = b(1e30)
     rows[g(0, 0)][9] = b(-1e-30)
@@ -127,6 +127,29 @@ def test_w4a8_linear_vs_reference(golden):
     o = O.w4a8_int8_linear_quantized(g["x"], g["qdata"], g["s_rel"], g["s_channel"], g["correction"], 128, 256)
     rel, mx = rel_l2(t2u(y), o)
     assert rel <= 2e-3
+
+
+@pytest.mark.parametrize("m", [200, 2048])
+def test_w4a8_linear_bias_with_correction(m):
+    """Asymmetric weights with a bias: bf16(bf16(bf16(dequant) + bias) + correction) on the single-CTA
+    (200 rows) and CTA-pair (2,048 rows) GEMMs, against the oracle composition within the float
+    tolerance, and the bias-free result plus bias within one bf16 rounding step."""
+    gen = torch.Generator().manual_seed(51 + m)
+    k, n = 3072, 1024
+    w = randn_bf16((n, k), gen, std=0.02)
+    x = randn_bf16((m, k), gen).cuda()
+    bias = randn_bf16((n,), gen).cuda()
+    q, s_rel, s_ch, corr = h3b200.quantize_w4a8_weight(w.cuda(), 128)
+    y = h3b200.w4a8_int8_linear(x, q, s_rel, s_ch, correction=corr, bias=bias, group_size=128)
+    y0 = h3b200.w4a8_int8_linear(x, q, s_rel, s_ch, correction=corr, group_size=128)
+    assert h3b200.device_status(0) == 0
+    rows = slice(0, 64)
+    o = O.w4a8_int8_linear_quantized(t2u(x[rows]), np_(q), np_(s_rel), np_(s_ch), t2u(corr), 128, 256,
+                                     bias_bf16=t2u(bias))
+    rel, mx = rel_l2(t2u(y[rows]), o)
+    assert rel <= 2e-3 and mx <= 2e-2
+    d = (y.float() - (y0.float() + bias.float())).abs()
+    assert float(d.max()) <= 2e-2 * float(y.float().abs().max())
 
 
 def test_w4a8_int32_accumulators_exact(golden):

@@ -202,6 +202,17 @@ int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ld
   return from_cuda(h3::launch_quantize_rows(x, ldx, m, k, act, nullptr, q, scale, S(stream)), "quantize_int8_rowwise");
 }
 
+int h3b200_quantize_int8_rowwise_stochastic(const void* x, int64_t m, int64_t k, int64_t ldx, int act,
+                                            int64_t seed, int8_t* q, float* scale, h3b200_stream_t stream) {
+  H3_GUARD("quantize_int8_rowwise_stochastic", stream);
+  if (seed <= 0) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_stochastic: seed must be > 0 (got %lld)", (long long)seed);
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_stochastic: unsupported act code %d", act);
+  if (m < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_stochastic: bad shape");
+  if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_stochastic: NULL pointer");
+  if (m > 0x7fffffffll) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_stochastic: m too large");
+  return from_cuda(h3::launch_quantize_rows_stochastic(x, ldx, m, k, act, (uint64_t)seed, q, scale, S(stream)), "quantize_int8_rowwise_stochastic");
+}
+
 int h3b200_quantize_int8_rowwise_absmax(const void* x, const float* absmax, int64_t m, int64_t k, int64_t ldx,
                                         int8_t* q, float* scale, h3b200_stream_t stream) {
   H3_GUARD("quantize_int8_rowwise_absmax", stream);
@@ -637,7 +648,6 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
     return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: K=%lld must be divisible by 16, group_size=%lld, and convrot_groupsize=%lld", (long long)k, (long long)group_size, (long long)convrot_group);
   if (convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: only convrot_groupsize 256 is built");
   if (correction != nullptr && (group_size % 8 || 256 % group_size)) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: asymmetric correction needs group_size dividing 256");
-  if (correction != nullptr && bias != nullptr) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: a bias is built for symmetric weights (no correction) only");
   if (m == 0 || n == 0) return H3B200_OK;
   if (!x || !grid || !s_channel || !out) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear: NULL pointer");
   if (n % 8) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear: needs n %% 8 == 0");

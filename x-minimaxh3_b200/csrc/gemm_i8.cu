@@ -190,6 +190,17 @@ __device__ __forceinline__ void dequant_to_f32(uint32_t (&r)[32], float xs, cons
   }
 }
 
+// The same with the bias of a W4A8 linear: bf16(bf16(acc * (xs * ws)) + bias), as fp32
+// bits (the correction is then added to this value, one rounding at the end).
+__device__ __forceinline__ void dequant_bias_to_f32(uint32_t (&r)[32], float xs, const float* ws_s,
+                                                    const float* bias_s) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float d = __uint_as_float(dequant_bits(r[j], xs, ws_s[j]) << 16);
+    r[j] = (uint32_t)bf16_bits(__fadd_rn(d, bias_s[j])) << 16;
+  }
+}
+
 // Two dequantized values bf16(acc * (xs * ws)) as a packed bf16 pair (f32x2 products,
 // the same roundings as dequant_bits).
 __device__ __forceinline__ uint32_t dequant_pair(uint32_t a0, uint32_t a1, float xs, float w0, float w1) {
@@ -786,7 +797,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const bool cok = col < p.n;
           ws_s[c] = cok ? __ldg(p.w_scale + (p.w_pc ? wrow : 0)) : 0.0f;
           float a = 0.0f;
-          if ((EPI == kEpiBF16 || EPI == kEpiQKV || EPI == kEpiSwiGLU) && p.bias != nullptr && cok)
+          if ((EPI == kEpiBF16 || EPI == kEpiBF16Corr || EPI == kEpiQKV || EPI == kEpiSwiGLU) && p.bias != nullptr &&
+              cok)
             a = __bfloat162float(p.bias[wrow]);
           if (kInBox && cok && (EPI != kEpiGatedResidual || p.row_map == nullptr)) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
@@ -974,7 +986,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t r[32];
             tmem_ld32(taddr + c, r);
             tmem_wait_ld();
-            dequant_to_f32(r, xs, ws_s + c);
+            if (EPI == kEpiBF16Corr && p.bias != nullptr)
+              dequant_bias_to_f32(r, xs, ws_s + c, aux_s + c);
+            else
+              dequant_to_f32(r, xs, ws_s + c);
             tmem_st32(taddr + c, r);
           }
           tmem_wait_st();

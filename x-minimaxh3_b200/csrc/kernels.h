@@ -96,6 +96,11 @@ cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStr
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
                                  int8_t* q, float* scale, cudaStream_t stream);
 
+// Stochastic rounding (seed > 0): the reference CUDA kernel's counter-based noise added
+// to the bf16 quotient, then floor (quantize.cu).
+cudaError_t launch_quantize_rows_stochastic(const void* x, int64_t ldx, int64_t m, int64_t k, int act,
+                                            uint64_t seed, int8_t* q, float* scale, cudaStream_t stream);
+
 // Returns cudaErrorNotSupported when the shape is outside the kernel's contract.
 cudaError_t launch_gemm_i8(const GemmArgs& args, cudaStream_t stream);
 

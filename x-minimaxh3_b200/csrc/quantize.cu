@@ -201,6 +201,47 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_scalar_kernel(const _
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// ---- stochastic rounding ----
+// The reference's CUDA kernel (backends/cuda/ops/int8_linear.cu:78-90 noise, :186-193
+// rounding): element idx = row * k + col of the contiguous [m, k] activation gets the
+// counter-based noise u = bf16(float(pcg_hash(lo32(idx + seed) ^ hi32(idx + seed)) >> 8)
+// * 2^-24) in [0, 1), and q = clamp(floor(bf16(bf16(x / bf16(scale)) + u)), -128, 127).
+// pcg_hash is the PCG-based integer hash of Jarzynski and Olano ("Hash Functions for GPU
+// Rendering", JCGT 2020): one LCG step, a data-dependent xorshift, a multiply and a
+// final xorshift. The row scale is the deterministic quantizer's.
+__device__ __forceinline__ uint32_t pcg_hash32(uint32_t x) {
+  const uint32_t state = x * 747796405u + 2891336453u;
+  const uint32_t word = ((state >> ((state >> 28u) + 4u)) ^ state) * 277803737u;
+  return (word >> 22u) ^ word;
+}
+__device__ __forceinline__ float sr_noise_bf16(uint64_t idx, uint64_t seed) {
+  const uint64_t key = idx + seed;
+  const uint32_t folded = (uint32_t)key ^ (uint32_t)(key >> 32);
+  return bf16_round((float)(pcg_hash32(folded) >> 8) * 0x1.0p-24f);
+}
+
+__global__ void __launch_bounds__(kQThreads) quantize_rows_stochastic_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                             int64_t ldx, int64_t m, int64_t k,
+                                                                             int act, uint64_t seed,
+                                                                             int8_t* __restrict__ q,
+                                                                             float* __restrict__ scale) {
+  __shared__ float red[kQThreads / 32];
+  const int64_t row = blockIdx.x;
+  if (row >= m) return;
+  const __nv_bfloat16* xr = x + row * ldx;
+  float amax = 0.0f;
+  for (int64_t i = threadIdx.x; i < k; i += kQThreads) amax = fmaxf(amax, fabsf(act_value(xr, k, i, act)));
+  const float s = row_scale(block_max(amax, red));
+  const float sb = quant_divisor(s);
+  for (int64_t i = threadIdx.x; i < k; i += kQThreads) {
+    const float t = bf16_round(__fdiv_rn(act_value(xr, k, i, act), sb));
+    float v = floorf(bf16_round(__fadd_rn(t, sr_noise_bf16((uint64_t)(row * k + i), seed))));
+    v = fminf(fmaxf(v, -128.0f), 127.0f);
+    q[row * k + i] = (int8_t)(int)v;
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
 template <bool GIVEN>
 cudaError_t launch_warp(int vpl, const __nv_bfloat16* x, int64_t ldx, int64_t m, int64_t k, int act, const float* am,
                         int8_t* q, float* s, cudaStream_t st) {
@@ -374,6 +415,18 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t 
   }
   quantize_rows_scalar_kernel<<<dim3((unsigned)m), dim3(kQThreads), 0, stream>>>(xb, ldx, m, k, act, absmax_in, q,
                                                                                   scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows_stochastic(const void* x, int64_t ldx, int64_t m, int64_t k, int act,
+                                            uint64_t seed, int8_t* q, float* scale, cudaStream_t stream) {
+  if (m == 0) return cudaSuccess;
+  {
+    const cudaError_t e = ensure_act_table(act, stream);
+    if (e != cudaSuccess) return e;
+  }
+  quantize_rows_stochastic_kernel<<<dim3((unsigned)m), dim3(kQThreads), 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, m, k, act, seed, q, scale);
   return cudaGetLastError();
 }
 

@@ -125,9 +125,9 @@ def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int | None = 0, 
 
     Replaces ``comfy_kitchen.quantize_int8_rowwise`` (__init__.py:702-709;
     eager eager/quantization.py:857-875; CUDA backends/cuda/ops/int8_linear.cu:157-200).
-    Stochastic rounding is not built (the DiT path never uses it)."""
-    if stochastic_rounding:
-        raise NotImplementedError("stochastic rounding is not built in h3b200")
+    ``stochastic_rounding`` > 0 is the seed of stochastic rounding: the reference CUDA
+    kernel's counter-based noise is added to the bf16 quotient, which is then floored
+    (``h3b200_quantize_int8_rowwise_stochastic``); <= 0 or None rounds to nearest even."""
     _need_cuda(x)
     if x.dtype != torch.bfloat16:
         raise ValueError(f"quantize_int8_rowwise expects bf16, got {x.dtype}")
@@ -136,8 +136,12 @@ def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int | None = 0, 
     m = x2.shape[0]
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
-    _lib.call("h3b200_quantize_int8_rowwise", x2.data_ptr(), m, k, ldx, input_act_code(input_act), q.data_ptr(),
-              s.data_ptr(), _stream(x))
+    if stochastic_rounding is not None and stochastic_rounding > 0:
+        _lib.call("h3b200_quantize_int8_rowwise_stochastic", x2.data_ptr(), m, k, ldx, input_act_code(input_act),
+                  int(stochastic_rounding), q.data_ptr(), s.data_ptr(), _stream(x))
+    else:
+        _lib.call("h3b200_quantize_int8_rowwise", x2.data_ptr(), m, k, ldx, input_act_code(input_act), q.data_ptr(),
+                  s.data_ptr(), _stream(x))
     return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
 
 
@@ -1033,8 +1037,8 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
                      input_act=None) -> torch.Tensor:
     """W4A8 linear (``comfy_kitchen`` w4a8_int8_linear, tensor/w4a8_int8.py:89-115; CUDA
     backends/cuda/__init__.py:2139-2298): ConvRot-quantize x, INT8 GEMM against
-    the decoded int8 grid, dequant by ``s_channel``, then the asymmetric group
-    correction (``correction`` given) or the bias (symmetric weights: the call is
+    the decoded int8 grid, dequant by ``s_channel`` (+ bias, rounded to bf16), then the
+    asymmetric group correction (``correction`` given; for symmetric weights the call is
     ``int8_linear(x, grid, s_channel, bias, convrot=True)``, eager/w4a8_int8.py:494-508).
     ``s_rel`` fp32 or float8_e4m3fn; ``codebook`` the 16 levels of the H3 release format.
 
@@ -1052,8 +1056,6 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     groups = k // group_size
     corr = None
     if correction is not None:
-        if bias is not None:
-            raise NotImplementedError("h3b200 builds a bias for symmetric W4A8 weights (no correction) only")
         if tuple(correction.shape) != (groups, n):
             raise ValueError(f"correction must have shape {(groups, n)}, got {tuple(correction.shape)}")
         corr = correction.to(torch.bfloat16).contiguous()
