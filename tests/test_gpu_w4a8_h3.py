@@ -123,8 +123,10 @@ def test_w4a8_linear_release_format_vs_reference(golden):
     ref = O.w4a8_symmetric_linear(fx["x_a"], fx["q_a"], fx["s_rel_a"], fx["s_ch_a"], fx["codebook_a"], fx["b_a"])
     rel, mx = rel_l2(t2u(y), ref)
     assert rel <= 1e-2 and mx <= 2e-2
-    with pytest.raises(NotImplementedError):
-        h3b200.w4a8_int8_linear(x, q, s_rel, s_ch, cb, torch.zeros(32, 384, dtype=torch.bfloat16, device="cuda"), b)
+    # a bias with an (all-zero) asymmetric correction: the correction adds exactly 0 to the
+    # bf16 dequant + bias value, so the result is the symmetric one bit for bit
+    yc = h3b200.w4a8_int8_linear(x, q, s_rel, s_ch, cb, torch.zeros(32, 384, dtype=torch.bfloat16, device="cuda"), b)
+    np.testing.assert_array_equal(t2u(yc), t2u(y))
 
 
 def _w4(fx):

@@ -74,30 +74,6 @@ struct Words8 {
   uint32_t w[8];
 };
 
-// 8 bf16 (one 16-byte vector) -> 8 int8: bf16(x * r) rounded to an integer (nearest
-// even) and saturated to [-128, 127] by one conversion each -- the reference's
-// clamp(rne(bf16(x / bf16(scale))), -128, 127) with r = rcp_rn(bf16(scale))
-// (quant_math.cuh explains why the product rounds like the division).
-__device__ __forceinline__ int rni_sat_s8(uint32_t f32bits) {
-  int r;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(__uint_as_float(f32bits)));
-  return r;
-}
-__device__ __forceinline__ uint2 quant_vec8_sat(const uint32_t (&w)[4], float r) {
-  const uint64_t r2 = f2_dup(r);
-  int q[8];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    uint32_t t0, t1;
-    f2_bits(f2_mul(bf16x2_to_f2(w[e]), r2), t0, t1);
-    const uint32_t b = bf16x2_from_bits(t0, t1);
-    q[2 * e] = rni_sat_s8(b << 16);
-    q[2 * e + 1] = rni_sat_s8(b & 0xFFFF0000u);
-  }
-  const uint32_t lo = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
-  const uint32_t hi = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
-  return make_uint2(lo, hi);
-}
 // running max of |bf16| over a bf16x2 pair (the sign of the result is not used)
 __device__ __forceinline__ uint32_t bf16x2_absmax(uint32_t acc, uint32_t w) {
   uint32_t r;
@@ -343,8 +319,8 @@ __global__ void __maxnreg__(128)
       const bool ok = g < ng;
       const uint32_t w0[4] = {park[i][0], park[i][1], park[i][2], park[i][3]};
       const uint32_t w1[4] = {park[i][4], park[i][5], park[i][6], park[i][7]};
-      const uint2 q0 = quant_vec8_sat(w0, rcp);
-      const uint2 q1 = quant_vec8_sat(w1, rcp);
+      const uint2 q0 = quant_vec8(make_uint4(w0[0], w0[1], w0[2], w0[3]), rcp);
+      const uint2 q1 = quant_vec8(make_uint4(w1[0], w1[1], w1[2], w1[3]), rcp);
       if (ok) stg_v4(q + row * K + g * 256 + 16 * li, make_uint4(q0.x, q0.y, q1.x, q1.y));
       if (sx != nullptr) {  // all lanes shuffle; partners stay inside the half-warp (offsets < 16)
         int isum = __dp4a((int)q0.x, 0x01010101, __dp4a((int)q0.y, 0x01010101,
