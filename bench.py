@@ -658,6 +658,49 @@ def run_ours(args, rank, world, local_rank):
     w4_ms = timed(k_w4a8, 10, stream)
     del work4, x3
 
+    # ---- small-M W4A8 linear (fc1's weight, 3,072 -> 12,288, same format): the packed int4 weight
+    #      unpacked in shared memory inside the GEMM (split-K) against decode-per-call + INT8 GEMM;
+    #      CUDA graphs of 10 calls so that host overhead is not timed ----
+    def graph_ms(fn, calls=10, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            for _ in range(calls):
+                fn()
+        gph.replay()
+        torch.cuda.synchronize()
+        ms = timed(gph.replay, reps, stream) / calls
+        del gph
+        return ms
+
+    small_m = {}
+    grid1 = torch.empty(D_FFN, D_MODEL, dtype=torch.int8, device=dev)
+    for mm in (1, 8, 16):
+        xs_ = torch.randn(mm, D_MODEL, generator=g3, device=dev).to(torch.bfloat16)
+        ys_ = torch.empty(mm, D_FFN, dtype=torch.bfloat16, device=dev)
+        wpk = torch.empty(int(lib.h3b200_w4a8_linear_packed_workspace_bytes(mm, D_FFN, D_MODEL, 128)),
+                          dtype=torch.uint8, device=dev)
+        wgd = torch.empty(int(lib.h3b200_w4a8_linear_workspace_bytes(mm, D_FFN, D_MODEL, 128)), dtype=torch.uint8,
+                          device=dev)
+
+        def k_packed():
+            lib.h3b200_w4a8_int8_linear_packed(xs_.data_ptr(), D_MODEL, w4.q1.data_ptr(), w4.s_rel1.data_ptr(), 0,
+                                               None, w4.s_ch1.data_ptr(), w4.corr1.data_ptr(), None, 128, 256, 0,
+                                               ys_.data_ptr(), mm, D_FFN, D_MODEL, wpk.data_ptr(), wpk.numel(),
+                                               torch.cuda.current_stream().cuda_stream)
+
+        def k_decoded():
+            lib.h3b200_dequant_int4_grouped_to_int8_ex(w4.q1.data_ptr(), w4.s_rel1.data_ptr(), 0, None, D_FFN, D_MODEL,
+                                                       128, grid1.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            lib.h3b200_w4a8_int8_linear(xs_.data_ptr(), D_MODEL, grid1.data_ptr(), w4.s_ch1.data_ptr(),
+                                        w4.corr1.data_ptr(), None, 128, 256, 0, ys_.data_ptr(), mm, D_FFN, D_MODEL,
+                                        wgd.data_ptr(), wgd.numel(), torch.cuda.current_stream().cuda_stream)
+
+        small_m[str(mm)] = {"packed_in_smem_us": 1e3 * graph_ms(k_packed), "decode_then_gemm_us": 1e3 * graph_ms(k_decoded)}
+        del xs_, ys_, wpk, wgd
+    del grid1
+
     # ---- H3 SwiGLU MLP at the H3 dims (d 5,376, fc1 out 28,672, ffn 14,336): ConvRot fc1 + bias,
     #      SwiGLU+ConvRot fc2 + bias, gated residual; 8,192-token chunks as in the reference ----
     H3_D, H3_FFN = 5376, 14336
@@ -913,6 +956,10 @@ def run_ours(args, rank, world, local_rank):
                                               "achieved": qk1_bytes / (qk1_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
                                               "unit": "GB/s", "frac": qk1_bytes / (qk1_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
                                               "bytes_per_token": H3_HEADS * 128 * 2 * 2},
+                "w4a8_linear_small_m": {"shape": "x [m, 3072] . W4 [12288, 3072]^T, asymmetric int4 group 128 + "
+                                                 "correction, ConvRot-256; microseconds per call (CUDA graphs)",
+                                        "by_m": small_m,
+                                        "weight_bytes_int4": D_FFN * D_MODEL // 2},
                 "w4a8_mlp_cfg2": {"ms": w4_ms, "tokens_per_s": M_TOKENS / (w4_ms * 1e-3),
                                   "int8_tops": M_TOKENS * OPS_PER_TOKEN / (w4_ms * 1e-3) / 1e12,
                                   "weights": "asymmetric int4, group 128, ConvRot-256, decoded per call"},

@@ -452,6 +452,28 @@ H3B200_API int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t*
                             h3b200_stream_t stream);
 
 /*
+ * The same linear from the packed int4 weight itself (qdata [n, k/2], even column in the
+ * low nibble; s_rel fp32 or fp8-e4m3 [n, k/group] per s_rel_dtype; codebook 16 fp32
+ * levels or NULL for u - 8), the reference's w4a8_int8_linear(x, qdata, s_rel, s_channel,
+ * codebook, correction, bias, group_size, convrot_groupsize) (tensor/w4a8_int8.py:89-115;
+ * CUDA backends/cuda/__init__.py:2139-2298 decodes into an int8 workspace first).
+ * For m <= 32, or m <= 16 with a correction (and k % 128 == 0, group a
+ * multiple of 16 dividing 128 or a multiple of 128, at most 128 correction groups), the
+ * GEMM reads the packed weight through TMA and unpacks it to int8 in shared memory, tile by
+ * tile, so the weight crosses HBM at 4 bits per element; K is split over CTAs so that few
+ * rows still fill the GPU, and the correction is summed on CUDA cores from a shared-memory
+ * copy (fp32, one rounding). Otherwise the grid is decoded once into the workspace and the
+ * call takes h3b200_w4a8_int8_linear. workspace: h3b200_w4a8_linear_packed_workspace_bytes(m, n, k, group).
+ */
+H3B200_API int64_t h3b200_w4a8_linear_packed_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group_size);
+H3B200_API int h3b200_w4a8_int8_linear_packed(const void* x, int64_t ldx, const uint8_t* qdata, const void* s_rel,
+                                              int s_rel_dtype, const float* codebook, const float* s_channel,
+                                              const void* correction, const void* bias, int64_t group_size,
+                                              int64_t convrot_group, int act, void* out, int64_t m, int64_t n,
+                                              int64_t k, void* workspace, int64_t workspace_bytes,
+                                              h3b200_stream_t stream);
+
+/*
  * Fused gated W4A8 MLP on a token chunk (config 2):
  *   h = w4a8_linear(x, W1); a = gelu_tanh(h); y = w4a8_linear(a, W2);
  *   out = residual + y * gate   (bf16 addcmul)

@@ -679,6 +679,80 @@ int h3b200_w4a8_int8_linear(const void* x, int64_t ldx, const int8_t* grid, cons
 }
 
 
+int64_t h3b200_w4a8_linear_packed_workspace_bytes(int64_t m, int64_t n, int64_t k, int64_t group_size) {
+  // large m: the decoded int8 grid in front of the grid path's own workspace; small m: the
+  // split-K int32 sums [m, n] and one counter per output tile after the quantized activation
+  if (!h3::gemm_w4_smallm_supported(m, n, k, group_size, 0))
+    return round_up(n * k, 256) + h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size);
+  const int64_t tiles = ((n + 255) / 256) * ((m + 127) / 128);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t splits = h3::gemm_w4_smallm_splits(m, n, k, h3::num_sms(dev));
+  (void)splits;
+  return h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size) + round_up(m * n * 4, 256) + round_up(tiles * 4, 256);
+}
+
+int h3b200_w4a8_int8_linear_packed(const void* x, int64_t ldx, const uint8_t* qdata, const void* s_rel,
+                                   int s_rel_dtype, const float* codebook, const float* s_channel,
+                                   const void* correction, const void* bias, int64_t group_size,
+                                   int64_t convrot_group, int act, void* out, int64_t m, int64_t n, int64_t k,
+                                   void* workspace, int64_t workspace_bytes, h3b200_stream_t stream) {
+  H3_GUARD("w4a8_int8_linear_packed", stream);
+  if (s_rel_dtype != H3B200_DTYPE_F32 && s_rel_dtype != H3B200_DTYPE_E4M3) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: s_rel dtype code must be 0 (float32) or 5 (float8_e4m3fn), got %d", s_rel_dtype);
+  if (act != H3B200_ACT_NONE && act != H3B200_ACT_GELU_TANH && act != H3B200_ACT_SWIGLU) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: unsupported act code %d", act);
+  if (m < 0 || n < 0 || k < 0 || ldx < k * act_width(act)) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: bad shape");
+  if (group_size < 4 || k % 16 || k % group_size || k % convrot_group || (16 % group_size && group_size % 16))
+    return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: K=%lld must be divisible by 16, group_size=%lld, and convrot_groupsize=%lld", (long long)k, (long long)group_size, (long long)convrot_group);
+  if (convrot_group != 256) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear_packed: only convrot_groupsize 256 is built");
+  if (m == 0 || n == 0) return H3B200_OK;
+  if (!x || !qdata || !s_rel || !s_channel || !out) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: NULL pointer");
+  if (n % 8) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear_packed: needs n %% 8 == 0");
+  const int64_t need = h3b200_w4a8_linear_packed_workspace_bytes(m, n, k, group_size);
+  if (workspace == nullptr || workspace_bytes < need) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: workspace too small (need %lld bytes)", (long long)need);
+  const int64_t groups = k / group_size;
+  if (h3::gemm_w4_smallm_supported(m, n, k, group_size, correction ? groups : 0) &&
+      !(reinterpret_cast<uintptr_t>(qdata) & 15)) {
+    // few rows: the GEMM unpacks the int4 weight in shared memory
+    if (correction != nullptr && (group_size % 8 || 256 % group_size)) return fail(H3B200_ERR_UNSUPPORTED, "w4a8_int8_linear_packed: asymmetric correction needs group_size dividing 256");
+    const int64_t kp = h3::correction_kpad(groups);
+    Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+    int8_t* xq = static_cast<int8_t*>(c.take(m * k));
+    float* xs = static_cast<float*>(c.take(m * 4));
+    void* sx = c.take(m * kp * 2);
+    const int64_t tiles = ((n + 255) / 256) * ((m + 127) / 128);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int splits = h3::gemm_w4_smallm_splits(m, n, k, h3::num_sms(dev));
+    int32_t* acc_ws = static_cast<int32_t*>(c.take(m * n * 4));  // the splits' int32 sums
+    unsigned int* tile_cnt = static_cast<unsigned int*>(c.take(tiles * 4));
+    if (!c.ok) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: workspace too small");
+    cudaStream_t st = S(stream);
+    // the sums and the tile counters start at zero (contiguous in the workspace)
+    cudaError_t e = cudaMemsetAsync(acc_ws, 0, (size_t)(reinterpret_cast<uint8_t*>(tile_cnt + tiles) -
+                                                        reinterpret_cast<uint8_t*>(acc_ws)), st);
+    if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear_packed: memset");
+    e = h3::launch_quantize_convrot(x, ldx, m, k, act, xq, xs, correction ? sx : nullptr, group_size, kp, st);
+    if (e != cudaSuccess) return from_cuda(e, "w4a8_int8_linear_packed: convrot quantize");
+    h3::W4SmallMArgs a;
+    a.xq = xq; a.xs = xs; a.qdata = qdata; a.s_rel = s_rel; a.s_rel_e4m3 = s_rel_dtype == H3B200_DTYPE_E4M3;
+    a.codebook = codebook; a.s_channel = s_channel; a.bias = bias;
+    a.sx = correction ? sx : nullptr; a.kp = kp; a.corr = correction;
+    a.out = out; a.ldo = n; a.m = m; a.n = n; a.k = k; a.group = group_size;
+    a.splits = splits; a.acc_ws = acc_ws; a.tile_cnt = tile_cnt;
+    return from_cuda(h3::launch_gemm_w4_smallm(a, st), "w4a8_int8_linear_packed: small-M W4 GEMM");
+  }
+  // many rows: decode the grid once into the workspace, then the INT8 GEMM path
+  Carver c{static_cast<uint8_t*>(workspace), workspace_bytes};
+  int8_t* grid = static_cast<int8_t*>(c.take(n * k));
+  if (!c.ok) return fail(H3B200_ERR_INVALID, "w4a8_int8_linear_packed: workspace too small");
+  uint8_t* rest = static_cast<uint8_t*>(workspace) + round_up(n * k, 256);
+  int stc = h3b200_dequant_int4_grouped_to_int8_ex(reinterpret_cast<const int8_t*>(qdata), s_rel, s_rel_dtype, codebook,
+                                                   n, k, group_size, grid, stream);
+  if (stc != H3B200_OK) return stc;
+  return h3b200_w4a8_int8_linear(x, ldx, grid, s_channel, correction, bias, group_size, convrot_group, act, out, m, n,
+                                 k, rest, workspace_bytes - round_up(n * k, 256), stream);
+}
+
 int64_t h3b200_fused_gated_mlp_swiglu_workspace_bytes(int64_t chunk_tokens, int64_t d, int64_t ffn) {
   if (chunk_tokens <= 0 || d <= 0 || ffn <= 0) return 0;
   const int64_t c = chunk_tokens;

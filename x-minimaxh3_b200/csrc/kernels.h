@@ -104,6 +104,36 @@ cudaError_t launch_quantize_rows_stochastic(const void* x, int64_t ldx, int64_t 
 // Returns cudaErrorNotSupported when the shape is outside the kernel's contract.
 cudaError_t launch_gemm_i8(const GemmArgs& args, cudaStream_t stream);
 
+// Small-M W4A8 linear with the int4 weight unpacked in shared memory (gemm_w4.cu):
+// xq int8 [m, k] (contiguous), xs fp32 [m]; qdata packed [n, k / 2]; s_rel fp32 or
+// fp8-e4m3 [n, k / group]; codebook 16 fp32 levels or null; s_channel fp32 [n];
+// bias bf16 [n] or null; sx bf16 [m, kp] and corr bf16 [k / group, n] (both or neither);
+// out bf16 [m, ldo].
+struct W4SmallMArgs {
+  const int8_t* xq = nullptr;
+  const float* xs = nullptr;
+  const uint8_t* qdata = nullptr;
+  const void* s_rel = nullptr;
+  bool s_rel_e4m3 = false;
+  const float* codebook = nullptr;
+  const float* s_channel = nullptr;
+  const void* bias = nullptr;
+  const void* sx = nullptr;
+  int64_t kp = 0;
+  const void* corr = nullptr;
+  void* out = nullptr;
+  int64_t ldo = 0;
+  int64_t m = 0, n = 0, k = 0, group = 0;
+  // split-K over `splits` CTAs per tile (gemm_w4_smallm_splits): acc_ws int32 [m, n] and
+  // tile_cnt [tiles] must be zero at launch
+  int64_t splits = 1;
+  int32_t* acc_ws = nullptr;
+  unsigned int* tile_cnt = nullptr;
+};
+bool gemm_w4_smallm_supported(int64_t m, int64_t n, int64_t k, int64_t group, int64_t groups_corr);
+int gemm_w4_smallm_splits(int64_t m, int64_t n, int64_t k, int sms);
+cudaError_t launch_gemm_w4_smallm(const W4SmallMArgs& args, cudaStream_t stream);
+
 struct NormRopeArgs {
   const void* q = nullptr;
   const void* k = nullptr;

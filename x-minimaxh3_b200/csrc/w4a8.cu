@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "quant_math.cuh"
+#include "w4_math.cuh"
 
 namespace h3 {
 namespace {
@@ -26,26 +27,12 @@ namespace {
 // rounding is cvt.rni (NaN -> 0), then an integer clamp.
 // ---------------------------------------------------------------------------
 
-// OCP FP8 E4M3 (float8_e4m3fn) -> fp32, exact: exponent bias 7 -> 127 is a
-// shift of the 7 magnitude bits by 20 plus 120 << 23; exponent 0 is m * 2^-9;
-// S.1111.111 is NaN.
-__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
-  const uint32_t mag = b & 0x7Fu;
-  float v = mag >= 8u ? __uint_as_float((mag << 20) + (120u << 23)) : (float)mag * 0.001953125f;
-  if (mag == 0x7Fu) v = __uint_as_float(0x7FC00000u);
-  return (b & 0x80u) ? -v : v;
-}
-
 template <bool E4M3>
 __device__ __forceinline__ float group_scale(const void* s_rel, int64_t i) {
   if constexpr (E4M3) return e4m3_to_f32(static_cast<const uint8_t*>(s_rel)[i]);
   else return static_cast<const float*>(s_rel)[i];
 }
 
-__device__ __forceinline__ uint32_t decode_one(float level, float s) {
-  const int v = __float2int_rn(__fmul_rn(level, s));
-  return (uint32_t)(uint8_t)(int8_t)max(-127, min(127, v));
-}
 
 
 // Unsigned 32-bit division by a launch constant d >= 1 (round-up method of

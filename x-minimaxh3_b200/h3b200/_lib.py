@@ -70,6 +70,9 @@ SIGNATURES = {
     "h3b200_dequant_int4_grouped_to_int8_ex": (_i32, [_p, _p, _i32, _p, _i64, _i64, _i64, _p, _p]),
     "h3b200_w4a8_int8_linear": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i32, _p, _i64, _i64, _i64, _p, _i64,
                                        _p]),
+    "h3b200_w4a8_linear_packed_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
+    "h3b200_w4a8_int8_linear_packed": (_i32, [_p, _i64, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i32, _p, _i64,
+                                              _i64, _i64, _p, _i64, _p]),
     "h3b200_fused_gated_mlp_w4a8_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "h3b200_fused_gated_mlp_swiglu_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "h3b200_fused_gated_mlp_swiglu": (_i32, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _p, _p, _i64, _p, _p, _i64, _p,

@@ -1043,7 +1043,10 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     ``s_rel`` fp32 or float8_e4m3fn; ``codebook`` the 16 levels of the H3 release format.
 
     ``grid`` is the decoded weight from :func:`dequant_int4_grouped_to_int8`;
-    pass it to keep the decode out of the per-call path (weights are static)."""
+    pass it to keep the decode out of the per-call path (weights are static). Without it
+    the packed weight goes to ``h3b200_w4a8_int8_linear_packed``: for up to 256 rows the
+    GEMM unpacks the int4 weight to int8 in shared memory tile by tile (the weight crosses
+    HBM at 4 bits), for more rows it is decoded once into a workspace grid."""
     _need_cuda(x, qdata, s_rel, s_channel)
     if out_dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
         raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
@@ -1051,8 +1054,6 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     k = kh * 2
     if _act_k(x, input_act) != k:
         raise ValueError(f"Input K={_act_k(x, input_act)} (after input_act) does not match qdata K={k}")
-    if grid is None:
-        grid = dequant_int4_grouped_to_int8(qdata, s_rel, group_size, codebook)
     groups = k // group_size
     corr = None
     if correction is not None:
@@ -1070,6 +1071,19 @@ def w4a8_int8_linear(x: torch.Tensor, qdata: torch.Tensor, s_rel: torch.Tensor, 
     x2, ldx = _rows(x)
     m = x2.shape[0]
     out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    if grid is None:
+        code = _s_rel_code(s_rel)
+        sr = s_rel.contiguous()
+        if tuple(sr.shape) != (n, groups):
+            raise ValueError(f"s_rel must have shape {(n, groups)}, got {tuple(sr.shape)}")
+        cb = _codebook(codebook, x.device)
+        qd = qdata.contiguous()
+        nbytes = int(_lib.load().h3b200_w4a8_linear_packed_workspace_bytes(m, n, k, group_size))
+        work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        _lib.call("h3b200_w4a8_int8_linear_packed", x2.data_ptr(), ldx, qd.data_ptr(), sr.data_ptr(), code, _ptr(cb),
+                  sch.data_ptr(), _ptr(corr), _ptr(b), group_size, convrot_groupsize, input_act_code(input_act),
+                  out.data_ptr(), m, n, k, work.data_ptr(), nbytes, _stream(x))
+        return out.reshape(*x.shape[:-1], n)
     nbytes = int(_lib.load().h3b200_w4a8_linear_workspace_bytes(m, n, k, group_size))
     work = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
     _lib.call("h3b200_w4a8_int8_linear", x2.data_ptr(), ldx, grid.contiguous().data_ptr(), sch.data_ptr(), _ptr(corr),
