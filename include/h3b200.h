@@ -556,6 +556,55 @@ H3B200_API int h3b200_fused_gated_mlp_swiglu_w4a8(const void* x, int64_t ldx, co
                                                   int64_t chunk_tokens, void* workspace, int64_t workspace_bytes,
                                                   h3b200_stream_t stream);
 
+/*
+ * Tensor-parallel gated W8A8 MLP over NVLink peer memory (one process per GPU).
+ * The reference runs the MLP on one GPU (try_fused_gated_mlp,
+ * h3serve/native_engine/model/fused_mlp.py:269-426); this splits it over a group
+ * of `world` GPUs: rank r owns fc1 rows [r ffn/world, (r+1) ffn/world) of W1 and the
+ * same columns of W2 (w1q int8 [ffn_shard, d], s1 fp32 [ffn_shard], w2q int8
+ * [d, ffn_shard] contiguous, s2 fp32 [d]); x, residual and gate are replicated.
+ * Per token chunk of c rows: quantize x, fc1 + GELU + row absmax on the own columns,
+ * the row absmax max-reduced over the ranks (pushed into every rank's slot, barrier,
+ * max), fc2 quantizing its own input with that global absmax and storing each int32
+ * partial row straight into the receive slot of the rank that owns the row (rows
+ * [q ceil(c/world), (q+1) ceil(c/world)) belong to rank q), barrier, then each owner
+ * sums the ranks' partials, applies dequant + gated residual and writes its rows to
+ * its own out and to every rank's gather buffer (copied into out after the next
+ * barrier). No NCCL call on the data path. out is bit-identical to
+ * h3b200_fused_gated_mlp on one GPU (int32 sums are exact; the requant uses the
+ * global absmax).
+ *
+ * Set-up: every rank calls h3b200_tp_comm_create with identical max_rows / d /
+ * ffn_shard and its rank, exchanges the H3B200_TP_HANDLE_BYTES handle bytes with the
+ * others (any host transport), and calls h3b200_tp_comm_open with all handles in rank
+ * order (CUDA IPC mappings; world == 1 needs no open). Then h3b200_tp_gated_mlp on
+ * every rank, with the same m and chunk_rows, in the same order. The cross-GPU
+ * barrier waits at most barrier_timeout_ns (0: 5 s) and records device status 0x201
+ * on expiry. h3b200_tp_comm_destroy after the last call has completed on every rank.
+ *
+ * h3b200_tp_stage / h3b200_tp_barrier expose the pipeline's steps (stage 1: quantize,
+ * fc1, absmax push; 2: absmax max, fc2 with routed rows; 3: owner rows; 4: copy the
+ * other owners' rows of chunk `chunk` into out). h3b200_tp_comm_link_local makes
+ * `world` communicators created in ONE process on ONE device each other's peers
+ * (no IPC; barriers become no-ops), so a test can run every rank's stages in
+ * order on one GPU.
+ */
+#define H3B200_TP_HANDLE_BYTES 192
+H3B200_API int h3b200_tp_comm_create(int rank, int world, int64_t max_rows, int64_t d, int64_t ffn_shard,
+                                     int64_t barrier_timeout_ns, void** comm, uint8_t* handle);
+H3B200_API int h3b200_tp_comm_open(void* comm, const uint8_t* handles);
+H3B200_API int h3b200_tp_comm_link_local(void* const* comms, int world);
+H3B200_API int h3b200_tp_comm_destroy(void* comm);
+H3B200_API int h3b200_tp_barrier(void* comm, h3b200_stream_t stream);
+H3B200_API int h3b200_tp_stage(void* comm, int stage, int64_t chunk, const void* x, int64_t ldx,
+                               const void* residual, int64_t ldr, const void* gate, const int8_t* w1q,
+                               const float* s1, const int8_t* w2q, const float* s2, void* out, int64_t ldo,
+                               int64_t lo, int64_t hi, h3b200_stream_t stream);
+H3B200_API int h3b200_tp_gated_mlp(void* comm, const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                                   const void* gate, const int8_t* w1q, const float* s1, const int8_t* w2q,
+                                   const float* s2, void* out, int64_t ldo, int64_t m, int64_t chunk_rows,
+                                   h3b200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,9 +1,13 @@
-"""GPU parity on 2 or 4 GPUs (NCCL): tensor-parallel MLP and token sharding vs one GPU.
+"""GPU parity on 2 or 4 GPUs: tensor-parallel MLP and token sharding vs one GPU.
 
 Each rank runs in its own spawned process with one GPU. The tensor-parallel MLP
-(fc1 column-split, all-reduce(MAX) of the row absmax, fc2 row-split, int32
-reduce-scatter + bf16 all-gather, or int32 all-reduce) and the token-sharded MLP must both reproduce the single-GPU
-fused MLP bit for bit. Skipped when fewer than 2 GPUs are visible.
+(fc1 column-split, the row absmax max-reduced over the ranks, fc2 row-split with its
+int32 partial sums reduced exactly) in all three exchange forms -- inside the kernels
+over NVLink peer memory ("p2p": IPC-mapped regions, flag barriers), NCCL int32
+reduce-scatter + bf16 all-gather, NCCL int32 all-reduce -- and the token-sharded MLP
+must all reproduce the single-GPU fused MLP bit for bit. A cross-GPU barrier that the
+other ranks never enter must expire on rank 0 with status 0x201 (bounded wait, no
+fault). Skipped when fewer than 2 GPUs are visible.
 """
 
 import datetime
@@ -62,6 +66,17 @@ def _worker(rank, world, port, outdir):
             "token_shard": bool(torch.equal(ts, ref)),
             "status": h3b200.device_status(rank),
         }
+        P.close_tp_comms()
+        # a barrier that only rank 0 enters: its 20 ms bounded wait expires, the kernel
+        # records 0x201 and returns; the other ranks never launch anything on it
+        comm = P.TPComm(64, d, ffn // world, barrier_timeout_s=0.02)
+        expired = 0x201
+        if rank == 0:
+            comm.barrier()
+            torch.cuda.synchronize()
+            expired = h3b200.device_status(rank, clear=True)
+        comm.close()
+        ok["barrier_expiry"] = expired == 0x201
         with open(os.path.join(outdir, f"rank{rank}.txt"), "w") as f:
             f.write(repr(ok))
     finally:
@@ -87,4 +102,4 @@ def test_tp_mlp_and_token_sharding_multi_gpu(tmp_path):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(world):
         res = eval((tmp_path / f"rank{r}.txt").read_text())
-        assert res == {"tp": True, "token_shard": True, "status": 0}, (r, res)
+        assert res == {"tp": True, "token_shard": True, "status": 0, "barrier_expiry": True}, (r, res)

@@ -114,7 +114,7 @@ def _worker(rank, world, port, mode, q):
             shard = P.TPShard.from_full(w1q, s1, w2q, s2, world, rank)
             full = ops.fused_mlp(res, x, w1q, s1, w2q, s2, gate, torch.empty_like(res))
             ok = True
-            for coll in P.COLLECTIVES:
+            for coll in P.PG_COLLECTIVES:
                 out = P.tp_gated_mlp(x, res, gate, shard, chunk_tokens=37, ops=ops, collective=coll)
                 ok = ok and bool(torch.equal(out.view(torch.int16), full.view(torch.int16)))
             q.put((rank, ok))

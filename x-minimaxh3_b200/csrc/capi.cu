@@ -1068,3 +1068,347 @@ int h3b200_int8_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, cons
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel MLP communicator. Each rank owns one cudaMalloc'd region, exported
+// through CUDA IPC and mapped by every other rank, laid out identically on all ranks:
+//   flags   u32 [kTpMaxWorld]                      flag q: last barrier epoch from rank q
+//   amax    u32 [2][world][max_rows]               slot q: rank q's fc1 row absmax (chunk parity)
+//   recv    i32 [2][world][per_max][d]             slot q: rank q's fc2 partial rows owned here
+//   gather  bf16 [2][max_rows][d]                  finished rows of the other owners
+// Chunk parity double-buffers every slot; the two barriers per chunk order each
+// reuse after the last read of the same parity (see h3b200_tp_gated_mlp).
+// ---------------------------------------------------------------------------
+namespace {
+
+struct TpHandle {
+  char magic[8];
+  int32_t rank, world;
+  int64_t max_rows, d, ffn;
+  uint64_t shared_bytes;
+  cudaIpcMemHandle_t ipc;
+};
+static_assert(sizeof(TpHandle) <= H3B200_TP_HANDLE_BYTES, "TP handle does not fit H3B200_TP_HANDLE_BYTES");
+constexpr char kTpMagic[8] = {'h', '3', 'b', '2', 'T', 'P', 'v', '1'};
+constexpr unsigned long long kTpDefaultTimeoutNs = 5000000000ull;
+
+struct TpComm {
+  int rank = 0, world = 1, device = 0;
+  bool linked_local = false;
+  int64_t max_rows = 0, d = 0, ffn = 0, per_max = 0;
+  unsigned long long timeout_ns = kTpDefaultTimeoutNs;
+  uint8_t* shared = nullptr;
+  size_t shared_bytes = 0, off_amax = 0, off_recv = 0, off_gather = 0;
+  uint8_t* peer[h3::kTpMaxWorld] = {};
+  bool ipc_open[h3::kTpMaxWorld] = {};
+  uint8_t* work = nullptr;
+  int8_t* xq = nullptr;
+  float* xs = nullptr;
+  uint32_t* amax = nullptr;
+  unsigned int* ready = nullptr;
+  void* a = nullptr;
+  int8_t* q2 = nullptr;
+  uint32_t epoch = 0;
+
+  uint32_t* flags(int q) const { return reinterpret_cast<uint32_t*>(peer[q]); }
+  uint32_t* amax_slot(int q, int parity, int slot) const {
+    return reinterpret_cast<uint32_t*>(peer[q] + off_amax) + ((int64_t)parity * world + slot) * max_rows;
+  }
+  int32_t* recv_slot(int q, int parity, int slot) const {
+    return reinterpret_cast<int32_t*>(peer[q] + off_recv) + ((int64_t)parity * world + slot) * per_max * d;
+  }
+  uint16_t* gather(int q, int parity) const {
+    return reinterpret_cast<uint16_t*>(peer[q] + off_gather) + (int64_t)parity * max_rows * d;
+  }
+  bool connected() const {
+    for (int q = 0; q < world; ++q)
+      if (peer[q] == nullptr) return false;
+    return true;
+  }
+};
+
+void tp_release(TpComm* c) {
+  for (int q = 0; q < h3::kTpMaxWorld; ++q)
+    if (c->ipc_open[q]) cudaIpcCloseMemHandle(c->peer[q]);
+  if (c->shared) cudaFree(c->shared);
+  if (c->work) cudaFree(c->work);
+  delete c;
+}
+
+int tp_barrier_impl(TpComm* c, cudaStream_t st) {
+  if (c->world == 1 || c->linked_local) return H3B200_OK;
+  ++c->epoch;
+  h3::TpPtrs out{};
+  for (int q = 0; q < c->world; ++q) out.p[q] = c->flags(q) + c->rank;
+  return from_cuda(h3::launch_tp_barrier(out, c->flags(c->rank), c->world, c->epoch, c->timeout_ns, st), "tp_barrier");
+}
+
+int tp_stage_impl(TpComm* c, int stage, int64_t chunk, const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                  const void* gate, const int8_t* w1q, const float* s1, const int8_t* w2q, const float* s2, void* out,
+                  int64_t ldo, int64_t lo, int64_t hi, cudaStream_t st) {
+  const int64_t rows = hi - lo, d = c->d, ffn = c->ffn;
+  const int parity = (int)(chunk & 1), me = c->rank, W = c->world;
+  const int64_t per = (rows + W - 1) / W;  // rows owned per rank in this chunk
+  cudaError_t e = cudaSuccess;
+  switch (stage) {
+    case 1: {  // quantize x, fc1 + GELU + row absmax, absmax into every rank's slot
+      e = h3::launch_quantize_rows(static_cast<const uint16_t*>(x) + lo * ldx, ldx, rows, d, H3B200_ACT_NONE, nullptr,
+                                   c->xq, c->xs, st);
+      if (e != cudaSuccess) return from_cuda(e, "tp_stage 1: quantize x");
+      const int64_t zero_bytes = reinterpret_cast<uint8_t*>(c->ready + h3::requant_ready_count(rows)) -
+                                 reinterpret_cast<uint8_t*>(c->amax);
+      if ((e = cudaMemsetAsync(c->amax, 0, (size_t)zero_bytes, st)) != cudaSuccess) return from_cuda(e, "tp_stage 1: memset");
+      h3::GemmArgs g1;
+      g1.a = c->xq; g1.w = w1q; g1.m = rows; g1.n = ffn; g1.k = d; g1.lda = d; g1.ldw = d;
+      g1.epilogue = h3::kEpiGeluAbsmax; g1.a_scale = c->xs; g1.w_scale = s1; g1.w_scale_per_channel = 1;
+      g1.out = c->a; g1.ldo = ffn; g1.row_absmax = reinterpret_cast<float*>(c->amax);
+      if ((e = h3::launch_gemm_i8(g1, st)) != cudaSuccess) return from_cuda(e, "tp_stage 1: fc1");
+      if (W > 1) {
+        h3::TpPtrs dst{};
+        for (int q = 0; q < W; ++q) dst.p[q] = c->amax_slot(q, parity, me);
+        e = h3::launch_tp_push_u32(c->amax, rows, dst, W, st);
+      }
+      return from_cuda(e, "tp_stage 1: absmax push");
+    }
+    case 2: {  // global absmax, fc2 (own requant) with every int32 row stored at its owner
+      if (W > 1 && (e = h3::launch_tp_max_u32(c->amax_slot(me, parity, 0), c->max_rows, W, rows, c->amax, st)) != cudaSuccess)
+        return from_cuda(e, "tp_stage 2: absmax max");
+      h3::GemmArgs g2;
+      g2.a = c->q2; g2.w = w2q; g2.m = rows; g2.n = d; g2.k = ffn; g2.lda = ffn; g2.ldw = ffn;
+      g2.epilogue = h3::kEpiI32;
+      g2.requant_src = c->a; g2.requant_lds = ffn; g2.requant_ready = c->ready;
+      g2.row_absmax = reinterpret_cast<float*>(c->amax);
+      g2.out = c->recv_slot(me, parity, me); g2.ldo = d;
+      g2.peer_rows = per;
+      for (int q = 0; q < W; ++q) g2.peer_out[q] = c->recv_slot(q, parity, me);
+      return from_cuda(h3::launch_gemm_i8(g2, st), "tp_stage 2: fc2 (requant, rows to their owners)");
+    }
+    case 3: {  // this rank's rows: sum of partials, dequant + gated residual, rows to every rank
+      const int64_t r0 = std::min<int64_t>(rows, (int64_t)me * per), r1 = std::min<int64_t>(rows, r0 + per);
+      if (r1 <= r0) return H3B200_OK;
+      h3::TpPtrs g{};
+      for (int q = 0; q < W; ++q)
+        if (q != me) g.p[q] = c->gather(q, parity) + r0 * d;
+      e = h3::launch_tp_finish(c->recv_slot(me, parity, 0), c->per_max * d, W, r1 - r0, d, c->amax + r0, s2, gate,
+                               static_cast<const uint16_t*>(residual) + (lo + r0) * ldr, ldr,
+                               static_cast<uint16_t*>(out) + (lo + r0) * ldo, ldo, g, st);
+      return from_cuda(e, "tp_stage 3: owner rows");
+    }
+    case 4: {  // the other owners' rows of this chunk, from the gather buffer into out
+      for (int q = 0; q < W && e == cudaSuccess; ++q) {
+        const int64_t q0 = std::min<int64_t>(rows, (int64_t)q * per), q1 = std::min<int64_t>(rows, q0 + per);
+        if (q == me || q1 <= q0) continue;
+        e = cudaMemcpy2DAsync(static_cast<uint16_t*>(out) + (lo + q0) * ldo, (size_t)ldo * 2,
+                              c->gather(me, parity) + q0 * d, (size_t)d * 2, (size_t)d * 2, (size_t)(q1 - q0),
+                              cudaMemcpyDeviceToDevice, st);
+      }
+      return from_cuda(e, "tp_stage 4: gathered rows");
+    }
+    default:
+      return fail(H3B200_ERR_INVALID, "tp_stage: stage must be 1..4, got %d", stage);
+  }
+}
+
+int tp_check_args(const char* what, TpComm* c, const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                  const void* gate, const int8_t* w1q, const float* s1, const int8_t* w2q, const float* s2,
+                  const void* out, int64_t ldo) {
+  if (c == nullptr) return fail(H3B200_ERR_INVALID, "%s: NULL communicator", what);
+  if (!c->connected()) return fail(H3B200_ERR_INVALID, "%s: communicator not connected (h3b200_tp_comm_open or h3b200_tp_comm_link_local first)", what);
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != c->device) return fail(H3B200_ERR_INVALID, "%s: current device %d is not the communicator's device %d", what, dev, c->device);
+  if (!x || !residual || !gate || !w1q || !s1 || !w2q || !s2 || !out) return fail(H3B200_ERR_INVALID, "%s: NULL pointer", what);
+  if (ldx < c->d || ldr < c->d || ldo < c->d || ldr % 8 || ldo % 8)
+    return fail(H3B200_ERR_INVALID, "%s: row strides must be >= d (residual and out: multiples of 8 elements)", what);
+  if ((reinterpret_cast<uintptr_t>(residual) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(gate) & 15) || (reinterpret_cast<uintptr_t>(w1q) & 15) ||
+      (reinterpret_cast<uintptr_t>(w2q) & 15))
+    return fail(H3B200_ERR_UNSUPPORTED, "%s: residual, out, gate and weights must be 16-byte aligned", what);
+  return H3B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int h3b200_tp_comm_create(int rank, int world, int64_t max_rows, int64_t d, int64_t ffn_shard,
+                          int64_t barrier_timeout_ns, void** comm, uint8_t* handle) {
+  if (comm == nullptr || handle == nullptr) return fail(H3B200_ERR_INVALID, "tp_comm_create: NULL output");
+  *comm = nullptr;
+  if (world < 1 || world > h3::kTpMaxWorld || rank < 0 || rank >= world)
+    return fail(H3B200_ERR_INVALID, "tp_comm_create: rank %d of world %d (1..%d ranks)", rank, world, h3::kTpMaxWorld);
+  if (max_rows <= 0 || d <= 0 || ffn_shard <= 0 || d % 16 || ffn_shard % 16 || max_rows > (1ll << 24))
+    return fail(H3B200_ERR_INVALID, "tp_comm_create: needs 0 < max_rows <= 2^24 and d, ffn_shard positive multiples of 16");
+  if (barrier_timeout_ns < 0) return fail(H3B200_ERR_INVALID, "tp_comm_create: negative barrier timeout");
+  TpComm* c = new TpComm();
+  c->rank = rank;
+  c->world = world;
+  c->max_rows = max_rows;
+  c->d = d;
+  c->ffn = ffn_shard;
+  c->per_max = (max_rows + world - 1) / world;
+  c->timeout_ns = barrier_timeout_ns > 0 ? (unsigned long long)barrier_timeout_ns : kTpDefaultTimeoutNs;
+  cudaError_t e = cudaGetDevice(&c->device);
+  size_t off = 256;  // flags
+  c->off_amax = off;
+  off += (size_t)round_up(2 * world * max_rows * 4, 256);
+  c->off_recv = off;
+  off += (size_t)round_up(2 * world * c->per_max * d * 4, 256);
+  c->off_gather = off;
+  off += (size_t)round_up(2 * max_rows * d * 2, 256);
+  c->shared_bytes = off;
+  if (e == cudaSuccess) e = cudaMalloc(&c->shared, c->shared_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->shared, 0, c->shared_bytes);
+  const int64_t work_bytes = round_up(max_rows * d, 256) + round_up(max_rows * 4, 256) +
+                             round_up((max_rows + h3::requant_ready_count(max_rows)) * 4, 256) +
+                             round_up(max_rows * ffn_shard * 2, 256) + round_up(max_rows * ffn_shard, 256) + 1024;
+  if (e == cudaSuccess) e = cudaMalloc(&c->work, (size_t)work_bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // flags are zero before any rank can map them
+  if (e != cudaSuccess) {
+    tp_release(c);
+    return from_cuda(e, "tp_comm_create");
+  }
+  Carver w{c->work, work_bytes};
+  c->xq = static_cast<int8_t*>(w.take(max_rows * d));
+  c->xs = static_cast<float*>(w.take(max_rows * 4));
+  c->amax = static_cast<uint32_t*>(w.take((max_rows + h3::requant_ready_count(max_rows)) * 4));
+  c->ready = reinterpret_cast<unsigned int*>(c->amax + max_rows);  // the requant counters follow the absmax
+  c->a = w.take(max_rows * ffn_shard * 2);
+  c->q2 = static_cast<int8_t*>(w.take(max_rows * ffn_shard));
+  if (!w.ok) {
+    tp_release(c);
+    return fail(H3B200_ERR_INVALID, "tp_comm_create: internal workspace layout");
+  }
+  c->peer[rank] = c->shared;
+  TpHandle h;
+  memset(&h, 0, sizeof(h));
+  memcpy(h.magic, kTpMagic, sizeof(kTpMagic));
+  h.rank = rank;
+  h.world = world;
+  h.max_rows = max_rows;
+  h.d = d;
+  h.ffn = ffn_shard;
+  h.shared_bytes = c->shared_bytes;
+  if (world > 1 && (e = cudaIpcGetMemHandle(&h.ipc, c->shared)) != cudaSuccess) {
+    tp_release(c);
+    return from_cuda(e, "tp_comm_create: cudaIpcGetMemHandle");
+  }
+  memset(handle, 0, H3B200_TP_HANDLE_BYTES);
+  memcpy(handle, &h, sizeof(h));
+  *comm = c;
+  return H3B200_OK;
+}
+
+int h3b200_tp_comm_open(void* comm, const uint8_t* handles) {
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (c == nullptr || handles == nullptr) return fail(H3B200_ERR_INVALID, "tp_comm_open: NULL argument");
+  if (c->linked_local) return fail(H3B200_ERR_INVALID, "tp_comm_open: communicator is linked locally");
+  TpHandle hs[h3::kTpMaxWorld];
+  for (int q = 0; q < c->world; ++q) {
+    memcpy(&hs[q], handles + (size_t)q * H3B200_TP_HANDLE_BYTES, sizeof(TpHandle));
+    const TpHandle& h = hs[q];
+    if (memcmp(h.magic, kTpMagic, sizeof(kTpMagic)) != 0 || h.rank != q || h.world != c->world ||
+        h.max_rows != c->max_rows || h.d != c->d || h.ffn != c->ffn || h.shared_bytes != c->shared_bytes)
+      return fail(H3B200_ERR_INVALID, "tp_comm_open: handle %d does not match this communicator (rank order, world, max_rows, d, ffn_shard)", q);
+    if (q != c->rank && c->ipc_open[q]) return fail(H3B200_ERR_INVALID, "tp_comm_open: already open");
+  }
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != c->device) return fail(H3B200_ERR_INVALID, "tp_comm_open: current device %d is not the communicator's device %d", dev, c->device);
+  for (int q = 0; q < c->world; ++q) {
+    if (q == c->rank) continue;
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, hs[q].ipc, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int r = 0; r < c->world; ++r)
+        if (c->ipc_open[r]) {
+          cudaIpcCloseMemHandle(c->peer[r]);
+          c->ipc_open[r] = false;
+          c->peer[r] = nullptr;
+        }
+      return from_cuda(e, "tp_comm_open: cudaIpcOpenMemHandle");
+    }
+    c->peer[q] = static_cast<uint8_t*>(p);
+    c->ipc_open[q] = true;
+  }
+  return H3B200_OK;
+}
+
+int h3b200_tp_comm_link_local(void* const* comms, int world) {
+  if (comms == nullptr || world < 1 || world > h3::kTpMaxWorld) return fail(H3B200_ERR_INVALID, "tp_comm_link_local: bad arguments");
+  TpComm* cs[h3::kTpMaxWorld];
+  for (int q = 0; q < world; ++q) {
+    cs[q] = static_cast<TpComm*>(comms[q]);
+    if (cs[q] == nullptr || cs[q]->world != world || cs[q]->rank != q || cs[q]->max_rows != cs[0]->max_rows ||
+        cs[q]->d != cs[0]->d || cs[q]->ffn != cs[0]->ffn || cs[q]->device != cs[0]->device)
+      return fail(H3B200_ERR_INVALID, "tp_comm_link_local: communicator %d is not rank %d of the same group on the same device", q, q);
+    for (int r = 0; r < world; ++r)
+      if (cs[q]->ipc_open[r]) return fail(H3B200_ERR_INVALID, "tp_comm_link_local: communicator %d is IPC-connected", q);
+  }
+  for (int q = 0; q < world; ++q) {
+    for (int r = 0; r < world; ++r) cs[q]->peer[r] = cs[r]->shared;
+    cs[q]->linked_local = true;
+  }
+  return H3B200_OK;
+}
+
+int h3b200_tp_comm_destroy(void* comm) {
+  if (comm != nullptr) tp_release(static_cast<TpComm*>(comm));
+  return H3B200_OK;
+}
+
+int h3b200_tp_barrier(void* comm, h3b200_stream_t stream) {
+  H3_GUARD("tp_barrier", stream);
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (c == nullptr || !c->connected()) return fail(H3B200_ERR_INVALID, "tp_barrier: communicator not connected");
+  return tp_barrier_impl(c, S(stream));
+}
+
+int h3b200_tp_stage(void* comm, int stage, int64_t chunk, const void* x, int64_t ldx, const void* residual,
+                    int64_t ldr, const void* gate, const int8_t* w1q, const float* s1, const int8_t* w2q,
+                    const float* s2, void* out, int64_t ldo, int64_t lo, int64_t hi, h3b200_stream_t stream) {
+  H3_GUARD("tp_stage", stream);
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (const int rc = tp_check_args("tp_stage", c, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo)) return rc;
+  if (chunk < 0 || lo < 0 || hi <= lo || hi - lo > c->max_rows)
+    return fail(H3B200_ERR_INVALID, "tp_stage: chunk rows [%lld, %lld) must be non-empty and at most max_rows", (long long)lo, (long long)hi);
+  return tp_stage_impl(c, stage, chunk, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo, lo, hi, S(stream));
+}
+
+int h3b200_tp_gated_mlp(void* comm, const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* gate,
+                        const int8_t* w1q, const float* s1, const int8_t* w2q, const float* s2, void* out,
+                        int64_t ldo, int64_t m, int64_t chunk_rows, h3b200_stream_t stream) {
+  H3_GUARD("tp_gated_mlp", stream);
+  TpComm* c = static_cast<TpComm*>(comm);
+  if (m < 0) return fail(H3B200_ERR_INVALID, "tp_gated_mlp: m < 0");
+  if (m == 0) return H3B200_OK;
+  if (const int rc = tp_check_args("tp_gated_mlp", c, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo)) return rc;
+  if (c->linked_local) return fail(H3B200_ERR_UNSUPPORTED, "tp_gated_mlp: locally linked communicators run stage by stage (h3b200_tp_stage)");
+  const int64_t chunk = chunk_rows > 0 ? std::min(chunk_rows, c->max_rows) : c->max_rows;
+  const cudaStream_t st = S(stream);
+  int rc = H3B200_OK;
+  int64_t prev_lo = 0, prev_hi = 0;
+  for (int64_t i = 0, lo = 0; lo < m; ++i, lo += chunk) {
+    const int64_t hi = std::min(m, lo + chunk);
+    // barrier A(i): every rank's owner rows of chunk i-1 are in the gather buffers
+    if ((rc = tp_stage_impl(c, 1, i, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo, lo, hi, st)) ||
+        (rc = tp_barrier_impl(c, st)))
+      return rc;
+    if (i > 0 && (rc = tp_stage_impl(c, 4, i - 1, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo, prev_lo,
+                                     prev_hi, st)))
+      return rc;
+    // barrier B(i): every rank's fc2 rows of chunk i are in their owners' receive slots
+    if ((rc = tp_stage_impl(c, 2, i, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo, lo, hi, st)) ||
+        (rc = tp_barrier_impl(c, st)) ||
+        (rc = tp_stage_impl(c, 3, i, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo, lo, hi, st)))
+      return rc;
+    prev_lo = lo;
+    prev_hi = hi;
+  }
+  const int64_t last = (m + chunk - 1) / chunk - 1;
+  if ((rc = tp_barrier_impl(c, st))) return rc;
+  return tp_stage_impl(c, 4, last, x, ldx, residual, ldr, gate, w1q, s1, w2q, s2, out, ldo, prev_lo, prev_hi, st);
+}
+
+}  // extern "C"
+

@@ -104,6 +104,9 @@ struct KParams {
   unsigned int* rq_horizon;   // highest block the tiles have asked for (zero at launch)
   int64_t rq_units;           // m * rq_upr
   int rq_upr;                 // units of kRqUnit elements per row
+  // kEpiI32 rows routed to their owners (GemmArgs::peer_out / peer_rows)
+  int32_t* peer_out[kTpMaxWorld];
+  int peer_rows;
 };
 
 template <int EPI>
@@ -249,7 +252,13 @@ __device__ __forceinline__ void gelu_chunk(const uint32_t (&r)[32], float xs, co
 // int32 accumulators of one 32-column chunk of one row, 128-bit stores.
 __device__ __forceinline__ void store_i32_chunk(const KParams& p, int row, int col0, const uint32_t (&r)[32]) {
   if (row < p.m) {
-    int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+    int32_t* o;
+    if (p.peer_rows > 0) {  // the owner's buffer (possibly another GPU's memory)
+      const int owner = row / p.peer_rows;
+      o = p.peer_out[owner] + (int64_t)(row - owner * p.peer_rows) * p.ldo + col0;
+    } else {
+      o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
+    }
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       if (col0 + 4 * g < p.n) stg_v4(o + 4 * g, make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]));
@@ -531,9 +540,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
                    const KParams p) {
-  // kEpiGatedResidualRq: the gated-residual epilogue on an A operand this kernel quantizes
-  constexpr bool kRq = EPI_ID == kEpiGatedResidualRq;
-  constexpr int EPI = kRq ? kEpiGatedResidual : EPI_ID;
+  // kEpiGatedResidualRq / kEpiI32Rq: the gated-residual / int32 epilogue on an A operand
+  // this kernel quantizes
+  constexpr bool kRq = EPI_ID == kEpiGatedResidualRq || EPI_ID == kEpiI32Rq;
+  constexpr int EPI = EPI_ID == kEpiGatedResidualRq ? kEpiGatedResidual : EPI_ID == kEpiI32Rq ? kEpiI32 : EPI_ID;
   constexpr bool kCorr = is_corr_epi<EPI>();
   constexpr bool kInBox = EPI == kEpiGatedResidual || EPI == kEpiGatedResidualCorr;
   constexpr int kBBytes = B_BYTES / CG;
@@ -1116,6 +1126,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if constexpr (EPI != kEpiI32) {
       if (lane == 0) bulk_wait_all();  // every output box written before the CTA exits
       __syncwarp();
+    } else {
+      if (p.peer_rows > 0) __threadfence_system();  // routed rows visible to the owners' GPUs
     }
   }
 
@@ -1190,7 +1202,9 @@ cudaError_t launch_epi(const TensorMaps& t, const KParams& kp, int grid, cudaStr
 template <int CG>
 cudaError_t launch_cg(int epilogue, const TensorMaps& t, const KParams& kp, int grid, cudaStream_t stream) {
   switch (epilogue) {
-    case kEpiI32: return launch_epi<kEpiI32, CG>(t, kp, grid, stream);
+    case kEpiI32:
+      if (kp.rq_src != nullptr) return launch_epi<kEpiI32Rq, CG>(t, kp, grid, stream);
+      return launch_epi<kEpiI32, CG>(t, kp, grid, stream);
     case kEpiBF16: return launch_epi<kEpiBF16, CG>(t, kp, grid, stream);
     case kEpiGeluAbsmax: return launch_epi<kEpiGeluAbsmax, CG>(t, kp, grid, stream);
     case kEpiGatedResidual:
@@ -1299,10 +1313,17 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
                                (reinterpret_cast<uintptr_t>(a.gate) & 15)))
     return cudaErrorNotSupported;
   if (a.requant_src != nullptr &&
-      (a.epilogue != kEpiGatedResidual || a.lda != a.k || a.k % 8 != 0 || a.requant_lds < a.k ||
+      ((a.epilogue != kEpiGatedResidual && a.epilogue != kEpiI32) || a.lda != a.k || a.k % 8 != 0 || a.requant_lds < a.k ||
        a.requant_lds % 8 != 0 || (reinterpret_cast<uintptr_t>(a.requant_src) & 15) || a.row_absmax == nullptr ||
        a.requant_ready == nullptr))
     return cudaErrorNotSupported;
+  if (a.peer_rows != 0) {
+    if (a.epilogue != kEpiI32 || a.peer_rows < 0 || a.peer_rows > INT32_MAX || a.ldo % 4 != 0 ||
+        (a.m + a.peer_rows - 1) / a.peer_rows > kTpMaxWorld)
+      return cudaErrorNotSupported;
+    for (int64_t o = 0; o < (a.m + a.peer_rows - 1) / a.peer_rows; ++o)
+      if (a.peer_out[o] == nullptr || (reinterpret_cast<uintptr_t>(a.peer_out[o]) & 15)) return cudaErrorNotSupported;
+  }
   const bool corr = a.epilogue == kEpiBF16Corr || a.epilogue == kEpiBF16CorrGelu || a.epilogue == kEpiGatedResidualCorr;
   if (corr && (a.sx == nullptr || a.corr_t == nullptr || a.kp <= 0 || a.kp % 64 != 0 || a.kp > kMaxCorrKp ||
                (reinterpret_cast<uintptr_t>(a.sx) & 15) || (reinterpret_cast<uintptr_t>(a.corr_t) & 15)))
@@ -1405,6 +1426,8 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.rq_horizon = a.requant_ready == nullptr ? nullptr : a.requant_ready + (a.m + 127) / 128;
   kp.rq_upr = (int)((a.k + kRqUnit - 1) / kRqUnit);
   kp.rq_units = a.m * kp.rq_upr;
+  for (int o = 0; o < kTpMaxWorld; ++o) kp.peer_out[o] = a.peer_out[o];
+  kp.peer_rows = (int)a.peer_rows;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

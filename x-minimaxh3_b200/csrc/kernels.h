@@ -28,7 +28,12 @@ enum GemmEpilogue : int {
   // internal: kEpiGatedResidual whose A operand the kernel quantizes itself
   // (GemmArgs::requant_src); chosen by launch_gemm_i8, not by callers
   kEpiGatedResidualRq = 9,
+  // internal: kEpiI32 on an A operand the kernel quantizes itself (requant_src set)
+  kEpiI32Rq = 10,
 };
+
+// Largest tensor-parallel group whose int32 rows one GEMM routes to their owners.
+constexpr int kTpMaxWorld = 8;
 
 struct GemmArgs {
   const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes
@@ -76,7 +81,29 @@ struct GemmArgs {
   const void* requant_src = nullptr;
   int64_t requant_lds = 0;
   unsigned int* requant_ready = nullptr;
+  // kEpiI32 with peer_rows > 0: output row r goes to peer_out[r / peer_rows] at row
+  // r % peer_rows (row stride ldo), instead of to out. The destinations may be other
+  // GPUs' memory (peer-mapped): the epilogue writes them with plain 16-byte stores
+  // and ends with a system-scope fence, so a stream-ordered barrier after the kernel
+  // publishes them.
+  int32_t* peer_out[kTpMaxWorld] = {};
+  int64_t peer_rows = 0;
 };
+
+// One pointer per rank of a tensor-parallel group (by value in kernel parameters).
+struct TpPtrs {
+  void* p[kTpMaxWorld];
+};
+
+// Tensor-parallel MLP exchange kernels (tp.cu); see that file for the protocol.
+cudaError_t launch_tp_push_u32(const uint32_t* src, int64_t n, const TpPtrs& dst, int ndst, cudaStream_t stream);
+cudaError_t launch_tp_barrier(const TpPtrs& flag_out, const uint32_t* my_flags, int world, uint32_t epoch,
+                              unsigned long long timeout_ns, cudaStream_t stream);
+cudaError_t launch_tp_max_u32(const uint32_t* slots, int64_t stride, int world, int64_t n, uint32_t* out,
+                              cudaStream_t stream);
+cudaError_t launch_tp_finish(const int32_t* recv, int64_t slot, int world, int64_t rows, int64_t n,
+                             const uint32_t* absmax, const float* ws, const void* gate, const void* residual,
+                             int64_t ldr, void* out, int64_t ldo, const TpPtrs& gather, cudaStream_t stream);
 
 // 32-bit words requant_ready needs for m rows: one counter per 128-row block (enough
 // for both tile shapes), then the progress word of the tiles.

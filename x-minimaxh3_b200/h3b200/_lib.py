@@ -83,7 +83,17 @@ SIGNATURES = {
     "h3b200_fused_gated_mlp_swiglu_w4a8": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _i64, _p,
                                                   _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64,
                                                   _p]),
+    "h3b200_tp_comm_create": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, ctypes.POINTER(_p), _p]),
+    "h3b200_tp_comm_open": (_i32, [_p, _p]),
+    "h3b200_tp_comm_link_local": (_i32, [ctypes.POINTER(_p), _i32]),
+    "h3b200_tp_comm_destroy": (_i32, [_p]),
+    "h3b200_tp_barrier": (_i32, [_p, _p]),
+    "h3b200_tp_stage": (_i32, [_p, _i32, _i64, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "h3b200_tp_gated_mlp": (_i32, [_p, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
 }
+
+TP_HANDLE_BYTES = 192
+STATUS_TP_BARRIER = 0x201
 
 _lock = threading.Lock()
 _lib = None

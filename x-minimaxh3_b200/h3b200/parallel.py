@@ -8,7 +8,17 @@ Two modes:
   range (and the matching rows of the RoPE table) and runs the single-GPU
   kernels on it. There is no collective on the data path; results equal the
   single-GPU results bit for bit.
-* Tensor-parallel MLP (long-video config). fc1 is column-split (rank r owns
+* Tensor-parallel MLP (long-video config), ``collective="p2p"`` (default on GPUs):
+  the exchange runs inside this package's kernels over NVLink peer memory
+  (:class:`TPComm`, ``h3b200_tp_*``): fc1's row absmax is pushed into every rank's
+  slot and max-reduced after a cross-GPU flag barrier, fc2 quantizes its own input
+  with that global absmax and its epilogue stores each int32 partial row directly
+  into the receive slot of the rank that owns the row (the reduce-scatter fused into
+  the GEMM), and each owner sums the partials, applies dequant + gated residual and
+  stores its finished rows into every rank's gather buffer (the all-gather fused into
+  that pass). No NCCL call on the data path.
+* Tensor-parallel MLP over NCCL (``collective="reduce_scatter"`` / ``"all_reduce"``,
+  also the path the CPU tests drive with gloo). fc1 is column-split (rank r owns
   ffn rows [r*ffn/g, (r+1)*ffn/g) of W1), GELU is local, and the per-token
   requant scale needs the row absmax over all ffn columns: one all-reduce(MAX)
   of an fp32 [M] vector, after which every rank quantizes with the global scale
@@ -27,6 +37,7 @@ this package) so the orchestration can be exercised on CPU ranks in tests.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -111,12 +122,151 @@ def _world(group=None) -> tuple[int, int]:
     return dist.get_world_size(group), dist.get_rank(group)
 
 
-COLLECTIVES = ("reduce_scatter", "all_reduce")
+COLLECTIVES = ("p2p", "reduce_scatter", "all_reduce")
+# the forms whose exchange goes through torch.distributed (any backend, any ``ops``)
+PG_COLLECTIVES = ("reduce_scatter", "all_reduce")
+
+
+class TPComm:
+    """Peer-memory communicator of the tensor-parallel MLP (``h3b200_tp_comm_*``).
+
+    Every rank of ``group`` builds one with the same ``max_rows`` (the token chunk),
+    ``d`` and ``ffn_shard`` (its fc1 width). The constructor exchanges the CUDA IPC
+    handles of the ranks' exchange regions over the process group (one all-gather)
+    and maps the other ranks' regions; from then on the data path uses no collective:
+    the kernels store into the peers' memory over NVLink and meet at flag barriers
+    in it (bounded waits: status 0x201 on expiry).
+
+    Call :meth:`close` on every rank once the last MLP has been issued everywhere
+    (it synchronises the device and the group before the regions are freed)."""
+
+    def __init__(self, max_rows: int, d: int, ffn_shard: int, group=None, barrier_timeout_s: float = 5.0,
+                 *, _local: tuple[int, int] | None = None):
+        from . import _lib
+
+        world, rank = _world(group) if _local is None else _local
+        self.world, self.rank, self.group = world, rank, group
+        self.max_rows, self.d, self.ffn = int(max_rows), int(d), int(ffn_shard)
+        self.device = torch.cuda.current_device()
+        self.linked = _local is not None
+        lib = _lib.load()
+        handle = (ctypes.c_uint8 * _lib.TP_HANDLE_BYTES)()
+        ptr = ctypes.c_void_p()
+        _lib.check(lib.h3b200_tp_comm_create(rank, world, self.max_rows, self.d, self.ffn,
+                                             int(barrier_timeout_s * 1e9), ctypes.byref(ptr), handle),
+                   "h3b200_tp_comm_create")
+        self._ptr = ptr
+        if _local is None and world > 1:
+            dev = self._group_device()
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=dev)
+            every = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(every, mine, group=group)
+            blob = b"".join(bytes(t.cpu().tolist()) for t in every)
+            _lib.check(lib.h3b200_tp_comm_open(ptr, (ctypes.c_uint8 * len(blob)).from_buffer_copy(blob)),
+                       "h3b200_tp_comm_open")
+            mapped = torch.ones(1, device=dev)
+            dist.all_reduce(mapped, group=group)  # every rank has mapped every region
+
+    def _group_device(self):
+        return torch.device("cuda", self.device) if dist.get_backend(self.group) == "nccl" else torch.device("cpu")
+
+    @classmethod
+    def linked_local(cls, world: int, max_rows: int, d: int, ffn_shard: int) -> list["TPComm"]:
+        """``world`` communicators in this process on the current device, each other's
+        peers without IPC (barriers are no-ops): for running every rank's stages in
+        order on one GPU (:meth:`stage`)."""
+        from . import _lib
+
+        comms = [cls(max_rows, d, ffn_shard, _local=(world, r)) for r in range(world)]
+        ptrs = (ctypes.c_void_p * world)(*[c._ptr.value for c in comms])
+        _lib.call("h3b200_tp_comm_link_local", ptrs, world)
+        return comms
+
+    def _args(self, x, residual, gate, shard, out):
+        if not (x.is_cuda and residual.is_cuda and out.is_cuda):
+            raise ValueError("TPComm: x, residual and out must be CUDA tensors")
+        for name, t in (("x", x), ("residual", residual), ("out", out), ("gate", gate)):
+            if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+                raise ValueError(f"TPComm: {name} must be bf16 with unit column stride")
+        if x.shape[1] != self.d or residual.shape != x.shape or out.shape != x.shape or gate.numel() != self.d:
+            raise ValueError(f"TPComm: x, residual, out must be [m, {self.d}] and gate [{self.d}]")
+        if tuple(shard.w1q.shape) != (self.ffn, self.d) or tuple(shard.w2q.shape) != (self.d, self.ffn) or \
+                not shard.w1q.is_contiguous() or not shard.w2q.is_contiguous():
+            raise ValueError(f"TPComm: shard weights must be w1q [{self.ffn}, {self.d}], w2q [{self.d}, {self.ffn}], "
+                             "contiguous")
+        return (x.data_ptr(), x.stride(0), residual.data_ptr(), residual.stride(0), gate.data_ptr(),
+                shard.w1q.data_ptr(), shard.s1.data_ptr(), shard.w2q.data_ptr(), shard.s2.data_ptr(),
+                out.data_ptr(), out.stride(0))
+
+    def run(self, x, residual, gate, shard: "TPShard", out, chunk_rows: int | None = None):
+        """The whole tensor-parallel MLP over ``x`` [m, d] (every rank, same arguments)."""
+        from . import _lib
+
+        _lib.call("h3b200_tp_gated_mlp", self._ptr, *self._args(x, residual, gate, shard, out), x.shape[0],
+                  int(chunk_rows or self.max_rows), torch.cuda.current_stream().cuda_stream)
+        return out
+
+    def stage(self, stage: int, chunk: int, x, residual, gate, shard: "TPShard", out, lo: int, hi: int):
+        """One step of chunk ``chunk`` (rows [lo, hi)): 1 quantize + fc1 + absmax push,
+        2 absmax max + fc2 with routed rows, 3 owner rows, 4 other owners' rows into out."""
+        from . import _lib
+
+        _lib.call("h3b200_tp_stage", self._ptr, stage, chunk, *self._args(x, residual, gate, shard, out), lo, hi,
+                  torch.cuda.current_stream().cuda_stream)
+
+    def barrier(self):
+        from . import _lib
+
+        _lib.call("h3b200_tp_barrier", self._ptr, torch.cuda.current_stream().cuda_stream)
+
+    def close(self):
+        """Free the exchange regions (every rank; after its last MLP call)."""
+        from . import _lib
+
+        if self._ptr is None or not self._ptr.value:
+            return
+        torch.cuda.synchronize(self.device)
+        if not self.linked and self.world > 1:
+            done = torch.ones(1, device=self._group_device())
+            dist.all_reduce(done, group=self.group)  # no rank still writes into another's region
+        _lib.call("h3b200_tp_comm_destroy", self._ptr)
+        self._ptr = None
+
+    def __del__(self):
+        # a group member cannot be freed without the others' agreement: only
+        # single-rank and locally linked communicators are released here
+        try:
+            if self._ptr is not None and self._ptr.value and (self.world == 1 or self.linked):
+                from . import _lib
+
+                torch.cuda.synchronize(self.device)
+                _lib.load().h3b200_tp_comm_destroy(self._ptr)
+                self._ptr = None
+        except Exception:
+            pass
+
+
+_COMMS: dict = {}
+
+
+def tp_comm(max_rows: int, d: int, ffn_shard: int, group=None) -> TPComm:
+    """The cached :class:`TPComm` of ``group`` for these sizes (created collectively on first use)."""
+    key = (id(group), torch.cuda.current_device(), int(max_rows), int(d), int(ffn_shard))
+    comm = _COMMS.get(key)
+    if comm is None:
+        comm = _COMMS[key] = TPComm(max_rows, d, ffn_shard, group=group)
+    return comm
+
+
+def close_tp_comms() -> None:
+    """Close every cached communicator (collective: call on every rank)."""
+    for key in list(_COMMS):
+        _COMMS.pop(key).close()
 
 
 def tp_gated_mlp(x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor, shard: TPShard,
                  group=None, chunk_tokens: int = 8192, ops=None, out: torch.Tensor | None = None,
-                 collective: str = "reduce_scatter") -> torch.Tensor:
+                 collective: str | None = None) -> torch.Tensor:
     """Tensor-parallel fused gated W8A8 MLP; ``x``/``residual`` [M, d] are replicated on every rank.
 
     Per token chunk: quantize x, fc1 on this rank's W1 rows with the GELU + row-absmax
@@ -129,20 +279,35 @@ def tp_gated_mlp(x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor, sh
       all-gather the bf16 output rows (6 bytes per output element cross the links
       instead of the all-reduce's 8, and each rank runs 1/world of the epilogue);
     * ``collective="all_reduce"``: all-reduce the int32 partials, every rank runs the
-      whole epilogue.
+      whole epilogue;
+    * ``collective="p2p"`` (the default for CUDA tensors with the package's kernels):
+      the same arithmetic with the exchanges inside the kernels over NVLink peer memory
+      (:class:`TPComm`); with one rank it is the single-GPU fused MLP per chunk.
 
     The reduction of chunk i runs asynchronously while chunk i+1 computes; chunk i's
     epilogue runs right after chunk i+1's fc2 is issued, so at most two chunks' partial
     sums are alive at once. Every rank takes the same collective steps in the same
     order. The output equals the single-GPU fused MLP bit for bit (int32 sums are exact
     in any order). With no process group (or one rank) no collective is issued."""
+    if collective is None:
+        collective = "p2p" if ops is None and x.is_cuda else "reduce_scatter"
     if collective not in COLLECTIVES:
         raise ValueError(f"collective must be one of {COLLECTIVES}, got {collective!r}")
+    if collective == "p2p" and ops is not None:
+        raise ValueError("collective='p2p' runs this package's kernels; it takes no ops object")
     ops = ops or CudaOps()
     world, rank = _world(group)
     m = x.shape[0]
     if out is None:
         out = torch.empty_like(residual)
+    if collective == "p2p":
+        if world == 1:
+            for lo in range(0, m, chunk_tokens):
+                hi = min(m, lo + chunk_tokens)
+                ops.fused_mlp(residual[lo:hi], x[lo:hi], shard.w1q, shard.s1, shard.w2q, shard.s2, gate, out[lo:hi])
+            return out
+        comm = tp_comm(chunk_tokens, x.shape[1], shard.w1q.shape[0], group)
+        return comm.run(x, residual, gate, shard, out, chunk_tokens)
     prev = None
     for lo in range(0, m, chunk_tokens):
         hi = min(m, lo + chunk_tokens)
