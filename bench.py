@@ -813,9 +813,10 @@ def run_ours(args, rank, world, local_rank):
     del q4, k4, x4, r4, o4, table4, work5
 
     # ---- config 4, tensor-parallel MLP: all 196,560 tokens replicated on every rank, W1 rows and
-    #      W2 columns split N ways (fc1 -> all-reduce(MAX) of the row absmax -> requant -> fc2 int32
-    #      partials -> reduce-scatter + epilogue on owned rows + bf16 all-gather, or int32 all-reduce),
-    #      8,192-token chunks; strong scaling (total work fixed) ----
+    #      W2 columns split N ways, 8,192-token chunks; strong scaling (total work fixed). "p2p": the
+    #      exchanges inside the kernels over NVLink peer memory (absmax push + flag barrier, fc2 rows
+    #      stored at their owners, owner pass pushing finished rows); the NCCL forms (int32
+    #      reduce-scatter + bf16 all-gather, or int32 all-reduce) are timed beside it ----
     gt = torch.Generator(device=dev).manual_seed(6)      # the same replicated inputs on every rank
     xt = torch.randn(M4, D_MODEL, generator=gt, device=dev).to(torch.bfloat16)
     rt = torch.randn(M4, D_MODEL, generator=gt, device=dev).to(torch.bfloat16)
@@ -831,7 +832,7 @@ def run_ours(args, rank, world, local_rank):
         return float(t.item())
 
     tp_ms = {}
-    for coll in (PAR.COLLECTIVES if world > 1 else PAR.COLLECTIVES[:1]):
+    for coll in (PAR.COLLECTIVES if world > 1 else ("p2p",)):
         def k_tp(coll=coll):
             PAR.tp_gated_mlp(xt, rt, gate, tp_shard, chunk_tokens=TP_CHUNK, out=ot, collective=coll)
 
@@ -862,6 +863,7 @@ def run_ours(args, rank, world, local_rank):
         tp_coll_ms = max_over_ranks(timed(k_coll, 3, stream))
         del am_t, acc_t, part_t, loc_t, gat_t
     del xt, rt, ot, tp_shard
+    PAR.close_tp_comms()  # every rank: the peer-memory exchange regions of the p2p form
 
     # ---- library INT8 reference: cuBLASLt through torch._int_mm, 8192^3, same box and run ----
     lib_int8_tops = None
@@ -964,11 +966,14 @@ def run_ours(args, rank, world, local_rank):
                                   "int8_tops": M_TOKENS * OPS_PER_TOKEN / (w4_ms * 1e-3) / 1e12,
                                   "weights": "asymmetric int4, group 128, ConvRot-256, decoded per call"},
                 "tp_mlp_cfg4": {"tokens_total": M4, "tensor_parallel": world, "chunk_tokens": TP_CHUNK,
-                                "ms": tp_ms["reduce_scatter"], "tokens_per_s": M4 / (tp_ms["reduce_scatter"] * 1e-3),
-                                "int8_tops": M4 * OPS_PER_TOKEN / (tp_ms["reduce_scatter"] * 1e-3) / 1e12,
-                                "collective": "int32 reduce-scatter + bf16 all-gather (NCCL), absmax all-reduce(MAX)",
-                                "all_reduce_variant_ms": tp_ms.get("all_reduce"),
-                                "collectives_alone_ms": tp_coll_ms,
+                                "ms": tp_ms["p2p"], "tokens_per_s": M4 / (tp_ms["p2p"] * 1e-3),
+                                "int8_tops": M4 * OPS_PER_TOKEN / (tp_ms["p2p"] * 1e-3) / 1e12,
+                                "collective": ("in-kernel over NVLink peer memory: absmax push + flag barrier, fc2 "
+                                               "int32 rows stored at their owners, owner rows pushed to every rank"
+                                               if world > 1 else "none (one rank: the fused MLP per chunk)"),
+                                "nccl_reduce_scatter_variant_ms": tp_ms.get("reduce_scatter"),
+                                "nccl_all_reduce_variant_ms": tp_ms.get("all_reduce"),
+                                "nccl_collectives_alone_ms": tp_coll_ms,
                                 "scaling": "strong (196,560 tokens in total at every N)"},
                 "long_video_block_cfg4": {"tokens_total": M4, "tokens_this_rank": m4, "ms": blk_ms,
                                           "tokens_per_s": M4 / (blk_ms * 1e-3),
