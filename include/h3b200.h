@@ -566,8 +566,8 @@ H3B200_API int h3b200_fused_gated_mlp_swiglu_w4a8(const void* x, int64_t ldx, co
  * Per token chunk of c rows: quantize x, fc1 + GELU + row absmax on the own columns,
  * the row absmax max-reduced over the ranks (pushed into every rank's slot, barrier,
  * max), fc2 quantizing its own input with that global absmax and storing each int32
- * partial row straight into the receive slot of the rank that owns the row (rows
- * [q ceil(c/world), (q+1) ceil(c/world)) belong to rank q), barrier, then each owner
+ * partial row straight into the receive slot of the rank that owns the row (blocks of
+ * 128 rows round-robin: row r belongs to rank (r / 128) % world), barrier, then each owner
  * sums the ranks' partials, applies dequant + gated residual and writes its rows to
  * its own out and to every rank's gather buffer (copied into out after the next
  * barrier). No NCCL call on the data path. out is bit-identical to

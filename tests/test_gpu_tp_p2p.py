@@ -28,8 +28,10 @@ def _problem(m, d, ffn, seed):
     return x, res, gate, wt
 
 
+# rows are owned in 128-row blocks round-robin: chunks of 1 to 11 blocks, partial last blocks,
+# ranks that own nothing in a chunk
 @pytest.mark.parametrize("world,m,chunk", [(2, 1000, 383), (4, 700, 256), (8, 383, 383), (4, 5, 3),
-                                           (2, 2048, 1024)])
+                                           (2, 2048, 1024), (4, 3000, 1500), (8, 2500, 1300)])
 def test_linked_ranks_match_single_gpu_mlp(world, m, chunk):
     d, ffn = 512, 2048
     x, res, gate, wt = _problem(m, d, ffn, seed=world * 100 + m)

@@ -1075,6 +1075,7 @@ int h3b200_int8_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, cons
 //   flags   u32 [kTpMaxWorld]                      flag q: last barrier epoch from rank q
 //   amax    u32 [2][world][max_rows]               slot q: rank q's fc1 row absmax (chunk parity)
 //   recv    i32 [2][world][per_max][d]             slot q: rank q's fc2 partial rows owned here
+//                                                  (compact: tp_local_row of the block-cyclic owner)
 //   gather  bf16 [2][max_rows][d]                  finished rows of the other owners
 // Chunk parity double-buffers every slot; the two barriers per chunk order each
 // reuse after the last read of the same parity (see h3b200_tp_gated_mlp).
@@ -1148,7 +1149,6 @@ int tp_stage_impl(TpComm* c, int stage, int64_t chunk, const void* x, int64_t ld
                   int64_t ldo, int64_t lo, int64_t hi, cudaStream_t st) {
   const int64_t rows = hi - lo, d = c->d, ffn = c->ffn;
   const int parity = (int)(chunk & 1), me = c->rank, W = c->world;
-  const int64_t per = (rows + W - 1) / W;  // rows owned per rank in this chunk
   cudaError_t e = cudaSuccess;
   switch (stage) {
     case 1: {  // quantize x, fc1 + GELU + row absmax, absmax into every rank's slot
@@ -1179,31 +1179,23 @@ int tp_stage_impl(TpComm* c, int stage, int64_t chunk, const void* x, int64_t ld
       g2.requant_src = c->a; g2.requant_lds = ffn; g2.requant_ready = c->ready;
       g2.row_absmax = reinterpret_cast<float*>(c->amax);
       g2.out = c->recv_slot(me, parity, me); g2.ldo = d;
-      g2.peer_rows = per;
+      g2.peer_world = W;
       for (int q = 0; q < W; ++q) g2.peer_out[q] = c->recv_slot(q, parity, me);
       return from_cuda(h3::launch_gemm_i8(g2, st), "tp_stage 2: fc2 (requant, rows to their owners)");
     }
     case 3: {  // this rank's rows: sum of partials, dequant + gated residual, rows to every rank
-      const int64_t r0 = std::min<int64_t>(rows, (int64_t)me * per), r1 = std::min<int64_t>(rows, r0 + per);
-      if (r1 <= r0) return H3B200_OK;
       h3::TpPtrs g{};
       for (int q = 0; q < W; ++q)
-        if (q != me) g.p[q] = c->gather(q, parity) + r0 * d;
-      e = h3::launch_tp_finish(c->recv_slot(me, parity, 0), c->per_max * d, W, r1 - r0, d, c->amax + r0, s2, gate,
-                               static_cast<const uint16_t*>(residual) + (lo + r0) * ldr, ldr,
-                               static_cast<uint16_t*>(out) + (lo + r0) * ldo, ldo, g, st);
+        if (q != me) g.p[q] = c->gather(q, parity);
+      e = h3::launch_tp_finish(c->recv_slot(me, parity, 0), c->per_max * d, W, me, rows, d, c->amax, s2, gate,
+                               static_cast<const uint16_t*>(residual) + lo * ldr, ldr,
+                               static_cast<uint16_t*>(out) + lo * ldo, ldo, g, st);
       return from_cuda(e, "tp_stage 3: owner rows");
     }
-    case 4: {  // the other owners' rows of this chunk, from the gather buffer into out
-      for (int q = 0; q < W && e == cudaSuccess; ++q) {
-        const int64_t q0 = std::min<int64_t>(rows, (int64_t)q * per), q1 = std::min<int64_t>(rows, q0 + per);
-        if (q == me || q1 <= q0) continue;
-        e = cudaMemcpy2DAsync(static_cast<uint16_t*>(out) + (lo + q0) * ldo, (size_t)ldo * 2,
-                              c->gather(me, parity) + q0 * d, (size_t)d * 2, (size_t)d * 2, (size_t)(q1 - q0),
-                              cudaMemcpyDeviceToDevice, st);
-      }
-      return from_cuda(e, "tp_stage 4: gathered rows");
-    }
+    case 4:  // the other owners' rows of this chunk, from the gather buffer into out
+      return from_cuda(h3::launch_tp_gather_rows(c->gather(me, parity), W, me, rows, d,
+                                                 static_cast<uint16_t*>(out) + lo * ldo, ldo, st),
+                       "tp_stage 4: gathered rows");
     default:
       return fail(H3B200_ERR_INVALID, "tp_stage: stage must be 1..4, got %d", stage);
   }
@@ -1246,7 +1238,7 @@ int h3b200_tp_comm_create(int rank, int world, int64_t max_rows, int64_t d, int6
   c->max_rows = max_rows;
   c->d = d;
   c->ffn = ffn_shard;
-  c->per_max = (max_rows + world - 1) / world;
+  c->per_max = h3::tp_owned_span(max_rows, world, 0);  // rank 0 owns the most rows
   c->timeout_ns = barrier_timeout_ns > 0 ? (unsigned long long)barrier_timeout_ns : kTpDefaultTimeoutNs;
   cudaError_t e = cudaGetDevice(&c->device);
   size_t off = 256;  // flags

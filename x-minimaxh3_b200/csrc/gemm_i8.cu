@@ -104,9 +104,9 @@ struct KParams {
   unsigned int* rq_horizon;   // highest block the tiles have asked for (zero at launch)
   int64_t rq_units;           // m * rq_upr
   int rq_upr;                 // units of kRqUnit elements per row
-  // kEpiI32 rows routed to their owners (GemmArgs::peer_out / peer_rows)
+  // kEpiI32 rows routed to their owners (GemmArgs::peer_out / peer_world)
   int32_t* peer_out[kTpMaxWorld];
-  int peer_rows;
+  int peer_world;
 };
 
 template <int EPI>
@@ -252,16 +252,38 @@ __device__ __forceinline__ void gelu_chunk(const uint32_t (&r)[32], float xs, co
 // int32 accumulators of one 32-column chunk of one row, 128-bit stores.
 __device__ __forceinline__ void store_i32_chunk(const KParams& p, int row, int col0, const uint32_t (&r)[32]) {
   if (row < p.m) {
-    int32_t* o;
-    if (p.peer_rows > 0) {  // the owner's buffer (possibly another GPU's memory)
-      const int owner = row / p.peer_rows;
-      o = p.peer_out[owner] + (int64_t)(row - owner * p.peer_rows) * p.ldo + col0;
-    } else {
-      o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
-    }
+    int32_t* o = static_cast<int32_t*>(p.out) + (int64_t)row * p.ldo + col0;
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       if (col0 + 4 * g < p.n) stg_v4(o + 4 * g, make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]));
+  }
+}
+
+// Routed int32 rows (p.peer_world > 0), usually another GPU's memory: lane t holds row
+// row_base + t's 32 columns [col0, col0 + 32). The warp passes them through its 2 KB
+// staging box (32 rows x 64 bytes, 16-byte chunks swizzled by (row >> 1) & 3), one
+// 16-column half at a time, so that each store instruction writes 8 rows x 64
+// contiguous bytes instead of 32 rows x 16 bytes: fewer, larger writes over NVLink.
+__device__ __forceinline__ void store_i32_chunk_routed(const KParams& p, int row_base, int col0,
+                                                       const uint32_t (&r)[32], uint8_t* box, int lane) {
+  uint8_t* my_row = box + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    __syncwarp();  // the previous half's reads of the box are done
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(my_row + ((q ^ sw) << 4)) =
+          make_uint4(r[16 * h + 4 * q], r[16 * h + 4 * q + 1], r[16 * h + 4 * q + 2], r[16 * h + 4 * q + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = 8 * i + (lane >> 2), q = lane & 3;
+      const uint4 v = *reinterpret_cast<const uint4*>(box + rr * 64 + ((q ^ ((rr >> 1) & 3)) << 4));
+      const int row = row_base + rr, col = col0 + 16 * h + 4 * q;
+      if (row < p.m && col < p.n)
+        stg_v4(p.peer_out[tp_owner(row, p.peer_world)] + tp_local_row(row, p.peer_world) * p.ldo + col, v);
+    }
   }
 }
 
@@ -1050,7 +1072,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_wait_ld();
           if (col_base + c >= p.n) continue;  // warp-uniform
           if constexpr (EPI == kEpiI32) {
-            store_i32_chunk(p, row, col_base + c, r);
+            if (p.peer_world > 0)
+              store_i32_chunk_routed(p, box_row0, col_base + c, r, box, lane);
+            else
+              store_i32_chunk(p, row, col_base + c, r);
           } else {
             if (box_row0 >= p.m) continue;      // warp-uniform: no row of this box exists
             if (lane == 0) bulk_wait_read_all();  // the previous box has been read by its store
@@ -1126,8 +1151,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if constexpr (EPI != kEpiI32) {
       if (lane == 0) bulk_wait_all();  // every output box written before the CTA exits
       __syncwarp();
-    } else {
-      if (p.peer_rows > 0) __threadfence_system();  // routed rows visible to the owners' GPUs
     }
   }
 
@@ -1317,11 +1340,10 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
        a.requant_lds % 8 != 0 || (reinterpret_cast<uintptr_t>(a.requant_src) & 15) || a.row_absmax == nullptr ||
        a.requant_ready == nullptr))
     return cudaErrorNotSupported;
-  if (a.peer_rows != 0) {
-    if (a.epilogue != kEpiI32 || a.peer_rows < 0 || a.peer_rows > INT32_MAX || a.ldo % 4 != 0 ||
-        (a.m + a.peer_rows - 1) / a.peer_rows > kTpMaxWorld)
+  if (a.peer_world != 0) {
+    if (a.epilogue != kEpiI32 || a.peer_world < 0 || a.peer_world > kTpMaxWorld || a.ldo % 4 != 0)
       return cudaErrorNotSupported;
-    for (int64_t o = 0; o < (a.m + a.peer_rows - 1) / a.peer_rows; ++o)
+    for (int o = 0; o < a.peer_world; ++o)
       if (a.peer_out[o] == nullptr || (reinterpret_cast<uintptr_t>(a.peer_out[o]) & 15)) return cudaErrorNotSupported;
   }
   const bool corr = a.epilogue == kEpiBF16Corr || a.epilogue == kEpiBF16CorrGelu || a.epilogue == kEpiGatedResidualCorr;
@@ -1427,7 +1449,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.rq_upr = (int)((a.k + kRqUnit - 1) / kRqUnit);
   kp.rq_units = a.m * kp.rq_upr;
   for (int o = 0; o < kTpMaxWorld; ++o) kp.peer_out[o] = a.peer_out[o];
-  kp.peer_rows = (int)a.peer_rows;
+  kp.peer_world = a.peer_world;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

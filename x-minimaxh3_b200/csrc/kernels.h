@@ -34,6 +34,24 @@ enum GemmEpilogue : int {
 
 // Largest tensor-parallel group whose int32 rows one GEMM routes to their owners.
 constexpr int kTpMaxWorld = 8;
+// Row ownership in the tensor-parallel MLP: blocks of kTpBlockRows rows go round-robin
+// over the ranks (block b belongs to rank b % world), so the two CTAs of a 256-row GEMM
+// tile write to different owners and the NVLink traffic of the routed rows spreads over
+// the whole GEMM. An owner keeps its rows compact: block b is its local block b / world.
+constexpr int kTpBlockRows = 128;
+__host__ __device__ inline int tp_owner(int64_t row, int world) { return (int)((row / kTpBlockRows) % world); }
+__host__ __device__ inline int64_t tp_local_row(int64_t row, int world) {
+  return (row / kTpBlockRows / world) * kTpBlockRows + row % kTpBlockRows;
+}
+// rows [0, tp_owned_span(c, world, o)) of owner o's compact buffer cover its rows of a
+// c-row chunk (the last block may be partial; local rows past it map to rows >= c)
+__host__ __device__ inline int64_t tp_owned_span(int64_t c, int world, int o) {
+  const int64_t nb = (c + kTpBlockRows - 1) / kTpBlockRows;
+  return (o < nb ? (nb - o + world - 1) / world : 0) * kTpBlockRows;
+}
+__host__ __device__ inline int64_t tp_chunk_row(int64_t local, int world, int o) {
+  return ((local / kTpBlockRows) * world + o) * kTpBlockRows + local % kTpBlockRows;
+}
 
 struct GemmArgs {
   const int8_t* a = nullptr;  // [m, k] int8, row stride lda bytes
@@ -81,13 +99,13 @@ struct GemmArgs {
   const void* requant_src = nullptr;
   int64_t requant_lds = 0;
   unsigned int* requant_ready = nullptr;
-  // kEpiI32 with peer_rows > 0: output row r goes to peer_out[r / peer_rows] at row
-  // r % peer_rows (row stride ldo), instead of to out. The destinations may be other
-  // GPUs' memory (peer-mapped): the epilogue writes them with plain 16-byte stores
-  // and ends with a system-scope fence, so a stream-ordered barrier after the kernel
-  // publishes them.
+  // kEpiI32 with peer_world > 0: output row r goes to its owner's buffer
+  // peer_out[tp_owner(r, peer_world)] at row tp_local_row(r, peer_world) (row stride
+  // ldo), instead of to out. The destinations may be other GPUs' memory (peer-mapped):
+  // the epilogue writes them with plain 16-byte stores, published by a stream-ordered
+  // cross-GPU barrier after the kernel (a system-scope release).
   int32_t* peer_out[kTpMaxWorld] = {};
-  int64_t peer_rows = 0;
+  int peer_world = 0;
 };
 
 // One pointer per rank of a tensor-parallel group (by value in kernel parameters).
@@ -101,9 +119,11 @@ cudaError_t launch_tp_barrier(const TpPtrs& flag_out, const uint32_t* my_flags, 
                               unsigned long long timeout_ns, cudaStream_t stream);
 cudaError_t launch_tp_max_u32(const uint32_t* slots, int64_t stride, int world, int64_t n, uint32_t* out,
                               cudaStream_t stream);
-cudaError_t launch_tp_finish(const int32_t* recv, int64_t slot, int world, int64_t rows, int64_t n,
+cudaError_t launch_tp_finish(const int32_t* recv, int64_t slot, int world, int owner, int64_t rows, int64_t n,
                              const uint32_t* absmax, const float* ws, const void* gate, const void* residual,
                              int64_t ldr, void* out, int64_t ldo, const TpPtrs& gather, cudaStream_t stream);
+cudaError_t launch_tp_gather_rows(const void* gather, int world, int owner, int64_t rows, int64_t n, void* out,
+                                  int64_t ldo, cudaStream_t stream);
 
 // 32-bit words requant_ready needs for m rows: one counter per 128-row block (enough
 // for both tile shapes), then the progress word of the tiles.
