@@ -162,7 +162,10 @@ class ClockSampler:
 # ``convrot`` / ``convrot_x`` (ConvRot-256 + row quantization of a K = 12288 / 3072 bf16 input),
 # ``norm_rope`` (AdaLN + RMSNorm + RoPE on Q and K, 24 heads x 128) or
 # ``rms_adaln`` / ``rms_adaln_h3`` (standalone RMS-AdaLN on a [M, 3072] hidden stream with one
-# modulation row / on H3's [M, 5376] with three segments). Shapes are those of the config-1 MLP and config-3
+# modulation row / on H3's [M, 5376] with three segments), ``tp2_linked`` (one chunk of M tokens of the
+# tensor-parallel MLP over two ranks linked on this one GPU, every stage of both ranks in order:
+# its fc2 launches are ``gemm_i8_kernel<10, 2>``, the GEMM whose epilogue stores each int32 row at its
+# owner; the outputs are checked against the fused MLP). Shapes are those of the config-1 MLP and config-3
 # norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
 # runs the kernels it needs to build its inputs, then launches the kernel under
 # study ``--iters`` times, so a profiler can skip the set-up launches by kernel
@@ -172,7 +175,7 @@ class ClockSampler:
 
 CASES = ["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "fc2_rq", "mlp", "mlp_w4a8", "mlp_swiglu",
          "mlp_swiglu_w4", "decode_w4", "qknorm_h3", "qkv_h3", "convrot", "convrot_x", "norm_rope", "rms_adaln",
-         "rms_adaln_h3"]
+         "rms_adaln_h3", "tp2_linked"]
 
 
 def _case_mlp_inputs(m: int, dev):
@@ -343,6 +346,28 @@ def run_case(case: str, m: int, iters: int, report: bool = False):
         elif case == "mlp":
             ms = _case_timed(lambda: h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate, out=out), iters,
                         report)
+        elif case == "tp2_linked":
+            from h3b200 import parallel as PAR
+
+            world = 2
+            comms = PAR.TPComm.linked_local(world, m, D_MODEL, D_FFN // world)
+            shards = [PAR.TPShard.from_full(wt.w1q, wt.s1, wt.w2q, wt.s2, world, r) for r in range(world)]
+            outs = [torch.empty_like(res) for _ in range(world)]
+            chunk = [0]
+
+            def tp_step():
+                for stage in (1, 2, 3, 4):
+                    for r in range(world):
+                        comms[r].stage(stage, chunk[0], x, res, gate, shards[r], outs[r], 0, m)
+                chunk[0] += 1
+
+            ms = _case_timed(tp_step, iters, report)
+            ref = h3b200.fused_gated_mlp(res, x, wt.w1q, wt.s1, wt.w2q, wt.s2, gate)
+            torch.cuda.synchronize()
+            if not all(bool(torch.equal(o, ref)) for o in outs):
+                raise SystemExit("tp2_linked: a rank's output differs from the fused MLP")
+            for c in comms:
+                c.close()
         else:
             raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
