@@ -265,7 +265,7 @@ def close_tp_comms() -> None:
 
 
 def tp_gated_mlp(x: torch.Tensor, residual: torch.Tensor, gate: torch.Tensor, shard: TPShard,
-                 group=None, chunk_tokens: int = 8192, ops=None, out: torch.Tensor | None = None,
+                 group=None, chunk_tokens: int = 32768, ops=None, out: torch.Tensor | None = None,
                  collective: str | None = None) -> torch.Tensor:
     """Tensor-parallel fused gated W8A8 MLP; ``x``/``residual`` [M, d] are replicated on every rank.
 
