@@ -116,6 +116,16 @@ H3B200_API int h3b200_quantize_int8_rowwise_stochastic(const void* x, int64_t m,
                                                        h3b200_stream_t stream);
 
 /*
+ * quantize_int8_rowwise of an fp16 activation (no input activation): the
+ * reference's arithmetic in fp16 (eager/quantization.py:815-826, 857-875): fp16 row
+ * absmax, scale = max(absmax / 127, 1e-30) in fp32 (stored), divisor fp16(scale)
+ * (2^-14 when that is zero), q = clamp(rne(fp16(x / divisor)), -128, 127).
+ * x: fp16 [m, k] at row stride ldx elements; q int8 [m, k]; scale fp32 [m].
+ */
+H3B200_API int h3b200_quantize_int8_rowwise_f16(const void* x, int64_t m, int64_t k, int64_t ldx, int8_t* q,
+                                                float* scale, h3b200_stream_t stream);
+
+/*
  * Quantizer body with a precomputed per-row absmax (fp32 [m]); same arithmetic
  * as h3b200_quantize_int8_rowwise. Used for fc2's input after the fc1 epilogue
  * has reduced the row absmax (the reference quantizes the activated fc1 output
@@ -140,7 +150,10 @@ H3B200_API int h3b200_int8_mm(const int8_t* a, const int8_t* w, int64_t m, int64
  * _C.cutlass_int8_dequant (dlpack_bindings.cpp:2713, cutlass_gemm_int8.cu:613),
  * with the eager epilogue association (eager/quantization.py:1044-1048).
  * w_scale_numel is 1 (tensor-wise) or n (per channel). bias may be NULL.
- * out_dtype must be H3B200_DTYPE_BF16.
+ * out_dtype H3B200_DTYPE_BF16 or H3B200_DTYPE_F16 (the reference's out_dtype,
+ * eager/quantization.py:1044-1053): with F16, out = fp16(float(acc) * (x_scale *
+ * w_scale)) and then fp16(out + bias), bias fp16 [n] (the reference converts the
+ * bias to the output dtype before adding).
  */
 H3B200_API int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_scale, const int8_t* w, const float* w_scale,
                                     int64_t w_scale_numel, const void* bias, int out_dtype, void* out, int64_t m,

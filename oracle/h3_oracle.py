@@ -39,6 +39,9 @@ __all__ = [
     "quantize_int8_rowwise",
     "quantize_int8_rowwise_given_absmax",
     "quantize_int8_rowwise_stochastic",
+    "quantize_int8_rowwise_f16",
+    "dequant_epilogue_f16",
+    "int8_linear_f16",
     "stochastic_noise_bf16",
     "gelu_tanh_bf16",
     "silu_bf16",
@@ -135,6 +138,25 @@ def quantize_int8_rowwise(x_bf16: np.ndarray):
     xf = bf16_to_f32(x_bf16)
     absmax = np.abs(xf).max(axis=-1, keepdims=True) if xf.shape[-1] else np.zeros(xf.shape[:-1] + (1,), np.float32)
     return _quantize_rows(xf, absmax)
+
+
+def quantize_int8_rowwise_f16(x_f16: np.ndarray):
+    """Per-row absmax INT8 quantization of an fp16 activation (numpy float16 array).
+
+    The same eager code (eager/quantization.py:815-826, 857-875) with x in fp16: the
+    row absmax in fp16 (exact), ``scale = max(absmax/127, 1e-30)`` in fp32, the divisor
+    ``scale.to(fp16)`` with ``finfo(fp16).tiny`` (2^-14) for a zero, the quotient formed
+    in fp32 and stored as fp16, round-half-even, clamp to [-128, 127]."""
+    xf = np.asarray(x_f16, np.float16).astype(np.float32)
+    absmax = np.abs(xf).max(axis=-1, keepdims=True) if xf.shape[-1] else np.zeros(xf.shape[:-1] + (1,), np.float32)
+    scale = np.maximum((absmax / F32(127.0)).astype(np.float32), F32(1e-30)).astype(np.float32)
+    with np.errstate(over="ignore"):
+        sh = scale.astype(np.float16).astype(np.float32)
+    sh = np.where(sh == 0, np.float32(np.finfo(np.float16).tiny), sh).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        quo = (xf / sh).astype(np.float32).astype(np.float16).astype(np.float32)
+    q = np.clip(np.rint(quo), -128.0, 127.0).astype(np.int8)
+    return q, scale
 
 
 def quantize_int8_rowwise_given_absmax(x_bf16: np.ndarray, absmax: np.ndarray):
@@ -302,6 +324,36 @@ def dequant_epilogue(acc: np.ndarray, x_scale: np.ndarray, w_scale: np.ndarray, 
     if bias_bf16 is not None:
         out = _bf16_round((out + bf16_to_f32(bias_bf16).reshape(1, -1)).astype(np.float32))
     return f32_to_bf16(out)
+
+
+def dequant_epilogue_f16(acc: np.ndarray, x_scale: np.ndarray, w_scale: np.ndarray, bias_f16=None) -> np.ndarray:
+    """``fp16(float(acc) * (x_scale[m] * w_scale[n]))`` (+ fp16 bias): ``dequant_epilogue``
+    with ``out_dtype=float16`` (eager/quantization.py:1034-1053; the bias is converted
+    to the output dtype and added in it). Returns numpy float16."""
+    xs = np.asarray(x_scale, np.float32).reshape(-1, 1)
+    ws = np.asarray(w_scale, np.float32).reshape(1, -1)
+    s = (xs * ws).astype(np.float32)
+    with np.errstate(over="ignore"):
+        out = (acc.astype(np.float32) * s).astype(np.float32).astype(np.float16)
+        if bias_f16 is not None:
+            b = np.asarray(bias_f16, np.float16).astype(np.float32).reshape(1, -1)
+            out = (out.astype(np.float32) + b).astype(np.float32).astype(np.float16)
+    return out
+
+
+def int8_linear_f16(x, w_i8, w_scale, bias=None, out_dtype="float16"):
+    """``int8_linear(x, weight, weight_scale, bias, out_dtype)`` with an fp16 activation
+    (numpy float16) or a bf16 one (uint16 bits), and an fp16 or bf16 output: the
+    quantizer of x's dtype, the int32 GEMM, the epilogue of the output dtype (bias
+    converted to it: numpy float16 for fp16, bf16 bits for bf16)."""
+    if np.asarray(x).dtype == np.float16:
+        q, s = quantize_int8_rowwise_f16(x)
+    else:
+        q, s = quantize_int8_rowwise(x)
+    acc = int8_matmul_accumulate(q, w_i8)
+    if out_dtype == "float16":
+        return dequant_epilogue_f16(acc, s, w_scale, bias)
+    return dequant_epilogue(acc, s, w_scale, bias)
 
 
 def int8_linear(x_bf16, w_i8, w_scale, bias_bf16=None, input_act=None):

@@ -393,6 +393,37 @@ def main() -> None:
         "x_cf": b16(xb), "scale_cf": b16(scb), "shift_cf": b16(shb), "out_cf": b16(ob),
     }
 
+    # fp16 activations and outputs: the same eager quantizer and linear with x in fp16
+    # (edge rows: zero, a scale that underflows fp16, values near the fp16 maximum) and
+    # out_dtype fp16, plus bf16 x -> fp16 out and fp16 x -> bf16 out.
+    g16 = torch.Generator().manual_seed(16)
+    x16 = (torch.randn(96, 512, generator=g16) * 2).to(torch.float16)
+    x16[1] = 0
+    x16[2] = (torch.randn(512, generator=g16) * 1e-7).to(torch.float16)   # fp16 subnormals
+    x16[3, 5] = 6.0e4
+    x16[4, :] = -1.5
+    w16 = (torch.randn(160, 512, generator=g16) * 0.02).to(torch.bfloat16)
+    wq16, ws16 = eq.quantize_int8_rowwise(w16)
+    ws16 = ws16.reshape(-1)
+    q16, s16 = eq.quantize_int8_rowwise(x16)
+    bias16 = torch.randn(160, generator=g16).to(torch.float16)
+    xbf = torch.randn(96, 512, generator=g16).to(torch.bfloat16)
+    biasbf = torch.randn(160, generator=g16).to(torch.bfloat16)
+    y16 = eq.int8_linear(x16, wq16, ws16, None, torch.float16)
+    y16b = eq.int8_linear(x16, wq16, ws16, bias16, torch.float16)
+    ymix = eq.int8_linear(xbf, wq16, ws16, biasbf, torch.float16)
+    y16bf = eq.int8_linear(x16, wq16, ws16, None, torch.bfloat16)
+    assert y16.dtype == torch.float16 and ymix.dtype == torch.float16 and y16bf.dtype == torch.bfloat16
+
+    def h16(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+    out["fp16_linear"] = {
+        "x16": h16(x16), "q16": q16.numpy(), "s16": s16.numpy(), "wq": wq16.numpy(), "ws": ws16.numpy(),
+        "bias16": h16(bias16), "xbf": b16(xbf), "biasbf": b16(biasbf),
+        "y16": h16(y16), "y16_bias": h16(y16b), "y_bf_in_f16_out": h16(ymix), "y_f16_in_bf_out": b16(y16bf),
+    }
+
     for name, arrays in out.items():
         if args.only is not None and name not in args.only:
             continue

@@ -232,3 +232,24 @@ def test_rms_adaln_oracle_pinned_to_reference(golden):
     out_cf = O.rms_adaln_rows(g["x_cf"].reshape(-1, d), None, g["scale_cf"].reshape(b, d),
                               g["shift_cf"].reshape(b, d), np.repeat(np.arange(b), t), 1e-6)
     np.testing.assert_array_equal(out_cf, g["out_cf"].reshape(-1, d))
+
+
+def test_fp16_quantizer_and_linear_bit_exact(golden):
+    """fp16 activations and outputs: the oracle's fp16 quantizer, epilogue and linear
+    against the reference's eager outputs (zero row, fp16-subnormal row whose scale
+    underflows, a value near the fp16 maximum, a constant row)."""
+    g = golden("fp16_linear")
+    x16 = g["x16"].view(np.float16)
+    q, s = O.quantize_int8_rowwise_f16(x16)
+    np.testing.assert_array_equal(q, g["q16"])
+    np.testing.assert_array_equal(s, g["s16"])
+    y = O.int8_linear_f16(x16, g["wq"], g["ws"])
+    np.testing.assert_array_equal(y.view(np.uint16), g["y16"])
+    yb = O.int8_linear_f16(x16, g["wq"], g["ws"], g["bias16"].view(np.float16))
+    np.testing.assert_array_equal(yb.view(np.uint16), g["y16_bias"])
+    # bf16 x, fp16 out: the reference converts the bf16 bias to fp16 before adding
+    bias_as_f16 = O.bf16_to_f32(g["biasbf"]).astype(np.float16)
+    ym = O.int8_linear_f16(g["xbf"], g["wq"], g["ws"], bias_as_f16)
+    np.testing.assert_array_equal(ym.view(np.uint16), g["y_bf_in_f16_out"])
+    yf = O.int8_linear_f16(x16, g["wq"], g["ws"], None, out_dtype="bfloat16")
+    np.testing.assert_array_equal(yf, g["y_f16_in_bf_out"])

@@ -202,6 +202,15 @@ int h3b200_quantize_int8_rowwise(const void* x, int64_t m, int64_t k, int64_t ld
   return from_cuda(h3::launch_quantize_rows(x, ldx, m, k, act, nullptr, q, scale, S(stream)), "quantize_int8_rowwise");
 }
 
+int h3b200_quantize_int8_rowwise_f16(const void* x, int64_t m, int64_t k, int64_t ldx, int8_t* q, float* scale,
+                                     h3b200_stream_t stream) {
+  H3_GUARD("quantize_int8_rowwise_f16", stream);
+  if (m < 0 || k < 0 || ldx < k) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_f16: bad shape m=%lld k=%lld ldx=%lld", (long long)m, (long long)k, (long long)ldx);
+  if (m > 0 && (x == nullptr || q == nullptr || scale == nullptr)) return fail(H3B200_ERR_INVALID, "quantize_int8_rowwise_f16: NULL pointer");
+  if (m > 0x7fffffffll) return fail(H3B200_ERR_UNSUPPORTED, "quantize_int8_rowwise_f16: m too large");
+  return from_cuda(h3::launch_quantize_rows_f16(x, ldx, m, k, q, scale, S(stream)), "quantize_int8_rowwise_f16");
+}
+
 int h3b200_quantize_int8_rowwise_stochastic(const void* x, int64_t m, int64_t k, int64_t ldx, int act,
                                             int64_t seed, int8_t* q, float* scale, h3b200_stream_t stream) {
   H3_GUARD("quantize_int8_rowwise_stochastic", stream);
@@ -240,7 +249,7 @@ int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_scale, cons
                                     int64_t n, int64_t k, h3b200_stream_t stream) {
   H3_GUARD("int8_linear_prequantized", stream);
   if (m < 0 || n < 0 || k < 0) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: negative shape");
-  if (out_dtype != H3B200_DTYPE_BF16) return fail(H3B200_ERR_UNSUPPORTED, "int8_linear_prequantized: only bf16 output is built (got code %d)", out_dtype);
+  if (out_dtype != H3B200_DTYPE_BF16 && out_dtype != H3B200_DTYPE_F16) return fail(H3B200_ERR_UNSUPPORTED, "int8_linear_prequantized: bf16 or fp16 output (got code %d)", out_dtype);
   if (w_scale_numel != 1 && w_scale_numel != n) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: weight scale must be scalar or per-output-channel, got %lld for n=%lld", (long long)w_scale_numel, (long long)n);
   if (m == 0 || n == 0) return H3B200_OK;
   if (!xq || !x_scale || !w || !w_scale || !out) return fail(H3B200_ERR_INVALID, "int8_linear_prequantized: NULL pointer");
@@ -250,6 +259,7 @@ int h3b200_int8_linear_prequantized(const int8_t* xq, const float* x_scale, cons
   g.epilogue = h3::kEpiBF16; g.a_scale = x_scale; g.w_scale = w_scale; g.w_scale_per_channel = w_scale_numel == n && n != 1 ? 1 : 0;
   if (w_scale_numel == n && n == 1) g.w_scale_per_channel = 0;
   g.bias = bias; g.out = out; g.ldo = n;
+  g.out_f16 = out_dtype == H3B200_DTYPE_F16 ? 1 : 0;
   return from_cuda(h3::launch_gemm_i8(g, S(stream)), "int8_linear_prequantized");
 }
 

@@ -107,6 +107,7 @@ struct KParams {
   // kEpiI32 rows routed to their owners (GemmArgs::peer_out / peer_world)
   int32_t* peer_out[kTpMaxWorld];
   int peer_world;
+  int out_f16;  // kEpiBF16: fp16 out and bias (GemmArgs::out_f16)
 };
 
 template <int EPI>
@@ -329,9 +330,16 @@ __device__ __forceinline__ void epilogue_values(const KParams& p, const uint32_t
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int j = 4 * q + e;
-        uint32_t b = dequant_bits(r[j], xs, wv[e]);
-        if constexpr (EPI == kEpiBF16) {
-          if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
+        uint32_t b;
+        if (EPI == kEpiBF16 && p.out_f16) {  // fp16 out: the same association, fp16 roundings
+          b = __half_as_ushort(__float2half_rn(__fmul_rn(__int2float_rn((int)r[j]), __fmul_rn(xs, wv[e]))));
+          if (p.bias != nullptr)
+            b = __half_as_ushort(__float2half_rn(__fadd_rn(__half2float(__ushort_as_half((unsigned short)b)), av[e])));
+        } else {
+          b = dequant_bits(r[j], xs, wv[e]);
+          if constexpr (EPI == kEpiBF16) {
+            if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), av[e]));
+          }
         }
         if constexpr (EPI == kEpiGatedResidual) {
           if (p.bias != nullptr) b = bf16_bits(__fadd_rn(__uint_as_float(b << 16), bias_s[j]));
@@ -831,7 +839,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           float a = 0.0f;
           if ((EPI == kEpiBF16 || EPI == kEpiBF16Corr || EPI == kEpiQKV || EPI == kEpiSwiGLU) && p.bias != nullptr &&
               cok)
-            a = __bfloat162float(p.bias[wrow]);
+            a = (EPI == kEpiBF16 && p.out_f16) ? __half2float(reinterpret_cast<const __half*>(p.bias)[wrow])
+                                               : __bfloat162float(p.bias[wrow]);
           if (kInBox && cok && (EPI != kEpiGatedResidual || p.row_map == nullptr)) a = __bfloat162float(p.gate[col]);
           aux_s[c] = a;
           if (EPI == kEpiGatedResidual && p.bias != nullptr) bias_s[c] = cok ? __bfloat162float(p.bias[col]) : 0.0f;
@@ -1340,6 +1349,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
        a.requant_lds % 8 != 0 || (reinterpret_cast<uintptr_t>(a.requant_src) & 15) || a.row_absmax == nullptr ||
        a.requant_ready == nullptr))
     return cudaErrorNotSupported;
+  if (a.out_f16 != 0 && a.epilogue != kEpiBF16) return cudaErrorNotSupported;
   if (a.peer_world != 0) {
     if (a.epilogue != kEpiI32 || a.peer_world < 0 || a.peer_world > kTpMaxWorld || a.ldo % 4 != 0)
       return cudaErrorNotSupported;
@@ -1379,7 +1389,8 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
     }
   } else if (a.epilogue == kEpiI32) {
     t.out = t.b;  // unused: int32 results are stored directly
-  } else if (!encode_tmap_2d(&t.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.out, (uint64_t)n_out, (uint64_t)a.m,
+  } else if (!encode_tmap_2d(&t.out, a.out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                             a.out, (uint64_t)n_out, (uint64_t)a.m,
                              (uint64_t)a.ldo * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return cudaErrorInvalidValue;
   }
@@ -1450,6 +1461,7 @@ cudaError_t launch_gemm_i8(const GemmArgs& a, cudaStream_t stream) {
   kp.rq_units = a.m * kp.rq_upr;
   for (int o = 0; o < kTpMaxWorld; ++o) kp.peer_out[o] = a.peer_out[o];
   kp.peer_world = a.peer_world;
+  kp.out_f16 = a.out_f16;
   if (pair) return launch_cg<2>(a.epilogue, t, kp, 2 * (int)std::min<int64_t>(tiles, (int64_t)(sms / 2)), stream);
   return launch_cg<1>(a.epilogue, t, kp, (int)std::min<int64_t>(tiles, (int64_t)sms), stream);
 }

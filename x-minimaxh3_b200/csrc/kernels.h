@@ -106,6 +106,8 @@ struct GemmArgs {
   // cross-GPU barrier after the kernel (a system-scope release).
   int32_t* peer_out[kTpMaxWorld] = {};
   int peer_world = 0;
+  // kEpiBF16 only: out and bias are fp16 (y = fp16(acc * (xs * ws)), + bias in fp16)
+  int out_f16 = 0;
 };
 
 // One pointer per rank of a tensor-parallel group (by value in kernel parameters).
@@ -142,6 +144,10 @@ cudaError_t launch_apply_act(const void* x, void* y, int64_t n, int act, cudaStr
 // [gate | up], 2 k wide, at stride ldx >= 2 k).
 cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t k, int act, const float* absmax_in,
                                  int8_t* q, float* scale, cudaStream_t stream);
+
+// Row quantizer of fp16 rows (no input activation): the reference's fp16 semantics (quantize.cu).
+cudaError_t launch_quantize_rows_f16(const void* x, int64_t ldx, int64_t m, int64_t k, int8_t* q, float* scale,
+                                     cudaStream_t stream);
 
 // Stochastic rounding (seed > 0): the reference CUDA kernel's counter-based noise added
 // to the bf16 quotient, then floor (quantize.cu).

@@ -201,6 +201,38 @@ __global__ void __launch_bounds__(kQThreads) quantize_rows_scalar_kernel(const _
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// ---- fp16 activations ----
+// The reference's quantizer on an fp16 x (backends/eager/quantization.py:815-826,
+// 857-875): the row absmax in fp16 (exact), scale = max(absmax / 127, 1e-30) in fp32,
+// the divisor fp16(scale) (torch.finfo(fp16).tiny = 2^-14 when that rounds to zero)
+// and q = clamp(rne(fp16(x / divisor)), -128, 127), the quotient formed in fp32 and
+// rounded once to fp16 as torch's fp16 division does. One CTA per row, two passes.
+__device__ __forceinline__ float quant_divisor_f16(float scale) {
+  const float sh = __half2float(__float2half_rn(scale));
+  return sh == 0.0f ? 6.103515625e-05f : sh;
+}
+
+__global__ void __launch_bounds__(kQThreads) quantize_rows_f16_kernel(const __half* __restrict__ x, int64_t ldx,
+                                                                      int64_t m, int64_t k, int8_t* __restrict__ q,
+                                                                      float* __restrict__ scale) {
+  __shared__ float red[kQThreads / 32];
+  const int64_t row = blockIdx.x;
+  if (row >= m) return;
+  const uint16_t* xr = reinterpret_cast<const uint16_t*>(x + row * ldx);
+  uint32_t amax_bits = 0u;  // |x| of fp16 values orders like their magnitude bits (a NaN wins)
+  for (int64_t i = threadIdx.x; i < k; i += kQThreads) amax_bits = max(amax_bits, (uint32_t)(xr[i] & 0x7FFFu));
+  const float rowmax = block_max(__half2float(__ushort_as_half((unsigned short)amax_bits)), red);
+  const float s = row_scale(rowmax);
+  const float d = quant_divisor_f16(s);
+  for (int64_t i = threadIdx.x; i < k; i += kQThreads) {
+    const float xv = __half2float(__ushort_as_half(xr[i]));
+    float v = rintf(__half2float(__float2half_rn(__fdiv_rn(xv, d))));
+    v = fminf(fmaxf(v, -128.0f), 127.0f);
+    q[row * k + i] = (int8_t)(int)v;
+  }
+  if (threadIdx.x == 0) scale[row] = s;
+}
+
 // ---- stochastic rounding ----
 // The reference's CUDA kernel (backends/cuda/ops/int8_linear.cu:78-90 noise, :186-193
 // rounding): element idx = row * k + col of the contiguous [m, k] activation gets the
@@ -415,6 +447,14 @@ cudaError_t launch_quantize_rows(const void* x, int64_t ldx, int64_t m, int64_t 
   }
   quantize_rows_scalar_kernel<<<dim3((unsigned)m), dim3(kQThreads), 0, stream>>>(xb, ldx, m, k, act, absmax_in, q,
                                                                                   scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows_f16(const void* x, int64_t ldx, int64_t m, int64_t k, int8_t* q, float* scale,
+                                     cudaStream_t stream) {
+  if (m == 0) return cudaSuccess;
+  quantize_rows_f16_kernel<<<dim3((unsigned)m), dim3(kQThreads), 0, stream>>>(static_cast<const __half*>(x), ldx, m,
+                                                                                k, q, scale);
   return cudaGetLastError();
 }
 

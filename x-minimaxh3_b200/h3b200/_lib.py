@@ -35,6 +35,7 @@ SIGNATURES = {
     "h3b200_swiglu": (_i32, [_p, _i64, _p, _i64, _i64, _i64, _p]),
     "h3b200_quantize_int8_rowwise": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _p, _p]),
     "h3b200_quantize_int8_rowwise_stochastic": (_i32, [_p, _i64, _i64, _i64, _i32, _i64, _p, _p, _p]),
+    "h3b200_quantize_int8_rowwise_f16": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p]),
     "h3b200_quantize_int8_rowwise_absmax": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p, _p]),
     "h3b200_int8_mm": (_i32, [_p, _p, _i64, _i64, _i64, _p, _p]),
     "h3b200_int8_linear_prequantized": (_i32, [_p, _p, _p, _p, _i64, _p, _i32, _p, _i64, _i64, _i64, _p]),

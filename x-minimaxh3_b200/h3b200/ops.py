@@ -65,6 +65,9 @@ def _need_cuda(*ts):
             raise ValueError("h3b200 operators take CUDA tensors only (no CPU fallback)")
 
 
+_OUT_CODES = {torch.bfloat16: 2, torch.float16: 1}  # H3B200_DTYPE_BF16 / H3B200_DTYPE_F16
+
+
 def _rows(x: torch.Tensor):
     """View x as [rows, K] with unit stride along K; returns (x2d, row_stride)."""
     k = x.shape[-1]
@@ -127,10 +130,23 @@ def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int | None = 0, 
     eager eager/quantization.py:857-875; CUDA backends/cuda/ops/int8_linear.cu:157-200).
     ``stochastic_rounding`` > 0 is the seed of stochastic rounding: the reference CUDA
     kernel's counter-based noise is added to the bf16 quotient, which is then floored
-    (``h3b200_quantize_int8_rowwise_stochastic``); <= 0 or None rounds to nearest even."""
+    (``h3b200_quantize_int8_rowwise_stochastic``); <= 0 or None rounds to nearest even.
+    An fp16 ``x`` is quantized with the reference's fp16 arithmetic (fp16 divisor and
+    quotient, ``h3b200_quantize_int8_rowwise_f16``); it takes no input activation and
+    no stochastic rounding."""
     _need_cuda(x)
+    if x.dtype == torch.float16:
+        if input_act is not None or (stochastic_rounding is not None and stochastic_rounding > 0):
+            raise NotImplementedError("fp16 activations are quantized without input_act and stochastic rounding "
+                                      "(the exact activation tables are built for bf16 inputs)")
+        x2, ldx = _rows(x)
+        m, k = x2.shape
+        q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+        s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+        _lib.call("h3b200_quantize_int8_rowwise_f16", x2.data_ptr(), m, k, ldx, q.data_ptr(), s.data_ptr(), _stream(x))
+        return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
     if x.dtype != torch.bfloat16:
-        raise ValueError(f"quantize_int8_rowwise expects bf16, got {x.dtype}")
+        raise ValueError(f"quantize_int8_rowwise expects bf16 or fp16, got {x.dtype}")
     k = _act_k(x, input_act)
     x2, ldx = _rows(x)
     m = x2.shape[0]
@@ -200,11 +216,12 @@ def int8_linear_prequantized(x_qdata: torch.Tensor, x_scale: torch.Tensor, weigh
                              out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     """INT8 linear from a row-quantized activation (backends/cuda/__init__.py:1934-1957).
 
-    ``out = bf16(float(acc) * (x_scale[row] * weight_scale[col])) (+ bias)`` with
-    the eager association (eager/quantization.py:1044-1048)."""
+    ``out = out_dtype(float(acc) * (x_scale[row] * weight_scale[col])) (+ bias)`` with
+    the eager association (eager/quantization.py:1044-1053): bf16 or fp16 out, the bias
+    converted to the output dtype and added in it."""
     _need_cuda(x_qdata, x_scale, weight)
-    if out_dtype != torch.bfloat16:
-        raise NotImplementedError("h3b200 builds bf16 outputs only")
+    if out_dtype not in _OUT_CODES:
+        raise NotImplementedError(f"h3b200 builds bf16 and fp16 outputs, got {out_dtype}")
     xq = x_qdata.reshape(-1, x_qdata.shape[-1]).contiguous()
     m, k = xq.shape
     n, kw = weight.shape
@@ -213,10 +230,10 @@ def int8_linear_prequantized(x_qdata: torch.Tensor, x_scale: torch.Tensor, weigh
     w = weight.contiguous()
     xs = x_scale.reshape(-1).to(torch.float32).contiguous()
     ws = _weight_scale(weight_scale, n, xq.device)
-    b = None if bias is None else bias.to(device=xq.device, dtype=torch.bfloat16).contiguous()
-    out = torch.empty((m, n), dtype=torch.bfloat16, device=xq.device)
+    b = None if bias is None else bias.to(device=xq.device, dtype=out_dtype).contiguous()
+    out = torch.empty((m, n), dtype=out_dtype, device=xq.device)
     _lib.call("h3b200_int8_linear_prequantized", xq.data_ptr(), xs.data_ptr(), w.data_ptr(), ws.data_ptr(),
-              ws.numel(), _ptr(b), _lib.DTYPE_BF16, out.data_ptr(), m, n, k, _stream(xq))
+              ws.numel(), _ptr(b), _OUT_CODES[out_dtype], out.data_ptr(), m, n, k, _stream(xq))
     return out.reshape(*x_qdata.shape[:-1], n)
 
 
@@ -307,8 +324,16 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     _need_cuda(x, weight)
     if out_dtype is None:
         out_dtype = torch.bfloat16
-    if out_dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
-        raise NotImplementedError("h3b200 builds bf16 activations and outputs only")
+    if out_dtype not in _OUT_CODES or x.dtype not in _OUT_CODES:
+        raise NotImplementedError(f"h3b200 builds bf16 / fp16 activations and outputs, got {x.dtype} -> {out_dtype}")
+    if x.dtype == torch.float16:
+        if input_act is not None or convrot:
+            raise NotImplementedError("fp16 activations: no input_act or convrot (the exact activation tables and "
+                                      "the correctly rounded rotation are built for bf16)")
+        if x.shape[-1] != weight.shape[-1]:
+            raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {weight.shape[-1]}")
+        xq, xs = quantize_int8_rowwise(x)
+        return int8_linear_prequantized(xq, xs, weight, weight_scale, bias, out_dtype)
     k = _act_k(x, input_act)  # swiglu: x rows are [gate | up], 2 K wide
     if k != weight.shape[-1]:
         raise ValueError(f"Input and weight inner dimensions must match, got {k} and {weight.shape[-1]}")
@@ -316,6 +341,9 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     n = weight.shape[0]
     if convrot:
         xq, xs = quantize_int8_rowwise_convrot(x, convrot_groupsize, input_act)
+        return int8_linear_prequantized(xq, xs, weight, weight_scale, bias, out_dtype)
+    if out_dtype != torch.bfloat16:        # bf16 x, fp16 out: quantize, then the fp16 epilogue
+        xq, xs = quantize_int8_rowwise(x, input_act=input_act)
         return int8_linear_prequantized(xq, xs, weight, weight_scale, bias, out_dtype)
     x2, ldx = _rows(x)
     m = x2.shape[0]
