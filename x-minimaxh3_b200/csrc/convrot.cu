@@ -42,14 +42,15 @@
 namespace h3 {
 namespace {
 
-// TW warps per team (6 or 8): 12 or 16 warps per CTA, at most 4 per SM sub-partition
-constexpr int kCvTeams = 2;
+// NT teams of TW warps: 2 x 6, 2 x 8 or 4 x 3 (12 or 16 warps per CTA, at most 4 per SM
+// sub-partition)
+constexpr int kCvMaxTeams = 4;
 constexpr int kCvMaxGph = 6;  // groups per half-warp: K <= 16 * 6 * 256
 constexpr int kCvMaxStages = 16;
 constexpr int kCvTileBytes = 2 * 16 * cv::kXRow;  // per consumer warp: one padded double tile per half-warp
 constexpr int kCvOffRed = 512;      // [team][phase][warp] row-max words, after the mbarriers
 constexpr int kCvOffTiles = 1024;
-constexpr int cv_off_ring(int tw) { return kCvOffTiles + kCvTeams * tw * kCvTileBytes; }
+constexpr int cv_off_ring(int warps) { return kCvOffTiles + warps * kCvTileBytes; }
 constexpr int kCvSmemLimit = 232448;
 constexpr unsigned kErrCvFull = 0x312, kErrCvTeam = 0x313, kErrCvDrain = 0x314;
 
@@ -110,7 +111,7 @@ __device__ __forceinline__ Words8 cv_group_slow(const uint8_t* st, int K, int g,
   return r;
 }
 
-template <int TW, int GPH, int ACT>
+template <int TW, int GPH, int ACT, int NT>
 __global__ void __maxnreg__(128)
     convrot_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t m, int8_t* __restrict__ q,
                    float* __restrict__ scale, __nv_bfloat16* __restrict__ sx, int sum_group, int64_t kp, int stages,
@@ -122,9 +123,10 @@ __global__ void __maxnreg__(128)
   extern __shared__ __align__(128) uint8_t cv_smem[];
   uint8_t* smem = cv_smem;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* team_bar = full_bar + kCvMaxStages;  // [kCvTeams]
+  static_assert(NT * TW <= 16 && NT <= kCvMaxTeams, "team layout");
+  uint64_t* team_bar = full_bar + kCvMaxStages;  // [NT]
   uint32_t* red = reinterpret_cast<uint32_t*>(smem + kCvOffRed);
-  uint8_t* ring = smem + cv_off_ring(TW);
+  uint8_t* ring = smem + cv_off_ring(NT * TW);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t G = gridDim.x;
   const int64_t cnt = m > (int64_t)blockIdx.x ? (m - blockIdx.x + G - 1) / G : 0;  // rows of this CTA
@@ -132,15 +134,15 @@ __global__ void __maxnreg__(128)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&full_bar[s], 1);
-    for (int t = 0; t < kCvTeams; ++t) mbar_init(&team_bar[t], TW);
+    for (int t = 0; t < NT; ++t) mbar_init(&team_bar[t], TW);
     fence_barrier_init();
   }
   __syncthreads();
 
   const int cw = warp;
   const int team = cw / TW, tw = cw - team * TW;
-  // The first lane of each team fills that team's stages: S is even, so stage j % S
-  // always holds rows of team j % 2. Rows team, team + 2, ... below S first; then row
+  // The first lane of each team fills that team's stages: S is a multiple of NT, so stage
+  // j % S always holds rows of team j % NT. Rows team, team + NT, ... below S first; then row
   // j + S as soon as the team has read row j (its row-absmax barrier completes after
   // every warp of the team has read the stage), overlapping the quantization of row j.
   const bool leader = tw == 0 && lane == 0;
@@ -151,7 +153,7 @@ __global__ void __maxnreg__(128)
   };
   int64_t filled = team;  // (leader) next row of the team to fill
   if (leader)
-    for (; filled < cnt && filled < S; filled += kCvTeams) fill(filled);
+    for (; filled < cnt && filled < S; filled += NT) fill(filled);
   const int h = lane >> 4, li = lane & 15;
   const int hw = 2 * tw + h;  // groups hw, hw + 2 TW, ...
   uint8_t* tile = smem + kCvOffTiles + cw * kCvTileBytes + h * (16 * cv::kXRow);
@@ -162,11 +164,11 @@ __global__ void __maxnreg__(128)
   const int lanes_per_sum = sum_group / 16;
   uint32_t team_phase = 0;
   int64_t waited = team;  // next row of the team whose fill has not been waited for
-  for (int64_t j = team; j < cnt; j += kCvTeams) {
+  for (int64_t j = team; j < cnt; j += NT) {
     const int s = (int)(j % S);
     const int64_t row = blockIdx.x + j * G;
     if (!mbar_wait(&full_bar[s], (uint32_t)(j / S) & 1u, kErrCvFull)) break;
-    waited = j + kCvTeams;
+    waited = j + NT;
     const uint8_t* st = ring + (size_t)s * row_bytes;
     uint32_t park[GPH][8];
     uint32_t amax = 0u;
@@ -306,7 +308,7 @@ __global__ void __maxnreg__(128)
     ++team_phase;
     if (leader && j + S < cnt) {
       fill(j + S);
-      filled = j + S + kCvTeams;
+      filled = j + S + NT;
     }
     uint32_t rowbits = rr[0];
 #pragma unroll
@@ -340,15 +342,15 @@ __global__ void __maxnreg__(128)
   // every copy this team's leader issued lands before the CTA may exit (rows left
   // unconsumed only after a bounded wait failed)
   if (leader)
-    for (int64_t i = waited; i < filled; i += kCvTeams)
+    for (int64_t i = waited; i < filled; i += NT)
       mbar_wait(&full_bar[i % S], (uint32_t)(i / S) & 1u, kErrCvDrain, 200000000ull);
 }
 
-template <int TW, int GPH>
+template <int TW, int GPH, int NT = 2>
 cudaError_t cv_launch(int act, const __nv_bfloat16* x, int64_t ldx, int64_t m, int8_t* q, float* scale,
                       __nv_bfloat16* sx, int sum_group, int64_t kp, int stages, int ng, int smem, unsigned grid,
                       cudaStream_t stream) {
-  constexpr int threads = 32 * kCvTeams * TW;
+  constexpr int threads = 32 * NT * TW;
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kCvSmemLimit);
     if (e != cudaSuccess) return e;
@@ -360,22 +362,25 @@ cudaError_t cv_launch(int act, const __nv_bfloat16* x, int64_t ldx, int64_t m, i
     kern<<<grid, threads, smem, stream>>>(x, ldx, m, q, scale, sx, sum_group, kp, stages, ng);
     return cudaGetLastError();
   };
-  if (act == H3B200_ACT_GELU_TANH) return go(convrot_kernel<TW, GPH, H3B200_ACT_GELU_TANH>);
-  if (act == H3B200_ACT_SWIGLU) return go(convrot_kernel<TW, GPH, H3B200_ACT_SWIGLU>);
-  return go(convrot_kernel<TW, GPH, H3B200_ACT_NONE>);
+  if (act == H3B200_ACT_GELU_TANH) return go(convrot_kernel<TW, GPH, H3B200_ACT_GELU_TANH, NT>);
+  if (act == H3B200_ACT_SWIGLU) return go(convrot_kernel<TW, GPH, H3B200_ACT_SWIGLU, NT>);
+  return go(convrot_kernel<TW, GPH, H3B200_ACT_NONE, NT>);
 }
 
-// Team size for a row of ng groups: rows of up to 24 groups keep every half-warp of
-// 6-warp teams busy (more warps would idle); longer rows use 8-warp teams (16 warps).
-int cv_team_warps(int64_t ng) { return ng <= 24 ? 6 : 8; }
+// Team layout for a row of ng groups: rows of up to 12 groups go to four 3-warp teams
+// (each row's work per team pass is short, so more rows in flight per CTA hide the
+// per-row barrier and copy latency); up to 24 groups keep every half-warp of two 6-warp
+// teams busy; longer rows use two 8-warp teams (16 warps).
+int cv_team_warps(int64_t ng) { return ng <= 12 ? 3 : ng <= 24 ? 6 : 8; }
+int cv_teams(int64_t ng) { return ng <= 12 ? 4 : 2; }
 
 }  // namespace
 
 int64_t convrot_max_k(int act) {
   // rows of at most 16 half-warps x 6 groups, and at least two stages of the raw row in shared memory
-  const int64_t by_regs = (int64_t)kCvTeams * 8 * kCvMaxGph * 256;
+  const int64_t by_regs = (int64_t)2 * 8 * kCvMaxGph * 256;
   const int64_t per_elem = act == H3B200_ACT_SWIGLU ? 4 : 2;
-  const int64_t by_smem = ((kCvSmemLimit - 1024 - cv_off_ring(8)) / 2 / per_elem) / 256 * 256;
+  const int64_t by_smem = ((kCvSmemLimit - 1024 - cv_off_ring(16)) / 2 / per_elem) / 256 * 256;
   return std::min(by_regs, by_smem);
 }
 
@@ -392,19 +397,23 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
     if (e != cudaSuccess) return e;
   }
   const int ng = (int)(k / 256);
-  const int tw = cv_team_warps(ng);
+  const int tw = cv_team_warps(ng), nt = cv_teams(ng);
   const int gph = (ng + 2 * tw - 1) / (2 * tw);
   const int64_t row_bytes = (act == H3B200_ACT_SWIGLU ? 4 : 2) * k;
-  int stages = (int)std::min<int64_t>(kCvMaxStages, (kCvSmemLimit - 1024 - cv_off_ring(tw)) / row_bytes);
-  stages &= ~1;  // even: each stage serves one team
-  if (stages < 2) return cudaErrorNotSupported;
-  const int smem = 1024 + cv_off_ring(tw) + stages * (int)row_bytes;
+  int stages = (int)std::min<int64_t>(kCvMaxStages, (kCvSmemLimit - 1024 - cv_off_ring(nt * tw)) / row_bytes);
+  stages -= stages % nt;  // a multiple of the team count: each stage serves one team
+  if (stages < nt) return cudaErrorNotSupported;
+  const int smem = 1024 + cv_off_ring(nt * tw) + stages * (int)row_bytes;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned grid = (unsigned)std::min<int64_t>(m, (int64_t)num_sms(dev));
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
   __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
   const int sg = sx != nullptr ? (int)sum_group : 16;
+  if (tw == 3) {
+    if (gph == 1) return cv_launch<3, 1, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    return cv_launch<3, 2, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+  }
   if (tw == 6) {
     if (gph == 1) return cv_launch<6, 1>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
     return cv_launch<6, 2>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
