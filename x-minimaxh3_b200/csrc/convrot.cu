@@ -367,12 +367,13 @@ cudaError_t cv_launch(int act, const __nv_bfloat16* x, int64_t ldx, int64_t m, i
   return go(convrot_kernel<TW, GPH, H3B200_ACT_NONE, NT>);
 }
 
-// Team layout for a row of ng groups: rows of up to 12 groups go to four 3-warp teams
+// Team layout for a row of ng groups: rows of up to 24 groups go to four 3-warp teams
 // (each row's work per team pass is short, so more rows in flight per CTA hide the
-// per-row barrier and copy latency); up to 24 groups keep every half-warp of two 6-warp
-// teams busy; longer rows use two 8-warp teams (16 warps).
-int cv_team_warps(int64_t ng) { return ng <= 12 ? 3 : ng <= 24 ? 6 : 8; }
-int cv_teams(int64_t ng) { return ng <= 12 ? 4 : 2; }
+// per-row barrier and copy latency: 32,760 x 3,072 216 -> 157 us, x 5,376 320 -> 293 us
+// against two 6-warp teams); longer rows use two 8-warp teams (16 warps).
+// (Four teams need at least two row stages each in shared memory, or a team would wait for
+// every row's copy; launch_quantize_convrot falls back to two teams otherwise.)
+int cv_team_warps(int64_t ng, bool four) { return four ? 3 : ng <= 24 ? 6 : 8; }
 
 }  // namespace
 
@@ -397,11 +398,15 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
     if (e != cudaSuccess) return e;
   }
   const int ng = (int)(k / 256);
-  const int tw = cv_team_warps(ng), nt = cv_teams(ng);
-  const int gph = (ng + 2 * tw - 1) / (2 * tw);
   const int64_t row_bytes = (act == H3B200_ACT_SWIGLU ? 4 : 2) * k;
-  int stages = (int)std::min<int64_t>(kCvMaxStages, (kCvSmemLimit - 1024 - cv_off_ring(nt * tw)) / row_bytes);
-  stages -= stages % nt;  // a multiple of the team count: each stage serves one team
+  auto stages_for = [&](int warps, int teams) {
+    const int st = (int)std::min<int64_t>(kCvMaxStages, (kCvSmemLimit - 1024 - cv_off_ring(warps)) / row_bytes);
+    return st - st % teams;  // a multiple of the team count: each stage serves one team
+  };
+  const bool four = ng <= 24 && stages_for(12, 4) >= 8;
+  const int tw = cv_team_warps(ng, four), nt = four ? 4 : 2;
+  const int gph = (ng + 2 * tw - 1) / (2 * tw);
+  const int stages = stages_for(nt * tw, nt);
   if (stages < nt) return cudaErrorNotSupported;
   const int smem = 1024 + cv_off_ring(nt * tw) + stages * (int)row_bytes;
   int dev = 0;
@@ -411,8 +416,12 @@ cudaError_t launch_quantize_convrot(const void* x, int64_t ldx, int64_t m, int64
   __nv_bfloat16* sxb = static_cast<__nv_bfloat16*>(sx);
   const int sg = sx != nullptr ? (int)sum_group : 16;
   if (tw == 3) {
-    if (gph == 1) return cv_launch<3, 1, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
-    return cv_launch<3, 2, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    switch (gph) {
+      case 1: return cv_launch<3, 1, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+      case 2: return cv_launch<3, 2, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+      case 3: return cv_launch<3, 3, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+      default: return cv_launch<3, 4, 4>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
+    }
   }
   if (tw == 6) {
     if (gph == 1) return cv_launch<6, 1>(act, xb, ldx, m, q, scale, sxb, sg, kp, stages, ng, smem, grid, stream);
