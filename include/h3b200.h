@@ -593,7 +593,11 @@ H3B200_API int h3b200_fused_gated_mlp_swiglu_w4a8(const void* x, int64_t ldx, co
  * order (CUDA IPC mappings; world == 1 needs no open). Then h3b200_tp_gated_mlp on
  * every rank, with the same m and chunk_rows, in the same order. The cross-GPU
  * barrier waits at most barrier_timeout_ns (0: 5 s) and records device status 0x201
- * on expiry. h3b200_tp_comm_destroy after the last call has completed on every rank.
+ * on expiry; the ranks' barrier counts then disagree, so clear the status and create
+ * new communicators on every rank before the next call. h3b200_tp_comm_destroy after
+ * the last call has completed on every rank (no peer may still write into the region).
+ * A communicator is used by one host thread at a time; its calls are ordered on the
+ * stream they are given.
  *
  * h3b200_tp_stage / h3b200_tp_barrier expose the pipeline's steps (stage 1: quantize,
  * fc1, absmax push; 2: absmax max, fc2 with routed rows; 3: owner rows; 4: copy the
