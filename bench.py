@@ -165,7 +165,9 @@ class ClockSampler:
 # modulation row / on H3's [M, 5376] with three segments), ``tp2_linked`` (one chunk of M tokens of the
 # tensor-parallel MLP over two ranks linked on this one GPU, every stage of both ranks in order:
 # its fc2 launches are ``gemm_i8_kernel<10, 2>``, the GEMM whose epilogue stores each int32 row at its
-# owner; the outputs are checked against the fused MLP). Shapes are those of the config-1 MLP and config-3
+# owner; the outputs are checked against the fused MLP), ``w4_smallm`` (the W4A8 linear of M rows, at most 16,
+# through fc1's config-2 weight 3,072 -> 12,288 with the asymmetric correction: ConvRot quantizer, then
+# ``gemm_w4_smallm_kernel`` unpacking the int4 weight in shared memory). Shapes are those of the config-1 MLP and config-3
 # norm-RoPE with M tokens; inputs are seeded synthetic data. Every case first
 # runs the kernels it needs to build its inputs, then launches the kernel under
 # study ``--iters`` times, so a profiler can skip the set-up launches by kernel
@@ -175,7 +177,7 @@ class ClockSampler:
 
 CASES = ["quantize", "fc1", "fc1_bf16", "fc1_i32", "requant", "fc2", "fc2_rq", "mlp", "mlp_w4a8", "mlp_swiglu",
          "mlp_swiglu_w4", "decode_w4", "qknorm_h3", "qkv_h3", "convrot", "convrot_x", "norm_rope", "rms_adaln",
-         "rms_adaln_h3", "tp2_linked"]
+         "rms_adaln_h3", "tp2_linked", "w4_smallm"]
 
 
 def _case_mlp_inputs(m: int, dev):
@@ -301,6 +303,15 @@ def run_case(case: str, m: int, iters: int, report: bool = False):
                                dtype=torch.uint8, device=dev)
             ms = _case_timed(lambda: ops.qkv_qknorm_rope(xq, xs, wq_, ws, None, heads, kn, kn, freqs, 1e-5, "qkv",
                                                     *outs, workspace=work), iters, report)
+    elif case == "w4_smallm":
+        if m > 16:
+            raise SystemExit("w4_smallm: at most 16 rows (larger calls take the decode path)")
+        g = torch.Generator(device=dev).manual_seed(3)
+        w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        q4, s_rel, s_ch, corr = h3b200.quantize_w4a8_weight(w1, 128)
+        x = torch.randn(m, D_MODEL, generator=g, device=dev).to(torch.bfloat16)
+        ms = _case_timed(lambda: h3b200.w4a8_int8_linear(x, q4, s_rel, s_ch, correction=corr, group_size=128),
+                         iters, report)
     elif case == "mlp_w4a8":
         g = torch.Generator(device=dev).manual_seed(3)
         w1 = (torch.randn(D_FFN, D_MODEL, generator=g, device=dev) * 0.02).to(torch.bfloat16)
